@@ -1,0 +1,192 @@
+"""Generate the golden fixtures in this folder from the reference ``pack3d`` package.
+
+Run once, in a container that holds the reference source tree (the fixtures
+are committed; tests only read them):
+
+    python tests/golden/make_golden.py /path/to/reference/src
+
+Everything is computed by the reference's own public functions on the CPU:
+``build_layout`` / ``TokenLayout.repack`` / ``prepare_geometry`` tables,
+``axial_rope``, ``compress_summaries``, ``pack3d_reference`` (outputs and
+every gradient through autograd) and ``PACK3DAttention`` (backend
+"reference").  Head dimension 48 -- the BASELINE shape -- is refused by the
+reference's validation (``src/pack3d/_validation.py:17-18``); for those cases
+this script wraps that validation so that only its head-dimension refusal is
+skipped, and the reference arithmetic runs unchanged.
+"""
+import hashlib
+import sys
+from pathlib import Path
+
+import torch
+
+sys.dont_write_bytecode = True
+OUT = Path(__file__).resolve().parent
+sys.path.insert(0, str(OUT))
+import cases  # noqa: E402  (seeded input recipes shared with the tests)
+
+
+def sha256(t):
+    return hashlib.sha256(t.contiguous().numpy().tobytes()).hexdigest()
+
+
+def layout_tables(layout):
+    geom = layout.geometry
+    mapping = geom._raster_to_packed
+    return {
+        "grid_shape": tuple(layout.grid_shape),
+        "order": layout.order.clone(),
+        "coords": layout.coords.clone(),
+        "neighbors": geom.neighbors.clone(),
+        "reverse_neighbors": geom.reverse_neighbors.clone(),
+        "blocks": geom.blocks.clone(),
+        "pool_size": geom.pool_size,
+        "radius_one_grid": geom._radius_one_grid,
+        "raster_to_packed": None if mapping is None else mapping.clone(),
+    }
+
+
+def layout_digest(layout):
+    t = layout_tables(layout)
+    return {k: (sha256(v) if torch.is_tensor(v) else v) for k, v in t.items()}
+
+
+def relaxed_head_dim(pack3d):
+    """Let the reference accept head_dim 48: skip only the head-dimension refusal."""
+    import pack3d.reference as reference_module
+
+    original = reference_module._validate_inputs
+
+    def validate(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature):
+        d = q.shape[-1]
+        if d in (16, 32, 64, 128):
+            return original(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature)
+        # Re-run the same checks on 16-wide channel views; shapes/dtypes/devices are unchanged.
+        view = [t[..., :16] for t in (q, kl, vl, kg, vg)]
+        return original(*view, weight[:16], bias, gate, sl[:16], sg[:16], geometry, temperature)
+
+    reference_module._validate_inputs = validate
+    return original
+
+
+def core_case(pack3d, name, n, d, b, h, g, volume, pool, dtype, seed, temperature, empty_block):
+    inputs, nb, blocks = cases.graph_case(n, d, b, h, g, volume, pool, dtype, seed, empty_block)
+    geometry = pack3d.prepare_geometry(nb, blocks, pool)
+    leaves = [t.clone().requires_grad_() for t in inputs]
+    y = pack3d.pack3d_reference(*leaves, geometry, temperature=temperature)
+    dy = cases.upstream(y.shape, y.dtype, seed)
+    grads = torch.autograd.grad(y, leaves, dy)
+    torch.save({"reverse_neighbors": geometry.reverse_neighbors, "y": y.detach(),
+                "grads": [t.detach() for t in grads]}, OUT / f"core_{name}.pt")
+
+
+def grid_case(pack3d, name, grid, b, h, g, d, dtype, seed, weighted):
+    """BASELINE-shaped pipeline on a small grid: RoPE -> pooling -> core, with every gradient."""
+    from pack3d.rope import axial_rope
+    layout = pack3d.build_layout(grid, (4, 4, 4), radius=2, pool_size=1)
+    layout = layout.repack(layout.order.argsort())          # raster storage of 4x4x4 cubes
+    geom = layout.geometry
+    inputs = cases.grid_inputs(geom.num_tokens, b, h, g, d, dtype, seed, weighted)
+    leaves = [t.clone().requires_grad_() for t in inputs]
+    rq, rkl, rkg = (axial_rope(t, layout.coords) for t in (leaves[0], leaves[1], leaves[3]))
+    y = pack3d.pack3d_reference(rq, rkl, leaves[2], rkg, *leaves[4:], geom)
+    dy = cases.upstream(y.shape, y.dtype, seed)
+    grads = torch.autograd.grad(y, leaves, dy)
+    torch.save({"y": y.detach(), "grads": [t.detach() for t in grads]}, OUT / f"grid_{name}.pt")
+
+
+def main(src):
+    sys.path.insert(0, str(src))
+    import pack3d
+    from pack3d.compression import compress_summaries
+    from pack3d.rope import axial_rope, balanced_pairs
+
+    torch.set_num_threads(8)
+    relaxed_head_dim(pack3d)
+
+    # --- geometry tables (bit-exact targets) -------------------------------------------
+    tables = {}
+    for key, args, kwargs in [
+        ("r1_raster_4x4x8", ((4, 4, 8), (1, 2, 2)), dict(pool_size=4, layout="raster_block")),
+        ("r1_native_4x4x8", ((4, 4, 8), (1, 2, 2)), dict(pool_size=4)),
+        ("r2_native_8x8x8", ((8, 8, 8), (4, 4, 4)), dict(radius=2, pool_size=1)),
+        ("r_mixed_odd", ((7, 11, 5), (1, 1, 5)), dict(radius=(1, 2, 0), pool_size=8)),
+        ("r1_native_16x16x16", ((16, 16, 16), (2, 2, 2)), dict(pool_size=4)),
+    ]:
+        # Small layouts keep their full tables; larger ones keep a SHA-256 per table.
+        keep = layout_tables if key in ("r1_raster_4x4x8", "r1_native_4x4x8", "r_mixed_odd") else layout_digest
+        layout = pack3d.build_layout(*args, **kwargs)
+        tables[key] = {"args": args, "kwargs": kwargs, "tables": keep(layout)}
+        p = torch.randperm(layout.geometry.num_tokens, generator=torch.Generator().manual_seed(7))
+        tables[key]["perm"] = p
+        tables[key]["repacked"] = keep(layout.repack(p))
+        tables[key]["raster"] = keep(layout.repack(layout.order.argsort()))
+    torch.save(tables, OUT / "layouts.pt")
+
+    digests = {}
+    for grid in ((16, 16, 16), (32, 32, 32), (64, 64, 64)):
+        native = pack3d.build_layout(grid, (4, 4, 4), radius=2, pool_size=1)
+        digests[f"r2_b4_native_{grid[0]}"] = layout_digest(native)
+        digests[f"r2_b4_raster_{grid[0]}"] = layout_digest(native.repack(native.order.argsort()))
+        print("digest", grid, flush=True)
+    torch.save(digests, OUT / "layout_digests.pt")
+
+    # --- RoPE ---------------------------------------------------------------------------
+    rope = []
+    gen = torch.Generator().manual_seed(11)
+    for d in (16, 48, 64):
+        for dtype in ((torch.float64, torch.bfloat16) if d != 48 else (torch.float32, torch.bfloat16)):
+            coords = torch.randint(0, 40, (13, 3), generator=gen)
+            x = torch.randn(2, 3, 13, d, generator=gen).to(dtype)
+            rope.append({"x": x, "coords": coords, "pairs": balanced_pairs(d),
+                         "y": axial_rope(x, coords)})
+            packed = (d // 2, 0, 0)
+            seq = torch.arange(13)
+            pc = torch.stack((seq, torch.zeros_like(seq), torch.zeros_like(seq)), -1)
+            rope.append({"x": x, "coords": pc, "pairs": packed, "y": axial_rope(x, pc, pairs=packed)})
+    torch.save(rope, OUT / "rope.pt")
+
+    # --- pooling ------------------------------------------------------------------------
+    pools = []
+    for d, dtype in ((16, torch.float64), (48, torch.float32), (48, torch.bfloat16)):
+        n, volume, pool = 29, 4, 3
+        blocks = torch.full((8, volume), -1, dtype=torch.int32)
+        blocks.flatten()[:n] = torch.arange(n)
+        blocks = torch.cat((torch.full((1, volume), -1, dtype=torch.int32), blocks))   # empty fine block
+        geom = pack3d.prepare_geometry(torch.arange(n)[:, None].int(), blocks, pool)
+        k = torch.randn(2, 2, n, d, generator=gen).to(dtype)
+        v = torch.randn(2, 2, n, d, generator=gen).to(dtype)
+        w = (torch.randn(d, generator=gen) * 0.3).to(dtype)
+        bias = (torch.randn(volume, generator=gen) * 0.2).to(dtype)
+        sk, sv = compress_summaries(k, v, w, bias, geom, temperature=0.7)
+        pools.append({"k": k, "v": v, "w": w, "bias": bias, "blocks": blocks, "pool_size": pool,
+                      "temperature": 0.7, "sk": sk, "sv": sv})
+    torch.save(pools, OUT / "pool.pt")
+
+    # --- attention core on custom graphs --------------------------------------------------
+    for case in cases.CORE_CASES:
+        core_case(pack3d, *case)
+
+    # --- BASELINE-shaped grid pipeline (RoPE + pooling + core + every gradient) ------------
+    for case in cases.GRID_CASES:
+        grid_case(pack3d, *case)
+
+    # --- the public layer, backend "reference" --------------------------------------------
+    for dtype, tag in ((torch.float64, "f64"), (torch.float32, "f32")):
+        torch.manual_seed(52)
+        layout = pack3d.build_layout((4, 4, 4), pool_size=2)
+        layer = pack3d.PACK3DAttention(32, heads=2, kv_heads=1, head_dim=16).to(dtype)
+        x = torch.randn(1, 64, 32, dtype=dtype, requires_grad=True)
+        y = layer(x, layout)
+        dy = torch.randn_like(y)
+        grads = torch.autograd.grad(y, (x, *layer.parameters()), dy)
+        torch.save({"state": {k: v.detach().clone() for k, v in layer.state_dict().items()},
+                    "x": x.detach(), "y": y.detach(), "dy": dy, "grads": [t.detach() for t in grads],
+                    "names": ["x", *[name for name, _ in layer.named_parameters()]],
+                    "layout": layout_tables(layout), "heads": 2, "kv_heads": 1, "head_dim": 16},
+                   OUT / f"layer_{tag}.pt")
+    print("golden fixtures written to", OUT)
+
+
+if __name__ == "__main__":
+    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src"))
