@@ -1,0 +1,143 @@
+/*
+ * pack3d_b200 -- C ABI of the Blackwell (sm_100a) PACK3D operator library.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream and returns a
+ * p3d_status.  Nothing here allocates device memory: outputs, saved state
+ * and workspaces are provided by the caller (the Python host layer uses
+ * torch tensors for that).  No entry point aborts the process; on failure
+ * p3d_last_error() describes the problem (thread-local).
+ *
+ * Reference interfaces replaced (paths relative to the reference project):
+ *   p3d_rope           src/pack3d/backends/triton/rotary.py:94-106  rotate_projections()
+ *                      (kernel _rotate rotary.py:11-45, inverse for _Rotary.backward :66-70)
+ *   p3d_pool_fwd       src/pack3d/backends/triton/kernels.py:13-40  _pool
+ *   p3d_attn_fwd       src/pack3d/backends/triton/kernels.py:289-311 forward()
+ *   p3d_attn_bwd       src/pack3d/backends/triton/kernels.py:314-356 backward()
+ *   p3d_*_workspace    (no counterpart: the reference allocates scratch with torch.empty,
+ *                      kernels.py:275-277,319-351)
+ */
+#ifndef PACK3D_B200_H
+#define PACK3D_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define P3D_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define P3D_API __attribute__((visibility("default")))
+#else
+#define P3D_API
+#endif
+
+typedef enum {
+  P3D_OK = 0,
+  P3D_ERR_INVALID_ARGUMENT = 1, /* shape / dtype / pointer / limit violation */
+  P3D_ERR_UNSUPPORTED = 2,      /* valid input outside what the library implements */
+  P3D_ERR_CUDA = 3,             /* a CUDA runtime call or launch failed */
+  P3D_ERR_WORKSPACE = 4,        /* workspace pointer missing or too small */
+  P3D_ERR_DEVICE = 5            /* no usable sm_100 device */
+} p3d_status;
+
+typedef enum { P3D_F32 = 0, P3D_F16 = 1, P3D_BF16 = 2 } p3d_dtype;
+
+/* Attention-forward flags. */
+#define P3D_FWD_SAVE_STATE 1u   /* write ol, og, lse_l, lse_g for the backward */
+#define P3D_FWD_FORCE_INDEXED 2u /* use the indexed (neighbour-table) kernels even on a stencil */
+
+/* Static description string of a status code. */
+P3D_API const char *p3d_strerror(int status);
+/* Detail of the last failure on the calling thread ("" if none). */
+P3D_API const char *p3d_last_error(void);
+P3D_API int p3d_abi_version(void);
+/* Number of visible sm_100 devices (0 without a GPU); never fails. */
+P3D_API int p3d_device_count(void);
+
+/*
+ * Axial rotary embedding of a strided [B, H, N, D] tensor into a contiguous
+ * [B, H, N, D] output (same dtype).  Element (b,h,n,d) of x is read at
+ * x + b*sb + h*sh + n*sn + d*sd (strides in elements).  Pair i of axis a
+ * (axes z,y,x own pairs pz,py,px in that channel order, interleaved
+ * (even, odd)) turns by coord[n][a] * freqs[i] radians, where freqs holds the
+ * concatenated per-axis frequency vectors (pz + py + px floats) and
+ * coord[n][a] = coords[n*coord_sn + a*coord_sa].  If phases != NULL it holds
+ * (cos, sin) float pairs for every (axis, coordinate value, pair): axis a's
+ * block starts at entry sum_{a'<a} extent[a'] * pairs[a'] and coordinate c,
+ * pair i is entry start + c * pairs[a] + i; coordinates must then lie in
+ * [0, extent[a]).  packed != 0 uses the row index n as the axis-0 position
+ * (packed-sequence RoPE; pairs must be (D/2, 0, 0)).  inverse != 0 applies the
+ * transposed rotation (the backward).  Replaces rotary.py:94-106.
+ */
+P3D_API int p3d_rope(const void *x, int64_t sb, int64_t sh, int64_t sn, int64_t sd, void *out, int dtype,
+             int batch, int heads, int tokens, int head_dim, const int64_t *coords, int64_t coord_sn,
+             int64_t coord_sa, int pz, int py, int px, const float *freqs, const float *phases,
+             int ez, int ey, int ex, int packed, int inverse, void *stream);
+
+/*
+ * Two-stage summary pooling (compression.py:7-44, kernels.py:13-40):
+ * k, v [B, G, N, D] (dtype) -> sk, sv [B, G, M, D] (dtype), M = ceil(F / pool).
+ * blocks [F, V] int32 token rows (-1 = empty slot); weight [D], bias [V] fp32.
+ * If sk32/sv32 are non-NULL the fp32 summaries are written there as well.
+ */
+P3D_API int p3d_pool_fwd(const void *k, const void *v, const float *weight, const float *bias,
+                 const int32_t *blocks, int fine_blocks, int slots, int pool_size, void *sk, void *sv,
+                 float *sk32, float *sv32, int dtype, int batch, int kv_heads, int tokens, int head_dim,
+                 float temperature, void *stream);
+
+/* Operator arguments shared by forward and backward (all device pointers, contiguous). */
+typedef struct {
+  int32_t batch, heads, kv_heads, tokens, head_dim;
+  int32_t dtype;      /* p3d_dtype of q, kl, vl, kg, vg, y, ol, og, sk, sv, dq.. dvg */
+  int32_t gate_dtype; /* p3d_dtype of gate and dgate */
+  float temperature;
+  const void *q, *kl, *vl, *kg, *vg; /* q [B,H,N,D]; the others [B,G,N,D]; q/kl/kg rotated */
+  const float *pool_weight;          /* [D] */
+  const float *slot_bias;            /* [V] */
+  const void *gate;                  /* [B,H,N] */
+  const float *local_scale;          /* [D] */
+  const float *global_scale;         /* [D] */
+  /* geometry */
+  const int32_t *neighbors; /* [N, width], -1 pads */
+  int32_t width;
+  const int32_t *reverse_neighbors; /* [N, reverse_width] */
+  int32_t reverse_width;
+  const int32_t *blocks; /* [fine_blocks, slots] */
+  int32_t fine_blocks, slots, pool_size;
+  /* complete voxel stencil (optional): grid extents, radius, raster->packed row map */
+  int32_t stencil; /* nonzero when the neighbour table is the full radius stencil of the grid */
+  int32_t grid[3];
+  int32_t radius[3];
+  const int32_t *raster_to_packed; /* [N] or NULL for raster storage */
+} p3d_operator;
+
+/*
+ * Forward (kernels.py:289-311).  Writes y [B,H,N,D] and the summaries sk, sv
+ * [B,G,M,D].  With P3D_FWD_SAVE_STATE also ol, og [B,H,N,D] (dtype) and
+ * lse_l, lse_g [B,H,N] fp32 (all-masked local rows store +inf).
+ * workspace: p3d_attn_fwd_workspace() bytes (may be 0).
+ */
+P3D_API int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, void *og, float *lse_l,
+                 float *lse_g, unsigned flags, void *workspace, size_t workspace_bytes, void *stream);
+P3D_API size_t p3d_attn_fwd_workspace(const p3d_operator *op, unsigned flags);
+
+/*
+ * Backward (kernels.py:314-356) from the saved forward state.  Writes dq
+ * [B,H,N,D], dkl, dvl, dkg, dvg [B,G,N,D] (dtype), dgate [B,H,N] (gate_dtype)
+ * and fp32 dweight [D], dbias [V], dlocal_scale [D], dglobal_scale [D].
+ * Deterministic: no floating-point atomics, fixed reduction order.
+ */
+P3D_API int p3d_attn_bwd(const p3d_operator *op, const void *dy, const void *sk, const void *sv, const void *ol,
+                 const void *og, const float *lse_l, const float *lse_g, void *dq, void *dkl, void *dvl,
+                 void *dkg, void *dvg, void *dgate, float *dweight, float *dbias, float *dlocal_scale,
+                 float *dglobal_scale, void *workspace, size_t workspace_bytes, void *stream);
+P3D_API size_t p3d_attn_bwd_workspace(const p3d_operator *op);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PACK3D_B200_H */

@@ -1,0 +1,81 @@
+"""The PACK3D attention layer with the B200 backend.
+
+Same constructor, parameters (and therefore state-dict names) and forward as
+the reference's ``src/pack3d/attention.py:12-89``: LayerNorm, Q and 4-way KV
+projections (cuBLAS through PyTorch), axial or packed-sequence RoPE of q /
+local k / global k, the 2-way gate softmax, the core, the output projection
+and the outer residual.  RoPE and the core run in ``libpack3d_b200.so``.
+The only backend is ``"b200"``: an explicit request that never falls back.
+"""
+import math
+
+import torch
+from torch import nn
+
+from ._validation import HEAD_DIMS, check_cuda
+from .geometry import TokenLayout
+from .ops import pack3d_streamed
+from .rope import balanced_pairs, rotate_projections
+
+
+class PACK3DAttention(nn.Module):
+    """Local residual plus gated compressed attention and an outer residual.
+
+    Input / output ``[batch, packed_tokens, dim]``; the layout travels with the
+    tokens.  Separate local / global K/V projections, one learned fine atom,
+    two-stage compression.
+    """
+
+    def __init__(self, dim, *, heads=4, kv_heads=2, head_dim=32, block_volume=8, backend="b200",
+                 position_encoding="axial", temperature=1.0):
+        super().__init__()
+        if any(type(v) is not int or v <= 0 for v in (dim, heads, kv_heads, head_dim, block_volume)):
+            raise ValueError("dimensions must be positive integers")
+        if heads % kv_heads or head_dim not in HEAD_DIMS or block_volume > 64:
+            raise ValueError("unsupported grouped-head dimensions or block volume")
+        if backend != "b200":
+            raise ValueError("backend must be explicitly b200")
+        if position_encoding not in ("axial", "packed"):
+            raise ValueError("position_encoding must be axial or packed")
+        if not math.isfinite(temperature) or temperature <= 0:
+            raise ValueError("temperature must be finite and positive")
+        self.dim, self.heads, self.kv_heads, self.head_dim = dim, heads, kv_heads, head_dim
+        self.backend, self.position_encoding = backend, position_encoding
+        self.temperature = float(temperature)
+        self.norm = nn.LayerNorm(dim)
+        self.to_q = nn.Linear(dim, heads * head_dim, bias=False)
+        self.to_kv = nn.Linear(dim, 4 * kv_heads * head_dim, bias=False)
+        self.pool_weight = nn.Parameter(torch.empty(head_dim))
+        nn.init.uniform_(self.pool_weight, -1 / math.sqrt(head_dim), 1 / math.sqrt(head_dim))
+        self.slot_bias = nn.Parameter(torch.empty(block_volume))
+        nn.init.normal_(self.slot_bias, std=0.02)
+        self.gate = nn.Linear(dim, heads * 2)
+        nn.init.zeros_(self.gate.bias)
+        self.local_scale = nn.Parameter(torch.ones(head_dim))
+        self.global_scale = nn.Parameter(torch.full((head_dim,), 0.25))
+        self.to_out = nn.Linear(heads * head_dim, dim, bias=False)
+
+    def forward(self, x, layout: TokenLayout):
+        layout.check_unmodified()
+        if x.ndim != 3 or x.shape[0] == 0 or x.shape[1:] != (layout.geometry.num_tokens, self.dim):
+            raise ValueError("x must be [batch,layout_tokens,dim] with a nonempty batch")
+        if x.device != layout.coords.device:
+            raise ValueError("x and layout are on different devices; move both with .to(device)")
+        if layout.geometry.blocks.shape[1] != len(self.slot_bias):
+            raise ValueError("layout canonical slot count must match block_volume")
+        if self.backend != "b200":
+            raise ValueError("unknown backend; implicit fallback is disabled")
+        residual, b, n = x, x.shape[0], x.shape[1]
+        x = self.norm(x)
+        q = self.to_q(x).reshape(b, n, self.heads, self.head_dim).transpose(1, 2)
+        kl, vl, kg, vg = (t.reshape(b, n, self.kv_heads, self.head_dim).transpose(1, 2)
+                          for t in self.to_kv(x).chunk(4, -1))
+        check_cuda(q)
+        packed = self.position_encoding == "packed"
+        pairs = (self.head_dim // 2, 0, 0) if packed else balanced_pairs(self.head_dim)
+        q, kl, kg = rotate_projections(q, kl, kg, layout.coords, pairs, layout.grid_shape, packed=packed)
+        gates = self.gate(x).reshape(b, n, self.heads, 2).softmax(-1)
+        gate = gates[..., 1].transpose(1, 2)
+        out = pack3d_streamed(q, kl, vl, kg, vg, self.pool_weight, self.slot_bias, gate, self.local_scale,
+                              self.global_scale, layout.geometry, temperature=self.temperature)
+        return residual + self.to_out(out.transpose(1, 2).reshape(b, n, -1))

@@ -1,0 +1,447 @@
+// C ABI entry points: argument validation, workspace layout and stage dispatch.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace p3d {
+
+static thread_local char g_last_error[512] = "";
+
+void set_error(const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int status, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int device_info(DeviceInfo *info) {
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  static bool filled[64] = {};
+  int dev = 0;
+  P3D_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(P3D_ERR_DEVICE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!filled[dev]) {
+    cudaDeviceProp prop;
+    P3D_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+    cache[dev].sm_count = prop.multiProcessorCount;
+    cache[dev].major = prop.major;
+    cache[dev].minor = prop.minor;
+    cache[dev].smem_optin = prop.sharedMemPerBlockOptin;
+    filled[dev] = true;
+  }
+  *info = cache[dev];
+  return P3D_OK;
+}
+
+namespace {
+
+// Bump allocator over a caller-provided workspace (256-byte aligned slices).
+struct Carver {
+  char *base;
+  size_t used = 0, cap;
+  Carver(void *b, size_t c) : base(static_cast<char *>(b)), cap(c) {}
+  template <typename T>
+  T *take(size_t count) {
+    used = (used + 255) & ~size_t(255);
+    T *p = base ? reinterpret_cast<T *>(base + used) : nullptr;
+    used += count * sizeof(T);
+    return p;
+  }
+  bool ok() const { return base != nullptr && used <= cap; }
+};
+
+int summaries_of(const p3d_operator *op) { return (op->fine_blocks + op->pool_size - 1) / op->pool_size; }
+
+int validate(const p3d_operator *op) {
+  P3D_CHECK_ARG(op != nullptr, "null operator descriptor");
+  P3D_CHECK_ARG(dtype_ok(op->dtype) && dtype_ok(op->gate_dtype), "unknown dtype");
+  P3D_CHECK_ARG(op->batch >= 1 && op->heads >= 1 && op->tokens >= 1 && op->kv_heads >= 1,
+                "batch, heads, kv_heads and tokens must be positive");
+  P3D_CHECK_ARG(op->heads % op->kv_heads == 0, "query heads must be divisible by KV heads");
+  P3D_CHECK_ARG(op->head_dim >= 2 && op->head_dim <= 128 && op->head_dim % 2 == 0,
+                "head_dim %d unsupported (even, <= 128)", op->head_dim);
+  P3D_CHECK_ARG(op->temperature > 0.f && op->temperature < __builtin_huge_valf(),
+                "temperature must be finite and positive");
+  P3D_CHECK_ARG(op->width >= 1 && op->width <= 128, "neighbour width must be in [1,128]");
+  P3D_CHECK_ARG(op->slots >= 1 && op->slots <= 64, "fine-block slots must be in [1,64]");
+  P3D_CHECK_ARG(op->pool_size >= 1 && op->pool_size <= 32, "pool_size must be in [1,32]");
+  P3D_CHECK_ARG(op->fine_blocks >= 1, "no fine blocks");
+  P3D_CHECK_ARG(op->q && op->kl && op->vl && op->kg && op->vg && op->gate, "null input tensor");
+  P3D_CHECK_ARG(op->pool_weight && op->slot_bias && op->local_scale && op->global_scale, "null parameter");
+  P3D_CHECK_ARG(op->neighbors && op->blocks, "null geometry table");
+  P3D_CHECK_ARG((int64_t)op->batch * op->heads * op->tokens * op->head_dim < (int64_t(1) << 40),
+                "tensor too large");
+  if (op->stencil) {
+    P3D_CHECK_ARG(op->grid[0] >= 1 && op->grid[1] >= 1 && op->grid[2] >= 1, "bad stencil grid");
+    P3D_CHECK_ARG((int64_t)op->grid[0] * op->grid[1] * op->grid[2] == op->tokens,
+                  "stencil grid does not match the token count");
+    P3D_CHECK_ARG(op->radius[0] >= 0 && op->radius[1] >= 0 && op->radius[2] >= 0, "bad stencil radius");
+  }
+  return P3D_OK;
+}
+
+IndexedArgs indexed_args(const p3d_operator *op, const void *sk, const void *sv) {
+  IndexedArgs a{};
+  a.dtype = op->dtype;
+  a.gate_dtype = op->gate_dtype;
+  a.batch = op->batch;
+  a.heads = op->heads;
+  a.kv_heads = op->kv_heads;
+  a.tokens = op->tokens;
+  a.head_dim = op->head_dim;
+  a.summaries = summaries_of(op);
+  a.q = op->q;
+  a.kl = op->kl;
+  a.vl = op->vl;
+  a.sk = sk;
+  a.sv = sv;
+  a.neighbors = op->neighbors;
+  a.width = op->width;
+  a.reverse = op->reverse_neighbors;
+  a.reverse_width = op->reverse_width;
+  a.gate = op->gate;
+  a.sl = op->local_scale;
+  a.sg = op->global_scale;
+  return a;
+}
+
+PoolArgs pool_args(const p3d_operator *op, void *sk, void *sv) {
+  PoolArgs p{};
+  p.k = op->kg;
+  p.v = op->vg;
+  p.weight = op->pool_weight;
+  p.bias = op->slot_bias;
+  p.blocks = op->blocks;
+  p.fine_blocks = op->fine_blocks;
+  p.slots = op->slots;
+  p.pool_size = op->pool_size;
+  p.summaries = summaries_of(op);
+  p.sk = sk;
+  p.sv = sv;
+  p.dtype = op->dtype;
+  p.bg = op->batch * op->kv_heads;
+  p.tokens = op->tokens;
+  p.head_dim = op->head_dim;
+  p.temperature = op->temperature;
+  p.vec = dtype_size(op->dtype) == 2 && op->head_dim % 8 == 0 && ((uintptr_t)op->kg & 15) == 0 &&
+          ((uintptr_t)op->vg & 15) == 0;
+  return p;
+}
+
+bool use_stencil_path(const p3d_operator *op, unsigned flags) {
+  if (flags & P3D_FWD_FORCE_INDEXED) return false;
+  if (!op->stencil) return false;
+  return stencil_fwd_supported(op->dtype, op->head_dim, op->radius, summaries_of(op));
+}
+
+// Forward workspace: indexed path needs an ol buffer when the caller saves no state;
+// the stencil path needs raster-ordered copies of q, kl, vl when storage is permuted.
+size_t fwd_layout(const p3d_operator *op, unsigned flags, void *base, size_t cap, void **ol_ws,
+                  void **q_r, void **kl_r, void **vl_r) {
+  Carver c(base, cap);
+  const size_t es = dtype_size(op->dtype);
+  const size_t q_elems = (size_t)op->batch * op->heads * op->tokens * op->head_dim;
+  const size_t kv_elems = (size_t)op->batch * op->kv_heads * op->tokens * op->head_dim;
+  if (use_stencil_path(op, flags)) {
+    if (op->raster_to_packed) {
+      *q_r = c.take<char>(q_elems * es);
+      *kl_r = c.take<char>(kv_elems * es);
+      *vl_r = c.take<char>(kv_elems * es);
+    }
+  } else if (!(flags & P3D_FWD_SAVE_STATE)) {
+    *ol_ws = c.take<char>(q_elems * es);
+  }
+  return c.used;
+}
+
+// dst[r, :] = src[map[r], :] for every (batch*head) slab: gathers packed rows into raster order.
+__global__ void gather_rows_kernel(const uint4 *src, uint4 *dst, const int32_t *map, int64_t slabs,
+                                   int tokens, int row_vecs) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = slabs * tokens * row_vecs;
+  if (t >= total) return;
+  const int v = (int)(t % row_vecs);
+  const int64_t rest = t / row_vecs;
+  const int r = (int)(rest % tokens);
+  const int64_t slab = rest / tokens;
+  dst[(slab * tokens + r) * row_vecs + v] = src[(slab * tokens + map[r]) * row_vecs + v];
+}
+
+int gather_rows(const void *src, void *dst, const int32_t *map, int64_t slabs, int tokens, size_t row_bytes,
+                cudaStream_t s) {
+  if (row_bytes % 16 || ((uintptr_t)src & 15) || ((uintptr_t)dst & 15))
+    return fail(P3D_ERR_UNSUPPORTED, "row gather needs 16-byte rows");
+  const int row_vecs = (int)(row_bytes / 16);
+  const int64_t total = slabs * tokens * row_vecs;
+  if (!total) return P3D_OK;
+  gather_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
+      static_cast<const uint4 *>(src), static_cast<uint4 *>(dst), map, slabs, tokens, row_vecs);
+  P3D_LAUNCH_CHECK();
+  return P3D_OK;
+}
+
+struct BwdBuffers {
+  void *dol, *dog;
+  float *delta_l, *delta_g, *dsl_part, *dsg_part, *dk_part, *dv_part, *dsk, *dsv, *dw_part, *db_part, *tmp;
+  int64_t mix_rows, pool_rows;
+  int splits;
+};
+
+size_t bwd_layout(const p3d_operator *op, void *base, size_t cap, BwdBuffers *b) {
+  Carver c(base, cap);
+  const size_t es = dtype_size(op->dtype);
+  const int M = summaries_of(op);
+  const int64_t rows = (int64_t)op->batch * op->heads * op->tokens;
+  const int64_t bh = (int64_t)op->batch * op->heads;
+  const int64_t bg = (int64_t)op->batch * op->kv_heads;
+  const int chunk = mix_bwd_chunk_rows();
+  b->mix_rows = bh * ((op->tokens + chunk - 1) / chunk);
+  b->pool_rows = bg * M;
+  b->splits = global_dkv_splits(op->tokens);
+  const int64_t d = op->head_dim;
+  b->dol = c.take<char>(rows * d * es);
+  b->dog = c.take<char>(rows * d * es);
+  b->delta_l = c.take<float>(rows);
+  b->delta_g = c.take<float>(rows);
+  b->dsl_part = c.take<float>(b->mix_rows * d);
+  b->dsg_part = c.take<float>(b->mix_rows * d);
+  b->dk_part = c.take<float>(bg * b->splits * M * d);
+  b->dv_part = c.take<float>(bg * b->splits * M * d);
+  b->dsk = c.take<float>(bg * M * d);
+  b->dsv = c.take<float>(bg * M * d);
+  b->dw_part = c.take<float>(b->pool_rows * d);
+  b->db_part = c.take<float>(b->pool_rows * op->slots);
+  const int64_t tmp = std::max({sum_rows_tmp(b->mix_rows, d), sum_rows_tmp(b->pool_rows, d),
+                                sum_rows_tmp(b->pool_rows, op->slots)});
+  b->tmp = c.take<float>(tmp);
+  return c.used;
+}
+
+}  // namespace
+}  // namespace p3d
+
+using namespace p3d;
+
+extern "C" {
+
+const char *p3d_strerror(int status) {
+  switch (status) {
+    case P3D_OK: return "success";
+    case P3D_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case P3D_ERR_UNSUPPORTED: return "unsupported input";
+    case P3D_ERR_CUDA: return "CUDA error";
+    case P3D_ERR_WORKSPACE: return "workspace missing or too small";
+    case P3D_ERR_DEVICE: return "no usable device";
+    default: return "unknown status";
+  }
+}
+
+const char *p3d_last_error(void) { return g_last_error; }
+
+int p3d_abi_version(void) { return P3D_ABI_VERSION; }
+
+int p3d_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  int count = 0;
+  for (int i = 0; i < n; ++i) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, i) == cudaSuccess && prop.major == 10) ++count;
+  }
+  return count;
+}
+
+int p3d_pool_fwd(const void *k, const void *v, const float *weight, const float *bias, const int32_t *blocks,
+                 int fine_blocks, int slots, int pool_size, void *sk, void *sv, float *sk32, float *sv32,
+                 int dtype, int batch, int kv_heads, int tokens, int head_dim, float temperature,
+                 void *stream) {
+  P3D_CHECK_ARG(dtype_ok(dtype), "p3d_pool_fwd: unknown dtype");
+  P3D_CHECK_ARG(k && v && weight && bias && blocks && sk && sv, "p3d_pool_fwd: null pointer");
+  P3D_CHECK_ARG(slots >= 1 && slots <= 64 && pool_size >= 1 && pool_size <= 32 && fine_blocks >= 1,
+                "p3d_pool_fwd: bad block table");
+  P3D_CHECK_ARG(head_dim >= 1 && head_dim <= 128, "p3d_pool_fwd: head_dim must be in [1,128]");
+  P3D_CHECK_ARG(temperature > 0.f, "p3d_pool_fwd: temperature must be positive");
+  PoolArgs p{};
+  p.k = k; p.v = v; p.weight = weight; p.bias = bias; p.blocks = blocks;
+  p.fine_blocks = fine_blocks; p.slots = slots; p.pool_size = pool_size;
+  p.summaries = (fine_blocks + pool_size - 1) / pool_size;
+  p.sk = sk; p.sv = sv; p.sk32 = sk32; p.sv32 = sv32;
+  p.dtype = dtype; p.bg = batch * kv_heads; p.tokens = tokens; p.head_dim = head_dim;
+  p.temperature = temperature;
+  p.vec = dtype_size(dtype) == 2 && head_dim % 8 == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0;
+  return launch_pool_fwd(p, static_cast<cudaStream_t>(stream));
+}
+
+size_t p3d_attn_fwd_workspace(const p3d_operator *op, unsigned flags) {
+  if (validate(op) != P3D_OK) return 0;
+  void *a = nullptr, *b = nullptr, *c = nullptr, *d = nullptr;
+  return fwd_layout(op, flags, nullptr, 0, &a, &b, &c, &d);
+}
+
+int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, void *og, float *lse_l,
+                 float *lse_g, unsigned flags, void *workspace, size_t workspace_bytes, void *stream) {
+  if (int st = validate(op)) return st;
+  P3D_CHECK_ARG(y && sk && sv, "p3d_attn_fwd: y, sk and sv are required");
+  const bool save = flags & P3D_FWD_SAVE_STATE;
+  P3D_CHECK_ARG(!save || (ol && og && lse_l && lse_g), "p3d_attn_fwd: saving state needs ol, og, lse_l, lse_g");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void *ol_ws = nullptr, *q_r = nullptr, *kl_r = nullptr, *vl_r = nullptr;
+  const size_t need = fwd_layout(op, flags, nullptr, 0, &ol_ws, &q_r, &kl_r, &vl_r);
+  if (need > 0) {
+    if (!workspace || workspace_bytes < need)
+      return fail(P3D_ERR_WORKSPACE, "p3d_attn_fwd: workspace of %zu bytes required", need);
+    fwd_layout(op, flags, workspace, workspace_bytes, &ol_ws, &q_r, &kl_r, &vl_r);
+  }
+  if (int st = launch_pool_fwd(pool_args(op, sk, sv), s)) return st;
+  if (use_stencil_path(op, flags)) {
+    StencilFwdArgs a{};
+    a.dtype = op->dtype;
+    a.gate_dtype = op->gate_dtype;
+    a.batch = op->batch;
+    a.heads = op->heads;
+    a.kv_heads = op->kv_heads;
+    a.head_dim = op->head_dim;
+    a.summaries = summaries_of(op);
+    for (int i = 0; i < 3; ++i) a.grid[i] = op->grid[i];
+    a.q = op->q;
+    a.kl = op->kl;
+    a.vl = op->vl;
+    if (op->raster_to_packed) {
+      const size_t row_bytes = (size_t)op->head_dim * dtype_size(op->dtype);
+      if (int st = gather_rows(op->q, q_r, op->raster_to_packed, (int64_t)op->batch * op->heads, op->tokens,
+                               row_bytes, s))
+        return st;
+      if (int st = gather_rows(op->kl, kl_r, op->raster_to_packed, (int64_t)op->batch * op->kv_heads,
+                               op->tokens, row_bytes, s))
+        return st;
+      if (int st = gather_rows(op->vl, vl_r, op->raster_to_packed, (int64_t)op->batch * op->kv_heads,
+                               op->tokens, row_bytes, s))
+        return st;
+      a.q = q_r;
+      a.kl = kl_r;
+      a.vl = vl_r;
+    }
+    a.raster_to_packed = op->raster_to_packed;
+    a.sk = sk;
+    a.sv = sv;
+    a.gate = op->gate;
+    a.sl = op->local_scale;
+    a.sg = op->global_scale;
+    a.y = y;
+    a.ol = save ? ol : nullptr;
+    a.og = save ? og : nullptr;
+    a.lse_l = save ? lse_l : nullptr;
+    a.lse_g = save ? lse_g : nullptr;
+    return launch_stencil_fwd(a, s);
+  }
+  const IndexedArgs a = indexed_args(op, sk, sv);
+  void *ol_buf = save ? ol : ol_ws;
+  if (int st = launch_local_fwd_indexed(a, ol_buf, save ? lse_l : nullptr, s)) return st;
+  return launch_global_fwd_mix(a, ol_buf, y, save ? og : nullptr, save ? lse_g : nullptr, s);
+}
+
+size_t p3d_attn_bwd_workspace(const p3d_operator *op) {
+  if (validate(op) != P3D_OK) return 0;
+  BwdBuffers b;
+  return bwd_layout(op, nullptr, 0, &b);
+}
+
+int p3d_attn_bwd(const p3d_operator *op, const void *dy, const void *sk, const void *sv, const void *ol,
+                 const void *og, const float *lse_l, const float *lse_g, void *dq, void *dkl, void *dvl, void *dkg,
+                 void *dvg, void *dgate, float *dweight, float *dbias, float *dlocal_scale, float *dglobal_scale,
+                 void *workspace, size_t workspace_bytes, void *stream) {
+  if (int st = validate(op)) return st;
+  P3D_CHECK_ARG(dy && sk && sv && ol && og && lse_l && lse_g, "p3d_attn_bwd: missing saved state");
+  P3D_CHECK_ARG(dq && dkl && dvl && dkg && dvg && dgate && dweight && dbias && dlocal_scale && dglobal_scale,
+                "p3d_attn_bwd: missing gradient output");
+  P3D_CHECK_ARG(op->reverse_neighbors && op->reverse_width >= 1 && op->reverse_width <= 128,
+                "p3d_attn_bwd: reverse adjacency required");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  BwdBuffers b;
+  const size_t need = bwd_layout(op, nullptr, 0, &b);
+  if (!workspace || workspace_bytes < need)
+    return fail(P3D_ERR_WORKSPACE, "p3d_attn_bwd: workspace of %zu bytes required", need);
+  bwd_layout(op, workspace, workspace_bytes, &b);
+  const int d = op->head_dim, M = summaries_of(op);
+  const int64_t bh = (int64_t)op->batch * op->heads, bg = (int64_t)op->batch * op->kv_heads;
+
+  MixBwdArgs mix{};
+  mix.dtype = op->dtype;
+  mix.gate_dtype = op->gate_dtype;
+  mix.bh = (int)bh;
+  mix.tokens = op->tokens;
+  mix.head_dim = d;
+  mix.chunk_rows = mix_bwd_chunk_rows();
+  mix.dy = dy;
+  mix.ol = ol;
+  mix.og = og;
+  mix.gate = op->gate;
+  mix.sl = op->local_scale;
+  mix.sg = op->global_scale;
+  mix.dol = b.dol;
+  mix.dog = b.dog;
+  mix.delta_l = b.delta_l;
+  mix.delta_g = b.delta_g;
+  mix.dgate = dgate;
+  mix.dsl_part = b.dsl_part;
+  mix.dsg_part = b.dsg_part;
+  if (int st = launch_mix_bwd(mix, s)) return st;
+
+  const IndexedArgs a = indexed_args(op, sk, sv);
+  if (int st = launch_local_dq_indexed(a, b.dol, lse_l, b.delta_l, dq, s)) return st;
+  if (int st = launch_local_dkv_indexed(a, b.dol, lse_l, b.delta_l, dkl, dvl, s)) return st;
+  if (int st = launch_global_dq(a, b.dog, lse_g, b.delta_g, dq, s)) return st;
+  if (int st = launch_global_dkv(a, b.dog, lse_g, b.delta_g, b.splits, b.dk_part, b.dv_part, s)) return st;
+  if (int st = launch_sum_middle(b.dk_part, b.dsk, bg, b.splits, (int64_t)M * d, s)) return st;
+  if (int st = launch_sum_middle(b.dv_part, b.dsv, bg, b.splits, (int64_t)M * d, s)) return st;
+
+  PoolBwdArgs pb{};
+  pb.k = op->kg;
+  pb.v = op->vg;
+  pb.weight = op->pool_weight;
+  pb.bias = op->slot_bias;
+  pb.blocks = op->blocks;
+  pb.fine_blocks = op->fine_blocks;
+  pb.slots = op->slots;
+  pb.pool_size = op->pool_size;
+  pb.summaries = M;
+  pb.dsk = b.dsk;
+  pb.dsv = b.dsv;
+  pb.dk = dkg;
+  pb.dv = dvg;
+  pb.dw_part = b.dw_part;
+  pb.db_part = b.db_part;
+  pb.dtype = op->dtype;
+  pb.bg = (int)bg;
+  pb.tokens = op->tokens;
+  pb.head_dim = d;
+  pb.temperature = op->temperature;
+  pb.vec = pool_args(op, nullptr, nullptr).vec;
+  if (int st = launch_pool_bwd(pb, s)) return st;
+
+  if (int st = launch_sum_rows(b.dw_part, dweight, b.pool_rows, d, b.tmp, s)) return st;
+  if (int st = launch_sum_rows(b.db_part, dbias, b.pool_rows, op->slots, b.tmp, s)) return st;
+  if (int st = launch_sum_rows(b.dsl_part, dlocal_scale, b.mix_rows, d, b.tmp, s)) return st;
+  if (int st = launch_sum_rows(b.dsg_part, dglobal_scale, b.mix_rows, d, b.tmp, s)) return st;
+  return P3D_OK;
+}
+
+}  // extern "C"

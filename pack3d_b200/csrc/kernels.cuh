@@ -1,0 +1,105 @@
+// Internal launch interfaces between the C ABI (capi.cu) and the kernel files.
+#pragma once
+
+#include "common.cuh"
+
+namespace p3d {
+
+struct PoolArgs {
+  const void *k, *v;  // [BG, N, D]
+  const float *weight, *bias;
+  const int32_t *blocks;
+  int fine_blocks, slots, pool_size, summaries;
+  void *sk, *sv;      // [BG, M, D] dtype
+  float *sk32, *sv32; // optional fp32 copies
+  int dtype, bg, tokens, head_dim;
+  float temperature;
+  bool vec;           // 16-byte row loads allowed
+};
+int launch_pool_fwd(const PoolArgs &p, cudaStream_t stream);
+
+struct PoolBwdArgs {
+  const void *k, *v;
+  const float *weight, *bias;
+  const int32_t *blocks;
+  int fine_blocks, slots, pool_size, summaries;
+  const float *dsk, *dsv;  // [BG, M, D] fp32
+  void *dk, *dv;           // [BG, N, D] dtype
+  float *dw_part;          // [BG*M, D]
+  float *db_part;          // [BG*M, V]
+  int dtype, bg, tokens, head_dim;
+  float temperature;
+  bool vec;
+};
+int launch_pool_bwd(const PoolBwdArgs &p, cudaStream_t stream);
+
+// ---- indexed (neighbour-table) kernels: every dtype, every head_dim <= 128 --------------
+struct IndexedArgs {
+  int dtype, gate_dtype;
+  int batch, heads, kv_heads, tokens, head_dim, summaries;
+  const void *q, *kl, *vl, *sk, *sv;    // sk, sv [B,G,M,D] dtype
+  const int32_t *neighbors;
+  int width;
+  const int32_t *reverse;
+  int reverse_width;
+  const void *gate;
+  const float *sl, *sg;
+};
+
+// Local branch forward: ol [B,H,N,D] dtype, lse_l [B,H,N] fp32 (nullable; +inf for all-masked rows).
+int launch_local_fwd_indexed(const IndexedArgs &a, void *ol, float *lse_l, cudaStream_t s);
+// Global branch forward + mix: y, og (nullable), lse_g (nullable).
+int launch_global_fwd_mix(const IndexedArgs &a, const void *ol, void *y, void *og, float *lse_g,
+                          cudaStream_t s);
+
+// Backward pieces.
+struct MixBwdArgs {
+  int dtype, gate_dtype, bh, tokens, head_dim, chunk_rows;
+  const void *dy, *ol, *og, *gate;
+  const float *sl, *sg;
+  void *dol, *dog;         // dtype
+  float *delta_l, *delta_g;
+  void *dgate;             // gate dtype
+  float *dsl_part, *dsg_part;  // [bh * ceil(N/chunk_rows), D]
+};
+int launch_mix_bwd(const MixBwdArgs &a, cudaStream_t s);
+inline int mix_bwd_chunk_rows() { return 128; }
+
+int launch_local_dq_indexed(const IndexedArgs &a, const void *dol, const float *lse_l, const float *delta_l,
+                            void *dq, cudaStream_t s);
+int launch_local_dkv_indexed(const IndexedArgs &a, const void *dol, const float *lse_l, const float *delta_l,
+                             void *dkl, void *dvl, cudaStream_t s);
+// Adds the global-branch dQ into dq (which holds the local-branch dQ).
+int launch_global_dq(const IndexedArgs &a, const void *dog, const float *lse_g, const float *delta_g, void *dq,
+                     cudaStream_t s);
+// Global-branch dSK / dSV split partials [B*G, splits, M, D] fp32.
+int launch_global_dkv(const IndexedArgs &a, const void *dog, const float *lse_g, const float *delta_g,
+                      int splits, float *dk_part, float *dv_part, cudaStream_t s);
+inline int global_dkv_splits(int tokens) {
+  int s = (tokens + 1023) / 1024;
+  return s < 1 ? 1 : (s > 32 ? 32 : s);
+}
+
+// Deterministic reductions.
+// out[a, c] = sum_{s < S} in[(a * S + s) * C + c]
+int launch_sum_middle(const float *in, float *out, int64_t outer, int S, int64_t C, cudaStream_t s);
+// out[c] = sum_{r < R} in[r * C + c]; tmp needs ceil(R / 256) * C floats.
+int launch_sum_rows(const float *in, float *out, int64_t R, int64_t C, float *tmp, cudaStream_t s);
+inline int64_t sum_rows_tmp(int64_t R, int64_t C) { return ((R + 255) / 256) * C; }
+
+// ---- tensor-core (tcgen05) fused forward on complete voxel stencils --------------------
+struct StencilFwdArgs {
+  int dtype, gate_dtype;
+  int batch, heads, kv_heads, head_dim, summaries;
+  int grid[3];
+  const void *q, *kl, *vl, *sk, *sv;  // q/kl/vl in raster order (contiguous [B,H|G,Z,Y,X,D])
+  const int32_t *raster_to_packed;    // output row map (NULL = raster)
+  const void *gate;
+  const float *sl, *sg;
+  void *y, *ol, *og;                  // ol/og nullable
+  float *lse_l, *lse_g;               // nullable
+};
+bool stencil_fwd_supported(int dtype, int head_dim, const int radius[3], int summaries);
+int launch_stencil_fwd(const StencilFwdArgs &a, cudaStream_t s);
+
+}  // namespace p3d

@@ -1,0 +1,98 @@
+"""The C-ABI library builds, loads without a GPU and exports every declared symbol.
+
+No compute entry point is called here (there may be no device); the product's
+CUDA requirement is checked to fail loudly instead of falling back.
+"""
+import re
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared():
+    names = set()
+    for header in (ROOT / "include").glob("*.h"):
+        names |= set(re.findall(r"P3D_API\s+[\w\s\*]*?\b(p3d_\w+)\s*\(", header.read_text()))
+    return names
+
+
+def test_header_declares_entry_points():
+    assert {"p3d_rope", "p3d_pool_fwd", "p3d_attn_fwd", "p3d_attn_bwd"} <= _declared()
+
+
+def test_library_exports_every_declared_symbol():
+    from pack3d_b200 import _native
+    handle = _native.lib()
+    nm = subprocess.run(["nm", "-D", "--defined-only", str(_native.LIB_PATH)], capture_output=True, text=True)
+    exported = set(re.findall(r"\bT (p3d_\w+)", nm.stdout))
+    missing = _declared() - exported
+    assert not missing, missing
+    for name in _declared():
+        assert getattr(handle, name) is not None
+    assert set(_native.exported_symbols()) == _declared()
+
+
+def test_library_metadata_calls():
+    from pack3d_b200 import _native
+    handle = _native.lib()
+    assert handle.p3d_abi_version() == 1
+    assert handle.p3d_strerror(0) == b"success"
+    assert handle.p3d_strerror(4).startswith(b"workspace")
+    assert handle.p3d_device_count() >= 0
+
+
+def test_struct_layout_matches_header():
+    """ctypes mirror of p3d_operator has the C layout (checked with the host compiler)."""
+    from pack3d_b200 import _native
+    src = ROOT / "include" / "pack3d_b200.h"
+    probe = ('#include <stddef.h>\n#include <stdio.h>\n#include "%s"\nint main(void){printf("%%zu %%zu %%zu\\n",'
+             ' sizeof(p3d_operator), offsetof(p3d_operator, blocks), offsetof(p3d_operator, raster_to_packed));}'
+             % src)
+    exe = Path(__file__).resolve().parent / ".struct_probe"
+    run = subprocess.run(["gcc", "-x", "c", "-", "-o", str(exe)], input=probe, text=True, capture_output=True)
+    assert run.returncode == 0, run.stderr
+    try:
+        out = subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()
+    finally:
+        exe.unlink(missing_ok=True)
+    op = _native.Operator
+    assert [int(v) for v in out] == [ctypes_size(op), op.blocks.offset, op.raster_to_packed.offset]
+
+
+def ctypes_size(t):
+    import ctypes
+    return ctypes.sizeof(t)
+
+
+def test_cpu_tensors_are_refused_not_computed():
+    from pack3d_b200 import build_layout, pack3d_streamed
+    layout = build_layout((4, 4, 4), (4, 4, 4), radius=2, pool_size=1)
+    g = layout.geometry
+    q = torch.randn(1, 1, 64, 48)
+    args = (q, q, q, q, q, torch.zeros(48), torch.zeros(64), torch.zeros(1, 1, 64), torch.ones(48), torch.ones(48))
+    with pytest.raises(ValueError, match="CUDA"):
+        pack3d_streamed(*args, g)
+    with pytest.raises(ValueError, match="backend"):
+        pack3d_streamed(*args, g, backend="triton")
+
+
+def test_layer_rejects_unsupported():
+    from pack3d_b200 import PACK3DAttention
+    for kwargs in ({"heads": 3}, {"temperature": 0}, {"backend": "reference"}, {"position_encoding": "none"},
+                   {"head_dim": 40}):
+        with pytest.raises(ValueError):
+            PACK3DAttention(32, **kwargs)
+    layer = PACK3DAttention(192, heads=4, kv_heads=4, head_dim=48, block_volume=64)
+    assert [n for n, _ in layer.named_parameters()] == [
+        "pool_weight", "slot_bias", "local_scale", "global_scale", "norm.weight", "norm.bias",
+        "to_q.weight", "to_kv.weight", "gate.weight", "gate.bias", "to_out.weight"]
+
+
+def test_import_does_not_pull_the_oracle():
+    code = "import sys, pack3d_b200; assert 'oracle' not in sys.modules; assert 'triton' not in sys.modules"
+    subprocess.run([sys.executable, "-c", code], check=True, cwd=str(ROOT))
