@@ -45,6 +45,7 @@ _SIGNATURES = {
     "p3d_last_error": (ctypes.c_char_p, []),
     "p3d_abi_version": (_c_int, []),
     "p3d_device_count": (_c_int, []),
+    "p3d_device_errors": (_c_int, [ctypes.POINTER(ctypes.c_uint)]),
     "p3d_rope": (_c_int, [_vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                           _vp, _c_i64, _c_i64, _c_int, _c_int, _c_int, _vp, _vp, _c_int, _c_int, _c_int,
                           _c_int, _c_int, _vp]),
@@ -95,6 +96,13 @@ def ptr(t):
 
 def stream_of(device):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def device_errors():
+    """Read and clear the device-side failure flags (bit 0: a bounded wait timed out)."""
+    flags = ctypes.c_uint(0)
+    check(lib().p3d_device_errors(ctypes.byref(flags)), "p3d_device_errors")
+    return flags.value
 
 
 def exported_symbols():

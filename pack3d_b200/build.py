@@ -72,7 +72,7 @@ def build(force=False, verbose=False, jobs=None):
         for name, log in logs:
             print(f"== {name}\n{log}")
     if force or todo or _stale(LIB, objects):
-        cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objects), "-lcuda"]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objects)]
         run = subprocess.run(cmd, capture_output=True, text=True)
         if run.returncode != 0:
             raise RuntimeError(f"link failed:\n{run.stderr}")

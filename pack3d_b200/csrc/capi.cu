@@ -269,6 +269,12 @@ int p3d_device_count(void) {
   return count;
 }
 
+int p3d_device_errors(unsigned *flags) {
+  P3D_CHECK_ARG(flags != nullptr, "p3d_device_errors: null output");
+  *flags = 0;
+  return take_fwd_errors(flags);
+}
+
 int p3d_pool_fwd(const void *k, const void *v, const float *weight, const float *bias, const int32_t *blocks,
                  int fine_blocks, int slots, int pool_size, void *sk, void *sv, float *sk32, float *sv32,
                  int dtype, int batch, int kv_heads, int tokens, int head_dim, float temperature,

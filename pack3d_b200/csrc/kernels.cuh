@@ -99,6 +99,9 @@ struct StencilFwdArgs {
   void *y, *ol, *og;                  // ol/og nullable
   float *lse_l, *lse_g;               // nullable
 };
+// Read-and-clear the device failure bits of the tensor-core kernel files (OR-ed into *flags).
+int take_fwd_errors(unsigned *flags);
+
 bool stencil_fwd_supported(int dtype, int head_dim, const int radius[3], int summaries);
 int launch_stencil_fwd(const StencilFwdArgs &a, cudaStream_t s);
 
