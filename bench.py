@@ -1,0 +1,438 @@
+#!/usr/bin/env python
+"""PACK3D layer benchmark on B200: bf16 forward tokens/s at 262,144 tokens.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One JSON line on rank 0.  A step is one forward of the whole ``PACK3DAttention``
+layer (LayerNorm, projections, RoPE, pooling, fused local + global attention,
+output projection, residual) over the 64^3 field, inputs resident in HBM, timed
+with CUDA events per step (L2 flushed between steps, outside the timed events),
+max over ranks.  ``e2e`` times the same public call with the input copied from
+pinned host memory and the output read back every step.  ``roofline`` is the
+fused stencil kernel (stage c) timed alone with CUDA events on its stream;
+``cpu_baseline`` is the CPU restatement of the reference path on this host.
+
+``--impl reference`` times the reference's CPU path (the CPU restatement; the
+reference itself is Python/Triton and refuses head_dim 48) on the host cores.
+"""
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "PACK3D layer bf16 fwd and fwd+bwd ms (tokens/s) at 262,144 tokens; 1-8 GPU"
+CONFIG = dict(grid=(64, 64, 64), batch=1, heads=4, kv_heads=4, head_dim=48, dim=192, block=(4, 4, 4), radius=2,
+              pool_size=1)
+L2_FLUSH_BYTES = 256 * 1024 * 1024
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a CUDA graph")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fwd-bwd-steps", type=int, default=3, help="timed fwd+bwd steps (0 disables)")
+    ap.add_argument("--kernel-only", type=int, default=0, metavar="N",
+                    help="profiling mode: run the stage-(c) kernel N times on the config-1 inputs and exit")
+    return ap.parse_args()
+
+
+def make_layout(grid):
+    from pack3d_b200 import build_layout
+    layout = build_layout(grid, CONFIG["block"], radius=CONFIG["radius"], pool_size=CONFIG["pool_size"])
+    return layout.repack(layout.order.argsort())        # raster storage of 4x4x4 cubes
+
+
+def make_layer(dtype, device):
+    from pack3d_b200 import PACK3DAttention
+    torch.manual_seed(0)
+    layer = PACK3DAttention(CONFIG["dim"], heads=CONFIG["heads"], kv_heads=CONFIG["kv_heads"],
+                            head_dim=CONFIG["head_dim"], block_volume=math.prod(CONFIG["block"]))
+    return layer.to(device=device, dtype=dtype)
+
+
+def mean_valid_neighbors(geometry):
+    return (geometry.neighbors >= 0).sum().item() / geometry.num_tokens
+
+
+# ------------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        clocks = [num(r[1]) for r in rows if num(r[1])]
+        max_clk = max((num(r[2]) for r in rows if num(r[2])), default=None)
+        loaded = [c for c, r in zip(clocks, rows) if num(r[3]) and num(r[3]) > 200] or clocks
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max_clk,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------- timing
+
+def timed_steps(step, steps, stream, flush=None):
+    """Per-step CUDA-event times (ms) on `stream`; the L2 flush runs between events."""
+    times = []
+    for _ in range(steps):
+        if flush is not None:
+            flush()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        step()
+        end.record(stream)
+        end.synchronize()
+        times.append(start.elapsed_time(end))
+    return times
+
+
+def ncu_traffic_per_launch():
+    """DRAM bytes (read + write) per launch of the stencil kernel from the committed ncu summary."""
+    path = ROOT / "profiles" / "stencil_fwd_config1.md"
+    if not path.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", path.read_text())
+    return float(m.group(1)) if m else None
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        peaks = json.loads(path.read_text())
+        return peaks.get("bf16_tflops"), peaks.get("bf16_tflops_sustained"), peaks.get("hbm_gbs"), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------------- CPU baseline
+
+def cpu_layer_seconds(sample_rows=8192, seed=0):
+    """Seconds for one config-1 layer forward with the CPU restatement of the reference, all host cores.
+
+    Projections, RoPE and pooling run for every token; the attention core and the
+    output projection run for `sample_rows` evenly spaced query rows (rows are
+    independent given the summaries) and are scaled to all rows.
+    """
+    import torch.nn.functional as F
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    layout = make_layout(CONFIG["grid"])
+    geom = layout.geometry
+    n = geom.num_tokens
+    h, g, d, dim = CONFIG["heads"], CONFIG["kv_heads"], CONFIG["head_dim"], CONFIG["dim"]
+    layer = make_layer(torch.float32, "cpu")
+    params = {k: v.detach() for k, v in layer.state_dict().items()}
+    x = torch.randn(CONFIG["batch"], n, dim, generator=torch.Generator().manual_seed(seed))
+    b = x.shape[0]
+    rows = torch.arange(0, n, max(1, n // sample_rows))
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        xn = F.layer_norm(x, (dim,), params["norm.weight"], params["norm.bias"])
+        q = F.linear(xn, params["to_q.weight"]).reshape(b, n, h, d).transpose(1, 2)
+        kl, vl, kg, vg = (t.reshape(b, n, g, d).transpose(1, 2) for t in F.linear(xn, params["to_kv.weight"]).chunk(4, -1))
+        gate = F.linear(xn, params["gate.weight"], params["gate.bias"]).reshape(b, n, h, 2).softmax(-1)[..., 1]
+        gate = gate.transpose(1, 2)
+        q, kl, kg = (oracle.axial_rope(t, layout.coords) for t in (q, kl, kg))
+        t1 = time.perf_counter()
+        oracle.compress_summaries(kg, vg, params["pool_weight"], params["slot_bias"], geom.blocks, 1)
+        t2 = time.perf_counter()
+        state = oracle.core_forward(q, kl, vl, kg, vg, params["pool_weight"], params["slot_bias"], gate,
+                                    params["local_scale"], params["global_scale"], geom.neighbors, geom.blocks, 1,
+                                    rows=rows, chunk=1024)
+        out = state["y"].transpose(1, 2).reshape(b, len(rows), -1)
+        _ = x[:, rows] + F.linear(out, params["to_out.weight"])
+        t3 = time.perf_counter()
+    full = (t1 - t0) + (t2 - t1) + ((t3 - t2) - (t2 - t1)) * n / len(rows)
+    sample = (f"LayerNorm, projections, RoPE and pooling for all {n} tokens; attention core and output "
+              f"projection for {len(rows)} evenly spaced query rows, scaled to {n} rows")
+    return full, t3 - t0, threads, sample
+
+
+# ------------------------------------------------------------------------------- GPU arm
+
+def run_b200(args, rank, world, device):
+    from pack3d_b200 import _native
+    from pack3d_b200 import ops as p3d_ops
+    from pack3d_b200.rope import balanced_pairs, rotate_projections
+    dtype = torch.bfloat16
+    layout = make_layout(CONFIG["grid"]).to(device)
+    geom = layout.geometry
+    n = geom.num_tokens
+    b = CONFIG["batch"]
+    layer = make_layer(dtype, device)
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    x = torch.randn(b, n, CONFIG["dim"], device=device, dtype=dtype, generator=gen)
+    stream = torch.cuda.current_stream(device)
+    flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+
+    def flush():
+        flush_buf.zero_()
+
+    def forward():
+        with torch.inference_mode():
+            return layer(x, layout)
+
+    for _ in range(max(args.warmup, 3)):
+        forward()
+    torch.cuda.synchronize(device)
+    use_graph = not args.no_graph and not args.kernel_only
+    if use_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.inference_mode():
+            side = torch.cuda.Stream(device)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                forward()
+            stream.wait_stream(side)
+            with torch.cuda.graph(graph):
+                y_graph = layer(x, layout)
+        step = graph.replay
+    else:
+        step = forward
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    with ClockSampler(device.index) as clocks:
+        times = timed_steps(step, 1 if args.kernel_only else args.steps, stream, flush)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    clock_summary = clocks.summary()
+    ms_local = sum(times) / len(times)
+    ms = ms_local
+    if world > 1:
+        t = torch.tensor([ms_local], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+
+    # ---- stage (c) kernel alone: fused local + global attention (for the roofline)
+    with torch.inference_mode():
+        xn = layer.norm(x)
+        hq, hd, g = CONFIG["heads"], CONFIG["head_dim"], CONFIG["kv_heads"]
+        q = layer.to_q(xn).reshape(b, n, hq, hd).transpose(1, 2)
+        kl, vl, kg, vg = (t.reshape(b, n, g, hd).transpose(1, 2) for t in layer.to_kv(xn).chunk(4, -1))
+        q, kl, kg = rotate_projections(q, kl, kg, layout.coords, balanced_pairs(hd), layout.grid_shape, packed=False)
+        gate = layer.gate(xn).reshape(b, n, hq, 2).softmax(-1)[..., 1].transpose(1, 2).contiguous()
+        vl, vg = vl.contiguous(), vg.contiguous()
+        params = (layer.pool_weight, layer.slot_bias, gate, layer.local_scale, layer.global_scale)
+        _, (sk, sv, *_rest) = p3d_ops.forward(q, kl, vl, kg, vg, *params, geom, 1.0, save_state=True)
+        kernel = lambda: p3d_ops.forward(q, kl, vl, kg, vg, *params, geom, 1.0,  # noqa: E731
+                                         save_state=False, summaries=(sk, sv))
+        if args.kernel_only:
+            times = timed_steps(kernel, args.kernel_only, stream)
+            print(json.dumps({"kernel_only_ms": [round(t, 4) for t in times]}), flush=True)
+            return None
+        for _ in range(3):
+            kernel()
+        kernel_times = timed_steps(kernel, max(args.steps, 10), stream)
+        op_fn = lambda: p3d_ops.forward(q, kl, vl, kg, vg, *params, geom, 1.0, save_state=False)  # noqa: E731
+        op_times = timed_steps(op_fn, max(args.steps, 10), stream, flush)
+    kernel_ms = statistics.median(kernel_times)
+    w_bar = mean_valid_neighbors(geom)
+    m = geom.num_summaries
+    flops = 4.0 * b * hq * n * hd * (m + w_bar)
+    peak, peak_sustained, hbm, peak_kind = measured_peaks()
+    achieved = flops / (kernel_ms * 1e-3) / 1e12
+
+    # ---- end to end through the public call: pinned host input in, output back out
+    x_host = x.detach().cpu().pin_memory()
+    y_host = torch.empty((b, n, CONFIG["dim"]), dtype=dtype).pin_memory()
+
+    def e2e_step():
+        xd = x_host.to(device, non_blocking=True)
+        with torch.inference_mode():
+            y = layer(xd, layout)
+        y_host.copy_(y, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    e2e_times = timed_steps(e2e_step, args.steps, stream, flush)
+    e2e_ms = sum(e2e_times) / len(e2e_times)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = t.item()
+
+    # ---- fwd+bwd (BASELINE config 3 shape: batch 2), fewer steps
+    fwd_bwd = None
+    if args.fwd_bwd_steps > 0:
+        xb = torch.randn(2, n, CONFIG["dim"], device=device, dtype=dtype, generator=gen).requires_grad_()
+        dyb = torch.randn_like(xb)
+
+        def train_step():
+            layer.zero_grad(set_to_none=True)
+            xb.grad = None
+            layer(xb, layout).backward(dyb)
+
+        train_step()
+        torch.cuda.synchronize(device)
+        fb_times = timed_steps(train_step, args.fwd_bwd_steps, stream, flush)
+        fb_ms = sum(fb_times) / len(fb_times)
+        if world > 1:
+            t = torch.tensor([fb_ms], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            fb_ms = t.item()
+        fwd_bwd = {"ms_per_step": round(fb_ms, 4), "tokens_per_s": round(world * 2 * n / (fb_ms * 1e-3), 1),
+                   "batch": 2, "steps": args.fwd_bwd_steps, "includes": "layer forward + backward, no optimizer"}
+
+    errors = _native.device_errors()
+    if errors:
+        raise RuntimeError(f"device error flags set: {errors}")
+    tokens = world * b * n
+    launches_per_step = 3 + 1 + 1      # RoPE q/kl/kg, pooling, fused stencil attention
+    line = {
+        "metric": METRIC,
+        "value": round(tokens / (ms * 1e-3), 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: x ~ N(0,1) (seeded), random-init PACK3DAttention weights (seed 0)",
+        "config": {"workload": "BASELINE config 1: 64^3 raster field, batch 1, dim 192 = 4 heads x 48, radius-2 "
+                               "5x5x5 neighbourhood, 4x4x4 mean-pool summaries (4096), layer forward",
+                   "grid": list(CONFIG["grid"]), "batch": b, "heads": hq, "kv_heads": g, "head_dim": hd,
+                   "dim": CONFIG["dim"], "summaries": m, "radius": CONFIG["radius"],
+                   "parallelism": "single GPU" if world == 1 else f"{world} independent replicas (one field per GPU)",
+                   "cuda_graph": use_graph,
+                   "l2": "flushed between timed steps (256 MiB write outside the timed events)"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "traffic": ncu_traffic_per_launch(),
+                     "kernel": "stencil_fwd_kernel (stage c: fused local + global attention)",
+                     "kernel_ms": round(kernel_ms, 4), "flop_per_launch": flops, "mean_valid_neighbors": w_bar,
+                     "peak_kind": peak_kind, "peak_sustained": peak_sustained},
+        "operator_ms": round(statistics.median(op_times), 4),
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+                "d2h_bytes_per_step": y_host.numel() * y_host.element_size()},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clock_summary,
+        "fwd_bwd": fwd_bwd,
+    }
+    if use_graph:
+        del graph, y_graph
+    return line
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cpu_s, wall, threads, sample = None, None, None, None
+        for _ in range(max(0, min(args.warmup, 1))):
+            cpu_layer_seconds(sample_rows=2048)
+        samples = []
+        for _ in range(max(1, min(args.steps, 3))):
+            cpu_s, wall, threads, sample = cpu_layer_seconds()
+            samples.append(cpu_s)
+        s = statistics.median(samples)
+        n = math.prod(CONFIG["grid"]) * CONFIG["batch"]
+        value = round(n / s, 1)
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": len(samples), "warmup": min(args.warmup, 1), "ms_per_step": round(s * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: x ~ N(0,1) (seeded), random-init PACK3DAttention weights (seed 0)",
+            "config": {"workload": "BASELINE config 1 (64^3, batch 1, 4 heads x 48, radius 2, 4096 summaries), "
+                                   "layer forward"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": sample + "; CPU restatement of the reference (it refuses head_dim 48)"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py --impl b200 needs a CUDA device")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=device)
+    line = run_b200(args, rank, world, device)
+    if line is None:
+        return
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu_s, wall, threads, sample = cpu_layer_seconds()
+        n = math.prod(CONFIG["grid"]) * CONFIG["batch"]
+        line["cpu_baseline"] = {"value": round(n / cpu_s, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": sample, "measured_wall_s": round(wall, 2)}
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

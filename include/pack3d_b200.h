@@ -49,6 +49,7 @@ typedef enum { P3D_F32 = 0, P3D_F16 = 1, P3D_BF16 = 2 } p3d_dtype;
 /* Attention-forward flags. */
 #define P3D_FWD_SAVE_STATE 1u   /* write ol, og, lse_l, lse_g for the backward */
 #define P3D_FWD_FORCE_INDEXED 2u /* use the indexed (neighbour-table) kernels even on a stencil */
+#define P3D_FWD_SUMMARIES_GIVEN 4u /* sk, sv already hold the pooled summaries: skip stage (b) */
 
 /* Static description string of a status code. */
 P3D_API const char *p3d_strerror(int status);

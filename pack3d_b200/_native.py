@@ -17,6 +17,7 @@ F32, F16, BF16 = 0, 1, 2
 DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 FWD_SAVE_STATE = 1
 FWD_FORCE_INDEXED = 2
+FWD_SUMMARIES_GIVEN = 4
 
 _c_int, _c_i64, _c_f32, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 

@@ -316,7 +316,8 @@ int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, 
       return fail(P3D_ERR_WORKSPACE, "p3d_attn_fwd: workspace of %zu bytes required", need);
     fwd_layout(op, flags, workspace, workspace_bytes, &ol_ws, &q_r, &kl_r, &vl_r);
   }
-  if (int st = launch_pool_fwd(pool_args(op, sk, sv), s)) return st;
+  if (!(flags & P3D_FWD_SUMMARIES_GIVEN))
+    if (int st = launch_pool_fwd(pool_args(op, sk, sv), s)) return st;
   if (use_stencil_path(op, flags)) {
     StencilFwdArgs a{};
     a.dtype = op->dtype;

@@ -71,8 +71,11 @@ def _as_gate(gate, q):
 
 
 def forward(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature, *, save_state=True,
-            force_indexed=False):
-    """Launch the forward; returns ``(y, (sk, sv, ol, og, lse_l, lse_g))`` (empty state when not saving)."""
+            force_indexed=False, summaries=None):
+    """Launch the forward; returns ``(y, (sk, sv, ol, og, lse_l, lse_g))`` (empty state when not saving).
+
+    ``summaries=(sk, sv)`` supplies already pooled summaries and runs stage (c) alone.
+    """
     b, h, n, d = q.shape
     g = kl.shape[1]
     gate = _as_gate(gate, q).contiguous()
@@ -81,8 +84,14 @@ def forward(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature
     m = geometry.num_summaries
     empty = lambda *shape, dtype=q.dtype: torch.empty(shape, dtype=dtype, device=q.device)  # noqa: E731
     y = empty(b, h, n, d)
-    sk, sv = empty(b, g, m, d), empty(b, g, m, d)
     flags = (_native.FWD_SAVE_STATE if save_state else 0) | (_native.FWD_FORCE_INDEXED if force_indexed else 0)
+    if summaries is None:
+        sk, sv = empty(b, g, m, d), empty(b, g, m, d)
+    else:
+        sk, sv = summaries
+        if sk.shape != (b, g, m, d) or sv.shape != sk.shape or sk.dtype != q.dtype or not sk.is_contiguous():
+            raise ValueError("given summaries must be contiguous [B, G, M, D] in the input dtype")
+        flags |= _native.FWD_SUMMARIES_GIVEN
     ol = og = lse_l = lse_g = None
     if save_state:
         ol, og = empty(b, h, n, d), empty(b, h, n, d)
