@@ -41,7 +41,7 @@ L2_FLUSH_BYTES = 256 * 1024 * 1024
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a CUDA graph")
@@ -87,7 +87,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -254,12 +254,12 @@ def run_b200(args, rank, world, device):
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize(device)
-    with ClockSampler(device.index) as clocks:
-        times = timed_steps(step, 1 if args.kernel_only else args.steps, stream, flush)
+    # nvidia-smi samples every 100 ms from here through the kernel, operator and e2e timing loops
+    clocks = ClockSampler(device.index).__enter__()
+    times = timed_steps(step, 1 if args.kernel_only else args.steps, stream, flush)
     torch.cuda.synchronize(device)
     if world > 1:
         torch.distributed.barrier()
-    clock_summary = clocks.summary()
     ms_local = sum(times) / len(times)
     ms = ms_local
     if world > 1:
@@ -283,6 +283,8 @@ def run_b200(args, rank, world, device):
         if args.kernel_only:
             times = timed_steps(kernel, args.kernel_only, stream)
             print(json.dumps({"kernel_only_ms": [round(t, 4) for t in times]}), flush=True)
+            clocks.__exit__(None, None, None)
+            clocks.summary()
             return None
         for _ in range(3):
             kernel()
@@ -310,6 +312,8 @@ def run_b200(args, rank, world, device):
         e2e_step()
     torch.cuda.synchronize(device)
     e2e_times = timed_steps(e2e_step, args.steps, stream, flush)
+    clocks.__exit__(None, None, None)
+    clock_summary = clocks.summary()
     e2e_ms = sum(e2e_times) / len(e2e_times)
     if world > 1:
         t = torch.tensor([e2e_ms], device=device)

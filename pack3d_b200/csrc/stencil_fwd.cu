@@ -9,22 +9,30 @@
 // (z, y, x), so softmax warp w of a tile owns query plane z = w and TMEM lanes
 // 32w..32w+31.
 //
-// Chunk sequence per tile (both tiles in lockstep, one shared smem ring):
-//   chunks 0..7   local: halo plane z-2+c of the tile, an 8x12 (y, x) window = 96
-//                 keys; a key is used iff it lies in the query's 5x5x5 cube and in
-//                 the volume (coordinate test, no neighbour table).  A warp whose
-//                 query plane is more than 2 planes away writes a zero P block.
-//   chunks 8..    global: 128 summaries per chunk.
+// Chunk sequence of each tile (one shared smem ring, both tiles in step), 96 keys each:
+//   chunks 0..7   local: halo plane z-2+c of the tile, its 8x12 (y, x) window.  A key
+//                 is used iff it lies in the query's 5x5x5 cube and in the volume
+//                 (coordinate test, no neighbour table).  A warp whose query plane is
+//                 more than 2 planes away writes a zero P block.
+//   chunks 8..    global: 96 summaries per chunk.
+// TMEM per tile (256 columns): two 96-column S buffers and one accumulator O.  The QK^T
+// MMA of chunk c+2 and the PV MMA of chunk c run while the softmax warps work on chunk
+// c+1, so the MMA thread is off the softmax critical path.  (On sm_100 an M=128, K=16
+// MMA takes >= ~46 cycles whatever N <= 64 is and ~56 at N=96, and every commit costs
+// about two MMAs: with head_dim 48 a chunk is long enough that it must overlap.)  O
+// holds the local accumulator during chunks 0..7; when they are done the normalised
+// local output is parked in shared memory, rounded to the storage dtype as the
+// reference rounds it before the mix, and O then accumulates the global branch.
 // Two independent online softmaxes (max / sum per row in registers, conditional
-// rescale of the TMEM accumulator only when the running max grows by > 2^8),
-// accumulators O_local and O_global in TMEM; the epilogue normalises both and
-// writes y (and optionally ol, og, lse_l, lse_g) through the raster->packed map.
+// rescale of O only when the running max grows by > 2^8).  The epilogue normalises the
+// global branch, mixes and writes y (and optionally ol, og, lse_l, lse_g) through the
+// raster->packed row map.
 //
 // Roles: warps 0-3 softmax tile A, warps 4-7 softmax tile B, warp 8 TMA producer,
 // warp 9 MMA issuer (one thread).  Operands live in shared memory in the
 // SWIZZLE_32B layout: Q / K are K-major boxes of 16 channels, V is the same bytes
-// read MN-major; P goes back into the S columns of TMEM as bf16/f16 pairs and
-// feeds the PV MMA as the TMEM A operand.  Every mbarrier wait is bounded.
+// read MN-major; P goes back into its S buffer in TMEM as bf16/f16 pairs and feeds
+// the PV MMA as the TMEM A operand.  Every mbarrier wait is bounded.
 #include <algorithm>
 #include <mutex>
 
@@ -41,39 +49,51 @@ __device__ unsigned g_fwd_errors = 0;  // failure bits of the kernels in this fi
 constexpr int kR = 2;                               // stencil radius handled here
 constexpr int kTZ = 4, kTY = 4, kTX = 8;            // one 128-row query tile
 constexpr int kHY = kTY + 2 * kR, kHX = kTX + 2 * kR, kHZ = kTZ + 2 * kR;
-constexpr int kPlane = kHY * kHX;                   // 96 keys per halo plane
+constexpr int kKeys = kHY * kHX;                    // 96 keys per chunk (a halo plane)
 constexpr int kLocalChunks = kHZ;                   // 8 halo planes per tile
-constexpr int kSumRows = 128;                       // summaries per global chunk
+constexpr int kSumRows = kKeys;                     // summaries per global chunk
 constexpr int kRows = 128;                          // queries per tile
 constexpr int kThreads = 320;
 constexpr int kProducerWarp = 8, kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kNegInf = -__builtin_huge_valf();
 
-static_assert(kPlane % 16 == 0, "halo plane must be a multiple of the MMA K step");
+static_assert(kKeys % 32 == 0, "chunk size must suit the MMA and TMEM access shapes");
 
 template <int D>
 struct Cfg {
   static constexpr int kK = D / 16;                 // 16-channel boxes per row
   static constexpr int kBoxQ = kRows * 32;          // one box = rows x 32 bytes
-  static constexpr int kBoxP = kPlane * 32;
-  static constexpr int kBoxS = kSumRows * 32;
+  static constexpr int kBoxK = kKeys * 32;          // 3072
   static constexpr int kQBytes = kK * kBoxQ;        // one query tile
-  static constexpr int kPlaneBytes = kK * kBoxP;    // one halo plane of K (or V)
-  static constexpr int kSumBytes = kK * kBoxS;      // one summary chunk of K (or V)
-  static constexpr int kStageRaw = (4 * kPlaneBytes > 2 * kSumBytes) ? 4 * kPlaneBytes : 2 * kSumBytes;
-  static constexpr int kStageBytes = (kStageRaw + 1023) / 1024 * 1024;
-  static constexpr int kStages = D <= 48 ? 4 : 3;
-  // + alignment slack; at least 116 KB so that one CTA (which owns all 512 TMEM columns) fits per SM
-  static constexpr int kSmemNeed = 2 * kQBytes + kStages * kStageBytes + 1024;
+  static constexpr int kKeyBytes = kK * kBoxK;      // one chunk of K (or V)
+  static constexpr int kStageBytes = (4 * kKeyBytes + 1023) / 1024 * 1024;  // local: K_A K_B V_A V_B
+  static constexpr int kOlBytes = kRows * D * 2;    // parked local output of one tile
+  static constexpr int kFixed = 2 * kQBytes + 2 * kOlBytes + 1024;
+  // 3 or 4 stages: at least chunks c .. c+2 resident, and at most 4 so that the stage
+  // release signal (a QK^T commit of tile B, see the producer) cannot alias phases.
+  static constexpr int kStages = (227 * 1024 - 2048 - kFixed) / kStageBytes > 4 ? 4
+                                                                                 : (227 * 1024 - 2048 - kFixed) / kStageBytes;
+  // at least 116 KB so that one CTA (which owns all 512 TMEM columns) fits per SM
+  static constexpr int kSmemNeed = kFixed + kStages * kStageBytes;
   static constexpr int kSmemBytes = kSmemNeed > 116 * 1024 ? kSmemNeed : 116 * 1024;
-  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+  static_assert(kStages >= 3 && kStages <= 4, "the ring must hold chunks c .. c+2");
+  static_assert(kSmemBytes <= 225 * 1024, "shared memory budget");
 };
 
-// TMEM columns of tile t: S/P [t*256, +128), O_global [+128, +D), O_local [+192, +D).
-constexpr uint32_t kColS = 0, kColOg = 128, kColOl = 192;
+// TMEM columns of tile t (base t*256): S buffers [0, 96) and [96, 192), O [192, 192 + D).
+constexpr uint32_t kSBuf = 96, kColO = 192;
 
-enum Bar { kQFull = 0, kFull = 1, kEmpty = 5, kSReady = 9, kPReady = 11, kPvDone = 13, kOReady = 15, kNumBars = 17 };
+enum Bar {
+  kQFull = 0,
+  kFull = 1,                  // [stage]; stages are released through kSReady (see producer)
+  kSReady = kFull + 4,        // [tile][buf]
+  kPReady = kSReady + 4,      // [tile][buf]
+  kPvDone = kPReady + 4,      // [tile][buf]: PV of the chunk that last used the buffer is done
+  kOReady = kPvDone + 4,      // [tile]
+  kDrain = kOReady + 2,       // MMA thread: every MMA it issued has completed
+  kNumBars = kDrain + 1
+};
 
 struct FwdParams {
   int Z, Y, X, tiles_z, tiles_y, tiles_x;
@@ -97,46 +117,55 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 template <bool BF16>
 __device__ __forceinline__ float2 unpack2(uint32_t v) {
   if constexpr (BF16) {
-    __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162 *>(&v);
-    return __bfloat1622float2(h);
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&v));
   } else {
-    __half2 h = *reinterpret_cast<__half2 *>(&v);
-    return __half22float2(h);
+    return __half22float2(*reinterpret_cast<const __half2 *>(&v));
   }
 }
 
-// Online-softmax bookkeeping of one branch for one row.  Rescales the TMEM
-// accumulator only when some row of the warp raised its max by more than 2^8.
-template <int D>
-__device__ __forceinline__ void update_max(float &m, float &l, float mx, float sc, uint32_t t_o) {
+// Online-softmax bookkeeping of one branch for one row, split in two so that the
+// scores are dead before the accumulator is touched:
+//   begin_max  picks the reference max for this chunk's exponentials.  The running
+//              max only moves when it grows by more than 2^8 (or on the first chunk);
+//              otherwise the stale max is kept and p <= 2^8.
+//   finish_max rescales the TMEM accumulator row and the running sum when the max
+//              moved (warp-collective TMEM access, per-row factor) and adds this
+//              chunk's sum.
+struct MaxUpdate {
+  float m_use;   // max the exponentials of this chunk are taken against
+  float factor;  // accumulator rescale factor (1 when the max did not move)
+  bool rescale;
+};
+
+__device__ __forceinline__ MaxUpdate begin_max(float m, float mx, float sc) {
   const float m_new = fmaxf(m, mx);
-  const bool first = (m == kNegInf);
-  const bool need = !first && (m_new - m) * sc > 8.f;
-  if (first) m = m_new;
-  if (__any_sync(0xffffffffu, need)) {
-    const float factor = need ? ex2_approx((m - m_new) * sc) : 1.f;
-    uint32_t o[16];
+  MaxUpdate u;
+  u.rescale = (m != kNegInf) && (m_new - m) * sc > 8.f;
+  u.m_use = (m == kNegInf || u.rescale) ? m_new : m;
+  u.factor = u.rescale ? ex2_approx((m - m_new) * sc) : 1.f;
+  return u;
+}
+
+template <int D>
+__device__ __forceinline__ void rescale_rows(float factor, uint32_t t_o) {
+  uint32_t o[16];
 #pragma unroll
-    for (int c = 0; c < D / 16; ++c) {
-      tmem_ld16(t_o + 16 * c, o);
-      tmem_wait_ld();
+  for (int c = 0; c < D / 16; ++c) {
+    tmem_ld16(t_o + 16 * c, o);
+    tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-      tmem_st16(t_o + 16 * c, o);
-    }
-    if (need) {
-      l *= factor;
-      m = m_new;
-    }
+    for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+    tmem_st16(t_o + 16 * c, o);
   }
 }
 
-// Exponentiate `n` scores (in registers) against max m, pack to 16-bit pairs and store
-// them as P into TMEM columns [t_p, t_p + n/2).  Returns the row sum of p.
+// Exponentiate N scores (in registers) against max m, pack to 16-bit pairs and store
+// them as P into TMEM columns [t_p, t_p + N/2).  Returns the row sum of p.
 template <int N, bool BF16>
 __device__ __forceinline__ float exp_store(const float *s, float m, float sc, uint32_t t_p) {
+  static_assert(N % 32 == 0, "N must be a multiple of 32");
   const float msc = (m == kNegInf) ? 0.f : m * sc;
-  float sum = 0.f;
+  float sum[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums: no serial add chain
 #pragma unroll
   for (int g = 0; g < N / 32; ++g) {
     uint32_t pk[16];
@@ -144,12 +173,23 @@ __device__ __forceinline__ float exp_store(const float *s, float m, float sc, ui
     for (int i = 0; i < 16; ++i) {
       const float p0 = ex2_approx(fmaf(s[32 * g + 2 * i], sc, -msc));
       const float p1 = ex2_approx(fmaf(s[32 * g + 2 * i + 1], sc, -msc));
-      sum += p0 + p1;
+      sum[i & 3] += p0 + p1;
       pk[i] = pack2<BF16>(p0, p1);
     }
     tmem_st16(t_p + 16 * g, pk);
   }
-  return sum;
+  return (sum[0] + sum[1]) + (sum[2] + sum[3]);
+}
+
+// Row maximum of N registers as a tree (8 independent chains, then pairwise).
+template <int N>
+__device__ __forceinline__ float row_max(const float *s) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = s[i];
+#pragma unroll
+  for (int i = 8; i < N; ++i) m[i & 7] = fmaxf(m[i & 7], s[i]);
+  return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
 }
 
 template <int D, bool BF16>
@@ -182,20 +222,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t q_smem = base;                        // tile A, then tile B
   const uint32_t ring = base + 2 * C::kQBytes;
+  uint8_t *ol_park = smem_raw + (base - raw) + 2 * C::kQBytes + C::kStages * C::kStageBytes;  // [tile][row][D]
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
 
   if (tid == 0) {
     mbar_init(bar(kQFull), 1);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(bar(kFull + s), 1);
-      mbar_init(bar(kEmpty + s), 1);
     }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(bar(kSReady + t), 1);
-      mbar_init(bar(kPReady + t), 4);
-      mbar_init(bar(kPvDone + t), 1);
-      mbar_init(bar(kOReady + t), 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(bar(kSReady + i), 1);
+      mbar_init(bar(kPReady + i), 4);
+      mbar_init(bar(kPvDone + i), 1);
     }
+    for (int t = 0; t < 2; ++t) mbar_init(bar(kOReady + t), 1);
+    mbar_init(bar(kDrain), 1);
     fence_mbar_init();
   }
   for (int i = tid; i < D; i += kThreads) {
@@ -225,97 +266,131 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < 2; ++t)
         for (int c = 0; c < C::kK; ++c)
           tma_load_5d(q_smem + t * C::kQBytes + c * C::kBoxQ, &tq, bar(kQFull), 16 * c, x0, y0, z0 + kTZ * t, bh);
+      int issued = 0;
       for (int ch = 0; ch < n_chunks; ++ch) {
         const int s = ch % C::kStages;
-        if (ch >= C::kStages && !mbar_wait(bar(kEmpty + s), ((ch / C::kStages) + 1) & 1, &g_fwd_errors)) break;
+        // Stage s last held chunk y = ch - kStages; its final reader is PV_B(y), and the MMA
+        // thread issues S_B(x), x = y + 2, right after it, so that commit's completion frees
+        // the stage.  Parity is unambiguous: the barrier's next completion, S_B(x + 2), needs
+        // chunk ch - kStages + 4 >= ch (kStages <= 4), which this thread has not loaded yet.
+        if (ch >= C::kStages) {
+          const int x = ch - C::kStages + 2;
+          if (!mbar_wait(bar(kSReady + 2 + (x & 1)), (x >> 1) & 1, &g_fwd_errors)) break;
+        }
         const uint32_t stage = ring + s * C::kStageBytes;
         const uint32_t full = bar(kFull + s);
         if (ch < kLocalChunks) {
-          mbar_expect_tx(full, 4 * C::kPlaneBytes);
+          mbar_expect_tx(full, 4 * C::kKeyBytes);
           for (int t = 0; t < 2; ++t) {
             const int z = z0 + kTZ * t - kR + ch;
             for (int c = 0; c < C::kK; ++c) {
-              tma_load_5d(stage + t * C::kPlaneBytes + c * C::kBoxP, &tkl, full, 16 * c, x0 - kR, y0 - kR, z, bg);
-              tma_load_5d(stage + (2 + t) * C::kPlaneBytes + c * C::kBoxP, &tvl, full, 16 * c, x0 - kR, y0 - kR, z,
+              tma_load_5d(stage + t * C::kKeyBytes + c * C::kBoxK, &tkl, full, 16 * c, x0 - kR, y0 - kR, z, bg);
+              tma_load_5d(stage + (2 + t) * C::kKeyBytes + c * C::kBoxK, &tvl, full, 16 * c, x0 - kR, y0 - kR, z,
                           bg);
             }
           }
         } else {
           const int g = ch - kLocalChunks;
-          mbar_expect_tx(full, 2 * C::kSumBytes);
+          mbar_expect_tx(full, 2 * C::kKeyBytes);
           for (int c = 0; c < C::kK; ++c) {
-            tma_load_3d(stage + c * C::kBoxS, &tsk, full, 16 * c, g * kSumRows, bg);
-            tma_load_3d(stage + C::kSumBytes + c * C::kBoxS, &tsv, full, 16 * c, g * kSumRows, bg);
+            tma_load_3d(stage + c * C::kBoxK, &tsk, full, 16 * c, g * kSumRows, bg);
+            tma_load_3d(stage + C::kKeyBytes + c * C::kBoxK, &tsv, full, 16 * c, g * kSumRows, bg);
           }
         }
+        issued = ch + 1;
       }
+      // Never leave copies in flight into shared memory this CTA is about to give up: wait
+      // (bounded) for the Q tiles and the last loads of every stage.  On the normal path
+      // these phases completed long ago; after a timed-out wait they may still be landing.
+      mbar_wait(bar(kQFull), 0, &g_fwd_errors, 100000000ull);
+      for (int ch = issued > C::kStages ? issued - C::kStages : 0; ch < issued; ++ch)
+        mbar_wait(bar(kFull + ch % C::kStages), (ch / C::kStages) & 1, &g_fwd_errors, 100000000ull);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_local = idesc_f16(128, kPlane, BF16, false);
-      constexpr uint32_t idesc_global = idesc_f16(128, kSumRows, BF16, false);
+      constexpr uint32_t idesc_s = idesc_f16(128, kKeys, BF16, false);
       constexpr uint32_t idesc_pv = idesc_f16(128, D, BF16, true);
+      // S_t(ch) = Q_t K(ch)^T into S buffer ch%2, then signal the tile's softmax warps.
+      auto issue_s = [&](int t, int ch) {
+        const uint32_t stage = ring + (ch % C::kStages) * C::kStageBytes;
+        const uint32_t k_base = ch < kLocalChunks ? stage + t * C::kKeyBytes : stage;
+        const uint32_t q_t = q_smem + t * C::kQBytes;
+        const uint32_t t_s = tmem + t * 256 + (ch & 1) * kSBuf;
+        for (int c = 0; c < C::kK; ++c)
+          mma_ss(t_s, desc_sw32(q_t + c * C::kBoxQ, 16, 256), desc_sw32(k_base + c * C::kBoxK, 16, 256), idesc_s,
+                 c > 0 ? 1u : 0u);
+        mma_commit(bar(kSReady + 2 * t + (ch & 1)));
+      };
+      // O_t += P_t(c) V(c) once the softmax warps have written P_t(c).
+      auto issue_pv = [&](int t, int c) -> bool {
+        if (!mbar_wait(bar(kPReady + 2 * t + (c & 1)), (c >> 1) & 1, &g_fwd_errors)) return false;
+        tc_fence_after();
+        const uint32_t stage = ring + (c % C::kStages) * C::kStageBytes;
+        const uint32_t v_base = c < kLocalChunks ? stage + (2 + t) * C::kKeyBytes : stage + C::kKeyBytes;
+        const uint32_t t_p = tmem + t * 256 + (c & 1) * kSBuf;
+        const bool first = (c == 0) || (c == kLocalChunks);  // O restarts for the global branch
+        for (int j = 0; j < kKeys / 16; ++j)
+          mma_ts(tmem + t * 256 + kColO, t_p + 8 * j, desc_sw32(v_base + j * 512, C::kBoxK, 256), idesc_pv,
+                 (first && j == 0) ? 0u : 1u);
+        mma_commit(bar(kPvDone + 2 * t + (c & 1)));
+        return true;
+      };
+      auto wait_full = [&](int ch) -> bool {
+        if (!mbar_wait(bar(kFull + ch % C::kStages), (ch / C::kStages) & 1, &g_fwd_errors)) return false;
+        tc_fence_after();
+        return true;
+      };
+      // S_t(c+2) writes the TMEM columns that PV_t(c) reads as its A operand (P_t(c)).
+      // tcgen05.mma ops are only ordered among themselves when they share an accumulator,
+      // so PV_t(c) must have completed before S_t(c+2) is issued.
+      auto wait_pv = [&](int t, int c) -> bool {
+        if (!mbar_wait(bar(kPvDone + 2 * t + (c & 1)), (c >> 1) & 1, &g_fwd_errors)) return false;
+        tc_fence_after();
+        return true;
+      };
+      // Prologue: both S buffers of both tiles.  Steady state per chunk c:
+      //   PV_A(c), PV_B(c), [PV_A(c) done] S_A(c+2), [PV_B(c) done] S_B(c+2)
+      // Waiting for PV_A(c) while PV_B(c) still executes keeps the tensor pipe busy.
       bool ok = mbar_wait(bar(kQFull), 0, &g_fwd_errors);
-      for (int ch = 0; ok && ch <= n_chunks; ++ch) {
-        if (ch < n_chunks) {
-          ok = mbar_wait(bar(kFull + ch % C::kStages), (ch / C::kStages) & 1, &g_fwd_errors);
-          if (!ok) break;
-          tc_fence_after();
-        }
-        for (int t = 0; t < 2 && ok; ++t) {
-          const uint32_t t_s = tmem + t * 256 + kColS;
-          if (ch > 0) {
-            // O_t += P_t(ch-1) V(ch-1)
-            const int c = ch - 1;
-            ok = mbar_wait(bar(kPReady + t), c & 1, &g_fwd_errors);
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t stage = ring + (c % C::kStages) * C::kStageBytes;
-            const bool local = c < kLocalChunks;
-            const uint32_t v_base = local ? stage + (2 + t) * C::kPlaneBytes : stage + C::kSumBytes;
-            const uint32_t lbo = local ? C::kBoxP : C::kBoxS;
-            const int ksteps = (local ? kPlane : kSumRows) / 16;
-            const uint32_t t_o = tmem + t * 256 + (local ? kColOl : kColOg);
-            const bool first = (c == 0) || (c == kLocalChunks);
-            for (int j = 0; j < ksteps; ++j)
-              mma_ts(t_o, t_s + 8 * j, desc_sw32(v_base + j * 512, lbo, 256), idesc_pv, (first && j == 0) ? 0u : 1u);
-            if (ch == n_chunks) {
-              mma_commit(bar(kOReady + t));
-            } else {
-              // S(ch) overwrites the P(ch-1) columns: wait until the PV MMA has read them.
-              mma_commit(bar(kPvDone + t));
-              ok = mbar_wait(bar(kPvDone + t), c & 1, &g_fwd_errors);
-              if (!ok) break;
-            }
-          }
-          if (ch < n_chunks) {
-            // S_t = Q_t K(ch)^T
-            const uint32_t stage = ring + (ch % C::kStages) * C::kStageBytes;
-            const bool local = ch < kLocalChunks;
-            const uint32_t k_base = local ? stage + t * C::kPlaneBytes : stage;
-            const uint32_t box = local ? C::kBoxP : C::kBoxS;
-            const uint32_t idesc = local ? idesc_local : idesc_global;
-            const uint32_t q_t = q_smem + t * C::kQBytes;
-            for (int c = 0; c < C::kK; ++c)
-              mma_ss(t_s, desc_sw32(q_t + c * C::kBoxQ, 16, 256), desc_sw32(k_base + c * box, 16, 256), idesc,
-                     c > 0 ? 1u : 0u);
-            mma_commit(bar(kSReady + t));
-          }
-        }
-        if (ok && ch > 0 && ch < n_chunks) mma_commit(bar(kEmpty + (ch - 1) % C::kStages));
+      for (int ch = 0; ok && ch < 2; ++ch) {
+        ok = wait_full(ch);
+        if (!ok) break;
+        issue_s(0, ch);
+        issue_s(1, ch);
       }
+      for (int c = 0; ok && c < n_chunks; ++c) {
+        const bool more = c + 2 < n_chunks;
+        ok = issue_pv(0, c) && issue_pv(1, c);
+        if (!ok || !more) continue;
+        ok = wait_full(c + 2) && wait_pv(0, c);
+        if (!ok) break;
+        issue_s(0, c + 2);
+        ok = wait_pv(1, c);
+        if (!ok) break;
+        issue_s(1, c + 2);  // its commit also releases chunk c's stage to the producer
+      }
+      if (ok) {
+        mma_commit(bar(kOReady));
+        mma_commit(bar(kOReady + 1));
+      }
+      // TMEM is freed after the final __syncthreads: make sure every MMA issued above has
+      // completed first, on the normal path and after a timed-out wait alike.
+      mma_commit(bar(kDrain));
+      mbar_wait(bar(kDrain), 0, &g_fwd_errors, 100000000ull);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
     const int t = warp >> 2, w = warp & 3;
     const uint32_t lanes = (uint32_t)(w * 32) << 16;
-    const uint32_t t_s = tmem + lanes + t * 256 + kColS;
-    const uint32_t t_og = tmem + lanes + t * 256 + kColOg;
-    const uint32_t t_ol = tmem + lanes + t * 256 + kColOl;
+    const uint32_t t_tile = tmem + lanes + t * 256;
+    const uint32_t t_o = t_tile + kColO;
+    const int row = w * 32 + lane;
     const int qz = w, qy = lane >> 3, qx = lane & 7;
     const int zq = z0 + kTZ * t + qz, yq = y0 + qy, xq = x0 + qx;
     const bool row_ok = zq < p.Z && yq < p.Y && xq < p.X;
+    uint32_t *park = reinterpret_cast<uint32_t *>(ol_park + (size_t)(t * kRows + row) * D * 2);
+    // keys of the 8x12 halo window inside this query's cube and inside the volume
     uint32_t mask[3] = {0u, 0u, 0u};
 #pragma unroll
     for (int hy = 0; hy < kHY; ++hy) {
@@ -330,106 +405,123 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sc = p.sc;
     float m_l = kNegInf, l_l = 0.f, m_g = kNegInf, l_g = 0.f;
     bool ok = true;
+    // Completion of PV_t(c), needed before O is read or rescaled.  Testing the phase only
+    // when needed is sound: the next completion of that buffer's barrier is PV_t(c+2), which
+    // needs this warp's P of chunk c+2.
+    auto wait_pv_done = [&](int c) -> bool {
+      const bool r = mbar_wait(bar(kPvDone + 2 * t + (c & 1)), (c >> 1) & 1, &g_fwd_errors);
+      if (r) tc_fence_after();
+      return r;
+    };
     for (int ch = 0; ch < n_chunks; ++ch) {
-      ok = mbar_wait(bar(kSReady + t), ch & 1, &g_fwd_errors);
+      const int buf = ch & 1;
+      const uint32_t t_s = t_tile + buf * kSBuf;
+      if (ch == kLocalChunks) {
+        // Local branch done: park its normalised output (storage dtype) and free O.
+        ok = wait_pv_done(kLocalChunks - 1);
+        if (!ok) break;
+        const float inv_l = l_l > 0.f ? 1.f / l_l : 0.f;
+#pragma unroll
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t o[16];
+          tmem_ld16(t_o + 16 * c, o);
+          tmem_wait_ld();
+          uint4 v[2];
+          uint32_t *pv = reinterpret_cast<uint32_t *>(v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            pv[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+          reinterpret_cast<uint4 *>(park)[2 * c] = v[0];
+          reinterpret_cast<uint4 *>(park)[2 * c + 1] = v[1];
+        }
+        tc_fence_before();
+      }
+      ok = mbar_wait(bar(kSReady + 2 * t + buf), (ch >> 1) & 1, &g_fwd_errors);
       if (!ok) break;
       tc_fence_after();
-      if (ch < kLocalChunks) {
-        const int zp = z0 + kTZ * t - kR + ch;
-        const bool need = (unsigned)(ch - qz) <= 2u * kR && zp >= 0 && zp < p.Z;  // warp-uniform
-        if (need) {
-          float s[kPlane];
+      const bool local = ch < kLocalChunks;
+      const int zp = z0 + kTZ * t - kR + ch;
+      const bool active = !local || ((unsigned)(ch - qz) <= 2u * kR && zp >= 0 && zp < p.Z);  // warp-uniform
+      if (active) {
+        float s[kKeys];
 #pragma unroll
-          for (int g = 0; g < kPlane / 32; ++g) tmem_ld32(t_s + 32 * g, reinterpret_cast<uint32_t *>(s + 32 * g));
-          tmem_wait_ld();
-          float mx = kNegInf;
+        for (int g = 0; g < kKeys / 32; ++g) tmem_ld32(t_s + 32 * g, reinterpret_cast<uint32_t *>(s + 32 * g));
+        tmem_wait_ld();
+        if (local) {
 #pragma unroll
-          for (int i = 0; i < kPlane; ++i) {
-            s[i] = (mask[i >> 5] >> (i & 31)) & 1u ? s[i] : kNegInf;
-            mx = fmaxf(mx, s[i]);
-          }
-          update_max<D>(m_l, l_l, mx, sc, t_ol);
-          l_l += exp_store<kPlane, BF16>(s, m_l, sc, t_s);
+          for (int i = 0; i < kKeys; ++i) s[i] = (mask[i >> 5] >> (i & 31)) & 1u ? s[i] : kNegInf;
         } else {
-          uint32_t zero[16];
+          const int valid = p.summaries - (ch - kLocalChunks) * kSumRows;
+          if (valid < kSumRows) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) zero[i] = 0u;
-#pragma unroll
-          for (int g = 0; g < kPlane / 32; ++g) tmem_st16(t_s + 16 * g, zero);
+            for (int i = 0; i < kSumRows; ++i) s[i] = i < valid ? s[i] : kNegInf;
+          }
+        }
+        const MaxUpdate u = begin_max(local ? m_l : m_g, row_max<kKeys>(s), sc);
+        const float sum = exp_store<kKeys, BF16>(s, u.m_use, sc, t_s);
+        if (__any_sync(0xffffffffu, u.rescale)) {
+          ok = wait_pv_done(ch - 1);
+          if (!ok) break;
+          rescale_rows<D>(u.factor, t_o);
+        }
+        if (local) {
+          l_l = l_l * u.factor + sum;
+          m_l = u.m_use;
+        } else {
+          l_g = l_g * u.factor + sum;
+          m_g = u.m_use;
         }
       } else {
-        const int g0 = (ch - kLocalChunks) * kSumRows;
-        const int valid = min(kSumRows, p.summaries - g0);
-        float s[kSumRows];
+        uint32_t zero[16];
 #pragma unroll
-        for (int g = 0; g < kSumRows / 32; ++g) tmem_ld32(t_s + 32 * g, reinterpret_cast<uint32_t *>(s + 32 * g));
-        tmem_wait_ld();
-        float mx = kNegInf;
-        if (valid == kSumRows) {
+        for (int i = 0; i < 16; ++i) zero[i] = 0u;
 #pragma unroll
-          for (int i = 0; i < kSumRows; ++i) mx = fmaxf(mx, s[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < kSumRows; ++i) {
-            s[i] = i < valid ? s[i] : kNegInf;
-            mx = fmaxf(mx, s[i]);
-          }
-        }
-        update_max<D>(m_g, l_g, mx, sc, t_og);
-        l_g += exp_store<kSumRows, BF16>(s, m_g, sc, t_s);
+        for (int g = 0; g < kKeys / 32; ++g) tmem_st16(t_s + 16 * g, zero);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kPReady + t));
+      if (lane == 0) mbar_arrive(bar(kPReady + 2 * t + buf));
     }
-    // ---- epilogue: normalise both branches, mix, store through the row map
+    // ---- epilogue: normalise the global branch, mix, store through the row map
     if (ok) ok = mbar_wait(bar(kOReady + t), 0, &g_fwd_errors);
     if (ok) {
       tc_fence_after();
-      uint32_t ol[D], og[D];
+      uint32_t og[D];
 #pragma unroll
-      for (int c = 0; c < D / 16; ++c) {
-        tmem_ld16(t_ol + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(ol + 16 * c));
-        tmem_ld16(t_og + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(og + 16 * c));
-      }
+      for (int c = 0; c < D / 16; ++c) tmem_ld16(t_o + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(og + 16 * c));
       tmem_wait_ld();
       if (row_ok) {
         int64_t rr = ((int64_t)zq * p.Y + yq) * p.X + xq;
         if (p.map) rr = p.map[rr];
-        const int64_t row = (int64_t)bh * p.tokens + rr;
-        const float gate = load_any(p.gate, p.gate_dtype, row);
-        const float inv_l = l_l > 0.f ? 1.f / l_l : 0.f;
+        const int64_t grow = (int64_t)bh * p.tokens + rr;
+        const float gate = load_any(p.gate, p.gate_dtype, grow);
         const float inv_g = 1.f / l_g;
-        uint32_t packed_y[D / 2], packed_l[D / 2], packed_g[D / 2];
+        uint32_t packed_y[D / 2], packed_g[D / 2];
 #pragma unroll
         for (int i = 0; i < D / 2; ++i) {
-          float yv[2], lv[2], gv[2];
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            const int d = 2 * i + k;
-            lv[k] = __uint_as_float(ol[d]) * inv_l;
-            gv[k] = __uint_as_float(og[d]) * inv_g;
-            yv[k] = __fadd_rn(__fmul_rn(s_sl[d], lv[k]), __fmul_rn(__fmul_rn(gate, s_sg[d]), gv[k]));
-          }
-          packed_y[i] = pack2<BF16>(yv[0], yv[1]);
-          packed_l[i] = pack2<BF16>(lv[0], lv[1]);
-          packed_g[i] = pack2<BF16>(gv[0], gv[1]);
+          const float2 lv = unpack2<BF16>(park[i]);
+          const float g0 = __uint_as_float(og[2 * i]) * inv_g, g1 = __uint_as_float(og[2 * i + 1]) * inv_g;
+          const float y0v = __fadd_rn(__fmul_rn(s_sl[2 * i], lv.x), __fmul_rn(__fmul_rn(gate, s_sg[2 * i]), g0));
+          const float y1v =
+              __fadd_rn(__fmul_rn(s_sl[2 * i + 1], lv.y), __fmul_rn(__fmul_rn(gate, s_sg[2 * i + 1]), g1));
+          packed_y[i] = pack2<BF16>(y0v, y1v);
+          packed_g[i] = pack2<BF16>(g0, g1);
         }
-        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.y) + row * D);
+        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.y) + grow * D);
 #pragma unroll
         for (int v = 0; v < D / 8; ++v)
           dst[v] = make_uint4(packed_y[4 * v], packed_y[4 * v + 1], packed_y[4 * v + 2], packed_y[4 * v + 3]);
         if (p.ol) {
-          uint4 *dl = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.ol) + row * D);
-          uint4 *dg = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.og) + row * D);
+          uint4 *dl = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.ol) + grow * D);
+          uint4 *dg = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.og) + grow * D);
 #pragma unroll
           for (int v = 0; v < D / 8; ++v) {
-            dl[v] = make_uint4(packed_l[4 * v], packed_l[4 * v + 1], packed_l[4 * v + 2], packed_l[4 * v + 3]);
+            dl[v] = reinterpret_cast<const uint4 *>(park)[v];
             dg[v] = make_uint4(packed_g[4 * v], packed_g[4 * v + 1], packed_g[4 * v + 2], packed_g[4 * v + 3]);
           }
-          p.lse_l[row] = m_l * p.inv_sqrt_d + logf(l_l);
-          p.lse_g[row] = m_g * p.inv_sqrt_d + logf(l_g);
+          p.lse_l[grow] = m_l * p.inv_sqrt_d + logf(l_l);
+          p.lse_g[grow] = m_g * p.inv_sqrt_d + logf(l_g);
         }
       }
     }
