@@ -132,6 +132,21 @@ P3D_API int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, vo
 P3D_API size_t p3d_attn_fwd_workspace(const p3d_operator *op, unsigned flags);
 
 /*
+ * Forward (inference, no saved state) that allocates nothing and needs no workspace.
+ * No counterpart in the reference.  For callers that cannot allocate device memory --
+ * plugins inside a host framework that owns all device memory, or real-time loops that
+ * must avoid the device synchronisation cudaMalloc / cudaFree can cause.  The caller
+ * passes inputs (op) and outputs y [B,H,N,D], sk, sv [B,G,M,D] as for p3d_attn_fwd.
+ * Runs the neighbour-table kernels; their one scratch buffer (the local-branch output,
+ * B*H*N*D*sizeof(dtype) bytes, at most 16 MiB -- larger inputs return
+ * P3D_ERR_UNSUPPORTED) lives in a fixed array inside the library that every GPU loading
+ * the library keeps until process exit.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress), so make that first call before any stream
+ * capture.  All calls share the array: calls whose kernels overlap on the GPU race.
+ */
+P3D_API int p3d_attn_fwd_noalloc(const p3d_operator *op, void *y, void *sk, void *sv, void *stream);
+
+/*
  * Backward (kernels.py:314-356) from the saved forward state.  Writes dq
  * [B,H,N,D], dkl, dvl, dkg, dvg [B,G,N,D] (dtype), dgate [B,H,N] (gate_dtype)
  * and fp32 dweight [D], dbias [V], dlocal_scale [D], dglobal_scale [D].

@@ -55,6 +55,7 @@ _SIGNATURES = {
     "p3d_attn_fwd": (_c_int, [ctypes.POINTER(Operator), _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_uint,
                               _vp, ctypes.c_size_t, _vp]),
     "p3d_attn_fwd_workspace": (ctypes.c_size_t, [ctypes.POINTER(Operator), ctypes.c_uint]),
+    "p3d_attn_fwd_noalloc": (_c_int, [ctypes.POINTER(Operator), _vp, _vp, _vp, _vp]),
     "p3d_attn_bwd": (_c_int, [ctypes.POINTER(Operator), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                               _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "p3d_attn_bwd_workspace": (ctypes.c_size_t, [ctypes.POINTER(Operator)]),
