@@ -164,7 +164,7 @@ def measured_peaks():
 
 # ------------------------------------------------------------------------- CPU baseline
 
-def cpu_layer_seconds(sample_rows=8192, seed=0):
+def cpu_layer_seconds(sample_rows=65536, seed=0):
     """Seconds for one config-1 layer forward with the CPU restatement of the reference, all host cores.
 
     Projections, RoPE and pooling run for every token; the attention core and the

@@ -58,10 +58,11 @@ P3D_API const char *p3d_last_error(void);
 P3D_API int p3d_abi_version(void);
 /* Number of visible sm_100 devices (0 without a GPU); never fails. */
 P3D_API int p3d_device_count(void);
-/* Read and clear the device-side failure flags of the current device (bit 0: a
- * bounded wait inside a tensor-core kernel timed out and the kernel unwound).
- * Synchronises with the device.  No reference counterpart (the Triton kernels
- * have no device-side waits). */
+/* Read and clear the device-side failure flags of the current device.  Bit 0: a
+ * bounded wait inside a tensor-core kernel timed out and the kernel unwound; bits
+ * 1-4 name the waiting role (2 TMA producer, 4 MMA issuer, 8 softmax / epilogue,
+ * 16 a drain before tensor memory is freed).  Synchronises with the device.  No
+ * reference counterpart (the Triton kernels have no device-side waits). */
 P3D_API int p3d_device_errors(unsigned *flags);
 
 /*

@@ -10,8 +10,15 @@ namespace p3d {
 namespace sm100 {
 
 // Device-side failure bits, kept by each kernel file in its own __device__ word and
-// read back (and cleared) through p3d_device_errors().
-enum : unsigned { kErrTimeout = 1u };
+// read back (and cleared) through p3d_device_errors().  Bit 0 says that a bounded wait
+// gave up; bits 1-4 say which role's wait it was.
+enum : unsigned {
+  kErrTimeout = 1u,
+  kErrProducer = 2u,   // TMA producer
+  kErrMma = 4u,        // MMA issuer
+  kErrSoftmax = 8u,    // softmax / epilogue warps
+  kErrTeardown = 16u   // a drain before TMEM is freed
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -49,9 +56,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait for phase `parity` of an mbarrier, giving up after timeout_ns: then the
-// timeout bit is set in *errors and false is returned, so the caller can unwind
-// instead of spinning forever.
 // Non-blocking test of a phase: cheaper than try_wait when the phase has already completed.
 __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -65,14 +69,31 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Wait for phase `parity` of an mbarrier, giving up after timeout_ns: then the
+// timeout bit is set in *errors and false is returned, so the caller can unwind
+// instead of spinning forever.
+//
+// Elapsed time is the sum of the forward steps of %globaltimer between consecutive
+// polls, each step capped at 1 ms, so that a re-synchronised (stepped) timer can
+// neither end a wait early nor extend it; the SM cycle counter, summed the same way,
+// bounds the wait as well (at 4 cycles per nanosecond of the limit) in case the
+// nanosecond timer stalls.  `role` is or-ed into *errors with kErrTimeout.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned *errors,
-                                          uint64_t timeout_ns = 2000000000ull) {
+                                          uint64_t timeout_ns = 2000000000ull, unsigned role = 0u) {
   if (mbar_test_wait(bar, parity)) return true;
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = global_timer_ns();
+  uint64_t t_last = global_timer_ns(), waited_ns = 0;
+  long long c_last = clock64(), waited_cycles = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if (global_timer_ns() - start > timeout_ns) {
-      atomicOr(errors, kErrTimeout);
+    const uint64_t t = global_timer_ns();
+    const long long c = clock64();
+    const long long dt = (long long)(t - t_last), dc = c - c_last;
+    t_last = t;
+    c_last = c;
+    if (dt > 0) waited_ns += dt < 1000000 ? (uint64_t)dt : 1000000ull;
+    if (dc > 0) waited_cycles += dc < 4000000 ? dc : 4000000;
+    if (waited_ns > timeout_ns || (unsigned long long)waited_cycles > 4ull * timeout_ns) {
+      atomicOr(errors, kErrTimeout | role);
       return false;
     }
   }

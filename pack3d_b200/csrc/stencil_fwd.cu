@@ -57,6 +57,7 @@ constexpr int kThreads = 320;
 constexpr int kProducerWarp = 8, kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kNegInf = -__builtin_huge_valf();
+constexpr uint64_t kWaitNs = 2000000000ull;        // every mbarrier wait gives up after 2 s
 
 static_assert(kKeys % 32 == 0, "chunk size must suit the MMA and TMEM access shapes");
 
@@ -70,8 +71,8 @@ struct Cfg {
   static constexpr int kStageBytes = (4 * kKeyBytes + 1023) / 1024 * 1024;  // local: K_A K_B V_A V_B
   static constexpr int kOlBytes = kRows * D * 2;    // parked local output of one tile
   static constexpr int kFixed = 2 * kQBytes + 2 * kOlBytes + 1024;
-  // 3 or 4 stages: at least chunks c .. c+2 resident, and at most 4 so that the stage
-  // release signal (a QK^T commit of tile B, see the producer) cannot alias phases.
+  // 3 or 4 stages: at least chunks c .. c+2 resident (S of chunk c+2 is issued while PV of
+  // chunk c may still read its stage); at most 4, the size of the per-stage barrier arrays.
   static constexpr int kStages = (227 * 1024 - 2048 - kFixed) / kStageBytes > 4 ? 4
                                                                                  : (227 * 1024 - 2048 - kFixed) / kStageBytes;
   // at least 116 KB so that one CTA (which owns all 512 TMEM columns) fits per SM
@@ -84,11 +85,17 @@ struct Cfg {
 // TMEM columns of tile t (base t*256): S buffers [0, 96) and [96, 192), O [192, 192 + D).
 constexpr uint32_t kSBuf = 96, kColO = 192;
 
+// S_t(c) is complete when its commit arrives.  Tile A commits to kSReady[0][c%2]; tile B
+// commits S_B(0), S_B(1) to kSReady[1][c] and S_B(c), c >= 2, to kEmpty[(c-2) % kStages]:
+// S_B(c) is issued after PV_B(c-2) has completed (and every MMA before it), so its
+// completion is also the moment chunk c-2's ring stage is free.  One release barrier per
+// stage keeps every parity wait unambiguous (see the producer).
 enum Bar {
   kQFull = 0,
-  kFull = 1,                  // [stage]; stages are released through kSReady (see producer)
-  kSReady = kFull + 4,        // [tile][buf]
-  kPReady = kSReady + 4,      // [tile][buf]
+  kFull = 1,                  // [stage]
+  kSReady = kFull + 4,        // [tile][buf] (tile B: chunks 0 and 1 only)
+  kEmpty = kSReady + 4,       // [stage]: released by S_B(c + 2), c the chunk it held
+  kPReady = kEmpty + 4,       // [tile][buf]
   kPvDone = kPReady + 4,      // [tile][buf]: PV of the chunk that last used the buffer is done
   kOReady = kPvDone + 4,      // [tile]
   kDrain = kOReady + 2,       // MMA thread: every MMA it issued has completed
@@ -229,6 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar(kQFull), 1);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(bar(kFull + s), 1);
+      mbar_init(bar(kEmpty + s), 1);
     }
     for (int i = 0; i < 4; ++i) {
       mbar_init(bar(kSReady + i), 1);
@@ -269,14 +277,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       for (int ch = 0; ch < n_chunks; ++ch) {
         const int s = ch % C::kStages;
-        // Stage s last held chunk y = ch - kStages; its final reader is PV_B(y), and the MMA
-        // thread issues S_B(x), x = y + 2, right after it, so that commit's completion frees
-        // the stage.  Parity is unambiguous: the barrier's next completion, S_B(x + 2), needs
-        // chunk ch - kStages + 4 >= ch (kStages <= 4), which this thread has not loaded yet.
-        if (ch >= C::kStages) {
-          const int x = ch - C::kStages + 2;
-          if (!mbar_wait(bar(kSReady + 2 + (x & 1)), (x >> 1) & 1, &g_fwd_errors)) break;
-        }
+        // Stage s last held chunk ch - kStages; kEmpty[s] completes once per release, so
+        // this is its completion number k = ch / kStages - 1.  A parity wait only tells
+        // completion k from its neighbours if both are ruled out: k - 1 was awaited here one
+        // ring turn ago (or k = 0 on a fresh barrier), and k + 1 is S_B(ch + 2), which needs
+        // chunk ch + 2, not loaded yet.  (Releasing through the two S-buffer barriers of tile
+        // B instead is ambiguous: their first waits can be one completion early or late.)
+        if (ch >= C::kStages &&
+            !mbar_wait(bar(kEmpty + s), (ch / C::kStages - 1) & 1, &g_fwd_errors, kWaitNs, kErrProducer))
+          break;
         const uint32_t stage = ring + s * C::kStageBytes;
         const uint32_t full = bar(kFull + s);
         if (ch < kLocalChunks) {
@@ -302,15 +311,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Never leave copies in flight into shared memory this CTA is about to give up: wait
       // (bounded) for the Q tiles and the last loads of every stage.  On the normal path
       // these phases completed long ago; after a timed-out wait they may still be landing.
-      mbar_wait(bar(kQFull), 0, &g_fwd_errors, 100000000ull);
+      mbar_wait(bar(kQFull), 0, &g_fwd_errors, kWaitNs, kErrTeardown);
       for (int ch = issued > C::kStages ? issued - C::kStages : 0; ch < issued; ++ch)
-        mbar_wait(bar(kFull + ch % C::kStages), (ch / C::kStages) & 1, &g_fwd_errors, 100000000ull);
+        mbar_wait(bar(kFull + ch % C::kStages), (ch / C::kStages) & 1, &g_fwd_errors, kWaitNs, kErrTeardown);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(128, kKeys, BF16, false);
       constexpr uint32_t idesc_pv = idesc_f16(128, D, BF16, true);
+      // Commits issued per barrier: teardown waits for the last phase of each, so that no
+      // arrive from a commit can land after the CTA has exited.
+      uint32_t commits[kNumBars];
+      for (int i = 0; i < kNumBars; ++i) commits[i] = 0u;
+      auto commit = [&](int b) {
+        mma_commit(bar(b));
+        ++commits[b];
+      };
       // S_t(ch) = Q_t K(ch)^T into S buffer ch%2, then signal the tile's softmax warps.
       auto issue_s = [&](int t, int ch) {
         const uint32_t stage = ring + (ch % C::kStages) * C::kStageBytes;
@@ -320,11 +337,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < C::kK; ++c)
           mma_ss(t_s, desc_sw32(q_t + c * C::kBoxQ, 16, 256), desc_sw32(k_base + c * C::kBoxK, 16, 256), idesc_s,
                  c > 0 ? 1u : 0u);
-        mma_commit(bar(kSReady + 2 * t + (ch & 1)));
+        commit(t == 1 && ch >= 2 ? kEmpty + (ch - 2) % C::kStages : kSReady + 2 * t + (ch & 1));
       };
       // O_t += P_t(c) V(c) once the softmax warps have written P_t(c).
       auto issue_pv = [&](int t, int c) -> bool {
-        if (!mbar_wait(bar(kPReady + 2 * t + (c & 1)), (c >> 1) & 1, &g_fwd_errors)) return false;
+        if (!mbar_wait(bar(kPReady + 2 * t + (c & 1)), (c >> 1) & 1, &g_fwd_errors, kWaitNs, kErrMma)) return false;
         tc_fence_after();
         const uint32_t stage = ring + (c % C::kStages) * C::kStageBytes;
         const uint32_t v_base = c < kLocalChunks ? stage + (2 + t) * C::kKeyBytes : stage + C::kKeyBytes;
@@ -333,11 +350,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < kKeys / 16; ++j)
           mma_ts(tmem + t * 256 + kColO, t_p + 8 * j, desc_sw32(v_base + j * 512, C::kBoxK, 256), idesc_pv,
                  (first && j == 0) ? 0u : 1u);
-        mma_commit(bar(kPvDone + 2 * t + (c & 1)));
+        commit(kPvDone + 2 * t + (c & 1));
         return true;
       };
       auto wait_full = [&](int ch) -> bool {
-        if (!mbar_wait(bar(kFull + ch % C::kStages), (ch / C::kStages) & 1, &g_fwd_errors)) return false;
+        if (!mbar_wait(bar(kFull + ch % C::kStages), (ch / C::kStages) & 1, &g_fwd_errors, kWaitNs, kErrMma))
+          return false;
         tc_fence_after();
         return true;
       };
@@ -345,14 +363,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // tcgen05.mma ops are only ordered among themselves when they share an accumulator,
       // so PV_t(c) must have completed before S_t(c+2) is issued.
       auto wait_pv = [&](int t, int c) -> bool {
-        if (!mbar_wait(bar(kPvDone + 2 * t + (c & 1)), (c >> 1) & 1, &g_fwd_errors)) return false;
+        if (!mbar_wait(bar(kPvDone + 2 * t + (c & 1)), (c >> 1) & 1, &g_fwd_errors, kWaitNs, kErrMma)) return false;
         tc_fence_after();
         return true;
       };
       // Prologue: both S buffers of both tiles.  Steady state per chunk c:
       //   PV_A(c), PV_B(c), [PV_A(c) done] S_A(c+2), [PV_B(c) done] S_B(c+2)
       // Waiting for PV_A(c) while PV_B(c) still executes keeps the tensor pipe busy.
-      bool ok = mbar_wait(bar(kQFull), 0, &g_fwd_errors);
+      bool ok = mbar_wait(bar(kQFull), 0, &g_fwd_errors, kWaitNs, kErrMma);
       for (int ch = 0; ok && ch < 2; ++ch) {
         ok = wait_full(ch);
         if (!ok) break;
@@ -371,13 +389,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         issue_s(1, c + 2);  // its commit also releases chunk c's stage to the producer
       }
       if (ok) {
-        mma_commit(bar(kOReady));
-        mma_commit(bar(kOReady + 1));
+        commit(kOReady);
+        commit(kOReady + 1);
       }
       // TMEM is freed after the final __syncthreads: make sure every MMA issued above has
-      // completed first, on the normal path and after a timed-out wait alike.
-      mma_commit(bar(kDrain));
-      mbar_wait(bar(kDrain), 0, &g_fwd_errors, 100000000ull);
+      // completed, and every commit has arrived, first -- on the normal path and after a
+      // timed-out wait alike.
+      commit(kDrain);
+      for (int i = 0; i < kNumBars; ++i)
+        if (commits[i]) mbar_wait(bar(i), (commits[i] - 1) & 1, &g_fwd_errors, kWaitNs, kErrTeardown);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
@@ -405,14 +425,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sc = p.sc;
     float m_l = kNegInf, l_l = 0.f, m_g = kNegInf, l_g = 0.f;
     bool ok = true;
+    // Bounded wait with a warp-uniform result: the warp reconverges and leaves together,
+    // so the warp-collective TMEM loads and stores that follow run on the whole warp.
+    auto wait_warp = [&](uint32_t b, uint32_t parity) -> bool {
+      const bool r = mbar_wait(b, parity, &g_fwd_errors, kWaitNs, kErrSoftmax);
+      const bool all = __all_sync(0xffffffffu, r);
+      if (all) tc_fence_after();
+      return all;
+    };
     // Completion of PV_t(c), needed before O is read or rescaled.  Testing the phase only
     // when needed is sound: the next completion of that buffer's barrier is PV_t(c+2), which
     // needs this warp's P of chunk c+2.
-    auto wait_pv_done = [&](int c) -> bool {
-      const bool r = mbar_wait(bar(kPvDone + 2 * t + (c & 1)), (c >> 1) & 1, &g_fwd_errors);
-      if (r) tc_fence_after();
-      return r;
-    };
+    auto wait_pv_done = [&](int c) -> bool { return wait_warp(bar(kPvDone + 2 * t + (c & 1)), (c >> 1) & 1); };
     for (int ch = 0; ch < n_chunks; ++ch) {
       const int buf = ch & 1;
       const uint32_t t_s = t_tile + buf * kSBuf;
@@ -436,9 +460,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
       }
-      ok = mbar_wait(bar(kSReady + 2 * t + buf), (ch >> 1) & 1, &g_fwd_errors);
+      // S_t(ch) complete (the barrier map is described at enum Bar).  Each is completion
+      // number k of its barrier with k - 1 awaited by this warp before (or k = 0), and
+      // completion k + 1 needs this warp's P of a later chunk.
+      if (t == 1 && ch >= 2)
+        ok = wait_warp(bar(kEmpty + (ch - 2) % C::kStages), ((ch - 2) / C::kStages) & 1);
+      else
+        ok = wait_warp(bar(kSReady + 2 * t + buf), (ch >> 1) & 1);
       if (!ok) break;
-      tc_fence_after();
       const bool local = ch < kLocalChunks;
       const int zp = z0 + kTZ * t - kR + ch;
       const bool active = !local || ((unsigned)(ch - qz) <= 2u * kR && zp >= 0 && zp < p.Z);  // warp-uniform
@@ -484,9 +513,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(bar(kPReady + 2 * t + buf));
     }
     // ---- epilogue: normalise the global branch, mix, store through the row map
-    if (ok) ok = mbar_wait(bar(kOReady + t), 0, &g_fwd_errors);
+    if (ok) ok = wait_warp(bar(kOReady + t), 0);
     if (ok) {
-      tc_fence_after();
       uint32_t og[D];
 #pragma unroll
       for (int c = 0; c < D / 16; ++c) tmem_ld16(t_o + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(og + 16 * c));
@@ -525,7 +553,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    tmem_wait_st();  // a warp that left the chunk loop early may still have TMEM stores in flight
   }
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {

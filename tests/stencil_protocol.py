@@ -1,0 +1,263 @@
+"""Executable model of the synchronisation protocol of the tensor-core stencil forward.
+
+The kernel (``pack3d_b200/csrc/stencil_fwd.cu``) coordinates one TMA producer thread,
+one MMA-issuing thread and eight softmax warps through mbarriers that are waited on by
+*phase parity*.  A parity wait cannot count: it passes when the barrier's current phase
+parity differs from the awaited one, and a freshly initialised barrier reports its
+"preceding phase" (parity 1) as complete.  This module replays that protocol step by
+step -- every role as a program, TMA copies and tensor-core operations as asynchronous
+events that complete later (MMAs in issue order) -- under random interleavings, with
+the hardware's parity semantics, and checks:
+
+* every wait passes only once the completion it stands for has happened;
+* no barrier gets an arrival while its pending count is zero (an over-arrival);
+* a ring stage is overwritten only after every MMA that reads its previous chunk has
+  completed, and is read only after its copy has landed;
+* a TMEM S buffer is rewritten only after the PV MMA reading its P has completed, P is
+  read by PV only after the four softmax warps stored it, and O is read or rescaled only
+  between PV completions;
+* every role finishes (no deadlock).
+
+The model mirrors the kernel's barrier map and wait parities one for one; a change to
+either must be made in both.  ``release="sready"`` replays the earlier stage-release
+scheme (through tile B's two S-ready barriers), which these checks reject.
+"""
+from __future__ import annotations
+
+import random
+from dataclasses import dataclass, field
+
+LOCAL_CHUNKS = 8
+
+
+class ProtocolError(AssertionError):
+    pass
+
+
+@dataclass
+class Barrier:
+    name: str
+    expected: int
+    pending: int = 0
+    tx: int = 0
+    completions: int = 0
+
+    def __post_init__(self):
+        self.pending = self.expected
+
+    def _maybe_complete(self):
+        if self.pending == 0 and self.tx == 0:
+            self.completions += 1
+            self.pending = self.expected
+
+    def arrive(self, tx=0):
+        if self.pending == 0:
+            raise ProtocolError(f"over-arrival on {self.name} (phase {self.completions})")
+        self.pending -= 1
+        self.tx += tx
+        self._maybe_complete()
+
+    def complete_tx(self, nbytes):
+        self.tx -= nbytes
+        self._maybe_complete()
+
+    def passes(self, parity):
+        """Hardware try_wait.parity: true iff the current phase parity differs."""
+        return (self.completions & 1) != parity
+
+
+@dataclass
+class State:
+    n_chunks: int
+    stages: int
+    bars: dict = field(default_factory=dict)
+    mma_queue: list = field(default_factory=list)   # issued, not completed (in order)
+    tma_inflight: list = field(default_factory=list)
+    mma_done: set = field(default_factory=set)       # ("S"|"PV", tile, chunk)
+    stage_chunk: dict = field(default_factory=dict)  # stage -> chunk whose copy was issued
+    stage_landed: dict = field(default_factory=dict)  # stage -> chunk whose copy landed
+    p_stored: dict = field(default_factory=dict)     # (tile, chunk) -> warps that stored P
+    pv_issued: set = field(default_factory=set)
+
+    def bar(self, name):
+        return self.bars[name]
+
+
+def _wait(state, name, parity, completion):
+    """A parity wait that stands for completion number `completion` of barrier `name`.
+
+    Returns True when it passes; raises when it passes before that completion."""
+    b = state.bar(name)
+    if not b.passes(parity):
+        return False
+    if b.completions < completion + 1:
+        raise ProtocolError(f"wait on {name} for completion {completion} passed at {b.completions}")
+    return True
+
+
+def producer(state, release):
+    """Lane 0 of the producer warp (stencil_fwd.cu, ``warp == kProducerWarp``)."""
+    k = state.stages
+    for ch in range(state.n_chunks):
+        s = ch % k
+        if ch >= k:
+            if release == "empty":
+                while not _wait(state, f"empty{s}", (ch // k - 1) & 1, ch // k - 1):
+                    yield ("wait", f"empty{s}")
+            else:  # earlier scheme: tile B's S-ready barrier of S_B(x), x = ch - k + 2
+                x = ch - k + 2
+                while not _wait(state, f"sready1{x & 1}", (x >> 1) & 1, x >> 1):
+                    yield ("wait", f"sready1{x & 1}")
+        old = state.stage_chunk.get(s)
+        if old is not None:
+            for op in (("S", 0, old), ("S", 1, old), ("PV", 0, old), ("PV", 1, old)):
+                if op not in state.mma_done:
+                    raise ProtocolError(f"stage {s} overwritten with chunk {ch} while {op} is outstanding")
+        state.bar(f"full{s}").arrive(tx=1)
+        state.stage_chunk[s] = ch
+        state.tma_inflight.append((s, ch))
+        yield ("step", None)
+
+
+def mma(state):
+    """The MMA-issuing thread (``warp == kMmaWarp``)."""
+    k, n = state.stages, state.n_chunks
+
+    def commit(name):
+        state.mma_queue.append(("commit", name))
+
+    def issue_s(t, ch):
+        s = ch % k
+        if state.stage_landed.get(s) != ch:
+            raise ProtocolError(f"S_{t}({ch}) reads stage {s} before chunk {ch} landed")
+        if ch >= 2 and ("PV", t, ch - 2) not in state.mma_done:
+            raise ProtocolError(f"S_{t}({ch}) overwrites P of chunk {ch - 2} before PV_{t}({ch - 2}) completed")
+        state.mma_queue.append(("S", t, ch))
+        commit(f"empty{(ch - 2) % k}" if (t == 1 and ch >= 2 and state.release == "empty")
+               else f"sready{t}{ch & 1}")
+
+    def waits(name, parity, completion):
+        while not _wait(state, name, parity, completion):
+            yield ("wait", name)
+
+    yield from waits("qfull", 0, 0)
+    for ch in range(2):
+        yield from waits(f"full{ch % k}", (ch // k) & 1, ch // k)
+        issue_s(0, ch)
+        issue_s(1, ch)
+        yield ("step", None)
+    for c in range(n):
+        for t in range(2):
+            yield from waits(f"pready{t}{c & 1}", (c >> 1) & 1, c >> 1)
+            if len(state.p_stored.get((t, c), ())) != 4:
+                raise ProtocolError(f"PV_{t}({c}) issued before all four warps stored P")
+            state.mma_queue.append(("PV", t, c))
+            state.pv_issued.add((t, c))
+            commit(f"pvdone{t}{c & 1}")
+            yield ("step", None)
+        if c + 2 >= n:
+            continue
+        ch = c + 2
+        yield from waits(f"full{ch % k}", (ch // k) & 1, ch // k)
+        yield from waits("pvdone0" + str(c & 1), (c >> 1) & 1, c >> 1)
+        issue_s(0, ch)
+        yield ("step", None)
+        yield from waits("pvdone1" + str(c & 1), (c >> 1) & 1, c >> 1)
+        issue_s(1, ch)
+        yield ("step", None)
+    commit("oready0")
+    commit("oready1")
+    commit("drain")
+    yield from waits("drain", 0, 0)
+
+
+def softmax(state, t, w, rng):
+    """Softmax warp w of tile t (warps 0-7)."""
+    k, n = state.stages, state.n_chunks
+
+    def waits(name, parity, completion):
+        while not _wait(state, name, parity, completion):
+            yield ("wait", name)
+
+    def pv_done(c):
+        yield from waits(f"pvdone{t}{c & 1}", (c >> 1) & 1, c >> 1)
+        if ("PV", t, c) not in state.mma_done:
+            raise ProtocolError(f"O of tile {t} touched before PV_{t}({c}) completed")
+        if (t, c + 1) in state.pv_issued:
+            raise ProtocolError(f"O of tile {t} touched after PV_{t}({c + 1}) was issued")
+
+    for ch in range(n):
+        if ch == LOCAL_CHUNKS:
+            yield from pv_done(LOCAL_CHUNKS - 1)
+        if t == 1 and ch >= 2 and state.release == "empty":
+            yield from waits(f"empty{(ch - 2) % k}", ((ch - 2) // k) & 1, (ch - 2) // k)
+        else:
+            yield from waits(f"sready{t}{ch & 1}", (ch >> 1) & 1, ch >> 1)
+        if ("S", t, ch) not in state.mma_done:
+            raise ProtocolError(f"S_{t}({ch}) read before it completed")
+        yield ("step", None)
+        state.p_stored.setdefault((t, ch), set()).add(w)
+        if ch not in (0, LOCAL_CHUNKS) and rng.random() < 0.3:  # data-dependent rescale of O
+            yield from pv_done(ch - 1)
+        state.bar(f"pready{t}{ch & 1}").arrive()
+        yield ("step", None)
+    yield from waits(f"oready{t}", 0, 0)
+
+
+def run(n_chunks=14, stages=4, seed=0, release="empty", max_steps=400000):
+    """Replay one random interleaving; raises ProtocolError on a violation or deadlock."""
+    rng = random.Random(seed)
+    state = State(n_chunks=n_chunks, stages=stages)
+    state.release = release
+    bars = {"qfull": 1, "drain": 1, "oready0": 1, "oready1": 1}
+    for s in range(4):
+        bars[f"full{s}"] = 1
+        bars[f"empty{s}"] = 1
+    for t in range(2):
+        for b in range(2):
+            bars[f"sready{t}{b}"] = 1
+            bars[f"pready{t}{b}"] = 4
+            bars[f"pvdone{t}{b}"] = 1
+    state.bars = {name: Barrier(name, cnt) for name, cnt in bars.items()}
+    state.bar("qfull").arrive(tx=0)
+    roles = {"producer": producer(state, release), "mma": mma(state)}
+    for t in range(2):
+        for w in range(4):
+            roles[f"softmax{t}{w}"] = softmax(state, t, w, random.Random(rng.random()))
+    epoch = 0            # bumped whenever an asynchronous event changes some barrier
+    blocked = {}         # role -> epoch of its last unsuccessful wait
+    for _ in range(max_steps):
+        events = ((["<copy lands>"] if state.tma_inflight else []) +
+                  (["<tensor op completes>"] if state.mma_queue else []))
+        if not roles and not events:
+            return state
+        live = [r for r in roles if blocked.get(r) != epoch]
+        if not live and not events:
+            raise ProtocolError(f"deadlock: {sorted(roles)} all wait")
+        choice = rng.choice(live + events * 3)
+        if choice == "<copy lands>":
+            s, ch = state.tma_inflight.pop(rng.randrange(len(state.tma_inflight)))
+            state.stage_landed[s] = ch
+            state.bar(f"full{s}").complete_tx(1)
+            epoch += 1
+        elif choice == "<tensor op completes>":
+            op = state.mma_queue.pop(0)  # tensor-core operations complete in issue order
+            if op[0] == "commit":
+                state.bar(op[1]).arrive()
+            else:
+                state.mma_done.add(op)
+            epoch += 1
+        else:
+            try:
+                kind, _ = next(roles[choice])
+            except StopIteration:
+                del roles[choice]
+                blocked.pop(choice, None)
+                epoch += 1
+                continue
+            if kind == "wait":
+                blocked[choice] = epoch
+            else:
+                blocked.pop(choice, None)
+                epoch += 1   # a role's step (an arrive, an issue) may unblock others
+    raise ProtocolError(f"no progress after {max_steps} steps: roles left {sorted(roles)}")

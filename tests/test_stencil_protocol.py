@@ -1,0 +1,28 @@
+"""CPU check of the stencil forward's mbarrier protocol (model in tests/stencil_protocol.py).
+
+The kernel's producer / MMA / softmax roles are replayed under many random
+interleavings with the hardware's parity-wait semantics.  The shipped barrier map must
+survive all of them; the earlier stage-release scheme, which let the producer pass its
+first release waits before the MMAs had finished with the stage, must be caught.
+"""
+import pytest
+
+import stencil_protocol as sp
+
+
+@pytest.mark.parametrize("stages", [3, 4])
+@pytest.mark.parametrize("n_chunks", [10, 15])
+def test_protocol_holds_under_random_interleavings(stages, n_chunks):
+    for seed in range(150):
+        sp.run(n_chunks=n_chunks, stages=stages, seed=seed, release="empty")
+
+
+def test_model_rejects_the_ambiguous_release_scheme():
+    failures = 0
+    for seed in range(100):
+        try:
+            sp.run(n_chunks=14, stages=4, seed=seed, release="sready")
+        except sp.ProtocolError as err:
+            assert "passed at 0" in str(err)
+            failures += 1
+    assert failures > 0
