@@ -195,8 +195,17 @@ int gather_rows(const void *src, void *dst, const int32_t *map, int64_t slabs, i
   return P3D_OK;
 }
 
+// The tensor-core backward needs what the tensor-core forward needs, and at least two
+// summaries (with one the global softmax is constant: no score gradient, reference
+// kernels.py:198-199).
+bool use_stencil_bwd(const p3d_operator *op) {
+  return op->stencil && summaries_of(op) >= 2 &&
+         stencil_fwd_supported(op->dtype, op->head_dim, op->radius, summaries_of(op));
+}
+
 struct BwdBuffers {
   void *dol, *dog;
+  void *q_r, *kl_r, *vl_r, *dol_r, *dog_r;  // raster-order copies (tensor-core path, permuted storage)
   float *delta_l, *delta_g, *dsl_part, *dsg_part, *dk_part, *dv_part, *dsk, *dsv, *dw_part, *db_part, *tmp;
   int64_t mix_rows, pool_rows;
   int splits;
@@ -216,6 +225,15 @@ size_t bwd_layout(const p3d_operator *op, void *base, size_t cap, BwdBuffers *b)
   const int64_t d = op->head_dim;
   b->dol = c.take<char>(rows * d * es);
   b->dog = c.take<char>(rows * d * es);
+  b->q_r = b->kl_r = b->vl_r = b->dol_r = b->dog_r = nullptr;
+  if (use_stencil_bwd(op) && op->raster_to_packed) {
+    const int64_t kv_rows = bg * op->tokens;
+    b->q_r = c.take<char>(rows * d * es);
+    b->dol_r = c.take<char>(rows * d * es);
+    b->dog_r = c.take<char>(rows * d * es);
+    b->kl_r = c.take<char>(kv_rows * d * es);
+    b->vl_r = c.take<char>(kv_rows * d * es);
+  }
   b->delta_l = c.take<float>(rows);
   b->delta_g = c.take<float>(rows);
   b->dsl_part = c.take<float>(b->mix_rows * d);
@@ -272,7 +290,8 @@ int p3d_device_count(void) {
 int p3d_device_errors(unsigned *flags) {
   P3D_CHECK_ARG(flags != nullptr, "p3d_device_errors: null output");
   *flags = 0;
-  return take_fwd_errors(flags);
+  if (int st = take_fwd_errors(flags)) return st;
+  return take_bwd_errors(flags);
 }
 
 int p3d_pool_fwd(const void *k, const void *v, const float *weight, const float *bias, const int32_t *blocks,
@@ -413,9 +432,48 @@ int p3d_attn_bwd(const p3d_operator *op, const void *dy, const void *sk, const v
   if (int st = launch_mix_bwd(mix, s)) return st;
 
   const IndexedArgs a = indexed_args(op, sk, sv);
-  if (int st = launch_local_dq_indexed(a, b.dol, lse_l, b.delta_l, dq, s)) return st;
-  if (int st = launch_local_dkv_indexed(a, b.dol, lse_l, b.delta_l, dkl, dvl, s)) return st;
-  if (int st = launch_global_dq(a, b.dog, lse_g, b.delta_g, dq, s)) return st;
+  if (use_stencil_bwd(op)) {
+    StencilBwdArgs t{};
+    t.dtype = op->dtype;
+    t.batch = op->batch;
+    t.heads = op->heads;
+    t.kv_heads = op->kv_heads;
+    t.head_dim = d;
+    t.summaries = M;
+    for (int i = 0; i < 3; ++i) t.grid[i] = op->grid[i];
+    t.q = op->q;
+    t.kl = op->kl;
+    t.vl = op->vl;
+    t.dol = b.dol;
+    t.dog = b.dog;
+    if (op->raster_to_packed) {
+      const size_t row_bytes = (size_t)d * dtype_size(op->dtype);
+      const void *src[5] = {op->q, op->kl, op->vl, b.dol, b.dog};
+      void *dst[5] = {b.q_r, b.kl_r, b.vl_r, b.dol_r, b.dog_r};
+      const int64_t heads[5] = {bh, bg, bg, bh, bh};
+      for (int i = 0; i < 5; ++i)
+        if (int st = gather_rows(src[i], dst[i], op->raster_to_packed, heads[i], op->tokens, row_bytes, s)) return st;
+      t.q = b.q_r;
+      t.kl = b.kl_r;
+      t.vl = b.vl_r;
+      t.dol = b.dol_r;
+      t.dog = b.dog_r;
+    }
+    t.sk = sk;
+    t.sv = sv;
+    t.lse_l = lse_l;
+    t.lse_g = lse_g;
+    t.delta_l = b.delta_l;
+    t.delta_g = b.delta_g;
+    t.raster_to_packed = op->raster_to_packed;
+    t.dq = dq;
+    if (int st = launch_stencil_bwd_dq(t, s)) return st;
+    if (int st = launch_local_dkv_indexed(a, b.dol, lse_l, b.delta_l, dkl, dvl, s)) return st;
+  } else {
+    if (int st = launch_local_dq_indexed(a, b.dol, lse_l, b.delta_l, dq, s)) return st;
+    if (int st = launch_local_dkv_indexed(a, b.dol, lse_l, b.delta_l, dkl, dvl, s)) return st;
+    if (int st = launch_global_dq(a, b.dog, lse_g, b.delta_g, dq, s)) return st;
+  }
   if (int st = launch_global_dkv(a, b.dog, lse_g, b.delta_g, b.splits, b.dk_part, b.dv_part, s)) return st;
   if (int st = launch_sum_middle(b.dk_part, b.dsk, bg, b.splits, (int64_t)M * d, s)) return st;
   if (int st = launch_sum_middle(b.dv_part, b.dsv, bg, b.splits, (int64_t)M * d, s)) return st;

@@ -105,4 +105,18 @@ int take_fwd_errors(unsigned *flags);
 bool stencil_fwd_supported(int dtype, int head_dim, const int radius[3], int summaries);
 int launch_stencil_fwd(const StencilFwdArgs &a, cudaStream_t s);
 
+// Tensor-core backward over a complete radius-2 stencil (stencil_bwd.cu).
+struct StencilBwdArgs {
+  int dtype;
+  int batch, heads, kv_heads, head_dim, summaries;
+  int grid[3];
+  const void *q, *kl, *vl, *dol, *dog;  // raster order (contiguous [B,H|G,Z,Y,X,D])
+  const void *sk, *sv;                  // [B,G,M,D]
+  const float *lse_l, *lse_g, *delta_l, *delta_g;  // [B*H, N] in the layout's row order
+  const int32_t *raster_to_packed;      // row map of lse / delta / outputs (NULL = raster)
+  void *dq;                             // [B,H,N,D] in the layout's row order
+};
+int launch_stencil_bwd_dq(const StencilBwdArgs &a, cudaStream_t s);
+int take_bwd_errors(unsigned *flags);
+
 }  // namespace p3d

@@ -1,0 +1,530 @@
+// Stage (d), query side: dQ of the fused local + global attention on tensor cores.
+//
+// Restates the query-gradient half of the reference backward (kernels.py:131-150 local,
+// :180-206 global; stencil.py:91-147 for the spatial local form) for a complete radius-2
+// voxel stencil in bf16 / f16.  With P recomputed from the saved logsumexp,
+//   dS = P * (dO V^T - Delta) / sqrt(D),   dQ = dS K
+// per branch (local: dO = dO_l, K/V = the 5x5x5 neighbours; global: dO = dO_g, K/V = all
+// summaries).  dS is rounded to the storage dtype before the product (the reference does
+// the same for the global branch, kernels.py:197); the two branch gradients are each
+// rounded, then added and rounded again (kernels.py:202-206).
+//
+// Work unit and chunk sequence are those of the forward kernel (stencil_fwd.cu): one
+// (batch, head), an 8x4x8 query box = two 128-row tiles, 8 local chunks (halo planes of an
+// 8x12 window) then ceil(M/96) global chunks.  Per tile, TMEM holds S [0, 96), dP
+// [96, 192) and the dQ accumulator [192, 192 + D).  Per chunk the MMA thread issues
+// S = Q K^T and dP = dO V^T; the softmax warps turn them into dS, written back as 16-bit
+// pairs over the first 48 dP columns, and the MMA thread accumulates dQ += dS K with dS as
+// the TMEM A operand and the K chunk (already in shared memory for S) read MN-major as B.
+// S of the next chunk is issued as soon as the softmax warps have released this chunk,
+// while dQ of this chunk runs; dP of the next chunk waits for dQ to finish reading dS.
+//
+// Roles: warps 0-3 tile A, 4-7 tile B, warp 8 TMA producer, warp 9 MMA issuer.  Every
+// mbarrier wait is bounded and every parity wait is unambiguous: each barrier completes
+// once per chunk (the ring's release barriers once per stage use) and each waiter awaits
+// its completions in order, its next completion needing the waiter's own next step.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
+
+namespace p3d {
+namespace {
+using namespace sm100;
+
+__device__ unsigned g_bwd_errors = 0;  // failure bits of the kernels in this file
+
+constexpr int kR = 2;
+constexpr int kTZ = 4, kTY = 4, kTX = 8;
+constexpr int kHY = kTY + 2 * kR, kHX = kTX + 2 * kR, kHZ = kTZ + 2 * kR;
+constexpr int kKeys = kHY * kHX;  // 96 keys per chunk
+constexpr int kLocalChunks = kHZ;
+constexpr int kSumRows = kKeys;
+constexpr int kRows = 128;
+constexpr int kThreads = 320;
+constexpr int kProducerWarp = 8, kMmaWarp = 9;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D>
+struct DqCfg {
+  static constexpr int kK = D / 16;
+  static constexpr int kBoxQ = kRows * 32;
+  static constexpr int kBoxK = kKeys * 32;
+  static constexpr int kQBytes = kK * kBoxQ;      // one 128-row tile of Q, dO_l or dO_g
+  static constexpr int kKeyBytes = kK * kBoxK;    // one chunk of K or V
+  static constexpr int kStageBytes = (4 * kKeyBytes + 1023) / 1024 * 1024;
+  static constexpr int kParkBytes = kRows * D * 2;
+  static constexpr int kFixed = 6 * kQBytes + 2 * kParkBytes + 1024;
+  static constexpr int kRoom = (227 * 1024 - 2048 - kFixed) / kStageBytes;
+  static constexpr int kStages = kRoom > 4 ? 4 : kRoom;
+  static constexpr int kSmemNeed = kFixed + kStages * kStageBytes;
+  static constexpr int kSmemBytes = kSmemNeed > 116 * 1024 ? kSmemNeed : 116 * 1024;
+  static_assert(kStages >= 2, "the ring must hold two chunks");
+  static_assert(kSmemBytes <= 225 * 1024, "shared memory budget");
+};
+
+constexpr uint32_t kColS = 0, kColDP = 96, kColDQ = 192;
+
+enum DqBar {
+  kQFull = 0,
+  kFull = 1,                 // [stage]
+  kEmpty = kFull + 4,        // [stage]: released by the commit after dQ_B of the chunk it held
+  kSReady = kEmpty + 4,      // [tile]: S_t(c) complete
+  kDPReady = kSReady + 2,    // [tile]: dP_t(c) complete
+  kDSReady = kDPReady + 2,   // [tile]: the tile's 4 softmax warps stored dS_t(c) (count 4)
+  kDQDone = kDSReady + 2,    // [tile]: dQ_t(c) complete
+  kDrain = kDQDone + 2,
+  kNumBars = kDrain + 1
+};
+
+struct DqParams {
+  int Z, Y, X, tiles_z, tiles_y, tiles_x;
+  int heads, kv_heads, summaries, global_chunks;
+  int64_t tokens;
+  float sc;        // log2(e) / sqrt(D)
+  float inv_sqrt_d;
+  const float *lse_l, *lse_g, *delta_l, *delta_g;  // [B*H, N] in the layout's row order
+  const int32_t *map;                               // raster -> packed rows (nullptr: raster)
+  void *dq;
+};
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  return BF16 ? pack_bf16(lo, hi) : pack_f16(lo, hi);
+}
+
+template <bool BF16>
+__device__ __forceinline__ float2 unpack2(uint32_t v) {
+  if constexpr (BF16) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&v));
+  } else {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&v));
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ float round_storage(float v) {
+  const float2 r = unpack2<BF16>(pack2<BF16>(v, 0.f));
+  return r.x;
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    stencil_bwd_dq_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdol,
+                          const __grid_constant__ CUtensorMap tdog, const __grid_constant__ CUtensorMap tkl,
+                          const __grid_constant__ CUtensorMap tvl, const __grid_constant__ CUtensorMap tsk,
+                          const __grid_constant__ CUtensorMap tsv, const DqParams p) {
+  using C = DqCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[kNumBars];
+  __shared__ uint32_t tmem_holder;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int unit = blockIdx.x;
+  const int tx = unit % p.tiles_x;
+  unit /= p.tiles_x;
+  const int ty = unit % p.tiles_y;
+  unit /= p.tiles_y;
+  const int tz = unit % p.tiles_z;
+  const int bh = unit / p.tiles_z;
+  const int x0 = tx * kTX, y0 = ty * kTY, z0 = tz * 2 * kTZ;
+  const int b = bh / p.heads, h = bh % p.heads;
+  const int bg = b * p.kv_heads + h / (p.heads / p.kv_heads);
+  const int n_chunks = kLocalChunks + p.global_chunks;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t q_smem = base;                         // [tile] Q
+  const uint32_t dol_smem = base + 2 * C::kQBytes;      // [tile] dO_l
+  const uint32_t dog_smem = base + 4 * C::kQBytes;      // [tile] dO_g
+  const uint32_t ring = base + 6 * C::kQBytes;
+  uint8_t *park_base = smem_raw + (base - raw) + 6 * C::kQBytes + C::kStages * C::kStageBytes;
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+
+  if (tid == 0) {
+    mbar_init(bar(kQFull), 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar(kFull + s), 1);
+      mbar_init(bar(kEmpty + s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(kSReady + t), 1);
+      mbar_init(bar(kDPReady + t), 1);
+      mbar_init(bar(kDSReady + t), 4);
+      mbar_init(bar(kDQDone + t), 1);
+    }
+    mbar_init(bar(kDrain), 1);
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(&tmem_holder), kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tdol);
+    prefetch_tmap(&tdog);
+    prefetch_tmap(&tkl);
+    prefetch_tmap(&tvl);
+    prefetch_tmap(&tsk);
+    prefetch_tmap(&tsv);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_holder;
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_expect_tx(bar(kQFull), 6 * C::kQBytes);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < C::kK; ++c) {
+          const int z = z0 + kTZ * t;
+          tma_load_5d(q_smem + t * C::kQBytes + c * C::kBoxQ, &tq, bar(kQFull), 16 * c, x0, y0, z, bh);
+          tma_load_5d(dol_smem + t * C::kQBytes + c * C::kBoxQ, &tdol, bar(kQFull), 16 * c, x0, y0, z, bh);
+          tma_load_5d(dog_smem + t * C::kQBytes + c * C::kBoxQ, &tdog, bar(kQFull), 16 * c, x0, y0, z, bh);
+        }
+      int issued = 0;
+      for (int ch = 0; ch < n_chunks; ++ch) {
+        const int s = ch % C::kStages;
+        // kEmpty[s] completes once per use of stage s: this is completion ch/kStages - 1.
+        // Completion - 1 was awaited here a ring turn ago (or this is the first), and
+        // completion + 1 needs chunk ch, which is not loaded yet.
+        if (ch >= C::kStages &&
+            !mbar_wait(bar(kEmpty + s), (ch / C::kStages - 1) & 1, &g_bwd_errors, kWaitNs, kErrProducer))
+          break;
+        const uint32_t stage = ring + s * C::kStageBytes;
+        const uint32_t full = bar(kFull + s);
+        if (ch < kLocalChunks) {
+          mbar_expect_tx(full, 4 * C::kKeyBytes);
+          for (int t = 0; t < 2; ++t) {
+            const int z = z0 + kTZ * t - kR + ch;
+            for (int c = 0; c < C::kK; ++c) {
+              tma_load_5d(stage + t * C::kKeyBytes + c * C::kBoxK, &tkl, full, 16 * c, x0 - kR, y0 - kR, z, bg);
+              tma_load_5d(stage + (2 + t) * C::kKeyBytes + c * C::kBoxK, &tvl, full, 16 * c, x0 - kR, y0 - kR, z,
+                          bg);
+            }
+          }
+        } else {
+          const int g = ch - kLocalChunks;
+          mbar_expect_tx(full, 2 * C::kKeyBytes);
+          for (int c = 0; c < C::kK; ++c) {
+            tma_load_3d(stage + c * C::kBoxK, &tsk, full, 16 * c, g * kSumRows, bg);
+            tma_load_3d(stage + C::kKeyBytes + c * C::kBoxK, &tsv, full, 16 * c, g * kSumRows, bg);
+          }
+        }
+        issued = ch + 1;
+      }
+      mbar_wait(bar(kQFull), 0, &g_bwd_errors, kWaitNs, kErrTeardown);
+      for (int ch = issued > C::kStages ? issued - C::kStages : 0; ch < issued; ++ch)
+        mbar_wait(bar(kFull + ch % C::kStages), (ch / C::kStages) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16(128, kKeys, BF16, false);  // S and dP: N = 96, K-major B
+      constexpr uint32_t idesc_dq = idesc_f16(128, D, BF16, true);     // dQ: N = D, B = K read MN-major
+      uint32_t commits[kNumBars];
+      for (int i = 0; i < kNumBars; ++i) commits[i] = 0u;
+      auto commit = [&](int bidx) {
+        mma_commit(bar(bidx));
+        ++commits[bidx];
+      };
+      auto stage_of = [&](int c) { return ring + (c % C::kStages) * C::kStageBytes; };
+      auto k_of = [&](int t, int c) { return c < kLocalChunks ? stage_of(c) + t * C::kKeyBytes : stage_of(c); };
+      auto v_of = [&](int t, int c) {
+        return c < kLocalChunks ? stage_of(c) + (2 + t) * C::kKeyBytes : stage_of(c) + C::kKeyBytes;
+      };
+      auto issue_s = [&](int t, int c) {
+        const uint32_t q_t = q_smem + t * C::kQBytes, k_base = k_of(t, c);
+        for (int kk = 0; kk < C::kK; ++kk)
+          mma_ss(tmem + t * 256 + kColS, desc_sw32(q_t + kk * C::kBoxQ, 16, 256),
+                 desc_sw32(k_base + kk * C::kBoxK, 16, 256), idesc_s, kk > 0 ? 1u : 0u);
+        commit(kSReady + t);
+      };
+      auto issue_dp = [&](int t, int c) {
+        const uint32_t do_t = (c < kLocalChunks ? dol_smem : dog_smem) + t * C::kQBytes, v_base = v_of(t, c);
+        for (int kk = 0; kk < C::kK; ++kk)
+          mma_ss(tmem + t * 256 + kColDP, desc_sw32(do_t + kk * C::kBoxQ, 16, 256),
+                 desc_sw32(v_base + kk * C::kBoxK, 16, 256), idesc_s, kk > 0 ? 1u : 0u);
+        commit(kDPReady + t);
+      };
+      auto issue_dq = [&](int t, int c) {
+        const uint32_t k_base = k_of(t, c);
+        const bool first = (c == 0) || (c == kLocalChunks);  // dQ restarts for the global branch
+        for (int j = 0; j < kKeys / 16; ++j)
+          mma_ts(tmem + t * 256 + kColDQ, tmem + t * 256 + kColDP + 8 * j, desc_sw32(k_base + j * 512, C::kBoxK, 256),
+                 idesc_dq, (first && j == 0) ? 0u : 1u);
+        commit(kDQDone + t);
+        if (t == 1) commit(kEmpty + c % C::kStages);  // every MMA reading chunk c's stage is issued
+      };
+      auto wait_bar = [&](int bidx, int completion) -> bool {
+        if (!mbar_wait(bar(bidx), completion & 1, &g_bwd_errors, kWaitNs, kErrMma)) return false;
+        tc_fence_after();
+        return true;
+      };
+      auto wait_full = [&](int c) { return wait_bar(kFull + c % C::kStages, c / C::kStages); };
+      // Prologue: S and dP of chunk 0 for both tiles.  Steady state per chunk c:
+      //   [dS_A(c)] dQ_A(c), S_A(c+1), [dS_B(c)] dQ_B(c), S_B(c+1),
+      //   [dQ_A(c) done] dP_A(c+1), [dQ_B(c) done] dP_B(c+1)
+      // S_t(c+1) overwrites S_t(c), which the softmax warps have read before storing dS_t(c);
+      // dP_t(c+1) overwrites dS_t(c), which dQ_t(c) reads (tcgen05.mma ops are ordered only
+      // when they share an accumulator), hence the wait for dQ_t(c).
+      bool ok = wait_bar(kQFull, 0) && wait_full(0);
+      if (ok) {
+        issue_s(0, 0);
+        issue_s(1, 0);
+        issue_dp(0, 0);
+        issue_dp(1, 0);
+      }
+      for (int c = 0; ok && c < n_chunks; ++c) {
+        const bool more = c + 1 < n_chunks;
+        ok = wait_bar(kDSReady + 0, c);
+        if (!ok) break;
+        issue_dq(0, c);
+        if (more) {
+          ok = wait_full(c + 1);
+          if (!ok) break;
+          issue_s(0, c + 1);
+        }
+        ok = wait_bar(kDSReady + 1, c);
+        if (!ok) break;
+        issue_dq(1, c);
+        if (!more) break;
+        issue_s(1, c + 1);
+        ok = wait_bar(kDQDone + 0, c);
+        if (!ok) break;
+        issue_dp(0, c + 1);
+        ok = wait_bar(kDQDone + 1, c);
+        if (!ok) break;
+        issue_dp(1, c + 1);
+      }
+      commit(kDrain);
+      for (int i = 0; i < kNumBars; ++i)
+        if (commits[i]) mbar_wait(bar(i), (commits[i] - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int t = warp >> 2, w = warp & 3;
+    const uint32_t lanes = (uint32_t)(w * 32) << 16;
+    const uint32_t t_tile = tmem + lanes + t * 256;
+    const int row = w * 32 + lane;
+    const int qz = w, qy = lane >> 3, qx = lane & 7;
+    const int zq = z0 + kTZ * t + qz, yq = y0 + qy, xq = x0 + qx;
+    const bool row_ok = zq < p.Z && yq < p.Y && xq < p.X;
+    int64_t grow = 0;
+    float lse2_l = __builtin_huge_valf(), lse2_g = __builtin_huge_valf(), delta_l = 0.f, delta_g = 0.f;
+    if (row_ok) {
+      int64_t rr = ((int64_t)zq * p.Y + yq) * p.X + xq;
+      if (p.map) rr = p.map[rr];
+      grow = (int64_t)bh * p.tokens + rr;
+      lse2_l = p.lse_l[grow] * kLog2e;  // +inf for a row with no valid neighbour: P = 0
+      lse2_g = p.lse_g[grow] * kLog2e;
+      delta_l = p.delta_l[grow];
+      delta_g = p.delta_g[grow];
+    }
+    uint32_t *park = reinterpret_cast<uint32_t *>(park_base + (size_t)(t * kRows + row) * D * 2);
+    uint32_t mask[3] = {0u, 0u, 0u};
+#pragma unroll
+    for (int hy = 0; hy < kHY; ++hy) {
+#pragma unroll
+      for (int hx = 0; hx < kHX; ++hx) {
+        const int c = hy * kHX + hx, yy = y0 - kR + hy, xx = x0 - kR + hx;
+        const bool in = (unsigned)(hy - qy) <= 2u * kR && (unsigned)(hx - qx) <= 2u * kR && yy >= 0 && yy < p.Y &&
+                        xx >= 0 && xx < p.X;
+        if (in) mask[c >> 5] |= 1u << (c & 31);
+      }
+    }
+    const float sc = p.sc, inv_sqrt_d = p.inv_sqrt_d;
+    auto wait_warp = [&](int bidx, int completion) -> bool {
+      const bool r = mbar_wait(bar(bidx), completion & 1, &g_bwd_errors, kWaitNs, kErrSoftmax);
+      const bool all = __all_sync(0xffffffffu, r);
+      if (all) tc_fence_after();
+      return all;
+    };
+    bool ok = true;
+    for (int ch = 0; ch < n_chunks; ++ch) {
+      if (ch == kLocalChunks) {
+        // Local branch done once dQ_t(7) has completed: round it to the storage dtype, park it.
+        ok = wait_warp(kDQDone + t, kLocalChunks - 1);
+        if (!ok) break;
+#pragma unroll
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t o[16];
+          tmem_ld16(t_tile + kColDQ + 16 * c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) park[8 * c + i] = pack2<BF16>(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
+        }
+      }
+      const bool local = ch < kLocalChunks;
+      const int zp = z0 + kTZ * t - kR + ch;
+      const bool active = !local || ((unsigned)(ch - qz) <= 2u * kR && zp >= 0 && zp < p.Z);  // warp-uniform
+      const float lse2 = local ? lse2_l : lse2_g, delta = local ? delta_l : delta_g;
+      ok = wait_warp(kSReady + t, ch);
+      if (!ok) break;
+      float pr[kKeys];
+      if (active) {
+#pragma unroll
+        for (int g = 0; g < kKeys / 32; ++g) tmem_ld32(t_tile + kColS + 32 * g, reinterpret_cast<uint32_t *>(pr + 32 * g));
+        tmem_wait_ld();
+        int valid = kKeys;
+        if (!local) valid = min(kKeys, p.summaries - (ch - kLocalChunks) * kSumRows);
+#pragma unroll
+        for (int i = 0; i < kKeys; ++i) {
+          const bool use = local ? ((mask[i >> 5] >> (i & 31)) & 1u) != 0u : i < valid;
+          pr[i] = use ? ex2_approx(fmaf(pr[i], sc, -lse2)) : 0.f;
+        }
+      }
+      ok = wait_warp(kDPReady + t, ch);
+      if (!ok) break;
+      if (active) {
+#pragma unroll
+        for (int g = 0; g < kKeys / 32; ++g) {
+          uint32_t dp[32];
+          tmem_ld32(t_tile + kColDP + 32 * g, dp);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float d0 = pr[32 * g + 2 * i] * (__uint_as_float(dp[2 * i]) - delta) * inv_sqrt_d;
+            const float d1 = pr[32 * g + 2 * i + 1] * (__uint_as_float(dp[2 * i + 1]) - delta) * inv_sqrt_d;
+            pk[i] = pack2<BF16>(d0, d1);
+          }
+          // dS group g goes to dP columns [16g, 16g + 16): already read (groups are read in order)
+          tmem_st16(t_tile + kColDP + 16 * g, pk);
+        }
+      } else {
+        uint32_t zero[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) zero[i] = 0u;
+#pragma unroll
+        for (int g = 0; g < kKeys / 32; ++g) tmem_st16(t_tile + kColDP + 16 * g, zero);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kDSReady + t));
+    }
+    // ---- epilogue: dq = round(round(dQ_l) + round(dQ_g)) through the row map
+    if (ok) ok = wait_warp(kDQDone + t, n_chunks - 1);
+    if (ok) {
+      uint32_t acc[D];
+#pragma unroll
+      for (int c = 0; c < D / 16; ++c) tmem_ld16(t_tile + kColDQ + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(acc + 16 * c));
+      tmem_wait_ld();
+      if (row_ok) {
+        uint32_t out[D / 2];
+#pragma unroll
+        for (int i = 0; i < D / 2; ++i) {
+          const float2 l = unpack2<BF16>(park[i]);
+          const float g0 = round_storage<BF16>(__uint_as_float(acc[2 * i]));
+          const float g1 = round_storage<BF16>(__uint_as_float(acc[2 * i + 1]));
+          out[i] = pack2<BF16>(l.x + g0, l.y + g1);
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.dq) + grow * D);
+#pragma unroll
+        for (int v = 0; v < D / 8; ++v) dst[v] = make_uint4(out[4 * v], out[4 * v + 1], out[4 * v + 2], out[4 * v + 3]);
+      }
+    }
+    tmem_wait_st();
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int D, bool BF16>
+int launch_dq_t(const StencilBwdArgs &a, cudaStream_t stream) {
+  using C = DqCfg<D>;
+  const int Z = a.grid[0], Y = a.grid[1], X = a.grid[2];
+  const uint64_t es = 2;
+  const uint64_t bh = (uint64_t)a.batch * a.heads, bgs = (uint64_t)a.batch * a.kv_heads;
+  CUtensorMap tq, tdol, tdog, tkl, tvl, tsk, tsv;
+  {
+    const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)Z, bh};
+    const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es, (uint64_t)Z * Y * X * D * es};
+    const uint32_t box[5] = {16, kTX, kTY, kTZ, 1};
+    if (int st = encode_operand(&tq, a.dtype, a.q, 5, dims, strides, box)) return st;
+    if (int st = encode_operand(&tdol, a.dtype, a.dol, 5, dims, strides, box)) return st;
+    if (int st = encode_operand(&tdog, a.dtype, a.dog, 5, dims, strides, box)) return st;
+  }
+  {
+    const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)Z, bgs};
+    const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es, (uint64_t)Z * Y * X * D * es};
+    const uint32_t box[5] = {16, kHX, kHY, 1, 1};
+    if (int st = encode_operand(&tkl, a.dtype, a.kl, 5, dims, strides, box)) return st;
+    if (int st = encode_operand(&tvl, a.dtype, a.vl, 5, dims, strides, box)) return st;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)D, (uint64_t)a.summaries, bgs};
+    const uint64_t strides[2] = {D * es, (uint64_t)a.summaries * D * es};
+    const uint32_t box[3] = {16, kSumRows, 1};
+    if (int st = encode_operand(&tsk, a.dtype, a.sk, 3, dims, strides, box)) return st;
+    if (int st = encode_operand(&tsv, a.dtype, a.sv, 3, dims, strides, box)) return st;
+  }
+  DqParams p{};
+  p.Z = Z;
+  p.Y = Y;
+  p.X = X;
+  p.tiles_z = (Z + 2 * kTZ - 1) / (2 * kTZ);
+  p.tiles_y = (Y + kTY - 1) / kTY;
+  p.tiles_x = (X + kTX - 1) / kTX;
+  p.heads = a.heads;
+  p.kv_heads = a.kv_heads;
+  p.summaries = a.summaries;
+  p.global_chunks = (a.summaries + kSumRows - 1) / kSumRows;
+  p.tokens = (int64_t)Z * Y * X;
+  p.sc = kLog2e / sqrtf((float)D);
+  p.inv_sqrt_d = 1.f / sqrtf((float)D);
+  p.lse_l = a.lse_l;
+  p.lse_g = a.lse_g;
+  p.delta_l = a.delta_l;
+  p.delta_g = a.delta_g;
+  p.map = a.raster_to_packed;
+  p.dq = a.dq;
+  const int64_t units = (int64_t)bh * p.tiles_z * p.tiles_y * p.tiles_x;
+  if (units <= 0) return P3D_OK;
+  if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");
+  auto kernel = stencil_bwd_dq_kernel<D, BF16>;
+  static bool configured = false;
+  if (!configured) {
+    P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+    configured = true;
+  }
+  kernel<<<(unsigned)units, kThreads, C::kSmemBytes, stream>>>(tq, tdol, tdog, tkl, tvl, tsk, tsv, p);
+  P3D_LAUNCH_CHECK();
+  return P3D_OK;
+}
+
+}  // namespace
+
+int launch_stencil_bwd_dq(const StencilBwdArgs &a, cudaStream_t s) {
+  const bool bf16 = a.dtype == P3D_BF16;
+  switch (a.head_dim) {
+    case 16: return bf16 ? launch_dq_t<16, true>(a, s) : launch_dq_t<16, false>(a, s);
+    case 32: return bf16 ? launch_dq_t<32, true>(a, s) : launch_dq_t<32, false>(a, s);
+    case 48: return bf16 ? launch_dq_t<48, true>(a, s) : launch_dq_t<48, false>(a, s);
+    case 64: return bf16 ? launch_dq_t<64, true>(a, s) : launch_dq_t<64, false>(a, s);
+    default: return fail(P3D_ERR_UNSUPPORTED, "stencil backward: head_dim %d", a.head_dim);
+  }
+}
+
+int take_bwd_errors(unsigned *flags) {
+  unsigned v = 0, zero = 0;
+  P3D_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_bwd_errors, sizeof(v)));
+  P3D_CUDA_TRY(cudaMemcpyToSymbol(g_bwd_errors, &zero, sizeof(zero)));
+  *flags |= v;
+  return P3D_OK;
+}
+
+}  // namespace p3d

@@ -34,11 +34,11 @@
 // read MN-major; P goes back into its S buffer in TMEM as bf16/f16 pairs and feeds
 // the PV MMA as the TMEM A operand.  Every mbarrier wait is bounded.
 #include <algorithm>
-#include <mutex>
 
 #include "common.cuh"
 #include "kernels.cuh"
 #include "sm100.cuh"
+#include "tma_host.cuh"
 
 namespace p3d {
 namespace {
@@ -566,36 +566,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------------- host side
 
-using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encode_fn() {
-  static EncodeTiled fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiled>(ptr);
-  });
-  return fn;
-}
-
-int encode(CUtensorMap *map, int dtype, const void *ptr, int rank, const uint64_t *dims, const uint64_t *strides,
-           const uint32_t *box) {
-  EncodeTiled fn = encode_fn();
-  if (!fn) return fail(P3D_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint32_t elem[5] = {1, 1, 1, 1, 1};
-  const CUresult r = fn(map, dtype == P3D_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        rank, const_cast<void *>(ptr), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(P3D_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return P3D_OK;
-}
-
 template <int D, bool BF16>
 int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
   using C = Cfg<D>;
@@ -607,21 +577,21 @@ int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
     const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)Z, bh};
     const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es, (uint64_t)Z * Y * X * D * es};
     const uint32_t box[5] = {16, kTX, kTY, kTZ, 1};
-    if (int st = encode(&tq, a.dtype, a.q, 5, dims, strides, box)) return st;
+    if (int st = encode_operand(&tq, a.dtype, a.q, 5, dims, strides, box)) return st;
   }
   {
     const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)Z, bgs};
     const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es, (uint64_t)Z * Y * X * D * es};
     const uint32_t box[5] = {16, kHX, kHY, 1, 1};
-    if (int st = encode(&tkl, a.dtype, a.kl, 5, dims, strides, box)) return st;
-    if (int st = encode(&tvl, a.dtype, a.vl, 5, dims, strides, box)) return st;
+    if (int st = encode_operand(&tkl, a.dtype, a.kl, 5, dims, strides, box)) return st;
+    if (int st = encode_operand(&tvl, a.dtype, a.vl, 5, dims, strides, box)) return st;
   }
   {
     const uint64_t dims[3] = {(uint64_t)D, (uint64_t)a.summaries, bgs};
     const uint64_t strides[2] = {D * es, (uint64_t)a.summaries * D * es};
     const uint32_t box[3] = {16, kSumRows, 1};
-    if (int st = encode(&tsk, a.dtype, a.sk, 3, dims, strides, box)) return st;
-    if (int st = encode(&tsv, a.dtype, a.sv, 3, dims, strides, box)) return st;
+    if (int st = encode_operand(&tsk, a.dtype, a.sk, 3, dims, strides, box)) return st;
+    if (int st = encode_operand(&tsv, a.dtype, a.sv, 3, dims, strides, box)) return st;
   }
   FwdParams p{};
   p.Z = Z;

@@ -107,13 +107,18 @@ def forward(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature
     return y, ((sk, sv, ol, og, lse_l, lse_g) if save_state else ())
 
 
-def backward(dy, inputs, saved, geometry, temperature):
-    """Launch the backward; returns the ten input gradients in the inputs' dtypes."""
+def backward(dy, inputs, saved, geometry, temperature, *, force_indexed=False):
+    """Launch the backward; returns the ten input gradients in the inputs' dtypes.
+
+    ``force_indexed`` runs the neighbour-table kernels even on a complete stencil.
+    """
     q, kl, vl, kg, vg, weight, bias, gate, sl, sg = inputs
     sk, sv, ol, og, lse_l, lse_g = saved
     gate_k = _as_gate(gate, q).contiguous()
     w32, b32, sl32, sg32 = (_f32(t) for t in (weight, bias, sl, sg))
     op, keep = _operator(q, kl, vl, kg, vg, w32, b32, gate_k, sl32, sg32, geometry, temperature)
+    if force_indexed:
+        op.stencil = 0
     dq, dkl, dvl, dkg, dvg = (torch.empty_like(t) for t in (q, kl, vl, kg, vg))
     dgate = torch.empty_like(gate_k)
     d = q.shape[-1]

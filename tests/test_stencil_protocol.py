@@ -26,3 +26,9 @@ def test_model_rejects_the_ambiguous_release_scheme():
             assert "passed at 0" in str(err)
             failures += 1
     assert failures > 0
+
+
+@pytest.mark.parametrize("stages", [2, 3, 4])
+def test_dq_protocol_holds_under_random_interleavings(stages):
+    for seed in range(150):
+        sp.run_dq(n_chunks=12, stages=stages, seed=seed)
