@@ -120,7 +120,12 @@ typedef struct {
   int32_t grid[3];
   int32_t radius[3];
   const int32_t *raster_to_packed; /* [N] or NULL for raster storage */
+  uint32_t options;                 /* P3D_OPT_* bits (0: pick the fastest kernels) */
 } p3d_operator;
+
+/* p3d_operator.options: run only the neighbour-table (indexed) kernels, as the reference's
+ * Triton backend is structured -- for comparison and testing. */
+#define P3D_OPT_INDEXED_ONLY 1u
 
 /*
  * Forward (kernels.py:289-311).  Writes y [B,H,N,D] and the summaries sk, sv

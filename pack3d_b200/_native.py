@@ -18,6 +18,7 @@ DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 FWD_SAVE_STATE = 1
 FWD_FORCE_INDEXED = 2
 FWD_SUMMARIES_GIVEN = 4
+OPT_INDEXED_ONLY = 1
 
 _c_int, _c_i64, _c_f32, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -37,7 +38,7 @@ class Operator(ctypes.Structure):
         ("blocks", _vp), ("fine_blocks", ctypes.c_int32), ("slots", ctypes.c_int32),
         ("pool_size", ctypes.c_int32),
         ("stencil", ctypes.c_int32), ("grid", ctypes.c_int32 * 3), ("radius", ctypes.c_int32 * 3),
-        ("raster_to_packed", _vp),
+        ("raster_to_packed", _vp), ("options", ctypes.c_uint32),
     ]
 
 

@@ -70,6 +70,7 @@ int summaries_of(const p3d_operator *op) { return (op->fine_blocks + op->pool_si
 int validate(const p3d_operator *op) {
   P3D_CHECK_ARG(op != nullptr, "null operator descriptor");
   P3D_CHECK_ARG(dtype_ok(op->dtype) && dtype_ok(op->gate_dtype), "unknown dtype");
+  P3D_CHECK_ARG((op->options & ~P3D_OPT_INDEXED_ONLY) == 0u, "unknown option bits 0x%x", op->options);
   P3D_CHECK_ARG(op->batch >= 1 && op->heads >= 1 && op->tokens >= 1 && op->kv_heads >= 1,
                 "batch, heads, kv_heads and tokens must be positive");
   P3D_CHECK_ARG(op->heads % op->kv_heads == 0, "query heads must be divisible by KV heads");
@@ -145,7 +146,7 @@ PoolArgs pool_args(const p3d_operator *op, void *sk, void *sv) {
 
 bool use_stencil_path(const p3d_operator *op, unsigned flags) {
   if (flags & P3D_FWD_FORCE_INDEXED) return false;
-  if (!op->stencil) return false;
+  if (!op->stencil || (op->options & P3D_OPT_INDEXED_ONLY)) return false;
   return stencil_fwd_supported(op->dtype, op->head_dim, op->radius, summaries_of(op));
 }
 
@@ -199,8 +200,13 @@ int gather_rows(const void *src, void *dst, const int32_t *map, int64_t slabs, i
 // summaries (with one the global softmax is constant: no score gradient, reference
 // kernels.py:198-199).
 bool use_stencil_bwd(const p3d_operator *op) {
-  return op->stencil && summaries_of(op) >= 2 &&
+  return op->stencil && !(op->options & P3D_OPT_INDEXED_ONLY) && summaries_of(op) >= 2 &&
          stencil_fwd_supported(op->dtype, op->head_dim, op->radius, summaries_of(op));
+}
+
+// Global dSK / dSV on tensor cores: any token order, 16-bit dtypes, at least two summaries.
+bool use_tc_global_dkv(const p3d_operator *op) {
+  return !(op->options & P3D_OPT_INDEXED_ONLY) && global_dkv_tc_supported(op->dtype, op->head_dim, summaries_of(op));
 }
 
 struct BwdBuffers {
@@ -208,7 +214,7 @@ struct BwdBuffers {
   void *q_r, *kl_r, *vl_r, *dol_r, *dog_r;  // raster-order copies (tensor-core path, permuted storage)
   float *delta_l, *delta_g, *dsl_part, *dsg_part, *dk_part, *dv_part, *dsk, *dsv, *dw_part, *db_part, *tmp;
   int64_t mix_rows, pool_rows;
-  int splits;
+  int splits, per_split;  // global dSK / dSV partials (per_split: tensor-core kernel only)
 };
 
 size_t bwd_layout(const p3d_operator *op, void *base, size_t cap, BwdBuffers *b) {
@@ -221,7 +227,15 @@ size_t bwd_layout(const p3d_operator *op, void *base, size_t cap, BwdBuffers *b)
   const int chunk = mix_bwd_chunk_rows();
   b->mix_rows = bh * ((op->tokens + chunk - 1) / chunk);
   b->pool_rows = bg * M;
-  b->splits = global_dkv_splits(op->tokens);
+  b->per_split = 0;
+  if (use_tc_global_dkv(op)) {
+    DeviceInfo info{};
+    if (device_info(&info) != P3D_OK) info.sm_count = 148;
+    global_dkv_tc_splits(op->batch, op->heads, op->kv_heads, op->tokens, M, info.sm_count, &b->splits,
+                         &b->per_split);
+  } else {
+    b->splits = global_dkv_splits(op->tokens);
+  }
   const int64_t d = op->head_dim;
   b->dol = c.take<char>(rows * d * es);
   b->dog = c.take<char>(rows * d * es);
@@ -474,7 +488,29 @@ int p3d_attn_bwd(const p3d_operator *op, const void *dy, const void *sk, const v
     if (int st = launch_local_dkv_indexed(a, b.dol, lse_l, b.delta_l, dkl, dvl, s)) return st;
     if (int st = launch_global_dq(a, b.dog, lse_g, b.delta_g, dq, s)) return st;
   }
-  if (int st = launch_global_dkv(a, b.dog, lse_g, b.delta_g, b.splits, b.dk_part, b.dv_part, s)) return st;
+  if (use_tc_global_dkv(op)) {
+    GlobalDkvArgs g{};
+    g.dtype = op->dtype;
+    g.batch = op->batch;
+    g.heads = op->heads;
+    g.kv_heads = op->kv_heads;
+    g.tokens = op->tokens;
+    g.head_dim = d;
+    g.summaries = M;
+    g.splits = b.splits;
+    g.per_split = b.per_split;
+    g.q = op->q;
+    g.dog = b.dog;
+    g.sk = sk;
+    g.sv = sv;
+    g.lse_g = lse_g;
+    g.delta_g = b.delta_g;
+    g.dk_part = b.dk_part;
+    g.dv_part = b.dv_part;
+    if (int st = launch_global_dkv_tc(g, s)) return st;
+  } else {
+    if (int st = launch_global_dkv(a, b.dog, lse_g, b.delta_g, b.splits, b.dk_part, b.dv_part, s)) return st;
+  }
   if (int st = launch_sum_middle(b.dk_part, b.dsk, bg, b.splits, (int64_t)M * d, s)) return st;
   if (int st = launch_sum_middle(b.dv_part, b.dsv, bg, b.splits, (int64_t)M * d, s)) return st;
 

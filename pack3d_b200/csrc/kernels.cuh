@@ -117,6 +117,21 @@ struct StencilBwdArgs {
   void *dq;                             // [B,H,N,D] in the layout's row order
 };
 int launch_stencil_bwd_dq(const StencilBwdArgs &a, cudaStream_t s);
+
+// Tensor-core global dSK / dSV split partials (any token order).
+struct GlobalDkvArgs {
+  int dtype;
+  int batch, heads, kv_heads, tokens, head_dim, summaries;
+  int splits, per_split;          // from global_dkv_tc_splits
+  const void *q, *dog;            // [B,H,N,D]
+  const void *sk, *sv;            // [B,G,M,D]
+  const float *lse_g, *delta_g;   // [B*H, N]
+  float *dk_part, *dv_part;       // [B*G, splits, M, D]
+};
+bool global_dkv_tc_supported(int dtype, int head_dim, int summaries);
+void global_dkv_tc_splits(int batch, int heads, int kv_heads, int tokens, int summaries, int sm_count, int *splits,
+                          int *per_split);
+int launch_global_dkv_tc(const GlobalDkvArgs &a, cudaStream_t s);
 int take_bwd_errors(unsigned *flags);
 
 }  // namespace p3d

@@ -506,6 +506,354 @@ int launch_dq_t(const StencilBwdArgs &a, cudaStream_t stream) {
   return P3D_OK;
 }
 
+
+// ============================================================================ global dSK / dSV
+//
+// Restates the summary-gradient half of the global branch (kernels.py:210-239): for a
+// tile of 128 summaries (TMEM lanes) and a stream of 128-query chunks (columns),
+//   S^T = SK Q^T, dP^T = SV dO_g^T, P^T = exp(S^T / sqrt(D) - lse), dS^T = P^T (dP^T - Delta) / sqrt(D)
+//   dSV += P^T dO_g,  dSK += dS^T Q          (P^T and dS^T rounded to the storage dtype)
+// over the query chunks of one split; splits write fp32 partials [B*G, splits, M, D] that a
+// fixed-order reduction sums.  The global branch ignores the geometry, so this kernel serves
+// any token order.  Summary rows past M read zeros and are not written; query columns past
+// N get lse = +inf (P = 0).
+//
+// TMEM: S^T [0, 128), dP^T [128, 256), P^T [256, 320), dS^T [320, 384) (16-bit pairs),
+// dSK [384, 384 + D), dSV [384 + D, 384 + 2D).  Eight softmax warps: warp w serves TMEM
+// lanes 32(w%4).. and query columns 64(w/4)..+64.  Per chunk the MMA thread issues S^T and
+// dP^T; the softmax warps pull them into registers and release the buffers (the next
+// chunk's S^T / dP^T start at once), then store P^T / dS^T once the previous chunk's dSV /
+// dSK products are done with them, and the MMA thread accumulates dSV and dSK.
+constexpr int kGRows = 128;   // summaries per tile
+constexpr int kGCols = 128;   // queries per chunk
+constexpr uint32_t kGColS = 0, kGColDP = 128, kGColP = 256, kGColDS = 320, kGColAcc = 384;
+
+template <int D>
+struct GkvCfg {
+  static constexpr int kK = D / 16;
+  static constexpr int kBox = 128 * 32;                 // 128 rows x 16 channels
+  static constexpr int kTileBytes = kK * kBox;          // one 128-row operand tile
+  static constexpr int kRowVals = kGCols * 4;           // one chunk of lse (or Delta), fp32
+  static constexpr int kStageBytes = (2 * kTileBytes + 2 * kRowVals + 1023) / 1024 * 1024;
+  static constexpr int kFixed = 2 * kTileBytes + 1024;
+  static constexpr int kRoom = (227 * 1024 - 2048 - kFixed) / kStageBytes;
+  static constexpr int kStages = kRoom > 4 ? 4 : kRoom;
+  static constexpr int kSmemNeed = kFixed + kStages * kStageBytes;
+  static constexpr int kSmemBytes = kSmemNeed > 116 * 1024 ? kSmemNeed : 116 * 1024;
+  static_assert(kStages >= 2, "the ring must hold two chunks");
+  static_assert(kGColAcc + 2 * D <= 512, "TMEM budget");
+};
+
+enum GkvBar {
+  kGKvFull = 0,
+  kGFull = 1,                  // [stage]: Q, dO_g copies (tx) + lse / Delta stores (one arrive)
+  kGEmpty = kGFull + 4,        // [stage]: released by the commit after dSV / dSK of its chunk
+  kGSReady = kGEmpty + 4,      // S^T(c) and dP^T(c) complete
+  kGSFree = kGSReady + 1,      // the 8 softmax warps have read S^T(c), dP^T(c) (count 8)
+  kGPdsReady = kGSFree + 1,    // the 8 softmax warps stored P^T(c), dS^T(c) (count 8)
+  kGPdsFree = kGPdsReady + 1,  // dSV(c), dSK(c) complete
+  kGDrain = kGPdsFree + 1,
+  kGNumBars = kGDrain + 1
+};
+
+struct GkvParams {
+  int heads, kv_heads, rep, tokens, summaries, m_tiles, splits, q_chunks, per_split;
+  float sc, inv_sqrt_d;
+  const float *lse_g, *delta_g;  // [B*H, N]
+  float *dk_part, *dv_part;      // [B*G, splits, M, D]
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    global_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                         const __grid_constant__ CUtensorMap tsk, const __grid_constant__ CUtensorMap tsv,
+                         const GkvParams p) {
+  using C = GkvCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[kGNumBars];
+  __shared__ uint32_t tmem_holder;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int split = blockIdx.x % p.splits;
+  const int mt = (blockIdx.x / p.splits) % p.m_tiles;
+  const int bg = blockIdx.x / (p.splits * p.m_tiles);
+  const int b = bg / p.kv_heads, g = bg % p.kv_heads;
+  const int m0 = mt * kGRows;
+  const int total = p.rep * p.q_chunks;
+  const int c_begin = split * p.per_split;
+  const int n_chunks = min(total, c_begin + p.per_split) - c_begin;  // >= 1 (host)
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t sk_smem = base, sv_smem = base + C::kTileBytes;
+  const uint32_t ring = base + 2 * C::kTileBytes;
+  uint8_t *ring_ptr = smem_raw + (base - raw) + 2 * C::kTileBytes;
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+
+  if (tid == 0) {
+    mbar_init(bar(kGKvFull), 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar(kGFull + s), 2);
+      mbar_init(bar(kGEmpty + s), 1);
+    }
+    mbar_init(bar(kGSReady), 1);
+    mbar_init(bar(kGSFree), 8);
+    mbar_init(bar(kGPdsReady), 8);
+    mbar_init(bar(kGPdsFree), 1);
+    mbar_init(bar(kGDrain), 1);
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(&tmem_holder), kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tdo);
+    prefetch_tmap(&tsk);
+    prefetch_tmap(&tsv);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_holder;
+  auto chunk_head = [&](int c) { return b * p.heads + g * p.rep + (c_begin + c) / p.q_chunks; };
+  auto chunk_row0 = [&](int c) { return ((c_begin + c) % p.q_chunks) * kGCols; };
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------------ producer (whole warp)
+    if (lane == 0) {
+      mbar_expect_tx(bar(kGKvFull), 2 * C::kTileBytes);
+      for (int c = 0; c < C::kK; ++c) {
+        tma_load_3d(sk_smem + c * C::kBox, &tsk, bar(kGKvFull), 16 * c, m0, bg);
+        tma_load_3d(sv_smem + c * C::kBox, &tsv, bar(kGKvFull), 16 * c, m0, bg);
+      }
+    }
+    int issued = 0;
+    for (int ch = 0; ch < n_chunks; ++ch) {
+      const int s = ch % C::kStages;
+      // kGEmpty[s]: completion ch/kStages - 1 (the same unambiguity argument as the dQ kernel)
+      bool ok = true;
+      if (lane == 0 && ch >= C::kStages)
+        ok = mbar_wait(bar(kGEmpty + s), (ch / C::kStages - 1) & 1, &g_bwd_errors, kWaitNs, kErrProducer);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      const uint32_t stage = ring + s * C::kStageBytes;
+      const uint32_t full = bar(kGFull + s);
+      const int bh = chunk_head(ch), n0 = chunk_row0(ch);
+      if (lane == 0) {
+        mbar_expect_tx(full, 2 * C::kTileBytes);
+        for (int c = 0; c < C::kK; ++c) {
+          tma_load_3d(stage + c * C::kBox, &tq, full, 16 * c, n0, bh);
+          tma_load_3d(stage + C::kTileBytes + c * C::kBox, &tdo, full, 16 * c, n0, bh);
+        }
+      }
+      // lse (as log2) and Delta of the chunk's queries; +inf past the last row (P = 0)
+      float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kTileBytes);
+      for (int j = lane; j < kGCols; j += 32) {
+        const int n = n0 + j;
+        const bool in = n < p.tokens;
+        const int64_t r = (int64_t)bh * p.tokens + n;
+        vals[j] = in ? p.lse_g[r] * kLog2e : __builtin_huge_valf();
+        vals[kGCols + j] = in ? p.delta_g[r] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(full);
+      issued = ch + 1;
+    }
+    if (lane == 0) {
+      mbar_wait(bar(kGKvFull), 0, &g_bwd_errors, kWaitNs, kErrTeardown);
+      for (int ch = issued > C::kStages ? issued - C::kStages : 0; ch < issued; ++ch)
+        mbar_wait(bar(kGFull + ch % C::kStages), (ch / C::kStages) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16(128, kGCols, BF16, false);
+      constexpr uint32_t idesc_acc = idesc_f16(128, D, BF16, true);
+      uint32_t commits[kGNumBars];
+      for (int i = 0; i < kGNumBars; ++i) commits[i] = 0u;
+      auto commit = [&](int bidx) {
+        mma_commit(bar(bidx));
+        ++commits[bidx];
+      };
+      auto stage_of = [&](int c) { return ring + (c % C::kStages) * C::kStageBytes; };
+      auto issue_s_dp = [&](int c) {
+        const uint32_t q = stage_of(c), dov = stage_of(c) + C::kTileBytes;
+        for (int kk = 0; kk < C::kK; ++kk)
+          mma_ss(tmem + kGColS, desc_sw32(sk_smem + kk * C::kBox, 16, 256), desc_sw32(q + kk * C::kBox, 16, 256),
+                 idesc_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < C::kK; ++kk)
+          mma_ss(tmem + kGColDP, desc_sw32(sv_smem + kk * C::kBox, 16, 256), desc_sw32(dov + kk * C::kBox, 16, 256),
+                 idesc_s, kk > 0 ? 1u : 0u);
+        commit(kGSReady);
+      };
+      auto issue_acc = [&](int c) {
+        const uint32_t q = stage_of(c), dov = stage_of(c) + C::kTileBytes;
+        for (int j = 0; j < kGCols / 16; ++j)
+          mma_ts(tmem + kGColAcc + D, tmem + kGColP + 8 * j, desc_sw32(dov + j * 512, C::kBox, 256), idesc_acc,
+                 (c == 0 && j == 0) ? 0u : 1u);
+        for (int j = 0; j < kGCols / 16; ++j)
+          mma_ts(tmem + kGColAcc, tmem + kGColDS + 8 * j, desc_sw32(q + j * 512, C::kBox, 256), idesc_acc,
+                 (c == 0 && j == 0) ? 0u : 1u);
+        commit(kGPdsFree);
+        commit(kGEmpty + c % C::kStages);  // every reader of chunk c's stage is issued
+      };
+      auto wait_bar = [&](int bidx, int completion) -> bool {
+        if (!mbar_wait(bar(bidx), completion & 1, &g_bwd_errors, kWaitNs, kErrMma)) return false;
+        tc_fence_after();
+        return true;
+      };
+      auto wait_full = [&](int c) { return wait_bar(kGFull + c % C::kStages, c / C::kStages); };
+      bool ok = wait_bar(kGKvFull, 0) && wait_full(0);
+      if (ok) issue_s_dp(0);
+      for (int c = 0; ok && c < n_chunks; ++c) {
+        ok = wait_bar(kGSFree, c);
+        if (!ok) break;
+        if (c + 1 < n_chunks) {
+          ok = wait_full(c + 1);
+          if (!ok) break;
+          issue_s_dp(c + 1);
+        }
+        ok = wait_bar(kGPdsReady, c);
+        if (!ok) break;
+        issue_acc(c);
+      }
+      commit(kGDrain);
+      for (int i = 0; i < kGNumBars; ++i)
+        if (commits[i]) mbar_wait(bar(i), (commits[i] - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax (8 warps) + epilogue
+    const int quarter = warp & 3, half = warp >> 2;
+    const uint32_t t_lanes = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int row = quarter * 32 + lane;  // summary m0 + row
+    const float sc = p.sc, inv_sqrt_d = p.inv_sqrt_d;
+    auto wait_warp = [&](int bidx, int completion) -> bool {
+      const bool r = mbar_wait(bar(bidx), completion & 1, &g_bwd_errors, kWaitNs, kErrSoftmax);
+      const bool all = __all_sync(0xffffffffu, r);
+      if (all) tc_fence_after();
+      return all;
+    };
+    bool ok = true;
+    for (int ch = 0; ch < n_chunks; ++ch) {
+      ok = wait_warp(kGSReady, ch);
+      if (!ok) break;
+      const float *vals = reinterpret_cast<const float *>(ring_ptr + (size_t)(ch % C::kStages) * C::kStageBytes +
+                                                          2 * C::kTileBytes);
+      uint32_t pw[2][16], dw[2][16];
+#pragma unroll
+      for (int gi = 0; gi < 2; ++gi) {
+        const int col0 = 64 * half + 32 * gi;
+        uint32_t sv[32], dv[32];
+        tmem_ld32(t_lanes + kGColS + col0, sv);
+        tmem_ld32(t_lanes + kGColDP + col0, dv);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int j = col0 + 2 * i;
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * i]), sc, -vals[j]));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * i + 1]), sc, -vals[j + 1]));
+          const float d0 = p0 * (__uint_as_float(dv[2 * i]) - vals[kGCols + j]) * inv_sqrt_d;
+          const float d1 = p1 * (__uint_as_float(dv[2 * i + 1]) - vals[kGCols + j + 1]) * inv_sqrt_d;
+          pw[gi][i] = pack2<BF16>(p0, p1);
+          dw[gi][i] = pack2<BF16>(d0, d1);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kGSFree));
+      if (ch > 0) {
+        ok = wait_warp(kGPdsFree, ch - 1);  // dSV / dSK of the previous chunk no longer read P^T / dS^T
+        if (!ok) break;
+      }
+#pragma unroll
+      for (int gi = 0; gi < 2; ++gi) {
+        tmem_st16(t_lanes + kGColP + 32 * half + 16 * gi, pw[gi]);
+        tmem_st16(t_lanes + kGColDS + 32 * half + 16 * gi, dw[gi]);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kGPdsReady));
+    }
+    if (ok) ok = wait_warp(kGPdsFree, n_chunks - 1);
+    if (ok) {
+      // warps 0-3 write dSK rows, warps 4-7 dSV rows
+      uint32_t acc[D];
+      const uint32_t col = kGColAcc + (half ? D : 0);
+#pragma unroll
+      for (int c = 0; c < D / 16; ++c) tmem_ld16(t_lanes + col + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(acc + 16 * c));
+      tmem_wait_ld();
+      const int m = m0 + row;
+      if (m < p.summaries) {
+        float *dst = (half ? p.dv_part : p.dk_part) + (((int64_t)bg * p.splits + split) * p.summaries + m) * D;
+#pragma unroll
+        for (int v = 0; v < D / 4; ++v)
+          reinterpret_cast<float4 *>(dst)[v] = make_float4(__uint_as_float(acc[4 * v]), __uint_as_float(acc[4 * v + 1]),
+                                                           __uint_as_float(acc[4 * v + 2]), __uint_as_float(acc[4 * v + 3]));
+      }
+    }
+    tmem_wait_st();
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int D, bool BF16>
+int launch_gkv_t(const GlobalDkvArgs &a, cudaStream_t stream) {
+  using C = GkvCfg<D>;
+  const uint64_t es = 2;
+  const uint64_t bh = (uint64_t)a.batch * a.heads, bgs = (uint64_t)a.batch * a.kv_heads;
+  CUtensorMap tq, tdo, tsk, tsv;
+  {
+    const uint64_t dims[3] = {(uint64_t)D, (uint64_t)a.tokens, bh};
+    const uint64_t strides[2] = {D * es, (uint64_t)a.tokens * D * es};
+    const uint32_t box[3] = {16, kGCols, 1};
+    if (int st = encode_operand(&tq, a.dtype, a.q, 3, dims, strides, box)) return st;
+    if (int st = encode_operand(&tdo, a.dtype, a.dog, 3, dims, strides, box)) return st;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)D, (uint64_t)a.summaries, bgs};
+    const uint64_t strides[2] = {D * es, (uint64_t)a.summaries * D * es};
+    const uint32_t box[3] = {16, kGRows, 1};
+    if (int st = encode_operand(&tsk, a.dtype, a.sk, 3, dims, strides, box)) return st;
+    if (int st = encode_operand(&tsv, a.dtype, a.sv, 3, dims, strides, box)) return st;
+  }
+  GkvParams p{};
+  p.heads = a.heads;
+  p.kv_heads = a.kv_heads;
+  p.rep = a.heads / a.kv_heads;
+  p.tokens = a.tokens;
+  p.summaries = a.summaries;
+  p.m_tiles = (a.summaries + kGRows - 1) / kGRows;
+  p.q_chunks = (a.tokens + kGCols - 1) / kGCols;
+  p.splits = a.splits;
+  p.per_split = a.per_split;
+  p.sc = kLog2e / sqrtf((float)D);
+  p.inv_sqrt_d = 1.f / sqrtf((float)D);
+  p.lse_g = a.lse_g;
+  p.delta_g = a.delta_g;
+  p.dk_part = a.dk_part;
+  p.dv_part = a.dv_part;
+  const int64_t units = (int64_t)bgs * p.m_tiles * p.splits;
+  if (units <= 0) return P3D_OK;
+  if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");
+  auto kernel = global_dkv_tc_kernel<D, BF16>;
+  static bool configured = false;
+  if (!configured) {
+    P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+    configured = true;
+  }
+  kernel<<<(unsigned)units, kThreads, C::kSmemBytes, stream>>>(tq, tdo, tsk, tsv, p);
+  P3D_LAUNCH_CHECK();
+  return P3D_OK;
+}
+
 }  // namespace
 
 int launch_stencil_bwd_dq(const StencilBwdArgs &a, cudaStream_t s) {
@@ -516,6 +864,54 @@ int launch_stencil_bwd_dq(const StencilBwdArgs &a, cudaStream_t s) {
     case 48: return bf16 ? launch_dq_t<48, true>(a, s) : launch_dq_t<48, false>(a, s);
     case 64: return bf16 ? launch_dq_t<64, true>(a, s) : launch_dq_t<64, false>(a, s);
     default: return fail(P3D_ERR_UNSUPPORTED, "stencil backward: head_dim %d", a.head_dim);
+  }
+}
+
+// Query-chunk splits of the global dSK / dSV kernel: a CTA count that fills whole waves
+// (at least four when the work allows), every split non-empty.
+void global_dkv_tc_splits(int batch, int heads, int kv_heads, int tokens, int summaries, int sm_count, int *splits,
+                          int *per_split) {
+  const int64_t base = (int64_t)batch * kv_heads * ((summaries + kGRows - 1) / kGRows);
+  const int64_t total = (int64_t)(heads / kv_heads) * ((tokens + kGCols - 1) / kGCols);
+  const int sms = sm_count > 0 ? sm_count : 148;
+  int best_s = 1;
+  double best_eff = -1.0;
+  for (int s = 1; s <= 64 && s <= total; ++s) {
+    const int64_t per = (total + s - 1) / s;
+    if (s > 1 && per < 8) break;
+    const int64_t s_eff = (total + per - 1) / per;
+    const int64_t ctas = base * s_eff;
+    const int64_t waves = (ctas + sms - 1) / sms;
+    const double eff = (double)ctas / (double)(waves * sms);
+    if (ctas >= 4 * sms && eff >= 0.9) {
+      best_s = (int)s_eff;
+      break;
+    }
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best_s = (int)s_eff;
+    }
+  }
+  *per_split = (int)((total + best_s - 1) / best_s);
+  *splits = (int)((total + *per_split - 1) / *per_split);
+}
+
+bool global_dkv_tc_supported(int dtype, int head_dim, int summaries) {
+  if (dtype != P3D_BF16 && dtype != P3D_F16) return false;
+  if (head_dim != 16 && head_dim != 32 && head_dim != 48 && head_dim != 64) return false;
+  if (summaries < 2) return false;
+  DeviceInfo info;
+  return device_info(&info) == P3D_OK && info.major == 10;
+}
+
+int launch_global_dkv_tc(const GlobalDkvArgs &a, cudaStream_t s) {
+  const bool bf16 = a.dtype == P3D_BF16;
+  switch (a.head_dim) {
+    case 16: return bf16 ? launch_gkv_t<16, true>(a, s) : launch_gkv_t<16, false>(a, s);
+    case 32: return bf16 ? launch_gkv_t<32, true>(a, s) : launch_gkv_t<32, false>(a, s);
+    case 48: return bf16 ? launch_gkv_t<48, true>(a, s) : launch_gkv_t<48, false>(a, s);
+    case 64: return bf16 ? launch_gkv_t<64, true>(a, s) : launch_gkv_t<64, false>(a, s);
+    default: return fail(P3D_ERR_UNSUPPORTED, "global dSK/dSV: head_dim %d", a.head_dim);
   }
 }
 

@@ -118,7 +118,7 @@ def backward(dy, inputs, saved, geometry, temperature, *, force_indexed=False):
     w32, b32, sl32, sg32 = (_f32(t) for t in (weight, bias, sl, sg))
     op, keep = _operator(q, kl, vl, kg, vg, w32, b32, gate_k, sl32, sg32, geometry, temperature)
     if force_indexed:
-        op.stencil = 0
+        op.options |= _native.OPT_INDEXED_ONLY
     dq, dkl, dvl, dkg, dvg = (torch.empty_like(t) for t in (q, kl, vl, kg, vg))
     dgate = torch.empty_like(gate_k)
     d = q.shape[-1]

@@ -411,3 +411,124 @@ def run_dq(n_chunks=12, stages=3, seed=0, max_steps=400000):
         for w in range(4):
             roles[f"softmax{t}{w}"] = dq_softmax(state, t, w)
     return _schedule(state, roles, rng, max_steps)
+
+
+# ------------------------------------------------------------------ global dSK / dSV kernel
+# Model of global_dkv_tc_kernel: one S^T / dP^T buffer pair (released by the eight softmax
+# warps once they have read it), one P^T / dS^T buffer (rewritten once the previous
+# chunk's dSV / dSK products completed), a ring of query chunks filled by TMA copies plus
+# the producer warp's own lse / Delta stores.
+
+def gkv_producer(state):
+    k = state.stages
+    for ch in range(state.n_chunks):
+        s = ch % k
+        if ch >= k:
+            while not _wait(state, f"empty{s}", (ch // k - 1) & 1, ch // k - 1):
+                yield ("wait", f"empty{s}")
+        old = state.stage_chunk.get(s)
+        if old is not None:
+            for op in (("SDP", 0, old), ("ACC", 0, old)):
+                if op not in state.mma_done:
+                    raise ProtocolError(f"stage {s} overwritten with chunk {ch} while {op} is outstanding")
+            if len(state.read_vals.get(old, ())) != 8:
+                raise ProtocolError(f"stage {s} overwritten while softmax warps may read chunk {old}'s lse")
+        state.bar(f"full{s}").arrive(tx=1)  # expect_tx + copies
+        state.stage_chunk[s] = ch
+        state.tma_inflight.append((s, ch))
+        yield ("step", None)
+        state.bar(f"full{s}").arrive()      # lse / Delta stores of the warp
+        yield ("step", None)
+
+
+def gkv_mma(state):
+    k, n = state.stages, state.n_chunks
+
+    def commit(name):
+        state.mma_queue.append(("commit", name))
+
+    def landed(c):
+        if state.stage_landed.get(c % k) != c:
+            raise ProtocolError(f"chunk {c} read before its copy landed")
+
+    def issue_sdp(c):
+        landed(c)
+        if c >= 1 and len(state.sdp_read.get(c - 1, ())) != 8:
+            raise ProtocolError(f"S/dP({c}) overwrite buffers still being read")
+        state.mma_queue.append(("SDP", 0, c))
+        commit("sready")
+
+    def issue_acc(c):
+        landed(c)
+        if len(state.pds_stored.get(c, ())) != 8:
+            raise ProtocolError(f"dSV/dSK({c}) issued before all warps stored P/dS")
+        state.mma_queue.append(("ACC", 0, c))
+        commit("pdsfree")
+        commit(f"empty{c % k}")
+
+    def waits(name, completion):
+        while not _wait(state, name, completion & 1, completion):
+            yield ("wait", name)
+
+    yield from waits("kvfull", 0)
+    yield from waits("full0", 0)
+    issue_sdp(0)
+    yield ("step", None)
+    for c in range(n):
+        yield from waits("sfree", c)
+        if c + 1 < n:
+            yield from waits(f"full{(c + 1) % k}", (c + 1) // k)
+            issue_sdp(c + 1)
+            yield ("step", None)
+        yield from waits("pdsready", c)
+        issue_acc(c)
+        yield ("step", None)
+    commit("drain")
+    yield from waits("drain", 0)
+
+
+def gkv_softmax(state, w):
+    n = state.n_chunks
+
+    def waits(name, completion):
+        while not _wait(state, name, completion & 1, completion):
+            yield ("wait", name)
+
+    for ch in range(n):
+        yield from waits("sready", ch)
+        if ("SDP", 0, ch) not in state.mma_done:
+            raise ProtocolError(f"S/dP({ch}) read before it completed")
+        if state.stage_chunk.get(ch % state.stages) != ch:
+            raise ProtocolError(f"lse of chunk {ch} read from a stage holding another chunk")
+        yield ("step", None)
+        state.read_vals.setdefault(ch, set()).add(w)
+        state.sdp_read.setdefault(ch, set()).add(w)
+        state.bar("sfree").arrive()
+        yield ("step", None)
+        if ch > 0:
+            yield from waits("pdsfree", ch - 1)
+            if ("ACC", 0, ch - 1) not in state.mma_done:
+                raise ProtocolError(f"P/dS({ch}) stored while dSV/dSK({ch - 1}) may read them")
+        state.pds_stored.setdefault(ch, set()).add(w)
+        state.bar("pdsready").arrive()
+        yield ("step", None)
+    yield from waits("pdsfree", n - 1)
+    if ("ACC", 0, n - 1) not in state.mma_done:
+        raise ProtocolError("accumulators read before the last products completed")
+
+
+def run_gkv(n_chunks=10, stages=4, seed=0, max_steps=400000):
+    """Replay one random interleaving of the global dSK / dSV kernel's protocol."""
+    rng = random.Random(seed)
+    state = State(n_chunks=n_chunks, stages=stages)
+    state.sdp_read, state.pds_stored, state.read_vals = {}, {}, {}
+    bars = {"kvfull": 1, "drain": 1, "sready": 1, "sfree": 8, "pdsready": 8, "pdsfree": 1}
+    for s in range(4):
+        bars[f"full{s}"] = 2
+        bars[f"empty{s}"] = 1
+    state.bars = {name: Barrier(name, cnt) for name, cnt in bars.items()}
+    state.bar("kvfull").arrive(tx=0)
+    roles = {"producer": gkv_producer(state), "mma": gkv_mma(state)}
+    for w in range(8):
+        roles[f"softmax{w}"] = gkv_softmax(state, w)
+    return _schedule(state, roles, rng, max_steps)

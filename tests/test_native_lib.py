@@ -50,8 +50,9 @@ def test_struct_layout_matches_header():
     """ctypes mirror of p3d_operator has the C layout (checked with the host compiler)."""
     from pack3d_b200 import _native
     src = ROOT / "include" / "pack3d_b200.h"
-    probe = ('#include <stddef.h>\n#include <stdio.h>\n#include "%s"\nint main(void){printf("%%zu %%zu %%zu\\n",'
-             ' sizeof(p3d_operator), offsetof(p3d_operator, blocks), offsetof(p3d_operator, raster_to_packed));}'
+    probe = ('#include <stddef.h>\n#include <stdio.h>\n#include "%s"\nint main(void){printf("%%zu %%zu %%zu %%zu\\n",'
+             ' sizeof(p3d_operator), offsetof(p3d_operator, blocks), offsetof(p3d_operator, raster_to_packed),'
+             ' offsetof(p3d_operator, options));}'
              % src)
     exe = Path(__file__).resolve().parent / ".struct_probe"
     run = subprocess.run(["gcc", "-x", "c", "-", "-o", str(exe)], input=probe, text=True, capture_output=True)
@@ -61,7 +62,8 @@ def test_struct_layout_matches_header():
     finally:
         exe.unlink(missing_ok=True)
     op = _native.Operator
-    assert [int(v) for v in out] == [ctypes_size(op), op.blocks.offset, op.raster_to_packed.offset]
+    assert [int(v) for v in out] == [ctypes_size(op), op.blocks.offset, op.raster_to_packed.offset,
+                                     op.options.offset]
 
 
 def ctypes_size(t):

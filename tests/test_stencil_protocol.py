@@ -32,3 +32,9 @@ def test_model_rejects_the_ambiguous_release_scheme():
 def test_dq_protocol_holds_under_random_interleavings(stages):
     for seed in range(150):
         sp.run_dq(n_chunks=12, stages=stages, seed=seed)
+
+
+@pytest.mark.parametrize("stages", [2, 3, 4])
+def test_global_dkv_protocol_holds_under_random_interleavings(stages):
+    for seed in range(150):
+        sp.run_gkv(n_chunks=10, stages=stages, seed=seed)
