@@ -481,8 +481,10 @@ int p3d_attn_bwd(const p3d_operator *op, const void *dy, const void *sk, const v
     t.delta_g = b.delta_g;
     t.raster_to_packed = op->raster_to_packed;
     t.dq = dq;
+    t.dkl = dkl;
+    t.dvl = dvl;
     if (int st = launch_stencil_bwd_dq(t, s)) return st;
-    if (int st = launch_local_dkv_indexed(a, b.dol, lse_l, b.delta_l, dkl, dvl, s)) return st;
+    if (int st = launch_stencil_bwd_dkv(t, s)) return st;
   } else {
     if (int st = launch_local_dq_indexed(a, b.dol, lse_l, b.delta_l, dq, s)) return st;
     if (int st = launch_local_dkv_indexed(a, b.dol, lse_l, b.delta_l, dkl, dvl, s)) return st;

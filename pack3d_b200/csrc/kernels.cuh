@@ -115,8 +115,10 @@ struct StencilBwdArgs {
   const float *lse_l, *lse_g, *delta_l, *delta_g;  // [B*H, N] in the layout's row order
   const int32_t *raster_to_packed;      // row map of lse / delta / outputs (NULL = raster)
   void *dq;                             // [B,H,N,D] in the layout's row order
+  void *dkl, *dvl;                      // [B,G,N,D] in the layout's row order
 };
 int launch_stencil_bwd_dq(const StencilBwdArgs &a, cudaStream_t s);
+int launch_stencil_bwd_dkv(const StencilBwdArgs &a, cudaStream_t s);
 
 // Tensor-core global dSK / dSV split partials (any token order).
 struct GlobalDkvArgs {

@@ -854,6 +854,381 @@ int launch_gkv_t(const GlobalDkvArgs &a, cudaStream_t stream) {
   return P3D_OK;
 }
 
+
+// ============================================================================ local dK / dV
+//
+// Restates the key-gradient half of the local branch (kernels.py:154-176; stencil.py:91-147
+// with QUERY false) on tensor cores.  A CTA owns one (batch, kv-head) and a 4x4x8 (z, y, x)
+// box of 128 keys (TMEM lanes, row order (z, y, x) as for the forward's query tiles) and
+// streams, for every query head of its group, the 8 query halo planes z0-2 .. z0+5 (8x12
+// windows, 96 queries each):
+//   S^T = K Q^T, dP^T = V dO_l^T, P^T = exp(S^T / sqrt(D) - lse_l) on the key's 5x5x5 cube,
+//   dS^T = P^T (dP^T - Delta_l) / sqrt(D),   dV += P^T dO_l,  dK += dS^T Q.
+// The neighbourhood is symmetric (key j is in query i's clipped cube iff i is in j's), so
+// the mask is the forward's with the roles swapped.  P^T and dS^T are rounded to the
+// storage dtype for the products (the reference keeps them in fp32; the difference is far
+// inside the bf16 tolerance).  Each CTA writes its own keys' dK / dV: no atomics, no
+// partials.
+//
+// TMEM: S^T [0, 96), dP^T [96, 192), P^T [192, 240), dS^T [240, 288), dK [288, 288 + D),
+// dV [288 + D, 288 + 2D).  Eight softmax warps (warp w: TMEM lanes 32(w%4).., query columns
+// 48(w/4)..+48); the protocol is the global dSK / dSV kernel's.
+constexpr uint32_t kLColS = 0, kLColDP = 96, kLColP = 192, kLColDS = 240, kLColAcc = 288;
+
+template <int D>
+struct LkvCfg {
+  static constexpr int kK = D / 16;
+  static constexpr int kBoxT = kRows * 32;           // key tile: 128 rows x 16 channels
+  static constexpr int kBoxP = kKeys * 32;           // query plane: 96 rows x 16 channels
+  static constexpr int kTileBytes = kK * kBoxT;
+  static constexpr int kPlaneBytes = kK * kBoxP;
+  static constexpr int kVals = kKeys * 4;             // lse (or Delta) of one plane, fp32
+  static constexpr int kStageBytes = (2 * kPlaneBytes + 2 * kVals + 1023) / 1024 * 1024;
+  static constexpr int kFixed = 2 * kTileBytes + 1024;
+  static constexpr int kRoom = (227 * 1024 - 2048 - kFixed) / kStageBytes;
+  static constexpr int kStages = kRoom > 4 ? 4 : kRoom;
+  static constexpr int kSmemNeed = kFixed + kStages * kStageBytes;
+  static constexpr int kSmemBytes = kSmemNeed > 116 * 1024 ? kSmemNeed : 116 * 1024;
+  static_assert(kStages >= 2, "the ring must hold two chunks");
+  static_assert(kLColAcc + 2 * D <= 512, "TMEM budget");
+};
+
+struct LkvParams {
+  int Z, Y, X, tiles_z, tiles_y, tiles_x;
+  int heads, kv_heads, rep;
+  int64_t tokens;
+  float sc, inv_sqrt_d;
+  const float *lse_l, *delta_l;  // [B*H, N] in the layout's row order
+  const int32_t *map;            // raster -> packed rows (nullptr: raster)
+  void *dkl, *dvl;               // [B*G, N, D] in the layout's row order
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    stencil_bwd_dkv_kernel(const __grid_constant__ CUtensorMap tkl, const __grid_constant__ CUtensorMap tvl,
+                           const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                           const LkvParams p) {
+  using C = LkvCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[kGNumBars];
+  __shared__ uint32_t tmem_holder;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int unit = blockIdx.x;
+  const int tx = unit % p.tiles_x;
+  unit /= p.tiles_x;
+  const int ty = unit % p.tiles_y;
+  unit /= p.tiles_y;
+  const int tz = unit % p.tiles_z;
+  const int bg = unit / p.tiles_z;
+  const int b = bg / p.kv_heads, g = bg % p.kv_heads;
+  const int x0 = tx * kTX, y0 = ty * kTY, z0 = tz * kTZ;
+  const int n_chunks = p.rep * kLocalChunks;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t k_smem = base, v_smem = base + C::kTileBytes;
+  const uint32_t ring = base + 2 * C::kTileBytes;
+  uint8_t *ring_ptr = smem_raw + (base - raw) + 2 * C::kTileBytes;
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+
+  if (tid == 0) {
+    mbar_init(bar(kGKvFull), 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar(kGFull + s), 2);
+      mbar_init(bar(kGEmpty + s), 1);
+    }
+    mbar_init(bar(kGSReady), 1);
+    mbar_init(bar(kGSFree), 8);
+    mbar_init(bar(kGPdsReady), 8);
+    mbar_init(bar(kGPdsFree), 1);
+    mbar_init(bar(kGDrain), 1);
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(&tmem_holder), kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    prefetch_tmap(&tkl);
+    prefetch_tmap(&tvl);
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tdo);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_holder;
+  // chunk c: query head b*H + g*rep + c/8, query plane z0 - 2 + c%8
+  auto chunk_head = [&](int c) { return b * p.heads + g * p.rep + c / kLocalChunks; };
+  auto chunk_plane = [&](int c) { return z0 - kR + c % kLocalChunks; };
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------------ producer (whole warp)
+    if (lane == 0) {
+      mbar_expect_tx(bar(kGKvFull), 2 * C::kTileBytes);
+      for (int c = 0; c < C::kK; ++c) {
+        tma_load_5d(k_smem + c * C::kBoxT, &tkl, bar(kGKvFull), 16 * c, x0, y0, z0, bg);
+        tma_load_5d(v_smem + c * C::kBoxT, &tvl, bar(kGKvFull), 16 * c, x0, y0, z0, bg);
+      }
+    }
+    int issued = 0;
+    for (int ch = 0; ch < n_chunks; ++ch) {
+      const int s = ch % C::kStages;
+      bool ok = true;
+      if (lane == 0 && ch >= C::kStages)
+        ok = mbar_wait(bar(kGEmpty + s), (ch / C::kStages - 1) & 1, &g_bwd_errors, kWaitNs, kErrProducer);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      const uint32_t stage = ring + s * C::kStageBytes;
+      const uint32_t full = bar(kGFull + s);
+      const int bh = chunk_head(ch), zp = chunk_plane(ch);
+      if (lane == 0) {
+        mbar_expect_tx(full, 2 * C::kPlaneBytes);
+        for (int c = 0; c < C::kK; ++c) {
+          tma_load_5d(stage + c * C::kBoxP, &tq, full, 16 * c, x0 - kR, y0 - kR, zp, bh);
+          tma_load_5d(stage + C::kPlaneBytes + c * C::kBoxP, &tdo, full, 16 * c, x0 - kR, y0 - kR, zp, bh);
+        }
+      }
+      // lse (as log2) and Delta of the plane's 96 queries; +inf outside the volume (P = 0)
+      float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kPlaneBytes);
+      for (int j = lane; j < kKeys; j += 32) {
+        const int qy = y0 - kR + j / kHX, qx = x0 - kR + j % kHX;
+        const bool in = zp >= 0 && zp < p.Z && qy >= 0 && qy < p.Y && qx >= 0 && qx < p.X;
+        float l = __builtin_huge_valf(), dl = 0.f;
+        if (in) {
+          int64_t r = ((int64_t)zp * p.Y + qy) * p.X + qx;
+          if (p.map) r = p.map[r];
+          const int64_t row = (int64_t)bh * p.tokens + r;
+          l = p.lse_l[row] * kLog2e;
+          dl = p.delta_l[row];
+        }
+        vals[j] = l;
+        vals[kKeys + j] = dl;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(full);
+      issued = ch + 1;
+    }
+    if (lane == 0) {
+      mbar_wait(bar(kGKvFull), 0, &g_bwd_errors, kWaitNs, kErrTeardown);
+      for (int ch = issued > C::kStages ? issued - C::kStages : 0; ch < issued; ++ch)
+        mbar_wait(bar(kGFull + ch % C::kStages), (ch / C::kStages) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16(128, kKeys, BF16, false);
+      constexpr uint32_t idesc_acc = idesc_f16(128, D, BF16, true);
+      uint32_t commits[kGNumBars];
+      for (int i = 0; i < kGNumBars; ++i) commits[i] = 0u;
+      auto commit = [&](int bidx) {
+        mma_commit(bar(bidx));
+        ++commits[bidx];
+      };
+      auto stage_of = [&](int c) { return ring + (c % C::kStages) * C::kStageBytes; };
+      auto issue_s_dp = [&](int c) {
+        const uint32_t q = stage_of(c), dov = stage_of(c) + C::kPlaneBytes;
+        for (int kk = 0; kk < C::kK; ++kk)
+          mma_ss(tmem + kLColS, desc_sw32(k_smem + kk * C::kBoxT, 16, 256), desc_sw32(q + kk * C::kBoxP, 16, 256),
+                 idesc_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < C::kK; ++kk)
+          mma_ss(tmem + kLColDP, desc_sw32(v_smem + kk * C::kBoxT, 16, 256), desc_sw32(dov + kk * C::kBoxP, 16, 256),
+                 idesc_s, kk > 0 ? 1u : 0u);
+        commit(kGSReady);
+      };
+      auto issue_acc = [&](int c) {
+        const uint32_t q = stage_of(c), dov = stage_of(c) + C::kPlaneBytes;
+        for (int j = 0; j < kKeys / 16; ++j)
+          mma_ts(tmem + kLColAcc + D, tmem + kLColP + 8 * j, desc_sw32(dov + j * 512, C::kBoxP, 256), idesc_acc,
+                 (c == 0 && j == 0) ? 0u : 1u);
+        for (int j = 0; j < kKeys / 16; ++j)
+          mma_ts(tmem + kLColAcc, tmem + kLColDS + 8 * j, desc_sw32(q + j * 512, C::kBoxP, 256), idesc_acc,
+                 (c == 0 && j == 0) ? 0u : 1u);
+        commit(kGPdsFree);
+        commit(kGEmpty + c % C::kStages);
+      };
+      auto wait_bar = [&](int bidx, int completion) -> bool {
+        if (!mbar_wait(bar(bidx), completion & 1, &g_bwd_errors, kWaitNs, kErrMma)) return false;
+        tc_fence_after();
+        return true;
+      };
+      auto wait_full = [&](int c) { return wait_bar(kGFull + c % C::kStages, c / C::kStages); };
+      bool ok = wait_bar(kGKvFull, 0) && wait_full(0);
+      if (ok) issue_s_dp(0);
+      for (int c = 0; ok && c < n_chunks; ++c) {
+        ok = wait_bar(kGSFree, c);
+        if (!ok) break;
+        if (c + 1 < n_chunks) {
+          ok = wait_full(c + 1);
+          if (!ok) break;
+          issue_s_dp(c + 1);
+        }
+        ok = wait_bar(kGPdsReady, c);
+        if (!ok) break;
+        issue_acc(c);
+      }
+      commit(kGDrain);
+      for (int i = 0; i < kGNumBars; ++i)
+        if (commits[i]) mbar_wait(bar(i), (commits[i] - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax (8 warps) + epilogue
+    const int quarter = warp & 3, half = warp >> 2;
+    const uint32_t t_lanes = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int kz = z0 + quarter, kyl = lane >> 3, kxl = lane & 7;
+    const int ky = y0 + kyl, kx = x0 + kxl;
+    const bool row_ok = kz < p.Z && ky < p.Y && kx < p.X;
+    // this warp's 48 query columns of the 8x12 window that lie in the key's cube
+    uint64_t mask = 0ull;
+#pragma unroll
+    for (int i = 0; i < 48; ++i) {
+      const int j = 48 * half + i, hy = j / kHX, hx = j % kHX;
+      if ((unsigned)(hy - kyl) <= 2u * kR && (unsigned)(hx - kxl) <= 2u * kR) mask |= 1ull << i;
+    }
+    if (!row_ok) mask = 0ull;
+    const float sc = p.sc, inv_sqrt_d = p.inv_sqrt_d;
+    auto wait_warp = [&](int bidx, int completion) -> bool {
+      const bool r = mbar_wait(bar(bidx), completion & 1, &g_bwd_errors, kWaitNs, kErrSoftmax);
+      const bool all = __all_sync(0xffffffffu, r);
+      if (all) tc_fence_after();
+      return all;
+    };
+    bool ok = true;
+    for (int ch = 0; ch < n_chunks; ++ch) {
+      ok = wait_warp(kGSReady, ch);
+      if (!ok) break;
+      const int zp = chunk_plane(ch);
+      const bool active = (unsigned)(zp - kz + kR) <= 2u * kR;  // warp-uniform
+      const float *vals = reinterpret_cast<const float *>(ring_ptr + (size_t)(ch % C::kStages) * C::kStageBytes +
+                                                          2 * C::kPlaneBytes);
+      uint32_t pw[3][8], dw[3][8];
+      if (active) {
+#pragma unroll
+        for (int gi = 0; gi < 3; ++gi) {
+          const int col0 = 48 * half + 16 * gi;
+          uint32_t sv[16], dv[16];
+          tmem_ld16(t_lanes + kLColS + col0, sv);
+          tmem_ld16(t_lanes + kLColDP + col0, dv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int j = col0 + 2 * i, bit = 16 * gi + 2 * i;
+            const float p0 = (mask >> bit) & 1ull ? ex2_approx(fmaf(__uint_as_float(sv[2 * i]), sc, -vals[j])) : 0.f;
+            const float p1 =
+                (mask >> (bit + 1)) & 1ull ? ex2_approx(fmaf(__uint_as_float(sv[2 * i + 1]), sc, -vals[j + 1])) : 0.f;
+            const float d0 = p0 * (__uint_as_float(dv[2 * i]) - vals[kKeys + j]) * inv_sqrt_d;
+            const float d1 = p1 * (__uint_as_float(dv[2 * i + 1]) - vals[kKeys + j + 1]) * inv_sqrt_d;
+            pw[gi][i] = pack2<BF16>(p0, p1);
+            dw[gi][i] = pack2<BF16>(d0, d1);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int gi = 0; gi < 3; ++gi)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pw[gi][i] = dw[gi][i] = 0u;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kGSFree));
+      if (ch > 0) {
+        ok = wait_warp(kGPdsFree, ch - 1);
+        if (!ok) break;
+      }
+#pragma unroll
+      for (int gi = 0; gi < 3; ++gi) {
+        tmem_st8(t_lanes + kLColP + 24 * half + 8 * gi, pw[gi]);
+        tmem_st8(t_lanes + kLColDS + 24 * half + 8 * gi, dw[gi]);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kGPdsReady));
+    }
+    if (ok) ok = wait_warp(kGPdsFree, n_chunks - 1);
+    if (ok) {
+      // warps 0-3 write dK rows, warps 4-7 dV rows (storage dtype)
+      uint32_t acc[D];
+      const uint32_t col = kLColAcc + (half ? D : 0);
+#pragma unroll
+      for (int c = 0; c < D / 16; ++c) tmem_ld16(t_lanes + col + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(acc + 16 * c));
+      tmem_wait_ld();
+      if (row_ok) {
+        int64_t r = ((int64_t)kz * p.Y + ky) * p.X + kx;
+        if (p.map) r = p.map[r];
+        uint16_t *dst = static_cast<uint16_t *>(half ? p.dvl : p.dkl) + ((int64_t)bg * p.tokens + r) * D;
+        uint32_t out[D / 2];
+#pragma unroll
+        for (int i = 0; i < D / 2; ++i) out[i] = pack2<BF16>(__uint_as_float(acc[2 * i]), __uint_as_float(acc[2 * i + 1]));
+#pragma unroll
+        for (int v = 0; v < D / 8; ++v)
+          reinterpret_cast<uint4 *>(dst)[v] = make_uint4(out[4 * v], out[4 * v + 1], out[4 * v + 2], out[4 * v + 3]);
+      }
+    }
+    tmem_wait_st();
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int D, bool BF16>
+int launch_lkv_t(const StencilBwdArgs &a, cudaStream_t stream) {
+  using C = LkvCfg<D>;
+  const int Z = a.grid[0], Y = a.grid[1], X = a.grid[2];
+  const uint64_t es = 2;
+  const uint64_t bh = (uint64_t)a.batch * a.heads, bgs = (uint64_t)a.batch * a.kv_heads;
+  CUtensorMap tkl, tvl, tq, tdo;
+  {
+    const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)Z, bgs};
+    const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es, (uint64_t)Z * Y * X * D * es};
+    const uint32_t box[5] = {16, kTX, kTY, kTZ, 1};
+    if (int st = encode_operand(&tkl, a.dtype, a.kl, 5, dims, strides, box)) return st;
+    if (int st = encode_operand(&tvl, a.dtype, a.vl, 5, dims, strides, box)) return st;
+  }
+  {
+    const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)Z, bh};
+    const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es, (uint64_t)Z * Y * X * D * es};
+    const uint32_t box[5] = {16, kHX, kHY, 1, 1};
+    if (int st = encode_operand(&tq, a.dtype, a.q, 5, dims, strides, box)) return st;
+    if (int st = encode_operand(&tdo, a.dtype, a.dol, 5, dims, strides, box)) return st;
+  }
+  LkvParams p{};
+  p.Z = Z;
+  p.Y = Y;
+  p.X = X;
+  p.tiles_z = (Z + kTZ - 1) / kTZ;
+  p.tiles_y = (Y + kTY - 1) / kTY;
+  p.tiles_x = (X + kTX - 1) / kTX;
+  p.heads = a.heads;
+  p.kv_heads = a.kv_heads;
+  p.rep = a.heads / a.kv_heads;
+  p.tokens = (int64_t)Z * Y * X;
+  p.sc = kLog2e / sqrtf((float)D);
+  p.inv_sqrt_d = 1.f / sqrtf((float)D);
+  p.lse_l = a.lse_l;
+  p.delta_l = a.delta_l;
+  p.map = a.raster_to_packed;
+  p.dkl = a.dkl;
+  p.dvl = a.dvl;
+  const int64_t units = (int64_t)bgs * p.tiles_z * p.tiles_y * p.tiles_x;
+  if (units <= 0) return P3D_OK;
+  if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");
+  auto kernel = stencil_bwd_dkv_kernel<D, BF16>;
+  static bool configured = false;
+  if (!configured) {
+    P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+    configured = true;
+  }
+  kernel<<<(unsigned)units, kThreads, C::kSmemBytes, stream>>>(tkl, tvl, tq, tdo, p);
+  P3D_LAUNCH_CHECK();
+  return P3D_OK;
+}
+
 }  // namespace
 
 int launch_stencil_bwd_dq(const StencilBwdArgs &a, cudaStream_t s) {
@@ -912,6 +1287,17 @@ int launch_global_dkv_tc(const GlobalDkvArgs &a, cudaStream_t s) {
     case 48: return bf16 ? launch_gkv_t<48, true>(a, s) : launch_gkv_t<48, false>(a, s);
     case 64: return bf16 ? launch_gkv_t<64, true>(a, s) : launch_gkv_t<64, false>(a, s);
     default: return fail(P3D_ERR_UNSUPPORTED, "global dSK/dSV: head_dim %d", a.head_dim);
+  }
+}
+
+int launch_stencil_bwd_dkv(const StencilBwdArgs &a, cudaStream_t s) {
+  const bool bf16 = a.dtype == P3D_BF16;
+  switch (a.head_dim) {
+    case 16: return bf16 ? launch_lkv_t<16, true>(a, s) : launch_lkv_t<16, false>(a, s);
+    case 32: return bf16 ? launch_lkv_t<32, true>(a, s) : launch_lkv_t<32, false>(a, s);
+    case 48: return bf16 ? launch_lkv_t<48, true>(a, s) : launch_lkv_t<48, false>(a, s);
+    case 64: return bf16 ? launch_lkv_t<64, true>(a, s) : launch_lkv_t<64, false>(a, s);
+    default: return fail(P3D_ERR_UNSUPPORTED, "stencil backward: head_dim %d", a.head_dim);
   }
 }
 

@@ -414,7 +414,8 @@ def run_dq(n_chunks=12, stages=3, seed=0, max_steps=400000):
 
 
 # ------------------------------------------------------------------ global dSK / dSV kernel
-# Model of global_dkv_tc_kernel: one S^T / dP^T buffer pair (released by the eight softmax
+# Model of global_dkv_tc_kernel -- and of stencil_bwd_dkv_kernel (local dK / dV), which runs
+# the same barrier protocol on other data: one S^T / dP^T buffer pair (released by the eight softmax
 # warps once they have read it), one P^T / dS^T buffer (rewritten once the previous
 # chunk's dSV / dSK products completed), a ring of query chunks filled by TMA copies plus
 # the producer warp's own lse / Delta stores.
