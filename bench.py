@@ -47,6 +47,8 @@ def parse_args():
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--fwd-bwd-steps", type=int, default=3, help="timed fwd+bwd steps (0 disables)")
+    ap.add_argument("--backward-only", type=int, default=0, metavar="N",
+                    help="profiling mode: run the operator backward N times on config-3 inputs and exit")
     ap.add_argument("--kernel-only", type=int, default=0, metavar="N",
                     help="profiling mode: run the stage-(c) kernel N times on the config-1 inputs and exit")
     return ap.parse_args()
@@ -209,10 +211,36 @@ def cpu_layer_seconds(sample_rows=65536, seed=0):
 
 # ------------------------------------------------------------------------------- GPU arm
 
+def backward_only(args, device):
+    """Profiling mode: the operator backward (stage d) alone on config-3 inputs (batch 2)."""
+    from pack3d_b200 import _native
+    from pack3d_b200 import ops as p3d_ops
+    layout = make_layout(CONFIG["grid"]).to(device)
+    geom = layout.geometry
+    n, hq, g, hd = geom.num_tokens, CONFIG["heads"], CONFIG["kv_heads"], CONFIG["head_dim"]
+    gen = torch.Generator(device=device).manual_seed(3)
+    rnd = lambda *shape: torch.randn(*shape, device=device, generator=gen).to(torch.bfloat16)  # noqa: E731
+    q, (kl, vl, kg, vg) = rnd(2, hq, n, hd), (rnd(2, g, n, hd) for _ in range(4))
+    f32 = dict(device=device, dtype=torch.float32)
+    params = (torch.zeros(hd, **f32), torch.zeros(64, **f32), torch.full((2, hq, n), 0.5, device=device,
+              dtype=torch.bfloat16), torch.ones(hd, **f32), torch.full((hd,), 0.25, **f32))
+    inputs = (q, kl, vl, kg, vg, *params)
+    _, saved = p3d_ops.forward(*inputs, geom, 1.0, save_state=True)
+    dy = rnd(2, hq, n, hd)
+    step = lambda: p3d_ops.backward(dy, inputs, saved, geom, 1.0)  # noqa: E731
+    for _ in range(max(args.warmup, 1)):
+        step()
+    times = timed_steps(step, args.backward_only, torch.cuda.current_stream(device))
+    errors = _native.device_errors()
+    print(json.dumps({"backward_only_ms": [round(t, 4) for t in times], "device_errors": errors}), flush=True)
+
+
 def run_b200(args, rank, world, device):
     from pack3d_b200 import _native
     from pack3d_b200 import ops as p3d_ops
     from pack3d_b200.rope import balanced_pairs, rotate_projections
+    if args.backward_only:
+        return backward_only(args, device)
     dtype = torch.bfloat16
     layout = make_layout(CONFIG["grid"]).to(device)
     geom = layout.geometry

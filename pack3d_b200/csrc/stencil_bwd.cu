@@ -558,6 +558,7 @@ enum GkvBar {
 
 struct GkvParams {
   int heads, kv_heads, rep, tokens, summaries, m_tiles, splits, q_chunks, per_split;
+  int bulk_vals;  // lse / Delta rows are 16-byte aligned (N % 4 == 0): bulk-copy them
   float sc, inv_sqrt_d;
   const float *lse_g, *delta_g;  // [B*H, N]
   float *dk_part, *dv_part;      // [B*G, splits, M, D]
@@ -640,23 +641,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t stage = ring + s * C::kStageBytes;
       const uint32_t full = bar(kGFull + s);
       const int bh = chunk_head(ch), n0 = chunk_row0(ch);
+      const int64_t r0 = (int64_t)bh * p.tokens + n0;
+      const uint32_t rows = (uint32_t)min(kGCols, p.tokens - n0);
+      // lse and Delta of the chunk's queries (columns past the last row are masked by the
+      // softmax warps): bulk copies beside the tensor tiles, or plain loads in registers
+      // first, then stores (so the loads are not serialised behind the stores).
+      const uint32_t vals_smem = stage + 2 * C::kTileBytes;
       if (lane == 0) {
-        mbar_expect_tx(full, 2 * C::kTileBytes);
+        mbar_expect_tx(full, 2 * C::kTileBytes + (p.bulk_vals ? 2 * rows * 4 : 0));
         for (int c = 0; c < C::kK; ++c) {
           tma_load_3d(stage + c * C::kBox, &tq, full, 16 * c, n0, bh);
           tma_load_3d(stage + C::kTileBytes + c * C::kBox, &tdo, full, 16 * c, n0, bh);
         }
+        if (p.bulk_vals) {
+          bulk_load(vals_smem, p.lse_g + r0, rows * 4, full);
+          bulk_load(vals_smem + C::kRowVals, p.delta_g + r0, rows * 4, full);
+        }
       }
-      // lse (as log2) and Delta of the chunk's queries; +inf past the last row (P = 0)
-      float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kTileBytes);
-      for (int j = lane; j < kGCols; j += 32) {
-        const int n = n0 + j;
-        const bool in = n < p.tokens;
-        const int64_t r = (int64_t)bh * p.tokens + n;
-        vals[j] = in ? p.lse_g[r] * kLog2e : __builtin_huge_valf();
-        vals[kGCols + j] = in ? p.delta_g[r] : 0.f;
+      if (!p.bulk_vals) {
+        float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kTileBytes);
+        float l[kGCols / 32], dl[kGCols / 32];
+#pragma unroll
+        for (int k = 0; k < kGCols / 32; ++k) {
+          const int j = lane + 32 * k;
+          l[k] = j < (int)rows ? __ldg(p.lse_g + r0 + j) : 0.f;
+          dl[k] = j < (int)rows ? __ldg(p.delta_g + r0 + j) : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < kGCols / 32; ++k) {
+          vals[lane + 32 * k] = l[k];
+          vals[kGCols + lane + 32 * k] = dl[k];
+        }
+        __syncwarp();
       }
-      __syncwarp();
       if (lane == 0) mbar_arrive(full);
       issued = ch + 1;
     }
@@ -738,8 +755,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int ch = 0; ch < n_chunks; ++ch) {
       ok = wait_warp(kGSReady, ch);
       if (!ok) break;
-      const float *vals = reinterpret_cast<const float *>(ring_ptr + (size_t)(ch % C::kStages) * C::kStageBytes +
-                                                          2 * C::kTileBytes);
+      const float4 *vals = reinterpret_cast<const float4 *>(ring_ptr + (size_t)(ch % C::kStages) * C::kStageBytes +
+                                                            2 * C::kTileBytes);
+      const int valid = min(kGCols, p.tokens - chunk_row0(ch));  // query columns inside the volume
       uint32_t pw[2][16], dw[2][16];
 #pragma unroll
       for (int gi = 0; gi < 2; ++gi) {
@@ -749,14 +767,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(t_lanes + kGColDP + col0, dv);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int j = col0 + 2 * i;
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * i]), sc, -vals[j]));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * i + 1]), sc, -vals[j + 1]));
-          const float d0 = p0 * (__uint_as_float(dv[2 * i]) - vals[kGCols + j]) * inv_sqrt_d;
-          const float d1 = p1 * (__uint_as_float(dv[2 * i + 1]) - vals[kGCols + j + 1]) * inv_sqrt_d;
-          pw[gi][i] = pack2<BF16>(p0, p1);
-          dw[gi][i] = pack2<BF16>(d0, d1);
+        for (int i4 = 0; i4 < 8; ++i4) {
+          const int j = col0 + 4 * i4;
+          const float4 l4 = vals[j / 4], d4 = vals[(kGCols + j) / 4];
+          const float ls[4] = {l4.x, l4.y, l4.z, l4.w}, ds[4] = {d4.x, d4.y, d4.z, d4.w};
+          float pp[4], dd[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = 4 * i4 + e;
+            // columns past the volume may hold stale values: they give exact zeros
+            const bool in = j + e < valid;
+            pp[e] = in ? ex2_approx(fmaf(__uint_as_float(sv[i]), sc, -ls[e] * kLog2e)) : 0.f;
+            dd[e] = in ? pp[e] * (__uint_as_float(dv[i]) - ds[e]) * inv_sqrt_d : 0.f;
+          }
+          pw[gi][2 * i4] = pack2<BF16>(pp[0], pp[1]);
+          pw[gi][2 * i4 + 1] = pack2<BF16>(pp[2], pp[3]);
+          dw[gi][2 * i4] = pack2<BF16>(dd[0], dd[1]);
+          dw[gi][2 * i4 + 1] = pack2<BF16>(dd[2], dd[3]);
         }
       }
       tc_fence_before();
@@ -834,6 +861,7 @@ int launch_gkv_t(const GlobalDkvArgs &a, cudaStream_t stream) {
   p.q_chunks = (a.tokens + kGCols - 1) / kGCols;
   p.splits = a.splits;
   p.per_split = a.per_split;
+  p.bulk_vals = a.tokens % 4 == 0 && ((uintptr_t)a.lse_g & 15) == 0 && ((uintptr_t)a.delta_g & 15) == 0;
   p.sc = kLog2e / sqrtf((float)D);
   p.inv_sqrt_d = 1.f / sqrtf((float)D);
   p.lse_g = a.lse_g;
@@ -989,21 +1017,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_5d(stage + C::kPlaneBytes + c * C::kBoxP, &tdo, full, 16 * c, x0 - kR, y0 - kR, zp, bh);
         }
       }
-      // lse (as log2) and Delta of the plane's 96 queries; +inf outside the volume (P = 0)
+      // lse (as log2) and Delta of the plane's 96 queries; +inf outside the volume (P = 0).
+      // All loads are issued before any store, so they overlap.
       float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kPlaneBytes);
-      for (int j = lane; j < kKeys; j += 32) {
+      float l[kKeys / 32], dl[kKeys / 32];
+#pragma unroll
+      for (int k = 0; k < kKeys / 32; ++k) {
+        const int j = lane + 32 * k;
         const int qy = y0 - kR + j / kHX, qx = x0 - kR + j % kHX;
         const bool in = zp >= 0 && zp < p.Z && qy >= 0 && qy < p.Y && qx >= 0 && qx < p.X;
-        float l = __builtin_huge_valf(), dl = 0.f;
+        l[k] = __builtin_huge_valf();
+        dl[k] = 0.f;
         if (in) {
           int64_t r = ((int64_t)zp * p.Y + qy) * p.X + qx;
-          if (p.map) r = p.map[r];
+          if (p.map) r = __ldg(p.map + r);
           const int64_t row = (int64_t)bh * p.tokens + r;
-          l = p.lse_l[row] * kLog2e;
-          dl = p.delta_l[row];
+          l[k] = __ldg(p.lse_l + row) * kLog2e;
+          dl[k] = __ldg(p.delta_l + row);
         }
-        vals[j] = l;
-        vals[kKeys + j] = dl;
+      }
+#pragma unroll
+      for (int k = 0; k < kKeys / 32; ++k) {
+        vals[lane + 32 * k] = l[k];
+        vals[kKeys + lane + 32 * k] = dl[k];
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(full);
