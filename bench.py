@@ -235,6 +235,129 @@ def backward_only(args, device):
     print(json.dumps({"backward_only_ms": [round(t, 4) for t in times], "device_errors": errors}), flush=True)
 
 
+def run_sharded(args, rank, world, device):
+    """N > 1: the config-1 field split into z-slabs, one per rank (the same 64^3 field at
+    every N: strong scaling).  Each rank runs the layer on its planes with the halo
+    exchange and the summary all-gather over NCCL (pack3d_b200.sharded)."""
+    from pack3d_b200 import _native
+    from pack3d_b200.rope import balanced_pairs, rotate_projections
+    from pack3d_b200.sharded import (ZSlabs, exchange_halos, gather_summaries, pool_summaries,
+                                     sharded_layer_forward, slab_forward, slab_layout)
+    grid, b, dim = CONFIG["grid"], CONFIG["batch"], CONFIG["dim"]
+    hq, g, hd = CONFIG["heads"], CONFIG["kv_heads"], CONFIG["head_dim"]
+    slabs = ZSlabs(grid, world, rank, radius=CONFIG["radius"], block_depth=CONFIG["block"][0])
+    layout = slab_layout(grid, CONFIG["block"], radius=CONFIG["radius"], slabs=slabs).to(device)
+    geom = layout.geometry
+    n_total, n = math.prod(grid), slabs.tokens
+    layer = make_layer(torch.bfloat16, device)
+    gen = torch.Generator(device=device).manual_seed(1000)
+    lo, hi = slabs.token_range()
+    x = torch.randn(b, n_total, dim, device=device, dtype=torch.bfloat16, generator=gen)[:, lo:hi].contiguous()
+    stream = torch.cuda.current_stream(device)
+    flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+
+    def flush():
+        flush_buf.zero_()
+
+    def step():
+        with torch.inference_mode():
+            return sharded_layer_forward(layer, x, layout)
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return t.item()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(device)
+    torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index).__enter__()
+    times = timed_steps(step, args.steps, stream, flush)
+    torch.cuda.synchronize(device)
+    torch.distributed.barrier()
+    ms = max_over_ranks(sum(times) / len(times))
+
+    # the slab forward kernel alone (halo and summaries already exchanged), for the roofline
+    with torch.inference_mode():
+        xn = layer.norm(x)
+        q = layer.to_q(xn).reshape(b, n, hq, hd).transpose(1, 2)
+        kl, vl, kg, vg = (t.reshape(b, n, g, hd).transpose(1, 2) for t in layer.to_kv(xn).chunk(4, -1))
+        q, kl, kg = rotate_projections(q, kl, kg, layout.coords, balanced_pairs(hd), layout.grid_shape, packed=False)
+        gate = layer.gate(xn).reshape(b, n, hq, 2).softmax(-1)[..., 1].transpose(1, 2).contiguous()
+        vl, vg = vl.contiguous(), vg.contiguous()
+        params = (layer.pool_weight, layer.slot_bias, gate, layer.local_scale, layer.global_scale)
+        skr, svr = pool_summaries(kg, vg, layer.pool_weight, layer.slot_bias, geom)
+        sk, sv = gather_summaries(skr), gather_summaries(svr)
+        kl_ext, vl_ext = exchange_halos(kl, slabs), exchange_halos(vl, slabs)
+        kernel = lambda: slab_forward(q, kl_ext, vl_ext, sk, sv, *params, geom, slabs)  # noqa: E731
+        for _ in range(3):
+            kernel()
+        torch.cuda.synchronize(device)
+        torch.distributed.barrier()
+        kernel_ms = max_over_ranks(statistics.median(timed_steps(kernel, max(args.steps, 10), stream)))
+
+    x_host = x.detach().cpu().pin_memory()
+    y_host = torch.empty((b, n, dim), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        xd = x_host.to(device, non_blocking=True)
+        with torch.inference_mode():
+            y = sharded_layer_forward(layer, xd, layout)
+        y_host.copy_(y, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    torch.distributed.barrier()
+    e2e_ms = max_over_ranks(sum(timed_steps(e2e_step, args.steps, stream, flush)) / args.steps)
+    clocks.__exit__(None, None, None)
+    clock_summary = clocks.summary()
+    errors = _native.device_errors()
+    if max_over_ranks(float(errors)):
+        raise RuntimeError(f"device error flags set: {errors}")
+
+    full_geom = make_layout(grid).geometry
+    w_bar, m = mean_valid_neighbors(full_geom), full_geom.num_summaries
+    flops_total = 4.0 * b * hq * n_total * hd * (m + w_bar)
+    peak, peak_sustained, _, peak_kind = measured_peaks()
+    achieved = flops_total / world / (kernel_ms * 1e-3) / 1e12
+    tokens = b * n_total
+    return {
+        "metric": METRIC,
+        "value": round(tokens / (ms * 1e-3), 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: x ~ N(0,1) (seeded), random-init PACK3DAttention weights (seed 0)",
+        "config": {"workload": "BASELINE config 1 field (64^3, batch 1, dim 192 = 4 heads x 48, radius 2, 4096 "
+                               "summaries) split into z-slabs, one per GPU; layer forward",
+                   "grid": list(grid), "batch": b, "heads": hq, "kv_heads": g, "head_dim": hd, "dim": dim,
+                   "summaries": m, "radius": CONFIG["radius"],
+                   "parallelism": f"{world} z-slabs of {slabs.planes} planes; NCCL halo exchange (2 planes "
+                                  "of kl, vl each way) + summary all-gather",
+                   "cuda_graph": False,
+                   "l2": "flushed between timed steps (256 MiB write outside the timed events)"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "kernel": "stencil_fwd_kernel on one slab (p3d_attn_fwd_slab), max over ranks",
+                     "kernel_ms": round(kernel_ms, 4), "flop_per_launch": flops_total / world,
+                     "peak_kind": peak_kind, "peak_sustained": peak_sustained},
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": x_host.numel() * x_host.element_size() * world,
+                "d2h_bytes_per_step": y_host.numel() * y_host.element_size() * world},
+        "gpu_launches": 5 * args.steps,
+        "clocks": clock_summary,
+    }
+
+
 def run_b200(args, rank, world, device):
     from pack3d_b200 import _native
     from pack3d_b200 import ops as p3d_ops
@@ -384,7 +507,7 @@ def run_b200(args, rank, world, device):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: x ~ N(0,1) (seeded), random-init PACK3DAttention weights (seed 0)",
@@ -434,7 +557,7 @@ def main():
         print(json.dumps({
             "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": len(samples), "warmup": min(args.warmup, 1), "ms_per_step": round(s * 1e3, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: x ~ N(0,1) (seeded), random-init PACK3DAttention weights (seed 0)",
             "config": {"workload": "BASELINE config 1 (64^3, batch 1, 4 heads x 48, radius 2, 4096 summaries), "
                                    "layer forward"},
@@ -449,12 +572,12 @@ def main():
     torch.cuda.set_device(device)
     if world > 1:
         import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)
-    line = run_b200(args, rank, world, device)
+    line = run_b200(args, rank, world, device) if world == 1 else run_sharded(args, rank, world, device)
     if line is None:
         return
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_s, wall, threads, sample = cpu_layer_seconds()
         n = math.prod(CONFIG["grid"]) * CONFIG["batch"]
         line["cpu_baseline"] = {"value": round(n / cpu_s, 1), "unit": "tokens/s", "cores": threads, "kind": "port",

@@ -138,6 +138,32 @@ P3D_API int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, vo
 P3D_API size_t p3d_attn_fwd_workspace(const p3d_operator *op, unsigned flags);
 
 /*
+ * z-slab extents of one rank when a volume is sharded across GPUs along z.  No counterpart
+ * in the reference, which runs on one GPU.  op->q, op->gate, y, ol, og, lse_* describe this
+ * rank's planes [center_z0, center_z0 + op->grid[0]); op->kl / op->vl hold the planes
+ * [halo_z0, halo_z0 + halo_planes): this rank's own plus the neighbours' halo planes
+ * (radius planes each side, clipped to the volume).
+ */
+typedef struct {
+  int32_t global_planes; /* z extent of the whole volume */
+  int32_t center_z0;     /* global z of this rank's first plane */
+  int32_t halo_z0;       /* global z of the first plane of op->kl / op->vl */
+  int32_t halo_planes;   /* planes in op->kl / op->vl */
+  int32_t summaries;     /* rows of the gathered sk / sv: the summaries of all ranks */
+} p3d_slab;
+
+/*
+ * Forward of one z-slab on tensor cores (complete radius-2 stencil, raster storage,
+ * 16-bit dtypes): local attention over op->kl / op->vl with halo planes, global attention
+ * over the gathered summaries sk, sv [B,G,slab->summaries,D] (pooled per rank with
+ * p3d_pool_fwd and all-gathered by the caller).  Writes y (and with P3D_FWD_SAVE_STATE ol,
+ * og, lse_l, lse_g) for this rank's rows.  Needs no workspace.  No counterpart in the
+ * reference (single-GPU only); the halo exchange and all-gather replace nothing there.
+ */
+P3D_API int p3d_attn_fwd_slab(const p3d_operator *op, const p3d_slab *slab, void *y, const void *sk, const void *sv,
+                      void *ol, void *og, float *lse_l, float *lse_g, unsigned flags, void *stream);
+
+/*
  * Forward (inference, no saved state) that allocates nothing and needs no workspace.
  * No counterpart in the reference.  For callers that cannot allocate device memory --
  * plugins inside a host framework that owns all device memory, or real-time loops that

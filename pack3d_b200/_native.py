@@ -42,6 +42,13 @@ class Operator(ctypes.Structure):
     ]
 
 
+class Slab(ctypes.Structure):
+    """Mirror of ``p3d_slab`` in ``include/pack3d_b200.h``."""
+
+    _fields_ = [("global_planes", ctypes.c_int32), ("center_z0", ctypes.c_int32), ("halo_z0", ctypes.c_int32),
+                ("halo_planes", ctypes.c_int32), ("summaries", ctypes.c_int32)]
+
+
 _SIGNATURES = {
     "p3d_strerror": (ctypes.c_char_p, [_c_int]),
     "p3d_last_error": (ctypes.c_char_p, []),
@@ -57,6 +64,8 @@ _SIGNATURES = {
                               _vp, ctypes.c_size_t, _vp]),
     "p3d_attn_fwd_workspace": (ctypes.c_size_t, [ctypes.POINTER(Operator), ctypes.c_uint]),
     "p3d_attn_fwd_noalloc": (_c_int, [ctypes.POINTER(Operator), _vp, _vp, _vp, _vp]),
+    "p3d_attn_fwd_slab": (_c_int, [ctypes.POINTER(Operator), ctypes.POINTER(Slab), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                   ctypes.c_uint, _vp]),
     "p3d_attn_bwd": (_c_int, [ctypes.POINTER(Operator), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                               _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "p3d_attn_bwd_workspace": (ctypes.c_size_t, [ctypes.POINTER(Operator)]),

@@ -361,6 +361,8 @@ int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, 
     a.head_dim = op->head_dim;
     a.summaries = summaries_of(op);
     for (int i = 0; i < 3; ++i) a.grid[i] = op->grid[i];
+    a.global_planes = a.k_planes = op->grid[0];
+    a.q_z0 = a.k_z0 = 0;
     a.q = op->q;
     a.kl = op->kl;
     a.vl = op->vl;
@@ -396,6 +398,60 @@ int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, 
   void *ol_buf = save ? ol : ol_ws;
   if (int st = launch_local_fwd_indexed(a, ol_buf, save ? lse_l : nullptr, s)) return st;
   return launch_global_fwd_mix(a, ol_buf, y, save ? og : nullptr, save ? lse_g : nullptr, s);
+}
+
+int p3d_attn_fwd_slab(const p3d_operator *op, const p3d_slab *slab, void *y, const void *sk, const void *sv,
+                      void *ol, void *og, float *lse_l, float *lse_g, unsigned flags, void *stream) {
+  if (int st = validate(op)) return st;
+  P3D_CHECK_ARG(slab != nullptr && y && sk && sv, "p3d_attn_fwd_slab: slab, y, sk and sv are required");
+  const bool save = flags & P3D_FWD_SAVE_STATE;
+  P3D_CHECK_ARG(!save || (ol && og && lse_l && lse_g), "p3d_attn_fwd_slab: saving state needs ol, og, lse_l, lse_g");
+  P3D_CHECK_ARG((flags & ~(unsigned)(P3D_FWD_SAVE_STATE | P3D_FWD_SUMMARIES_GIVEN)) == 0u,
+                "p3d_attn_fwd_slab: unsupported flags 0x%x", flags);
+  P3D_CHECK_ARG(op->stencil && !op->raster_to_packed,
+                "p3d_attn_fwd_slab: needs a complete stencil in raster storage");
+  P3D_CHECK_ARG(!(op->options & P3D_OPT_INDEXED_ONLY), "p3d_attn_fwd_slab: has no indexed form");
+  if (!stencil_fwd_supported(op->dtype, op->head_dim, op->radius, slab->summaries))
+    return fail(P3D_ERR_UNSUPPORTED, "p3d_attn_fwd_slab: needs bf16/f16, head_dim 16/32/48/64, radius 2 and sm_100");
+  const int nz = op->grid[0], r = op->radius[0];
+  const int need_lo = std::max(0, slab->center_z0 - r);
+  const int need_hi = std::min(slab->global_planes, slab->center_z0 + nz + r);
+  P3D_CHECK_ARG(slab->global_planes >= 1 && slab->center_z0 >= 0 && slab->center_z0 + nz <= slab->global_planes,
+                "p3d_attn_fwd_slab: rank planes [%d, %d) outside the volume of %d planes", slab->center_z0,
+                slab->center_z0 + nz, slab->global_planes);
+  P3D_CHECK_ARG(slab->halo_z0 <= need_lo && slab->halo_z0 + slab->halo_planes >= need_hi && slab->halo_z0 >= 0 &&
+                    slab->halo_z0 + slab->halo_planes <= slab->global_planes,
+                "p3d_attn_fwd_slab: kl/vl planes [%d, %d) do not cover [%d, %d)", slab->halo_z0,
+                slab->halo_z0 + slab->halo_planes, need_lo, need_hi);
+  P3D_CHECK_ARG(slab->summaries >= 1, "p3d_attn_fwd_slab: no summaries");
+  StencilFwdArgs a{};
+  a.dtype = op->dtype;
+  a.gate_dtype = op->gate_dtype;
+  a.batch = op->batch;
+  a.heads = op->heads;
+  a.kv_heads = op->kv_heads;
+  a.head_dim = op->head_dim;
+  a.summaries = slab->summaries;
+  for (int i = 0; i < 3; ++i) a.grid[i] = op->grid[i];
+  a.global_planes = slab->global_planes;
+  a.q_z0 = slab->center_z0;
+  a.k_z0 = slab->halo_z0;
+  a.k_planes = slab->halo_planes;
+  a.q = op->q;
+  a.kl = op->kl;
+  a.vl = op->vl;
+  a.raster_to_packed = nullptr;
+  a.sk = sk;
+  a.sv = sv;
+  a.gate = op->gate;
+  a.sl = op->local_scale;
+  a.sg = op->global_scale;
+  a.y = y;
+  a.ol = save ? ol : nullptr;
+  a.og = save ? og : nullptr;
+  a.lse_l = save ? lse_l : nullptr;
+  a.lse_g = save ? lse_g : nullptr;
+  return launch_stencil_fwd(a, static_cast<cudaStream_t>(stream));
 }
 
 size_t p3d_attn_bwd_workspace(const p3d_operator *op) {

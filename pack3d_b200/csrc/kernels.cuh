@@ -91,7 +91,11 @@ inline int64_t sum_rows_tmp(int64_t R, int64_t C) { return ((R + 255) / 256) * C
 struct StencilFwdArgs {
   int dtype, gate_dtype;
   int batch, heads, kv_heads, head_dim, summaries;
-  int grid[3];
+  int grid[3];                        // query (centre) buffer: grid[0] planes of grid[1] x grid[2]
+  // z-slab extents (whole volume: global_planes = k_planes = grid[0], q_z0 = k_z0 = 0):
+  int global_planes;                  // planes of the whole volume (keys outside are masked)
+  int q_z0;                           // global z of the query buffer's first plane
+  int k_z0, k_planes;                 // global z and plane count of the kl / vl buffers
   const void *q, *kl, *vl, *sk, *sv;  // q/kl/vl in raster order (contiguous [B,H|G,Z,Y,X,D])
   const int32_t *raster_to_packed;    // output row map (NULL = raster)
   const void *gate;

@@ -103,7 +103,8 @@ enum Bar {
 };
 
 struct FwdParams {
-  int Z, Y, X, tiles_z, tiles_y, tiles_x;
+  int Z, Y, X, tiles_z, tiles_y, tiles_x;  // Z: planes of the query (centre) buffer
+  int Zg, qz0, kz0;  // global planes; global z of query-buffer plane 0 and of K/V-buffer plane 0
   int heads, kv_heads, summaries, global_chunks;
   int64_t tokens;
   float sc;          // log2(e) / sqrt(D): scores -> exp2 domain
@@ -291,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ch < kLocalChunks) {
           mbar_expect_tx(full, 4 * C::kKeyBytes);
           for (int t = 0; t < 2; ++t) {
-            const int z = z0 + kTZ * t - kR + ch;
+            const int z = p.qz0 + z0 + kTZ * t - kR + ch - p.kz0;  // plane in the K/V buffer
             for (int c = 0; c < C::kK; ++c) {
               tma_load_5d(stage + t * C::kKeyBytes + c * C::kBoxK, &tkl, full, 16 * c, x0 - kR, y0 - kR, z, bg);
               tma_load_5d(stage + (2 + t) * C::kKeyBytes + c * C::kBoxK, &tvl, full, 16 * c, x0 - kR, y0 - kR, z,
@@ -469,8 +470,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = wait_warp(bar(kSReady + 2 * t + buf), (ch >> 1) & 1);
       if (!ok) break;
       const bool local = ch < kLocalChunks;
-      const int zp = z0 + kTZ * t - kR + ch;
-      const bool active = !local || ((unsigned)(ch - qz) <= 2u * kR && zp >= 0 && zp < p.Z);  // warp-uniform
+      const int zp = p.qz0 + z0 + kTZ * t - kR + ch;  // global plane of this local chunk
+      const bool active = !local || ((unsigned)(ch - qz) <= 2u * kR && zp >= 0 && zp < p.Zg);  // warp-uniform
       if (active) {
         float s[kKeys];
 #pragma unroll
@@ -580,8 +581,9 @@ int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
     if (int st = encode_operand(&tq, a.dtype, a.q, 5, dims, strides, box)) return st;
   }
   {
-    const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)Z, bgs};
-    const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es, (uint64_t)Z * Y * X * D * es};
+    const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)a.k_planes, bgs};
+    const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es,
+                                 (uint64_t)a.k_planes * Y * X * D * es};
     const uint32_t box[5] = {16, kHX, kHY, 1, 1};
     if (int st = encode_operand(&tkl, a.dtype, a.kl, 5, dims, strides, box)) return st;
     if (int st = encode_operand(&tvl, a.dtype, a.vl, 5, dims, strides, box)) return st;
@@ -595,6 +597,9 @@ int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
   }
   FwdParams p{};
   p.Z = Z;
+  p.Zg = a.global_planes;
+  p.qz0 = a.q_z0;
+  p.kz0 = a.k_z0;
   p.Y = Y;
   p.X = X;
   p.tiles_z = (Z + 2 * kTZ - 1) / (2 * kTZ);
