@@ -50,6 +50,7 @@ typedef enum { P3D_F32 = 0, P3D_F16 = 1, P3D_BF16 = 2 } p3d_dtype;
 #define P3D_FWD_SAVE_STATE 1u   /* write ol, og, lse_l, lse_g for the backward */
 #define P3D_FWD_FORCE_INDEXED 2u /* use the indexed (neighbour-table) kernels even on a stencil */
 #define P3D_FWD_SUMMARIES_GIVEN 4u /* sk, sv already hold the pooled summaries: skip stage (b) */
+#define P3D_FWD_Y_ROWS 8u /* write y token-major, [B,N,H,D] (the layout to_out reads), not [B,H,N,D] */
 
 /* Static description string of a status code. */
 P3D_API const char *p3d_strerror(int status);
@@ -95,6 +96,22 @@ P3D_API int p3d_pool_fwd(const void *k, const void *v, const float *weight, cons
                  const int32_t *blocks, int fine_blocks, int slots, int pool_size, void *sk, void *sv,
                  float *sk32, float *sv32, int dtype, int batch, int kv_heads, int tokens, int head_dim,
                  float temperature, void *stream);
+
+/*
+ * Layer glue (reference attention.py:53-89), HBM-bound helpers of the layer's inference path.
+ * p3d_layer_norm: y = LayerNorm(x) over the last dimension (nn.LayerNorm, attention.py:64),
+ *   x, y [rows, dim], weight, bias [dim], all in dtype (bf16 / f16), fp32 statistics.
+ * p3d_qkv_split: from the projections qp [B,N,H*D] (to_q) and kvp [B,N,4*G*D] (to_kv, channel
+ *   blocks kl, vl, kg, vg; attention.py:70-72) write q, kl, vl, kg, vg [B,H|G,N,D]; q, kl, kg
+ *   rotated by the axial RoPE phase table (the table of p3d_rope, rotary.py:74-85; coordinates
+ *   coords [N,3]), vl, vg copied.  One pass in place of three rotations and two strided copies
+ *   (rotary.py:94-106 and the .contiguous() copies of autograd.py:13).
+ */
+P3D_API int p3d_layer_norm(const void *x, const void *weight, const void *bias, void *y, int dtype, int64_t rows,
+                   int dim, float eps, void *stream);
+P3D_API int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl, void *vl, void *kg, void *vg,
+                  int dtype, int batch, int heads, int kv_heads, int tokens, int head_dim, const int64_t *coords,
+                  int pz, int py, int px, const float *phases, int ez, int ey, int ex, void *stream);
 
 /* Operator arguments shared by forward and backward (all device pointers, contiguous). */
 typedef struct {

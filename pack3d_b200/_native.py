@@ -18,6 +18,7 @@ DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 FWD_SAVE_STATE = 1
 FWD_FORCE_INDEXED = 2
 FWD_SUMMARIES_GIVEN = 4
+FWD_Y_ROWS = 8
 OPT_INDEXED_ONLY = 1
 
 _c_int, _c_i64, _c_f32, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
@@ -58,6 +59,9 @@ _SIGNATURES = {
     "p3d_rope": (_c_int, [_vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                           _vp, _c_i64, _c_i64, _c_int, _c_int, _c_int, _vp, _vp, _c_int, _c_int, _c_int,
                           _c_int, _c_int, _vp]),
+    "p3d_layer_norm": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_i64, _c_int, _c_f32, _vp]),
+    "p3d_qkv_split": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                               _vp, _c_int, _c_int, _c_int, _vp, _c_int, _c_int, _c_int, _vp]),
     "p3d_pool_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _c_int,
                               _c_int, _c_int, _c_int, _c_int, _c_f32, _vp]),
     "p3d_attn_fwd": (_c_int, [ctypes.POINTER(Operator), _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_uint,

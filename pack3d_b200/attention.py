@@ -66,6 +66,8 @@ class PACK3DAttention(nn.Module):
         if self.backend != "b200":
             raise ValueError("unknown backend; implicit fallback is disabled")
         residual, b, n = x, x.shape[0], x.shape[1]
+        if self._fast_inference(x):
+            return self._forward_inference(x, layout)
         x = self.norm(x)
         q = self.to_q(x).reshape(b, n, self.heads, self.head_dim).transpose(1, 2)
         kl, vl, kg, vg = (t.reshape(b, n, self.kv_heads, self.head_dim).transpose(1, 2)
@@ -79,3 +81,55 @@ class PACK3DAttention(nn.Module):
         out = pack3d_streamed(q, kl, vl, kg, vg, self.pool_weight, self.slot_bias, gate, self.local_scale,
                               self.global_scale, layout.geometry, temperature=self.temperature)
         return residual + self.to_out(out.transpose(1, 2).reshape(b, n, -1))
+
+    def _fast_inference(self, x):
+        """Gradient-free 16-bit axial calls take the fused glue path (same arithmetic)."""
+        return (not torch.is_grad_enabled() or not (x.requires_grad or any(p.requires_grad for p in self.parameters()))) \
+            and x.dtype in (torch.bfloat16, torch.float16) and self.position_encoding == "axial" \
+            and x.is_cuda and self.dim % 8 == 0 and self.head_dim % 8 == 0 \
+            and all(p.dtype == x.dtype for p in self.parameters())
+
+    def _forward_inference(self, x, layout):
+        """The same layer as :meth:`forward` with the glue fused into library kernels.
+
+        LayerNorm runs in ``p3d_layer_norm``; one ``p3d_qkv_split`` pass turns the two
+        projection outputs into rotated q / kl / kg and head-major vl / vg; the core writes
+        its output token-major so the output projection reads it without a transpose copy.
+        """
+        from . import _native
+        from .ops import forward as core_forward
+        from .rope import phase_tables
+        b, n = x.shape[0], x.shape[1]
+        h, g, d = self.heads, self.kv_heads, self.head_dim
+        x = x.contiguous()
+        xn = torch.empty_like(x)
+        dev = x.device
+        code = _native.DTYPE_CODE[x.dtype]
+        lib = _native.lib()
+        stream = _native.stream_of(dev)
+        with torch.cuda.device(dev):
+            _native.check(lib.p3d_layer_norm(_native.ptr(x), _native.ptr(self.norm.weight), _native.ptr(self.norm.bias),
+                                             _native.ptr(xn), code, b * n, self.dim, float(self.norm.eps), stream),
+                          "p3d_layer_norm")
+        qp, kvp = self.to_q(xn), self.to_kv(xn)
+        pairs = balanced_pairs(d)
+        extents = tuple(int(e) for e in layout.grid_shape)
+        _, phases = phase_tables(dev, pairs, extents)
+        if phases is None:   # coordinate extents too large for a table: the general RoPE path
+            q, kl, kg = rotate_projections(qp.reshape(b, n, h, d).transpose(1, 2),
+                                           *(t.reshape(b, n, g, d).transpose(1, 2) for t in kvp.chunk(4, -1)[0::2]),
+                                           layout.coords, pairs, extents, packed=False)
+            vl, vg = (t.reshape(b, n, g, d).transpose(1, 2).contiguous() for t in kvp.chunk(4, -1)[1::2])
+        else:
+            coords = layout.coords.to(device=dev, dtype=torch.int64).contiguous()
+            q = torch.empty((b, h, n, d), dtype=x.dtype, device=dev)
+            kl, vl, kg, vg = (torch.empty((b, g, n, d), dtype=x.dtype, device=dev) for _ in range(4))
+            with torch.cuda.device(dev):
+                _native.check(lib.p3d_qkv_split(_native.ptr(qp), _native.ptr(kvp), _native.ptr(q), _native.ptr(kl),
+                                                _native.ptr(vl), _native.ptr(kg), _native.ptr(vg), code, b, h, g, n, d,
+                                                _native.ptr(coords), *pairs, _native.ptr(phases), *extents, stream),
+                              "p3d_qkv_split")
+        gate = self.gate(xn).reshape(b, n, h, 2).softmax(-1)[..., 1].transpose(1, 2).contiguous()
+        y, _ = core_forward(q, kl, vl, kg, vg, self.pool_weight, self.slot_bias, gate, self.local_scale,
+                            self.global_scale, layout.geometry, self.temperature, save_state=False, y_rows=True)
+        return x + self.to_out(y.transpose(1, 2).reshape(b, n, -1))

@@ -339,6 +339,9 @@ int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, 
                  float *lse_g, unsigned flags, void *workspace, size_t workspace_bytes, void *stream) {
   if (int st = validate(op)) return st;
   P3D_CHECK_ARG(y && sk && sv, "p3d_attn_fwd: y, sk and sv are required");
+  P3D_CHECK_ARG((flags & ~(unsigned)(P3D_FWD_SAVE_STATE | P3D_FWD_FORCE_INDEXED | P3D_FWD_SUMMARIES_GIVEN |
+                                     P3D_FWD_Y_ROWS)) == 0u,
+                "p3d_attn_fwd: unknown flags 0x%x", flags);
   const bool save = flags & P3D_FWD_SAVE_STATE;
   P3D_CHECK_ARG(!save || (ol && og && lse_l && lse_g), "p3d_attn_fwd: saving state needs ol, og, lse_l, lse_g");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -392,9 +395,11 @@ int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, 
     a.og = save ? og : nullptr;
     a.lse_l = save ? lse_l : nullptr;
     a.lse_g = save ? lse_g : nullptr;
+    a.y_rows = (flags & P3D_FWD_Y_ROWS) != 0;
     return launch_stencil_fwd(a, s);
   }
-  const IndexedArgs a = indexed_args(op, sk, sv);
+  IndexedArgs a = indexed_args(op, sk, sv);
+  a.y_rows = (flags & P3D_FWD_Y_ROWS) != 0;
   void *ol_buf = save ? ol : ol_ws;
   if (int st = launch_local_fwd_indexed(a, ol_buf, save ? lse_l : nullptr, s)) return st;
   return launch_global_fwd_mix(a, ol_buf, y, save ? og : nullptr, save ? lse_g : nullptr, s);
@@ -406,7 +411,7 @@ int p3d_attn_fwd_slab(const p3d_operator *op, const p3d_slab *slab, void *y, con
   P3D_CHECK_ARG(slab != nullptr && y && sk && sv, "p3d_attn_fwd_slab: slab, y, sk and sv are required");
   const bool save = flags & P3D_FWD_SAVE_STATE;
   P3D_CHECK_ARG(!save || (ol && og && lse_l && lse_g), "p3d_attn_fwd_slab: saving state needs ol, og, lse_l, lse_g");
-  P3D_CHECK_ARG((flags & ~(unsigned)(P3D_FWD_SAVE_STATE | P3D_FWD_SUMMARIES_GIVEN)) == 0u,
+  P3D_CHECK_ARG((flags & ~(unsigned)(P3D_FWD_SAVE_STATE | P3D_FWD_SUMMARIES_GIVEN | P3D_FWD_Y_ROWS)) == 0u,
                 "p3d_attn_fwd_slab: unsupported flags 0x%x", flags);
   P3D_CHECK_ARG(op->stencil && !op->raster_to_packed,
                 "p3d_attn_fwd_slab: needs a complete stencil in raster storage");
@@ -451,6 +456,7 @@ int p3d_attn_fwd_slab(const p3d_operator *op, const p3d_slab *slab, void *y, con
   a.og = save ? og : nullptr;
   a.lse_l = save ? lse_l : nullptr;
   a.lse_g = save ? lse_g : nullptr;
+  a.y_rows = (flags & P3D_FWD_Y_ROWS) != 0;
   return launch_stencil_fwd(a, static_cast<cudaStream_t>(stream));
 }
 

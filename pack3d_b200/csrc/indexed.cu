@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(kWarps * 32)
       const float local = to_f32<T>(ol[qoff + ch]);
       // y = sl * ol + (gate * sg) * og, each product rounded as in the reference
       const float v = __fadd_rn(__fmul_rn(a.sl[ch], local), __fmul_rn(__fmul_rn(gate, a.sg[ch]), o));
-      y[qoff + ch] = from_f32<T>(v);
+      y[(a.y_rows ? ((int64_t)r.b * a.tokens + r.i) * a.heads + r.h : r.row) * d + ch] = from_f32<T>(v);
       if (og) og[qoff + ch] = from_f32<T>(o);
     }
   }

@@ -44,6 +44,7 @@ struct IndexedArgs {
   int reverse_width;
   const void *gate;
   const float *sl, *sg;
+  int y_rows;  // global/mix forward: y token-major [B,N,H,D]
 };
 
 // Local branch forward: ol [B,H,N,D] dtype, lse_l [B,H,N] fp32 (nullable; +inf for all-masked rows).
@@ -102,6 +103,7 @@ struct StencilFwdArgs {
   const float *sl, *sg;
   void *y, *ol, *og;                  // ol/og nullable
   float *lse_l, *lse_g;               // nullable
+  int y_rows;                         // y token-major [B,N,H,D]
 };
 // Read-and-clear the device failure bits of the tensor-core kernel files (OR-ed into *flags).
 int take_fwd_errors(unsigned *flags);

@@ -1,0 +1,245 @@
+// Layer glue of the PACK3D attention layer on the inference path (attention.py:53-89):
+//
+//   p3d_layer_norm  LayerNorm over the channel dimension (nn.LayerNorm, attention.py:64):
+//                   one warp per token row, fp32 mean / variance, 16-byte accesses.
+//   p3d_qkv_split   the projection split of attention.py:70-81 in one pass: reads the
+//                   row-major to_q / to_kv outputs [B, N, H*D] and [B, N, 4*G*D] (to_kv's
+//                   channel blocks are kl, vl, kg, vg) and writes the five head-major
+//                   tensors [B, H|G, N, D]; q, kl and kg are rotated by the axial RoPE
+//                   phase table exactly as p3d_rope does (rotary.py:11-45), vl and vg
+//                   copied.  Replaces three rotations and two strided copies.
+// Both are HBM bound: one read and one write of every byte.
+#include "common.cuh"
+
+namespace p3d {
+namespace {
+
+constexpr int kWarps = 8;
+
+template <typename T>
+__device__ __forceinline__ void load8(const T *src, float (&v)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4 *>(src);
+  const T *e = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = to_f32<T>(e[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T *dst, const float (&v)[8]) {
+  uint4 raw;
+  T *e = reinterpret_cast<T *>(&raw);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) e[i] = from_f32<T>(v[i]);
+  *reinterpret_cast<uint4 *>(dst) = raw;
+}
+
+// ---------------------------------------------------------------------------- LayerNorm
+template <typename T, int kChunks>
+__global__ void __launch_bounds__(kWarps * 32)
+    layer_norm_kernel(const T *x, const T *weight, const T *bias, T *y, int64_t rows, int dim, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T *xr = x + row * dim;
+  float v[kChunks][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) {
+    const int c = (lane + 32 * k) * 8;
+    if (c < dim) {
+      load8<T>(xr + c, v[k]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum += v[k][i];
+    }
+  }
+  const float mean = warp_sum(sum) / (float)dim;
+  float sq = 0.f;
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) {
+    const int c = (lane + 32 * k) * 8;
+    if (c < dim) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[k][i] - mean;
+        sq += d * d;
+      }
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(sq) / (float)dim + eps);
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) {
+    const int c = (lane + 32 * k) * 8;
+    if (c < dim) {
+      float w[8], b[8], o[8];
+      load8<T>(weight + c, w);
+      load8<T>(bias + c, b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = (v[k][i] - mean) * rstd * w[i] + b[i];
+      store8<T>(y + row * dim + c, o);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------- projection split
+struct SplitParams {
+  const void *qp, *kvp;
+  void *out[5];  // q, kl, vl, kg, vg
+  int batch, heads, kv_heads, tokens;
+  const int64_t *coords;  // [N, 3]
+  int pairs[3];
+  int start[3];           // first phase-table entry of each axis
+  const float *phases;    // (cos, sin) per (axis, coordinate, pair)
+};
+
+constexpr int kTokensPerWarp = 4;
+
+// Rotate the 4 pairs (8 channels) starting at pair `pair0` of a head by the token's phases.
+__device__ __forceinline__ void rotate8(float (&v)[8], int pair0, const SplitParams &p, const int64_t (&c)[3]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int pair = pair0 + j;
+    int axis = 0, local = pair;
+    if (local >= p.pairs[0]) {
+      local -= p.pairs[0];
+      axis = 1;
+      if (local >= p.pairs[1]) {
+        local -= p.pairs[1];
+        axis = 2;
+      }
+    }
+    const int64_t entry = p.start[axis] + c[axis] * p.pairs[axis] + local;
+    const float2 cs = *reinterpret_cast<const float2 *>(p.phases + 2 * entry);
+    const float even = v[2 * j], odd = v[2 * j + 1];
+    // each product rounded separately, as the reference's elementwise torch arithmetic
+    v[2 * j] = __fsub_rn(__fmul_rn(even, cs.x), __fmul_rn(odd, cs.y));
+    v[2 * j + 1] = __fadd_rn(__fmul_rn(even, cs.y), __fmul_rn(odd, cs.x));
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kWarps * 32) qkv_split_kernel(SplitParams p) {
+  constexpr int kGroups = D / 8;  // 16-byte chunks per head row
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+  const int n_begin = (blockIdx.x * kWarps + (threadIdx.x >> 5)) * kTokensPerWarp;
+  const int qw = p.heads * kGroups, kvw = 4 * p.kv_heads * kGroups;  // chunks per row
+  for (int t = 0; t < kTokensPerWarp; ++t) {
+    const int n = n_begin + t;
+    if (n >= p.tokens) return;
+    const int64_t c[3] = {p.coords[3 * (int64_t)n], p.coords[3 * (int64_t)n + 1], p.coords[3 * (int64_t)n + 2]};
+    const T *qrow = static_cast<const T *>(p.qp) + ((int64_t)b * p.tokens + n) * (qw * 8);
+    const T *kvrow = static_cast<const T *>(p.kvp) + ((int64_t)b * p.tokens + n) * (kvw * 8);
+    for (int k = lane; k < qw; k += 32) {
+      const int h = k / kGroups, grp = k % kGroups;
+      float v[8];
+      load8<T>(qrow + 8 * k, v);
+      rotate8(v, 4 * grp, p, c);
+      store8<T>(static_cast<T *>(p.out[0]) + (((int64_t)b * p.heads + h) * p.tokens + n) * D + 8 * grp, v);
+    }
+    for (int k = lane; k < kvw; k += 32) {
+      const int part = k / (p.kv_heads * kGroups);   // 0 kl, 1 vl, 2 kg, 3 vg
+      const int rest = k - part * p.kv_heads * kGroups;
+      const int g = rest / kGroups, grp = rest % kGroups;
+      float v[8];
+      load8<T>(kvrow + 8 * k, v);
+      if (part == 0 || part == 2) rotate8(v, 4 * grp, p, c);
+      store8<T>(static_cast<T *>(p.out[1 + part]) + (((int64_t)b * p.kv_heads + g) * p.tokens + n) * D + 8 * grp, v);
+    }
+  }
+}
+
+template <typename T>
+int launch_split(const SplitParams &p, int head_dim, cudaStream_t s) {
+  const dim3 grid((unsigned)((p.tokens + kWarps * kTokensPerWarp - 1) / (kWarps * kTokensPerWarp)),
+                  (unsigned)p.batch);
+  switch (head_dim) {
+    case 16: qkv_split_kernel<T, 16><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 32: qkv_split_kernel<T, 32><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 48: qkv_split_kernel<T, 48><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 64: qkv_split_kernel<T, 64><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 128: qkv_split_kernel<T, 128><<<grid, kWarps * 32, 0, s>>>(p); break;
+    default: return fail(P3D_ERR_UNSUPPORTED, "p3d_qkv_split: head_dim %d", head_dim);
+  }
+  P3D_LAUNCH_CHECK();
+  return P3D_OK;
+}
+
+template <typename T>
+int launch_ln(const void *x, const void *w, const void *b, void *y, int64_t rows, int dim, float eps,
+              cudaStream_t s) {
+  const unsigned blocks = (unsigned)((rows + kWarps - 1) / kWarps);
+  const int chunks = (dim / 8 + 31) / 32;
+  auto args = [&](auto kernel) {
+    kernel<<<blocks, kWarps * 32, 0, s>>>(static_cast<const T *>(x), static_cast<const T *>(w),
+                                          static_cast<const T *>(b), static_cast<T *>(y), rows, dim, eps);
+  };
+  switch (chunks) {
+    case 1: args(layer_norm_kernel<T, 1>); break;
+    case 2: args(layer_norm_kernel<T, 2>); break;
+    case 3: args(layer_norm_kernel<T, 3>); break;
+    case 4: args(layer_norm_kernel<T, 4>); break;
+    default: return fail(P3D_ERR_UNSUPPORTED, "p3d_layer_norm: dim %d above 1024", dim);
+  }
+  P3D_LAUNCH_CHECK();
+  return P3D_OK;
+}
+
+bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace
+}  // namespace p3d
+
+using namespace p3d;
+
+extern "C" int p3d_layer_norm(const void *x, const void *weight, const void *bias, void *y, int dtype, int64_t rows,
+                              int dim, float eps, void *stream) {
+  P3D_CHECK_ARG(dtype == P3D_BF16 || dtype == P3D_F16, "p3d_layer_norm: bf16 or f16 only");
+  P3D_CHECK_ARG(x && weight && bias && y, "p3d_layer_norm: null pointer");
+  P3D_CHECK_ARG(rows >= 0 && dim >= 8 && dim % 8 == 0, "p3d_layer_norm: dim must be a positive multiple of 8");
+  P3D_CHECK_ARG(aligned16(x) && aligned16(weight) && aligned16(bias) && aligned16(y),
+                "p3d_layer_norm: 16-byte aligned tensors required");
+  P3D_CHECK_ARG(eps >= 0.f, "p3d_layer_norm: negative eps");
+  if (rows == 0) return P3D_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return dtype == P3D_BF16 ? launch_ln<__nv_bfloat16>(x, weight, bias, y, rows, dim, eps, s)
+                           : launch_ln<__half>(x, weight, bias, y, rows, dim, eps, s);
+}
+
+extern "C" int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl, void *vl, void *kg, void *vg,
+                             int dtype, int batch, int heads, int kv_heads, int tokens, int head_dim,
+                             const int64_t *coords, int pz, int py, int px, const float *phases, int ez, int ey,
+                             int ex, void *stream) {
+  P3D_CHECK_ARG(dtype == P3D_BF16 || dtype == P3D_F16, "p3d_qkv_split: bf16 or f16 only");
+  P3D_CHECK_ARG(qp && kvp && q && kl && vl && kg && vg && coords && phases, "p3d_qkv_split: null pointer");
+  P3D_CHECK_ARG(batch >= 0 && heads >= 1 && kv_heads >= 1 && heads % kv_heads == 0 && tokens >= 0,
+                "p3d_qkv_split: bad batch / head / token counts");
+  P3D_CHECK_ARG(head_dim % 8 == 0 && 2 * (pz + py + px) == head_dim && pz >= 0 && py >= 0 && px >= 0,
+                "p3d_qkv_split: pairs (%d,%d,%d) do not allocate head_dim %d", pz, py, px, head_dim);
+  P3D_CHECK_ARG(ez >= 1 && ey >= 1 && ex >= 1, "p3d_qkv_split: bad table extents");
+  const void *ptrs[7] = {qp, kvp, q, kl, vl, kg, vg};
+  for (const void *t : ptrs) P3D_CHECK_ARG(aligned16(t), "p3d_qkv_split: 16-byte aligned tensors required");
+  if ((int64_t)batch * tokens == 0) return P3D_OK;
+  P3D_CHECK_ARG(batch <= 65535, "p3d_qkv_split: batch above 65535");
+  SplitParams p{};
+  p.qp = qp;
+  p.kvp = kvp;
+  p.out[0] = q;
+  p.out[1] = kl;
+  p.out[2] = vl;
+  p.out[3] = kg;
+  p.out[4] = vg;
+  p.batch = batch;
+  p.heads = heads;
+  p.kv_heads = kv_heads;
+  p.tokens = tokens;
+  p.coords = coords;
+  p.pairs[0] = pz;
+  p.pairs[1] = py;
+  p.pairs[2] = px;
+  p.start[0] = 0;
+  p.start[1] = ez * pz;
+  p.start[2] = ez * pz + ey * py;
+  p.phases = phases;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return dtype == P3D_BF16 ? launch_split<__nv_bfloat16>(p, head_dim, s) : launch_split<__half>(p, head_dim, s);
+}

@@ -115,6 +115,7 @@ struct FwdParams {
   const int32_t *map;  // raster -> packed rows (nullptr: raster storage)
   void *y, *ol, *og;
   float *lse_l, *lse_g;
+  int y_rows;  // y is [B, N, H, D] (token-major) instead of [B, H, N, D]
 };
 
 template <bool BF16>
@@ -537,7 +538,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           packed_y[i] = pack2<BF16>(y0v, y1v);
           packed_g[i] = pack2<BF16>(g0, g1);
         }
-        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.y) + grow * D);
+        const int64_t yrow = p.y_rows ? ((int64_t)b * p.tokens + rr) * p.heads + h : grow;
+        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.y) + yrow * D);
 #pragma unroll
         for (int v = 0; v < D / 8; ++v)
           dst[v] = make_uint4(packed_y[4 * v], packed_y[4 * v + 1], packed_y[4 * v + 2], packed_y[4 * v + 3]);
@@ -622,6 +624,7 @@ int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
   p.og = a.og;
   p.lse_l = a.lse_l;
   p.lse_g = a.lse_g;
+  p.y_rows = a.y_rows;
   const int64_t units = (int64_t)bh * p.tiles_z * p.tiles_y * p.tiles_x;
   if (units <= 0) return P3D_OK;
   if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");

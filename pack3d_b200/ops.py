@@ -71,10 +71,12 @@ def _as_gate(gate, q):
 
 
 def forward(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature, *, save_state=True,
-            force_indexed=False, summaries=None):
+            force_indexed=False, summaries=None, y_rows=False):
     """Launch the forward; returns ``(y, (sk, sv, ol, og, lse_l, lse_g))`` (empty state when not saving).
 
     ``summaries=(sk, sv)`` supplies already pooled summaries and runs stage (c) alone.
+    ``y_rows`` writes y token-major: the result is a [B, H, N, D] view of a [B, N, H, D]
+    tensor, so ``y.transpose(1, 2).reshape(B, N, H * D)`` needs no copy.
     """
     b, h, n, d = q.shape
     g = kl.shape[1]
@@ -83,8 +85,9 @@ def forward(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature
     op, keep = _operator(q, kl, vl, kg, vg, w32, b32, gate, sl32, sg32, geometry, temperature)
     m = geometry.num_summaries
     empty = lambda *shape, dtype=q.dtype: torch.empty(shape, dtype=dtype, device=q.device)  # noqa: E731
-    y = empty(b, h, n, d)
+    y = empty(b, n, h, d).permute(0, 2, 1, 3) if y_rows else empty(b, h, n, d)
     flags = (_native.FWD_SAVE_STATE if save_state else 0) | (_native.FWD_FORCE_INDEXED if force_indexed else 0)
+    flags |= _native.FWD_Y_ROWS if y_rows else 0
     if summaries is None:
         sk, sv = empty(b, g, m, d), empty(b, g, m, d)
     else:

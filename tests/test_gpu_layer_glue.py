@@ -1,0 +1,92 @@
+"""The fused layer glue of the inference path: p3d_qkv_split, p3d_layer_norm, token-major y."""
+import pytest
+import torch
+
+from pack3d_b200 import PACK3DAttention, _native, build_layout
+from pack3d_b200 import ops as p3d_ops
+from pack3d_b200.rope import balanced_pairs, phase_tables, rotate_projections
+
+pytestmark = pytest.mark.gpu
+
+
+def _layout(grid, raster=True):
+    layout = build_layout(grid, (4, 4, 4), radius=2, pool_size=1)
+    return layout.repack(layout.order.argsort()) if raster else layout
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("h,g,d", [(4, 4, 48), (4, 2, 32), (2, 1, 16), (2, 2, 64)])
+def test_qkv_split_matches_rotation_and_copies(cuda_device, dtype, h, g, d):
+    layout = _layout((8, 12, 16), raster=False).to(cuda_device)
+    b, n = 2, layout.geometry.num_tokens
+    gen = torch.Generator(device=cuda_device).manual_seed(h + g + d)
+    qp = torch.randn(b, n, h * d, device=cuda_device, generator=gen).to(dtype)
+    kvp = torch.randn(b, n, 4 * g * d, device=cuda_device, generator=gen).to(dtype)
+    pairs = balanced_pairs(d)
+    extents = layout.grid_shape
+    _, phases = phase_tables(cuda_device, pairs, extents)
+    outs = [torch.empty((b, h, n, d), dtype=dtype, device=cuda_device)]
+    outs += [torch.empty((b, g, n, d), dtype=dtype, device=cuda_device) for _ in range(4)]
+    coords = layout.coords.contiguous()
+    with torch.cuda.device(cuda_device):
+        _native.check(_native.lib().p3d_qkv_split(
+            _native.ptr(qp), _native.ptr(kvp), *[_native.ptr(t) for t in outs], _native.DTYPE_CODE[dtype], b, h, g, n,
+            d, _native.ptr(coords), *pairs, _native.ptr(phases), *extents, _native.stream_of(cuda_device)),
+            "p3d_qkv_split")
+    q, kl, vl, kg, vg = outs
+    chunks = [t.reshape(b, n, g, d).transpose(1, 2) for t in kvp.chunk(4, -1)]
+    wq, wkl, wkg = rotate_projections(qp.reshape(b, n, h, d).transpose(1, 2), chunks[0], chunks[2], layout.coords,
+                                      pairs, extents, packed=False)
+    assert torch.equal(q, wq) and torch.equal(kl, wkl) and torch.equal(kg, wkg)
+    assert torch.equal(vl, chunks[1].contiguous()) and torch.equal(vg, chunks[3].contiguous())
+
+
+@pytest.mark.parametrize("dim", [192, 384, 64])
+def test_layer_norm_matches_torch(cuda_device, dim):
+    gen = torch.Generator(device=cuda_device).manual_seed(dim)
+    x = (torch.randn(3, 1000, dim, device=cuda_device, generator=gen) * 3 + 1).to(torch.bfloat16)
+    norm = torch.nn.LayerNorm(dim).to(cuda_device, torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.normal_()
+        norm.bias.normal_()
+    y = torch.empty_like(x)
+    with torch.cuda.device(cuda_device):
+        _native.check(_native.lib().p3d_layer_norm(_native.ptr(x), _native.ptr(norm.weight), _native.ptr(norm.bias),
+                                                   _native.ptr(y), _native.BF16, 3000, dim, 1e-5,
+                                                   _native.stream_of(cuda_device)), "p3d_layer_norm")
+    want = norm(x)
+    err = (y.float() - want.float()).abs()
+    # one bf16 step of the larger magnitude at most
+    assert (err <= 2.0 ** -7 * torch.maximum(y.float().abs(), want.float().abs()) + 1e-3).all()
+
+
+@pytest.mark.parametrize("raster", [True, False])
+def test_token_major_output_matches(cuda_device, raster):
+    import oracle
+    from cases import grid_inputs
+    layout = _layout((8, 8, 16), raster)
+    n = layout.geometry.num_tokens
+    raw = grid_inputs(n, 2, 4, 4, 48, torch.float32, 4, True)
+    rot = [oracle.axial_rope(raw[i], layout.coords) if i in (0, 1, 3) else raw[i] for i in range(5)]
+    inputs = [t.to(torch.bfloat16).to(cuda_device) for t in rot] + [t.to(cuda_device) for t in raw[5:]]
+    geom = layout.geometry.to(cuda_device)
+    for force_indexed in (False, True):
+        y, _ = p3d_ops.forward(*inputs, geom, 1.0, save_state=False, force_indexed=force_indexed)
+        y_rows, _ = p3d_ops.forward(*inputs, geom, 1.0, save_state=False, force_indexed=force_indexed, y_rows=True)
+        assert y_rows.shape == y.shape and y_rows.transpose(1, 2).is_contiguous()
+        assert torch.equal(y_rows, y)
+
+
+def test_fast_inference_layer_matches_the_autograd_path(cuda_device):
+    layout = _layout((16, 16, 16)).to(cuda_device)
+    torch.manual_seed(0)
+    layer = PACK3DAttention(192, heads=4, kv_heads=4, head_dim=48, block_volume=64).to(cuda_device, torch.bfloat16)
+    x = torch.randn(2, layout.geometry.num_tokens, 192, device=cuda_device).to(torch.bfloat16)
+    with torch.no_grad():
+        fast = layer(x, layout)
+    slow = layer(x.clone().requires_grad_(), layout)
+    with torch.no_grad():
+        assert layer._fast_inference(x)
+    assert not layer._fast_inference(x.clone().requires_grad_())
+    assert (fast.float() - slow.detach().float()).abs().max().item() <= 2e-2 * max(1.0, slow.abs().max().item())
+    assert _native.device_errors() == 0
