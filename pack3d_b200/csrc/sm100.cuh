@@ -56,6 +56,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may suspend the thread for up to `hint_ns` (it resumes as soon as the phase
+// completes): a waiting warp then takes no issue slots from the warps that do the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Non-blocking test of a phase: cheaper than try_wait when the phase has already completed.
 __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -84,7 +98,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t_last = global_timer_ns(), waited_ns = 0;
   long long c_last = clock64(), waited_cycles = 0;
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
     const uint64_t t = global_timer_ns();
     const long long c = clock64();
     const long long dt = (long long)(t - t_last), dc = c - c_last;

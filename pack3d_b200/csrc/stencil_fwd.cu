@@ -4,22 +4,20 @@
 // kernels.py:44-103) for a complete radius-2 voxel stencil in bf16 / f16:
 //   y = sl * softmax_local(q kl^T / sqrt(D)) vl + (gate * sg) * softmax_global(q sk^T / sqrt(D)) sv
 //
-// Work unit (one CTA): one (batch, head) and an 8x4x8 (z, y, x) box of queries,
-// split into two 128-row query tiles A (z 0..3) and B (z 4..7).  Rows are ordered
-// (z, y, x), so softmax warp w of a tile owns query plane z = w and TMEM lanes
-// 32w..32w+31.
+// Work unit (one CTA): one (batch, head) and a 4x4x8 (z, y, x) tile of 128 queries.
+// Rows are ordered (z, y, x), so softmax warp w owns query plane z = w and TMEM lanes
+// 32w..32w+31.  Two CTAs share an SM (each owns 256 TMEM columns and its own MMA issuer:
+// an issuing thread blocks ~60 cycles per tcgen05.mma and ~140 per commit, so two issuers
+// per SM double the rate at which the tensor pipe is fed).
 //
-// Chunk sequence of each tile (one shared smem ring, both tiles in step), 96 keys each:
+// Chunk sequence, 96 keys each:
 //   chunks 0..7   local: halo plane z-2+c of the tile, its 8x12 (y, x) window.  A key
 //                 is used iff it lies in the query's 5x5x5 cube and in the volume
 //                 (coordinate test, no neighbour table).  A warp whose query plane is
 //                 more than 2 planes away writes a zero P block.
 //   chunks 8..    global: 96 summaries per chunk.
-// TMEM per tile (256 columns): two 96-column S buffers and one accumulator O.  The QK^T
-// MMA of chunk c+2 and the PV MMA of chunk c run while the softmax warps work on chunk
-// c+1, so the MMA thread is off the softmax critical path.  (On sm_100 an M=128, K=16
-// MMA takes >= ~46 cycles whatever N <= 64 is and ~56 at N=96, and every commit costs
-// about two MMAs: with head_dim 48 a chunk is long enough that it must overlap.)  O
+// TMEM (256 columns): two 96-column S buffers and one accumulator O.  The QK^T MMA of
+// chunk c+2 and the PV MMA of chunk c run while the softmax warps work on chunk c+1.  O
 // holds the local accumulator during chunks 0..7; when they are done the normalised
 // local output is parked in shared memory, rounded to the storage dtype as the
 // reference rounds it before the mix, and O then accumulates the global branch.
@@ -28,11 +26,11 @@
 // global branch, mixes and writes y (and optionally ol, og, lse_l, lse_g) through the
 // raster->packed row map.
 //
-// Roles: warps 0-3 softmax tile A, warps 4-7 softmax tile B, warp 8 TMA producer,
-// warp 9 MMA issuer (one thread).  Operands live in shared memory in the
-// SWIZZLE_32B layout: Q / K are K-major boxes of 16 channels, V is the same bytes
-// read MN-major; P goes back into its S buffer in TMEM as bf16/f16 pairs and feeds
-// the PV MMA as the TMEM A operand.  Every mbarrier wait is bounded.
+// Roles: warps 0-3 softmax, warp 4 TMA producer, warp 5 MMA issuer (one thread).
+// Operands live in shared memory in the SWIZZLE_32B layout: Q / K are K-major boxes of
+// 16 channels, V is the same bytes read MN-major; P goes back into its S buffer in TMEM
+// as bf16/f16 pairs and feeds the PV MMA as the TMEM A operand.  Every mbarrier wait is
+// bounded.
 #include <algorithm>
 
 #include "common.cuh"
@@ -53,9 +51,9 @@ constexpr int kKeys = kHY * kHX;                    // 96 keys per chunk (a halo
 constexpr int kLocalChunks = kHZ;                   // 8 halo planes per tile
 constexpr int kSumRows = kKeys;                     // summaries per global chunk
 constexpr int kRows = 128;                          // queries per tile
-constexpr int kThreads = 320;
-constexpr int kProducerWarp = 8, kMmaWarp = 9;
-constexpr uint32_t kTmemCols = 512;
+constexpr int kThreads = 192;
+constexpr int kProducerWarp = 4, kMmaWarp = 5;
+constexpr uint32_t kTmemCols = 256;                 // two CTAs per SM
 constexpr float kNegInf = -__builtin_huge_valf();
 constexpr uint64_t kWaitNs = 2000000000ull;        // every mbarrier wait gives up after 2 s
 
@@ -66,39 +64,40 @@ struct Cfg {
   static constexpr int kK = D / 16;                 // 16-channel boxes per row
   static constexpr int kBoxQ = kRows * 32;          // one box = rows x 32 bytes
   static constexpr int kBoxK = kKeys * 32;          // 3072
-  static constexpr int kQBytes = kK * kBoxQ;        // one query tile
+  static constexpr int kQBytes = kK * kBoxQ;        // the query tile
   static constexpr int kKeyBytes = kK * kBoxK;      // one chunk of K (or V)
-  static constexpr int kStageBytes = (4 * kKeyBytes + 1023) / 1024 * 1024;  // local: K_A K_B V_A V_B
-  static constexpr int kOlBytes = kRows * D * 2;    // parked local output of one tile
-  static constexpr int kFixed = 2 * kQBytes + 2 * kOlBytes + 1024;
+  static constexpr int kStageBytes = (2 * kKeyBytes + 1023) / 1024 * 1024;  // K, V
+  static constexpr int kOlBytes = kRows * D * 2;    // parked local output
+  static constexpr int kFixed = kQBytes + kOlBytes + 1024;
+  // Two CTAs per SM: at most 113 KB each; and more than a third of the SM's 228 KB, so
+  // that a third CTA (whose TMEM allocation would have to wait) never lands on an SM.
+  static constexpr int kMaxSmem = 113 * 1024, kMinSmem = 78 * 1024;
   // 3 or 4 stages: at least chunks c .. c+2 resident (S of chunk c+2 is issued while PV of
   // chunk c may still read its stage); at most 4, the size of the per-stage barrier arrays.
-  static constexpr int kStages = (227 * 1024 - 2048 - kFixed) / kStageBytes > 4 ? 4
-                                                                                 : (227 * 1024 - 2048 - kFixed) / kStageBytes;
-  // at least 116 KB so that one CTA (which owns all 512 TMEM columns) fits per SM
+  static constexpr int kRoom = (kMaxSmem - kFixed) / kStageBytes;
+  static constexpr int kStages = kRoom > 4 ? 4 : kRoom;
   static constexpr int kSmemNeed = kFixed + kStages * kStageBytes;
-  static constexpr int kSmemBytes = kSmemNeed > 116 * 1024 ? kSmemNeed : 116 * 1024;
+  static constexpr int kSmemBytes = kSmemNeed > kMinSmem ? kSmemNeed : kMinSmem;
   static_assert(kStages >= 3 && kStages <= 4, "the ring must hold chunks c .. c+2");
-  static_assert(kSmemBytes <= 225 * 1024, "shared memory budget");
+  static_assert(kSmemBytes <= kMaxSmem, "shared memory budget");
 };
 
-// TMEM columns of tile t (base t*256): S buffers [0, 96) and [96, 192), O [192, 192 + D).
+// TMEM columns: S buffers [0, 96) and [96, 192), O [192, 192 + D).
 constexpr uint32_t kSBuf = 96, kColO = 192;
 
-// S_t(c) is complete when its commit arrives.  Tile A commits to kSReady[0][c%2]; tile B
-// commits S_B(0), S_B(1) to kSReady[1][c] and S_B(c), c >= 2, to kEmpty[(c-2) % kStages]:
-// S_B(c) is issued after PV_B(c-2) has completed (and every MMA before it), so its
-// completion is also the moment chunk c-2's ring stage is free.  One release barrier per
-// stage keeps every parity wait unambiguous (see the producer).
+// S(c) is complete when its commit arrives: S(0), S(1) commit to kSReady[c], and S(c),
+// c >= 2, to kEmpty[(c-2) % kStages]: S(c) is issued after PV(c-2) has completed (and every
+// MMA before it), so its completion is also the moment chunk c-2's ring stage is free.
+// One release barrier per stage keeps every parity wait unambiguous (see the producer).
 enum Bar {
   kQFull = 0,
   kFull = 1,                  // [stage]
-  kSReady = kFull + 4,        // [tile][buf] (tile B: chunks 0 and 1 only)
-  kEmpty = kSReady + 4,       // [stage]: released by S_B(c + 2), c the chunk it held
-  kPReady = kEmpty + 4,       // [tile][buf]
-  kPvDone = kPReady + 4,      // [tile][buf]: PV of the chunk that last used the buffer is done
-  kOReady = kPvDone + 4,      // [tile]
-  kDrain = kOReady + 2,       // MMA thread: every MMA it issued has completed
+  kSReady = kFull + 4,        // [buf] (chunks 0 and 1)
+  kEmpty = kSReady + 2,       // [stage]: released by S(c + 2), c the chunk it held
+  kPReady = kEmpty + 4,       // [buf] (count 4: the softmax warps stored P)
+  kPvDone = kPReady + 2,      // [buf]: PV of the chunk that last used the buffer is done
+  kOReady = kPvDone + 2,
+  kDrain = kOReady + 1,       // MMA thread: every MMA it issued has completed
   kNumBars = kDrain + 1
 };
 
@@ -202,7 +201,7 @@ __device__ __forceinline__ float row_max(const float *s) {
 }
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     stencil_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkl,
                        const __grid_constant__ CUtensorMap tvl, const __grid_constant__ CUtensorMap tsk,
                        const __grid_constant__ CUtensorMap tsv, const FwdParams p) {
@@ -221,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   unit /= p.tiles_y;
   const int tz = unit % p.tiles_z;
   const int bh = unit / p.tiles_z;
-  const int x0 = tx * kTX, y0 = ty * kTY, z0 = tz * 2 * kTZ;
+  const int x0 = tx * kTX, y0 = ty * kTY, z0 = tz * kTZ;
   const int b = bh / p.heads, h = bh % p.heads;
   const int bg = b * p.kv_heads + h / (p.heads / p.kv_heads);
   const int n_chunks = kLocalChunks + p.global_chunks;
@@ -229,9 +228,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- shared memory carve-up (1024-byte aligned)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
-  const uint32_t q_smem = base;                        // tile A, then tile B
-  const uint32_t ring = base + 2 * C::kQBytes;
-  uint8_t *ol_park = smem_raw + (base - raw) + 2 * C::kQBytes + C::kStages * C::kStageBytes;  // [tile][row][D]
+  const uint32_t q_smem = base;
+  const uint32_t ring = base + C::kQBytes;
+  uint8_t *ol_park = smem_raw + (base - raw) + C::kQBytes + C::kStages * C::kStageBytes;  // [row][D]
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
 
   if (tid == 0) {
@@ -240,12 +239,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kFull + s), 1);
       mbar_init(bar(kEmpty + s), 1);
     }
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(bar(kSReady + i), 1);
       mbar_init(bar(kPReady + i), 4);
       mbar_init(bar(kPvDone + i), 1);
     }
-    for (int t = 0; t < 2; ++t) mbar_init(bar(kOReady + t), 1);
+    mbar_init(bar(kOReady), 1);
     mbar_init(bar(kDrain), 1);
     fence_mbar_init();
   }
@@ -272,37 +271,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      mbar_expect_tx(bar(kQFull), 2 * C::kQBytes);
-      for (int t = 0; t < 2; ++t)
-        for (int c = 0; c < C::kK; ++c)
-          tma_load_5d(q_smem + t * C::kQBytes + c * C::kBoxQ, &tq, bar(kQFull), 16 * c, x0, y0, z0 + kTZ * t, bh);
+      mbar_expect_tx(bar(kQFull), C::kQBytes);
+      for (int c = 0; c < C::kK; ++c)
+        tma_load_5d(q_smem + c * C::kBoxQ, &tq, bar(kQFull), 16 * c, x0, y0, z0, bh);
       int issued = 0;
       for (int ch = 0; ch < n_chunks; ++ch) {
         const int s = ch % C::kStages;
-        // Stage s last held chunk ch - kStages; kEmpty[s] completes once per release, so
-        // this is its completion number k = ch / kStages - 1.  A parity wait only tells
-        // completion k from its neighbours if both are ruled out: k - 1 was awaited here one
-        // ring turn ago (or k = 0 on a fresh barrier), and k + 1 is S_B(ch + 2), which needs
-        // chunk ch + 2, not loaded yet.  (Releasing through the two S-buffer barriers of tile
-        // B instead is ambiguous: their first waits can be one completion early or late.)
+        // kEmpty[s] completes once per use of stage s: this is completion ch/kStages - 1.
+        // A parity wait only tells it from its neighbours if both are ruled out: the one
+        // before was awaited here a ring turn ago (or this is the first), and the one
+        // after is S(ch + 2), which needs chunk ch + 2, not loaded yet.
         if (ch >= C::kStages &&
             !mbar_wait(bar(kEmpty + s), (ch / C::kStages - 1) & 1, &g_fwd_errors, kWaitNs, kErrProducer))
           break;
         const uint32_t stage = ring + s * C::kStageBytes;
         const uint32_t full = bar(kFull + s);
+        mbar_expect_tx(full, 2 * C::kKeyBytes);
         if (ch < kLocalChunks) {
-          mbar_expect_tx(full, 4 * C::kKeyBytes);
-          for (int t = 0; t < 2; ++t) {
-            const int z = p.qz0 + z0 + kTZ * t - kR + ch - p.kz0;  // plane in the K/V buffer
-            for (int c = 0; c < C::kK; ++c) {
-              tma_load_5d(stage + t * C::kKeyBytes + c * C::kBoxK, &tkl, full, 16 * c, x0 - kR, y0 - kR, z, bg);
-              tma_load_5d(stage + (2 + t) * C::kKeyBytes + c * C::kBoxK, &tvl, full, 16 * c, x0 - kR, y0 - kR, z,
-                          bg);
-            }
+          const int z = p.qz0 + z0 - kR + ch - p.kz0;  // plane in the K/V buffer
+          for (int c = 0; c < C::kK; ++c) {
+            tma_load_5d(stage + c * C::kBoxK, &tkl, full, 16 * c, x0 - kR, y0 - kR, z, bg);
+            tma_load_5d(stage + C::kKeyBytes + c * C::kBoxK, &tvl, full, 16 * c, x0 - kR, y0 - kR, z, bg);
           }
         } else {
           const int g = ch - kLocalChunks;
-          mbar_expect_tx(full, 2 * C::kKeyBytes);
           for (int c = 0; c < C::kK; ++c) {
             tma_load_3d(stage + c * C::kBoxK, &tsk, full, 16 * c, g * kSumRows, bg);
             tma_load_3d(stage + C::kKeyBytes + c * C::kBoxK, &tsv, full, 16 * c, g * kSumRows, bg);
@@ -311,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued = ch + 1;
       }
       // Never leave copies in flight into shared memory this CTA is about to give up: wait
-      // (bounded) for the Q tiles and the last loads of every stage.  On the normal path
+      // (bounded) for the Q tile and the last loads of every stage.  On the normal path
       // these phases completed long ago; after a timed-out wait they may still be landing.
       mbar_wait(bar(kQFull), 0, &g_fwd_errors, kWaitNs, kErrTeardown);
       for (int ch = issued > C::kStages ? issued - C::kStages : 0; ch < issued; ++ch)
@@ -326,33 +318,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       // arrive from a commit can land after the CTA has exited.
       uint32_t commits[kNumBars];
       for (int i = 0; i < kNumBars; ++i) commits[i] = 0u;
-      auto commit = [&](int b) {
-        mma_commit(bar(b));
-        ++commits[b];
+      auto commit = [&](int b_idx) {
+        mma_commit(bar(b_idx));
+        ++commits[b_idx];
       };
-      // S_t(ch) = Q_t K(ch)^T into S buffer ch%2, then signal the tile's softmax warps.
-      auto issue_s = [&](int t, int ch) {
-        const uint32_t stage = ring + (ch % C::kStages) * C::kStageBytes;
-        const uint32_t k_base = ch < kLocalChunks ? stage + t * C::kKeyBytes : stage;
-        const uint32_t q_t = q_smem + t * C::kQBytes;
-        const uint32_t t_s = tmem + t * 256 + (ch & 1) * kSBuf;
+      // Shared-memory descriptors are built once; an operand's descriptor is its base plus
+      // (byte offset >> 4), one add per MMA (addresses stay inside the 14-bit field).
+      const uint64_t desc_q = desc_sw32(q_smem, 16, 256);          // the Q tile, K-major
+      const uint64_t desc_k = desc_sw32(ring, 16, 256);            // K chunks in the ring, K-major
+      const uint64_t desc_v = desc_sw32(ring, C::kBoxK, 256);      // V chunks in the ring, MN-major
+      // S(ch) = Q K(ch)^T into S buffer ch%2, then signal the softmax warps.
+      auto issue_s = [&](int ch) {
+        const uint64_t bk = desc_k + ((uint32_t)((ch % C::kStages) * C::kStageBytes) >> 4);
+        const uint32_t t_s = tmem + (ch & 1) * kSBuf;
+#pragma unroll
         for (int c = 0; c < C::kK; ++c)
-          mma_ss(t_s, desc_sw32(q_t + c * C::kBoxQ, 16, 256), desc_sw32(k_base + c * C::kBoxK, 16, 256), idesc_s,
-                 c > 0 ? 1u : 0u);
-        commit(t == 1 && ch >= 2 ? kEmpty + (ch - 2) % C::kStages : kSReady + 2 * t + (ch & 1));
+          mma_ss(t_s, desc_q + c * (C::kBoxQ >> 4), bk + c * (C::kBoxK >> 4), idesc_s, c > 0 ? 1u : 0u);
+        commit(ch >= 2 ? kEmpty + (ch - 2) % C::kStages : kSReady + ch);
       };
-      // O_t += P_t(c) V(c) once the softmax warps have written P_t(c).
-      auto issue_pv = [&](int t, int c) -> bool {
-        if (!mbar_wait(bar(kPReady + 2 * t + (c & 1)), (c >> 1) & 1, &g_fwd_errors, kWaitNs, kErrMma)) return false;
+      // O += P(c) V(c) once the softmax warps have written P(c).
+      auto issue_pv = [&](int c) -> bool {
+        if (!mbar_wait(bar(kPReady + (c & 1)), (c >> 1) & 1, &g_fwd_errors, kWaitNs, kErrMma)) return false;
         tc_fence_after();
-        const uint32_t stage = ring + (c % C::kStages) * C::kStageBytes;
-        const uint32_t v_base = c < kLocalChunks ? stage + (2 + t) * C::kKeyBytes : stage + C::kKeyBytes;
-        const uint32_t t_p = tmem + t * 256 + (c & 1) * kSBuf;
+        const uint64_t bv = desc_v + ((uint32_t)((c % C::kStages) * C::kStageBytes + C::kKeyBytes) >> 4);
+        const uint32_t t_p = tmem + (c & 1) * kSBuf, t_o = tmem + kColO;
         const bool first = (c == 0) || (c == kLocalChunks);  // O restarts for the global branch
+#pragma unroll
         for (int j = 0; j < kKeys / 16; ++j)
-          mma_ts(tmem + t * 256 + kColO, t_p + 8 * j, desc_sw32(v_base + j * 512, C::kBoxK, 256), idesc_pv,
-                 (first && j == 0) ? 0u : 1u);
-        commit(kPvDone + 2 * t + (c & 1));
+          mma_ts(t_o, t_p + 8 * j, bv + j * (512 >> 4), idesc_pv, (first && j == 0) ? 0u : 1u);
+        commit(kPvDone + (c & 1));
         return true;
       };
       auto wait_full = [&](int ch) -> bool {
@@ -361,39 +355,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         return true;
       };
-      // S_t(c+2) writes the TMEM columns that PV_t(c) reads as its A operand (P_t(c)).
+      // S(c+2) writes the TMEM columns that PV(c) reads as its A operand (P(c)).
       // tcgen05.mma ops are only ordered among themselves when they share an accumulator,
-      // so PV_t(c) must have completed before S_t(c+2) is issued.
-      auto wait_pv = [&](int t, int c) -> bool {
-        if (!mbar_wait(bar(kPvDone + 2 * t + (c & 1)), (c >> 1) & 1, &g_fwd_errors, kWaitNs, kErrMma)) return false;
+      // so PV(c) must have completed before S(c+2) is issued.
+      auto wait_pv = [&](int c) -> bool {
+        if (!mbar_wait(bar(kPvDone + (c & 1)), (c >> 1) & 1, &g_fwd_errors, kWaitNs, kErrMma)) return false;
         tc_fence_after();
         return true;
       };
-      // Prologue: both S buffers of both tiles.  Steady state per chunk c:
-      //   PV_A(c), PV_B(c), [PV_A(c) done] S_A(c+2), [PV_B(c) done] S_B(c+2)
-      // Waiting for PV_A(c) while PV_B(c) still executes keeps the tensor pipe busy.
+      // Prologue: both S buffers.  Steady state per chunk c: PV(c), [PV(c) done] S(c+2).
       bool ok = mbar_wait(bar(kQFull), 0, &g_fwd_errors, kWaitNs, kErrMma);
       for (int ch = 0; ok && ch < 2; ++ch) {
         ok = wait_full(ch);
         if (!ok) break;
-        issue_s(0, ch);
-        issue_s(1, ch);
+        issue_s(ch);
       }
       for (int c = 0; ok && c < n_chunks; ++c) {
-        const bool more = c + 2 < n_chunks;
-        ok = issue_pv(0, c) && issue_pv(1, c);
-        if (!ok || !more) continue;
-        ok = wait_full(c + 2) && wait_pv(0, c);
+        ok = issue_pv(c);
+        if (!ok || c + 2 >= n_chunks) continue;
+        ok = wait_full(c + 2) && wait_pv(c);
         if (!ok) break;
-        issue_s(0, c + 2);
-        ok = wait_pv(1, c);
-        if (!ok) break;
-        issue_s(1, c + 2);  // its commit also releases chunk c's stage to the producer
+        issue_s(c + 2);  // its commit also releases chunk c's stage to the producer
       }
-      if (ok) {
-        commit(kOReady);
-        commit(kOReady + 1);
-      }
+      if (ok) commit(kOReady);
       // TMEM is freed after the final __syncthreads: make sure every MMA issued above has
       // completed, and every commit has arrived, first -- on the normal path and after a
       // timed-out wait alike.
@@ -403,15 +387,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    const int t = warp >> 2, w = warp & 3;
+    const int w = warp;
     const uint32_t lanes = (uint32_t)(w * 32) << 16;
-    const uint32_t t_tile = tmem + lanes + t * 256;
+    const uint32_t t_tile = tmem + lanes;
     const uint32_t t_o = t_tile + kColO;
     const int row = w * 32 + lane;
     const int qz = w, qy = lane >> 3, qx = lane & 7;
-    const int zq = z0 + kTZ * t + qz, yq = y0 + qy, xq = x0 + qx;
+    const int zq = z0 + qz, yq = y0 + qy, xq = x0 + qx;
     const bool row_ok = zq < p.Z && yq < p.Y && xq < p.X;
-    uint32_t *park = reinterpret_cast<uint32_t *>(ol_park + (size_t)(t * kRows + row) * D * 2);
+    uint32_t *park = reinterpret_cast<uint32_t *>(ol_park + (size_t)row * D * 2);
     // keys of the 8x12 halo window inside this query's cube and inside the volume
     uint32_t mask[3] = {0u, 0u, 0u};
 #pragma unroll
@@ -429,16 +413,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     // Bounded wait with a warp-uniform result: the warp reconverges and leaves together,
     // so the warp-collective TMEM loads and stores that follow run on the whole warp.
-    auto wait_warp = [&](uint32_t b, uint32_t parity) -> bool {
-      const bool r = mbar_wait(b, parity, &g_fwd_errors, kWaitNs, kErrSoftmax);
+    auto wait_warp = [&](uint32_t b_addr, uint32_t parity) -> bool {
+      const bool r = mbar_wait(b_addr, parity, &g_fwd_errors, kWaitNs, kErrSoftmax);
       const bool all = __all_sync(0xffffffffu, r);
       if (all) tc_fence_after();
       return all;
     };
-    // Completion of PV_t(c), needed before O is read or rescaled.  Testing the phase only
-    // when needed is sound: the next completion of that buffer's barrier is PV_t(c+2), which
+    // Completion of PV(c), needed before O is read or rescaled.  Testing the phase only
+    // when needed is sound: the next completion of that buffer's barrier is PV(c+2), which
     // needs this warp's P of chunk c+2.
-    auto wait_pv_done = [&](int c) -> bool { return wait_warp(bar(kPvDone + 2 * t + (c & 1)), (c >> 1) & 1); };
+    auto wait_pv_done = [&](int c) -> bool { return wait_warp(bar(kPvDone + (c & 1)), (c >> 1) & 1); };
     for (int ch = 0; ch < n_chunks; ++ch) {
       const int buf = ch & 1;
       const uint32_t t_s = t_tile + buf * kSBuf;
@@ -462,16 +446,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
       }
-      // S_t(ch) complete (the barrier map is described at enum Bar).  Each is completion
+      // S(ch) complete (the barrier map is described at enum Bar).  Each is completion
       // number k of its barrier with k - 1 awaited by this warp before (or k = 0), and
       // completion k + 1 needs this warp's P of a later chunk.
-      if (t == 1 && ch >= 2)
+      if (ch >= 2)
         ok = wait_warp(bar(kEmpty + (ch - 2) % C::kStages), ((ch - 2) / C::kStages) & 1);
       else
-        ok = wait_warp(bar(kSReady + 2 * t + buf), (ch >> 1) & 1);
+        ok = wait_warp(bar(kSReady + ch), 0);
       if (!ok) break;
       const bool local = ch < kLocalChunks;
-      const int zp = p.qz0 + z0 + kTZ * t - kR + ch;  // global plane of this local chunk
+      const int zp = p.qz0 + z0 - kR + ch;  // global plane of this local chunk
       const bool active = !local || ((unsigned)(ch - qz) <= 2u * kR && zp >= 0 && zp < p.Zg);  // warp-uniform
       if (active) {
         float s[kKeys];
@@ -512,10 +496,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kPReady + 2 * t + buf));
+      if (lane == 0) mbar_arrive(bar(kPReady + buf));
     }
     // ---- epilogue: normalise the global branch, mix, store through the row map
-    if (ok) ok = wait_warp(bar(kOReady + t), 0);
+    if (ok) ok = wait_warp(bar(kOReady), 0);
     if (ok) {
       uint32_t og[D];
 #pragma unroll
@@ -604,7 +588,7 @@ int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
   p.kz0 = a.k_z0;
   p.Y = Y;
   p.X = X;
-  p.tiles_z = (Z + 2 * kTZ - 1) / (2 * kTZ);
+  p.tiles_z = (Z + kTZ - 1) / kTZ;
   p.tiles_y = (Y + kTY - 1) / kTY;
   p.tiles_x = (X + kTX - 1) / kTX;
   p.heads = a.heads;

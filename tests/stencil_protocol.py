@@ -147,7 +147,8 @@ def mma(state):
         issue_s(1, ch)
         yield ("step", None)
     for c in range(n):
-        for t in range(2):
+        ch = c + 2
+        for t in range(2):   # PV_t(c), then (after it completed) S_t(c+2): tiles are decoupled
             yield from waits(f"pready{t}{c & 1}", (c >> 1) & 1, c >> 1)
             if len(state.p_stored.get((t, c), ())) != 4:
                 raise ProtocolError(f"PV_{t}({c}) issued before all four warps stored P")
@@ -155,16 +156,13 @@ def mma(state):
             state.pv_issued.add((t, c))
             commit(f"pvdone{t}{c & 1}")
             yield ("step", None)
-        if c + 2 >= n:
-            continue
-        ch = c + 2
-        yield from waits(f"full{ch % k}", (ch // k) & 1, ch // k)
-        yield from waits("pvdone0" + str(c & 1), (c >> 1) & 1, c >> 1)
-        issue_s(0, ch)
-        yield ("step", None)
-        yield from waits("pvdone1" + str(c & 1), (c >> 1) & 1, c >> 1)
-        issue_s(1, ch)
-        yield ("step", None)
+            if ch >= n:
+                continue
+            if t == 0:
+                yield from waits(f"full{ch % k}", (ch // k) & 1, ch // k)
+            yield from waits(f"pvdone{t}{c & 1}", (c >> 1) & 1, c >> 1)
+            issue_s(t, ch)
+            yield ("step", None)
     commit("oready0")
     commit("oready1")
     commit("drain")
@@ -532,4 +530,123 @@ def run_gkv(n_chunks=10, stages=4, seed=0, max_steps=400000):
     roles = {"producer": gkv_producer(state), "mma": gkv_mma(state)}
     for w in range(8):
         roles[f"softmax{w}"] = gkv_softmax(state, w)
+    return _schedule(state, roles, rng, max_steps)
+
+
+# --------------------------------------------------------------- forward, one tile per CTA
+# Model of the shipped stencil_fwd_kernel: one 128-row tile, two S buffers; S(0), S(1)
+# commit to sready[c], S(c >= 2) to empty[(c-2) % stages], which the producer (stage
+# release) and the softmax warps (S ready) both wait on.
+
+def fwd1_producer(state):
+    k = state.stages
+    for ch in range(state.n_chunks):
+        s = ch % k
+        if ch >= k:
+            while not _wait(state, f"empty{s}", (ch // k - 1) & 1, ch // k - 1):
+                yield ("wait", f"empty{s}")
+        old = state.stage_chunk.get(s)
+        if old is not None:
+            for op in (("S", 0, old), ("PV", 0, old)):
+                if op not in state.mma_done:
+                    raise ProtocolError(f"stage {s} overwritten with chunk {ch} while {op} is outstanding")
+        state.bar(f"full{s}").arrive(tx=1)
+        state.stage_chunk[s] = ch
+        state.tma_inflight.append((s, ch))
+        yield ("step", None)
+
+
+def fwd1_mma(state):
+    k, n = state.stages, state.n_chunks
+
+    def commit(name):
+        state.mma_queue.append(("commit", name))
+
+    def waits(name, completion):
+        while not _wait(state, name, completion & 1, completion):
+            yield ("wait", name)
+
+    def issue_s(ch):
+        if state.stage_landed.get(ch % k) != ch:
+            raise ProtocolError(f"S({ch}) reads stage {ch % k} before chunk {ch} landed")
+        if ch >= 2 and ("PV", 0, ch - 2) not in state.mma_done:
+            raise ProtocolError(f"S({ch}) overwrites P of chunk {ch - 2} before PV({ch - 2}) completed")
+        state.mma_queue.append(("S", 0, ch))
+        commit(f"empty{(ch - 2) % k}" if ch >= 2 else f"sready{ch}")
+
+    yield from waits("qfull", 0)
+    for ch in range(min(2, n)):
+        yield from waits(f"full{ch % k}", ch // k)
+        issue_s(ch)
+        yield ("step", None)
+    for c in range(n):
+        yield from waits(f"pready{c & 1}", c >> 1)
+        if len(state.p_stored.get((0, c), ())) != 4:
+            raise ProtocolError(f"PV({c}) issued before all four warps stored P")
+        state.mma_queue.append(("PV", 0, c))
+        state.pv_issued.add((0, c))
+        commit(f"pvdone{c & 1}")
+        yield ("step", None)
+        if c + 2 >= n:
+            continue
+        yield from waits(f"full{(c + 2) % k}", (c + 2) // k)
+        yield from waits(f"pvdone{c & 1}", c >> 1)
+        issue_s(c + 2)
+        yield ("step", None)
+    commit("oready")
+    commit("drain")
+    yield from waits("drain", 0)
+
+
+def fwd1_softmax(state, w, rng):
+    k, n = state.stages, state.n_chunks
+
+    def waits(name, completion):
+        while not _wait(state, name, completion & 1, completion):
+            yield ("wait", name)
+
+    def pv_done(c):
+        yield from waits(f"pvdone{c & 1}", c >> 1)
+        if ("PV", 0, c) not in state.mma_done:
+            raise ProtocolError(f"O touched before PV({c}) completed")
+        if (0, c + 1) in state.pv_issued:
+            raise ProtocolError(f"O touched after PV({c + 1}) was issued")
+
+    for ch in range(n):
+        if ch == LOCAL_CHUNKS:
+            yield from pv_done(LOCAL_CHUNKS - 1)
+        if ch >= 2:
+            yield from waits(f"empty{(ch - 2) % k}", (ch - 2) // k)
+        else:
+            yield from waits(f"sready{ch}", 0)
+        if ("S", 0, ch) not in state.mma_done:
+            raise ProtocolError(f"S({ch}) read before it completed")
+        yield ("step", None)
+        state.p_stored.setdefault((0, ch), set()).add(w)
+        if ch not in (0, LOCAL_CHUNKS) and rng.random() < 0.3:  # data-dependent rescale of O
+            yield from pv_done(ch - 1)
+        state.bar(f"pready{ch & 1}").arrive()
+        yield ("step", None)
+    yield from waits("oready", 0)
+    if ("PV", 0, n - 1) not in state.mma_done:
+        raise ProtocolError("O read before the last PV completed")
+
+
+def run_fwd(n_chunks=14, stages=4, seed=0, max_steps=400000):
+    """Replay one random interleaving of the (one-tile) forward kernel's protocol."""
+    rng = random.Random(seed)
+    state = State(n_chunks=n_chunks, stages=stages)
+    bars = {"qfull": 1, "drain": 1, "oready": 1}
+    for s in range(4):
+        bars[f"full{s}"] = 1
+        bars[f"empty{s}"] = 1
+    for b in range(2):
+        bars[f"sready{b}"] = 1
+        bars[f"pready{b}"] = 4
+        bars[f"pvdone{b}"] = 1
+    state.bars = {name: Barrier(name, cnt) for name, cnt in bars.items()}
+    state.bar("qfull").arrive(tx=0)
+    roles = {"producer": fwd1_producer(state), "mma": fwd1_mma(state)}
+    for w in range(4):
+        roles[f"softmax{w}"] = fwd1_softmax(state, w, random.Random(rng.random()))
     return _schedule(state, roles, rng, max_steps)

@@ -12,9 +12,15 @@ import stencil_protocol as sp
 
 @pytest.mark.parametrize("stages", [3, 4])
 @pytest.mark.parametrize("n_chunks", [10, 15])
-def test_protocol_holds_under_random_interleavings(stages, n_chunks):
+def test_forward_protocol_holds_under_random_interleavings(stages, n_chunks):
     for seed in range(150):
-        sp.run(n_chunks=n_chunks, stages=stages, seed=seed, release="empty")
+        sp.run_fwd(n_chunks=n_chunks, stages=stages, seed=seed)
+
+
+def test_two_tile_protocol_with_release_barriers_holds():
+    """The earlier two-tile forward, repaired with per-stage release barriers."""
+    for seed in range(100):
+        sp.run(n_chunks=14, stages=4, seed=seed, release="empty")
 
 
 def test_model_rejects_the_ambiguous_release_scheme():
