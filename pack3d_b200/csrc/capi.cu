@@ -517,6 +517,8 @@ int p3d_attn_bwd(const p3d_operator *op, const void *dy, const void *sk, const v
     t.head_dim = d;
     t.summaries = M;
     for (int i = 0; i < 3; ++i) t.grid[i] = op->grid[i];
+    t.global_planes = t.k_planes = op->grid[0];
+    t.q_z0 = t.k_z0 = 0;
     t.q = op->q;
     t.kl = op->kl;
     t.vl = op->vl;

@@ -115,7 +115,9 @@ int launch_stencil_fwd(const StencilFwdArgs &a, cudaStream_t s);
 struct StencilBwdArgs {
   int dtype;
   int batch, heads, kv_heads, head_dim, summaries;
-  int grid[3];
+  int grid[3];                          // centre buffer (queries for dQ, keys for dK / dV)
+  // z-slab extents (whole volume: global_planes = k_planes = grid[0], q_z0 = k_z0 = 0):
+  int global_planes, q_z0, k_z0, k_planes;
   const void *q, *kl, *vl, *dol, *dog;  // raster order (contiguous [B,H|G,Z,Y,X,D])
   const void *sk, *sv;                  // [B,G,M,D]
   const float *lse_l, *lse_g, *delta_l, *delta_g;  // [B*H, N] in the layout's row order

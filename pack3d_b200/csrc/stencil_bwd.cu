@@ -10,16 +10,17 @@
 // rounded, then added and rounded again (kernels.py:202-206).
 //
 // Work unit and chunk sequence are those of the forward kernel (stencil_fwd.cu): one
-// (batch, head), an 8x4x8 query box = two 128-row tiles, 8 local chunks (halo planes of an
-// 8x12 window) then ceil(M/96) global chunks.  Per tile, TMEM holds S [0, 96), dP
-// [96, 192) and the dQ accumulator [192, 192 + D).  Per chunk the MMA thread issues
-// S = Q K^T and dP = dO V^T; the softmax warps turn them into dS, written back as 16-bit
-// pairs over the first 48 dP columns, and the MMA thread accumulates dQ += dS K with dS as
-// the TMEM A operand and the K chunk (already in shared memory for S) read MN-major as B.
-// S of the next chunk is issued as soon as the softmax warps have released this chunk,
-// while dQ of this chunk runs; dP of the next chunk waits for dQ to finish reading dS.
+// (batch, head) and a 4x4x8 tile of 128 queries per CTA, two CTAs per SM; 8 local chunks
+// (halo planes of an 8x12 window) then ceil(M/96) global chunks.  TMEM (256 columns) holds
+// S [0, 96), dP [96, 192) and the dQ accumulator [192, 192 + D).  Per chunk the MMA thread
+// issues S = Q K^T and dP = dO V^T; the softmax warps turn them into dS, written back as
+// 16-bit pairs over the first 48 dP columns, and the MMA thread accumulates dQ += dS K with
+// dS as the TMEM A operand and the K chunk (already in shared memory for S) read MN-major
+// as B.  S of the next chunk is issued as soon as the softmax warps have released this
+// chunk, while dQ of this chunk runs; dP of the next chunk waits for dQ to finish reading
+// dS.
 //
-// Roles: warps 0-3 tile A, 4-7 tile B, warp 8 TMA producer, warp 9 MMA issuer.  Every
+// Roles: warps 0-3 softmax, warp 4 TMA producer, warp 5 MMA issuer.  Every
 // mbarrier wait is bounded and every parity wait is unambiguous: each barrier completes
 // once per chunk (the ring's release barriers once per stage use) and each waiter awaits
 // its completions in order, its next completion needing the waiter's own next step.
@@ -49,22 +50,29 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr float kLog2e = 1.4426950408889634f;
 
+constexpr int kDqThreads = 192;                   // one tile per CTA, two CTAs per SM
+constexpr int kDqProducerWarp = 4, kDqMmaWarp = 5;
+constexpr uint32_t kDqTmemCols = 256;
+
 template <int D>
 struct DqCfg {
   static constexpr int kK = D / 16;
   static constexpr int kBoxQ = kRows * 32;
   static constexpr int kBoxK = kKeys * 32;
-  static constexpr int kQBytes = kK * kBoxQ;      // one 128-row tile of Q, dO_l or dO_g
+  static constexpr int kQBytes = kK * kBoxQ;      // the 128-row tile of Q, dO_l or dO_g
   static constexpr int kKeyBytes = kK * kBoxK;    // one chunk of K or V
-  static constexpr int kStageBytes = (4 * kKeyBytes + 1023) / 1024 * 1024;
+  static constexpr int kStageBytes = (2 * kKeyBytes + 1023) / 1024 * 1024;
   static constexpr int kParkBytes = kRows * D * 2;
-  static constexpr int kFixed = 6 * kQBytes + 2 * kParkBytes + 1024;
-  static constexpr int kRoom = (227 * 1024 - 2048 - kFixed) / kStageBytes;
+  static constexpr int kFixed = 3 * kQBytes + kParkBytes + 1024;
+  // two CTAs per SM (<= 113 KB each), never three (> 76 KB: a third CTA's TMEM
+  // allocation would have to wait)
+  static constexpr int kMaxSmem = 113 * 1024, kMinSmem = 78 * 1024;
+  static constexpr int kRoom = (kMaxSmem - kFixed) / kStageBytes;
   static constexpr int kStages = kRoom > 4 ? 4 : kRoom;
   static constexpr int kSmemNeed = kFixed + kStages * kStageBytes;
-  static constexpr int kSmemBytes = kSmemNeed > 116 * 1024 ? kSmemNeed : 116 * 1024;
+  static constexpr int kSmemBytes = kSmemNeed > kMinSmem ? kSmemNeed : kMinSmem;
   static_assert(kStages >= 2, "the ring must hold two chunks");
-  static_assert(kSmemBytes <= 225 * 1024, "shared memory budget");
+  static_assert(kSmemBytes <= kMaxSmem, "shared memory budget");
 };
 
 constexpr uint32_t kColS = 0, kColDP = 96, kColDQ = 192;
@@ -72,17 +80,19 @@ constexpr uint32_t kColS = 0, kColDP = 96, kColDQ = 192;
 enum DqBar {
   kQFull = 0,
   kFull = 1,                 // [stage]
-  kEmpty = kFull + 4,        // [stage]: released by the commit after dQ_B of the chunk it held
-  kSReady = kEmpty + 4,      // [tile]: S_t(c) complete
-  kDPReady = kSReady + 2,    // [tile]: dP_t(c) complete
-  kDSReady = kDPReady + 2,   // [tile]: the tile's 4 softmax warps stored dS_t(c) (count 4)
-  kDQDone = kDSReady + 2,    // [tile]: dQ_t(c) complete
-  kDrain = kDQDone + 2,
+  kEmpty = kFull + 4,        // [stage]: arrived by the MMA thread once dQ of the chunk it held completed
+  kSReady = kEmpty + 4,      // S(c) complete
+  kSFree = kSReady + 1,      // the 4 softmax warps hold S(c) in registers (count 4)
+  kDPReady = kSFree + 1,     // dP(c) complete
+  kDSReady = kDPReady + 1,   // the 4 softmax warps stored dS(c) (count 4)
+  kDQDone = kDSReady + 1,    // dQ(c) complete
+  kDrain = kDQDone + 1,
   kNumBars = kDrain + 1
 };
 
 struct DqParams {
-  int Z, Y, X, tiles_z, tiles_y, tiles_x;
+  int Z, Y, X, tiles_z, tiles_y, tiles_x;  // Z: planes of the query (centre) buffer
+  int Zg, qz0, kz0;  // global planes; global z of query-buffer plane 0 and of K/V-buffer plane 0
   int heads, kv_heads, summaries, global_chunks;
   int64_t tokens;
   float sc;        // log2(e) / sqrt(D)
@@ -113,7 +123,7 @@ __device__ __forceinline__ float round_storage(float v) {
 }
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kDqThreads, 2)
     stencil_bwd_dq_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdol,
                           const __grid_constant__ CUtensorMap tdog, const __grid_constant__ CUtensorMap tkl,
                           const __grid_constant__ CUtensorMap tvl, const __grid_constant__ CUtensorMap tsk,
@@ -131,18 +141,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   unit /= p.tiles_y;
   const int tz = unit % p.tiles_z;
   const int bh = unit / p.tiles_z;
-  const int x0 = tx * kTX, y0 = ty * kTY, z0 = tz * 2 * kTZ;
+  const int x0 = tx * kTX, y0 = ty * kTY, z0 = tz * kTZ;
   const int b = bh / p.heads, h = bh % p.heads;
   const int bg = b * p.kv_heads + h / (p.heads / p.kv_heads);
   const int n_chunks = kLocalChunks + p.global_chunks;
 
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
-  const uint32_t q_smem = base;                         // [tile] Q
-  const uint32_t dol_smem = base + 2 * C::kQBytes;      // [tile] dO_l
-  const uint32_t dog_smem = base + 4 * C::kQBytes;      // [tile] dO_g
-  const uint32_t ring = base + 6 * C::kQBytes;
-  uint8_t *park_base = smem_raw + (base - raw) + 6 * C::kQBytes + C::kStages * C::kStageBytes;
+  const uint32_t q_smem = base;                     // Q
+  const uint32_t dol_smem = base + C::kQBytes;      // dO_l
+  const uint32_t dog_smem = base + 2 * C::kQBytes;  // dO_g
+  const uint32_t ring = base + 3 * C::kQBytes;
+  uint8_t *park_base = smem_raw + (base - raw) + 3 * C::kQBytes + C::kStages * C::kStageBytes;
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
 
   if (tid == 0) {
@@ -151,20 +161,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kFull + s), 1);
       mbar_init(bar(kEmpty + s), 1);
     }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(bar(kSReady + t), 1);
-      mbar_init(bar(kDPReady + t), 1);
-      mbar_init(bar(kDSReady + t), 4);
-      mbar_init(bar(kDQDone + t), 1);
-    }
+    mbar_init(bar(kSReady), 1);
+    mbar_init(bar(kSFree), 4);
+    mbar_init(bar(kDPReady), 1);
+    mbar_init(bar(kDSReady), 4);
+    mbar_init(bar(kDQDone), 1);
     mbar_init(bar(kDrain), 1);
     fence_mbar_init();
   }
-  if (warp == kMmaWarp) {
-    tmem_alloc(smem_u32(&tmem_holder), kTmemCols);
+  if (warp == kDqMmaWarp) {
+    tmem_alloc(smem_u32(&tmem_holder), kDqTmemCols);
     tmem_relinquish();
   }
-  if (warp == kProducerWarp && lane == 0) {
+  if (warp == kDqProducerWarp && lane == 0) {
     prefetch_tmap(&tq);
     prefetch_tmap(&tdol);
     prefetch_tmap(&tdog);
@@ -178,17 +187,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_holder;
 
-  if (warp == kProducerWarp) {
+  if (warp == kDqProducerWarp) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      mbar_expect_tx(bar(kQFull), 6 * C::kQBytes);
-      for (int t = 0; t < 2; ++t)
-        for (int c = 0; c < C::kK; ++c) {
-          const int z = z0 + kTZ * t;
-          tma_load_5d(q_smem + t * C::kQBytes + c * C::kBoxQ, &tq, bar(kQFull), 16 * c, x0, y0, z, bh);
-          tma_load_5d(dol_smem + t * C::kQBytes + c * C::kBoxQ, &tdol, bar(kQFull), 16 * c, x0, y0, z, bh);
-          tma_load_5d(dog_smem + t * C::kQBytes + c * C::kBoxQ, &tdog, bar(kQFull), 16 * c, x0, y0, z, bh);
-        }
+      mbar_expect_tx(bar(kQFull), 3 * C::kQBytes);
+      for (int c = 0; c < C::kK; ++c) {
+        tma_load_5d(q_smem + c * C::kBoxQ, &tq, bar(kQFull), 16 * c, x0, y0, z0, bh);
+        tma_load_5d(dol_smem + c * C::kBoxQ, &tdol, bar(kQFull), 16 * c, x0, y0, z0, bh);
+        tma_load_5d(dog_smem + c * C::kBoxQ, &tdog, bar(kQFull), 16 * c, x0, y0, z0, bh);
+      }
       int issued = 0;
       for (int ch = 0; ch < n_chunks; ++ch) {
         const int s = ch % C::kStages;
@@ -200,19 +207,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         const uint32_t stage = ring + s * C::kStageBytes;
         const uint32_t full = bar(kFull + s);
+        mbar_expect_tx(full, 2 * C::kKeyBytes);
         if (ch < kLocalChunks) {
-          mbar_expect_tx(full, 4 * C::kKeyBytes);
-          for (int t = 0; t < 2; ++t) {
-            const int z = z0 + kTZ * t - kR + ch;
-            for (int c = 0; c < C::kK; ++c) {
-              tma_load_5d(stage + t * C::kKeyBytes + c * C::kBoxK, &tkl, full, 16 * c, x0 - kR, y0 - kR, z, bg);
-              tma_load_5d(stage + (2 + t) * C::kKeyBytes + c * C::kBoxK, &tvl, full, 16 * c, x0 - kR, y0 - kR, z,
-                          bg);
-            }
+          const int z = p.qz0 + z0 - kR + ch - p.kz0;  // plane in the K/V buffer
+          for (int c = 0; c < C::kK; ++c) {
+            tma_load_5d(stage + c * C::kBoxK, &tkl, full, 16 * c, x0 - kR, y0 - kR, z, bg);
+            tma_load_5d(stage + C::kKeyBytes + c * C::kBoxK, &tvl, full, 16 * c, x0 - kR, y0 - kR, z, bg);
           }
         } else {
           const int g = ch - kLocalChunks;
-          mbar_expect_tx(full, 2 * C::kKeyBytes);
           for (int c = 0; c < C::kK; ++c) {
             tma_load_3d(stage + c * C::kBoxK, &tsk, full, 16 * c, g * kSumRows, bg);
             tma_load_3d(stage + C::kKeyBytes + c * C::kBoxK, &tsv, full, 16 * c, g * kSumRows, bg);
@@ -224,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ch = issued > C::kStages ? issued - C::kStages : 0; ch < issued; ++ch)
         mbar_wait(bar(kFull + ch % C::kStages), (ch / C::kStages) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == kDqMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(128, kKeys, BF16, false);  // S and dP: N = 96, K-major B
@@ -235,33 +238,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(bar(bidx));
         ++commits[bidx];
       };
-      auto stage_of = [&](int c) { return ring + (c % C::kStages) * C::kStageBytes; };
-      auto k_of = [&](int t, int c) { return c < kLocalChunks ? stage_of(c) + t * C::kKeyBytes : stage_of(c); };
-      auto v_of = [&](int t, int c) {
-        return c < kLocalChunks ? stage_of(c) + (2 + t) * C::kKeyBytes : stage_of(c) + C::kKeyBytes;
-      };
-      auto issue_s = [&](int t, int c) {
-        const uint32_t q_t = q_smem + t * C::kQBytes, k_base = k_of(t, c);
+      const uint64_t desc_q = desc_sw32(q_smem, 16, 256);
+      const uint64_t desc_dol = desc_sw32(dol_smem, 16, 256), desc_dog = desc_sw32(dog_smem, 16, 256);
+      const uint64_t desc_k = desc_sw32(ring, 16, 256);          // K / V chunks, K-major
+      const uint64_t desc_kmn = desc_sw32(ring, C::kBoxK, 256);  // K chunks read MN-major
+      auto stage_off = [&](int c) { return (uint32_t)((c % C::kStages) * C::kStageBytes) >> 4; };
+      auto issue_s = [&](int c) {
+        const uint64_t bk = desc_k + stage_off(c);
+#pragma unroll
         for (int kk = 0; kk < C::kK; ++kk)
-          mma_ss(tmem + t * 256 + kColS, desc_sw32(q_t + kk * C::kBoxQ, 16, 256),
-                 desc_sw32(k_base + kk * C::kBoxK, 16, 256), idesc_s, kk > 0 ? 1u : 0u);
-        commit(kSReady + t);
+          mma_ss(tmem + kColS, desc_q + kk * (C::kBoxQ >> 4), bk + kk * (C::kBoxK >> 4), idesc_s, kk > 0 ? 1u : 0u);
+        commit(kSReady);
       };
-      auto issue_dp = [&](int t, int c) {
-        const uint32_t do_t = (c < kLocalChunks ? dol_smem : dog_smem) + t * C::kQBytes, v_base = v_of(t, c);
+      auto issue_dp = [&](int c) {
+        const uint64_t ad = c < kLocalChunks ? desc_dol : desc_dog;
+        const uint64_t bv = desc_k + stage_off(c) + (C::kKeyBytes >> 4);
+#pragma unroll
         for (int kk = 0; kk < C::kK; ++kk)
-          mma_ss(tmem + t * 256 + kColDP, desc_sw32(do_t + kk * C::kBoxQ, 16, 256),
-                 desc_sw32(v_base + kk * C::kBoxK, 16, 256), idesc_s, kk > 0 ? 1u : 0u);
-        commit(kDPReady + t);
+          mma_ss(tmem + kColDP, ad + kk * (C::kBoxQ >> 4), bv + kk * (C::kBoxK >> 4), idesc_s, kk > 0 ? 1u : 0u);
+        commit(kDPReady);
       };
-      auto issue_dq = [&](int t, int c) {
-        const uint32_t k_base = k_of(t, c);
+      auto issue_dq = [&](int c) {
+        const uint64_t bk = desc_kmn + stage_off(c);
         const bool first = (c == 0) || (c == kLocalChunks);  // dQ restarts for the global branch
+#pragma unroll
         for (int j = 0; j < kKeys / 16; ++j)
-          mma_ts(tmem + t * 256 + kColDQ, tmem + t * 256 + kColDP + 8 * j, desc_sw32(k_base + j * 512, C::kBoxK, 256),
-                 idesc_dq, (first && j == 0) ? 0u : 1u);
-        commit(kDQDone + t);
-        if (t == 1) commit(kEmpty + c % C::kStages);  // every MMA reading chunk c's stage is issued
+          mma_ts(tmem + kColDQ, tmem + kColDP + 8 * j, bk + j * (512 >> 4), idesc_dq, (first && j == 0) ? 0u : 1u);
+        commit(kDQDone);
       };
       auto wait_bar = [&](int bidx, int completion) -> bool {
         if (!mbar_wait(bar(bidx), completion & 1, &g_bwd_errors, kWaitNs, kErrMma)) return false;
@@ -269,40 +272,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       auto wait_full = [&](int c) { return wait_bar(kFull + c % C::kStages, c / C::kStages); };
-      // Prologue: S and dP of chunk 0 for both tiles.  Steady state per chunk c:
-      //   [dS_A(c)] dQ_A(c), S_A(c+1), [dS_B(c)] dQ_B(c), S_B(c+1),
-      //   [dQ_A(c) done] dP_A(c+1), [dQ_B(c) done] dP_B(c+1)
-      // S_t(c+1) overwrites S_t(c), which the softmax warps have read before storing dS_t(c);
-      // dP_t(c+1) overwrites dS_t(c), which dQ_t(c) reads (tcgen05.mma ops are ordered only
-      // when they share an accumulator), hence the wait for dQ_t(c).
+      // Prologue: S and dP of chunk 0.  Steady state per chunk c:
+      //   [S(c) in registers] S(c+1), [dS(c)] dQ(c), [dQ(c) done] release stage c, dP(c+1)
+      // S(c+1) overwrites S(c) once the softmax warps hold it in registers, so it runs while
+      // they compute P(c) and dS(c); dP(c+1) overwrites dS(c), which dQ(c) reads
+      // (tcgen05.mma ops are ordered only when they share an accumulator), hence the wait
+      // for dQ(c) -- whose completion also frees chunk c's ring stage (S(c) and dP(c) were
+      // complete before the softmax warps used them).
       bool ok = wait_bar(kQFull, 0) && wait_full(0);
       if (ok) {
-        issue_s(0, 0);
-        issue_s(1, 0);
-        issue_dp(0, 0);
-        issue_dp(1, 0);
+        issue_s(0);
+        issue_dp(0);
       }
       for (int c = 0; ok && c < n_chunks; ++c) {
         const bool more = c + 1 < n_chunks;
-        ok = wait_bar(kDSReady + 0, c);
-        if (!ok) break;
-        issue_dq(0, c);
         if (more) {
-          ok = wait_full(c + 1);
+          ok = wait_bar(kSFree, c) && wait_full(c + 1);
           if (!ok) break;
-          issue_s(0, c + 1);
+          issue_s(c + 1);
         }
-        ok = wait_bar(kDSReady + 1, c);
+        ok = wait_bar(kDSReady, c);
         if (!ok) break;
-        issue_dq(1, c);
+        issue_dq(c);
         if (!more) break;
-        issue_s(1, c + 1);
-        ok = wait_bar(kDQDone + 0, c);
+        ok = wait_bar(kDQDone, c);
         if (!ok) break;
-        issue_dp(0, c + 1);
-        ok = wait_bar(kDQDone + 1, c);
-        if (!ok) break;
-        issue_dp(1, c + 1);
+        mbar_arrive(bar(kEmpty + c % C::kStages));
+        issue_dp(c + 1);
       }
       commit(kDrain);
       for (int i = 0; i < kNumBars; ++i)
@@ -310,12 +306,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    const int t = warp >> 2, w = warp & 3;
-    const uint32_t lanes = (uint32_t)(w * 32) << 16;
-    const uint32_t t_tile = tmem + lanes + t * 256;
+    const int w = warp;
+    const uint32_t t_tile = tmem + ((uint32_t)(w * 32) << 16);
     const int row = w * 32 + lane;
     const int qz = w, qy = lane >> 3, qx = lane & 7;
-    const int zq = z0 + kTZ * t + qz, yq = y0 + qy, xq = x0 + qx;
+    const int zq = z0 + qz, yq = y0 + qy, xq = x0 + qx;
     const bool row_ok = zq < p.Z && yq < p.Y && xq < p.X;
     int64_t grow = 0;
     float lse2_l = __builtin_huge_valf(), lse2_g = __builtin_huge_valf(), delta_l = 0.f, delta_g = 0.f;
@@ -328,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       delta_l = p.delta_l[grow];
       delta_g = p.delta_g[grow];
     }
-    uint32_t *park = reinterpret_cast<uint32_t *>(park_base + (size_t)(t * kRows + row) * D * 2);
+    uint32_t *park = reinterpret_cast<uint32_t *>(park_base + (size_t)row * D * 2);
     uint32_t mask[3] = {0u, 0u, 0u};
 #pragma unroll
     for (int hy = 0; hy < kHY; ++hy) {
@@ -350,8 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int ch = 0; ch < n_chunks; ++ch) {
       if (ch == kLocalChunks) {
-        // Local branch done once dQ_t(7) has completed: round it to the storage dtype, park it.
-        ok = wait_warp(kDQDone + t, kLocalChunks - 1);
+        // Local branch done once dQ(7) has completed: round it to the storage dtype, park it.
+        ok = wait_warp(kDQDone, kLocalChunks - 1);
         if (!ok) break;
 #pragma unroll
         for (int c = 0; c < D / 16; ++c) {
@@ -363,16 +358,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const bool local = ch < kLocalChunks;
-      const int zp = z0 + kTZ * t - kR + ch;
-      const bool active = !local || ((unsigned)(ch - qz) <= 2u * kR && zp >= 0 && zp < p.Z);  // warp-uniform
+      const int zp = p.qz0 + z0 - kR + ch;  // global plane of this local chunk
+      const bool active = !local || ((unsigned)(ch - qz) <= 2u * kR && zp >= 0 && zp < p.Zg);  // warp-uniform
       const float lse2 = local ? lse2_l : lse2_g, delta = local ? delta_l : delta_g;
-      ok = wait_warp(kSReady + t, ch);
+      ok = wait_warp(kSReady, ch);
       if (!ok) break;
       float pr[kKeys];
       if (active) {
 #pragma unroll
         for (int g = 0; g < kKeys / 32; ++g) tmem_ld32(t_tile + kColS + 32 * g, reinterpret_cast<uint32_t *>(pr + 32 * g));
         tmem_wait_ld();
+      }
+      // S(ch) is in registers (or not needed): the S buffer may take S(ch+1)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kSFree));
+      if (active) {
         int valid = kKeys;
         if (!local) valid = min(kKeys, p.summaries - (ch - kLocalChunks) * kSumRows);
 #pragma unroll
@@ -381,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           pr[i] = use ? ex2_approx(fmaf(pr[i], sc, -lse2)) : 0.f;
         }
       }
-      ok = wait_warp(kDPReady + t, ch);
+      ok = wait_warp(kDPReady, ch);
       if (!ok) break;
       if (active) {
 #pragma unroll
@@ -409,10 +410,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kDSReady + t));
+      if (lane == 0) mbar_arrive(bar(kDSReady));
     }
     // ---- epilogue: dq = round(round(dQ_l) + round(dQ_g)) through the row map
-    if (ok) ok = wait_warp(kDQDone + t, n_chunks - 1);
+    if (ok) ok = wait_warp(kDQDone, n_chunks - 1);
     if (ok) {
       uint32_t acc[D];
 #pragma unroll
@@ -437,9 +438,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kDqMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, kDqTmemCols);
   }
 }
 
@@ -459,8 +460,9 @@ int launch_dq_t(const StencilBwdArgs &a, cudaStream_t stream) {
     if (int st = encode_operand(&tdog, a.dtype, a.dog, 5, dims, strides, box)) return st;
   }
   {
-    const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)Z, bgs};
-    const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es, (uint64_t)Z * Y * X * D * es};
+    const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)a.k_planes, bgs};
+    const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es,
+                                 (uint64_t)a.k_planes * Y * X * D * es};
     const uint32_t box[5] = {16, kHX, kHY, 1, 1};
     if (int st = encode_operand(&tkl, a.dtype, a.kl, 5, dims, strides, box)) return st;
     if (int st = encode_operand(&tvl, a.dtype, a.vl, 5, dims, strides, box)) return st;
@@ -474,9 +476,12 @@ int launch_dq_t(const StencilBwdArgs &a, cudaStream_t stream) {
   }
   DqParams p{};
   p.Z = Z;
+  p.Zg = a.global_planes;
+  p.qz0 = a.q_z0;
+  p.kz0 = a.k_z0;
   p.Y = Y;
   p.X = X;
-  p.tiles_z = (Z + 2 * kTZ - 1) / (2 * kTZ);
+  p.tiles_z = (Z + kTZ - 1) / kTZ;
   p.tiles_y = (Y + kTY - 1) / kTY;
   p.tiles_x = (X + kTX - 1) / kTX;
   p.heads = a.heads;
@@ -501,7 +506,7 @@ int launch_dq_t(const StencilBwdArgs &a, cudaStream_t stream) {
     P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
     configured = true;
   }
-  kernel<<<(unsigned)units, kThreads, C::kSmemBytes, stream>>>(tq, tdol, tdog, tkl, tvl, tsk, tsv, p);
+  kernel<<<(unsigned)units, kDqThreads, C::kSmemBytes, stream>>>(tq, tdol, tdog, tkl, tvl, tsk, tsv, p);
   P3D_LAUNCH_CHECK();
   return P3D_OK;
 }

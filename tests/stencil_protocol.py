@@ -267,9 +267,9 @@ def _schedule(state, roles, rng, max_steps):
 
 
 # ----------------------------------------------------------------------------- dQ kernel
-# Model of stencil_bwd_dq_kernel (pack3d_b200/csrc/stencil_bwd.cu): per tile a single S
-# buffer, a single dP buffer that receives dS, and the dQ accumulator; the ring's stages
-# are released by the commit after dQ_B of the chunk they held.
+# Model of stencil_bwd_dq_kernel (pack3d_b200/csrc/stencil_bwd.cu): one 128-query tile per
+# CTA with a single S buffer, a single dP buffer that receives dS, and the dQ accumulator;
+# the ring's stages are released by the commit after dQ of the chunk they held.
 
 def dq_producer(state):
     k = state.stages
@@ -280,7 +280,7 @@ def dq_producer(state):
                 yield ("wait", f"empty{s}")
         old = state.stage_chunk.get(s)
         if old is not None:
-            for op in [(kind, t, old) for kind in ("S", "DP", "DQ") for t in range(2)]:
+            for op in [(kind, 0, old) for kind in ("S", "DP", "DQ")]:
                 if op not in state.mma_done:
                     raise ProtocolError(f"stage {s} overwritten with chunk {ch} while {op} is outstanding")
         state.bar(f"full{s}").arrive(tx=1)
@@ -299,67 +299,58 @@ def dq_mma(state):
         if state.stage_landed.get(c % k) != c:
             raise ProtocolError(f"chunk {c} read before its copy landed")
 
-    def issue_s(t, c):
+    def issue_s(c):
         landed(c)
-        if c >= 1 and len(state.ds_stored.get((t, c - 1), ())) != 4:
-            raise ProtocolError(f"S_{t}({c}) overwrites S while the softmax may still read S_{t}({c - 1})")
-        state.mma_queue.append(("S", t, c))
-        commit(f"sready{t}")
+        if c >= 1 and len(state.s_read.get(c - 1, ())) != 4:
+            raise ProtocolError(f"S({c}) overwrites S while the softmax may still read S({c - 1})")
+        state.mma_queue.append(("S", 0, c))
+        commit("sready")
 
-    def issue_dp(t, c):
+    def issue_dp(c):
         landed(c)
-        if c >= 1 and ("DQ", t, c - 1) not in state.mma_done:
-            raise ProtocolError(f"dP_{t}({c}) overwrites dS_{t}({c - 1}) before dQ_{t}({c - 1}) completed")
-        state.mma_queue.append(("DP", t, c))
-        commit(f"dpready{t}")
+        if c >= 1 and ("DQ", 0, c - 1) not in state.mma_done:
+            raise ProtocolError(f"dP({c}) overwrites dS({c - 1}) before dQ({c - 1}) completed")
+        state.mma_queue.append(("DP", 0, c))
+        commit("dpready")
 
-    def issue_dq(t, c):
+    def issue_dq(c):
         landed(c)
-        if len(state.ds_stored.get((t, c), ())) != 4:
-            raise ProtocolError(f"dQ_{t}({c}) issued before all four warps stored dS")
-        state.mma_queue.append(("DQ", t, c))
-        state.dq_issued.add((t, c))
-        commit(f"dqdone{t}")
-        if t == 1:
-            commit(f"empty{c % k}")
+        if len(state.ds_stored.get(c, ())) != 4:
+            raise ProtocolError(f"dQ({c}) issued before all four warps stored dS")
+        state.mma_queue.append(("DQ", 0, c))
+        state.dq_issued.add(c)
+        commit("dqdone")
 
     def waits(name, completion):
         while not _wait(state, name, completion & 1, completion):
             yield ("wait", name)
 
     yield from waits("qfull", 0)
-    yield from waits(f"full{0}", 0)
-    for t in range(2):
-        issue_s(t, 0)
-    for t in range(2):
-        issue_dp(t, 0)
+    yield from waits("full0", 0)
+    issue_s(0)
+    issue_dp(0)
     yield ("step", None)
     for c in range(n):
         more = c + 1 < n
-        yield from waits("dsready0", c)
-        issue_dq(0, c)
-        yield ("step", None)
         if more:
+            yield from waits("sfree", c)
             yield from waits(f"full{(c + 1) % k}", (c + 1) // k)
-            issue_s(0, c + 1)
+            issue_s(c + 1)
             yield ("step", None)
-        yield from waits("dsready1", c)
-        issue_dq(1, c)
+        yield from waits("dsready", c)
+        issue_dq(c)
         yield ("step", None)
         if not more:
             break
-        issue_s(1, c + 1)
-        yield from waits("dqdone0", c)
-        issue_dp(0, c + 1)
-        yield ("step", None)
-        yield from waits("dqdone1", c)
-        issue_dp(1, c + 1)
+        yield from waits("dqdone", c)
+        state.bar(f"empty{c % k}").arrive()   # dQ(c), the stage's last reader, completed
+        issue_dp(c + 1)
         yield ("step", None)
     commit("drain")
     yield from waits("drain", 0)
 
 
-def dq_softmax(state, t, w):
+def dq_softmax(state, w):
     n = state.n_chunks
 
     def waits(name, completion):
@@ -368,46 +359,42 @@ def dq_softmax(state, t, w):
 
     for ch in range(n):
         if ch == LOCAL_CHUNKS:
-            yield from waits(f"dqdone{t}", LOCAL_CHUNKS - 1)
-            if ("DQ", t, LOCAL_CHUNKS - 1) not in state.mma_done or (t, LOCAL_CHUNKS) in state.dq_issued:
-                raise ProtocolError(f"dQ_l of tile {t} read outside its window")
-        yield from waits(f"sready{t}", ch)
-        if ("S", t, ch) not in state.mma_done:
-            raise ProtocolError(f"S_{t}({ch}) read before it completed")
+            yield from waits("dqdone", LOCAL_CHUNKS - 1)
+            if ("DQ", 0, LOCAL_CHUNKS - 1) not in state.mma_done or LOCAL_CHUNKS in state.dq_issued:
+                raise ProtocolError("dQ_l read outside its window")
+        yield from waits("sready", ch)
+        if ("S", 0, ch) not in state.mma_done:
+            raise ProtocolError(f"S({ch}) read before it completed")
+        state.s_read.setdefault(ch, set()).add(w)
+        state.bar("sfree").arrive()
         yield ("step", None)
-        yield from waits(f"dpready{t}", ch)
-        if ("DP", t, ch) not in state.mma_done:
-            raise ProtocolError(f"dP_{t}({ch}) read before it completed")
-        if ch >= 1 and ("DQ", t, ch - 1) not in state.mma_done:
-            raise ProtocolError(f"dS_{t}({ch}) overwrites dS_{t}({ch - 1}) while dQ_{t}({ch - 1}) may read it")
-        state.ds_stored.setdefault((t, ch), set()).add(w)
-        state.bar(f"dsready{t}").arrive()
+        yield from waits("dpready", ch)
+        if ("DP", 0, ch) not in state.mma_done:
+            raise ProtocolError(f"dP({ch}) read before it completed")
+        if ch >= 1 and ("DQ", 0, ch - 1) not in state.mma_done:
+            raise ProtocolError(f"dS({ch}) overwrites dS({ch - 1}) while dQ({ch - 1}) may read it")
+        state.ds_stored.setdefault(ch, set()).add(w)
+        state.bar("dsready").arrive()
         yield ("step", None)
-    yield from waits(f"dqdone{t}", n - 1)
-    if ("DQ", t, n - 1) not in state.mma_done:
-        raise ProtocolError(f"dQ of tile {t} read before the last product completed")
+    yield from waits("dqdone", n - 1)
+    if ("DQ", 0, n - 1) not in state.mma_done:
+        raise ProtocolError("dQ read before the last product completed")
 
 
 def run_dq(n_chunks=12, stages=3, seed=0, max_steps=400000):
     """Replay one random interleaving of the dQ kernel's protocol."""
     rng = random.Random(seed)
     state = State(n_chunks=n_chunks, stages=stages)
-    state.ds_stored, state.dq_issued = {}, set()
-    bars = {"qfull": 1, "drain": 1}
+    state.ds_stored, state.dq_issued, state.s_read = {}, set(), {}
+    bars = {"qfull": 1, "drain": 1, "sready": 1, "sfree": 4, "dpready": 1, "dsready": 4, "dqdone": 1}
     for s in range(4):
         bars[f"full{s}"] = 1
         bars[f"empty{s}"] = 1
-    for t in range(2):
-        bars[f"sready{t}"] = 1
-        bars[f"dpready{t}"] = 1
-        bars[f"dsready{t}"] = 4
-        bars[f"dqdone{t}"] = 1
     state.bars = {name: Barrier(name, cnt) for name, cnt in bars.items()}
     state.bar("qfull").arrive(tx=0)
     roles = {"producer": dq_producer(state), "mma": dq_mma(state)}
-    for t in range(2):
-        for w in range(4):
-            roles[f"softmax{t}{w}"] = dq_softmax(state, t, w)
+    for w in range(4):
+        roles[f"softmax{w}"] = dq_softmax(state, w)
     return _schedule(state, roles, rng, max_steps)
 
 
