@@ -181,6 +181,40 @@ P3D_API int p3d_attn_fwd_slab(const p3d_operator *op, const p3d_slab *slab, void
                       void *ol, void *og, float *lse_l, float *lse_g, unsigned flags, void *stream);
 
 /*
+ * The backward in stages, for callers that interleave communication between them (the
+ * z-slab sharding: mix -> halo exchange -> attention -> reduce-scatter of dsk, dsv ->
+ * pooling).  p3d_attn_bwd runs the same kernels in one call.
+ *
+ * p3d_bwd_mix (kernels.py:107-127 _mix_bwd): dol = dy*sl, dog = dy*gate*sg [B,H,N,D] (dtype),
+ *   delta_l/g = rowsum(dO*O) [B,H,N] fp32, dgate [B,H,N] (gate dtype), and dlocal_scale,
+ *   dglobal_scale [D] fp32 summed over op's rows.
+ * p3d_bwd_attn_slab (kernels.py:131-239 on one z-slab; no reference counterpart for the
+ *   slab form): op->q, dol, dog, lse_*, delta_* are this rank's rows; op->kl / op->vl and
+ *   q_halo, dol_halo, lse_l_halo, delta_l_halo hold the slab's halo planes (extents of
+ *   p3d_slab, as for p3d_attn_fwd_slab); sk, sv the gathered summaries.  Writes dq, dkl,
+ *   dvl for this rank's rows and dsk, dsv [B,G,slab->summaries,D] fp32: this rank's
+ *   queries' contribution to every summary's gradient.
+ * p3d_pool_bwd (kernels.py:243-272 _pool_bwd): the pooling VJP from fp32 dsk, dsv
+ *   [B,G,M,D]: dk, dv [B,G,N,D] (dtype) and dweight [D], dbias [V] fp32.
+ */
+P3D_API int p3d_bwd_mix(const p3d_operator *op, const void *dy, const void *ol, const void *og, void *dol, void *dog,
+                float *delta_l, float *delta_g, void *dgate, float *dlocal_scale, float *dglobal_scale,
+                void *workspace, size_t workspace_bytes, void *stream);
+P3D_API size_t p3d_bwd_mix_workspace(const p3d_operator *op);
+P3D_API int p3d_bwd_attn_slab(const p3d_operator *op, const p3d_slab *slab, const void *sk, const void *sv,
+                      const float *lse_l, const float *lse_g, const void *dol, const void *dog,
+                      const float *delta_l, const float *delta_g, const void *q_halo, const void *dol_halo,
+                      const float *lse_l_halo, const float *delta_l_halo, void *dq, void *dkl, void *dvl,
+                      float *dsk, float *dsv, void *workspace, size_t workspace_bytes, void *stream);
+P3D_API size_t p3d_bwd_attn_slab_workspace(const p3d_operator *op, const p3d_slab *slab);
+P3D_API int p3d_pool_bwd(const void *k, const void *v, const float *weight, const float *bias, const int32_t *blocks,
+                 int fine_blocks, int slots, int pool_size, const float *dsk, const float *dsv, void *dk, void *dv,
+                 float *dweight, float *dbias, int dtype, int batch, int kv_heads, int tokens, int head_dim,
+                 float temperature, void *workspace, size_t workspace_bytes, void *stream);
+P3D_API size_t p3d_pool_bwd_workspace(int fine_blocks, int slots, int pool_size, int batch, int kv_heads,
+                              int head_dim);
+
+/*
  * Forward (inference, no saved state) that allocates nothing and needs no workspace.
  * No counterpart in the reference.  For callers that cannot allocate device memory --
  * plugins inside a host framework that owns all device memory, or real-time loops that

@@ -73,6 +73,14 @@ _SIGNATURES = {
     "p3d_attn_bwd": (_c_int, [ctypes.POINTER(Operator), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                               _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "p3d_attn_bwd_workspace": (ctypes.c_size_t, [ctypes.POINTER(Operator)]),
+    "p3d_bwd_mix": (_c_int, [ctypes.POINTER(Operator)] + [_vp] * 10 + [_vp, ctypes.c_size_t, _vp]),
+    "p3d_bwd_mix_workspace": (ctypes.c_size_t, [ctypes.POINTER(Operator)]),
+    "p3d_bwd_attn_slab": (_c_int, [ctypes.POINTER(Operator), ctypes.POINTER(Slab)] + [_vp] * 17 +
+                          [_vp, ctypes.c_size_t, _vp]),
+    "p3d_bwd_attn_slab_workspace": (ctypes.c_size_t, [ctypes.POINTER(Operator), ctypes.POINTER(Slab)]),
+    "p3d_pool_bwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp,
+                              _c_int, _c_int, _c_int, _c_int, _c_int, _c_f32, _vp, ctypes.c_size_t, _vp]),
+    "p3d_pool_bwd_workspace": (ctypes.c_size_t, [_c_int] * 6),
 }
 
 _lock = threading.Lock()

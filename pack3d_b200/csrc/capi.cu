@@ -547,6 +547,12 @@ int p3d_attn_bwd(const p3d_operator *op, const void *dy, const void *sk, const v
     t.dq = dq;
     t.dkl = dkl;
     t.dvl = dvl;
+    t.q_halo = t.q;
+    t.dol_halo = t.dol;
+    t.lse_l_halo = lse_l;
+    t.delta_l_halo = b.delta_l;
+    t.x_z0 = 0;
+    t.x_planes = op->grid[0];
     if (int st = launch_stencil_bwd_dq(t, s)) return st;
     if (int st = launch_stencil_bwd_dkv(t, s)) return st;
   } else {
@@ -609,6 +615,248 @@ int p3d_attn_bwd(const p3d_operator *op, const void *dy, const void *sk, const v
   if (int st = launch_sum_rows(b.dsl_part, dlocal_scale, b.mix_rows, d, b.tmp, s)) return st;
   if (int st = launch_sum_rows(b.dsg_part, dglobal_scale, b.mix_rows, d, b.tmp, s)) return st;
   return P3D_OK;
+}
+
+
+// ------------------------------------------------------------------ staged backward
+// The backward in three stages, for callers that interleave their own communication:
+// the z-slab sharding runs mix -> (halo exchange) -> attention -> (reduce-scatter of the
+// summary gradients) -> pooling.  p3d_attn_bwd is the composition of the same kernels.
+
+static size_t mix_layout(const p3d_operator *op, void *base, size_t cap, float **dsl_part, float **dsg_part,
+                         float **tmp, int64_t *mix_rows) {
+  Carver c(base, cap);
+  const int chunk = mix_bwd_chunk_rows();
+  const int64_t bh = (int64_t)op->batch * op->heads;
+  *mix_rows = bh * ((op->tokens + chunk - 1) / chunk);
+  *dsl_part = c.take<float>(*mix_rows * op->head_dim);
+  *dsg_part = c.take<float>(*mix_rows * op->head_dim);
+  *tmp = c.take<float>(sum_rows_tmp(*mix_rows, op->head_dim));
+  return c.used;
+}
+
+size_t p3d_bwd_mix_workspace(const p3d_operator *op) {
+  if (validate(op) != P3D_OK) return 0;
+  float *a, *b, *t;
+  int64_t r;
+  return mix_layout(op, nullptr, 0, &a, &b, &t, &r);
+}
+
+int p3d_bwd_mix(const p3d_operator *op, const void *dy, const void *ol, const void *og, void *dol, void *dog,
+                float *delta_l, float *delta_g, void *dgate, float *dlocal_scale, float *dglobal_scale, void *workspace,
+                size_t workspace_bytes, void *stream) {
+  if (int st = validate(op)) return st;
+  P3D_CHECK_ARG(dy && ol && og && dol && dog && delta_l && delta_g && dgate && dlocal_scale && dglobal_scale,
+                "p3d_bwd_mix: null argument");
+  float *dsl_part, *dsg_part, *tmp;
+  int64_t mix_rows;
+  const size_t need = mix_layout(op, nullptr, 0, &dsl_part, &dsg_part, &tmp, &mix_rows);
+  if (!workspace || workspace_bytes < need)
+    return fail(P3D_ERR_WORKSPACE, "p3d_bwd_mix: workspace of %zu bytes required", need);
+  mix_layout(op, workspace, workspace_bytes, &dsl_part, &dsg_part, &tmp, &mix_rows);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  MixBwdArgs mix{};
+  mix.dtype = op->dtype;
+  mix.gate_dtype = op->gate_dtype;
+  mix.bh = op->batch * op->heads;
+  mix.tokens = op->tokens;
+  mix.head_dim = op->head_dim;
+  mix.chunk_rows = mix_bwd_chunk_rows();
+  mix.dy = dy;
+  mix.ol = ol;
+  mix.og = og;
+  mix.gate = op->gate;
+  mix.sl = op->local_scale;
+  mix.sg = op->global_scale;
+  mix.dol = dol;
+  mix.dog = dog;
+  mix.delta_l = delta_l;
+  mix.delta_g = delta_g;
+  mix.dgate = dgate;
+  mix.dsl_part = dsl_part;
+  mix.dsg_part = dsg_part;
+  if (int st = launch_mix_bwd(mix, s)) return st;
+  if (int st = launch_sum_rows(dsl_part, dlocal_scale, mix_rows, op->head_dim, tmp, s)) return st;
+  return launch_sum_rows(dsg_part, dglobal_scale, mix_rows, op->head_dim, tmp, s);
+}
+
+static int check_slab(const p3d_operator *op, const p3d_slab *slab, const char *what) {
+  P3D_CHECK_ARG(slab != nullptr, "%s: null slab", what);
+  P3D_CHECK_ARG(op->stencil && !op->raster_to_packed, "%s: needs a complete stencil in raster storage", what);
+  P3D_CHECK_ARG(!(op->options & P3D_OPT_INDEXED_ONLY), "%s: has no indexed form", what);
+  if (!stencil_fwd_supported(op->dtype, op->head_dim, op->radius, slab->summaries) || slab->summaries < 2 ||
+      !global_dkv_tc_supported(op->dtype, op->head_dim, slab->summaries))
+    return fail(P3D_ERR_UNSUPPORTED, "%s: needs bf16/f16, head_dim 16/32/48/64, radius 2, >= 2 summaries, sm_100",
+                what);
+  const int nz = op->grid[0], r = op->radius[0];
+  const int need_lo = std::max(0, slab->center_z0 - r);
+  const int need_hi = std::min(slab->global_planes, slab->center_z0 + nz + r);
+  P3D_CHECK_ARG(slab->global_planes >= 1 && slab->center_z0 >= 0 && slab->center_z0 + nz <= slab->global_planes,
+                "%s: rank planes [%d, %d) outside the volume of %d planes", what, slab->center_z0,
+                slab->center_z0 + nz, slab->global_planes);
+  P3D_CHECK_ARG(slab->halo_z0 <= need_lo && slab->halo_z0 + slab->halo_planes >= need_hi && slab->halo_z0 >= 0 &&
+                    slab->halo_z0 + slab->halo_planes <= slab->global_planes,
+                "%s: halo planes [%d, %d) do not cover [%d, %d)", what, slab->halo_z0,
+                slab->halo_z0 + slab->halo_planes, need_lo, need_hi);
+  return P3D_OK;
+}
+
+static size_t attn_slab_layout(const p3d_operator *op, int summaries, void *base, size_t cap, float **dk_part,
+                               float **dv_part, int *splits, int *per_split) {
+  Carver c(base, cap);
+  DeviceInfo info{};
+  if (device_info(&info) != P3D_OK) info.sm_count = 148;
+  global_dkv_tc_splits(op->batch, op->heads, op->kv_heads, op->tokens, summaries, info.sm_count, splits, per_split);
+  const int64_t n = (int64_t)op->batch * op->kv_heads * *splits * summaries * op->head_dim;
+  *dk_part = c.take<float>(n);
+  *dv_part = c.take<float>(n);
+  return c.used;
+}
+
+size_t p3d_bwd_attn_slab_workspace(const p3d_operator *op, const p3d_slab *slab) {
+  if (validate(op) != P3D_OK || !slab) return 0;
+  float *a, *b;
+  int sp, per;
+  return attn_slab_layout(op, slab->summaries, nullptr, 0, &a, &b, &sp, &per);
+}
+
+int p3d_bwd_attn_slab(const p3d_operator *op, const p3d_slab *slab, const void *sk, const void *sv,
+                      const float *lse_l, const float *lse_g, const void *dol, const void *dog, const float *delta_l,
+                      const float *delta_g, const void *q_halo, const void *dol_halo, const float *lse_l_halo,
+                      const float *delta_l_halo, void *dq, void *dkl, void *dvl, float *dsk, float *dsv,
+                      void *workspace, size_t workspace_bytes, void *stream) {
+  if (int st = validate(op)) return st;
+  if (int st = check_slab(op, slab, "p3d_bwd_attn_slab")) return st;
+  P3D_CHECK_ARG(sk && sv && lse_l && lse_g && dol && dog && delta_l && delta_g && q_halo && dol_halo && lse_l_halo &&
+                    delta_l_halo && dq && dkl && dvl && dsk && dsv,
+                "p3d_bwd_attn_slab: null argument");
+  float *dk_part, *dv_part;
+  int splits, per_split;
+  const size_t need = attn_slab_layout(op, slab->summaries, nullptr, 0, &dk_part, &dv_part, &splits, &per_split);
+  if (!workspace || workspace_bytes < need)
+    return fail(P3D_ERR_WORKSPACE, "p3d_bwd_attn_slab: workspace of %zu bytes required", need);
+  attn_slab_layout(op, slab->summaries, workspace, workspace_bytes, &dk_part, &dv_part, &splits, &per_split);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  StencilBwdArgs t{};
+  t.dtype = op->dtype;
+  t.batch = op->batch;
+  t.heads = op->heads;
+  t.kv_heads = op->kv_heads;
+  t.head_dim = op->head_dim;
+  t.summaries = slab->summaries;
+  for (int i = 0; i < 3; ++i) t.grid[i] = op->grid[i];
+  t.global_planes = slab->global_planes;
+  t.q_z0 = slab->center_z0;
+  t.k_z0 = slab->halo_z0;
+  t.k_planes = slab->halo_planes;
+  t.q = op->q;
+  t.kl = op->kl;
+  t.vl = op->vl;
+  t.dol = dol;
+  t.dog = dog;
+  t.sk = sk;
+  t.sv = sv;
+  t.lse_l = lse_l;
+  t.lse_g = lse_g;
+  t.delta_l = delta_l;
+  t.delta_g = delta_g;
+  t.raster_to_packed = nullptr;
+  t.dq = dq;
+  t.dkl = dkl;
+  t.dvl = dvl;
+  t.q_halo = q_halo;
+  t.dol_halo = dol_halo;
+  t.lse_l_halo = lse_l_halo;
+  t.delta_l_halo = delta_l_halo;
+  t.x_z0 = slab->halo_z0;
+  t.x_planes = slab->halo_planes;
+  if (int st = launch_stencil_bwd_dq(t, s)) return st;
+  if (int st = launch_stencil_bwd_dkv(t, s)) return st;
+  GlobalDkvArgs g{};
+  g.dtype = op->dtype;
+  g.batch = op->batch;
+  g.heads = op->heads;
+  g.kv_heads = op->kv_heads;
+  g.tokens = op->tokens;
+  g.head_dim = op->head_dim;
+  g.summaries = slab->summaries;
+  g.splits = splits;
+  g.per_split = per_split;
+  g.q = op->q;
+  g.dog = dog;
+  g.sk = sk;
+  g.sv = sv;
+  g.lse_g = lse_g;
+  g.delta_g = delta_g;
+  g.dk_part = dk_part;
+  g.dv_part = dv_part;
+  if (int st = launch_global_dkv_tc(g, s)) return st;
+  const int64_t bg = (int64_t)op->batch * op->kv_heads;
+  if (int st = launch_sum_middle(dk_part, dsk, bg, splits, (int64_t)slab->summaries * op->head_dim, s)) return st;
+  return launch_sum_middle(dv_part, dsv, bg, splits, (int64_t)slab->summaries * op->head_dim, s);
+}
+
+static size_t pool_bwd_layout(int64_t pool_rows, int dim, int slots, void *base, size_t cap, float **dw_part,
+                              float **db_part, float **tmp) {
+  Carver c(base, cap);
+  *dw_part = c.take<float>(pool_rows * dim);
+  *db_part = c.take<float>(pool_rows * slots);
+  *tmp = c.take<float>(std::max(sum_rows_tmp(pool_rows, dim), sum_rows_tmp(pool_rows, slots)));
+  return c.used;
+}
+
+size_t p3d_pool_bwd_workspace(int fine_blocks, int slots, int pool_size, int batch, int kv_heads, int head_dim) {
+  if (fine_blocks < 1 || slots < 1 || pool_size < 1 || batch < 1 || kv_heads < 1 || head_dim < 1) return 0;
+  const int64_t rows = (int64_t)batch * kv_heads * ((fine_blocks + pool_size - 1) / pool_size);
+  float *a, *b, *t;
+  return pool_bwd_layout(rows, head_dim, slots, nullptr, 0, &a, &b, &t);
+}
+
+int p3d_pool_bwd(const void *k, const void *v, const float *weight, const float *bias, const int32_t *blocks,
+                 int fine_blocks, int slots, int pool_size, const float *dsk, const float *dsv, void *dk, void *dv,
+                 float *dweight, float *dbias, int dtype, int batch, int kv_heads, int tokens, int head_dim,
+                 float temperature, void *workspace, size_t workspace_bytes, void *stream) {
+  P3D_CHECK_ARG(dtype_ok(dtype), "p3d_pool_bwd: unknown dtype");
+  P3D_CHECK_ARG(k && v && weight && bias && blocks && dsk && dsv && dk && dv && dweight && dbias,
+                "p3d_pool_bwd: null pointer");
+  P3D_CHECK_ARG(fine_blocks >= 1 && slots >= 1 && slots <= 64 && pool_size >= 1 && pool_size <= 32,
+                "p3d_pool_bwd: bad blocks description");
+  P3D_CHECK_ARG(batch >= 1 && kv_heads >= 1 && tokens >= 1 && head_dim >= 2 && head_dim <= 128,
+                "p3d_pool_bwd: bad extents");
+  P3D_CHECK_ARG(temperature > 0.f && temperature < __builtin_huge_valf(), "p3d_pool_bwd: bad temperature");
+  const int M = (fine_blocks + pool_size - 1) / pool_size;
+  const int64_t rows = (int64_t)batch * kv_heads * M;
+  float *dw_part, *db_part, *tmp;
+  const size_t need = pool_bwd_layout(rows, head_dim, slots, nullptr, 0, &dw_part, &db_part, &tmp);
+  if (!workspace || workspace_bytes < need)
+    return fail(P3D_ERR_WORKSPACE, "p3d_pool_bwd: workspace of %zu bytes required", need);
+  pool_bwd_layout(rows, head_dim, slots, workspace, workspace_bytes, &dw_part, &db_part, &tmp);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  PoolBwdArgs pb{};
+  pb.k = k;
+  pb.v = v;
+  pb.weight = weight;
+  pb.bias = bias;
+  pb.blocks = blocks;
+  pb.fine_blocks = fine_blocks;
+  pb.slots = slots;
+  pb.pool_size = pool_size;
+  pb.summaries = M;
+  pb.dsk = dsk;
+  pb.dsv = dsv;
+  pb.dk = dk;
+  pb.dv = dv;
+  pb.dw_part = dw_part;
+  pb.db_part = db_part;
+  pb.dtype = dtype;
+  pb.bg = batch * kv_heads;
+  pb.tokens = tokens;
+  pb.head_dim = head_dim;
+  pb.temperature = temperature;
+  pb.vec = dtype_size(dtype) == 2 && head_dim % 8 == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0;
+  if (int st = launch_pool_bwd(pb, s)) return st;
+  if (int st = launch_sum_rows(dw_part, dweight, rows, head_dim, tmp, s)) return st;
+  return launch_sum_rows(db_part, dbias, rows, slots, tmp, s);
 }
 
 }  // extern "C"

@@ -124,6 +124,11 @@ struct StencilBwdArgs {
   const int32_t *raster_to_packed;      // row map of lse / delta / outputs (NULL = raster)
   void *dq;                             // [B,H,N,D] in the layout's row order
   void *dkl, *dvl;                      // [B,G,N,D] in the layout's row order
+  // query-side buffers of the local dK / dV (whole volume: the centre buffers, x_z0 = 0,
+  // x_planes = grid[0]; a z-slab: the rank's planes plus the neighbours' halo planes)
+  const void *q_halo, *dol_halo;
+  const float *lse_l_halo, *delta_l_halo;
+  int x_z0, x_planes;
 };
 int launch_stencil_bwd_dq(const StencilBwdArgs &a, cudaStream_t s);
 int launch_stencil_bwd_dkv(const StencilBwdArgs &a, cudaStream_t s);

@@ -927,11 +927,14 @@ struct LkvCfg {
 };
 
 struct LkvParams {
-  int Z, Y, X, tiles_z, tiles_y, tiles_x;
+  int Z, Y, X, tiles_z, tiles_y, tiles_x;  // Z: planes of the key (centre) buffer
+  int Zg, cz0, kz0;      // global planes; global z of the first key plane and of kl / vl plane 0
+  int xz0;               // global z of plane 0 of the query-side buffers (q, dO_l, lse_l, Delta_l)
   int heads, kv_heads, rep;
-  int64_t tokens;
+  int64_t tokens;        // rows of the key buffer's grid (outputs)
+  int64_t xtokens;       // rows of the query-side buffers per (batch, head)
   float sc, inv_sqrt_d;
-  const float *lse_l, *delta_l;  // [B*H, N] in the layout's row order
+  const float *lse_l, *delta_l;  // [B*H, xtokens] in the layout's row order
   const int32_t *map;            // raster -> packed rows (nullptr: raster)
   void *dkl, *dvl;               // [B*G, N, D] in the layout's row order
 };
@@ -994,15 +997,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = tmem_holder;
   // chunk c: query head b*H + g*rep + c/8, query plane z0 - 2 + c%8
   auto chunk_head = [&](int c) { return b * p.heads + g * p.rep + c / kLocalChunks; };
-  auto chunk_plane = [&](int c) { return z0 - kR + c % kLocalChunks; };
+  auto chunk_plane = [&](int c) { return p.cz0 + z0 - kR + c % kLocalChunks; };  // global z
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ producer (whole warp)
     if (lane == 0) {
       mbar_expect_tx(bar(kGKvFull), 2 * C::kTileBytes);
       for (int c = 0; c < C::kK; ++c) {
-        tma_load_5d(k_smem + c * C::kBoxT, &tkl, bar(kGKvFull), 16 * c, x0, y0, z0, bg);
-        tma_load_5d(v_smem + c * C::kBoxT, &tvl, bar(kGKvFull), 16 * c, x0, y0, z0, bg);
+        tma_load_5d(k_smem + c * C::kBoxT, &tkl, bar(kGKvFull), 16 * c, x0, y0, p.cz0 + z0 - p.kz0, bg);
+        tma_load_5d(v_smem + c * C::kBoxT, &tvl, bar(kGKvFull), 16 * c, x0, y0, p.cz0 + z0 - p.kz0, bg);
       }
     }
     int issued = 0;
@@ -1018,8 +1021,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         mbar_expect_tx(full, 2 * C::kPlaneBytes);
         for (int c = 0; c < C::kK; ++c) {
-          tma_load_5d(stage + c * C::kBoxP, &tq, full, 16 * c, x0 - kR, y0 - kR, zp, bh);
-          tma_load_5d(stage + C::kPlaneBytes + c * C::kBoxP, &tdo, full, 16 * c, x0 - kR, y0 - kR, zp, bh);
+          tma_load_5d(stage + c * C::kBoxP, &tq, full, 16 * c, x0 - kR, y0 - kR, zp - p.xz0, bh);
+          tma_load_5d(stage + C::kPlaneBytes + c * C::kBoxP, &tdo, full, 16 * c, x0 - kR, y0 - kR, zp - p.xz0,
+                      bh);
         }
       }
       // lse (as log2) and Delta of the plane's 96 queries; +inf outside the volume (P = 0).
@@ -1030,13 +1034,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; k < kKeys / 32; ++k) {
         const int j = lane + 32 * k;
         const int qy = y0 - kR + j / kHX, qx = x0 - kR + j % kHX;
-        const bool in = zp >= 0 && zp < p.Z && qy >= 0 && qy < p.Y && qx >= 0 && qx < p.X;
+        const bool in = zp >= 0 && zp < p.Zg && qy >= 0 && qy < p.Y && qx >= 0 && qx < p.X;
         l[k] = __builtin_huge_valf();
         dl[k] = 0.f;
         if (in) {
-          int64_t r = ((int64_t)zp * p.Y + qy) * p.X + qx;
+          int64_t r = ((int64_t)(zp - p.xz0) * p.Y + qy) * p.X + qx;
           if (p.map) r = __ldg(p.map + r);
-          const int64_t row = (int64_t)bh * p.tokens + r;
+          const int64_t row = (int64_t)bh * p.xtokens + r;
           l[k] = __ldg(p.lse_l + row) * kLog2e;
           dl[k] = __ldg(p.delta_l + row);
         }
@@ -1139,7 +1143,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = wait_warp(kGSReady, ch);
       if (!ok) break;
       const int zp = chunk_plane(ch);
-      const bool active = (unsigned)(zp - kz + kR) <= 2u * kR;  // warp-uniform
+      const bool active = (unsigned)(zp - (p.cz0 + kz) + kR) <= 2u * kR;  // warp-uniform
       const float *vals = reinterpret_cast<const float *>(ring_ptr + (size_t)(ch % C::kStages) * C::kStageBytes +
                                                           2 * C::kPlaneBytes);
       uint32_t pw[3][8], dw[3][8];
@@ -1225,18 +1229,20 @@ int launch_lkv_t(const StencilBwdArgs &a, cudaStream_t stream) {
   const uint64_t bh = (uint64_t)a.batch * a.heads, bgs = (uint64_t)a.batch * a.kv_heads;
   CUtensorMap tkl, tvl, tq, tdo;
   {
-    const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)Z, bgs};
-    const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es, (uint64_t)Z * Y * X * D * es};
+    const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)a.k_planes, bgs};
+    const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es,
+                                 (uint64_t)a.k_planes * Y * X * D * es};
     const uint32_t box[5] = {16, kTX, kTY, kTZ, 1};
     if (int st = encode_operand(&tkl, a.dtype, a.kl, 5, dims, strides, box)) return st;
     if (int st = encode_operand(&tvl, a.dtype, a.vl, 5, dims, strides, box)) return st;
   }
   {
-    const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)Z, bh};
-    const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es, (uint64_t)Z * Y * X * D * es};
+    const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)a.x_planes, bh};
+    const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es,
+                                 (uint64_t)a.x_planes * Y * X * D * es};
     const uint32_t box[5] = {16, kHX, kHY, 1, 1};
-    if (int st = encode_operand(&tq, a.dtype, a.q, 5, dims, strides, box)) return st;
-    if (int st = encode_operand(&tdo, a.dtype, a.dol, 5, dims, strides, box)) return st;
+    if (int st = encode_operand(&tq, a.dtype, a.q_halo, 5, dims, strides, box)) return st;
+    if (int st = encode_operand(&tdo, a.dtype, a.dol_halo, 5, dims, strides, box)) return st;
   }
   LkvParams p{};
   p.Z = Z;
@@ -1249,10 +1255,15 @@ int launch_lkv_t(const StencilBwdArgs &a, cudaStream_t stream) {
   p.kv_heads = a.kv_heads;
   p.rep = a.heads / a.kv_heads;
   p.tokens = (int64_t)Z * Y * X;
+  p.Zg = a.global_planes;
+  p.cz0 = a.q_z0;
+  p.kz0 = a.k_z0;
+  p.xz0 = a.x_z0;
+  p.xtokens = (int64_t)a.x_planes * Y * X;
   p.sc = kLog2e / sqrtf((float)D);
   p.inv_sqrt_d = 1.f / sqrtf((float)D);
-  p.lse_l = a.lse_l;
-  p.delta_l = a.delta_l;
+  p.lse_l = a.lse_l_halo;
+  p.delta_l = a.delta_l_halo;
   p.map = a.raster_to_packed;
   p.dkl = a.dkl;
   p.dvl = a.dvl;

@@ -233,11 +233,10 @@ def sharded_layer_forward(layer, x, layout: SlabLayout, group=None):
     ``x`` [B, rank tokens, dim] holds this rank's tokens in raster order.  LayerNorm,
     projections, gate and output projection are per token and run locally; RoPE uses the
     global coordinates; the attention core runs sharded (``sharded_core_forward``).
-    Inference only: the sharded backward is not provided.
+    Differentiable: the core's backward is sharded (``sharded_core_backward``); parameter
+    gradients are this rank's share, to be summed over ranks like any replicated layer's.
     """
     from .rope import balanced_pairs, rotate_projections
-    if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in layer.parameters())):
-        raise NotImplementedError("the sharded layer runs inference only; wrap the call in torch.no_grad()")
     layout.check_unmodified()
     if layer.position_encoding != "axial":
         raise ValueError("the sharded layer supports axial position encoding only")
@@ -250,7 +249,178 @@ def sharded_layer_forward(layer, x, layout: SlabLayout, group=None):
     kl, vl, kg, vg = (t.reshape(b, n, g, d).transpose(1, 2) for t in layer.to_kv(xn).chunk(4, -1))
     q, kl, kg = rotate_projections(q, kl, kg, layout.coords, balanced_pairs(d), layout.grid_shape, packed=False)
     gate = layer.gate(xn).reshape(b, n, h, 2).softmax(-1)[..., 1].transpose(1, 2).contiguous()
-    y = sharded_core_forward(q, kl, vl.contiguous(), kg, vg.contiguous(), layer.pool_weight, layer.slot_bias, gate,
-                             layer.local_scale, layer.global_scale, layout.geometry, layout.slabs, group,
-                             layer.temperature)
+    args = (q, kl, vl.contiguous(), kg, vg.contiguous(), layer.pool_weight, layer.slot_bias, gate, layer.local_scale,
+            layer.global_scale, layout.geometry, layout.slabs, group, layer.temperature)
+    if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in layer.parameters())):
+        y = sharded_core(*args)
+    else:
+        y = sharded_core_forward(*args)
     return x + layer.to_out(y.transpose(1, 2).reshape(b, n, -1))
+
+
+# ----------------------------------------------------------------------------- backward
+#
+# Backward of the attention core on one rank (``sharded_core_backward``):
+#
+# 1. mix backward of the rank's rows (``p3d_bwd_mix``): dO_l, dO_g, Delta_l, Delta_g, the
+#    gate gradient and the rank's share of the branch-scale gradients;
+# 2. exchange halo planes of q, dO_l, lse_l and Delta_l: the local dK / dV of a key is
+#    computed by the key's owner from every query that attends to it, including the
+#    neighbours' (no dK / dV is sent back);
+# 3. dQ, local dK / dV and the rank's contribution to every summary gradient
+#    (``p3d_bwd_attn_slab``);
+# 4. reduce-scatter the summary gradients to the ranks that own the summaries;
+# 5. pooling backward of the rank's own summaries (``p3d_pool_bwd``).
+#
+# Parameter gradients (pooling weight and bias, branch scales) are this rank's
+# contributions, as for any layer whose parameters are replicated: the caller sums them
+# over ranks with its other parameter gradients.
+
+def _workspace(nbytes, device):
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def slab_mix_backward(dy, q, kl, vl, kg, vg, weight, bias, gate, sl, sg, ol, og, geometry, temperature=1.0):
+    """Stage 1 on one rank: ``(dol, dog, delta_l, delta_g, dgate, dsl, dsg)``."""
+    b, h, n, d = q.shape
+    gate_k = _as_gate(gate, q).contiguous()
+    w32, b32, sl32, sg32 = (_f32(t) for t in (weight, bias, sl, sg))
+    op, keep = _operator(q, kl, vl, kg, vg, w32, b32, gate_k, sl32, sg32, geometry, temperature)
+    dol, dog = torch.empty_like(q), torch.empty_like(q)
+    f32 = dict(dtype=torch.float32, device=q.device)
+    delta_l, delta_g = torch.empty((b, h, n), **f32), torch.empty((b, h, n), **f32)
+    dgate = torch.empty_like(gate_k)
+    dsl, dsg = torch.empty(d, **f32), torch.empty(d, **f32)
+    lib = _native.lib()
+    ws = _workspace(lib.p3d_bwd_mix_workspace(op), q.device)
+    with torch.cuda.device(q.device):
+        status = lib.p3d_bwd_mix(op, _native.ptr(dy), _native.ptr(ol), _native.ptr(og), _native.ptr(dol),
+                                 _native.ptr(dog), _native.ptr(delta_l), _native.ptr(delta_g), _native.ptr(dgate),
+                                 _native.ptr(dsl), _native.ptr(dsg), _native.ptr(ws), ws.numel(),
+                                 _native.stream_of(q.device))
+    _native.check(status, "p3d_bwd_mix")
+    del keep
+    return dol, dog, delta_l, delta_g, dgate, dsl, dsg
+
+
+def slab_attention_backward(q, kl_ext, vl_ext, sk, sv, lse_l, lse_g, dol, dog, delta_l, delta_g, q_ext, dol_ext,
+                            lse_l_ext, delta_l_ext, weight, bias, gate, sl, sg, geometry, slabs: ZSlabs,
+                            temperature=1.0):
+    """Stage 3 on one rank: ``(dq, dkl, dvl, dsk, dsv)``; dsk, dsv [B, G, M_all, D] fp32."""
+    b, h, n, d = q.shape
+    g = kl_ext.shape[1]
+    gate_k = _as_gate(gate, q).contiguous()
+    w32, b32, sl32, sg32 = (_f32(t) for t in (weight, bias, sl, sg))
+    op, keep = _operator(q, kl_ext, vl_ext, kl_ext, vl_ext, w32, b32, gate_k, sl32, sg32, geometry, temperature)
+    slab = _native.Slab(slabs.grid[0], slabs.z0, slabs.halo_z0, slabs.halo_planes, sk.shape[2])
+    dq = torch.empty_like(q)
+    dkl = torch.empty((b, g, n, d), dtype=q.dtype, device=q.device)
+    dvl = torch.empty_like(dkl)
+    dsk = torch.empty((b, g, sk.shape[2], d), dtype=torch.float32, device=q.device)
+    dsv = torch.empty_like(dsk)
+    lib = _native.lib()
+    ws = _workspace(lib.p3d_bwd_attn_slab_workspace(op, ctypes.byref(slab)), q.device)
+    args = [sk, sv, lse_l, lse_g, dol, dog, delta_l, delta_g, q_ext, dol_ext, lse_l_ext, delta_l_ext, dq, dkl, dvl,
+            dsk, dsv]
+    with torch.cuda.device(q.device):
+        status = lib.p3d_bwd_attn_slab(op, ctypes.byref(slab), *[_native.ptr(t) for t in args], _native.ptr(ws),
+                                       ws.numel(), _native.stream_of(q.device))
+    _native.check(status, "p3d_bwd_attn_slab")
+    del keep
+    return dq, dkl, dvl, dsk, dsv
+
+
+def slab_pool_backward(kg, vg, weight, bias, geometry, dsk, dsv, temperature=1.0):
+    """Stage 5 on one rank: ``(dkg, dvg, dweight, dbias)`` from its summaries' gradients."""
+    b, g, n, d = kg.shape
+    tables = _device_tables(geometry, kg.device)
+    fine, slots = geometry.blocks.shape
+    dkg, dvg = torch.empty_like(kg), torch.empty_like(vg)
+    f32 = dict(dtype=torch.float32, device=kg.device)
+    dw, db = torch.empty(d, **f32), torch.empty(slots, **f32)
+    w32, b32 = _f32(weight), _f32(bias)
+    # bound to names: a temporary whose pointer alone is passed is freed (and its block reused) before the launch
+    dsk, dsv = dsk.contiguous(), dsv.contiguous()
+    lib = _native.lib()
+    ws = _workspace(lib.p3d_pool_bwd_workspace(fine, slots, geometry.pool_size, b, g, d), kg.device)
+    with torch.cuda.device(kg.device):
+        status = lib.p3d_pool_bwd(_native.ptr(kg), _native.ptr(vg), _native.ptr(w32), _native.ptr(b32),
+                                  _native.ptr(tables["blocks"]), fine, slots, geometry.pool_size,
+                                  _native.ptr(dsk), _native.ptr(dsv), _native.ptr(dkg),
+                                  _native.ptr(dvg), _native.ptr(dw), _native.ptr(db), _native.DTYPE_CODE[kg.dtype], b,
+                                  g, n, d, float(temperature), _native.ptr(ws), ws.numel(),
+                                  _native.stream_of(kg.device))
+    _native.check(status, "p3d_pool_bwd")
+    return dkg, dvg, dw, db
+
+
+def scatter_summary_grads(ds, group=None):
+    """Sum ``ds`` [B, G, world*M_rank, D] over ranks; each rank keeps its own M_rank rows."""
+    world = dist.get_world_size(group)
+    if world == 1:
+        return ds.contiguous()
+    b, g, m_all, d = ds.shape
+    m = m_all // world
+    chunks = ds.reshape(b, g, world, m, d).permute(2, 0, 1, 3, 4).contiguous()
+    out = torch.empty((b, g, m, d), dtype=ds.dtype, device=ds.device)
+    if dist.get_backend(group) == "nccl":
+        dist.reduce_scatter_tensor(out, chunks.reshape(-1), group=group)
+    else:   # gloo has no reduce-scatter: all-reduce, keep this rank's part
+        dist.all_reduce(chunks, group=group)
+        out.copy_(chunks[dist.get_rank(group)])
+    return out
+
+
+def _exchange_rows(t, slabs, group):
+    """Halo exchange of a per-row tensor [B, H, N] (lse, Delta)."""
+    return exchange_halos(t.unsqueeze(-1).contiguous(), slabs, group).squeeze(-1)
+
+
+class _ShardedCore(torch.autograd.Function):
+    """The sharded attention core with its sharded backward (first order)."""
+
+    @staticmethod
+    def forward(ctx, q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, slabs, group, temperature):
+        q, kl, vl, kg, vg, gate = (t.contiguous() for t in (q, kl, vl, kg, vg, gate))
+        sk_rank, sv_rank = pool_summaries(kg, vg, weight, bias, geometry, temperature)
+        sk, sv = gather_summaries(sk_rank, group), gather_summaries(sv_rank, group)
+        kl_ext, vl_ext = exchange_halos(kl, slabs, group), exchange_halos(vl, slabs, group)
+        y, state = slab_forward(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, geometry, slabs, temperature,
+                                save_state=True)
+        _, _, ol, og, lse_l, lse_g = state
+        ctx.save_for_backward(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, kl_ext, vl_ext, sk, sv, ol, og, lse_l,
+                              lse_g)
+        ctx.geometry, ctx.slabs, ctx.group, ctx.temperature = geometry, slabs, group, temperature
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (q, kl, vl, kg, vg, weight, bias, gate, sl, sg, kl_ext, vl_ext, sk, sv, ol, og, lse_l,
+         lse_g) = ctx.saved_tensors
+        grads = sharded_core_backward(dy.contiguous(), (q, kl, vl, kg, vg, weight, bias, gate, sl, sg),
+                                      (kl_ext, vl_ext, sk, sv, ol, og, lse_l, lse_g), ctx.geometry, ctx.slabs,
+                                      ctx.group, ctx.temperature)
+        return (*grads, None, None, None, None)
+
+
+def sharded_core_backward(dy, inputs, saved, geometry, slabs: ZSlabs, group=None, temperature=1.0):
+    """All ten input gradients of this rank's core (parameter gradients: this rank's share)."""
+    q, kl, vl, kg, vg, weight, bias, gate, sl, sg = inputs
+    kl_ext, vl_ext, sk, sv, ol, og, lse_l, lse_g = saved
+    dol, dog, delta_l, delta_g, dgate, dsl, dsg = slab_mix_backward(dy, q, kl, vl, kg, vg, weight, bias, gate, sl,
+                                                                    sg, ol, og, geometry, temperature)
+    q_ext, dol_ext = exchange_halos(q, slabs, group), exchange_halos(dol, slabs, group)
+    lse_l_ext, delta_l_ext = _exchange_rows(lse_l, slabs, group), _exchange_rows(delta_l, slabs, group)
+    dq, dkl, dvl, dsk, dsv = slab_attention_backward(q, kl_ext, vl_ext, sk, sv, lse_l, lse_g, dol, dog, delta_l,
+                                                     delta_g, q_ext, dol_ext, lse_l_ext, delta_l_ext, weight, bias,
+                                                     gate, sl, sg, geometry, slabs, temperature)
+    dsk_rank, dsv_rank = scatter_summary_grads(dsk, group), scatter_summary_grads(dsv, group)
+    dkg, dvg, dw, db = slab_pool_backward(kg, vg, weight, bias, geometry, dsk_rank, dsv_rank, temperature)
+    return (dq, dkl, dvl, dkg, dvg, dw.to(weight.dtype), db.to(bias.dtype), dgate.to(gate.dtype), dsl.to(sl.dtype),
+            dsg.to(sg.dtype))
+
+
+def sharded_core(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, slabs: ZSlabs, group=None, temperature=1.0):
+    """This rank's attention core output; differentiable (sharded backward)."""
+    return _ShardedCore.apply(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, slabs, group,
+                              float(temperature))

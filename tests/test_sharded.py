@@ -165,3 +165,136 @@ def test_sharded_forward_over_nccl():
         lo, hi = s.token_range()
         assert errors == 0
         assert (y.float() - y_full[:, :, lo:hi].float().cpu()).abs().max().item() <= 2e-2, rank
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4])
+def test_slab_backward_matches_the_whole_volume(cuda_device, world):
+    """Every stage of the sharded backward, ranks emulated in turn (exchanges = slices)."""
+    from cases import upstream
+    from pack3d_b200 import _native
+    from pack3d_b200 import ops as p3d_ops
+    from pack3d_b200.sharded import (pool_summaries, slab_attention_backward, slab_forward, slab_mix_backward,
+                                     slab_pool_backward)
+    grid = (32, 16, 24)
+    layout, inputs = _case(grid, torch.bfloat16, 12)
+    dev = [t.to(cuda_device) for t in inputs]
+    geom = layout.geometry.to(cuda_device)
+    n = layout.geometry.num_tokens
+    dy = upstream((1, 4, n, 48), torch.bfloat16, 12).to(cuda_device)
+    _, saved = p3d_ops.forward(*dev, geom, 1.0, save_state=True)
+    want = p3d_ops.backward(dy, dev, saved, geom, 1.0)
+
+    slabs = [ZSlabs(grid, world, r) for r in range(world)]
+    geoms = [slab_layout(grid, slabs=s).to(cuda_device).geometry for s in slabs]
+    parts = [_slab_inputs(dev, s) for s in slabs]
+    pooled = [pool_summaries(p[3], p[4], p[5], p[6], g) for p, g in zip(parts, geoms)]
+    sk = torch.cat([p[0] for p in pooled], dim=2)
+    sv = torch.cat([p[1] for p in pooled], dim=2)
+    fwd, mix = [], []
+    for s, g, p in zip(slabs, geoms, parts):
+        q, kl_ext, vl_ext, kg, vg, weight, bias, gate, sl, sg = p
+        _, state = slab_forward(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, g, s, save_state=True)
+        lo, hi = s.token_range()
+        pt = s.plane_tokens
+        kl_c = kl_ext[:, :, s.halo_lo * pt:(s.halo_lo + s.planes) * pt].contiguous()
+        vl_c = vl_ext[:, :, s.halo_lo * pt:(s.halo_lo + s.planes) * pt].contiguous()
+        fwd.append(state)
+        mix.append(slab_mix_backward(dy[:, :, lo:hi].contiguous(), q, kl_c, vl_c, kg, vg, weight, bias, gate, sl, sg,
+                                     state[2], state[3], g))
+    # the exchanged halos, assembled from every rank's rows
+    cat = lambda i: torch.cat([m[i] for m in mix], dim=2)  # noqa: E731
+    dol_all, delta_l_all = cat(0), cat(2)
+    q_all = dev[0]
+    lse_l_all = torch.cat([f[4] for f in fwd], dim=2)
+    dsk_sum = dsv_sum = 0
+    per_rank = []
+    for s, g, p, f, m in zip(slabs, geoms, parts, fwd, mix):
+        q, kl_ext, vl_ext, kg, vg, weight, bias, gate, sl, sg = p
+        pt = s.plane_tokens
+        ext = slice(s.halo_z0 * pt, (s.halo_z0 + s.halo_planes) * pt)
+        dq, dkl, dvl, dsk, dsv = slab_attention_backward(
+            q, kl_ext, vl_ext, sk, sv, f[4], f[5], m[0], m[1], m[2], m[3], q_all[:, :, ext].contiguous(),
+            dol_all[:, :, ext].contiguous(), lse_l_all[:, :, ext].contiguous(), delta_l_all[:, :, ext].contiguous(),
+            weight, bias, gate, sl, sg, g, s)
+        dsk_sum, dsv_sum = dsk_sum + dsk, dsv_sum + dsv
+        per_rank.append((dq, dkl, dvl))
+    m_rank = sk.shape[2] // world
+    dw_sum = db_sum = dsl_sum = dsg_sum = 0
+    tol = lambda t: 2e-2 * max(1.0, t.float().abs().max().item())  # noqa: E731
+    for r, (s, g, p, m) in enumerate(zip(slabs, geoms, parts, mix)):
+        lo, hi = s.token_range()
+        rows = slice(r * m_rank, (r + 1) * m_rank)
+        dkg, dvg, dw, db = slab_pool_backward(p[3], p[4], p[5], p[6], g, dsk_sum[:, :, rows], dsv_sum[:, :, rows])
+        dq, dkl, dvl = per_rank[r]
+        for name, got, ref in (("dq", dq, want[0]), ("dkl", dkl, want[1]), ("dvl", dvl, want[2]),
+                               ("dkg", dkg, want[3]), ("dvg", dvg, want[4]), ("dgate", m[4], want[7])):
+            ref = ref[:, :, lo:hi]
+            assert (got.float() - ref.float()).abs().max().item() <= tol(ref), (name, r)
+        dw_sum, db_sum = dw_sum + dw, db_sum + db
+        dsl_sum, dsg_sum = dsl_sum + m[5], dsg_sum + m[6]
+    for name, got, ref in (("dweight", dw_sum, want[5]), ("dbias", db_sum, want[6]), ("dsl", dsl_sum, want[8]),
+                           ("dsg", dsg_sum, want[9])):
+        assert (got.float() - ref.float()).abs().max().item() <= tol(ref) + 1e-3, name
+    assert _native.device_errors() == 0
+
+
+def _train_worker(rank, world, port, grid, out):
+    from pack3d_b200 import PACK3DAttention, _native
+    from pack3d_b200.sharded import sharded_layer_forward
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=dev, timeout=datetime.timedelta(seconds=60))
+    try:
+        torch.manual_seed(0)
+        layer = PACK3DAttention(192, heads=4, kv_heads=4, head_dim=48, block_volume=64).to(dev, torch.bfloat16)
+        n = grid[0] * grid[1] * grid[2]
+        gen = torch.Generator().manual_seed(5)
+        x_full = torch.randn(1, n, 192, generator=gen).to(torch.bfloat16)
+        dy_full = torch.randn(1, n, 192, generator=gen).to(torch.bfloat16)
+        s = ZSlabs(grid, world, rank)
+        lay = slab_layout(grid, slabs=s).to(dev)
+        lo, hi = s.token_range()
+        x = x_full[:, lo:hi].to(dev).requires_grad_()
+        y = sharded_layer_forward(layer, x, lay)
+        y.backward(dy_full[:, lo:hi].to(dev))
+        for p in layer.parameters():            # replicated parameters: sum the ranks' shares
+            dist.all_reduce(p.grad)
+        torch.cuda.synchronize(dev)
+        out[rank] = (y.detach().cpu(), x.grad.cpu(), {k: p.grad.cpu() for k, p in layer.named_parameters()},
+                     _native.device_errors())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_sharded_training_step_over_nccl():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from pack3d_b200 import PACK3DAttention, build_layout
+    world, grid = 2, (32, 16, 24)
+    with mp.get_context("spawn").Manager() as manager:
+        out = manager.dict()
+        mp.spawn(_train_worker, args=(world, _free_port(), grid, out), nprocs=world, join=True)
+        results = dict(out)
+    dev = torch.device("cuda", 0)
+    layout = build_layout(grid, (4, 4, 4), radius=2, pool_size=1)
+    layout = layout.repack(layout.order.argsort()).to(dev)
+    torch.manual_seed(0)
+    layer = PACK3DAttention(192, heads=4, kv_heads=4, head_dim=48, block_volume=64).to(dev, torch.bfloat16)
+    n = grid[0] * grid[1] * grid[2]
+    gen = torch.Generator().manual_seed(5)
+    x = torch.randn(1, n, 192, generator=gen).to(torch.bfloat16).to(dev).requires_grad_()
+    dy = torch.randn(1, n, 192, generator=gen).to(torch.bfloat16).to(dev)
+    y = layer(x, layout)
+    y.backward(dy)
+    tol = lambda t: 2e-2 * max(1.0, t.float().abs().max().item())  # noqa: E731
+    for rank in range(world):
+        y_r, dx_r, grads, errors = results[rank]
+        lo, hi = ZSlabs(grid, world, rank).token_range()
+        assert errors == 0
+        assert (y_r.float() - y[:, lo:hi].detach().float().cpu()).abs().max().item() <= tol(y)
+        assert (dx_r.float() - x.grad[:, lo:hi].float().cpu()).abs().max().item() <= tol(x.grad), rank
+        for name, p in layer.named_parameters():
+            assert (grads[name].float() - p.grad.float().cpu()).abs().max().item() <= tol(p.grad), (name, rank)
