@@ -173,30 +173,37 @@ template <int N, bool BF16>
 __device__ __forceinline__ float exp_store(const float *s, float m, float sc, uint32_t t_p) {
   static_assert(N % 32 == 0, "N must be a multiple of 32");
   const float msc = (m == kNegInf) ? 0.f : m * sc;
-  float sum[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums: no serial add chain
+  const float2 sc2 = make_float2(sc, sc), nmsc2 = make_float2(-msc, -msc);
+  float2 sum[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // independent partial sums
 #pragma unroll
   for (int g = 0; g < N / 32; ++g) {
     uint32_t pk[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float p0 = ex2_approx(fmaf(s[32 * g + 2 * i], sc, -msc));
-      const float p1 = ex2_approx(fmaf(s[32 * g + 2 * i + 1], sc, -msc));
-      sum[i & 3] += p0 + p1;
+      // fmaf(s, sc, -msc) on each lane of the pair
+      const float2 x = fma2(make_float2(s[32 * g + 2 * i], s[32 * g + 2 * i + 1]), sc2, nmsc2);
+      const float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
+      sum[i & 1] = add2(sum[i & 1], make_float2(p0, p1));
       pk[i] = pack2<BF16>(p0, p1);
     }
     tmem_st16(t_p + 16 * g, pk);
   }
-  return (sum[0] + sum[1]) + (sum[2] + sum[3]);
+  const float2 t = add2(sum[0], sum[1]);
+  return t.x + t.y;
 }
 
 // Row maximum of N registers as a tree (8 independent chains, then pairwise).
 template <int N>
 __device__ __forceinline__ float row_max(const float *s) {
+  static_assert(N % 16 == 0, "N must be a multiple of 16");
   float m[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) m[i] = s[i];
+  for (int k = 0; k < 8; ++k) m[k] = fmaxf(s[2 * k], s[2 * k + 1]);
 #pragma unroll
-  for (int i = 8; i < N; ++i) m[i & 7] = fmaxf(m[i & 7], s[i]);
+  for (int i = 16; i < N; i += 16) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m[k] = max3(m[k], s[i + 2 * k], s[i + 2 * k + 1]);
+  }
   return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
 }
 
