@@ -279,6 +279,25 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
 }
+// 2^x for a pair, on the FMA pipe instead of the MUFU: Cody-Waite reduction x = j + f with
+// j = rint(x) (the 1.5 * 2^23 rounding trick) and f in [-0.5, 0.5], a degree-3 polynomial
+// for 2^f (coefficients fitted here for minimax relative error on [-0.5, 0.5]: max
+// relative error 7.5e-5, below the 2^-9 of the bf16 P it feeds), and j added into the
+// exponent field.  Inputs below -126 are clamped (-inf -> ~2^-126, not 0); x <= 127.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kMagic = 12582912.f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 jj = add2(x, make_float2(kMagic, kMagic));          // rint(x) in the low bits
+  const float2 r = add2(jj, make_float2(-kMagic, -kMagic));        // rint(x)
+  const float2 f = fma2(r, make_float2(-1.f, -1.f), x);            // x - rint(x)
+  float2 p = fma2(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.24261114f, 0.24261114f));
+  p = fma2(p, f, make_float2(0.69326097f, 0.69326097f));
+  p = fma2(p, f, make_float2(0.99992806f, 0.99992806f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(jj.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(jj.y) << 23)));
+}
+
 // Maximum of three (sm_100 three-input max; NaN handling as fmaxf).
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;

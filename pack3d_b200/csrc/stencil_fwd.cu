@@ -182,7 +182,15 @@ __device__ __forceinline__ float exp_store(const float *s, float m, float sc, ui
     for (int i = 0; i < 16; ++i) {
       // fmaf(s, sc, -msc) on each lane of the pair
       const float2 x = fma2(make_float2(s[32 * g + 2 * i], s[32 * g + 2 * i + 1]), sc2, nmsc2);
-      const float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
+      float p0, p1;
+      if ((i & 3) == 3) {  // a quarter of the exponentials on the FMA pipe: the MUFU is the bound
+        const float2 e = exp2_poly2(x);
+        p0 = e.x;
+        p1 = e.y;
+      } else {
+        p0 = ex2_approx(x.x);
+        p1 = ex2_approx(x.y);
+      }
       sum[i & 1] = add2(sum[i & 1], make_float2(p0, p1));
       pk[i] = pack2<BF16>(p0, p1);
     }
