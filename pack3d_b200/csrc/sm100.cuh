@@ -279,6 +279,16 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
 }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 // 2^x for a pair, on the FMA pipe instead of the MUFU: Cody-Waite reduction x = j + f with
 // j = rint(x) (the 1.5 * 2^23 rounding trick) and f in [-0.5, 0.5], a degree-3 polynomial
 // for 2^f (coefficients fitted here for minimax relative error on [-0.5, 0.5]: max

@@ -6,8 +6,11 @@
 //   dS = P * (dO V^T - Delta) / sqrt(D),   dQ = dS K
 // per branch (local: dO = dO_l, K/V = the 5x5x5 neighbours; global: dO = dO_g, K/V = all
 // summaries).  dS is rounded to the storage dtype before the product (the reference does
-// the same for the global branch, kernels.py:197); the two branch gradients are each
-// rounded, then added and rounded again (kernels.py:202-206).
+// the same for the global branch, kernels.py:197); here the rounded operand is P (dP -
+// Delta) and the 1/sqrt(D) is applied once to the fp32 dQ accumulator (one multiply per
+// output instead of one per score; the rounding is relative, so the result agrees within
+// the dtype's rounding).  The two branch gradients are each rounded, then added and
+// rounded again (kernels.py:202-206).
 //
 // Work unit and chunk sequence are those of the forward kernel (stencil_fwd.cu): one
 // (batch, head) and a 4x4x8 tile of 128 queries per CTA, two CTAs per SM; 8 local chunks
@@ -354,7 +357,9 @@ __global__ void __launch_bounds__(kDqThreads, 2)
           tmem_ld16(t_tile + kColDQ + 16 * c, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 8; ++i) park[8 * c + i] = pack2<BF16>(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
+          for (int i = 0; i < 8; ++i)
+            park[8 * c + i] =
+                pack2<BF16>(__uint_as_float(o[2 * i]) * inv_sqrt_d, __uint_as_float(o[2 * i + 1]) * inv_sqrt_d);
         }
       }
       const bool local = ch < kLocalChunks;
@@ -376,10 +381,20 @@ __global__ void __launch_bounds__(kDqThreads, 2)
       if (active) {
         int valid = kKeys;
         if (!local) valid = min(kKeys, p.summaries - (ch - kLocalChunks) * kSumRows);
+        if (local || valid < kKeys) {
 #pragma unroll
-        for (int i = 0; i < kKeys; ++i) {
-          const bool use = local ? ((mask[i >> 5] >> (i & 31)) & 1u) != 0u : i < valid;
-          pr[i] = use ? ex2_approx(fmaf(pr[i], sc, -lse2)) : 0.f;
+          for (int i = 0; i < kKeys; ++i) {
+            const bool use = local ? ((mask[i >> 5] >> (i & 31)) & 1u) != 0u : i < valid;
+            pr[i] = use ? ex2_approx(fmaf(pr[i], sc, -lse2)) : 0.f;
+          }
+        } else {  // a full global chunk: no mask, paired scale
+          const float2 sc2 = make_float2(sc, sc), nl2 = make_float2(-lse2, -lse2);
+#pragma unroll
+          for (int i = 0; i < kKeys; i += 2) {
+            const float2 x = fma2(make_float2(pr[i], pr[i + 1]), sc2, nl2);
+            pr[i] = ex2_approx(x.x);
+            pr[i + 1] = ex2_approx(x.y);
+          }
         }
       }
       ok = wait_warp(kDPReady, ch);
@@ -391,11 +406,13 @@ __global__ void __launch_bounds__(kDqThreads, 2)
           tmem_ld32(t_tile + kColDP + 32 * g, dp);
           tmem_wait_ld();
           uint32_t pk[16];
+          // dS = P (dP - Delta); its 1/sqrt(D) is applied to the dQ accumulator
+          const float2 nd2 = make_float2(-delta, -delta);
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float d0 = pr[32 * g + 2 * i] * (__uint_as_float(dp[2 * i]) - delta) * inv_sqrt_d;
-            const float d1 = pr[32 * g + 2 * i + 1] * (__uint_as_float(dp[2 * i + 1]) - delta) * inv_sqrt_d;
-            pk[i] = pack2<BF16>(d0, d1);
+            const float2 t = add2(make_float2(__uint_as_float(dp[2 * i]), __uint_as_float(dp[2 * i + 1])), nd2);
+            const float2 d = mul2(make_float2(pr[32 * g + 2 * i], pr[32 * g + 2 * i + 1]), t);
+            pk[i] = pack2<BF16>(d.x, d.y);
           }
           // dS group g goes to dP columns [16g, 16g + 16): already read (groups are read in order)
           tmem_st16(t_tile + kColDP + 16 * g, pk);
@@ -424,8 +441,8 @@ __global__ void __launch_bounds__(kDqThreads, 2)
 #pragma unroll
         for (int i = 0; i < D / 2; ++i) {
           const float2 l = unpack2<BF16>(park[i]);
-          const float g0 = round_storage<BF16>(__uint_as_float(acc[2 * i]));
-          const float g1 = round_storage<BF16>(__uint_as_float(acc[2 * i + 1]));
+          const float g0 = round_storage<BF16>(__uint_as_float(acc[2 * i]) * inv_sqrt_d);
+          const float g1 = round_storage<BF16>(__uint_as_float(acc[2 * i + 1]) * inv_sqrt_d);
           out[i] = pack2<BF16>(l.x + g0, l.y + g1);
         }
         uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.dq) + grow * D);
@@ -518,7 +535,8 @@ int launch_dq_t(const StencilBwdArgs &a, cudaStream_t stream) {
 // tile of 128 summaries (TMEM lanes) and a stream of 128-query chunks (columns),
 //   S^T = SK Q^T, dP^T = SV dO_g^T, P^T = exp(S^T / sqrt(D) - lse), dS^T = P^T (dP^T - Delta) / sqrt(D)
 //   dSV += P^T dO_g,  dSK += dS^T Q          (P^T and dS^T rounded to the storage dtype)
-// over the query chunks of one split; splits write fp32 partials [B*G, splits, M, D] that a
+// over the query chunks of one split (the rounded dS^T operand is P^T (dP^T - Delta); the
+// 1/sqrt(D) multiplies the fp32 dSK accumulator once, when it is written); splits write fp32 partials [B*G, splits, M, D] that a
 // fixed-order reduction sums.  The global branch ignores the geometry, so this kernel serves
 // any token order.  Summary rows past M read zeros and are not written; query columns past
 // N get lse = +inf (P = 0).
@@ -771,24 +789,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(t_lanes + kGColS + col0, sv);
         tmem_ld32(t_lanes + kGColDP + col0, dv);
         tmem_wait_ld();
+        // P^T = exp2(S^T sc - lse log2e); dS^T = P^T (dP^T - Delta) (its 1/sqrt(D) is applied
+        // to the dSK accumulator at the end)
+        if (col0 + 32 <= valid) {  // every column inside the volume: paired, no masks
+          const float2 sc2 = make_float2(sc, sc), nl2e = make_float2(-kLog2e, -kLog2e);
 #pragma unroll
-        for (int i4 = 0; i4 < 8; ++i4) {
-          const int j = col0 + 4 * i4;
-          const float4 l4 = vals[j / 4], d4 = vals[(kGCols + j) / 4];
-          const float ls[4] = {l4.x, l4.y, l4.z, l4.w}, ds[4] = {d4.x, d4.y, d4.z, d4.w};
-          float pp[4], dd[4];
+          for (int i4 = 0; i4 < 8; ++i4) {
+            const int j = col0 + 4 * i4;
+            const float4 l4 = vals[j / 4], d4 = vals[(kGCols + j) / 4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = 4 * i4 + e;
-            // columns past the volume may hold stale values: they give exact zeros
-            const bool in = j + e < valid;
-            pp[e] = in ? ex2_approx(fmaf(__uint_as_float(sv[i]), sc, -ls[e] * kLog2e)) : 0.f;
-            dd[e] = in ? pp[e] * (__uint_as_float(dv[i]) - ds[e]) * inv_sqrt_d : 0.f;
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int i = 4 * i4 + 2 * h2;
+              const float2 l2 = h2 ? make_float2(l4.z, l4.w) : make_float2(l4.x, l4.y);
+              const float2 nd2 = h2 ? make_float2(-d4.z, -d4.w) : make_float2(-d4.x, -d4.y);
+              const float2 x =
+                  fma2(make_float2(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), sc2, mul2(l2, nl2e));
+              const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+              const float2 dd = mul2(pp, add2(make_float2(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])), nd2));
+              pw[gi][2 * i4 + h2] = pack2<BF16>(pp.x, pp.y);
+              dw[gi][2 * i4 + h2] = pack2<BF16>(dd.x, dd.y);
+            }
           }
-          pw[gi][2 * i4] = pack2<BF16>(pp[0], pp[1]);
-          pw[gi][2 * i4 + 1] = pack2<BF16>(pp[2], pp[3]);
-          dw[gi][2 * i4] = pack2<BF16>(dd[0], dd[1]);
-          dw[gi][2 * i4 + 1] = pack2<BF16>(dd[2], dd[3]);
+        } else {
+#pragma unroll
+          for (int i4 = 0; i4 < 8; ++i4) {
+            const int j = col0 + 4 * i4;
+            const float4 l4 = vals[j / 4], d4 = vals[(kGCols + j) / 4];
+            const float ls[4] = {l4.x, l4.y, l4.z, l4.w}, ds[4] = {d4.x, d4.y, d4.z, d4.w};
+            float pp[4], dd[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = 4 * i4 + e;
+              // columns past the volume may hold stale values: they give exact zeros
+              const bool in = j + e < valid;
+              pp[e] = in ? ex2_approx(fmaf(__uint_as_float(sv[i]), sc, -ls[e] * kLog2e)) : 0.f;
+              dd[e] = in ? pp[e] * (__uint_as_float(dv[i]) - ds[e]) : 0.f;
+            }
+            pw[gi][2 * i4] = pack2<BF16>(pp[0], pp[1]);
+            pw[gi][2 * i4 + 1] = pack2<BF16>(pp[2], pp[3]);
+            dw[gi][2 * i4] = pack2<BF16>(dd[0], dd[1]);
+            dw[gi][2 * i4 + 1] = pack2<BF16>(dd[2], dd[3]);
+          }
         }
       }
       tc_fence_before();
@@ -819,10 +860,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = m0 + row;
       if (m < p.summaries) {
         float *dst = (half ? p.dv_part : p.dk_part) + (((int64_t)bg * p.splits + split) * p.summaries + m) * D;
+        const float scale = half ? 1.f : inv_sqrt_d;  // dSK: the 1/sqrt(D) of dS
 #pragma unroll
         for (int v = 0; v < D / 4; ++v)
-          reinterpret_cast<float4 *>(dst)[v] = make_float4(__uint_as_float(acc[4 * v]), __uint_as_float(acc[4 * v + 1]),
-                                                           __uint_as_float(acc[4 * v + 2]), __uint_as_float(acc[4 * v + 3]));
+          reinterpret_cast<float4 *>(dst)[v] =
+              make_float4(__uint_as_float(acc[4 * v]) * scale, __uint_as_float(acc[4 * v + 1]) * scale,
+                          __uint_as_float(acc[4 * v + 2]) * scale, __uint_as_float(acc[4 * v + 3]) * scale);
       }
     }
     tmem_wait_st();
