@@ -49,6 +49,8 @@ def parse_args():
     ap.add_argument("--fwd-bwd-steps", type=int, default=3, help="timed fwd+bwd steps (0 disables)")
     ap.add_argument("--backward-only", type=int, default=0, metavar="N",
                     help="profiling mode: run the operator backward N times on config-3 inputs and exit")
+    ap.add_argument("--train-only", type=int, default=0, metavar="N",
+                    help="profiling mode: run the config-3 layer forward + backward N times and exit")
     ap.add_argument("--kernel-only", type=int, default=0, metavar="N",
                     help="profiling mode: run the stage-(c) kernel N times on the config-1 inputs and exit")
     return ap.parse_args()
@@ -235,6 +237,28 @@ def backward_only(args, device):
     print(json.dumps({"backward_only_ms": [round(t, 4) for t in times], "device_errors": errors}), flush=True)
 
 
+def train_only(args, device):
+    """Profiling mode: the config-3 layer forward + backward (batch 2) alone."""
+    from pack3d_b200 import _native
+    layout = make_layout(CONFIG["grid"]).to(device)
+    layer = make_layer(torch.bfloat16, device)
+    gen = torch.Generator(device=device).manual_seed(4)
+    x = torch.randn(2, layout.geometry.num_tokens, CONFIG["dim"], device=device, generator=gen)
+    x = x.to(torch.bfloat16).requires_grad_()
+    dy = torch.randn_like(x)
+
+    def step():
+        layer.zero_grad(set_to_none=True)
+        x.grad = None
+        layer(x, layout).backward(dy)
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    times = timed_steps(step, args.train_only, torch.cuda.current_stream(device))
+    errors = _native.device_errors()
+    print(json.dumps({"train_step_ms": [round(t, 4) for t in times], "device_errors": errors}), flush=True)
+
+
 def run_sharded(args, rank, world, device):
     """N > 1: the config-1 field split into z-slabs, one per rank (the same 64^3 field at
     every N: strong scaling).  Each rank runs the layer on its planes with the halo
@@ -364,6 +388,8 @@ def run_b200(args, rank, world, device):
     from pack3d_b200.rope import balanced_pairs, rotate_projections
     if args.backward_only:
         return backward_only(args, device)
+    if args.train_only:
+        return train_only(args, device)
     dtype = torch.bfloat16
     layout = make_layout(CONFIG["grid"]).to(device)
     geom = layout.geometry
