@@ -365,8 +365,9 @@ def run_sharded(args, rank, world, device):
                                "summaries) split into z-slabs, one per GPU; layer forward",
                    "grid": list(grid), "batch": b, "heads": hq, "kv_heads": g, "head_dim": hd, "dim": dim,
                    "summaries": m, "radius": CONFIG["radius"],
-                   "parallelism": f"{world} z-slabs of {slabs.planes} planes; NCCL halo exchange (2 planes "
-                                  "of kl, vl each way) + summary all-gather",
+                   "parallelism": f"{world} z-slabs of {slabs.planes} planes; one batch of NCCL point-to-point "
+                                  "operations per layer: halo exchange (2 planes of kl, vl each way) + summary "
+                                  "all-gather",
                    "cuda_graph": False,
                    "l2": "flushed between timed steps (256 MiB write outside the timed events)"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",

@@ -96,8 +96,17 @@ class PACK3DAttention(nn.Module):
         projection outputs into rotated q / kl / kg and head-major vl / vg; the core writes
         its output token-major so the output projection reads it without a transpose copy.
         """
-        from . import _native
         from .ops import forward as core_forward
+        b, n = x.shape[0], x.shape[1]
+        x, q, kl, vl, kg, vg, gate = self._inference_glue(x, layout.coords, layout.grid_shape)
+        y, _ = core_forward(q, kl, vl, kg, vg, self.pool_weight, self.slot_bias, gate, self.local_scale,
+                            self.global_scale, layout.geometry, self.temperature, save_state=False, y_rows=True)
+        return x + self.to_out(y.transpose(1, 2).reshape(b, n, -1))
+
+    def _inference_glue(self, x, coords, grid_shape):
+        """LayerNorm, projections, RoPE at ``coords`` (extents ``grid_shape``) and the gate of
+        the fused inference path: ``(x, q, kl, vl, kg, vg, gate)``, head-major."""
+        from . import _native
         from .rope import phase_tables
         b, n = x.shape[0], x.shape[1]
         h, g, d = self.heads, self.kv_heads, self.head_dim
@@ -113,15 +122,15 @@ class PACK3DAttention(nn.Module):
                           "p3d_layer_norm")
         qp, kvp = self.to_q(xn), self.to_kv(xn)
         pairs = balanced_pairs(d)
-        extents = tuple(int(e) for e in layout.grid_shape)
+        extents = tuple(int(e) for e in grid_shape)
         _, phases = phase_tables(dev, pairs, extents)
         if phases is None:   # coordinate extents too large for a table: the general RoPE path
             q, kl, kg = rotate_projections(qp.reshape(b, n, h, d).transpose(1, 2),
                                            *(t.reshape(b, n, g, d).transpose(1, 2) for t in kvp.chunk(4, -1)[0::2]),
-                                           layout.coords, pairs, extents, packed=False)
+                                           coords, pairs, extents, packed=False)
             vl, vg = (t.reshape(b, n, g, d).transpose(1, 2).contiguous() for t in kvp.chunk(4, -1)[1::2])
         else:
-            coords = layout.coords.to(device=dev, dtype=torch.int64).contiguous()
+            coords = coords.to(device=dev, dtype=torch.int64).contiguous()
             q = torch.empty((b, h, n, d), dtype=x.dtype, device=dev)
             kl, vl, kg, vg = (torch.empty((b, g, n, d), dtype=x.dtype, device=dev) for _ in range(4))
             with torch.cuda.device(dev):
@@ -130,6 +139,4 @@ class PACK3DAttention(nn.Module):
                                                 _native.ptr(coords), *pairs, _native.ptr(phases), *extents, stream),
                               "p3d_qkv_split")
         gate = self.gate(xn).reshape(b, n, h, 2).softmax(-1)[..., 1].transpose(1, 2).contiguous()
-        y, _ = core_forward(q, kl, vl, kg, vg, self.pool_weight, self.slot_bias, gate, self.local_scale,
-                            self.global_scale, layout.geometry, self.temperature, save_state=False, y_rows=True)
-        return x + self.to_out(y.transpose(1, 2).reshape(b, n, -1))
+        return x, q, kl, vl, kg, vg, gate

@@ -155,6 +155,53 @@ def exchange_halos(t, slabs: ZSlabs, group=None):
     return torch.cat(parts, dim=2) if len(parts) > 1 else t.contiguous()
 
 
+def exchange_slab(kl, vl, sk_rank, sv_rank, slabs: ZSlabs, group=None):
+    """The forward's whole exchange as one batch of point-to-point operations: the halo
+    planes of ``kl`` and ``vl`` with both neighbours and this rank's summaries with every
+    rank (an all-gather written as sends and receives, so that it shares the batch).
+
+    Returns ``(kl_ext, vl_ext, sk, sv)`` as :func:`exchange_halos` and
+    :func:`gather_summaries` would.
+    """
+    world = dist.get_world_size(group)
+    b, g, n, d = kl.shape
+    if n != slabs.tokens or vl.shape != kl.shape:
+        raise ValueError("tensor rows do not match the slab")
+    pt = slabs.plane_tokens
+    rank_of = (lambda r: r) if group is None else (lambda r: dist.get_global_rank(group, r))
+    ops = []
+    halos = {}
+    for name, t in (("k", kl), ("v", vl)):
+        if slabs.halo_lo:
+            lo = slabs.halo_lo * pt
+            halos[name, "lo"] = torch.empty((b, g, lo, d), dtype=t.dtype, device=t.device)
+            ops.append(dist.P2POp(dist.isend, t[:, :, :lo].contiguous(), rank_of(slabs.rank - 1), group))
+            ops.append(dist.P2POp(dist.irecv, halos[name, "lo"], rank_of(slabs.rank - 1), group))
+        if slabs.halo_hi:
+            hi = slabs.halo_hi * pt
+            halos[name, "hi"] = torch.empty((b, g, hi, d), dtype=t.dtype, device=t.device)
+            ops.append(dist.P2POp(dist.isend, t[:, :, n - hi:].contiguous(), rank_of(slabs.rank + 1), group))
+            ops.append(dist.P2POp(dist.irecv, halos[name, "hi"], rank_of(slabs.rank + 1), group))
+    sk_rank, sv_rank = sk_rank.contiguous(), sv_rank.contiguous()
+    parts = {name: [None] * world for name in ("k", "v")}
+    for name, s in (("k", sk_rank), ("v", sv_rank)):
+        for r in range(world):
+            if r == slabs.rank:
+                parts[name][r] = s
+                continue
+            parts[name][r] = torch.empty_like(s)
+            ops.append(dist.P2POp(dist.isend, s, rank_of(r), group))
+            ops.append(dist.P2POp(dist.irecv, parts[name][r], rank_of(r), group))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+    ext = []
+    for name, t in (("k", kl), ("v", vl)):
+        pieces = [p for p in (halos.get((name, "lo")), t, halos.get((name, "hi"))) if p is not None]
+        ext.append(torch.cat(pieces, dim=2) if len(pieces) > 1 else t.contiguous())
+    return ext[0], ext[1], torch.cat(parts["k"], dim=2), torch.cat(parts["v"], dim=2)
+
+
 def gather_summaries(s, group=None):
     """``s`` [B, G, M_rank, D] -> [B, G, world*M_rank, D], rank-major."""
     world = dist.get_world_size(group)
@@ -184,11 +231,12 @@ def pool_summaries(kg, vg, weight, bias, geometry, temperature=1.0):
 
 
 def slab_forward(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, geometry, slabs: ZSlabs, temperature=1.0,
-                 save_state=False):
+                 save_state=False, y_rows=False):
     """``p3d_attn_fwd_slab`` on one rank: returns ``(y, state)``.
 
     ``kl_ext`` / ``vl_ext`` hold the rank's planes plus its halo planes; ``sk`` / ``sv`` the
-    gathered summaries of all ranks.
+    gathered summaries of all ranks.  With ``y_rows`` y is stored token-major ([B, N, H, D];
+    the returned [B, H, N, D] tensor is a view of it).
     """
     b, h, n, d = q.shape
     if n != slabs.tokens or kl_ext.shape[2] != slabs.halo_planes * slabs.plane_tokens:
@@ -199,14 +247,17 @@ def slab_forward(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, geometry
     if geometry.stencil is None or op.raster_to_packed:
         raise ValueError("slab forward needs the complete stencil of a raster-stored slab")
     slab = _native.Slab(slabs.grid[0], slabs.z0, slabs.halo_z0, slabs.halo_planes, sk.shape[2])
-    y = torch.empty_like(q)
+    if y_rows:
+        y = torch.empty((b, n, h, d), dtype=q.dtype, device=q.device).transpose(1, 2)
+    else:
+        y = torch.empty_like(q)
     ol = og = lse_l = lse_g = None
-    flags = 0
+    flags = _native.FWD_Y_ROWS if y_rows else 0
     if save_state:
         ol, og = torch.empty_like(q), torch.empty_like(q)
         lse_l = torch.empty((b, h, n), dtype=torch.float32, device=q.device)
         lse_g = torch.empty_like(lse_l)
-        flags = _native.FWD_SAVE_STATE
+        flags |= _native.FWD_SAVE_STATE
     with torch.cuda.device(q.device):
         status = _native.lib().p3d_attn_fwd_slab(op, ctypes.byref(slab), _native.ptr(y), _native.ptr(sk),
                                                  _native.ptr(sv), _native.ptr(ol), _native.ptr(og),
@@ -244,6 +295,15 @@ def sharded_layer_forward(layer, x, layout: SlabLayout, group=None):
     if n != layout.slabs.tokens or x.shape[2] != layer.dim:
         raise ValueError("x must be [batch, rank tokens, dim]")
     h, g, d = layer.heads, layer.kv_heads, layer.head_dim
+    if layer._fast_inference(x):
+        # the fused glue of the single-GPU inference path, one exchange batch, token-major y
+        x, q, kl, vl, kg, vg, gate = layer._inference_glue(x, layout.coords, layout.grid_shape)
+        sk_rank, sv_rank = pool_summaries(kg, vg, layer.pool_weight, layer.slot_bias, layout.geometry,
+                                          layer.temperature)
+        kl_ext, vl_ext, sk, sv = exchange_slab(kl, vl, sk_rank, sv_rank, layout.slabs, group)
+        y, _ = slab_forward(q, kl_ext, vl_ext, sk, sv, layer.pool_weight, layer.slot_bias, gate, layer.local_scale,
+                            layer.global_scale, layout.geometry, layout.slabs, layer.temperature, y_rows=True)
+        return x + layer.to_out(y.transpose(1, 2).reshape(b, n, -1))
     xn = layer.norm(x)
     q = layer.to_q(xn).reshape(b, n, h, d).transpose(1, 2)
     kl, vl, kg, vg = (t.reshape(b, n, g, d).transpose(1, 2) for t in layer.to_kv(xn).chunk(4, -1))

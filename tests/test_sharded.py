@@ -10,7 +10,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from pack3d_b200.sharded import ZSlabs, exchange_halos, gather_summaries, slab_layout
+from pack3d_b200.sharded import ZSlabs, exchange_halos, exchange_slab, gather_summaries, slab_layout
 
 
 def _free_port():
@@ -57,7 +57,12 @@ def _exchange_worker(rank, world, port, grid, out):
         want = full[:, :, s.halo_z0 * pt:(s.halo_z0 + s.halo_planes) * pt]
         summ = torch.full((2, 3, 5, 4), float(rank))
         gathered = gather_summaries(summ)
-        out[rank] = (torch.equal(ext, want), gathered[:, :, :, 0].flatten().tolist())
+        # the one-batch exchange of the inference path gives the same tensors
+        kl, vl = full[:, :, lo:hi].contiguous(), 2 * full[:, :, lo:hi]
+        kx, vx, skx, svx = exchange_slab(kl, vl, summ, summ + 0.5, s)
+        same = (torch.equal(kx, want) and torch.equal(vx, 2 * want) and torch.equal(skx, gathered)
+                and torch.equal(svx, gathered + 0.5))
+        out[rank] = (torch.equal(ext, want) and same, gathered[:, :, :, 0].flatten().tolist())
     finally:
         dist.destroy_process_group()
 
@@ -256,6 +261,8 @@ def _train_worker(rank, world, port, grid, out):
         s = ZSlabs(grid, world, rank)
         lay = slab_layout(grid, slabs=s).to(dev)
         lo, hi = s.token_range()
+        with torch.inference_mode():   # the fused inference path (one exchange batch)
+            y_inf = sharded_layer_forward(layer, x_full[:, lo:hi].to(dev), lay).cpu()
         x = x_full[:, lo:hi].to(dev).requires_grad_()
         y = sharded_layer_forward(layer, x, lay)
         y.backward(dy_full[:, lo:hi].to(dev))
@@ -263,7 +270,7 @@ def _train_worker(rank, world, port, grid, out):
             dist.all_reduce(p.grad)
         torch.cuda.synchronize(dev)
         out[rank] = (y.detach().cpu(), x.grad.cpu(), {k: p.grad.cpu() for k, p in layer.named_parameters()},
-                     _native.device_errors())
+                     _native.device_errors(), y_inf)
     finally:
         dist.destroy_process_group()
 
@@ -291,10 +298,11 @@ def test_sharded_training_step_over_nccl():
     y.backward(dy)
     tol = lambda t: 2e-2 * max(1.0, t.float().abs().max().item())  # noqa: E731
     for rank in range(world):
-        y_r, dx_r, grads, errors = results[rank]
+        y_r, dx_r, grads, errors, y_inf = results[rank]
         lo, hi = ZSlabs(grid, world, rank).token_range()
         assert errors == 0
         assert (y_r.float() - y[:, lo:hi].detach().float().cpu()).abs().max().item() <= tol(y)
+        assert (y_inf.float() - y[:, lo:hi].detach().float().cpu()).abs().max().item() <= tol(y), rank
         assert (dx_r.float() - x.grad[:, lo:hi].float().cpu()).abs().max().item() <= tol(x.grad), rank
         for name, p in layer.named_parameters():
             assert (grads[name].float() - p.grad.float().cpu()).abs().max().item() <= tol(p.grad), (name, rank)
