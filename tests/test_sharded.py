@@ -306,3 +306,60 @@ def test_sharded_training_step_over_nccl():
         assert (dx_r.float() - x.grad[:, lo:hi].float().cpu()).abs().max().item() <= tol(x.grad), rank
         for name, p in layer.named_parameters():
             assert (grads[name].float() - p.grad.float().cpu()).abs().max().item() <= tol(p.grad), (name, rank)
+
+
+def _graph_worker(rank, world, port, grid, out):
+    """The sharded inference layer captured in a CUDA graph (its NCCL point-to-point batch
+    included) and replayed: the same output as the eager call, twice in a row."""
+    from pack3d_b200 import PACK3DAttention, _native
+    from pack3d_b200.sharded import sharded_layer_forward
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=dev, timeout=datetime.timedelta(seconds=60))
+    graph = None
+    try:
+        torch.manual_seed(0)
+        layer = PACK3DAttention(192, heads=4, kv_heads=4, head_dim=48, block_volume=64).to(dev, torch.bfloat16)
+        n = grid[0] * grid[1] * grid[2]
+        x_full = torch.randn(1, n, 192, generator=torch.Generator().manual_seed(6)).to(torch.bfloat16)
+        s = ZSlabs(grid, world, rank)
+        lay = slab_layout(grid, slabs=s).to(dev)
+        lo, hi = s.token_range()
+        x = x_full[:, lo:hi].to(dev)
+        with torch.inference_mode():
+            want = sharded_layer_forward(layer, x, lay).clone()
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    sharded_layer_forward(layer, x, lay)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                y = sharded_layer_forward(layer, x, lay)
+            got = []
+            for _ in range(2):
+                graph.replay()
+                torch.cuda.synchronize(dev)
+                got.append(y.clone())
+        out[rank] = ([torch.equal(g, want) for g in got], _native.device_errors())
+    finally:
+        del graph   # a graph holding NCCL calls is released before the process group
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_sharded_inference_layer_replays_as_a_cuda_graph():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world, grid = 2, (32, 16, 24)
+    with mp.get_context("spawn").Manager() as manager:
+        out = manager.dict()
+        mp.spawn(_graph_worker, args=(world, _free_port(), grid, out), nprocs=world, join=True)
+        results = dict(out)
+    for rank in range(world):
+        same, errors = results[rank]
+        assert errors == 0
+        assert all(same), rank
