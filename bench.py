@@ -49,6 +49,9 @@ def parse_args():
     ap.add_argument("--fwd-bwd-steps", type=int, default=3, help="timed fwd+bwd steps (0 disables)")
     ap.add_argument("--backward-only", type=int, default=0, metavar="N",
                     help="profiling mode: run the operator backward N times on config-3 inputs and exit")
+    ap.add_argument("--config4", type=int, default=0, metavar="K",
+                    help="separate mode: BASELINE config 4 (128^3 field, dim 384 = 8 heads x 48) layer forward + "
+                         "backward, K timed steps, on the launch's N GPUs (z-slabs for N > 1); one JSON line")
     ap.add_argument("--train-only", type=int, default=0, metavar="N",
                     help="profiling mode: run the config-3 layer forward + backward N times and exit")
     ap.add_argument("--kernel-only", type=int, default=0, metavar="N",
@@ -257,6 +260,70 @@ def train_only(args, device):
     times = timed_steps(step, args.train_only, torch.cuda.current_stream(device))
     errors = _native.device_errors()
     print(json.dumps({"train_step_ms": [round(t, 4) for t in times], "device_errors": errors}), flush=True)
+
+
+CONFIG4 = dict(grid=(128, 128, 128), batch=1, heads=8, kv_heads=8, head_dim=48, dim=384, block=(4, 4, 4), radius=2)
+
+
+def config4_fwd_bwd(args, rank, world, device):
+    """the layer forward + backward on a 128^3 field (2,097,152 tokens),
+    dim 384 = 8 heads x 48, bf16.  N = 1: the whole field on one GPU; N > 1: z-slabs, the
+    sharded core (halo exchange, summary all-gather, summary-gradient reduce-scatter) and an
+    all-reduce of the replicated parameters' gradients, as a data-parallel step would.
+    The field is stored in raster order (the reference config's Morton storage is a pure
+    repack of it, tested for equivariance elsewhere)."""
+    from pack3d_b200 import PACK3DAttention, _native
+    from pack3d_b200.sharded import ZSlabs, sharded_layer_forward, slab_layout
+    grid = CONFIG4["grid"]
+    if world == 1:
+        layout = make_layout(grid).to(device)
+        forward = lambda layer, x: layer(x, layout)  # noqa: E731
+        n = math.prod(grid)
+    else:
+        slabs = ZSlabs(grid, world, rank, radius=CONFIG4["radius"], block_depth=CONFIG4["block"][0])
+        layout = slab_layout(grid, CONFIG4["block"], radius=CONFIG4["radius"], slabs=slabs).to(device)
+        forward = lambda layer, x: sharded_layer_forward(layer, x, layout)  # noqa: E731
+        n = slabs.tokens
+    torch.manual_seed(0)
+    layer = PACK3DAttention(CONFIG4["dim"], heads=CONFIG4["heads"], kv_heads=CONFIG4["kv_heads"],
+                            head_dim=CONFIG4["head_dim"], block_volume=math.prod(CONFIG4["block"]))
+    layer = layer.to(device=device, dtype=torch.bfloat16)
+    gen = torch.Generator(device=device).manual_seed(2000 + rank)
+    x = torch.randn(CONFIG4["batch"], n, CONFIG4["dim"], device=device, generator=gen).to(torch.bfloat16)
+    x.requires_grad_()
+    dy = torch.randn_like(x)
+
+    def step():
+        layer.zero_grad(set_to_none=True)
+        x.grad = None
+        forward(layer, x).backward(dy)
+        if world > 1:
+            for p in layer.parameters():
+                torch.distributed.all_reduce(p.grad)
+
+    step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    times = timed_steps(step, args.config4, torch.cuda.current_stream(device))
+    ms = sum(times) / len(times)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    errors = _native.device_errors()
+    if errors:
+        raise RuntimeError(f"device error flags set: {errors}")
+    total = math.prod(grid) * CONFIG4["batch"]
+    return {"mode": "config4", "metric": "PACK3D layer bf16 fwd+bwd tokens/s, BASELINE config 4", "n_gpus": world,
+            "steps": args.config4, "ms_per_step": round(ms, 3), "tokens_per_s": round(total / (ms * 1e-3), 1),
+            "scaling": "strong",
+            "config": {"workload": "BASELINE config 4: 128^3 field (2,097,152 tokens, raster storage), batch 1, "
+                                   "dim 384 = 8 heads x 48, radius 2, 32,768 summaries; layer forward + backward "
+                                   "(no optimizer)" + ("" if world == 1 else "; z-slabs over NCCL, parameter "
+                                                                             "gradients all-reduced"),
+                       "grid": list(grid), "dim": CONFIG4["dim"], "heads": CONFIG4["heads"],
+                       "head_dim": CONFIG4["head_dim"]}}
 
 
 def run_sharded(args, rank, world, device):
@@ -620,6 +687,13 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)
+    if args.config4:
+        line = config4_fwd_bwd(args, rank, world, device)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
     line = run_b200(args, rank, world, device) if world == 1 else run_sharded(args, rank, world, device)
     if line is None:
         return
