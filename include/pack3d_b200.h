@@ -113,6 +113,26 @@ P3D_API int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl, vo
                   int dtype, int batch, int heads, int kv_heads, int tokens, int head_dim, const int64_t *coords,
                   int pz, int py, int px, const float *phases, int ez, int ey, int ex, void *stream);
 
+/*
+ * Layer glue of the training path (their backward halves):
+ * p3d_qkv_merge: the backward of p3d_qkv_split -- replaces _Rotary.backward (rotary.py:66-70,
+ *   the inverse rotation of dq, dkl, dkg) and the transposes / chunk concatenation autograd
+ *   does for attention.py:70-72: dq [B,H,N,D], dkl, dvl, dkg, dvg [B,G,N,D] -> dqp [B,N,H*D],
+ *   dkvp [B,N,4*G*D] (channel blocks kl, vl, kg, vg).  Same arguments as p3d_qkv_split;
+ *   bit-identical to rotating back with p3d_rope (inverse = 1) and copying.
+ * p3d_layer_norm_bwd: the backward of p3d_layer_norm (nn.LayerNorm, attention.py:64): dx
+ *   [rows, dim] in dtype, dweight and dbias [dim] fp32 (sums over rows in fixed order,
+ *   bitwise repeatable); workspace of p3d_layer_norm_bwd_workspace(rows, dim) bytes.
+ */
+P3D_API int p3d_qkv_merge(const void *dq, const void *dkl, const void *dvl, const void *dkg, const void *dvg,
+                  void *dqp, void *dkvp, int dtype, int batch, int heads, int kv_heads, int tokens, int head_dim,
+                  const int64_t *coords, int pz, int py, int px, const float *phases, int ez, int ey, int ex,
+                  void *stream);
+P3D_API size_t p3d_layer_norm_bwd_workspace(int64_t rows, int dim);
+P3D_API int p3d_layer_norm_bwd(const void *x, const void *weight, const void *dy, void *dx, float *dweight,
+                       float *dbias, int dtype, int64_t rows, int dim, float eps, void *workspace,
+                       size_t workspace_bytes, void *stream);
+
 /* Operator arguments shared by forward and backward (all device pointers, contiguous). */
 typedef struct {
   int32_t batch, heads, kv_heads, tokens, head_dim;

@@ -15,7 +15,8 @@ from torch import nn
 from ._validation import HEAD_DIMS, check_cuda
 from .geometry import TokenLayout
 from .ops import pack3d_streamed
-from .rope import balanced_pairs, rotate_projections
+from . import glue
+from .rope import balanced_pairs, phase_tables, rotate_projections
 
 
 class PACK3DAttention(nn.Module):
@@ -54,6 +55,9 @@ class PACK3DAttention(nn.Module):
         self.local_scale = nn.Parameter(torch.ones(head_dim))
         self.global_scale = nn.Parameter(torch.full((head_dim,), 0.25))
         self.to_out = nn.Linear(heads * head_dim, dim, bias=False)
+        # 16-bit CUDA training calls run LayerNorm and the projection split (with RoPE) in the
+        # fused library kernels of pack3d_b200.glue; False keeps the per-op PyTorch path.
+        self.fused_glue = True
 
     def forward(self, x, layout: TokenLayout):
         layout.check_unmodified()
@@ -68,19 +72,38 @@ class PACK3DAttention(nn.Module):
         residual, b, n = x, x.shape[0], x.shape[1]
         if self._fast_inference(x):
             return self._forward_inference(x, layout)
-        x = self.norm(x)
-        q = self.to_q(x).reshape(b, n, self.heads, self.head_dim).transpose(1, 2)
-        kl, vl, kg, vg = (t.reshape(b, n, self.kv_heads, self.head_dim).transpose(1, 2)
-                          for t in self.to_kv(x).chunk(4, -1))
-        check_cuda(q)
         packed = self.position_encoding == "packed"
         pairs = (self.head_dim // 2, 0, 0) if packed else balanced_pairs(self.head_dim)
-        q, kl, kg = rotate_projections(q, kl, kg, layout.coords, pairs, layout.grid_shape, packed=packed)
+        phases = self._fused_glue_table(x, layout, pairs)
+        if phases is not None:
+            # the fused training glue: LayerNorm and the projection split (with RoPE) and their
+            # backward halves in the library kernels (pack3d_b200.glue)
+            x = glue.layer_norm(x, self.norm)
+            coords = layout.coords.to(device=x.device, dtype=torch.int64).contiguous()
+            q, kl, vl, kg, vg = glue.qkv_split(self.to_q(x), self.to_kv(x), coords, phases, pairs,
+                                               layout.grid_shape, self.heads, self.kv_heads, self.head_dim)
+        else:
+            x = self.norm(x)
+            q = self.to_q(x).reshape(b, n, self.heads, self.head_dim).transpose(1, 2)
+            kl, vl, kg, vg = (t.reshape(b, n, self.kv_heads, self.head_dim).transpose(1, 2)
+                              for t in self.to_kv(x).chunk(4, -1))
+            check_cuda(q)
+            q, kl, kg = rotate_projections(q, kl, kg, layout.coords, pairs, layout.grid_shape, packed=packed)
         gates = self.gate(x).reshape(b, n, self.heads, 2).softmax(-1)
         gate = gates[..., 1].transpose(1, 2)
         out = pack3d_streamed(q, kl, vl, kg, vg, self.pool_weight, self.slot_bias, gate, self.local_scale,
                               self.global_scale, layout.geometry, temperature=self.temperature)
         return residual + self.to_out(out.transpose(1, 2).reshape(b, n, -1))
+
+    def _fused_glue_table(self, x, layout, pairs):
+        """The RoPE phase table when the fused training glue applies (16-bit CUDA tensors of
+        the layer's dtype, axial RoPE, 16-byte rows), else None."""
+        if not (self.fused_glue and x.is_cuda and x.dtype in (torch.bfloat16, torch.float16)
+                and self.position_encoding == "axial" and self.dim % 8 == 0 and self.head_dim % 8 == 0
+                and all(p.dtype == x.dtype for p in self.parameters())):
+            return None
+        _, phases = phase_tables(x.device, pairs, tuple(int(e) for e in layout.grid_shape))
+        return phases
 
     def _fast_inference(self, x):
         """Gradient-free 16-bit axial calls take the fused glue path (same arithmetic)."""

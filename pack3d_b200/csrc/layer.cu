@@ -8,8 +8,16 @@
 //                   tensors [B, H|G, N, D]; q, kl and kg are rotated by the axial RoPE
 //                   phase table exactly as p3d_rope does (rotary.py:11-45), vl and vg
 //                   copied.  Replaces three rotations and two strided copies.
-// Both are HBM bound: one read and one write of every byte.
+//   p3d_qkv_merge   its backward (rotary.py:66-70 inverse rotation, then the transposes and
+//                   the chunk concatenation autograd would do): the five head-major
+//                   gradients -> the row-major to_q / to_kv output gradients, dq / dkl / dkg
+//                   rotated back by the same table (sine negated, products rounded as in
+//                   p3d_rope's inverse), so the result equals rotation + copies bit for bit.
+//   p3d_layer_norm_bwd  LayerNorm backward: dx per row (mean / rstd recomputed as in the
+//                   forward), fp32 per-warp partials of dweight / dbias reduced in fixed order.
+// All are HBM bound: one read and one write of every byte.
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace p3d {
 namespace {
@@ -80,6 +88,99 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
+// LayerNorm backward: each warp walks rows with a grid stride; per row, with mean / rstd
+// recomputed exactly as the forward computes them,
+//   xhat = (x - mean) rstd,  g = dy w,  dx = rstd (g - mean(g) - xhat mean(g xhat)),
+// and the warp's fp32 partials of dweight = sum dy xhat, dbias = sum dy are written per warp
+// (reduced afterwards in fixed order: bitwise-repeatable).
+constexpr int kLnBwdBlocks = 1024;  // at most 8192 warps: the partials' row count
+
+template <typename T, int kChunks>
+__global__ void __launch_bounds__(kWarps * 32)
+    layer_norm_bwd_kernel(const T *x, const T *weight, const T *dy, T *dx, float *dw_part, float *db_part,
+                          int64_t rows, int dim, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_id = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int64_t n_warps = (int64_t)gridDim.x * kWarps;
+  float w[kChunks][8], accw[kChunks][8], accb[kChunks][8];
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) {
+    const int c = (lane + 32 * k) * 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) accw[k][i] = accb[k][i] = w[k][i] = 0.f;
+    if (c < dim) load8<T>(weight + c, w[k]);
+  }
+  const float inv_dim = 1.f / (float)dim;
+  for (int64_t row = warp_id; row < rows; row += n_warps) {
+    float v[kChunks][8], g[kChunks][8];
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < kChunks; ++k) {
+      const int c = (lane + 32 * k) * 8;
+      if (c < dim) {
+        load8<T>(x + row * dim + c, v[k]);
+        load8<T>(dy + row * dim + c, g[k]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum += v[k][i];
+      }
+    }
+    const float mean = warp_sum(sum) / (float)dim;
+    float sq = 0.f;
+#pragma unroll
+    for (int k = 0; k < kChunks; ++k) {
+      const int c = (lane + 32 * k) * 8;
+      if (c < dim) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float d = v[k][i] - mean;
+          sq += d * d;
+        }
+      }
+    }
+    const float rstd = rsqrtf(warp_sum(sq) / (float)dim + eps);
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < kChunks; ++k) {
+      const int c = (lane + 32 * k) * 8;
+      if (c < dim) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float xhat = (v[k][i] - mean) * rstd;
+          const float gw = g[k][i] * w[k][i];
+          s1 += gw;
+          s2 += gw * xhat;
+          accw[k][i] += g[k][i] * xhat;
+          accb[k][i] += g[k][i];
+          v[k][i] = xhat;
+          g[k][i] = gw;
+        }
+      }
+    }
+    const float m1 = warp_sum(s1) * inv_dim, m2 = warp_sum(s2) * inv_dim;
+#pragma unroll
+    for (int k = 0; k < kChunks; ++k) {
+      const int c = (lane + 32 * k) * 8;
+      if (c < dim) {
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = rstd * (g[k][i] - m1 - v[k][i] * m2);
+        store8<T>(dx + row * dim + c, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) {
+    const int c = (lane + 32 * k) * 8;
+    if (c < dim) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        dw_part[warp_id * dim + c + i] = accw[k][i];
+        db_part[warp_id * dim + c + i] = accb[k][i];
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------- projection split
 struct SplitParams {
   const void *qp, *kvp;
@@ -93,7 +194,9 @@ struct SplitParams {
 
 constexpr int kTokensPerWarp = 4;
 
-// Rotate the 4 pairs (8 channels) starting at pair `pair0` of a head by the token's phases.
+// Rotate the 4 pairs (8 channels) starting at pair `pair0` of a head by the token's phases
+// (by their inverse with INVERSE: the sine negated).
+template <bool INVERSE = false>
 __device__ __forceinline__ void rotate8(float (&v)[8], int pair0, const SplitParams &p, const int64_t (&c)[3]) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -108,7 +211,8 @@ __device__ __forceinline__ void rotate8(float (&v)[8], int pair0, const SplitPar
       }
     }
     const int64_t entry = p.start[axis] + c[axis] * p.pairs[axis] + local;
-    const float2 cs = *reinterpret_cast<const float2 *>(p.phases + 2 * entry);
+    float2 cs = *reinterpret_cast<const float2 *>(p.phases + 2 * entry);
+    if (INVERSE) cs.y = -cs.y;
     const float even = v[2 * j], odd = v[2 * j + 1];
     // each product rounded separately, as the reference's elementwise torch arithmetic
     v[2 * j] = __fsub_rn(__fmul_rn(even, cs.x), __fmul_rn(odd, cs.y));
@@ -148,6 +252,57 @@ __global__ void __launch_bounds__(kWarps * 32) qkv_split_kernel(SplitParams p) {
   }
 }
 
+// The backward of qkv_split_kernel: p.out[] are the five head-major gradients (read),
+// p.qp / p.kvp the row-major projection gradients (written).
+template <typename T, int D>
+__global__ void __launch_bounds__(kWarps * 32) qkv_merge_kernel(SplitParams p) {
+  constexpr int kGroups = D / 8;
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+  const int n_begin = (blockIdx.x * kWarps + (threadIdx.x >> 5)) * kTokensPerWarp;
+  const int qw = p.heads * kGroups, kvw = 4 * p.kv_heads * kGroups;
+  for (int t = 0; t < kTokensPerWarp; ++t) {
+    const int n = n_begin + t;
+    if (n >= p.tokens) return;
+    const int64_t c[3] = {p.coords[3 * (int64_t)n], p.coords[3 * (int64_t)n + 1], p.coords[3 * (int64_t)n + 2]};
+    T *qrow = static_cast<T *>(const_cast<void *>(p.qp)) + ((int64_t)b * p.tokens + n) * (qw * 8);
+    T *kvrow = static_cast<T *>(const_cast<void *>(p.kvp)) + ((int64_t)b * p.tokens + n) * (kvw * 8);
+    for (int k = lane; k < qw; k += 32) {
+      const int h = k / kGroups, grp = k % kGroups;
+      float v[8];
+      load8<T>(static_cast<const T *>(p.out[0]) + (((int64_t)b * p.heads + h) * p.tokens + n) * D + 8 * grp, v);
+      rotate8<true>(v, 4 * grp, p, c);
+      store8<T>(qrow + 8 * k, v);
+    }
+    for (int k = lane; k < kvw; k += 32) {
+      const int part = k / (p.kv_heads * kGroups);   // 0 kl, 1 vl, 2 kg, 3 vg
+      const int rest = k - part * p.kv_heads * kGroups;
+      const int g = rest / kGroups, grp = rest % kGroups;
+      float v[8];
+      load8<T>(static_cast<const T *>(p.out[1 + part]) + (((int64_t)b * p.kv_heads + g) * p.tokens + n) * D + 8 * grp,
+               v);
+      if (part == 0 || part == 2) rotate8<true>(v, 4 * grp, p, c);
+      store8<T>(kvrow + 8 * k, v);
+    }
+  }
+}
+
+template <typename T>
+int launch_merge(const SplitParams &p, int head_dim, cudaStream_t s) {
+  const dim3 grid((unsigned)((p.tokens + kWarps * kTokensPerWarp - 1) / (kWarps * kTokensPerWarp)),
+                  (unsigned)p.batch);
+  switch (head_dim) {
+    case 16: qkv_merge_kernel<T, 16><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 32: qkv_merge_kernel<T, 32><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 48: qkv_merge_kernel<T, 48><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 64: qkv_merge_kernel<T, 64><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 128: qkv_merge_kernel<T, 128><<<grid, kWarps * 32, 0, s>>>(p); break;
+    default: return fail(P3D_ERR_UNSUPPORTED, "p3d_qkv_merge: head_dim %d", head_dim);
+  }
+  P3D_LAUNCH_CHECK();
+  return P3D_OK;
+}
+
 template <typename T>
 int launch_split(const SplitParams &p, int head_dim, cudaStream_t s) {
   const dim3 grid((unsigned)((p.tokens + kWarps * kTokensPerWarp - 1) / (kWarps * kTokensPerWarp)),
@@ -184,6 +339,42 @@ int launch_ln(const void *x, const void *w, const void *b, void *y, int64_t rows
   return P3D_OK;
 }
 
+template <typename T>
+int launch_ln_bwd(const void *x, const void *w, const void *dy, void *dx, float *dw_part, float *db_part,
+                  int64_t rows, int dim, float eps, unsigned blocks, cudaStream_t s) {
+  const int chunks = (dim / 8 + 31) / 32;
+  auto args = [&](auto kernel) {
+    kernel<<<blocks, kWarps * 32, 0, s>>>(static_cast<const T *>(x), static_cast<const T *>(w),
+                                          static_cast<const T *>(dy), static_cast<T *>(dx), dw_part, db_part, rows,
+                                          dim, eps);
+  };
+  switch (chunks) {
+    case 1: args(layer_norm_bwd_kernel<T, 1>); break;
+    case 2: args(layer_norm_bwd_kernel<T, 2>); break;
+    case 3: args(layer_norm_bwd_kernel<T, 3>); break;
+    case 4: args(layer_norm_bwd_kernel<T, 4>); break;
+    default: return fail(P3D_ERR_UNSUPPORTED, "p3d_layer_norm_bwd: dim %d above 1024", dim);
+  }
+  P3D_LAUNCH_CHECK();
+  return P3D_OK;
+}
+
+unsigned ln_bwd_blocks(int64_t rows) {
+  const int64_t b = (rows + kWarps - 1) / kWarps;
+  return (unsigned)(b < kLnBwdBlocks ? (b > 0 ? b : 1) : kLnBwdBlocks);
+}
+
+// workspace: dweight / dbias partials [warps, dim] each, then the row-sum scratch
+size_t ln_bwd_layout(int64_t rows, int dim, void *base, float **dw_part, float **db_part, float **tmp) {
+  const int64_t warps = (int64_t)ln_bwd_blocks(rows) * kWarps;
+  const size_t part = (size_t)warps * dim * sizeof(float);
+  char *p = static_cast<char *>(base);
+  *dw_part = reinterpret_cast<float *>(p);
+  *db_part = reinterpret_cast<float *>(p + part);
+  *tmp = reinterpret_cast<float *>(p + 2 * part);
+  return 2 * part + (size_t)sum_rows_tmp(warps, dim) * sizeof(float);
+}
+
 bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
 }  // namespace
@@ -205,21 +396,65 @@ extern "C" int p3d_layer_norm(const void *x, const void *weight, const void *bia
                            : launch_ln<__half>(x, weight, bias, y, rows, dim, eps, s);
 }
 
+namespace {
+// Arguments shared by p3d_qkv_split and p3d_qkv_merge (names as in p3d_qkv_split).
+int check_split(const char *name, const void *const (&ptrs)[7], int dtype, int batch, int heads, int kv_heads,
+                int tokens, int head_dim, const int64_t *coords, int pz, int py, int px, const float *phases, int ez,
+                int ey, int ex) {
+  P3D_CHECK_ARG(dtype == P3D_BF16 || dtype == P3D_F16, "%s: bf16 or f16 only", name);
+  for (const void *t : ptrs) P3D_CHECK_ARG(t != nullptr, "%s: null pointer", name);
+  P3D_CHECK_ARG(coords && phases, "%s: null pointer", name);
+  P3D_CHECK_ARG(batch >= 0 && heads >= 1 && kv_heads >= 1 && heads % kv_heads == 0 && tokens >= 0,
+                "%s: bad batch / head / token counts", name);
+  P3D_CHECK_ARG(head_dim % 8 == 0 && 2 * (pz + py + px) == head_dim && pz >= 0 && py >= 0 && px >= 0,
+                "%s: pairs (%d,%d,%d) do not allocate head_dim %d", name, pz, py, px, head_dim);
+  P3D_CHECK_ARG(ez >= 1 && ey >= 1 && ex >= 1, "%s: bad table extents", name);
+  for (const void *t : ptrs) P3D_CHECK_ARG(aligned16(t), "%s: 16-byte aligned tensors required", name);
+  P3D_CHECK_ARG(batch <= 65535, "%s: batch above 65535", name);
+  return P3D_OK;
+}
+}  // namespace
+
+extern "C" size_t p3d_layer_norm_bwd_workspace(int64_t rows, int dim) {
+  if (rows < 1 || dim < 8) return 0;
+  float *a, *b, *t;
+  return ln_bwd_layout(rows, dim, nullptr, &a, &b, &t);
+}
+
+extern "C" int p3d_layer_norm_bwd(const void *x, const void *weight, const void *dy, void *dx, float *dweight,
+                                  float *dbias, int dtype, int64_t rows, int dim, float eps, void *workspace,
+                                  size_t workspace_bytes, void *stream) {
+  P3D_CHECK_ARG(dtype == P3D_BF16 || dtype == P3D_F16, "p3d_layer_norm_bwd: bf16 or f16 only");
+  P3D_CHECK_ARG(x && weight && dy && dx && dweight && dbias, "p3d_layer_norm_bwd: null pointer");
+  P3D_CHECK_ARG(rows >= 1 && dim >= 8 && dim % 8 == 0, "p3d_layer_norm_bwd: rows >= 1, dim a positive multiple of 8");
+  P3D_CHECK_ARG(aligned16(x) && aligned16(weight) && aligned16(dy) && aligned16(dx),
+                "p3d_layer_norm_bwd: 16-byte aligned tensors required");
+  P3D_CHECK_ARG(eps >= 0.f, "p3d_layer_norm_bwd: negative eps");
+  float *dw_part, *db_part, *tmp;
+  const size_t need = ln_bwd_layout(rows, dim, workspace, &dw_part, &db_part, &tmp);
+  if (!workspace || workspace_bytes < need)
+    return fail(P3D_ERR_WORKSPACE, "p3d_layer_norm_bwd: workspace of %zu bytes required", need);
+  P3D_CHECK_ARG(((uintptr_t)workspace & 15) == 0, "p3d_layer_norm_bwd: 16-byte aligned workspace required");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = ln_bwd_blocks(rows);
+  const int st = dtype == P3D_BF16
+                     ? launch_ln_bwd<__nv_bfloat16>(x, weight, dy, dx, dw_part, db_part, rows, dim, eps, blocks, s)
+                     : launch_ln_bwd<__half>(x, weight, dy, dx, dw_part, db_part, rows, dim, eps, blocks, s);
+  if (st) return st;
+  const int64_t warps = (int64_t)blocks * kWarps;
+  if (int e = launch_sum_rows(dw_part, dweight, warps, dim, tmp, s)) return e;
+  return launch_sum_rows(db_part, dbias, warps, dim, tmp, s);
+}
+
 extern "C" int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl, void *vl, void *kg, void *vg,
                              int dtype, int batch, int heads, int kv_heads, int tokens, int head_dim,
                              const int64_t *coords, int pz, int py, int px, const float *phases, int ez, int ey,
                              int ex, void *stream) {
-  P3D_CHECK_ARG(dtype == P3D_BF16 || dtype == P3D_F16, "p3d_qkv_split: bf16 or f16 only");
-  P3D_CHECK_ARG(qp && kvp && q && kl && vl && kg && vg && coords && phases, "p3d_qkv_split: null pointer");
-  P3D_CHECK_ARG(batch >= 0 && heads >= 1 && kv_heads >= 1 && heads % kv_heads == 0 && tokens >= 0,
-                "p3d_qkv_split: bad batch / head / token counts");
-  P3D_CHECK_ARG(head_dim % 8 == 0 && 2 * (pz + py + px) == head_dim && pz >= 0 && py >= 0 && px >= 0,
-                "p3d_qkv_split: pairs (%d,%d,%d) do not allocate head_dim %d", pz, py, px, head_dim);
-  P3D_CHECK_ARG(ez >= 1 && ey >= 1 && ex >= 1, "p3d_qkv_split: bad table extents");
-  const void *ptrs[7] = {qp, kvp, q, kl, vl, kg, vg};
-  for (const void *t : ptrs) P3D_CHECK_ARG(aligned16(t), "p3d_qkv_split: 16-byte aligned tensors required");
+  const void *const ptrs[7] = {qp, kvp, q, kl, vl, kg, vg};
+  if (int st = check_split("p3d_qkv_split", ptrs, dtype, batch, heads, kv_heads, tokens, head_dim, coords, pz, py,
+                           px, phases, ez, ey, ex))
+    return st;
   if ((int64_t)batch * tokens == 0) return P3D_OK;
-  P3D_CHECK_ARG(batch <= 65535, "p3d_qkv_split: batch above 65535");
   SplitParams p{};
   p.qp = qp;
   p.kvp = kvp;
@@ -242,4 +477,37 @@ extern "C" int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl,
   p.phases = phases;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return dtype == P3D_BF16 ? launch_split<__nv_bfloat16>(p, head_dim, s) : launch_split<__half>(p, head_dim, s);
+}
+
+extern "C" int p3d_qkv_merge(const void *dq, const void *dkl, const void *dvl, const void *dkg, const void *dvg,
+                             void *dqp, void *dkvp, int dtype, int batch, int heads, int kv_heads, int tokens,
+                             int head_dim, const int64_t *coords, int pz, int py, int px, const float *phases, int ez,
+                             int ey, int ex, void *stream) {
+  const void *const ptrs[7] = {dqp, dkvp, dq, dkl, dvl, dkg, dvg};
+  if (int st = check_split("p3d_qkv_merge", ptrs, dtype, batch, heads, kv_heads, tokens, head_dim, coords, pz, py,
+                           px, phases, ez, ey, ex))
+    return st;
+  if ((int64_t)batch * tokens == 0) return P3D_OK;
+  SplitParams p{};
+  p.qp = dqp;
+  p.kvp = dkvp;
+  p.out[0] = const_cast<void *>(dq);
+  p.out[1] = const_cast<void *>(dkl);
+  p.out[2] = const_cast<void *>(dvl);
+  p.out[3] = const_cast<void *>(dkg);
+  p.out[4] = const_cast<void *>(dvg);
+  p.batch = batch;
+  p.heads = heads;
+  p.kv_heads = kv_heads;
+  p.tokens = tokens;
+  p.coords = coords;
+  p.pairs[0] = pz;
+  p.pairs[1] = py;
+  p.pairs[2] = px;
+  p.start[0] = 0;
+  p.start[1] = ez * pz;
+  p.start[2] = ez * pz + ey * py;
+  p.phases = phases;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return dtype == P3D_BF16 ? launch_merge<__nv_bfloat16>(p, head_dim, s) : launch_merge<__half>(p, head_dim, s);
 }

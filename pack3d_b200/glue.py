@@ -1,0 +1,111 @@
+"""Fused layer glue for the training path of :class:`PACK3DAttention` (reference
+``attention.py:53-89``): autograd functions over the library's glue kernels.
+
+* :func:`layer_norm` -- ``nn.LayerNorm`` (``attention.py:64``) as ``p3d_layer_norm`` with
+  ``p3d_layer_norm_bwd`` as its backward (dweight / dbias summed in fixed order).
+* :func:`qkv_split` -- the projection split of ``attention.py:70-81``: the row-major
+  ``to_q`` / ``to_kv`` outputs become rotated head-major q, kl, kg and head-major vl, vg in
+  one ``p3d_qkv_split`` pass; its backward, ``p3d_qkv_merge``, rotates dq, dkl, dkg back and
+  writes the row-major projection gradients in one pass (bit-identical to the inverse
+  rotation of ``rotary.py:66-70`` followed by autograd's transposes and concatenation).
+
+16-bit tensors on the GPU only; the layer falls back to its per-op path otherwise.
+"""
+from __future__ import annotations
+
+import torch
+from torch.autograd.function import once_differentiable
+
+from . import _native
+
+
+def _empty_ws(nbytes, device):
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+
+
+class _LayerNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):
+        x = x.contiguous()
+        y = torch.empty_like(x)
+        rows, dim = x.numel() // x.shape[-1], x.shape[-1]
+        with torch.cuda.device(x.device):
+            _native.check(_native.lib().p3d_layer_norm(_native.ptr(x), _native.ptr(weight), _native.ptr(bias),
+                                                       _native.ptr(y), _native.DTYPE_CODE[x.dtype], rows, dim,
+                                                       float(eps), _native.stream_of(x.device)), "p3d_layer_norm")
+        ctx.save_for_backward(x, weight)
+        ctx.eps = float(eps)
+        return y
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, dy):
+        x, weight = ctx.saved_tensors
+        dy = dy.contiguous()
+        rows, dim = x.numel() // x.shape[-1], x.shape[-1]
+        dx = torch.empty_like(x)
+        f32 = dict(dtype=torch.float32, device=x.device)
+        dw, db = torch.empty(dim, **f32), torch.empty(dim, **f32)
+        lib = _native.lib()
+        ws = _empty_ws(lib.p3d_layer_norm_bwd_workspace(rows, dim), x.device)
+        with torch.cuda.device(x.device):
+            _native.check(lib.p3d_layer_norm_bwd(_native.ptr(x), _native.ptr(weight), _native.ptr(dy), _native.ptr(dx),
+                                                 _native.ptr(dw), _native.ptr(db), _native.DTYPE_CODE[x.dtype], rows,
+                                                 dim, ctx.eps, _native.ptr(ws), ws.numel(),
+                                                 _native.stream_of(x.device)), "p3d_layer_norm_bwd")
+        return dx, dw.to(weight.dtype), db.to(weight.dtype), None
+
+
+def layer_norm(x, norm):
+    """``norm(x)`` for an ``nn.LayerNorm`` over the last dimension, in the library kernels."""
+    return _LayerNorm.apply(x, norm.weight, norm.bias, norm.eps)
+
+
+class _QKVSplit(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qp, kvp, coords, phases, pairs, extents, heads, kv_heads, head_dim):
+        b, n = qp.shape[0], qp.shape[1]
+        qp, kvp = qp.contiguous(), kvp.contiguous()
+        dev, dt = qp.device, qp.dtype
+        q = torch.empty((b, heads, n, head_dim), dtype=dt, device=dev)
+        kl, vl, kg, vg = (torch.empty((b, kv_heads, n, head_dim), dtype=dt, device=dev) for _ in range(4))
+        with torch.cuda.device(dev):
+            _native.check(_native.lib().p3d_qkv_split(
+                _native.ptr(qp), _native.ptr(kvp), _native.ptr(q), _native.ptr(kl), _native.ptr(vl), _native.ptr(kg),
+                _native.ptr(vg), _native.DTYPE_CODE[dt], b, heads, kv_heads, n, head_dim, _native.ptr(coords), *pairs,
+                _native.ptr(phases), *extents, _native.stream_of(dev)), "p3d_qkv_split")
+        ctx.save_for_backward(coords, phases)
+        ctx.meta = (pairs, extents, heads, kv_heads, head_dim, b, n, dt)
+        return q, kl, vl, kg, vg
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, dq, dkl, dvl, dkg, dvg):
+        coords, phases = ctx.saved_tensors
+        pairs, extents, heads, kv_heads, head_dim, b, n, dt = ctx.meta
+        dev = coords.device
+
+        def grad(t, h):
+            if t is None:
+                return torch.zeros((b, h, n, head_dim), dtype=dt, device=dev)
+            return t.to(dt).contiguous()
+
+        dq = grad(dq, heads)
+        dkl, dvl, dkg, dvg = (grad(t, kv_heads) for t in (dkl, dvl, dkg, dvg))
+        dqp = torch.empty((b, n, heads * head_dim), dtype=dt, device=dev)
+        dkvp = torch.empty((b, n, 4 * kv_heads * head_dim), dtype=dt, device=dev)
+        with torch.cuda.device(dev):
+            _native.check(_native.lib().p3d_qkv_merge(
+                _native.ptr(dq), _native.ptr(dkl), _native.ptr(dvl), _native.ptr(dkg), _native.ptr(dvg),
+                _native.ptr(dqp), _native.ptr(dkvp), _native.DTYPE_CODE[dt], b, heads, kv_heads, n, head_dim,
+                _native.ptr(coords), *pairs, _native.ptr(phases), *extents, _native.stream_of(dev)), "p3d_qkv_merge")
+        return dqp, dkvp, None, None, None, None, None, None, None
+
+
+def qkv_split(qp, kvp, coords, phases, pairs, extents, heads, kv_heads, head_dim):
+    """Differentiable ``p3d_qkv_split``: ``(q, kl, vl, kg, vg)`` head-major, q / kl / kg rotated.
+
+    ``coords`` int64 ``[N, 3]`` and ``phases`` (the RoPE table of ``rope.phase_tables``) on the
+    projections' device."""
+    return _QKVSplit.apply(qp, kvp, coords, phases, tuple(int(p) for p in pairs), tuple(int(e) for e in extents),
+                           int(heads), int(kv_heads), int(head_dim))

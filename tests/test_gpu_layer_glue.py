@@ -90,3 +90,83 @@ def test_fast_inference_layer_matches_the_autograd_path(cuda_device):
     assert not layer._fast_inference(x.clone().requires_grad_())
     assert (fast.float() - slow.detach().float()).abs().max().item() <= 2e-2 * max(1.0, slow.abs().max().item())
     assert _native.device_errors() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("h,g,d", [(4, 4, 48), (4, 2, 32), (8, 8, 48)])
+def test_qkv_merge_is_the_exact_backward_of_the_split(cuda_device, dtype, h, g, d):
+    from pack3d_b200 import glue
+    from pack3d_b200.rope import _rotate
+    layout = _layout((8, 12, 16), raster=False).to(cuda_device)
+    b, n = 2, layout.geometry.num_tokens
+    gen = torch.Generator(device=cuda_device).manual_seed(h + 3 * g + d)
+    pairs = balanced_pairs(d)
+    extents = layout.grid_shape
+    _, phases = phase_tables(cuda_device, pairs, extents)
+    coords = layout.coords.to(torch.int64).contiguous()
+    grads = [torch.randn(b, h, n, d, device=cuda_device, generator=gen).to(dtype)]
+    grads += [torch.randn(b, g, n, d, device=cuda_device, generator=gen).to(dtype) for _ in range(4)]
+    qp = torch.randn(b, n, h * d, device=cuda_device, generator=gen).to(dtype).requires_grad_()
+    kvp = torch.randn(b, n, 4 * g * d, device=cuda_device, generator=gen).to(dtype).requires_grad_()
+    outs = glue.qkv_split(qp, kvp, coords, phases, pairs, extents, h, g, d)
+    torch.autograd.backward(outs, grads)
+    # the per-op backward: inverse rotation (p3d_rope), then the transposes and the concatenation
+    inv = lambda t: _rotate(t, layout.coords, pairs, tuple(extents), False, inverse=True)  # noqa: E731
+    dq, dkl, dvl, dkg, dvg = inv(grads[0]), inv(grads[1]), grads[2], inv(grads[3]), grads[4]
+    want_q = dq.transpose(1, 2).reshape(b, n, h * d)
+    want_kv = torch.cat([t.transpose(1, 2).reshape(b, n, g * d) for t in (dkl, dvl, dkg, dvg)], -1)
+    assert torch.equal(qp.grad, want_q) and torch.equal(kvp.grad, want_kv)
+
+
+@pytest.mark.parametrize("dim", [192, 384])
+def test_layer_norm_backward_matches_torch(cuda_device, dim):
+    from pack3d_b200 import glue
+    gen = torch.Generator(device=cuda_device).manual_seed(dim)
+    x = (torch.randn(2, 3000, dim, device=cuda_device, generator=gen) * 2 + 0.5).to(torch.bfloat16)
+    dy = torch.randn(2, 3000, dim, device=cuda_device, generator=gen).to(torch.bfloat16)
+    norm = torch.nn.LayerNorm(dim).to(cuda_device, torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.normal_()
+        norm.bias.normal_()
+    xa = x.clone().requires_grad_()
+    glue.layer_norm(xa, norm).backward(dy)
+    got = (xa.grad, norm.weight.grad.clone(), norm.bias.grad.clone())
+    norm.zero_grad()
+    # fp32 reference of the same op
+    w32 = norm.weight.detach().float().requires_grad_()
+    b32 = norm.bias.detach().float().requires_grad_()
+    xc = x.float().requires_grad_()
+    torch.nn.functional.layer_norm(xc, (dim,), w32, b32, norm.eps).backward(dy.float())
+    want = (xc.grad, w32.grad, b32.grad)
+    for g_, w_ in zip(got, want):
+        tol = 2e-2 * max(1.0, w_.abs().max().item())
+        assert (g_.float() - w_).abs().max().item() <= tol
+    # fixed-order sums: a repeated backward is bitwise identical
+    xa2 = x.clone().requires_grad_()
+    norm.zero_grad()
+    glue.layer_norm(xa2, norm).backward(dy)
+    assert torch.equal(xa2.grad, got[0]) and torch.equal(norm.weight.grad, got[1])
+
+
+def test_fused_training_glue_matches_the_per_op_path(cuda_device):
+    layout = _layout((16, 16, 16)).to(cuda_device)
+    torch.manual_seed(0)
+    layer = PACK3DAttention(192, heads=4, kv_heads=4, head_dim=48, block_volume=64).to(cuda_device, torch.bfloat16)
+    gen = torch.Generator(device=cuda_device).manual_seed(9)
+    x = torch.randn(2, layout.geometry.num_tokens, 192, device=cuda_device, generator=gen).to(torch.bfloat16)
+    dy = torch.randn_like(x)
+    results = []
+    for fused in (True, False):
+        layer.fused_glue = fused
+        layer.zero_grad(set_to_none=True)
+        xi = x.clone().requires_grad_()
+        y = layer(xi, layout)
+        y.backward(dy)
+        results.append((y.detach(), xi.grad, {k: p.grad.clone() for k, p in layer.named_parameters()}))
+    (y0, dx0, g0), (y1, dx1, g1) = results
+    tol = lambda t: 2e-2 * max(1.0, t.float().abs().max().item())  # noqa: E731
+    assert (y0.float() - y1.float()).abs().max().item() <= tol(y1)
+    assert (dx0.float() - dx1.float()).abs().max().item() <= tol(dx1)
+    for k in g1:
+        assert (g0[k].float() - g1[k].float()).abs().max().item() <= tol(g1[k]), k
+    assert _native.device_errors() == 0
