@@ -52,6 +52,10 @@ def parse_args():
     ap.add_argument("--config4", type=int, default=0, metavar="K",
                     help="separate mode: BASELINE config 4 (128^3 field, dim 384 = 8 heads x 48) layer forward + "
                          "backward, K timed steps, on the launch's N GPUs (z-slabs for N > 1); one JSON line")
+    ap.add_argument("--allen15", type=int, default=0, metavar="K",
+                    help="separate mode: the reference's published 'allen15' preset (32x128x64 raster, dim 512, "
+                         "8 q-heads / 2 kv-heads x 64, radius 1, (1,4,4) raster blocks, pool 16), layer inference "
+                         "and forward + backward, K timed steps each; one JSON line")
     ap.add_argument("--train-only", type=int, default=0, metavar="N",
                     help="profiling mode: run the config-3 layer forward + backward N times and exit")
     ap.add_argument("--kernel-only", type=int, default=0, metavar="N",
@@ -238,6 +242,52 @@ def backward_only(args, device):
     times = timed_steps(step, args.backward_only, torch.cuda.current_stream(device))
     errors = _native.device_errors()
     print(json.dumps({"backward_only_ms": [round(t, 4) for t in times], "device_errors": errors}), flush=True)
+
+
+ALLEN15 = dict(grid=(32, 128, 64), block=(1, 4, 4), radius=1, pool_size=16, dim=512, heads=8, kv_heads=2,
+               head_dim=64)
+
+
+def allen15(args, device):
+    """The preset of the reference's only published timings (H200, Triton backend, batch 1:
+    layer inference 4.644 ms, forward + backward 15.098 ms, bf16, raster storage), on this
+    GPU: the same layer, layout, dtype and batch."""
+    from pack3d_b200 import PACK3DAttention, _native, build_layout
+    cfg = ALLEN15
+    layout = build_layout(cfg["grid"], cfg["block"], radius=cfg["radius"], pool_size=cfg["pool_size"],
+                          layout="raster_block").to(device)
+    n = layout.geometry.num_tokens
+    torch.manual_seed(0)
+    layer = PACK3DAttention(cfg["dim"], heads=cfg["heads"], kv_heads=cfg["kv_heads"], head_dim=cfg["head_dim"],
+                            block_volume=math.prod(cfg["block"])).to(device=device, dtype=torch.bfloat16)
+    gen = torch.Generator(device=device).manual_seed(15)
+    x = torch.randn(1, n, cfg["dim"], device=device, generator=gen).to(torch.bfloat16)
+    dy = torch.randn_like(x)
+    stream = torch.cuda.current_stream(device)
+
+    def infer():
+        with torch.inference_mode():
+            layer(x, layout)
+
+    xg = x.clone().requires_grad_()
+
+    def train():
+        layer.zero_grad(set_to_none=True)
+        xg.grad = None
+        layer(xg, layout).backward(dy)
+
+    out = {}
+    for name, fn in (("inference", infer), ("fwd_bwd", train)):
+        for _ in range(max(args.warmup, 2)):
+            fn()
+        torch.cuda.synchronize(device)
+        times = timed_steps(fn, args.allen15, stream)
+        out[name] = round(statistics.median(times), 4)
+    errors = _native.device_errors()
+    print(json.dumps({"mode": "allen15", "inference_ms": out["inference"], "fwd_bwd_ms": out["fwd_bwd"],
+                      "reference_h200_ms": {"inference": 4.644, "fwd_bwd": 15.098},
+                      "tokens": n, "summaries": layout.geometry.num_summaries, "stencil": layout.geometry.stencil,
+                      "eager": True, "device_errors": errors}), flush=True)
 
 
 def train_only(args, device):
@@ -477,6 +527,8 @@ def run_b200(args, rank, world, device):
         return backward_only(args, device)
     if args.train_only:
         return train_only(args, device)
+    if args.allen15:
+        return allen15(args, device)
     dtype = torch.bfloat16
     layout = make_layout(CONFIG["grid"]).to(device)
     geom = layout.geometry

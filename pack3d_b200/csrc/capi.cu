@@ -199,8 +199,12 @@ int gather_rows(const void *src, void *dst, const int32_t *map, int64_t slabs, i
 // The tensor-core backward needs what the tensor-core forward needs, and at least two
 // summaries (with one the global softmax is constant: no score gradient, reference
 // kernels.py:198-199).
+// The tensor-core backward kernels (dQ, local dK/dV) are built for radius 2 only; the
+// forward also takes radius 1.
+bool radius_two(const p3d_operator *op) { return op->radius[0] == 2 && op->radius[1] == 2 && op->radius[2] == 2; }
+
 bool use_stencil_bwd(const p3d_operator *op) {
-  return op->stencil && !(op->options & P3D_OPT_INDEXED_ONLY) && summaries_of(op) >= 2 &&
+  return op->stencil && !(op->options & P3D_OPT_INDEXED_ONLY) && summaries_of(op) >= 2 && radius_two(op) &&
          stencil_fwd_supported(op->dtype, op->head_dim, op->radius, summaries_of(op));
 }
 
@@ -356,6 +360,7 @@ int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, 
     if (int st = launch_pool_fwd(pool_args(op, sk, sv), s)) return st;
   if (use_stencil_path(op, flags)) {
     StencilFwdArgs a{};
+    a.radius = op->radius[0];
     a.dtype = op->dtype;
     a.gate_dtype = op->gate_dtype;
     a.batch = op->batch;
@@ -417,7 +422,7 @@ int p3d_attn_fwd_slab(const p3d_operator *op, const p3d_slab *slab, void *y, con
                 "p3d_attn_fwd_slab: needs a complete stencil in raster storage");
   P3D_CHECK_ARG(!(op->options & P3D_OPT_INDEXED_ONLY), "p3d_attn_fwd_slab: has no indexed form");
   if (!stencil_fwd_supported(op->dtype, op->head_dim, op->radius, slab->summaries))
-    return fail(P3D_ERR_UNSUPPORTED, "p3d_attn_fwd_slab: needs bf16/f16, head_dim 16/32/48/64, radius 2 and sm_100");
+    return fail(P3D_ERR_UNSUPPORTED, "p3d_attn_fwd_slab: needs bf16/f16, head_dim 16/32/48/64, radius 1 or 2 and sm_100");
   const int nz = op->grid[0], r = op->radius[0];
   const int need_lo = std::max(0, slab->center_z0 - r);
   const int need_hi = std::min(slab->global_planes, slab->center_z0 + nz + r);
@@ -430,6 +435,7 @@ int p3d_attn_fwd_slab(const p3d_operator *op, const p3d_slab *slab, void *y, con
                 slab->halo_z0 + slab->halo_planes, need_lo, need_hi);
   P3D_CHECK_ARG(slab->summaries >= 1, "p3d_attn_fwd_slab: no summaries");
   StencilFwdArgs a{};
+  a.radius = op->radius[0];
   a.dtype = op->dtype;
   a.gate_dtype = op->gate_dtype;
   a.batch = op->batch;
@@ -685,7 +691,7 @@ static int check_slab(const p3d_operator *op, const p3d_slab *slab, const char *
   P3D_CHECK_ARG(op->stencil && !op->raster_to_packed, "%s: needs a complete stencil in raster storage", what);
   P3D_CHECK_ARG(!(op->options & P3D_OPT_INDEXED_ONLY), "%s: has no indexed form", what);
   if (!stencil_fwd_supported(op->dtype, op->head_dim, op->radius, slab->summaries) || slab->summaries < 2 ||
-      !global_dkv_tc_supported(op->dtype, op->head_dim, slab->summaries))
+      !radius_two(op) || !global_dkv_tc_supported(op->dtype, op->head_dim, slab->summaries))
     return fail(P3D_ERR_UNSUPPORTED, "%s: needs bf16/f16, head_dim 16/32/48/64, radius 2, >= 2 summaries, sm_100",
                 what);
   const int nz = op->grid[0], r = op->radius[0];

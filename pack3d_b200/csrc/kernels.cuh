@@ -104,6 +104,7 @@ struct StencilFwdArgs {
   void *y, *ol, *og;                  // ol/og nullable
   float *lse_l, *lse_g;               // nullable
   int y_rows;                         // y token-major [B,N,H,D]
+  int radius;                         // stencil radius (1 or 2, all axes)
 };
 // Read-and-clear the device failure bits of the tensor-core kernel files (OR-ed into *flags).
 int take_fwd_errors(unsigned *flags);

@@ -44,12 +44,7 @@ using namespace sm100;
 
 __device__ unsigned g_fwd_errors = 0;  // failure bits of the kernels in this file
 
-constexpr int kR = 2;                               // stencil radius handled here
 constexpr int kTZ = 4, kTY = 4, kTX = 8;            // one 128-row query tile
-constexpr int kHY = kTY + 2 * kR, kHX = kTX + 2 * kR, kHZ = kTZ + 2 * kR;
-constexpr int kKeys = kHY * kHX;                    // 96 keys per chunk (a halo plane)
-constexpr int kLocalChunks = kHZ;                   // 8 halo planes per tile
-constexpr int kSumRows = kKeys;                     // summaries per global chunk
 constexpr int kRows = 128;                          // queries per tile
 constexpr int kThreads = 192;
 constexpr int kProducerWarp = 4, kMmaWarp = 5;
@@ -57,13 +52,27 @@ constexpr uint32_t kTmemCols = 256;                 // two CTAs per SM
 constexpr float kNegInf = -__builtin_huge_valf();
 constexpr uint64_t kWaitNs = 2000000000ull;        // every mbarrier wait gives up after 2 s
 
-static_assert(kKeys % 32 == 0, "chunk size must suit the MMA and TMEM access shapes");
+// Chunk geometry of a radius-R stencil (R = 1 or 2): a local chunk is one halo plane of the
+// tile, a kHY x kHX (y, x) window; chunks are kKeys wide (the window rounded up to 32 keys;
+// the padding rows of every ring stage are zero and masked) and global chunks take kKeys
+// summaries.  TMEM: S buffers [0, kKeys) and [kKeys, 2 kKeys), O [2 kKeys, 2 kKeys + D).
+template <int R>
+struct Geo {
+  static constexpr int kR = R;
+  static constexpr int kHY = kTY + 2 * R, kHX = kTX + 2 * R, kHZ = kTZ + 2 * R;
+  static constexpr int kWin = kHY * kHX;                // 96 (R = 2), 60 (R = 1)
+  static constexpr int kKeys = (kWin + 31) / 32 * 32;   // 96, 64
+  static constexpr int kLocalChunks = kHZ;              // 8, 6 halo planes per tile
+  static constexpr int kSumRows = kKeys;                // summaries per global chunk
+  static constexpr uint32_t kSBuf = kKeys, kColO = 2 * kKeys;
+  static_assert(kKeys % 32 == 0 && kKeys <= 96, "chunk size must suit the MMA, TMEM and register budgets");
+};
 
-template <int D>
+template <int D, int KEYS>
 struct Cfg {
   static constexpr int kK = D / 16;                 // 16-channel boxes per row
   static constexpr int kBoxQ = kRows * 32;          // one box = rows x 32 bytes
-  static constexpr int kBoxK = kKeys * 32;          // 3072
+  static constexpr int kBoxK = KEYS * 32;           // 3072 (96 keys), 2048 (64)
   static constexpr int kQBytes = kK * kBoxQ;        // the query tile
   static constexpr int kKeyBytes = kK * kBoxK;      // one chunk of K (or V)
   static constexpr int kStageBytes = (2 * kKeyBytes + 1023) / 1024 * 1024;  // K, V
@@ -81,9 +90,6 @@ struct Cfg {
   static_assert(kStages >= 3 && kStages <= 4, "the ring must hold chunks c .. c+2");
   static_assert(kSmemBytes <= kMaxSmem, "shared memory budget");
 };
-
-// TMEM columns: S buffers [0, 96) and [96, 192), O [192, 192 + D).
-constexpr uint32_t kSBuf = 96, kColO = 192;
 
 // S(c) is complete when its commit arrives: S(0), S(1) commit to kSReady[c], and S(c),
 // c >= 2, to kEmpty[(c-2) % kStages]: S(c) is issued after PV(c-2) has completed (and every
@@ -215,12 +221,16 @@ __device__ __forceinline__ float row_max(const float *s) {
   return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, int R>
 __global__ void __launch_bounds__(kThreads, 2)
     stencil_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkl,
                        const __grid_constant__ CUtensorMap tvl, const __grid_constant__ CUtensorMap tsk,
                        const __grid_constant__ CUtensorMap tsv, const FwdParams p) {
-  using C = Cfg<D>;
+  using G = Geo<R>;
+  constexpr int kR = G::kR, kHY = G::kHY, kHX = G::kHX, kWin = G::kWin, kKeys = G::kKeys;
+  constexpr int kLocalChunks = G::kLocalChunks, kSumRows = G::kSumRows;
+  constexpr uint32_t kSBuf = G::kSBuf, kColO = G::kColO;
+  using C = Cfg<D, kKeys>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[kNumBars];
   __shared__ uint32_t tmem_holder;
@@ -267,6 +277,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     s_sl[i] = p.sl[i];
     s_sg[i] = p.sg[i];
   }
+  if constexpr (kWin < kKeys) {
+    // The TMA boxes of a local chunk fill kWin of the kKeys rows of every 16-channel box; the
+    // rest must read as zeros (masked scores, zero V rows) until the global chunks, which
+    // fill whole boxes, reuse the stage.  Zero the ring once, then order these generic-proxy
+    // stores before the tensor cores' (async-proxy) reads.
+    uint4 *ring_v = reinterpret_cast<uint4 *>(smem_raw + (base - raw) + C::kQBytes);
+    for (int i = tid; i < C::kStages * C::kStageBytes / 16; i += kThreads) ring_v[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
+  }
   if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(&tmem_holder), kTmemCols);
     tmem_relinquish();
@@ -301,7 +320,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         const uint32_t stage = ring + s * C::kStageBytes;
         const uint32_t full = bar(kFull + s);
-        mbar_expect_tx(full, 2 * C::kKeyBytes);
+        // a local chunk's boxes hold kWin rows each, a global chunk's all kKeys (rows past M
+        // are zero-filled and still counted)
+        mbar_expect_tx(full, ch < kLocalChunks ? 2 * C::kK * kWin * 32 : 2 * C::kKeyBytes);
         if (ch < kLocalChunks) {
           const int z = p.qz0 + z0 - kR + ch - p.kz0;  // plane in the K/V buffer
           for (int c = 0; c < C::kK; ++c) {
@@ -568,9 +589,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 // ---------------------------------------------------------------------- host side
 
-template <int D, bool BF16>
+template <int D, bool BF16, int R>
 int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
-  using C = Cfg<D>;
+  using G = Geo<R>;
+  constexpr int kHY = G::kHY, kHX = G::kHX, kSumRows = G::kSumRows;
+  using C = Cfg<D, G::kKeys>;
   const int Z = a.grid[0], Y = a.grid[1], X = a.grid[2];
   const uint64_t es = 2;
   const uint64_t bh = (uint64_t)a.batch * a.heads, bgs = (uint64_t)a.batch * a.kv_heads;
@@ -627,7 +650,7 @@ int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
   const int64_t units = (int64_t)bh * p.tiles_z * p.tiles_y * p.tiles_x;
   if (units <= 0) return P3D_OK;
   if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");
-  auto kernel = stencil_fwd_kernel<D, BF16>;
+  auto kernel = stencil_fwd_kernel<D, BF16, R>;
   static bool configured = false;
   if (!configured) {
     P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
@@ -643,21 +666,30 @@ int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
 bool stencil_fwd_supported(int dtype, int head_dim, const int radius[3], int summaries) {
   if (dtype != P3D_BF16 && dtype != P3D_F16) return false;
   if (head_dim != 16 && head_dim != 32 && head_dim != 48 && head_dim != 64) return false;
-  if (radius[0] != kR || radius[1] != kR || radius[2] != kR) return false;
+  if (radius[0] != radius[1] || radius[1] != radius[2] || (radius[0] != 1 && radius[0] != 2)) return false;
   if (summaries < 1) return false;
   DeviceInfo info;
   if (device_info(&info) != P3D_OK || info.major != 10) return false;
   return true;
 }
 
-int launch_stencil_fwd(const StencilFwdArgs &a, cudaStream_t s) {
+template <int R>
+int launch_fwd_radius(const StencilFwdArgs &a, cudaStream_t s) {
   const bool bf16 = a.dtype == P3D_BF16;
   switch (a.head_dim) {
-    case 16: return bf16 ? launch_t<16, true>(a, s) : launch_t<16, false>(a, s);
-    case 32: return bf16 ? launch_t<32, true>(a, s) : launch_t<32, false>(a, s);
-    case 48: return bf16 ? launch_t<48, true>(a, s) : launch_t<48, false>(a, s);
-    case 64: return bf16 ? launch_t<64, true>(a, s) : launch_t<64, false>(a, s);
+    case 16: return bf16 ? launch_t<16, true, R>(a, s) : launch_t<16, false, R>(a, s);
+    case 32: return bf16 ? launch_t<32, true, R>(a, s) : launch_t<32, false, R>(a, s);
+    case 48: return bf16 ? launch_t<48, true, R>(a, s) : launch_t<48, false, R>(a, s);
+    case 64: return bf16 ? launch_t<64, true, R>(a, s) : launch_t<64, false, R>(a, s);
     default: return fail(P3D_ERR_UNSUPPORTED, "stencil forward: head_dim %d", a.head_dim);
+  }
+}
+
+int launch_stencil_fwd(const StencilFwdArgs &a, cudaStream_t s) {
+  switch (a.radius) {
+    case 1: return launch_fwd_radius<1>(a, s);
+    case 2: return launch_fwd_radius<2>(a, s);
+    default: return fail(P3D_ERR_UNSUPPORTED, "stencil forward: radius %d", a.radius);
   }
 }
 

@@ -85,3 +85,38 @@ def test_stencil_forward_is_deterministic(cuda_device):
     a, _ = _run(inputs, layout.geometry, cuda_device, save_state=False)
     b, _ = _run(inputs, layout.geometry, cuda_device, save_state=False)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("grid,block,pool,kind,b,h,g,d,dtype", [
+    ((8, 8, 16), (4, 4, 4), 1, "cubes", 1, 4, 4, 48, torch.bfloat16),
+    ((8, 32, 16), (1, 4, 4), 16, "raster_block", 1, 8, 2, 64, torch.bfloat16),   # the allen15 preset, small
+    ((6, 12, 20), (1, 4, 4), 4, "raster_block", 2, 4, 2, 32, torch.float16),     # partial tiles on every axis
+    ((4, 8, 8), (4, 4, 4), 1, "cubes", 1, 2, 2, 16, torch.bfloat16),
+])
+def test_radius_one_stencil_forward_matches_indexed_and_oracle(cuda_device, grid, block, pool, kind, b, h, g, d,
+                                                               dtype):
+    """Radius 1: 6x10 halo windows padded to 64-key chunks, 6 halo planes."""
+    if kind == "cubes":
+        layout = build_layout(grid, block, radius=1, pool_size=pool)
+        layout = layout.repack(layout.order.argsort())
+    else:
+        layout = build_layout(grid, block, radius=1, pool_size=pool, layout="raster_block")
+    geom = layout.geometry
+    assert geom.stencil == (tuple(grid), (1, 1, 1))
+    n = geom.num_tokens
+    raw = grid_inputs(n, b, h, g, d, torch.float32, sum(grid) + d, True, volume=block[0] * block[1] * block[2])
+    inputs = [oracle.axial_rope(raw[i], layout.coords) if i in (0, 1, 3) else raw[i] for i in range(5)]
+    inputs = [t.to(dtype) for t in inputs] + raw[5:]
+    y_tc, (sk, sv, ol, og, lse_l, lse_g) = _run(inputs, geom, cuda_device)
+    y_ix, (_, _, ol_i, og_i, ll_i, lg_i) = _run(inputs, geom, cuda_device, force_indexed=True)
+    torch.cuda.synchronize()
+    assert _native.device_errors() == 0
+    tol = 2e-2
+    assert (y_tc.float() - y_ix.float()).abs().max().item() <= tol
+    assert (ol.float() - ol_i.float()).abs().max().item() <= tol
+    assert (og.float() - og_i.float()).abs().max().item() <= tol
+    assert (lse_l - ll_i).abs().max().item() <= 1e-2
+    assert (lse_g - lg_i).abs().max().item() <= 1e-2
+    want = oracle.core_forward(*[t.float() if t.dtype != torch.float32 else t for t in inputs[:5]], *inputs[5:],
+                               geom.neighbors, geom.blocks, pool, chunk=2048)
+    assert (y_tc.float().cpu() - want["y"].float()).abs().max().item() <= tol
