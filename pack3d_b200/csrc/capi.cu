@@ -199,12 +199,12 @@ int gather_rows(const void *src, void *dst, const int32_t *map, int64_t slabs, i
 // The tensor-core backward needs what the tensor-core forward needs, and at least two
 // summaries (with one the global softmax is constant: no score gradient, reference
 // kernels.py:198-199).
-// The tensor-core backward kernels (dQ, local dK/dV) are built for radius 2 only; the
-// forward also takes radius 1.
+// The z-slab (multi-GPU) backward is built and tested for radius 2, the BASELINE radius;
+// the single-GPU tensor-core kernels take radius 1 or 2.
 bool radius_two(const p3d_operator *op) { return op->radius[0] == 2 && op->radius[1] == 2 && op->radius[2] == 2; }
 
 bool use_stencil_bwd(const p3d_operator *op) {
-  return op->stencil && !(op->options & P3D_OPT_INDEXED_ONLY) && summaries_of(op) >= 2 && radius_two(op) &&
+  return op->stencil && !(op->options & P3D_OPT_INDEXED_ONLY) && summaries_of(op) >= 2 &&
          stencil_fwd_supported(op->dtype, op->head_dim, op->radius, summaries_of(op));
 }
 
@@ -516,6 +516,7 @@ int p3d_attn_bwd(const p3d_operator *op, const void *dy, const void *sk, const v
   const IndexedArgs a = indexed_args(op, sk, sv);
   if (use_stencil_bwd(op)) {
     StencilBwdArgs t{};
+    t.radius = op->radius[0];
     t.dtype = op->dtype;
     t.batch = op->batch;
     t.heads = op->heads;
@@ -744,6 +745,7 @@ int p3d_bwd_attn_slab(const p3d_operator *op, const p3d_slab *slab, const void *
   attn_slab_layout(op, slab->summaries, workspace, workspace_bytes, &dk_part, &dv_part, &splits, &per_split);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   StencilBwdArgs t{};
+  t.radius = op->radius[0];
   t.dtype = op->dtype;
   t.batch = op->batch;
   t.heads = op->heads;

@@ -115,6 +115,7 @@ int launch_stencil_fwd(const StencilFwdArgs &a, cudaStream_t s);
 // Tensor-core backward over a complete radius-2 stencil (stencil_bwd.cu).
 struct StencilBwdArgs {
   int dtype;
+  int radius;                           // stencil radius (1 or 2, all axes)
   int batch, heads, kv_heads, head_dim, summaries;
   int grid[3];                          // centre buffer (queries for dQ, keys for dK / dV)
   // z-slab extents (whole volume: global_planes = k_planes = grid[0], q_z0 = k_z0 = 0):

@@ -1,10 +1,10 @@
 // Stage (d), query side: dQ of the fused local + global attention on tensor cores.
 //
 // Restates the query-gradient half of the reference backward (kernels.py:131-150 local,
-// :180-206 global; stencil.py:91-147 for the spatial local form) for a complete radius-2
-// voxel stencil in bf16 / f16.  With P recomputed from the saved logsumexp,
+// :180-206 global; stencil.py:91-147 for the spatial local form) for a complete radius-1
+// or radius-2 voxel stencil in bf16 / f16.  With P recomputed from the saved logsumexp,
 //   dS = P * (dO V^T - Delta) / sqrt(D),   dQ = dS K
-// per branch (local: dO = dO_l, K/V = the 5x5x5 neighbours; global: dO = dO_g, K/V = all
+// per branch (local: dO = dO_l, K/V = the 3x3x3 or 5x5x5 neighbours; global: dO = dO_g, K/V = all
 // summaries).  dS is rounded to the storage dtype before the product (the reference does
 // the same for the global branch, kernels.py:197); here the rounded operand is P (dP -
 // Delta) and the 1/sqrt(D) is applied once to the fp32 dQ accumulator (one multiply per
@@ -14,10 +14,12 @@
 //
 // Work unit and chunk sequence are those of the forward kernel (stencil_fwd.cu): one
 // (batch, head) and a 4x4x8 tile of 128 queries per CTA, two CTAs per SM; 8 local chunks
-// (halo planes of an 8x12 window) then ceil(M/96) global chunks.  TMEM (256 columns) holds
-// S [0, 96), dP [96, 192) and the dQ accumulator [192, 192 + D).  Per chunk the MMA thread
+// (halo planes of an 8x12 window) then ceil(M/96) global chunks at radius 2; 6 planes of a
+// 6x10 window padded to 64 keys, and 64-summary chunks, at radius 1 (BGeo).  TMEM (256
+// columns) holds S [0, W), dP [W, 2W) and the dQ accumulator [2W, 2W + D), W the chunk
+// width (96 or 64).  Per chunk the MMA thread
 // issues S = Q K^T and dP = dO V^T; the softmax warps turn them into dS, written back as
-// 16-bit pairs over the first 48 dP columns, and the MMA thread accumulates dQ += dS K with
+// 16-bit pairs over the first W/2 dP columns, and the MMA thread accumulates dQ += dS K with
 // dS as the TMEM A operand and the K chunk (already in shared memory for S) read MN-major
 // as B.  S of the next chunk is issued as soon as the softmax warps have released this
 // chunk, while dQ of this chunk runs; dP of the next chunk waits for dQ to finish reading
@@ -40,13 +42,23 @@ using namespace sm100;
 
 __device__ unsigned g_bwd_errors = 0;  // failure bits of the kernels in this file
 
-constexpr int kR = 2;
 constexpr int kTZ = 4, kTY = 4, kTX = 8;
-constexpr int kHY = kTY + 2 * kR, kHX = kTX + 2 * kR, kHZ = kTZ + 2 * kR;
-constexpr int kKeys = kHY * kHX;  // 96 keys per chunk
-constexpr int kLocalChunks = kHZ;
-constexpr int kSumRows = kKeys;
 constexpr int kRows = 128;
+
+// Chunk geometry of a radius-R stencil (R = 1 or 2), as in the forward kernel: a halo plane
+// of a 4x4x8 tile is a kHY x kHX window of kWin keys (or queries), padded to kKeys (a
+// multiple of 32); the padding rows of the ring are zero and masked.
+template <int R>
+struct BGeo {
+  static constexpr int kR = R;
+  static constexpr int kHY = kTY + 2 * R, kHX = kTX + 2 * R, kHZ = kTZ + 2 * R;
+  static constexpr int kWin = kHY * kHX;                // 96 (R = 2), 60 (R = 1)
+  static constexpr int kKeys = (kWin + 31) / 32 * 32;   // 96, 64
+  static constexpr int kLocalChunks = kHZ;              // 8, 6
+  static constexpr int kSumRows = kKeys;
+  static constexpr int kHalf = kKeys / 2;               // query columns per softmax warp (dK / dV)
+  static_assert(kKeys % 32 == 0 && kHalf % 16 == 0, "chunk width must suit the MMA and TMEM shapes");
+};
 constexpr int kThreads = 320;
 constexpr int kProducerWarp = 8, kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
@@ -57,11 +69,11 @@ constexpr int kDqThreads = 192;                   // one tile per CTA, two CTAs 
 constexpr int kDqProducerWarp = 4, kDqMmaWarp = 5;
 constexpr uint32_t kDqTmemCols = 256;
 
-template <int D>
+template <int D, int KEYS>
 struct DqCfg {
   static constexpr int kK = D / 16;
   static constexpr int kBoxQ = kRows * 32;
-  static constexpr int kBoxK = kKeys * 32;
+  static constexpr int kBoxK = KEYS * 32;
   static constexpr int kQBytes = kK * kBoxQ;      // the 128-row tile of Q, dO_l or dO_g
   static constexpr int kKeyBytes = kK * kBoxK;    // one chunk of K or V
   static constexpr int kStageBytes = (2 * kKeyBytes + 1023) / 1024 * 1024;
@@ -77,8 +89,6 @@ struct DqCfg {
   static_assert(kStages >= 2, "the ring must hold two chunks");
   static_assert(kSmemBytes <= kMaxSmem, "shared memory budget");
 };
-
-constexpr uint32_t kColS = 0, kColDP = 96, kColDQ = 192;
 
 enum DqBar {
   kQFull = 0,
@@ -125,13 +135,18 @@ __device__ __forceinline__ float round_storage(float v) {
   return r.x;
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, int R>
 __global__ void __launch_bounds__(kDqThreads, 2)
     stencil_bwd_dq_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdol,
                           const __grid_constant__ CUtensorMap tdog, const __grid_constant__ CUtensorMap tkl,
                           const __grid_constant__ CUtensorMap tvl, const __grid_constant__ CUtensorMap tsk,
                           const __grid_constant__ CUtensorMap tsv, const DqParams p) {
-  using C = DqCfg<D>;
+  using G = BGeo<R>;
+  constexpr int kR = G::kR, kHY = G::kHY, kHX = G::kHX, kWin = G::kWin, kKeys = G::kKeys;
+  constexpr int kLocalChunks = G::kLocalChunks, kSumRows = G::kSumRows;
+  // TMEM: S [0, kKeys), dP [kKeys, 2 kKeys) (dS written back over its first half), dQ after
+  constexpr uint32_t kColS = 0, kColDP = kKeys, kColDQ = 2 * kKeys;
+  using C = DqCfg<D, kKeys>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[kNumBars];
   __shared__ uint32_t tmem_holder;
@@ -172,6 +187,13 @@ __global__ void __launch_bounds__(kDqThreads, 2)
     mbar_init(bar(kDrain), 1);
     fence_mbar_init();
   }
+  if constexpr (kWin < kKeys) {
+    // local chunks fill kWin of the kKeys rows of each box: the rest reads as zeros (see the
+    // forward kernel) until a global chunk reuses the stage
+    uint4 *ring_v = reinterpret_cast<uint4 *>(smem_raw + (base - raw) + 3 * C::kQBytes);
+    for (int i = tid; i < C::kStages * C::kStageBytes / 16; i += kDqThreads) ring_v[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
+  }
   if (warp == kDqMmaWarp) {
     tmem_alloc(smem_u32(&tmem_holder), kDqTmemCols);
     tmem_relinquish();
@@ -210,7 +232,7 @@ __global__ void __launch_bounds__(kDqThreads, 2)
           break;
         const uint32_t stage = ring + s * C::kStageBytes;
         const uint32_t full = bar(kFull + s);
-        mbar_expect_tx(full, 2 * C::kKeyBytes);
+        mbar_expect_tx(full, ch < kLocalChunks ? 2 * C::kK * kWin * 32 : 2 * C::kKeyBytes);
         if (ch < kLocalChunks) {
           const int z = p.qz0 + z0 - kR + ch - p.kz0;  // plane in the K/V buffer
           for (int c = 0; c < C::kK; ++c) {
@@ -233,7 +255,7 @@ __global__ void __launch_bounds__(kDqThreads, 2)
   } else if (warp == kDqMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_f16(128, kKeys, BF16, false);  // S and dP: N = 96, K-major B
+      constexpr uint32_t idesc_s = idesc_f16(128, kKeys, BF16, false);  // S and dP: N = kKeys, K-major B
       constexpr uint32_t idesc_dq = idesc_f16(128, D, BF16, true);     // dQ: N = D, B = K read MN-major
       uint32_t commits[kNumBars];
       for (int i = 0; i < kNumBars; ++i) commits[i] = 0u;
@@ -461,9 +483,11 @@ __global__ void __launch_bounds__(kDqThreads, 2)
   }
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, int R>
 int launch_dq_t(const StencilBwdArgs &a, cudaStream_t stream) {
-  using C = DqCfg<D>;
+  using G = BGeo<R>;
+  constexpr int kHY = G::kHY, kHX = G::kHX, kSumRows = G::kSumRows;
+  using C = DqCfg<D, G::kKeys>;
   const int Z = a.grid[0], Y = a.grid[1], X = a.grid[2];
   const uint64_t es = 2;
   const uint64_t bh = (uint64_t)a.batch * a.heads, bgs = (uint64_t)a.batch * a.kv_heads;
@@ -517,7 +541,7 @@ int launch_dq_t(const StencilBwdArgs &a, cudaStream_t stream) {
   const int64_t units = (int64_t)bh * p.tiles_z * p.tiles_y * p.tiles_x;
   if (units <= 0) return P3D_OK;
   if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");
-  auto kernel = stencil_bwd_dq_kernel<D, BF16>;
+  auto kernel = stencil_bwd_dq_kernel<D, BF16, R>;
   static bool configured = false;
   if (!configured) {
     P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
@@ -946,19 +970,20 @@ int launch_gkv_t(const GlobalDkvArgs &a, cudaStream_t stream) {
 // inside the bf16 tolerance).  Each CTA writes its own keys' dK / dV: no atomics, no
 // partials.
 //
-// TMEM: S^T [0, 96), dP^T [96, 192), P^T [192, 240), dS^T [240, 288), dK [288, 288 + D),
-// dV [288 + D, 288 + 2D).  Eight softmax warps (warp w: TMEM lanes 32(w%4).., query columns
-// 48(w/4)..+48); the protocol is the global dSK / dSV kernel's.
-constexpr uint32_t kLColS = 0, kLColDP = 96, kLColP = 192, kLColDS = 240, kLColAcc = 288;
-
-template <int D>
+// TMEM (W = kKeys, 96 at radius 2): S^T [0, W), dP^T [W, 2W), P^T [2W, 2.5W), dS^T
+// [2.5W, 3W), dK [3W, 3W + D), dV [3W + D, 3W + 2D).  Eight softmax warps (warp w: TMEM
+// lanes 32(w%4).., query columns (W/2)(w/4)..+W/2); the protocol is the global dSK / dSV
+// kernel's.
+template <int D, int KEYS>
 struct LkvCfg {
+  static constexpr uint32_t kLColS = 0, kLColDP = KEYS, kLColP = 2 * KEYS, kLColDS = 2 * KEYS + KEYS / 2,
+                            kLColAcc = 3 * KEYS;
   static constexpr int kK = D / 16;
   static constexpr int kBoxT = kRows * 32;           // key tile: 128 rows x 16 channels
-  static constexpr int kBoxP = kKeys * 32;           // query plane: 96 rows x 16 channels
+  static constexpr int kBoxP = KEYS * 32;            // query plane: KEYS rows x 16 channels
   static constexpr int kTileBytes = kK * kBoxT;
   static constexpr int kPlaneBytes = kK * kBoxP;
-  static constexpr int kVals = kKeys * 4;             // lse (or Delta) of one plane, fp32
+  static constexpr int kVals = KEYS * 4;              // lse (or Delta) of one plane, fp32
   static constexpr int kStageBytes = (2 * kPlaneBytes + 2 * kVals + 1023) / 1024 * 1024;
   static constexpr int kFixed = 2 * kTileBytes + 1024;
   static constexpr int kRoom = (227 * 1024 - 2048 - kFixed) / kStageBytes;
@@ -982,12 +1007,17 @@ struct LkvParams {
   void *dkl, *dvl;               // [B*G, N, D] in the layout's row order
 };
 
-template <int D, bool BF16>
+template <int D, bool BF16, int R>
 __global__ void __launch_bounds__(kThreads, 1)
     stencil_bwd_dkv_kernel(const __grid_constant__ CUtensorMap tkl, const __grid_constant__ CUtensorMap tvl,
                            const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
                            const LkvParams p) {
-  using C = LkvCfg<D>;
+  using G = BGeo<R>;
+  constexpr int kR = G::kR, kHX = G::kHX, kWin = G::kWin, kKeys = G::kKeys, kHalf = G::kHalf;
+  constexpr int kLocalChunks = G::kLocalChunks;
+  using C = LkvCfg<D, kKeys>;
+  constexpr uint32_t kLColS = C::kLColS, kLColDP = C::kLColDP, kLColP = C::kLColP, kLColDS = C::kLColDS,
+                     kLColAcc = C::kLColAcc;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[kGNumBars];
   __shared__ uint32_t tmem_holder;
@@ -1023,6 +1053,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar(kGPdsFree), 1);
     mbar_init(bar(kGDrain), 1);
     fence_mbar_init();
+  }
+  if constexpr (kWin < kKeys) {
+    // the query planes fill kWin of the kKeys rows of each box: the rest reads as zeros
+    uint4 *ring_v = reinterpret_cast<uint4 *>(ring_ptr);
+    for (int i = tid; i < C::kStages * C::kStageBytes / 16; i += kThreads) ring_v[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
   }
   if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(&tmem_holder), kTmemCols);
@@ -1062,14 +1098,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t full = bar(kGFull + s);
       const int bh = chunk_head(ch), zp = chunk_plane(ch);
       if (lane == 0) {
-        mbar_expect_tx(full, 2 * C::kPlaneBytes);
+        mbar_expect_tx(full, 2 * C::kK * kWin * 32);
         for (int c = 0; c < C::kK; ++c) {
           tma_load_5d(stage + c * C::kBoxP, &tq, full, 16 * c, x0 - kR, y0 - kR, zp - p.xz0, bh);
           tma_load_5d(stage + C::kPlaneBytes + c * C::kBoxP, &tdo, full, 16 * c, x0 - kR, y0 - kR, zp - p.xz0,
                       bh);
         }
       }
-      // lse (as log2) and Delta of the plane's 96 queries; +inf outside the volume (P = 0).
+      // lse (as log2) and Delta of the plane's kWin queries; +inf outside the volume and on
+      // the padding columns (P = 0).
       // All loads are issued before any store, so they overlap.
       float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kPlaneBytes);
       float l[kKeys / 32], dl[kKeys / 32];
@@ -1077,7 +1114,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; k < kKeys / 32; ++k) {
         const int j = lane + 32 * k;
         const int qy = y0 - kR + j / kHX, qx = x0 - kR + j % kHX;
-        const bool in = zp >= 0 && zp < p.Zg && qy >= 0 && qy < p.Y && qx >= 0 && qx < p.X;
+        const bool in = j < kWin && zp >= 0 && zp < p.Zg && qy >= 0 && qy < p.Y && qx >= 0 && qx < p.X;
         l[k] = __builtin_huge_valf();
         dl[k] = 0.f;
         if (in) {
@@ -1166,12 +1203,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int kz = z0 + quarter, kyl = lane >> 3, kxl = lane & 7;
     const int ky = y0 + kyl, kx = x0 + kxl;
     const bool row_ok = kz < p.Z && ky < p.Y && kx < p.X;
-    // this warp's 48 query columns of the 8x12 window that lie in the key's cube
+    // this warp's kHalf query columns of the halo window that lie in the key's cube
     uint64_t mask = 0ull;
 #pragma unroll
-    for (int i = 0; i < 48; ++i) {
-      const int j = 48 * half + i, hy = j / kHX, hx = j % kHX;
-      if ((unsigned)(hy - kyl) <= 2u * kR && (unsigned)(hx - kxl) <= 2u * kR) mask |= 1ull << i;
+    for (int i = 0; i < kHalf; ++i) {
+      const int j = kHalf * half + i, hy = j / kHX, hx = j % kHX;
+      if (j < kWin && (unsigned)(hy - kyl) <= 2u * kR && (unsigned)(hx - kxl) <= 2u * kR) mask |= 1ull << i;
     }
     if (!row_ok) mask = 0ull;
     const float sc = p.sc, inv_sqrt_d = p.inv_sqrt_d;
@@ -1189,11 +1226,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool active = (unsigned)(zp - (p.cz0 + kz) + kR) <= 2u * kR;  // warp-uniform
       const float *vals = reinterpret_cast<const float *>(ring_ptr + (size_t)(ch % C::kStages) * C::kStageBytes +
                                                           2 * C::kPlaneBytes);
-      uint32_t pw[3][8], dw[3][8];
+      uint32_t pw[kHalf / 16][8], dw[kHalf / 16][8];
       if (active) {
 #pragma unroll
-        for (int gi = 0; gi < 3; ++gi) {
-          const int col0 = 48 * half + 16 * gi;
+        for (int gi = 0; gi < kHalf / 16; ++gi) {
+          const int col0 = kHalf * half + 16 * gi;
           uint32_t sv[16], dv[16];
           tmem_ld16(t_lanes + kLColS + col0, sv);
           tmem_ld16(t_lanes + kLColDP + col0, dv);
@@ -1212,7 +1249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
 #pragma unroll
-        for (int gi = 0; gi < 3; ++gi)
+        for (int gi = 0; gi < kHalf / 16; ++gi)
 #pragma unroll
           for (int i = 0; i < 8; ++i) pw[gi][i] = dw[gi][i] = 0u;
       }
@@ -1224,9 +1261,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
       }
 #pragma unroll
-      for (int gi = 0; gi < 3; ++gi) {
-        tmem_st8(t_lanes + kLColP + 24 * half + 8 * gi, pw[gi]);
-        tmem_st8(t_lanes + kLColDS + 24 * half + 8 * gi, dw[gi]);
+      for (int gi = 0; gi < kHalf / 16; ++gi) {
+        tmem_st8(t_lanes + kLColP + (kHalf / 2) * half + 8 * gi, pw[gi]);
+        tmem_st8(t_lanes + kLColDS + (kHalf / 2) * half + 8 * gi, dw[gi]);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -1264,9 +1301,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, int R>
 int launch_lkv_t(const StencilBwdArgs &a, cudaStream_t stream) {
-  using C = LkvCfg<D>;
+  using G = BGeo<R>;
+  constexpr int kHY = G::kHY, kHX = G::kHX;
+  using C = LkvCfg<D, G::kKeys>;
   const int Z = a.grid[0], Y = a.grid[1], X = a.grid[2];
   const uint64_t es = 2;
   const uint64_t bh = (uint64_t)a.batch * a.heads, bgs = (uint64_t)a.batch * a.kv_heads;
@@ -1313,7 +1352,7 @@ int launch_lkv_t(const StencilBwdArgs &a, cudaStream_t stream) {
   const int64_t units = (int64_t)bgs * p.tiles_z * p.tiles_y * p.tiles_x;
   if (units <= 0) return P3D_OK;
   if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");
-  auto kernel = stencil_bwd_dkv_kernel<D, BF16>;
+  auto kernel = stencil_bwd_dkv_kernel<D, BF16, R>;
   static bool configured = false;
   if (!configured) {
     P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
@@ -1326,14 +1365,23 @@ int launch_lkv_t(const StencilBwdArgs &a, cudaStream_t stream) {
 
 }  // namespace
 
-int launch_stencil_bwd_dq(const StencilBwdArgs &a, cudaStream_t s) {
+template <int R>
+static int launch_dq_radius(const StencilBwdArgs &a, cudaStream_t s) {
   const bool bf16 = a.dtype == P3D_BF16;
   switch (a.head_dim) {
-    case 16: return bf16 ? launch_dq_t<16, true>(a, s) : launch_dq_t<16, false>(a, s);
-    case 32: return bf16 ? launch_dq_t<32, true>(a, s) : launch_dq_t<32, false>(a, s);
-    case 48: return bf16 ? launch_dq_t<48, true>(a, s) : launch_dq_t<48, false>(a, s);
-    case 64: return bf16 ? launch_dq_t<64, true>(a, s) : launch_dq_t<64, false>(a, s);
+    case 16: return bf16 ? launch_dq_t<16, true, R>(a, s) : launch_dq_t<16, false, R>(a, s);
+    case 32: return bf16 ? launch_dq_t<32, true, R>(a, s) : launch_dq_t<32, false, R>(a, s);
+    case 48: return bf16 ? launch_dq_t<48, true, R>(a, s) : launch_dq_t<48, false, R>(a, s);
+    case 64: return bf16 ? launch_dq_t<64, true, R>(a, s) : launch_dq_t<64, false, R>(a, s);
     default: return fail(P3D_ERR_UNSUPPORTED, "stencil backward: head_dim %d", a.head_dim);
+  }
+}
+
+int launch_stencil_bwd_dq(const StencilBwdArgs &a, cudaStream_t s) {
+  switch (a.radius) {
+    case 1: return launch_dq_radius<1>(a, s);
+    case 2: return launch_dq_radius<2>(a, s);
+    default: return fail(P3D_ERR_UNSUPPORTED, "stencil backward: radius %d", a.radius);
   }
 }
 
@@ -1385,14 +1433,23 @@ int launch_global_dkv_tc(const GlobalDkvArgs &a, cudaStream_t s) {
   }
 }
 
-int launch_stencil_bwd_dkv(const StencilBwdArgs &a, cudaStream_t s) {
+template <int R>
+static int launch_dkv_radius(const StencilBwdArgs &a, cudaStream_t s) {
   const bool bf16 = a.dtype == P3D_BF16;
   switch (a.head_dim) {
-    case 16: return bf16 ? launch_lkv_t<16, true>(a, s) : launch_lkv_t<16, false>(a, s);
-    case 32: return bf16 ? launch_lkv_t<32, true>(a, s) : launch_lkv_t<32, false>(a, s);
-    case 48: return bf16 ? launch_lkv_t<48, true>(a, s) : launch_lkv_t<48, false>(a, s);
-    case 64: return bf16 ? launch_lkv_t<64, true>(a, s) : launch_lkv_t<64, false>(a, s);
+    case 16: return bf16 ? launch_lkv_t<16, true, R>(a, s) : launch_lkv_t<16, false, R>(a, s);
+    case 32: return bf16 ? launch_lkv_t<32, true, R>(a, s) : launch_lkv_t<32, false, R>(a, s);
+    case 48: return bf16 ? launch_lkv_t<48, true, R>(a, s) : launch_lkv_t<48, false, R>(a, s);
+    case 64: return bf16 ? launch_lkv_t<64, true, R>(a, s) : launch_lkv_t<64, false, R>(a, s);
     default: return fail(P3D_ERR_UNSUPPORTED, "stencil backward: head_dim %d", a.head_dim);
+  }
+}
+
+int launch_stencil_bwd_dkv(const StencilBwdArgs &a, cudaStream_t s) {
+  switch (a.radius) {
+    case 1: return launch_dkv_radius<1>(a, s);
+    case 2: return launch_dkv_radius<2>(a, s);
+    default: return fail(P3D_ERR_UNSUPPORTED, "stencil backward: radius %d", a.radius);
   }
 }
 

@@ -105,3 +105,29 @@ def test_stencil_backward_is_deterministic(cuda_device):
     b = _grads(inputs, dy, layout.geometry, cuda_device, force_indexed=False)
     for name, x, y in zip(NAMES, a, b):
         assert torch.equal(x, y), name
+
+
+@pytest.mark.parametrize("grid,block,pool,kind,b,h,g,d,dtype", [
+    ((8, 8, 16), (4, 4, 4), 1, "cubes", 1, 4, 4, 48, torch.bfloat16),
+    ((8, 32, 16), (1, 4, 4), 16, "raster_block", 1, 8, 2, 64, torch.bfloat16),   # the allen15 preset, small
+    ((6, 12, 20), (1, 4, 4), 4, "raster_block", 2, 4, 2, 32, torch.float16),     # partial tiles on every axis
+])
+def test_radius_one_stencil_backward_matches_indexed(cuda_device, grid, block, pool, kind, b, h, g, d, dtype):
+    """Radius 1: 6x10 halo windows padded to 64-column chunks in dQ and local dK / dV."""
+    if kind == "cubes":
+        layout = build_layout(grid, block, radius=1, pool_size=pool)
+        layout = layout.repack(layout.order.argsort())
+    else:
+        layout = build_layout(grid, block, radius=1, pool_size=pool, layout="raster_block")
+    geom = layout.geometry
+    n = geom.num_tokens
+    raw = grid_inputs(n, b, h, g, d, torch.float32, sum(grid) + d + 2, True, volume=block[0] * block[1] * block[2])
+    inputs = [oracle.axial_rope(raw[i], layout.coords) if i in (0, 1, 3) else raw[i] for i in range(5)]
+    inputs = [t.to(dtype) for t in inputs] + raw[5:]
+    dy = upstream((b, h, n, d), dtype, sum(grid) + 1)
+    tc = _grads(inputs, dy, geom, cuda_device, force_indexed=False)
+    ix = _grads(inputs, dy, geom, cuda_device, force_indexed=True)
+    torch.cuda.synchronize()
+    assert _native.device_errors() == 0
+    for name, got, want in zip(NAMES, tc, ix):
+        assert _err(got, want) <= 2e-2 * _scale(want), (name, _err(got, want))
