@@ -56,6 +56,7 @@ def parse_args():
                     help="separate mode: the reference's published 'allen15' preset (32x128x64 raster, dim 512, "
                          "8 q-heads / 2 kv-heads x 64, radius 1, (1,4,4) raster blocks, pool 16), layer inference "
                          "and forward + backward, K timed steps each; one JSON line")
+    ap.add_argument("--no-allen15", action="store_true", help="skip the allen15 preset in the N = 1 line")
     ap.add_argument("--train-only", type=int, default=0, metavar="N",
                     help="profiling mode: run the config-3 layer forward + backward N times and exit")
     ap.add_argument("--kernel-only", type=int, default=0, metavar="N",
@@ -249,9 +250,14 @@ ALLEN15 = dict(grid=(32, 128, 64), block=(1, 4, 4), radius=1, pool_size=16, dim=
 
 
 def allen15(args, device):
+    """``--allen15 K``: :func:`allen15_measure` as one JSON line."""
+    print(json.dumps(allen15_measure(args.allen15, args.warmup, device)), flush=True)
+
+
+def allen15_measure(steps, warmup, device):
     """The preset of the reference's only published timings (H200, Triton backend, batch 1:
     layer inference 4.644 ms, forward + backward 15.098 ms, bf16, raster storage), on this
-    GPU: the same layer, layout, dtype and batch."""
+    GPU: the same layer, layout, dtype and batch, eager calls, medians of CUDA-event times."""
     from pack3d_b200 import PACK3DAttention, _native, build_layout
     cfg = ALLEN15
     layout = build_layout(cfg["grid"], cfg["block"], radius=cfg["radius"], pool_size=cfg["pool_size"],
@@ -278,16 +284,20 @@ def allen15(args, device):
 
     out = {}
     for name, fn in (("inference", infer), ("fwd_bwd", train)):
-        for _ in range(max(args.warmup, 2)):
+        for _ in range(max(warmup, 2)):
             fn()
         torch.cuda.synchronize(device)
-        times = timed_steps(fn, args.allen15, stream)
+        times = timed_steps(fn, steps, stream)
         out[name] = round(statistics.median(times), 4)
     errors = _native.device_errors()
-    print(json.dumps({"mode": "allen15", "inference_ms": out["inference"], "fwd_bwd_ms": out["fwd_bwd"],
-                      "reference_h200_ms": {"inference": 4.644, "fwd_bwd": 15.098},
-                      "tokens": n, "summaries": layout.geometry.num_summaries, "stencil": layout.geometry.stencil,
-                      "eager": True, "device_errors": errors}), flush=True)
+    if errors:
+        raise RuntimeError(f"device error flags set: {errors}")
+    return {"mode": "allen15", "workload": "the reference's published 'allen15' preset: 32x128x64 raster, dim 512, "
+                                           "8 q-heads / 2 kv-heads x 64, radius 1, (1,4,4) raster blocks, pool 16, "
+                                           "bf16, batch 1",
+            "inference_ms": out["inference"], "fwd_bwd_ms": out["fwd_bwd"],
+            "reference_h200_ms": {"inference": 4.644, "fwd_bwd": 15.098},
+            "tokens": n, "summaries": layout.geometry.num_summaries, "eager": True, "steps": steps}
 
 
 def train_only(args, device):
@@ -749,6 +759,8 @@ def main():
     line = run_b200(args, rank, world, device) if world == 1 else run_sharded(args, rank, world, device)
     if line is None:
         return
+    if world == 1 and not args.no_allen15 and not args.kernel_only:
+        line["allen15"] = allen15_measure(5, 2, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_s, wall, threads, sample = cpu_layer_seconds()
         n = math.prod(CONFIG["grid"]) * CONFIG["batch"]
