@@ -133,6 +133,23 @@ P3D_API int p3d_layer_norm_bwd(const void *x, const void *weight, const void *dy
                        float *dbias, int dtype, int64_t rows, int dim, float eps, void *workspace,
                        size_t workspace_bytes, void *stream);
 
+/*
+ * Geometry tables (host code, no GPU): the native builders behind pack3d_b200.geometry for
+ * complete voxel stencils -- replace the tensor passes of build_layout's neighbour table and
+ * prepare_geometry's reverse adjacency (reference geometry.py:224-266, 54-101) and of
+ * TokenLayout.repack (geometry.py:190-220); bit-identical, multithreaded over rows
+ * (threads <= 0: all hardware threads).
+ * p3d_stencil_neighbors: order [n] int64 (packed row -> raster index of a Z x Y x X grid) ->
+ *   neighbors [n, W] int32 (W = prod(2r+1), offsets z-major from -r, -1 outside) and sorted
+ *   [n, W] (each row's valid entries ascending, -1 last); *max_valid = widest row.
+ * p3d_repack_neighbors: new row i = old row perm[i]: nb_new [n, W] = old table transported,
+ *   sorted and *max_valid as above.
+ */
+P3D_API int p3d_stencil_neighbors(int Z, int Y, int X, int rz, int ry, int rx, const int64_t *order, int64_t n,
+                          int32_t *neighbors, int32_t *sorted, int32_t *max_valid, int threads);
+P3D_API int p3d_repack_neighbors(int64_t n, int width, const int32_t *nb_old, const int64_t *perm,
+                         int32_t *nb_new, int32_t *sorted, int32_t *max_valid, int threads);
+
 /* Operator arguments shared by forward and backward (all device pointers, contiguous). */
 typedef struct {
   int32_t batch, heads, kv_heads, tokens, head_dim;

@@ -64,6 +64,9 @@ _SIGNATURES = {
                                _vp, _c_int, _c_int, _c_int, _vp, _c_int, _c_int, _c_int, _vp]),
     "p3d_qkv_merge": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                _vp, _c_int, _c_int, _c_int, _vp, _c_int, _c_int, _c_int, _vp]),
+    "p3d_stencil_neighbors": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_i64, _vp, _vp, _vp,
+                                       _c_int]),
+    "p3d_repack_neighbors": (_c_int, [_c_i64, _c_int, _vp, _vp, _vp, _vp, _vp, _c_int]),
     "p3d_layer_norm_bwd_workspace": (ctypes.c_size_t, [_c_i64, _c_int]),
     "p3d_layer_norm_bwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_i64, _c_int, _c_f32, _vp,
                                     ctypes.c_size_t, _vp]),

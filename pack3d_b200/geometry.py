@@ -295,11 +295,16 @@ class TokenLayout:
         inverse = torch.empty_like(p)
         inverse[p] = torch.arange(n)
         old = self.geometry
-        nb = old.neighbors.cpu()[p].long()
         blocks = old.blocks.cpu().long()
-        nb = torch.where(nb >= 0, inverse[nb.clamp_min(0)], -1)
         blocks = torch.where(blocks >= 0, inverse[blocks.clamp_min(0)], -1)
-        geom = _prepare(nb, blocks, old.pool_size, symmetric=old._stencil is not None)
+        lib = _native_geometry() if old._stencil is not None else None
+        if lib is not None:
+            nb, reverse = _native_repack_tables(lib, old.neighbors.cpu(), p)
+            geom = _geometry_from_tables(nb, reverse, blocks.to(torch.int32), old.pool_size, n)
+        else:
+            nb = old.neighbors.cpu()[p].long()
+            nb = torch.where(nb >= 0, inverse[nb.clamp_min(0)], -1)
+            geom = _prepare(nb, blocks, old.pool_size, symmetric=old._stencil is not None)
         tags = {}
         if old._radius_one_grid is not None:
             tags.update(_radius_one_grid=old._radius_one_grid,
@@ -310,6 +315,64 @@ class TokenLayout:
             geom = geom._retag(**tags)
         moved = TokenLayout(self.grid_shape, self.order.cpu()[p].clone(), self.coords.cpu()[p].clone(), geom)
         return moved.to(self.order.device)
+
+
+def _native_geometry():
+    """The library's host builders (``p3d_stencil_neighbors`` / ``p3d_repack_neighbors``: one
+    multithreaded pass, bit-identical to the tensor formulation in this module), or None
+    when the library is not built -- the tensor formulation then builds the same tables."""
+    try:
+        from . import _native
+        return _native.lib()
+    except (OSError, RuntimeError):
+        return None
+
+
+def _native_check(status, what):
+    from . import _native
+    _native.check(status, what)
+
+
+def _geometry_from_tables(nb32, reverse32, blocks32, pool_size, n):
+    """A geometry from natively built stencil tables (valid by construction: every checked
+    property of ``_prepare`` holds for a complete stencil and its repacks)."""
+    if type(pool_size) is not int or not 1 <= pool_size <= MAX_POOL:
+        raise ValueError("pool_size must be an integer in [1,32]")
+    if nb32.shape[1] > MAX_NEIGHBORS or blocks32.shape[1] > MAX_SLOTS:
+        raise ValueError("at most 128 neighbors and 64 fine-block slots are supported")
+    if max(nb32.numel(), blocks32.numel()) >= 2**31:
+        raise ValueError("geometry exceeds the 32-bit kernel indexing limit")
+    return Pack3DGeometry(nb32, reverse32, blocks32, pool_size, n, _seal=_SEAL)
+
+
+def _native_stencil_tables(lib, shape, radius, order):
+    """``(neighbors, reverse)`` int32 of the complete stencil over packed rows ``order``."""
+    import ctypes
+    n, width = order.shape[0], math.prod(2 * r + 1 for r in radius)
+    order = order.contiguous()
+    nb = torch.empty((n, width), dtype=torch.int32)
+    ordered = torch.empty_like(nb)
+    widest = ctypes.c_int32(0)
+    _native_check(lib.p3d_stencil_neighbors(*shape, *radius, ctypes.c_void_p(order.data_ptr()), n,
+                                            ctypes.c_void_p(nb.data_ptr()), ctypes.c_void_p(ordered.data_ptr()),
+                                            ctypes.byref(widest), 0), "p3d_stencil_neighbors")
+    return nb, ordered[:, :max(1, widest.value)].contiguous()
+
+
+def _native_repack_tables(lib, neighbors, permutation):
+    """``(neighbors, reverse)`` int32 of a symmetric graph transported by ``permutation``."""
+    import ctypes
+    nb_old = neighbors.to(torch.int32).contiguous()
+    n, width = nb_old.shape
+    perm = permutation.to(torch.int64).contiguous()
+    nb = torch.empty_like(nb_old)
+    ordered = torch.empty_like(nb_old)
+    widest = ctypes.c_int32(0)
+    _native_check(lib.p3d_repack_neighbors(n, width, ctypes.c_void_p(nb_old.data_ptr()),
+                                           ctypes.c_void_p(perm.data_ptr()), ctypes.c_void_p(nb.data_ptr()),
+                                           ctypes.c_void_p(ordered.data_ptr()), ctypes.byref(widest), 0),
+                  "p3d_repack_neighbors")
+    return nb, ordered[:, :max(1, widest.value)].contiguous()
 
 
 def _stencil_neighbors(coords, inverse, shape, radius):
@@ -358,9 +421,13 @@ def build_layout(grid_shape, block_shape=(2, 2, 2), *, radius=1, pool_size=4,
     coords = coords[order]
     inverse = torch.empty_like(order)
     inverse[order] = torch.arange(n)
-    neighbors = _stencil_neighbors(coords, inverse, shape, rad)
     blocks = torch.arange(n).reshape(-1, math.prod(block))
-    geom = _prepare(neighbors, blocks, pool_size, symmetric=True)
+    lib = _native_geometry()
+    if lib is not None:
+        nb, reverse = _native_stencil_tables(lib, shape, rad, order)
+        geom = _geometry_from_tables(nb, reverse, blocks.to(torch.int32), pool_size, n)
+    else:
+        geom = _prepare(_stencil_neighbors(coords, inverse, shape, rad), blocks, pool_size, symmetric=True)
     raster = layout == "raster_block"
     tags = dict(_stencil=(shape, rad), _stencil_map=None if raster else inverse.to(torch.int32))
     if rad == (1, 1, 1) and n >= 4096 and shape[0] >= 2 and shape[1] >= 2 and shape[2] >= 4:

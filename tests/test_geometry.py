@@ -130,3 +130,31 @@ def test_reverse_adjacency_of_custom_graph(golden):
 def test_grid_coordinates():
     c = grid_coordinates((2, 3, 4))
     assert c.shape == (24, 3) and c[5].tolist() == [0, 1, 1] and c[-1].tolist() == [1, 2, 3]
+
+
+@pytest.mark.parametrize("grid,block,radius,pool,kind", [
+    ((16, 16, 16), (4, 4, 4), 2, 1, "native_block_morton"),
+    ((8, 12, 20), (4, 4, 4), 1, 4, "native_block_morton"),
+    ((6, 12, 20), (1, 4, 4), 1, 4, "raster_block"),
+    ((8, 8, 8), (2, 2, 2), (1, 2, 0), 2, "native_block_morton"),
+    ((4, 4, 8), (2, 2, 2), 0, 1, "raster_block"),
+])
+def test_native_tables_equal_the_tensor_formulation(monkeypatch, grid, block, radius, pool, kind):
+    """The library's host builders reproduce build_layout and repack bit for bit."""
+    import pack3d_b200.geometry as geometry
+    if geometry._native_geometry() is None:
+        pytest.skip("library not built")
+    native = build_layout(grid, block, radius=radius, pool_size=pool, layout=kind)
+    perm = torch.randperm(native.geometry.num_tokens, generator=torch.Generator().manual_seed(sum(grid)))
+    native_raster, native_random = native.repack(native.order.argsort()), native.repack(perm)
+    monkeypatch.setattr(geometry, "_native_geometry", lambda: None)
+    tensor = build_layout(grid, block, radius=radius, pool_size=pool, layout=kind)
+    tensor_raster, tensor_random = tensor.repack(tensor.order.argsort()), tensor.repack(perm)
+    for a, b in ((native, tensor), (native_raster, tensor_raster), (native_random, tensor_random)):
+        assert torch.equal(a.order, b.order) and torch.equal(a.coords, b.coords)
+        for x, y in zip(a.geometry.tensors, b.geometry.tensors):
+            assert x.dtype == y.dtype == torch.int32 and torch.equal(x, y)
+        assert a.geometry.stencil == b.geometry.stencil
+        for tag in ("_stencil_map", "_raster_to_packed", "_radius_one_grid"):
+            ta, tb = getattr(a.geometry, tag), getattr(b.geometry, tag)
+            assert (ta is None and tb is None) or (torch.is_tensor(ta) and torch.equal(ta, tb)) or ta == tb
