@@ -194,13 +194,17 @@ struct SplitParams {
 
 constexpr int kTokensPerWarp = 4;
 
-// Rotate the 4 pairs (8 channels) starting at pair `pair0` of a head by the token's phases
-// (by their inverse with INVERSE: the sine negated).
-template <bool INVERSE = false>
-__device__ __forceinline__ void rotate8(float (&v)[8], int pair0, const SplitParams &p, const int64_t (&c)[3]) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int pair = pair0 + j;
+// The token's phase-table entries ((cos, sin) of pairs `lane` and `lane + 32`; D/2 <= 64
+// pairs): one read per pair and token, handed to the lanes that rotate by shuffles -- each
+// pair's phase serves every head of q, kl and kg.
+template <int D>
+struct Phases {
+  float2 lo, hi;
+};
+
+template <int D>
+__device__ __forceinline__ Phases<D> token_phases(const SplitParams &p, const int64_t (&c)[3], int lane) {
+  auto fetch = [&](int pair) -> float2 {
     int axis = 0, local = pair;
     if (local >= p.pairs[0]) {
       local -= p.pairs[0];
@@ -211,7 +215,27 @@ __device__ __forceinline__ void rotate8(float (&v)[8], int pair0, const SplitPar
       }
     }
     const int64_t entry = p.start[axis] + c[axis] * p.pairs[axis] + local;
-    float2 cs = *reinterpret_cast<const float2 *>(p.phases + 2 * entry);
+    return *reinterpret_cast<const float2 *>(p.phases + 2 * entry);
+  };
+  Phases<D> ph{make_float2(1.f, 0.f), make_float2(1.f, 0.f)};
+  if (lane < D / 2) ph.lo = fetch(lane);
+  if (D / 2 > 32 && lane + 32 < D / 2) ph.hi = fetch(lane + 32);
+  return ph;
+}
+
+// Rotate the 4 pairs (8 channels) starting at pair `pair0` of a head by the token's phases
+// (by their inverse with INVERSE: the sine negated).  Warp-collective: every lane calls it.
+template <int D, bool INVERSE>
+__device__ __forceinline__ void rotate8(float (&v)[8], int pair0, const Phases<D> &ph) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int pair = pair0 + j;
+    float2 cs = make_float2(__shfl_sync(0xffffffffu, ph.lo.x, pair & 31), __shfl_sync(0xffffffffu, ph.lo.y, pair & 31));
+    if constexpr (D / 2 > 32) {
+      const float2 hi =
+          make_float2(__shfl_sync(0xffffffffu, ph.hi.x, pair & 31), __shfl_sync(0xffffffffu, ph.hi.y, pair & 31));
+      if (pair >= 32) cs = hi;
+    }
     if (INVERSE) cs.y = -cs.y;
     const float even = v[2 * j], odd = v[2 * j + 1];
     // each product rounded separately, as the reference's elementwise torch arithmetic
@@ -220,69 +244,60 @@ __device__ __forceinline__ void rotate8(float (&v)[8], int pair0, const SplitPar
   }
 }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kWarps * 32) qkv_split_kernel(SplitParams p) {
+template <typename T>
+__device__ __forceinline__ T *pick(const SplitParams &p, int part) {  // out[1 + part] without a local array
+  void *o = part == 0 ? p.out[1] : part == 1 ? p.out[2] : part == 2 ? p.out[3] : p.out[4];
+  return static_cast<T *>(o);
+}
+
+// One pass per token row: MERGE = false is the split (row-major projections -> head-major,
+// q / kl / kg rotated), MERGE = true its backward (head-major gradients -> row-major
+// projection gradients, rotated back).  Lanes walk the row's 16-byte chunks; every lane
+// takes every iteration (the rotation's shuffles), loads and stores are predicated.
+template <typename T, int D, bool MERGE>
+__global__ void __launch_bounds__(kWarps * 32) qkv_pass_kernel(SplitParams p) {
   constexpr int kGroups = D / 8;  // 16-byte chunks per head row
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.y;
   const int n_begin = (blockIdx.x * kWarps + (threadIdx.x >> 5)) * kTokensPerWarp;
   const int qw = p.heads * kGroups, kvw = 4 * p.kv_heads * kGroups;  // chunks per row
+  T *qrow_w = static_cast<T *>(const_cast<void *>(p.qp)), *kvrow_w = static_cast<T *>(const_cast<void *>(p.kvp));
   for (int t = 0; t < kTokensPerWarp; ++t) {
     const int n = n_begin + t;
-    if (n >= p.tokens) return;
+    if (n >= p.tokens) return;  // warp-uniform
     const int64_t c[3] = {p.coords[3 * (int64_t)n], p.coords[3 * (int64_t)n + 1], p.coords[3 * (int64_t)n + 2]};
-    const T *qrow = static_cast<const T *>(p.qp) + ((int64_t)b * p.tokens + n) * (qw * 8);
-    const T *kvrow = static_cast<const T *>(p.kvp) + ((int64_t)b * p.tokens + n) * (kvw * 8);
-    for (int k = lane; k < qw; k += 32) {
-      const int h = k / kGroups, grp = k % kGroups;
-      float v[8];
-      load8<T>(qrow + 8 * k, v);
-      rotate8(v, 4 * grp, p, c);
-      store8<T>(static_cast<T *>(p.out[0]) + (((int64_t)b * p.heads + h) * p.tokens + n) * D + 8 * grp, v);
+    const Phases<D> ph = token_phases<D>(p, c, lane);
+    T *qrow = qrow_w + ((int64_t)b * p.tokens + n) * (qw * 8);
+    T *kvrow = kvrow_w + ((int64_t)b * p.tokens + n) * (kvw * 8);
+    for (int it = 0; it < (qw + 31) / 32; ++it) {
+      const int k = lane + 32 * it;
+      const bool act = k < qw;
+      const int kk = act ? k : 0, h = kk / kGroups, grp = kk % kGroups;
+      T *head = static_cast<T *>(p.out[0]) + (((int64_t)b * p.heads + h) * p.tokens + n) * D + 8 * grp;
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (act) load8<T>(MERGE ? head : qrow + 8 * k, v);
+      rotate8<D, MERGE>(v, 4 * grp, ph);
+      if (act) store8<T>(MERGE ? qrow + 8 * k : head, v);
     }
-    for (int k = lane; k < kvw; k += 32) {
-      const int part = k / (p.kv_heads * kGroups);   // 0 kl, 1 vl, 2 kg, 3 vg
-      const int rest = k - part * p.kv_heads * kGroups;
+    for (int it = 0; it < (kvw + 31) / 32; ++it) {
+      const int k = lane + 32 * it;
+      const bool act = k < kvw;
+      const int kk = act ? k : 0;
+      const int part = kk / (p.kv_heads * kGroups);   // 0 kl, 1 vl, 2 kg, 3 vg
+      const int rest = kk - part * p.kv_heads * kGroups;
       const int g = rest / kGroups, grp = rest % kGroups;
-      float v[8];
-      load8<T>(kvrow + 8 * k, v);
-      if (part == 0 || part == 2) rotate8(v, 4 * grp, p, c);
-      store8<T>(static_cast<T *>(p.out[1 + part]) + (((int64_t)b * p.kv_heads + g) * p.tokens + n) * D + 8 * grp, v);
-    }
-  }
-}
-
-// The backward of qkv_split_kernel: p.out[] are the five head-major gradients (read),
-// p.qp / p.kvp the row-major projection gradients (written).
-template <typename T, int D>
-__global__ void __launch_bounds__(kWarps * 32) qkv_merge_kernel(SplitParams p) {
-  constexpr int kGroups = D / 8;
-  const int lane = threadIdx.x & 31;
-  const int b = blockIdx.y;
-  const int n_begin = (blockIdx.x * kWarps + (threadIdx.x >> 5)) * kTokensPerWarp;
-  const int qw = p.heads * kGroups, kvw = 4 * p.kv_heads * kGroups;
-  for (int t = 0; t < kTokensPerWarp; ++t) {
-    const int n = n_begin + t;
-    if (n >= p.tokens) return;
-    const int64_t c[3] = {p.coords[3 * (int64_t)n], p.coords[3 * (int64_t)n + 1], p.coords[3 * (int64_t)n + 2]};
-    T *qrow = static_cast<T *>(const_cast<void *>(p.qp)) + ((int64_t)b * p.tokens + n) * (qw * 8);
-    T *kvrow = static_cast<T *>(const_cast<void *>(p.kvp)) + ((int64_t)b * p.tokens + n) * (kvw * 8);
-    for (int k = lane; k < qw; k += 32) {
-      const int h = k / kGroups, grp = k % kGroups;
-      float v[8];
-      load8<T>(static_cast<const T *>(p.out[0]) + (((int64_t)b * p.heads + h) * p.tokens + n) * D + 8 * grp, v);
-      rotate8<true>(v, 4 * grp, p, c);
-      store8<T>(qrow + 8 * k, v);
-    }
-    for (int k = lane; k < kvw; k += 32) {
-      const int part = k / (p.kv_heads * kGroups);   // 0 kl, 1 vl, 2 kg, 3 vg
-      const int rest = k - part * p.kv_heads * kGroups;
-      const int g = rest / kGroups, grp = rest % kGroups;
-      float v[8];
-      load8<T>(static_cast<const T *>(p.out[1 + part]) + (((int64_t)b * p.kv_heads + g) * p.tokens + n) * D + 8 * grp,
-               v);
-      if (part == 0 || part == 2) rotate8<true>(v, 4 * grp, p, c);
-      store8<T>(kvrow + 8 * k, v);
+      T *head = pick<T>(p, part) + (((int64_t)b * p.kv_heads + g) * p.tokens + n) * D + 8 * grp;
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (act) load8<T>(MERGE ? head : kvrow + 8 * k, v);
+      float r[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) r[i] = v[i];
+      rotate8<D, MERGE>(r, 4 * grp, ph);
+      if (part == 0 || part == 2) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = r[i];
+      }
+      if (act) store8<T>(MERGE ? kvrow + 8 * k : head, v);
     }
   }
 }
@@ -292,11 +307,11 @@ int launch_merge(const SplitParams &p, int head_dim, cudaStream_t s) {
   const dim3 grid((unsigned)((p.tokens + kWarps * kTokensPerWarp - 1) / (kWarps * kTokensPerWarp)),
                   (unsigned)p.batch);
   switch (head_dim) {
-    case 16: qkv_merge_kernel<T, 16><<<grid, kWarps * 32, 0, s>>>(p); break;
-    case 32: qkv_merge_kernel<T, 32><<<grid, kWarps * 32, 0, s>>>(p); break;
-    case 48: qkv_merge_kernel<T, 48><<<grid, kWarps * 32, 0, s>>>(p); break;
-    case 64: qkv_merge_kernel<T, 64><<<grid, kWarps * 32, 0, s>>>(p); break;
-    case 128: qkv_merge_kernel<T, 128><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 16: qkv_pass_kernel<T, 16, true><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 32: qkv_pass_kernel<T, 32, true><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 48: qkv_pass_kernel<T, 48, true><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 64: qkv_pass_kernel<T, 64, true><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 128: qkv_pass_kernel<T, 128, true><<<grid, kWarps * 32, 0, s>>>(p); break;
     default: return fail(P3D_ERR_UNSUPPORTED, "p3d_qkv_merge: head_dim %d", head_dim);
   }
   P3D_LAUNCH_CHECK();
@@ -308,11 +323,11 @@ int launch_split(const SplitParams &p, int head_dim, cudaStream_t s) {
   const dim3 grid((unsigned)((p.tokens + kWarps * kTokensPerWarp - 1) / (kWarps * kTokensPerWarp)),
                   (unsigned)p.batch);
   switch (head_dim) {
-    case 16: qkv_split_kernel<T, 16><<<grid, kWarps * 32, 0, s>>>(p); break;
-    case 32: qkv_split_kernel<T, 32><<<grid, kWarps * 32, 0, s>>>(p); break;
-    case 48: qkv_split_kernel<T, 48><<<grid, kWarps * 32, 0, s>>>(p); break;
-    case 64: qkv_split_kernel<T, 64><<<grid, kWarps * 32, 0, s>>>(p); break;
-    case 128: qkv_split_kernel<T, 128><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 16: qkv_pass_kernel<T, 16, false><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 32: qkv_pass_kernel<T, 32, false><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 48: qkv_pass_kernel<T, 48, false><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 64: qkv_pass_kernel<T, 64, false><<<grid, kWarps * 32, 0, s>>>(p); break;
+    case 128: qkv_pass_kernel<T, 128, false><<<grid, kWarps * 32, 0, s>>>(p); break;
     default: return fail(P3D_ERR_UNSUPPORTED, "p3d_qkv_split: head_dim %d", head_dim);
   }
   P3D_LAUNCH_CHECK();
