@@ -57,6 +57,8 @@ def parse_args():
                          "8 q-heads / 2 kv-heads x 64, radius 1, (1,4,4) raster blocks, pool 16), layer inference "
                          "and forward + backward, K timed steps each; one JSON line")
     ap.add_argument("--no-allen15", action="store_true", help="skip the allen15 preset in the N = 1 line")
+    ap.add_argument("--infer-only", type=int, default=0, metavar="N",
+                    help="profiling mode: run the config-1 layer inference forward N times (eager) and exit")
     ap.add_argument("--train-only", type=int, default=0, metavar="N",
                     help="profiling mode: run the config-3 layer forward + backward N times and exit")
     ap.add_argument("--kernel-only", type=int, default=0, metavar="N",
@@ -300,6 +302,26 @@ def allen15_measure(steps, warmup, device):
             "tokens": n, "summaries": layout.geometry.num_summaries, "eager": True, "steps": steps}
 
 
+def infer_only(args, device):
+    """Profiling mode: the config-1 layer inference forward alone (eager calls)."""
+    from pack3d_b200 import _native
+    layout = make_layout(CONFIG["grid"]).to(device)
+    layer = make_layer(torch.bfloat16, device)
+    gen = torch.Generator(device=device).manual_seed(5)
+    x = torch.randn(CONFIG["batch"], layout.geometry.num_tokens, CONFIG["dim"], device=device, generator=gen)
+    x = x.to(torch.bfloat16)
+
+    def step():
+        with torch.inference_mode():
+            layer(x, layout)
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    times = timed_steps(step, args.infer_only, torch.cuda.current_stream(device))
+    errors = _native.device_errors()
+    print(json.dumps({"infer_step_ms": [round(t, 4) for t in times], "device_errors": errors}), flush=True)
+
+
 def train_only(args, device):
     """Profiling mode: the config-3 layer forward + backward (batch 2) alone."""
     from pack3d_b200 import _native
@@ -537,6 +559,8 @@ def run_b200(args, rank, world, device):
         return backward_only(args, device)
     if args.train_only:
         return train_only(args, device)
+    if args.infer_only:
+        return infer_only(args, device)
     if args.allen15:
         return allen15(args, device)
     dtype = torch.bfloat16

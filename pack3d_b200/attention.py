@@ -124,7 +124,13 @@ class PACK3DAttention(nn.Module):
         x, q, kl, vl, kg, vg, gate = self._inference_glue(x, layout.coords, layout.grid_shape)
         y, _ = core_forward(q, kl, vl, kg, vg, self.pool_weight, self.slot_bias, gate, self.local_scale,
                             self.global_scale, layout.geometry, self.temperature, save_state=False, y_rows=True)
-        return x + self.to_out(y.transpose(1, 2).reshape(b, n, -1))
+        return self._out_residual(x, y)
+
+    def _out_residual(self, x, y_rows):
+        """``x + to_out(y)`` for a token-major core output, the residual added inside the GEMM."""
+        b, n = x.shape[0], x.shape[1]
+        out = torch.addmm(x.reshape(b * n, self.dim), y_rows.transpose(1, 2).reshape(b * n, -1), self.to_out.weight.t())
+        return out.view(b, n, self.dim)
 
     def _inference_glue(self, x, coords, grid_shape):
         """LayerNorm, projections, RoPE at ``coords`` (extents ``grid_shape``) and the gate of

@@ -303,7 +303,7 @@ def sharded_layer_forward(layer, x, layout: SlabLayout, group=None):
         kl_ext, vl_ext, sk, sv = exchange_slab(kl, vl, sk_rank, sv_rank, layout.slabs, group)
         y, _ = slab_forward(q, kl_ext, vl_ext, sk, sv, layer.pool_weight, layer.slot_bias, gate, layer.local_scale,
                             layer.global_scale, layout.geometry, layout.slabs, layer.temperature, y_rows=True)
-        return x + layer.to_out(y.transpose(1, 2).reshape(b, n, -1))
+        return layer._out_residual(x, y)
     xn = layer.norm(x)
     q = layer.to_q(xn).reshape(b, n, h, d).transpose(1, 2)
     kl, vl, kg, vg = (t.reshape(b, n, g, d).transpose(1, 2) for t in layer.to_kv(xn).chunk(4, -1))
