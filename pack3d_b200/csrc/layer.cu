@@ -204,17 +204,15 @@ struct Phases {
 
 template <int D>
 __device__ __forceinline__ Phases<D> token_phases(const SplitParams &p, const int64_t (&c)[3], int lane) {
-  auto fetch = [&](int pair) -> float2 {
-    int axis = 0, local = pair;
-    if (local >= p.pairs[0]) {
-      local -= p.pairs[0];
-      axis = 1;
-      if (local >= p.pairs[1]) {
-        local -= p.pairs[1];
-        axis = 2;
-      }
+  auto fetch = [&](int pair) -> float2 {  // selects, not indexing: keeps c and p in registers
+    int64_t entry;
+    if (pair < p.pairs[0]) {
+      entry = p.start[0] + c[0] * p.pairs[0] + pair;
+    } else if (pair < p.pairs[0] + p.pairs[1]) {
+      entry = p.start[1] + c[1] * p.pairs[1] + (pair - p.pairs[0]);
+    } else {
+      entry = p.start[2] + c[2] * p.pairs[2] + (pair - p.pairs[0] - p.pairs[1]);
     }
-    const int64_t entry = p.start[axis] + c[axis] * p.pairs[axis] + local;
     return *reinterpret_cast<const float2 *>(p.phases + 2 * entry);
   };
   Phases<D> ph{make_float2(1.f, 0.f), make_float2(1.f, 0.f)};
@@ -252,52 +250,103 @@ __device__ __forceinline__ T *pick(const SplitParams &p, int part) {  // out[1 +
 
 // One pass per token row: MERGE = false is the split (row-major projections -> head-major,
 // q / kl / kg rotated), MERGE = true its backward (head-major gradients -> row-major
-// projection gradients, rotated back).  Lanes walk the row's 16-byte chunks; every lane
-// takes every iteration (the rotation's shuffles), loads and stores are predicated.
+// projection gradients, rotated back).  A token's 16-byte chunks (q heads, then kl, vl, kg,
+// vg) are spread over the lanes, kBatch chunks per lane; all of a batch's loads are issued
+// before its first rotation (and the phase-table read sits between them), so a warp keeps
+// kBatch x 512 bytes in flight.  Every lane takes every rotation (its shuffles); loads and
+// stores are predicated.
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4 &raw, float (&v)[8]) {
+  const T *e = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = to_f32<T>(e[i]);
+}
+
+// Chunk k of a token row -- q heads first, then the kl, vl, kg, vg parts -- as token-
+// independent offsets: the head-major chunk of token n is head + n * D, the row-major chunk
+// (q row or kv row) is at element off of the row.
+template <typename T>
+struct RowChunk {
+  T *head;  // head-major tensor chunk of token 0
+  int off;  // element offset within the q row (q) or the kv row
+  int grp;  // chunk within the head row
+  bool q;   // in the q row
+  bool rot; // q, kl, kg: rotated
+};
+
+template <typename T, int D>
+__device__ __forceinline__ RowChunk<T> row_chunk(const SplitParams &p, int b, int k, int qw, int kv_part) {
+  constexpr int kGroups = D / 8;
+  RowChunk<T> c;
+  if (k < qw) {
+    const int h = k / kGroups;
+    c.grp = k % kGroups;
+    c.off = 8 * k;
+    c.head = static_cast<T *>(p.out[0]) + ((int64_t)b * p.heads + h) * p.tokens * D + 8 * c.grp;
+    c.q = true;
+    c.rot = true;
+  } else {
+    const int x = k - qw, part = x / kv_part;  // 0 kl, 1 vl, 2 kg, 3 vg
+    const int rest = x - part * kv_part, g = rest / kGroups;
+    c.grp = rest % kGroups;
+    c.off = 8 * x;
+    c.head = pick<T>(p, part) + ((int64_t)b * p.kv_heads + g) * p.tokens * D + 8 * c.grp;
+    c.q = false;
+    c.rot = (part & 1) == 0;
+  }
+  return c;
+}
+
 template <typename T, int D, bool MERGE>
-__global__ void __launch_bounds__(kWarps * 32) qkv_pass_kernel(SplitParams p) {
-  constexpr int kGroups = D / 8;  // 16-byte chunks per head row
+__global__ void __launch_bounds__(kWarps * 32, 3) qkv_pass_kernel(SplitParams p) {
+  constexpr int kBatch = 4;  // chunks per lane loaded ahead of the rotations
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.y;
   const int n_begin = (blockIdx.x * kWarps + (threadIdx.x >> 5)) * kTokensPerWarp;
-  const int qw = p.heads * kGroups, kvw = 4 * p.kv_heads * kGroups;  // chunks per row
+  const int qw = p.heads * (D / 8), kv_part = p.kv_heads * (D / 8);  // chunks per row: q, one kv part
+  const int total = qw + 4 * kv_part;
   T *qrow_w = static_cast<T *>(const_cast<void *>(p.qp)), *kvrow_w = static_cast<T *>(const_cast<void *>(p.kvp));
-  for (int t = 0; t < kTokensPerWarp; ++t) {
-    const int n = n_begin + t;
-    if (n >= p.tokens) return;  // warp-uniform
-    const int64_t c[3] = {p.coords[3 * (int64_t)n], p.coords[3 * (int64_t)n + 1], p.coords[3 * (int64_t)n + 2]};
-    const Phases<D> ph = token_phases<D>(p, c, lane);
-    T *qrow = qrow_w + ((int64_t)b * p.tokens + n) * (qw * 8);
-    T *kvrow = kvrow_w + ((int64_t)b * p.tokens + n) * (kvw * 8);
-    for (int it = 0; it < (qw + 31) / 32; ++it) {
-      const int k = lane + 32 * it;
-      const bool act = k < qw;
-      const int kk = act ? k : 0, h = kk / kGroups, grp = kk % kGroups;
-      T *head = static_cast<T *>(p.out[0]) + (((int64_t)b * p.heads + h) * p.tokens + n) * D + 8 * grp;
-      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (act) load8<T>(MERGE ? head : qrow + 8 * k, v);
-      rotate8<D, MERGE>(v, 4 * grp, ph);
-      if (act) store8<T>(MERGE ? qrow + 8 * k : head, v);
+  for (int base = 0; base < total; base += 32 * kBatch) {
+    RowChunk<T> ch[kBatch];
+    bool any_rot[kBatch];  // warp-uniform: the iteration holds a q, kl or kg chunk
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int k = base + lane + 32 * i;
+      ch[i] = row_chunk<T, D>(p, b, k < total ? k : 0, qw, kv_part);
+      const int lo = base + 32 * i, hi = lo + 32;
+      any_rot[i] = lo < qw + kv_part || (lo < qw + 3 * kv_part && hi > qw + 2 * kv_part);
     }
-    for (int it = 0; it < (kvw + 31) / 32; ++it) {
-      const int k = lane + 32 * it;
-      const bool act = k < kvw;
-      const int kk = act ? k : 0;
-      const int part = kk / (p.kv_heads * kGroups);   // 0 kl, 1 vl, 2 kg, 3 vg
-      const int rest = kk - part * p.kv_heads * kGroups;
-      const int g = rest / kGroups, grp = rest % kGroups;
-      T *head = pick<T>(p, part) + (((int64_t)b * p.kv_heads + g) * p.tokens + n) * D + 8 * grp;
-      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (act) load8<T>(MERGE ? head : kvrow + 8 * k, v);
-      float r[8];
+    for (int t = 0; t < kTokensPerWarp; ++t) {
+      const int n = n_begin + t;
+      if (n >= p.tokens) break;  // warp-uniform
+      T *qrow = qrow_w + ((int64_t)b * p.tokens + n) * (qw * 8);
+      T *kvrow = kvrow_w + ((int64_t)b * p.tokens + n) * (4 * kv_part * 8);
+      uint4 raw[kBatch];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) r[i] = v[i];
-      rotate8<D, MERGE>(r, 4 * grp, ph);
-      if (part == 0 || part == 2) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = r[i];
+      for (int i = 0; i < kBatch; ++i) {
+        raw[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (base + lane + 32 * i < total)
+          raw[i] = *reinterpret_cast<const uint4 *>(MERGE ? ch[i].head + (int64_t)n * D
+                                                          : (ch[i].q ? qrow : kvrow) + ch[i].off);
       }
-      if (act) store8<T>(MERGE ? kvrow + 8 * k : head, v);
+      const int64_t c[3] = {p.coords[3 * (int64_t)n], p.coords[3 * (int64_t)n + 1], p.coords[3 * (int64_t)n + 2]};
+      const Phases<D> ph = token_phases<D>(p, c, lane);
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        if (base + 32 * i >= total) break;  // warp-uniform
+        float v[8];
+        unpack8<T>(raw[i], v);
+        if (any_rot[i]) {
+          float r[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) r[e] = v[e];
+          rotate8<D, MERGE>(r, 4 * ch[i].grp, ph);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = ch[i].rot ? r[e] : v[e];
+        }
+        if (base + lane + 32 * i < total)
+          store8<T>(MERGE ? (ch[i].q ? qrow : kvrow) + ch[i].off : ch[i].head + (int64_t)n * D, v);
+      }
     }
   }
 }
