@@ -194,67 +194,12 @@ struct SplitParams {
 
 constexpr int kTokensPerWarp = 4;
 
-// The token's phase-table entries ((cos, sin) of pairs `lane` and `lane + 32`; D/2 <= 64
-// pairs): one read per pair and token, handed to the lanes that rotate by shuffles -- each
-// pair's phase serves every head of q, kl and kg.
-template <int D>
-struct Phases {
-  float2 lo, hi;
-};
-
-template <int D>
-__device__ __forceinline__ Phases<D> token_phases(const SplitParams &p, const int64_t (&c)[3], int lane) {
-  auto fetch = [&](int pair) -> float2 {  // selects, not indexing: keeps c and p in registers
-    int64_t entry;
-    if (pair < p.pairs[0]) {
-      entry = p.start[0] + c[0] * p.pairs[0] + pair;
-    } else if (pair < p.pairs[0] + p.pairs[1]) {
-      entry = p.start[1] + c[1] * p.pairs[1] + (pair - p.pairs[0]);
-    } else {
-      entry = p.start[2] + c[2] * p.pairs[2] + (pair - p.pairs[0] - p.pairs[1]);
-    }
-    return *reinterpret_cast<const float2 *>(p.phases + 2 * entry);
-  };
-  Phases<D> ph{make_float2(1.f, 0.f), make_float2(1.f, 0.f)};
-  if (lane < D / 2) ph.lo = fetch(lane);
-  if (D / 2 > 32 && lane + 32 < D / 2) ph.hi = fetch(lane + 32);
-  return ph;
-}
-
-// Rotate the 4 pairs (8 channels) starting at pair `pair0` of a head by the token's phases
-// (by their inverse with INVERSE: the sine negated).  Warp-collective: every lane calls it.
-template <int D, bool INVERSE>
-__device__ __forceinline__ void rotate8(float (&v)[8], int pair0, const Phases<D> &ph) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int pair = pair0 + j;
-    float2 cs = make_float2(__shfl_sync(0xffffffffu, ph.lo.x, pair & 31), __shfl_sync(0xffffffffu, ph.lo.y, pair & 31));
-    if constexpr (D / 2 > 32) {
-      const float2 hi =
-          make_float2(__shfl_sync(0xffffffffu, ph.hi.x, pair & 31), __shfl_sync(0xffffffffu, ph.hi.y, pair & 31));
-      if (pair >= 32) cs = hi;
-    }
-    if (INVERSE) cs.y = -cs.y;
-    const float even = v[2 * j], odd = v[2 * j + 1];
-    // each product rounded separately, as the reference's elementwise torch arithmetic
-    v[2 * j] = __fsub_rn(__fmul_rn(even, cs.x), __fmul_rn(odd, cs.y));
-    v[2 * j + 1] = __fadd_rn(__fmul_rn(even, cs.y), __fmul_rn(odd, cs.x));
-  }
-}
-
 template <typename T>
 __device__ __forceinline__ T *pick(const SplitParams &p, int part) {  // out[1 + part] without a local array
   void *o = part == 0 ? p.out[1] : part == 1 ? p.out[2] : part == 2 ? p.out[3] : p.out[4];
   return static_cast<T *>(o);
 }
 
-// One pass per token row: MERGE = false is the split (row-major projections -> head-major,
-// q / kl / kg rotated), MERGE = true its backward (head-major gradients -> row-major
-// projection gradients, rotated back).  A token's 16-byte chunks (q heads, then kl, vl, kg,
-// vg) are spread over the lanes, kBatch chunks per lane; all of a batch's loads are issued
-// before its first rotation (and the phase-table read sits between them), so a warp keeps
-// kBatch x 512 bytes in flight.  Every lane takes every rotation (its shuffles); loads and
-// stores are predicated.
 template <typename T>
 __device__ __forceinline__ void unpack8(const uint4 &raw, float (&v)[8]) {
   const T *e = reinterpret_cast<const T *>(&raw);
@@ -262,90 +207,98 @@ __device__ __forceinline__ void unpack8(const uint4 &raw, float (&v)[8]) {
   for (int i = 0; i < 8; ++i) v[i] = to_f32<T>(e[i]);
 }
 
-// Chunk k of a token row -- q heads first, then the kl, vl, kg, vg parts -- as token-
-// independent offsets: the head-major chunk of token n is head + n * D, the row-major chunk
-// (q row or kv row) is at element off of the row.
-template <typename T>
-struct RowChunk {
-  T *head;  // head-major tensor chunk of token 0
-  int off;  // element offset within the q row (q) or the kv row
-  int grp;  // chunk within the head row
-  bool q;   // in the q row
-  bool rot; // q, kl, kg: rotated
-};
-
-template <typename T, int D>
-__device__ __forceinline__ RowChunk<T> row_chunk(const SplitParams &p, int b, int k, int qw, int kv_part) {
-  constexpr int kGroups = D / 8;
-  RowChunk<T> c;
-  if (k < qw) {
-    const int h = k / kGroups;
-    c.grp = k % kGroups;
-    c.off = 8 * k;
-    c.head = static_cast<T *>(p.out[0]) + ((int64_t)b * p.heads + h) * p.tokens * D + 8 * c.grp;
-    c.q = true;
-    c.rot = true;
+// (cos, sin) of rotation pair `pair` at the token's coordinates: pairs [0, pairs[0]) turn
+// with z, the next pairs[1] with y, the rest with x.  Selects, not indexing: keeps c and p
+// in registers.
+__device__ __forceinline__ float2 pair_phase(const SplitParams &p, const int64_t (&c)[3], int pair) {
+  int64_t entry;
+  if (pair < p.pairs[0]) {
+    entry = p.start[0] + c[0] * p.pairs[0] + pair;
+  } else if (pair < p.pairs[0] + p.pairs[1]) {
+    entry = p.start[1] + c[1] * p.pairs[1] + (pair - p.pairs[0]);
   } else {
-    const int x = k - qw, part = x / kv_part;  // 0 kl, 1 vl, 2 kg, 3 vg
-    const int rest = x - part * kv_part, g = rest / kGroups;
-    c.grp = rest % kGroups;
-    c.off = 8 * x;
-    c.head = pick<T>(p, part) + ((int64_t)b * p.kv_heads + g) * p.tokens * D + 8 * c.grp;
-    c.q = false;
-    c.rot = (part & 1) == 0;
+    entry = p.start[2] + c[2] * p.pairs[2] + (pair - p.pairs[0] - p.pairs[1]);
   }
-  return c;
+  return *reinterpret_cast<const float2 *>(p.phases + 2 * entry);
 }
 
+// One pass over a token's head rows (q heads, then the kl, vl, kg, vg heads): MERGE = false
+// is the split (row-major projections -> head-major, q / kl / kg rotated), MERGE = true its
+// backward (head-major gradients -> row-major projection gradients, rotated back).  Lane =
+// row * C + chunk for C = D / 8 chunks per head row and 32 / C rows per warp pass, so a
+// lane always holds the same 4 pairs of a head row: it reads their (cos, sin) once per token
+// and every rotation is lane-local.  kBatch passes of loads are issued before the first
+// rotation.  Each product and sum is rounded separately, as the reference's elementwise torch
+// arithmetic (rotary.py).
 template <typename T, int D, bool MERGE>
-__global__ void __launch_bounds__(kWarps * 32, 3) qkv_pass_kernel(SplitParams p) {
-  constexpr int kBatch = 4;  // chunks per lane loaded ahead of the rotations
+__global__ void __launch_bounds__(kWarps * 32, 4) qkv_pass_kernel(SplitParams p) {
+  constexpr int C = D / 8;       // 16-byte chunks per head row
+  constexpr int kRows = 32 / C;  // head rows per warp pass
+  constexpr int kBatch = 4;      // passes loaded ahead of the rotations
   const int lane = threadIdx.x & 31;
+  const int sub = lane / C, grp = lane - sub * C;
+  const bool on = sub < kRows;
   const int b = blockIdx.y;
   const int n_begin = (blockIdx.x * kWarps + (threadIdx.x >> 5)) * kTokensPerWarp;
-  const int qw = p.heads * (D / 8), kv_part = p.kv_heads * (D / 8);  // chunks per row: q, one kv part
-  const int total = qw + 4 * kv_part;
+  const int rows = p.heads + 4 * p.kv_heads;  // head rows per token
+  const int qw = p.heads * D, kvw = 4 * p.kv_heads * D;  // elements per projection row
   T *qrow_w = static_cast<T *>(const_cast<void *>(p.qp)), *kvrow_w = static_cast<T *>(const_cast<void *>(p.kvp));
-  for (int base = 0; base < total; base += 32 * kBatch) {
-    RowChunk<T> ch[kBatch];
-    bool any_rot[kBatch];  // warp-uniform: the iteration holds a q, kl or kg chunk
+  for (int base = 0; base < rows; base += kRows * kBatch) {
+    // token-independent: each pass's head row, its head-major tensor row of token 0, its
+    // offset in the projection rows, whether it rotates
+    T *head[kBatch];
+    int off[kBatch];
+    bool isq[kBatch], rot[kBatch], act[kBatch];
 #pragma unroll
     for (int i = 0; i < kBatch; ++i) {
-      const int k = base + lane + 32 * i;
-      ch[i] = row_chunk<T, D>(p, b, k < total ? k : 0, qw, kv_part);
-      const int lo = base + 32 * i, hi = lo + 32;
-      any_rot[i] = lo < qw + kv_part || (lo < qw + 3 * kv_part && hi > qw + 2 * kv_part);
+      const int hr = base + i * kRows + sub;
+      act[i] = on && hr < rows;
+      const int r = act[i] ? hr : 0;
+      isq[i] = r < p.heads;
+      if (isq[i]) {
+        head[i] = static_cast<T *>(p.out[0]) + ((int64_t)b * p.heads + r) * p.tokens * D + 8 * grp;
+        off[i] = r * D + 8 * grp;
+        rot[i] = true;
+      } else {
+        const int x = r - p.heads, part = x / p.kv_heads, g = x - part * p.kv_heads;  // 0 kl, 1 vl, 2 kg, 3 vg
+        head[i] = pick<T>(p, part) + ((int64_t)b * p.kv_heads + g) * p.tokens * D + 8 * grp;
+        off[i] = x * D + 8 * grp;
+        rot[i] = (part & 1) == 0;
+      }
     }
     for (int t = 0; t < kTokensPerWarp; ++t) {
       const int n = n_begin + t;
       if (n >= p.tokens) break;  // warp-uniform
-      T *qrow = qrow_w + ((int64_t)b * p.tokens + n) * (qw * 8);
-      T *kvrow = kvrow_w + ((int64_t)b * p.tokens + n) * (4 * kv_part * 8);
+      T *qrow = qrow_w + ((int64_t)b * p.tokens + n) * qw;
+      T *kvrow = kvrow_w + ((int64_t)b * p.tokens + n) * kvw;
       uint4 raw[kBatch];
 #pragma unroll
       for (int i = 0; i < kBatch; ++i) {
         raw[i] = make_uint4(0u, 0u, 0u, 0u);
-        if (base + lane + 32 * i < total)
-          raw[i] = *reinterpret_cast<const uint4 *>(MERGE ? ch[i].head + (int64_t)n * D
-                                                          : (ch[i].q ? qrow : kvrow) + ch[i].off);
+        if (act[i])
+          raw[i] = *reinterpret_cast<const uint4 *>(MERGE ? head[i] + (int64_t)n * D : (isq[i] ? qrow : kvrow) + off[i]);
       }
       const int64_t c[3] = {p.coords[3 * (int64_t)n], p.coords[3 * (int64_t)n + 1], p.coords[3 * (int64_t)n + 2]};
-      const Phases<D> ph = token_phases<D>(p, c, lane);
+      float2 cs[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        cs[j] = pair_phase(p, c, 4 * grp + j);
+        if (MERGE) cs[j].y = -cs[j].y;  // the inverse rotation: sine negated
+      }
 #pragma unroll
       for (int i = 0; i < kBatch; ++i) {
-        if (base + 32 * i >= total) break;  // warp-uniform
+        if (!act[i]) continue;
         float v[8];
         unpack8<T>(raw[i], v);
-        if (any_rot[i]) {
-          float r[8];
+        if (rot[i]) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) r[e] = v[e];
-          rotate8<D, MERGE>(r, 4 * ch[i].grp, ph);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = ch[i].rot ? r[e] : v[e];
+          for (int j = 0; j < 4; ++j) {
+            const float even = v[2 * j], odd = v[2 * j + 1];
+            v[2 * j] = __fsub_rn(__fmul_rn(even, cs[j].x), __fmul_rn(odd, cs[j].y));
+            v[2 * j + 1] = __fadd_rn(__fmul_rn(even, cs[j].y), __fmul_rn(odd, cs[j].x));
+          }
         }
-        if (base + lane + 32 * i < total)
-          store8<T>(MERGE ? (ch[i].q ? qrow : kvrow) + ch[i].off : ch[i].head + (int64_t)n * D, v);
+        store8<T>(MERGE ? (isq[i] ? qrow : kvrow) + off[i] : head[i] + (int64_t)n * D, v);
       }
     }
   }

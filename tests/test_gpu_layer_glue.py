@@ -15,7 +15,7 @@ def _layout(grid, raster=True):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("h,g,d", [(4, 4, 48), (4, 2, 32), (2, 1, 16), (2, 2, 64)])
+@pytest.mark.parametrize("h,g,d", [(4, 4, 48), (4, 2, 32), (2, 1, 16), (2, 2, 64), (3, 1, 128), (6, 3, 48)])
 def test_qkv_split_matches_rotation_and_copies(cuda_device, dtype, h, g, d):
     layout = _layout((8, 12, 16), raster=False).to(cuda_device)
     b, n = 2, layout.geometry.num_tokens
@@ -93,7 +93,7 @@ def test_fast_inference_layer_matches_the_autograd_path(cuda_device):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("h,g,d", [(4, 4, 48), (4, 2, 32), (8, 8, 48)])
+@pytest.mark.parametrize("h,g,d", [(4, 4, 48), (4, 2, 32), (8, 8, 48), (3, 1, 128), (2, 1, 16)])
 def test_qkv_merge_is_the_exact_backward_of_the_split(cuda_device, dtype, h, g, d):
     from pack3d_b200 import glue
     from pack3d_b200.rope import _rotate
