@@ -34,8 +34,20 @@ int fail(int status, const char *fmt, ...);
 template <typename T> __device__ __forceinline__ float to_f32(T v);
 template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
 template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+// bf16 -> fp32 is exact as a 16-bit shift of the bit pattern: integer operations only.
 template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
-  return __bfloat162float(v);
+  return __uint_as_float((uint32_t)__bfloat16_as_ushort(v) << 16);
+}
+
+// The two 16-bit values of a packed word as fp32, low half first.  bf16 -> fp32 is exact as
+// a 16-bit shift of the bit pattern (two integer operations, no conversion unit); f16 uses
+// the paired hardware conversion.
+template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t w);
+template <> __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <> __device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2 *>(&w));
 }
 
 template <typename T> __device__ __forceinline__ T from_f32(float v);
@@ -53,7 +65,7 @@ template <typename T> __device__ __forceinline__ float round_to(float v) {
 __device__ __forceinline__ float load_any(const void *p, int dtype, int64_t i) {
   switch (dtype) {
     case P3D_F16: return __half2float(static_cast<const __half *>(p)[i]);
-    case P3D_BF16: return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
+    case P3D_BF16: return to_f32<__nv_bfloat16>(static_cast<const __nv_bfloat16 *>(p)[i]);
     default: return static_cast<const float *>(p)[i];
   }
 }

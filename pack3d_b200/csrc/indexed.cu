@@ -200,6 +200,150 @@ __global__ void __launch_bounds__(kWarps * 32) mix_bwd_kernel(MixBwdArgs a) {
   }
 }
 
+// The mix backward for 16-bit rows with D in {8, 16, 32, 48, 64, 128} and 16-byte-aligned
+// tensors: the same per-element arithmetic as mix_bwd_kernel, laid out for bandwidth.  A row
+// is a segment of S lanes (S = the power of two >= D / 8), one 16-byte chunk per lane, so a
+// warp pass covers 32 / S rows and kBatch passes of loads are issued before the first use.
+// The per-row sums (Delta_l, Delta_g, dgate) reduce inside the segment (xor shuffles); the
+// per-channel sums (dsl, dsg) accumulate per lane over the lane's rows and combine across
+// segments at the end.  Summation orders differ from mix_bwd_kernel (fp32 rounding).
+template <int D>
+struct MixVec {
+  static constexpr int kC = D / 8;  // chunks per row
+  static constexpr int kS = kC <= 1 ? 1 : kC <= 2 ? 2 : kC <= 4 ? 4 : kC <= 8 ? 8 : 16;  // lanes per row
+  static constexpr int kR = 32 / kS;  // rows per warp pass
+  static constexpr int kBatch = 4;    // passes loaded ahead
+};
+
+template <typename T>
+__device__ __forceinline__ void unpack8f(const uint4 &raw, float (&v)[8]) {
+  const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack2<T>(u[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2f(float x, float y) {
+  const T lo = from_f32<T>(x), hi = from_f32<T>(y);
+  uint16_t a, b;
+  memcpy(&a, &lo, 2);
+  memcpy(&b, &hi, 2);
+  return (uint32_t)a | ((uint32_t)b << 16);
+}
+
+template <int S>
+__device__ __forceinline__ float segment_sum(float v) {
+#pragma unroll
+  for (int o = 1; o < S; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kWarps * 32) mix_bwd_vec_kernel(MixBwdArgs a) {
+  using G = MixVec<D>;
+  const int lane = threadIdx.x & 31, seg = lane / G::kS, c = lane % G::kS;
+  const bool on = c < G::kC;
+  const int chunks = (a.tokens + a.chunk_rows - 1) / a.chunk_rows;
+  const int64_t wid = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (wid >= (int64_t)a.bh * chunks) return;
+  const int bh = (int)(wid / chunks);
+  const int r0 = (int)(wid % chunks) * a.chunk_rows;
+  const int r1 = min(a.tokens, r0 + a.chunk_rows);
+  const T *dy = static_cast<const T *>(a.dy), *ol = static_cast<const T *>(a.ol);
+  const T *og = static_cast<const T *>(a.og);
+  T *dol = static_cast<T *>(a.dol), *dog = static_cast<T *>(a.dog);
+  float sl[8], sg[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    sl[e] = on ? a.sl[8 * c + e] : 0.f;
+    sg[e] = on ? a.sg[8 * c + e] : 0.f;
+  }
+  float dsl[8], dsg[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) dsl[e] = dsg[e] = 0.f;
+  for (int base = r0; base < r1; base += G::kR * G::kBatch) {
+    uint4 rgy[G::kBatch], rlo[G::kBatch], rgo[G::kBatch];  // raw 16-byte chunks, unpacked on use
+    float gate[G::kBatch];
+#pragma unroll
+    for (int i = 0; i < G::kBatch; ++i) {
+      const int t = base + i * G::kR + seg;
+      const int64_t row = (int64_t)bh * a.tokens + (t < r1 ? t : r0);
+      const int64_t off = row * D + 8 * c;
+      rgy[i] = rlo[i] = rgo[i] = make_uint4(0u, 0u, 0u, 0u);
+      if (on && t < r1) {
+        rgy[i] = *reinterpret_cast<const uint4 *>(dy + off);
+        rlo[i] = *reinterpret_cast<const uint4 *>(ol + off);
+        rgo[i] = *reinterpret_cast<const uint4 *>(og + off);
+      }
+      gate[i] = load_any(a.gate, a.gate_dtype, row);
+    }
+#pragma unroll
+    for (int i = 0; i < G::kBatch; ++i) {
+      if (base + i * G::kR >= r1) break;  // warp-uniform
+      const int t = base + i * G::kR + seg;
+      const bool valid = on && t < r1;
+      const int64_t row = (int64_t)bh * a.tokens + t;
+      float gy[8], lo[8], go[8];
+      unpack8f<T>(rgy[i], gy);
+      unpack8f<T>(rlo[i], lo);
+      unpack8f<T>(rgo[i], go);
+      float dl = 0.f, dg = 0.f, dgate = 0.f;
+      uint32_t pl[4], pg[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        float g_l[2], g_g[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float g_y = gy[e + h];
+          // Delta uses the same rounded branch gradients the attention VJPs consume.
+          g_l[h] = round_to<T>(g_y * sl[e + h]);
+          g_g[h] = round_to<T>((g_y * gate[i]) * sg[e + h]);
+          dl = fmaf(g_l[h], lo[e + h], dl);
+          dg = fmaf(g_g[h], go[e + h], dg);
+          dgate = fmaf(g_y * go[e + h], sg[e + h], dgate);
+          if (valid) {
+            dsl[e + h] = fmaf(g_y, lo[e + h], dsl[e + h]);
+            dsg[e + h] = fmaf(g_y * go[e + h], gate[i], dsg[e + h]);
+          }
+        }
+        pl[e / 2] = pack2f<T>(g_l[0], g_l[1]);
+        pg[e / 2] = pack2f<T>(g_g[0], g_g[1]);
+      }
+      if (valid) {
+        *reinterpret_cast<uint4 *>(dol + row * D + 8 * c) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+        *reinterpret_cast<uint4 *>(dog + row * D + 8 * c) = make_uint4(pg[0], pg[1], pg[2], pg[3]);
+      }
+      dl = segment_sum<G::kS>(dl);
+      dg = segment_sum<G::kS>(dg);
+      dgate = segment_sum<G::kS>(dgate);
+      if (c == 0 && t < r1) {
+        a.delta_l[row] = dl;
+        a.delta_g[row] = dg;
+        store_any(a.dgate, a.gate_dtype, row, dgate);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+#pragma unroll
+    for (int o = G::kS; o < 32; o <<= 1) {
+      dsl[e] += __shfl_xor_sync(0xffffffffu, dsl[e], o);
+      dsg[e] += __shfl_xor_sync(0xffffffffu, dsg[e], o);
+    }
+  }
+  if (seg == 0 && on) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      a.dsl_part[wid * D + 8 * c + e] = dsl[e];
+      a.dsg_part[wid * D + 8 * c + e] = dsg[e];
+    }
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kWarps * 32)
     local_dq_kernel(IndexedArgs a, const T *dol, const float *lse_l, const float *delta_l, T *dq, bool vec) {
@@ -488,7 +632,23 @@ int launch_mix_bwd(const MixBwdArgs &a, cudaStream_t s) {
   const int chunks = (a.tokens + a.chunk_rows - 1) / a.chunk_rows;
   const int64_t warps = (int64_t)a.bh * chunks;
   if (!warps) return P3D_OK;
-  P3D_BY_DTYPE(a.dtype, T, mix_bwd_kernel<T><<<grid_for(warps), kWarps * 32, 0, s>>>(a));
+  const bool vec = a.dtype != P3D_F32 && ((uintptr_t)a.dy & 15) == 0 && ((uintptr_t)a.ol & 15) == 0 &&
+                   ((uintptr_t)a.og & 15) == 0 && ((uintptr_t)a.dol & 15) == 0 && ((uintptr_t)a.dog & 15) == 0;
+  auto by_dim = [&](auto tag) -> bool {
+    using T = decltype(tag);
+    switch (a.head_dim) {
+      case 8: mix_bwd_vec_kernel<T, 8><<<grid_for(warps), kWarps * 32, 0, s>>>(a); return true;
+      case 16: mix_bwd_vec_kernel<T, 16><<<grid_for(warps), kWarps * 32, 0, s>>>(a); return true;
+      case 32: mix_bwd_vec_kernel<T, 32><<<grid_for(warps), kWarps * 32, 0, s>>>(a); return true;
+      case 48: mix_bwd_vec_kernel<T, 48><<<grid_for(warps), kWarps * 32, 0, s>>>(a); return true;
+      case 64: mix_bwd_vec_kernel<T, 64><<<grid_for(warps), kWarps * 32, 0, s>>>(a); return true;
+      case 128: mix_bwd_vec_kernel<T, 128><<<grid_for(warps), kWarps * 32, 0, s>>>(a); return true;
+      default: return false;
+    }
+  };
+  bool done = false;
+  if (vec) done = a.dtype == P3D_BF16 ? by_dim(__nv_bfloat16{}) : by_dim(__half{});
+  if (!done) P3D_BY_DTYPE(a.dtype, T, mix_bwd_kernel<T><<<grid_for(warps), kWarps * 32, 0, s>>>(a));
   P3D_LAUNCH_CHECK();
   return P3D_OK;
 }

@@ -202,9 +202,13 @@ __device__ __forceinline__ T *pick(const SplitParams &p, int part) {  // out[1 +
 
 template <typename T>
 __device__ __forceinline__ void unpack8(const uint4 &raw, float (&v)[8]) {
-  const T *e = reinterpret_cast<const T *>(&raw);
+  const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = to_f32<T>(e[i]);
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack2<T>(u[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
 }
 
 // (cos, sin) of rotation pair `pair` at the token's coordinates: pairs [0, pairs[0]) turn

@@ -324,14 +324,16 @@ __device__ __forceinline__ float2 staged_dot2(const uint4 *row0, const uint4 *ro
 #pragma unroll
   for (int c = 0; c < D / 8; ++c) {
     const uint4 r0 = row0[c], r1 = row1[c];
-    const T *e0 = reinterpret_cast<const T *>(&r0);
-    const T *e1 = reinterpret_cast<const T *>(&r1);
+    const uint32_t u0[4] = {r0.x, r0.y, r0.z, r0.w}, u1[4] = {r1.x, r1.y, r1.z, r1.w};
     const float4 w0 = *reinterpret_cast<const float4 *>(w + 8 * c);
     const float4 w1 = *reinterpret_cast<const float4 *>(w + 8 * c + 4);
     const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      acc = fma2(make_float2(to_f32<T>(e0[i]), to_f32<T>(e1[i])), make_float2(wv[i], wv[i]), acc);
+    for (int i = 0; i < 4; ++i) {
+      const float2 a = unpack2<T>(u0[i]), b = unpack2<T>(u1[i]);
+      acc = fma2(make_float2(a.x, b.x), make_float2(wv[2 * i], wv[2 * i]), acc);
+      acc = fma2(make_float2(a.y, b.y), make_float2(wv[2 * i + 1], wv[2 * i + 1]), acc);
+    }
   }
   return acc;
 }
@@ -339,10 +341,10 @@ __device__ __forceinline__ float2 staged_dot2(const uint4 *row0, const uint4 *ro
 // acc[i] += a * chunk[i] over the 8 channels of a 16-byte chunk (pairs packed f32x2).
 template <typename T>
 __device__ __forceinline__ void axpy8(float a, const uint4 &raw, float2 (&acc)[4]) {
-  const T *e = reinterpret_cast<const T *>(&raw);
+  const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
   const float2 aa = make_float2(a, a);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) acc[i] = fma2(aa, make_float2(to_f32<T>(e[2 * i]), to_f32<T>(e[2 * i + 1])), acc[i]);
+  for (int i = 0; i < 4; ++i) acc[i] = fma2(aa, unpack2<T>(u[i]), acc[i]);
 }
 
 __device__ __forceinline__ uint32_t bits16(__half v) { return __half_as_ushort(v); }
@@ -488,6 +490,22 @@ __global__ void __launch_bounds__(kStageWarps * 32, 7) pool_bwd_staged_kernel(Po
   const int f_begin = m * p.pool_size, f_end = min(p.fine_blocks, (m + 1) * p.pool_size);
   int idx[2];
   if (has) stage_block<T, D>(S, K, Vt, p.blocks, f_begin, V, idx);
+  // the summary's gradient rows and its block-table entries load while the rows gather
+  constexpr int kCh = (D + 31) / 32;
+  const int64_t srow = ((int64_t)bg * M + m) * D;
+  float gk[kCh], gv[kCh];
+#pragma unroll
+  for (int i = 0; i < kCh; ++i) {
+    const int ch = lane + 32 * i;
+    gk[i] = has && ch < D ? p.dsk[srow + ch] : 0.f;
+    gv[i] = has && ch < D ? p.dsv[srow + ch] : 0.f;
+  }
+  int count = 0;  // nonempty fine blocks: the coarse mean's divisor
+  for (int f = f_begin; has && f < f_end; ++f) {
+    const bool any = (lane < V && p.blocks[(int64_t)f * V + lane] >= 0) ||
+                     (lane + 32 < V && p.blocks[(int64_t)f * V + lane + 32] >= 0);
+    count += __any_sync(0xffffffffu, any) ? 1 : 0;
+  }
   float *w = reinterpret_cast<float *>(stage_smem);
   float *bias = w + D;
   for (int i = threadIdx.x; i < D; i += blockDim.x) w[i] = p.weight[i];
@@ -497,17 +515,14 @@ __global__ void __launch_bounds__(kStageWarps * 32, 7) pool_bwd_staged_kernel(Po
   const float inv_temp = 1.f / p.temperature;
   const int grp = lane / G::kChunks, chunk = lane - grp * G::kChunks;
   const bool mapped = grp < G::kGroups;
-  int count = 0;  // nonempty fine blocks: the coarse mean's divisor
-  for (int f = f_begin; f < f_end; ++f) {
-    const bool any = (lane < V && p.blocks[(int64_t)f * V + lane] >= 0) ||
-                     (lane + 32 < V && p.blocks[(int64_t)f * V + lane + 32] >= 0);
-    count += __any_sync(0xffffffffu, any) ? 1 : 0;
-  }
   const float inv_count = 1.f / (float)count;
-  const int64_t srow = ((int64_t)bg * M + m) * D;
-  for (int ch = lane; ch < D; ch += 32) {
-    S.grad[ch] = p.dsk[srow + ch] * inv_count;
-    S.grad[D + ch] = p.dsv[srow + ch] * inv_count;
+#pragma unroll
+  for (int i = 0; i < kCh; ++i) {
+    const int ch = lane + 32 * i;
+    if (ch < D) {
+      S.grad[ch] = gk[i] * inv_count;
+      S.grad[D + ch] = gv[i] * inv_count;
+    }
   }
   float2 dw[4];
 #pragma unroll
@@ -537,20 +552,26 @@ __global__ void __launch_bounds__(kStageWarps * 32, 7) pool_bwd_staged_kernel(Po
       const uint64_t valid = valid_slots(idx);
       __syncwarp();
       // dK / dV member rows: lane per (row, 16-byte chunk), one 16-byte store each.
-#pragma unroll 4
+#pragma unroll 2
       for (int i = 0; i < (64 * G::kChunks + 31) / 32; ++i) {
         const int e = lane + 32 * i, r = e / G::kChunks, c = e - r * G::kChunks;
         if (e >= V * G::kChunks) break;  // e grows with i
         const int row = S.idx[r];
         if (row < 0) continue;
         const float a = S.a[r], dsv = S.ds[r];
+        float gk[8], gv[8], wc[8];  // this chunk's 8 channels of dfine_k, dfine_v, w
+        *reinterpret_cast<float4 *>(gk) = *reinterpret_cast<const float4 *>(S.grad + 8 * c);
+        *reinterpret_cast<float4 *>(gk + 4) = *reinterpret_cast<const float4 *>(S.grad + 8 * c + 4);
+        *reinterpret_cast<float4 *>(gv) = *reinterpret_cast<const float4 *>(S.grad + D + 8 * c);
+        *reinterpret_cast<float4 *>(gv + 4) = *reinterpret_cast<const float4 *>(S.grad + D + 8 * c + 4);
+        *reinterpret_cast<float4 *>(wc) = *reinterpret_cast<const float4 *>(w + 8 * c);
+        *reinterpret_cast<float4 *>(wc + 4) = *reinterpret_cast<const float4 *>(w + 8 * c + 4);
         uint32_t pk[4], pv[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int ch = 8 * c + 2 * i;
-          pk[i] = pack2<T>(fmaf(a, S.grad[ch], dsv * (w[ch] * inv_temp)),
-                           fmaf(a, S.grad[ch + 1], dsv * (w[ch + 1] * inv_temp)));
-          pv[i] = pack2<T>(a * S.grad[D + ch], a * S.grad[D + ch + 1]);
+          pk[i] = pack2<T>(fmaf(a, gk[2 * i], dsv * (wc[2 * i] * inv_temp)),
+                           fmaf(a, gk[2 * i + 1], dsv * (wc[2 * i + 1] * inv_temp)));
+          pv[i] = pack2<T>(a * gv[2 * i], a * gv[2 * i + 1]);
         }
         *reinterpret_cast<uint4 *>(DK + (int64_t)row * D + 8 * c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         *reinterpret_cast<uint4 *>(DV + (int64_t)row * D + 8 * c) = make_uint4(pv[0], pv[1], pv[2], pv[3]);
@@ -564,10 +585,9 @@ __global__ void __launch_bounds__(kStageWarps * 32, 7) pool_bwd_staged_kernel(Po
           if (s < V && ((valid >> s) & 1)) {
             const float2 dsv = make_float2(S.ds[s], S.ds[s]);
             const uint4 raw = S.k[s * G::kStride + chunk];
-            const T *e = reinterpret_cast<const T *>(&raw);
+            const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dw[i] = fma2(dsv, mul2(make_float2(to_f32<T>(e[2 * i]), to_f32<T>(e[2 * i + 1])), it2), dw[i]);
+            for (int i = 0; i < 4; ++i) dw[i] = fma2(dsv, mul2(unpack2<T>(u[i]), it2), dw[i]);
           }
         }
       }

@@ -130,8 +130,8 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 
 template <bool BF16>
 __device__ __forceinline__ float2 unpack2(uint32_t v) {
-  if constexpr (BF16) {
-    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&v));
+  if constexpr (BF16) {  // exact: the bf16 bit patterns shifted into fp32 position
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
   } else {
     return __half22float2(*reinterpret_cast<const __half2 *>(&v));
   }
