@@ -181,6 +181,176 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
+// ------------------------------------------------------- LayerNorm, segment layout
+// For dim = 64 K (K <= 4): a row is a segment of 8 lanes, lane l of the segment holding the
+// row's 16-byte chunks l + 8 j (j < K), so each j reads one 128-byte line per row; a warp pass
+// covers 4 rows.  Row sums reduce inside the segment (3 xor shuffles instead of 5 across the
+// warp), all 32 lanes work for any such dim, and in the forward the next row group's loads
+// (a grid-stride walk) are issued before the current one is reduced.
+// Same per-element arithmetic as the kernels above; the row sums add in a different order.
+template <int S>
+__device__ __forceinline__ float seg_sum(float v) {
+#pragma unroll
+  for (int o = 1; o < S; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8x(const uint4 &raw, float (&v)[8]) {
+  const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack2<T>(u[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kWarps * 32, 3)
+    layer_norm_seg_kernel(const T *x, const T *weight, const T *bias, T *y, int64_t rows, float eps) {
+  constexpr int D = 64 * K;
+  const int lane = threadIdx.x & 31, seg = lane >> 3, l = lane & 7;
+  const int64_t n_warps = (int64_t)gridDim.x * kWarps;
+  auto load_group = [&](int64_t g, uint4 (&raw)[K]) {
+    const int64_t row = 4 * g + seg;
+#pragma unroll
+    for (int j = 0; j < K; ++j)
+      raw[j] = row < rows ? *reinterpret_cast<const uint4 *>(x + row * D + 8 * (l + 8 * j)) : make_uint4(0u, 0u, 0u, 0u);
+  };
+  int64_t g = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  uint4 raw[K];
+  load_group(g, raw);
+  for (; 4 * g < rows; g += n_warps) {
+    float v[K][8];
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      unpack8x<T>(raw[j], v[j]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum += v[j][i];
+    }
+    load_group(g + n_warps, raw);  // the next row group is in flight during this one's math
+    const float mean = seg_sum<8>(sum) / (float)D;
+    float sq = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[j][i] - mean;
+        sq += d * d;
+      }
+    const float rstd = rsqrtf(seg_sum<8>(sq) / (float)D + eps);
+    const int64_t row = 4 * g + seg;
+    if (row < rows) {
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        float w[8], b[8], o[8];
+        load8<T>(weight + 8 * (l + 8 * j), w);  // L1-resident after the first row group
+        load8<T>(bias + 8 * (l + 8 * j), b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = (v[j][i] - mean) * rstd * w[i] + b[i];
+        store8<T>(y + row * D + 8 * (l + 8 * j), o);
+      }
+    }
+  }
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kWarps * 32, 2)
+    layer_norm_bwd_seg_kernel(const T *x, const T *weight, const T *dy, T *dx, float *dw_part, float *db_part,
+                              int64_t rows, float eps) {
+  constexpr int D = 64 * K;
+  const int lane = threadIdx.x & 31, seg = lane >> 3, l = lane & 7;
+  const int64_t warp_id = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int64_t n_warps = (int64_t)gridDim.x * kWarps;
+  float accw[K][8], accb[K][8];
+#pragma unroll
+  for (int j = 0; j < K; ++j)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) accw[j][i] = accb[j][i] = 0.f;
+  const float inv_dim = 1.f / (float)D;
+  for (int64_t g = warp_id; 4 * g < rows; g += n_warps) {
+    const int64_t row = 4 * g + seg;
+    const bool on = row < rows;
+    uint4 rx[K], rg[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      rx[j] = rg[j] = make_uint4(0u, 0u, 0u, 0u);
+      if (on) {
+        rx[j] = *reinterpret_cast<const uint4 *>(x + row * D + 8 * (l + 8 * j));
+        rg[j] = *reinterpret_cast<const uint4 *>(dy + row * D + 8 * (l + 8 * j));
+      }
+    }
+    float v[K][8], gr[K][8];
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      unpack8x<T>(rx[j], v[j]);
+      unpack8x<T>(rg[j], gr[j]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum += v[j][i];
+    }
+    const float mean = seg_sum<8>(sum) / (float)D;
+    float sq = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[j][i] - mean;
+        sq += d * d;
+      }
+    const float rstd = rsqrtf(seg_sum<8>(sq) / (float)D + eps);
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      float w[8];
+      load8<T>(weight + 8 * (l + 8 * j), w);  // L1-resident after the first row group
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float xhat = (v[j][i] - mean) * rstd;
+        const float gw = gr[j][i] * w[i];
+        s1 += gw;
+        s2 += gw * xhat;
+        accw[j][i] += gr[j][i] * xhat;  // rows outside the tensor load zeros: no contribution
+        accb[j][i] += gr[j][i];
+        v[j][i] = xhat;
+        gr[j][i] = gw;
+      }
+    }
+    const float m1 = seg_sum<8>(s1) * inv_dim, m2 = seg_sum<8>(s2) * inv_dim;
+    if (on) {
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = rstd * (gr[j][i] - m1 - v[j][i] * m2);
+        store8<T>(dx + row * D + 8 * (l + 8 * j), o);
+      }
+    }
+  }
+  // the four segments' partials of each channel, then segment 0 writes the warp's row
+#pragma unroll
+  for (int j = 0; j < K; ++j)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      accw[j][i] += __shfl_xor_sync(0xffffffffu, accw[j][i], 8);
+      accw[j][i] += __shfl_xor_sync(0xffffffffu, accw[j][i], 16);
+      accb[j][i] += __shfl_xor_sync(0xffffffffu, accb[j][i], 8);
+      accb[j][i] += __shfl_xor_sync(0xffffffffu, accb[j][i], 16);
+    }
+  if (seg == 0) {
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      float *pw = dw_part + warp_id * D + 8 * (l + 8 * j), *pb = db_part + warp_id * D + 8 * (l + 8 * j);
+      *reinterpret_cast<float4 *>(pw) = make_float4(accw[j][0], accw[j][1], accw[j][2], accw[j][3]);
+      *reinterpret_cast<float4 *>(pw + 4) = make_float4(accw[j][4], accw[j][5], accw[j][6], accw[j][7]);
+      *reinterpret_cast<float4 *>(pb) = make_float4(accb[j][0], accb[j][1], accb[j][2], accb[j][3]);
+      *reinterpret_cast<float4 *>(pb + 4) = make_float4(accb[j][4], accb[j][5], accb[j][6], accb[j][7]);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------- projection split
 struct SplitParams {
   const void *qp, *kvp;
@@ -343,6 +513,24 @@ int launch_split(const SplitParams &p, int head_dim, cudaStream_t s) {
 template <typename T>
 int launch_ln(const void *x, const void *w, const void *b, void *y, int64_t rows, int dim, float eps,
               cudaStream_t s) {
+  if (dim % 64 == 0 && dim <= 256) {  // segment layout: 4 rows per warp pass, grid-stride
+    DeviceInfo info{};
+    if (int st = device_info(&info)) return st;
+    const int64_t want = (rows + 4 * kWarps - 1) / (4 * kWarps), cap = (int64_t)info.sm_count * 3;
+    const unsigned blocks = (unsigned)(want < cap ? want : cap);
+    auto seg = [&](auto kernel) {
+      kernel<<<blocks, kWarps * 32, 0, s>>>(static_cast<const T *>(x), static_cast<const T *>(w),
+                                            static_cast<const T *>(b), static_cast<T *>(y), rows, eps);
+    };
+    switch (dim / 64) {
+      case 1: seg(layer_norm_seg_kernel<T, 1>); break;
+      case 2: seg(layer_norm_seg_kernel<T, 2>); break;
+      case 3: seg(layer_norm_seg_kernel<T, 3>); break;
+      default: seg(layer_norm_seg_kernel<T, 4>); break;
+    }
+    P3D_LAUNCH_CHECK();
+    return P3D_OK;
+  }
   const unsigned blocks = (unsigned)((rows + kWarps - 1) / kWarps);
   const int chunks = (dim / 8 + 31) / 32;
   auto args = [&](auto kernel) {
@@ -363,6 +551,20 @@ int launch_ln(const void *x, const void *w, const void *b, void *y, int64_t rows
 template <typename T>
 int launch_ln_bwd(const void *x, const void *w, const void *dy, void *dx, float *dw_part, float *db_part,
                   int64_t rows, int dim, float eps, unsigned blocks, cudaStream_t s) {
+  if (dim % 64 == 0 && dim <= 192) {  // segment layout (same grid: one partials row per warp)
+    auto seg = [&](auto kernel) {
+      kernel<<<blocks, kWarps * 32, 0, s>>>(static_cast<const T *>(x), static_cast<const T *>(w),
+                                            static_cast<const T *>(dy), static_cast<T *>(dx), dw_part, db_part, rows,
+                                            eps);
+    };
+    switch (dim / 64) {
+      case 1: seg(layer_norm_bwd_seg_kernel<T, 1>); break;
+      case 2: seg(layer_norm_bwd_seg_kernel<T, 2>); break;
+      default: seg(layer_norm_bwd_seg_kernel<T, 3>); break;
+    }
+    P3D_LAUNCH_CHECK();
+    return P3D_OK;
+  }
   const int chunks = (dim / 8 + 31) / 32;
   auto args = [&](auto kernel) {
     kernel<<<blocks, kWarps * 32, 0, s>>>(static_cast<const T *>(x), static_cast<const T *>(w),

@@ -41,10 +41,11 @@ def test_qkv_split_matches_rotation_and_copies(cuda_device, dtype, h, g, d):
     assert torch.equal(vl, chunks[1].contiguous()) and torch.equal(vg, chunks[3].contiguous())
 
 
-@pytest.mark.parametrize("dim", [192, 384, 64])
+@pytest.mark.parametrize("dim", [192, 384, 64, 128, 256, 40])
 def test_layer_norm_matches_torch(cuda_device, dim):
+    # 64 k <= 256: segment layout (4 rows per warp pass; 2999 rows leave a ragged last group)
     gen = torch.Generator(device=cuda_device).manual_seed(dim)
-    x = (torch.randn(3, 1000, dim, device=cuda_device, generator=gen) * 3 + 1).to(torch.bfloat16)
+    x = (torch.randn(1, 2999, dim, device=cuda_device, generator=gen) * 3 + 1).to(torch.bfloat16)
     norm = torch.nn.LayerNorm(dim).to(cuda_device, torch.bfloat16)
     with torch.no_grad():
         norm.weight.normal_()
@@ -52,7 +53,7 @@ def test_layer_norm_matches_torch(cuda_device, dim):
     y = torch.empty_like(x)
     with torch.cuda.device(cuda_device):
         _native.check(_native.lib().p3d_layer_norm(_native.ptr(x), _native.ptr(norm.weight), _native.ptr(norm.bias),
-                                                   _native.ptr(y), _native.BF16, 3000, dim, 1e-5,
+                                                   _native.ptr(y), _native.BF16, 2999, dim, 1e-5,
                                                    _native.stream_of(cuda_device)), "p3d_layer_norm")
     want = norm(x)
     err = (y.float() - want.float()).abs()
@@ -118,12 +119,12 @@ def test_qkv_merge_is_the_exact_backward_of_the_split(cuda_device, dtype, h, g, 
     assert torch.equal(qp.grad, want_q) and torch.equal(kvp.grad, want_kv)
 
 
-@pytest.mark.parametrize("dim", [192, 384])
+@pytest.mark.parametrize("dim", [192, 384, 64, 128, 40])
 def test_layer_norm_backward_matches_torch(cuda_device, dim):
     from pack3d_b200 import glue
     gen = torch.Generator(device=cuda_device).manual_seed(dim)
-    x = (torch.randn(2, 3000, dim, device=cuda_device, generator=gen) * 2 + 0.5).to(torch.bfloat16)
-    dy = torch.randn(2, 3000, dim, device=cuda_device, generator=gen).to(torch.bfloat16)
+    x = (torch.randn(2, 2999, dim, device=cuda_device, generator=gen) * 2 + 0.5).to(torch.bfloat16)
+    dy = torch.randn(2, 2999, dim, device=cuda_device, generator=gen).to(torch.bfloat16)
     norm = torch.nn.LayerNorm(dim).to(cuda_device, torch.bfloat16)
     with torch.no_grad():
         norm.weight.normal_()
