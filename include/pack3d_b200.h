@@ -180,6 +180,9 @@ typedef struct {
 /* p3d_operator.options: run only the neighbour-table (indexed) kernels, as the reference's
  * Triton backend is structured -- for comparison and testing. */
 #define P3D_OPT_INDEXED_ONLY 1u
+/* p3d_operator.options: the dy of p3d_attn_bwd / p3d_bwd_mix is token-major, [B,N,H,D] (the
+ * layout of the output projection's input gradient), instead of [B,H,N,D]. */
+#define P3D_OPT_DY_ROWS 2u
 
 /*
  * Forward (kernels.py:289-311).  Writes y [B,H,N,D] and the summaries sk, sv

@@ -20,6 +20,7 @@ FWD_FORCE_INDEXED = 2
 FWD_SUMMARIES_GIVEN = 4
 FWD_Y_ROWS = 8
 OPT_INDEXED_ONLY = 1
+OPT_DY_ROWS = 2
 
 _c_int, _c_i64, _c_f32, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 

@@ -14,7 +14,7 @@ from torch import nn
 
 from ._validation import HEAD_DIMS, check_cuda
 from .geometry import TokenLayout
-from .ops import pack3d_streamed
+from .ops import pack3d_streamed, pack3d_token_major
 from . import glue
 from .rope import balanced_pairs, phase_tables, rotate_projections
 
@@ -91,6 +91,11 @@ class PACK3DAttention(nn.Module):
             q, kl, kg = rotate_projections(q, kl, kg, layout.coords, pairs, layout.grid_shape, packed=packed)
         gates = self.gate(x).reshape(b, n, self.heads, 2).softmax(-1)
         gate = gates[..., 1].transpose(1, 2)
+        if phases is not None:
+            # token-major core output: to_out reads it, and takes the residual, in one GEMM
+            out = pack3d_token_major(q, kl, vl, kg, vg, self.pool_weight, self.slot_bias, gate, self.local_scale,
+                                     self.global_scale, layout.geometry, temperature=self.temperature)
+            return self._out_residual(residual, out)
         out = pack3d_streamed(q, kl, vl, kg, vg, self.pool_weight, self.slot_bias, gate, self.local_scale,
                               self.global_scale, layout.geometry, temperature=self.temperature)
         return residual + self.to_out(out.transpose(1, 2).reshape(b, n, -1))

@@ -70,7 +70,8 @@ int summaries_of(const p3d_operator *op) { return (op->fine_blocks + op->pool_si
 int validate(const p3d_operator *op) {
   P3D_CHECK_ARG(op != nullptr, "null operator descriptor");
   P3D_CHECK_ARG(dtype_ok(op->dtype) && dtype_ok(op->gate_dtype), "unknown dtype");
-  P3D_CHECK_ARG((op->options & ~P3D_OPT_INDEXED_ONLY) == 0u, "unknown option bits 0x%x", op->options);
+  P3D_CHECK_ARG((op->options & ~(P3D_OPT_INDEXED_ONLY | P3D_OPT_DY_ROWS)) == 0u, "unknown option bits 0x%x",
+                op->options);
   P3D_CHECK_ARG(op->batch >= 1 && op->heads >= 1 && op->tokens >= 1 && op->kv_heads >= 1,
                 "batch, heads, kv_heads and tokens must be positive");
   P3D_CHECK_ARG(op->heads % op->kv_heads == 0, "query heads must be divisible by KV heads");
@@ -498,6 +499,8 @@ int p3d_attn_bwd(const p3d_operator *op, const void *dy, const void *sk, const v
   mix.tokens = op->tokens;
   mix.head_dim = d;
   mix.chunk_rows = mix_bwd_chunk_rows();
+  mix.heads = op->heads;
+  mix.dy_rows = (op->options & P3D_OPT_DY_ROWS) ? 1 : 0;
   mix.dy = dy;
   mix.ol = ol;
   mix.og = og;
@@ -669,6 +672,8 @@ int p3d_bwd_mix(const p3d_operator *op, const void *dy, const void *ol, const vo
   mix.tokens = op->tokens;
   mix.head_dim = op->head_dim;
   mix.chunk_rows = mix_bwd_chunk_rows();
+  mix.heads = op->heads;
+  mix.dy_rows = (op->options & P3D_OPT_DY_ROWS) ? 1 : 0;
   mix.dy = dy;
   mix.ol = ol;
   mix.og = og;

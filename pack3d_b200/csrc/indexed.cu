@@ -162,6 +162,7 @@ __global__ void __launch_bounds__(kWarps * 32) mix_bwd_kernel(MixBwdArgs a) {
   float dsl[4] = {0.f, 0.f, 0.f, 0.f}, dsg[4] = {0.f, 0.f, 0.f, 0.f};
   for (int i = r0; i < r1; ++i) {
     const int64_t row = (int64_t)bh * a.tokens + i;
+    const int64_t dy_row = a.dy_rows ? ((int64_t)(bh / a.heads) * a.tokens + i) * a.heads + bh % a.heads : row;
     const float gate = load_any(a.gate, a.gate_dtype, row);
     float dl = 0.f, dg = 0.f, dgate = 0.f;
 #pragma unroll
@@ -169,7 +170,7 @@ __global__ void __launch_bounds__(kWarps * 32) mix_bwd_kernel(MixBwdArgs a) {
       const int ch = lane + 32 * c;
       if (ch >= d) continue;
       const int64_t off = row * d + ch;
-      const float g_y = to_f32<T>(dy[off]), o_l = to_f32<T>(ol[off]), o_g = to_f32<T>(og[off]);
+      const float g_y = to_f32<T>(dy[dy_row * d + ch]), o_l = to_f32<T>(ol[off]), o_g = to_f32<T>(og[off]);
       // Delta uses the same rounded branch gradients the attention VJPs consume.
       const float g_l = round_to<T>(g_y * a.sl[ch]);
       const float g_g = round_to<T>((g_y * gate) * a.sg[ch]);
@@ -271,11 +272,13 @@ __global__ void __launch_bounds__(kWarps * 32) mix_bwd_vec_kernel(MixBwdArgs a) 
 #pragma unroll
     for (int i = 0; i < G::kBatch; ++i) {
       const int t = base + i * G::kR + seg;
-      const int64_t row = (int64_t)bh * a.tokens + (t < r1 ? t : r0);
+      const int tt = t < r1 ? t : r0;
+      const int64_t row = (int64_t)bh * a.tokens + tt;
       const int64_t off = row * D + 8 * c;
+      const int64_t dy_row = a.dy_rows ? ((int64_t)(bh / a.heads) * a.tokens + tt) * a.heads + bh % a.heads : row;
       rgy[i] = rlo[i] = rgo[i] = make_uint4(0u, 0u, 0u, 0u);
       if (on && t < r1) {
-        rgy[i] = *reinterpret_cast<const uint4 *>(dy + off);
+        rgy[i] = *reinterpret_cast<const uint4 *>(dy + dy_row * D + 8 * c);
         rlo[i] = *reinterpret_cast<const uint4 *>(ol + off);
         rgo[i] = *reinterpret_cast<const uint4 *>(og + off);
       }

@@ -56,6 +56,7 @@ int launch_global_fwd_mix(const IndexedArgs &a, const void *ol, void *y, void *o
 // Backward pieces.
 struct MixBwdArgs {
   int dtype, gate_dtype, bh, tokens, head_dim, chunk_rows;
+  int heads, dy_rows;  // dy_rows: dy is [B,N,H,D] (row (b,h,i) at ((b N + i) H + h) D)
   const void *dy, *ol, *og, *gate;
   const float *sl, *sg;
   void *dol, *dog;         // dtype

@@ -110,10 +110,11 @@ def forward(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature
     return y, ((sk, sv, ol, og, lse_l, lse_g) if save_state else ())
 
 
-def backward(dy, inputs, saved, geometry, temperature, *, force_indexed=False):
+def backward(dy, inputs, saved, geometry, temperature, *, force_indexed=False, dy_rows=False):
     """Launch the backward; returns the ten input gradients in the inputs' dtypes.
 
     ``force_indexed`` runs the neighbour-table kernels even on a complete stencil.
+    ``dy_rows``: dy is a [B, H, N, D] view of a contiguous [B, N, H, D] tensor (token-major).
     """
     q, kl, vl, kg, vg, weight, bias, gate, sl, sg = inputs
     sk, sv, ol, og, lse_l, lse_g = saved
@@ -122,6 +123,8 @@ def backward(dy, inputs, saved, geometry, temperature, *, force_indexed=False):
     op, keep = _operator(q, kl, vl, kg, vg, w32, b32, gate_k, sl32, sg32, geometry, temperature)
     if force_indexed:
         op.options |= _native.OPT_INDEXED_ONLY
+    if dy_rows:
+        op.options |= _native.OPT_DY_ROWS
     dq, dkl, dvl, dkg, dvg = (torch.empty_like(t) for t in (q, kl, vl, kg, vg))
     dgate = torch.empty_like(gate_k)
     d = q.shape[-1]
@@ -143,11 +146,20 @@ def backward(dy, inputs, saved, geometry, temperature, *, force_indexed=False):
             dsl.to(sl.dtype), dsg.to(sg.dtype))
 
 
+def _token_major(t):
+    """True when the [B, H, N, D] tensor t is a view of a contiguous [B, N, H, D] tensor."""
+    return t.transpose(1, 2).is_contiguous()
+
+
 class _Pack3D(torch.autograd.Function):
+    """The core as an autograd function.  ``y_rows`` returns y token-major (a [B, H, N, D]
+    view of a [B, N, H, D] tensor, as the layer's output projection reads it); a gradient
+    arriving in that layout is consumed without a copy (``P3D_OPT_DY_ROWS``)."""
+
     @staticmethod
-    def forward(ctx, q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature):
+    def forward(ctx, q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature, y_rows=False):
         inputs = tuple(t.contiguous() for t in (q, kl, vl, kg, vg, weight, bias, gate, sl, sg))
-        y, saved = forward(*inputs, geometry, temperature)
+        y, saved = forward(*inputs, geometry, temperature, y_rows=y_rows)
         ctx.save_for_backward(*inputs, *saved, *geometry.tensors)
         ctx.geometry, ctx.temperature = geometry, temperature
         return y
@@ -157,8 +169,27 @@ class _Pack3D(torch.autograd.Function):
     def backward(ctx, dy):
         ctx.geometry.check_unmodified()
         saved = ctx.saved_tensors
-        grads = backward(dy.contiguous(), saved[:10], saved[10:16], ctx.geometry, ctx.temperature)
-        return (*grads, None, None)
+        if dy.is_contiguous():
+            grads = backward(dy, saved[:10], saved[10:16], ctx.geometry, ctx.temperature)
+        elif _token_major(dy):
+            grads = backward(dy, saved[:10], saved[10:16], ctx.geometry, ctx.temperature, dy_rows=True)
+        else:
+            grads = backward(dy.contiguous(), saved[:10], saved[10:16], ctx.geometry, ctx.temperature)
+        return (*grads, None, None, None)
+
+
+def pack3d_token_major(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry: Pack3DGeometry, *,
+                       temperature=1.0):
+    """:func:`pack3d_streamed` with y returned token-major: a [B, H, N, D] view of a [B, N, H, D]
+    tensor, so ``y.transpose(1, 2).reshape(B, N, H * D)`` (the output projection's input) is
+    free, and its gradient reaches the backward without a transpose copy."""
+    validate_inputs(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature)
+    check_cuda(q)
+    inputs = (q, kl, vl, kg, vg, weight, bias, gate, sl, sg)
+    if torch.is_grad_enabled() and any(t.requires_grad for t in inputs):
+        return _Pack3D.apply(*inputs, geometry, float(temperature), True)
+    y, _ = forward(*(t.contiguous() for t in inputs), geometry, float(temperature), save_state=False, y_rows=True)
+    return y
 
 
 def pack3d_streamed(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry: Pack3DGeometry, *,

@@ -239,3 +239,25 @@ def test_indexed_and_custom_graph_paths_agree(cuda_device):
     assert max_abs(a, b) <= 2e-2
     y, _ = p3d_ops.forward(*[t.contiguous() for t in inputs], custom.geometry, 1.0, save_state=False)
     assert y.shape == a.shape
+
+
+@pytest.mark.parametrize("dtype,d", [(torch.bfloat16, 48), (torch.float16, 64), (torch.float32, 48), (torch.bfloat16, 16)])
+def test_token_major_output_and_gradient_are_layout_only(cuda_device, dtype, d):
+    """``pack3d_token_major`` / ``P3D_OPT_DY_ROWS`` change storage order only: the same y and
+    bitwise the same gradients as the head-major call with a contiguous dy."""
+    from pack3d_b200.ops import pack3d_token_major
+    layout = _grid_layout((8, 8, 16)).to(cuda_device)
+    n = layout.geometry.num_tokens
+    inputs = [t.to(cuda_device) for t in grid_inputs(n, 2, 4, 2, d, dtype, 5, True)]
+    gen = torch.Generator(device=cuda_device).manual_seed(3)
+    dy_rows = torch.randn(2, n, 4, d, device=cuda_device, generator=gen).to(dtype)   # [B, N, H, D]
+    results = []
+    for fn, dy in ((pack3d_streamed, dy_rows.transpose(1, 2).contiguous()), (pack3d_token_major, dy_rows.transpose(1, 2))):
+        leaves = [t.clone().requires_grad_() for t in inputs]
+        y = fn(*leaves, layout.geometry)
+        grads = torch.autograd.grad(y, leaves, dy)
+        results.append((y, grads))
+    (y0, g0), (y1, g1) = results
+    assert y1.transpose(1, 2).is_contiguous() and torch.equal(y0, y1)
+    for nm, a, b in zip(NAMES, g0, g1):
+        assert torch.equal(a, b), nm
