@@ -114,6 +114,20 @@ P3D_API int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl, vo
                   int pz, int py, int px, const float *phases, int ez, int ey, int ex, void *stream);
 
 /*
+ * p3d_qkv_project: the projections and the split in one kernel -- the two nn.Linear calls of
+ *   attention.py:70-72 (to_q, to_kv; weights wq [H*D, dim], wkv [4*G*D, dim], no bias) on x
+ *   [B*N, dim], followed by p3d_qkv_split: each projection is rounded to dtype, as the GEMM's
+ *   output would be, then rotated and stored head-major as p3d_qkv_split stores it.  The
+ *   projections never reach HBM.  Shapes p3d_qkv_project_supported() rejects return
+ *   P3D_ERR_UNSUPPORTED (callers then run the GEMMs and p3d_qkv_split).
+ */
+P3D_API int p3d_qkv_project_supported(int dtype, int dim, int heads, int kv_heads, int head_dim);
+P3D_API int p3d_qkv_project(const void *x, const void *wq, const void *wkv, void *q, void *kl, void *vl, void *kg,
+                    void *vg, int dtype, int batch, int heads, int kv_heads, int tokens, int dim, int head_dim,
+                    const int64_t *coords, int pz, int py, int px, const float *phases, int ez, int ey, int ex,
+                    void *stream);
+
+/*
  * Layer glue of the training path (their backward halves):
  * p3d_qkv_merge: the backward of p3d_qkv_split -- replaces _Rotary.backward (rotary.py:66-70,
  *   the inverse rotation of dq, dkl, dkg) and the transposes / chunk concatenation autograd

@@ -58,6 +58,10 @@ class PACK3DAttention(nn.Module):
         # 16-bit CUDA training calls run LayerNorm and the projection split (with RoPE) in the
         # fused library kernels of pack3d_b200.glue; False keeps the per-op PyTorch path.
         self.fused_glue = True
+        # p3d_qkv_project (projections + split in one tensor-core kernel) instead of the two
+        # cuBLAS projections and p3d_qkv_split: less HBM traffic, but not faster at present
+        # (0.355 vs 0.324 ms at config 1), so off by default
+        self.fused_projection = False
 
     def forward(self, x, layout: TokenLayout):
         layout.check_unmodified()
@@ -80,8 +84,13 @@ class PACK3DAttention(nn.Module):
             # backward halves in the library kernels (pack3d_b200.glue)
             x = glue.layer_norm(x, self.norm)
             coords = layout.coords.to(device=x.device, dtype=torch.int64).contiguous()
-            q, kl, vl, kg, vg = glue.qkv_split(self.to_q(x), self.to_kv(x), coords, phases, pairs,
-                                               layout.grid_shape, self.heads, self.kv_heads, self.head_dim)
+            if self.fused_projection and glue.project_supported(x, self.to_q.weight, self.to_kv.weight, self.heads,
+                                                                self.kv_heads, self.head_dim):
+                q, kl, vl, kg, vg = glue.qkv_project(x, self.to_q.weight, self.to_kv.weight, coords, phases, pairs,
+                                                     layout.grid_shape, self.heads, self.kv_heads, self.head_dim)
+            else:
+                q, kl, vl, kg, vg = glue.qkv_split(self.to_q(x), self.to_kv(x), coords, phases, pairs,
+                                                   layout.grid_shape, self.heads, self.kv_heads, self.head_dim)
         else:
             x = self.norm(x)
             q = self.to_q(x).reshape(b, n, self.heads, self.head_dim).transpose(1, 2)
@@ -154,10 +163,18 @@ class PACK3DAttention(nn.Module):
             _native.check(lib.p3d_layer_norm(_native.ptr(x), _native.ptr(self.norm.weight), _native.ptr(self.norm.bias),
                                              _native.ptr(xn), code, b * n, self.dim, float(self.norm.eps), stream),
                           "p3d_layer_norm")
-        qp, kvp = self.to_q(xn), self.to_kv(xn)
         pairs = balanced_pairs(d)
         extents = tuple(int(e) for e in grid_shape)
         _, phases = phase_tables(dev, pairs, extents)
+        if phases is not None and self.fused_projection and glue.project_supported(xn, self.to_q.weight,
+                                                                                  self.to_kv.weight, h, g, d):
+            # projections, split and RoPE in one kernel: the projections never reach HBM
+            coords = coords.to(device=dev, dtype=torch.int64).contiguous()
+            q, kl, vl, kg, vg = glue.project_split_raw(xn, self.to_q.weight, self.to_kv.weight, coords, phases, pairs,
+                                                       extents, h, g, d)
+            gate = self.gate(xn).reshape(b, n, h, 2).softmax(-1)[..., 1].transpose(1, 2).contiguous()
+            return x, q, kl, vl, kg, vg, gate
+        qp, kvp = self.to_q(xn), self.to_kv(xn)
         if phases is None:   # coordinate extents too large for a table: the general RoPE path
             q, kl, kg = rotate_projections(qp.reshape(b, n, h, d).transpose(1, 2),
                                            *(t.reshape(b, n, g, d).transpose(1, 2) for t in kvp.chunk(4, -1)[0::2]),

@@ -310,6 +310,7 @@ int p3d_device_errors(unsigned *flags) {
   P3D_CHECK_ARG(flags != nullptr, "p3d_device_errors: null output");
   *flags = 0;
   if (int st = take_fwd_errors(flags)) return st;
+  if (int st = take_proj_errors(flags)) return st;
   return take_bwd_errors(flags);
 }
 

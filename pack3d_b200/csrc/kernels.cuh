@@ -54,6 +54,24 @@ int launch_global_fwd_mix(const IndexedArgs &a, const void *ol, void *y, void *o
                           cudaStream_t s);
 
 // Backward pieces.
+// ---- fused projection + split + axial RoPE (csrc/proj.cu) ---------------------------------
+struct ProjArgs {
+  int dtype;                    // P3D_BF16 / P3D_F16
+  int rows, tokens, dim;        // rows = batch * tokens of x [rows, dim]
+  int heads, kv_heads, head_dim;
+  int group_heads;              // head rows per column group (proj_group_heads)
+  const void *x, *wq, *wkv;     // wq [heads*D, dim], wkv [4*kv_heads*D, dim] (nn.Linear weights)
+  void *out[5];                 // q [B,H,N,D], kl, vl, kg, vg [B,G,N,D]
+  const int64_t *coords;        // [N, 3]
+  int pairs[3], start[3];
+  const float *phases;
+  int table_floats;             // floats in the phase table
+};
+int proj_group_heads(int head_dim, int heads, int kv_heads, int dim, size_t smem_limit);
+size_t proj_smem_bytes(int dim, int group_cols);
+int launch_proj_split(const ProjArgs &a, cudaStream_t stream);
+int take_proj_errors(unsigned *flags);
+
 struct MixBwdArgs {
   int dtype, gate_dtype, bh, tokens, head_dim, chunk_rows;
   int heads, dy_rows;  // dy_rows: dy is [B,N,H,D] (row (b,h,i) at ((b N + i) H + h) D)

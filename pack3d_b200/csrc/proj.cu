@@ -1,0 +1,440 @@
+// Fused projection + split + axial RoPE (inference and training forward of the layer glue).
+//
+// The layer computes qp = LN(x) Wq^T and kvp = LN(x) Wkv^T (attention.py:53-89; the reference
+// runs them as two nn.Linear calls) and then splits them head-major, rotating q, kl and kg
+// (rotary.py).  p3d_qkv_split does the split from the bf16 projections in HBM; this kernel
+// removes the projections' round trip through HBM: for a 128-token tile it multiplies on the
+// tensor cores (tcgen05, fp32 accumulators in TMEM) and its epilogue rounds each projection
+// to the storage type -- as the GEMM's output would be -- then rotates and stores head-major
+// exactly as p3d_qkv_split does from that rounded value.
+//
+// Columns of Z = [q | kl | vl | kg | vg] are split into groups of G_h head rows (q groups,
+// then kv groups; a group never straddles q and kv).  A CTA owns one group: its slice of W
+// (G_h D rows x dim) stays in shared memory while it walks token tiles t = c, c + n, ... .
+// The CTAs of the different groups walk the same tiles at about the same time, so each X
+// tile comes from HBM once and from L2 for the other groups.
+//
+// Roles (576 threads): warp 0 TMA producer (W slice once, X tiles through a 2-stage ring),
+// warp 1 MMA issuer (Z tile into one of two TMEM accumulators), warps 2-17 epilogue: a token
+// row (TMEM lane) per thread, four warps per lane quarter splitting the group's heads.  The
+// RoPE phase table is staged in shared memory once per CTA; a token's coordinates are fetched
+// a tile ahead, so the epilogue does not wait on global loads.  Every wait is bounded (2 s): on a timeout the kernel records an
+// error bit (p3d_device_errors), drains its copies and MMAs and frees TMEM.
+#include "common.cuh"
+#include "kernels.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
+
+namespace p3d {
+namespace {
+
+using namespace sm100;
+
+__device__ unsigned g_proj_errors = 0;
+
+constexpr int kSplit = 4;                        // epilogue warps per TMEM lane quarter
+constexpr int kEpilogueThreads = 128 * kSplit;
+constexpr int kThreads = 64 + kEpilogueThreads;
+constexpr int kProducerWarp = 0, kMmaWarp = 1;  // warps 2..: epilogue
+constexpr int kMaxTableFloats = 8192;           // phase tables up to 32 KB live in shared memory
+constexpr int kTile = 128;                      // tokens per tile (MMA M)
+constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr int kTmemCols = 512;
+
+enum : int {
+  kWFull = 0,
+  kXFull = 1,       // [2]
+  kXEmpty = 3,      // [2]
+  kAccFull = 5,     // [2]
+  kAccEmpty = 7,    // [2], 128 arrivals (the epilogue threads)
+  kDrain = 9,
+  kNumBars = 10
+};
+
+struct ProjParams {
+  int rows;            // B * N token rows of X
+  int tokens;          // N
+  int kc;              // dim / 64: 64-channel (128-byte, SWIZZLE_128B) boxes along K
+  int heads, kv_heads;
+  int group_heads;     // head rows per group (G_h)
+  int groups_q;        // groups over the q head rows; the rest cover the 4 kv_heads kv head rows
+  int groups;
+  int ctas_per_group;
+  void *out[5];        // q [B,H,N,D], kl, vl, kg, vg [B,G,N,D]
+  const int64_t *coords;
+  int pairs[3], start[3];
+  const float *phases;
+  int table_floats;    // 2 * (ez pz + ey py + ex px); staged in shared memory when <= kMaxTableFloats
+};
+
+// (cos, sin) of rotation pair `pair` of a token at coordinates c, from the table `tab`.
+__device__ __forceinline__ float2 pair_cs(const ProjParams &p, const float *tab, const int (&c)[3], int pair) {
+  int entry;
+  if (pair < p.pairs[0]) {
+    entry = p.start[0] + c[0] * p.pairs[0] + pair;
+  } else if (pair < p.pairs[0] + p.pairs[1]) {
+    entry = p.start[1] + c[1] * p.pairs[1] + (pair - p.pairs[0]);
+  } else {
+    entry = p.start[2] + c[2] * p.pairs[2] + (pair - p.pairs[0] - p.pairs[1]);
+  }
+  return *reinterpret_cast<const float2 *>(tab + 2 * entry);
+}
+
+template <bool BF16>
+__device__ __forceinline__ float2 unpack_pair(uint32_t v) {  // exact
+  if constexpr (BF16) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+  } else {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&v));
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
+  return BF16 ? pack_bf16(lo, hi) : pack_f16(lo, hi);
+}
+
+template <bool BF16, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    proj_split_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap twq,
+                      const __grid_constant__ CUtensorMap twkv, const ProjParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.group_heads * D;                 // accumulator columns (MMA N)
+  const uint32_t x_atom = kTile * 128;             // bytes of one 64-channel box of an X tile
+  const uint32_t w_atom = (uint32_t)G * 128;       // of the W slice (G multiple of 16: 1024-aligned)
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t w_smem = base;
+  const uint32_t x_smem = w_smem + p.kc * w_atom;  // 2 stages of kc * x_atom
+  const uint32_t x_stage = p.kc * x_atom;
+  const uint32_t bars = x_smem + 2 * x_stage;
+  float *table = reinterpret_cast<float *>(smem_raw + (bars + 8u * kNumBars + 15u - raw) / 16u * 16u);
+  __shared__ uint32_t tmem_holder;
+  auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
+
+  const int group = blockIdx.x % p.groups, slot = blockIdx.x / p.groups;
+  const bool is_q = group < p.groups_q;
+  const int head0 = (is_q ? group : group - p.groups_q) * p.group_heads;  // first head row of the group
+  const int n_tiles = (p.rows + kTile - 1) / kTile;
+  const int my_tiles = slot < n_tiles ? (n_tiles - 1 - slot) / p.ctas_per_group + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(kWFull), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(kXFull + s), 1);
+      mbar_init(bar(kXEmpty + s), 1);
+      mbar_init(bar(kAccFull + s), 1);
+      mbar_init(bar(kAccEmpty + s), kEpilogueThreads);
+    }
+    mbar_init(bar(kDrain), 1);
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(&tmem_holder), kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    prefetch_tmap(&tx);
+    prefetch_tmap(is_q ? &twq : &twkv);
+  }
+  const bool table_in_smem = p.table_floats <= kMaxTableFloats;
+  if (table_in_smem)
+    for (int i = threadIdx.x; i < p.table_floats; i += kThreads) table[i] = p.phases[i];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_holder;
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const CUtensorMap *tw = is_q ? &twq : &twkv;
+      mbar_expect_tx(bar(kWFull), p.kc * w_atom);
+      for (int c = 0; c < p.kc; ++c) tma_load_3d(w_smem + c * w_atom, tw, bar(kWFull), 64 * c, head0 * D, 0);
+      int issued = 0;
+      for (int i = 0; i < my_tiles; ++i) {
+        const int s = i & 1, t = slot + i * p.ctas_per_group;
+        // XEmpty[s] completes once per use of stage s; completion i/2 - 1 frees it for tile i.
+        // Its neighbours are ruled out: the one before was awaited a ring turn ago, the one
+        // after needs tile i, not loaded yet.
+        if (i >= 2 && !mbar_wait(bar(kXEmpty + s), ((i >> 1) - 1) & 1, &g_proj_errors, kWaitNs, kErrProducer)) break;
+        const uint32_t st = x_smem + s * x_stage;
+        mbar_expect_tx(bar(kXFull + s), p.kc * x_atom);
+        for (int c = 0; c < p.kc; ++c) tma_load_3d(st + c * x_atom, &tx, bar(kXFull + s), 64 * c, t * kTile, 0);
+        issued = i + 1;
+      }
+      // no copies in flight into shared memory this CTA gives up
+      mbar_wait(bar(kWFull), 0, &g_proj_errors, kWaitNs, kErrTeardown);
+      for (int i = issued > 2 ? issued - 2 : 0; i < issued; ++i)
+        mbar_wait(bar(kXFull + (i & 1)), (i >> 1) & 1, &g_proj_errors, kWaitNs, kErrTeardown);
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(kTile, G, BF16, false);
+      uint32_t commits[kNumBars];
+      for (int i = 0; i < kNumBars; ++i) commits[i] = 0u;
+      auto commit = [&](int b_idx) {
+        mma_commit(bar(b_idx));
+        ++commits[b_idx];
+      };
+      const uint64_t desc_w = desc_sw128(w_smem, 1024);  // K-major, 8-row groups of 128-byte rows
+      const uint64_t desc_x = desc_sw128(x_smem, 1024);
+      bool ok = mbar_wait(bar(kWFull), 0, &g_proj_errors, kWaitNs, kErrMma);
+      for (int i = 0; ok && i < my_tiles; ++i) {
+        const int s = i & 1, a = i & 1;
+        ok = mbar_wait(bar(kXFull + s), (i >> 1) & 1, &g_proj_errors, kWaitNs, kErrMma);
+        // accumulator a was last used by tile i - 2: the epilogue must have read it out
+        if (ok && i >= 2) ok = mbar_wait(bar(kAccEmpty + a), ((i >> 1) - 1) & 1, &g_proj_errors, kWaitNs, kErrMma);
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t dx = desc_x + ((uint32_t)(s * x_stage) >> 4);
+        for (int c = 0; c < p.kc; ++c)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)  // K = 16 slices: 32 bytes along the 128-byte rows
+            mma_ss(tmem + a * G, dx + ((c * x_atom + 32 * k) >> 4), desc_w + ((c * w_atom + 32 * k) >> 4), idesc,
+                   (c | k) ? 1u : 0u);
+        commit(kXEmpty + s);
+        commit(kAccFull + a);
+      }
+      commit(kDrain);
+      for (int i = 0; i < kNumBars; ++i)
+        if (commits[i]) mbar_wait(bar(i), (commits[i] - 1) & 1, &g_proj_errors, kWaitNs, kErrTeardown);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;                   // TMEM lanes this warp may access
+    const int split = (warp - 2) >> 2;              // heads j = split, split + kSplit, ...
+    const int r = quarter * 32 + lane;              // token row within the tile = TMEM lane
+    const uint32_t t_lanes = tmem + ((uint32_t)(quarter * 32) << 16);
+    const float *tab = table_in_smem ? table : p.phases;
+    const int head_rows = is_q ? p.heads : 4 * p.kv_heads;
+    // coordinates of this thread's token in tile i (fetched one tile ahead)
+    auto fetch = [&](int i, int (&c)[3]) {
+      const int row = (slot + i * p.ctas_per_group) * kTile + r;
+      c[0] = c[1] = c[2] = 0;
+      if (i < my_tiles && row < p.rows) {
+        const int n = row % p.tokens;
+        c[0] = (int)p.coords[3 * (int64_t)n];
+        c[1] = (int)p.coords[3 * (int64_t)n + 1];
+        c[2] = (int)p.coords[3 * (int64_t)n + 2];
+      }
+    };
+    int cnext[3];
+    fetch(0, cnext);
+    for (int i = 0; i < my_tiles; ++i) {
+      const int a = i & 1, t = slot + i * p.ctas_per_group;
+      const int c3[3] = {cnext[0], cnext[1], cnext[2]};
+      fetch(i + 1, cnext);
+      const bool ready = mbar_wait(bar(kAccFull + a), (i >> 1) & 1, &g_proj_errors, kWaitNs, kErrSoftmax);
+      if (!__all_sync(0xffffffffu, ready)) break;
+      tc_fence_after();
+      const int row = t * kTile + r;
+      const bool valid = row < p.rows;
+      const int b = valid ? row / p.tokens : 0, n = valid ? row - b * p.tokens : 0;
+      for (int j = split; j < p.group_heads; j += kSplit) {
+        const int hr = head0 + j;  // head row within q, or within the 4 kv parts
+        if (hr >= head_rows) break;  // a short last group (warp-uniform)
+        uint32_t acc[D];
+#pragma unroll
+        for (int q16 = 0; q16 < D / 16; ++q16)
+          tmem_ld16(t_lanes + a * G + j * D + 16 * q16, *reinterpret_cast<uint32_t(*)[16]>(acc + 16 * q16));
+        tmem_wait_ld();
+        if (!valid) continue;
+        int part = 0, hh = hr;
+        if (!is_q) {
+          part = hr / p.kv_heads;
+          hh = hr - part * p.kv_heads;
+        }
+        const bool rot = is_q || (part & 1) == 0;  // q, kl, kg
+        const int ht = is_q ? p.heads : p.kv_heads;
+        uint32_t packed[D / 2];
+#pragma unroll
+        for (int q2 = 0; q2 < D / 2; ++q2) {
+          // the projection pair rounded to the storage type (as the GEMM output would be)
+          packed[q2] = pack_pair<BF16>(__uint_as_float(acc[2 * q2]), __uint_as_float(acc[2 * q2 + 1]));
+        }
+        if (rot) {
+#pragma unroll
+          for (int q2 = 0; q2 < D / 2; ++q2) {
+            const float2 e_o = unpack_pair<BF16>(packed[q2]);
+            const float2 c = pair_cs(p, tab, c3, q2);
+            const float even = __fsub_rn(__fmul_rn(e_o.x, c.x), __fmul_rn(e_o.y, c.y));
+            const float odd = __fadd_rn(__fmul_rn(e_o.x, c.y), __fmul_rn(e_o.y, c.x));
+            packed[q2] = pack_pair<BF16>(even, odd);
+          }
+        }
+        void *o = is_q ? p.out[0] : p.out[1 + part];
+        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(o) + (((int64_t)b * ht + hh) * p.tokens + n) * D);
+#pragma unroll
+        for (int v = 0; v < D / 8; ++v)
+          dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+      }
+      tc_fence_before();
+      mbar_arrive(bar(kAccEmpty + a));
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <bool BF16, int D>
+int launch_proj(const ProjArgs &a, cudaStream_t stream) {
+  const uint64_t es = 2;
+  const int K = a.dim;
+  CUtensorMap tx, twq, twkv;
+  const int gh = a.group_heads;
+  {
+    const uint64_t dims[3] = {(uint64_t)K, (uint64_t)a.rows, 1};
+    const uint64_t strides[2] = {K * es, (uint64_t)a.rows * K * es};
+    const uint32_t box[3] = {64, kTile, 1};
+    if (int st = encode_operand_sw128(&tx, a.dtype, a.x, 3, dims, strides, box)) return st;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)K, (uint64_t)a.heads * D, 1};
+    const uint64_t strides[2] = {K * es, (uint64_t)a.heads * D * K * es};
+    const uint32_t box[3] = {64, (uint32_t)(gh * D), 1};
+    if (int st = encode_operand_sw128(&twq, a.dtype, a.wq, 3, dims, strides, box)) return st;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)K, (uint64_t)4 * a.kv_heads * D, 1};
+    const uint64_t strides[2] = {K * es, (uint64_t)4 * a.kv_heads * D * K * es};
+    const uint32_t box[3] = {64, (uint32_t)(gh * D), 1};
+    if (int st = encode_operand_sw128(&twkv, a.dtype, a.wkv, 3, dims, strides, box)) return st;
+  }
+  ProjParams p{};
+  p.rows = a.rows;
+  p.tokens = a.tokens;
+  p.kc = K / 64;
+  p.heads = a.heads;
+  p.kv_heads = a.kv_heads;
+  p.group_heads = gh;
+  p.groups_q = (a.heads + gh - 1) / gh;
+  p.groups = p.groups_q + (4 * a.kv_heads + gh - 1) / gh;
+  DeviceInfo info{};
+  if (int st = device_info(&info)) return st;
+  p.ctas_per_group = info.sm_count / p.groups > 0 ? info.sm_count / p.groups : 1;
+  for (int i = 0; i < 5; ++i) p.out[i] = a.out[i];
+  p.coords = a.coords;
+  for (int i = 0; i < 3; ++i) {
+    p.pairs[i] = a.pairs[i];
+    p.start[i] = a.start[i];
+  }
+  p.phases = a.phases;
+  p.table_floats = a.table_floats;
+  const size_t smem = proj_smem_bytes(a.dim, gh * D);
+  auto kernel = proj_split_kernel<BF16, D>;
+  static size_t configured = 0;
+  if (smem > configured) {
+    P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    configured = smem;
+  }
+  kernel<<<p.groups * p.ctas_per_group, kThreads, smem, stream>>>(tx, twq, twkv, p);
+  P3D_LAUNCH_CHECK();
+  return P3D_OK;
+}
+
+}  // namespace
+
+size_t proj_smem_bytes(int dim, int group_cols) {
+  // W slice + 2 X stages (64-channel boxes of 128-byte rows) + barriers + the phase table (at
+  // most kMaxTableFloats) + 1024 alignment slack
+  return (size_t)(dim / 64) * group_cols * 128 + 2 * (size_t)(dim / 64) * kTile * 128 + 8 * kNumBars + 16 +
+         4 * (size_t)kMaxTableFloats + 1024;
+}
+
+int proj_group_heads(int head_dim, int heads, int kv_heads, int dim, size_t smem_limit) {
+  int gh = 256 / head_dim;  // MMA N <= 256 and 2 accumulators in 512 TMEM columns
+  if (gh > heads) gh = heads;
+  if (gh > 4 * kv_heads) gh = 4 * kv_heads;
+  // the W slice shrinks with the group (+ 1 KB of static shared memory)
+  while (gh > 1 && proj_smem_bytes(dim, gh * head_dim) + 1024 > smem_limit) --gh;
+  return gh < 1 ? 1 : gh;
+}
+
+int launch_proj_split(const ProjArgs &a, cudaStream_t stream) {
+  if (a.rows == 0) return P3D_OK;
+  const bool bf16 = a.dtype == P3D_BF16;
+  switch (a.head_dim) {
+    case 16: return bf16 ? launch_proj<true, 16>(a, stream) : launch_proj<false, 16>(a, stream);
+    case 32: return bf16 ? launch_proj<true, 32>(a, stream) : launch_proj<false, 32>(a, stream);
+    case 48: return bf16 ? launch_proj<true, 48>(a, stream) : launch_proj<false, 48>(a, stream);
+    case 64: return bf16 ? launch_proj<true, 64>(a, stream) : launch_proj<false, 64>(a, stream);
+    case 128: return bf16 ? launch_proj<true, 128>(a, stream) : launch_proj<false, 128>(a, stream);
+    default: return fail(P3D_ERR_UNSUPPORTED, "p3d_qkv_project: head_dim %d", a.head_dim);
+  }
+}
+
+int take_proj_errors(unsigned *flags) {
+  unsigned v = 0, zero = 0;
+  P3D_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_proj_errors, sizeof(v)));
+  P3D_CUDA_TRY(cudaMemcpyToSymbol(g_proj_errors, &zero, sizeof(zero)));
+  *flags |= v;
+  return P3D_OK;
+}
+
+}  // namespace p3d
+
+using namespace p3d;
+
+extern "C" int p3d_qkv_project_supported(int dtype, int dim, int heads, int kv_heads, int head_dim) {
+  if (dtype != P3D_BF16 && dtype != P3D_F16) return 0;
+  if (head_dim != 16 && head_dim != 32 && head_dim != 48 && head_dim != 64 && head_dim != 128) return 0;
+  if (dim < 64 || dim % 64 != 0 || heads < 1 || kv_heads < 1 || heads % kv_heads != 0) return 0;
+  DeviceInfo info{};
+  if (device_info(&info) != P3D_OK) return 0;
+  const int gh = proj_group_heads(head_dim, heads, kv_heads, dim, info.smem_optin);
+  return proj_smem_bytes(dim, gh * head_dim) + 1024 <= info.smem_optin ? 1 : 0;
+}
+
+extern "C" int p3d_qkv_project(const void *x, const void *wq, const void *wkv, void *q, void *kl, void *vl, void *kg,
+                               void *vg, int dtype, int batch, int heads, int kv_heads, int tokens, int dim,
+                               int head_dim, const int64_t *coords, int pz, int py, int px, const float *phases,
+                               int ez, int ey, int ex, void *stream) {
+  P3D_CHECK_ARG(x && wq && wkv && q && kl && vl && kg && vg && coords && phases, "p3d_qkv_project: null pointer");
+  P3D_CHECK_ARG(batch >= 0 && tokens >= 0 && (int64_t)batch * tokens < (int64_t(1) << 31),
+                "p3d_qkv_project: bad batch / token counts");
+  P3D_CHECK_ARG(pz >= 0 && py >= 0 && px >= 0 && 2 * (pz + py + px) == head_dim && ez >= 1 && ey >= 1 && ex >= 1,
+                "p3d_qkv_project: bad rotation pairs / extents");
+  for (const void *t : {x, wq, wkv, (const void *)q, (const void *)kl, (const void *)vl, (const void *)kg,
+                        (const void *)vg})
+    P3D_CHECK_ARG(((uintptr_t)t & 15) == 0, "p3d_qkv_project: 16-byte aligned tensors required");
+  if (!p3d_qkv_project_supported(dtype, dim, heads, kv_heads, head_dim))
+    return fail(P3D_ERR_UNSUPPORTED, "p3d_qkv_project: unsupported shape (dtype %d, dim %d, heads %d/%d, D %d)",
+                dtype, dim, heads, kv_heads, head_dim);
+  ProjArgs a{};
+  a.dtype = dtype;
+  a.rows = batch * tokens;
+  a.tokens = tokens;
+  a.dim = dim;
+  a.heads = heads;
+  a.kv_heads = kv_heads;
+  a.head_dim = head_dim;
+  DeviceInfo info{};
+  if (int st = device_info(&info)) return st;
+  a.group_heads = proj_group_heads(head_dim, heads, kv_heads, dim, info.smem_optin);
+  a.x = x;
+  a.wq = wq;
+  a.wkv = wkv;
+  a.out[0] = q;
+  a.out[1] = kl;
+  a.out[2] = vl;
+  a.out[3] = kg;
+  a.out[4] = vg;
+  a.coords = coords;
+  a.pairs[0] = pz;
+  a.pairs[1] = py;
+  a.pairs[2] = px;
+  a.start[0] = 0;
+  a.start[1] = ez * pz;
+  a.start[2] = ez * pz + ey * py;
+  a.phases = phases;
+  a.table_floats = 2 * (ez * pz + ey * py + ex * px);
+  return launch_proj_split(a, static_cast<cudaStream_t>(stream));
+}

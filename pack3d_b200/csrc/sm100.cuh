@@ -248,6 +248,19 @@ __device__ __forceinline__ uint64_t desc_sw32(uint32_t smem_addr, uint32_t lbo_b
   return d;
 }
 
+// Shared-memory matrix descriptor, SWIZZLE_128B K-major layout: 8-row groups of 128-byte rows
+// (1024-byte atoms, 1024-byte aligned) at stride sbo.  A K = 16 slice of a 16-bit operand is
+// 32 bytes of each row: successive slices advance the start address by 32 bytes.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_addr, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;  // leading-dimension offset: unused for swizzled K-major
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;  // layout type SWIZZLE_128B
+  return d;
+}
+
 // Instruction descriptor of kind::f16 with fp32 accumulation.
 //   ab_bf16: operands are bf16 (else f16); b_mn_major: B is MN-major (else K-major).
 __host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool ab_bf16, bool b_mn_major) {

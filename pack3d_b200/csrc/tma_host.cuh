@@ -49,6 +49,13 @@ inline int encode_operand(CUtensorMap *map, int dtype, const void *ptr, int rank
                       rank, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
+// 16-bit operand tiles with 64-channel (128-byte) rows, SWIZZLE_128B.
+inline int encode_operand_sw128(CUtensorMap *map, int dtype, const void *ptr, int rank, const uint64_t *dims,
+                                const uint64_t *strides, const uint32_t *box) {
+  return encode_tiled(map, dtype == P3D_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ptr,
+                      rank, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 // fp32 per-row values (logsumexp, Delta), no swizzle.
 inline int encode_rows_f32(CUtensorMap *map, const float *ptr, int rank, const uint64_t *dims, const uint64_t *strides,
                            const uint32_t *box) {

@@ -109,3 +109,87 @@ def qkv_split(qp, kvp, coords, phases, pairs, extents, heads, kv_heads, head_dim
     projections' device."""
     return _QKVSplit.apply(qp, kvp, coords, phases, tuple(int(p) for p in pairs), tuple(int(e) for e in extents),
                            int(heads), int(kv_heads), int(head_dim))
+
+
+def _merge(dq, dkl, dvl, dkg, dvg, coords, phases, pairs, extents, heads, kv_heads, head_dim, b, n, dt):
+    """``p3d_qkv_merge``: head-major gradients -> the projection gradients (dqp, dkvp)."""
+    dev = coords.device
+
+    def grad(t, h):
+        if t is None:
+            return torch.zeros((b, h, n, head_dim), dtype=dt, device=dev)
+        return t.to(dt).contiguous()
+
+    dq = grad(dq, heads)
+    dkl, dvl, dkg, dvg = (grad(t, kv_heads) for t in (dkl, dvl, dkg, dvg))
+    dqp = torch.empty((b, n, heads * head_dim), dtype=dt, device=dev)
+    dkvp = torch.empty((b, n, 4 * kv_heads * head_dim), dtype=dt, device=dev)
+    with torch.cuda.device(dev):
+        _native.check(_native.lib().p3d_qkv_merge(
+            _native.ptr(dq), _native.ptr(dkl), _native.ptr(dvl), _native.ptr(dkg), _native.ptr(dvg),
+            _native.ptr(dqp), _native.ptr(dkvp), _native.DTYPE_CODE[dt], b, heads, kv_heads, n, head_dim,
+            _native.ptr(coords), *pairs, _native.ptr(phases), *extents, _native.stream_of(dev)), "p3d_qkv_merge")
+    return dqp, dkvp
+
+
+def project_supported(x, wq, wkv, heads, kv_heads, head_dim):
+    """Whether ``p3d_qkv_project`` runs this shape (16-bit, contiguous 16-byte-aligned weights)."""
+    if x.dtype not in (torch.bfloat16, torch.float16) or not x.is_cuda:
+        return False
+    if not (wq.is_contiguous() and wkv.is_contiguous() and wq.dtype == x.dtype and wkv.dtype == x.dtype):
+        return False
+    if wq.data_ptr() % 16 or wkv.data_ptr() % 16:
+        return False
+    with torch.cuda.device(x.device):
+        return bool(_native.lib().p3d_qkv_project_supported(_native.DTYPE_CODE[x.dtype], x.shape[-1], heads,
+                                                            kv_heads, head_dim))
+
+
+def project_split_raw(x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, head_dim):
+    """``p3d_qkv_project`` on x [B, N, dim] (no autograd): ``(q, kl, vl, kg, vg)``."""
+    b, n, dim = x.shape
+    x = x.contiguous()
+    dev, dt = x.device, x.dtype
+    q = torch.empty((b, heads, n, head_dim), dtype=dt, device=dev)
+    kl, vl, kg, vg = (torch.empty((b, kv_heads, n, head_dim), dtype=dt, device=dev) for _ in range(4))
+    with torch.cuda.device(dev):
+        _native.check(_native.lib().p3d_qkv_project(
+            _native.ptr(x), _native.ptr(wq), _native.ptr(wkv), _native.ptr(q), _native.ptr(kl), _native.ptr(vl),
+            _native.ptr(kg), _native.ptr(vg), _native.DTYPE_CODE[dt], b, heads, kv_heads, n, dim, head_dim,
+            _native.ptr(coords), *pairs, _native.ptr(phases), *extents, _native.stream_of(dev)), "p3d_qkv_project")
+    return q, kl, vl, kg, vg
+
+
+class _QKVProject(torch.autograd.Function):
+    """The projections (to_q, to_kv: no bias) and the split in one kernel; backward: the merge,
+    then dx = dqp Wq + dkvp Wkv (the second GEMM accumulating into the first) and the weight
+    gradients."""
+
+    @staticmethod
+    def forward(ctx, x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, head_dim):
+        x = x.contiguous()
+        outs = project_split_raw(x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, head_dim)
+        ctx.save_for_backward(x, wq, wkv, coords, phases)
+        ctx.meta = (pairs, extents, heads, kv_heads, head_dim)
+        return outs
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, dq, dkl, dvl, dkg, dvg):
+        x, wq, wkv, coords, phases = ctx.saved_tensors
+        pairs, extents, heads, kv_heads, head_dim = ctx.meta
+        b, n, dim = x.shape
+        dqp, dkvp = _merge(dq, dkl, dvl, dkg, dvg, coords, phases, pairs, extents, heads, kv_heads, head_dim, b, n,
+                           x.dtype)
+        dqp2, dkvp2, x2 = dqp.view(b * n, -1), dkvp.view(b * n, -1), x.view(b * n, dim)
+        dx = torch.mm(dqp2, wq).addmm_(dkvp2, wkv)
+        dwq = torch.mm(dqp2.t(), x2) if ctx.needs_input_grad[1] else None
+        dwkv = torch.mm(dkvp2.t(), x2) if ctx.needs_input_grad[2] else None
+        return dx.view(b, n, dim), dwq, dwkv, None, None, None, None, None, None, None
+
+
+def qkv_project(x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, head_dim):
+    """Differentiable ``x -> (x Wq^T, x Wkv^T) -> split``: ``(q, kl, vl, kg, vg)`` head-major,
+    q / kl / kg rotated, through ``p3d_qkv_project`` (check ``project_supported`` first)."""
+    return _QKVProject.apply(x, wq, wkv, coords, phases, tuple(int(p) for p in pairs),
+                             tuple(int(e) for e in extents), int(heads), int(kv_heads), int(head_dim))
