@@ -578,14 +578,30 @@ __global__ void sum_middle_kernel(const float *in, float *out, int64_t outer, in
   out[t] = acc;
 }
 
-__global__ void sum_rows_kernel(const float *in, float *out, int64_t R, int64_t C, int rows_per_group) {
-  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+// Column sums of a row-major [R, C] fp32 matrix, in a fixed order (bitwise repeatable).
+// Block (x, g) sums rows [g*rows_per_group, ...) of the column chunk x (kSumCols columns):
+// thread t takes column t % kSumCols and every S-th row from sub-row t / kSumCols (S =
+// kSumThreads / kSumCols), and the S partials of a column are added in sub-row order.
+constexpr int kSumThreads = 256, kSumCols = 64;
+__global__ void __launch_bounds__(kSumThreads) sum_rows_kernel(const float *in, float *out, int64_t R, int64_t C,
+                                                               int rows_per_group) {
+  __shared__ float part[kSumThreads];
+  const int cols = C < kSumCols ? (int)C : kSumCols;
+  const int subs = kSumThreads / cols;
+  const int t = threadIdx.x, cl = t % cols, sub = t / cols;
+  const int64_t c = (int64_t)blockIdx.x * kSumCols + cl;
   const int64_t group = blockIdx.y;
-  if (c >= C) return;
   const int64_t r0 = group * rows_per_group, r1 = std::min<int64_t>(R, r0 + rows_per_group);
   float acc = 0.f;
-  for (int64_t r = r0; r < r1; ++r) acc += in[r * C + c];
-  out[group * C + c] = acc;
+  if (sub < subs && c < C)
+    for (int64_t r = r0 + sub; r < r1; r += subs) acc += in[r * C + c];
+  part[t] = acc;
+  __syncthreads();
+  if (sub == 0 && c < C) {
+    float total = 0.f;
+    for (int s = 0; s < subs; ++s) total += part[s * cols + cl];
+    out[group * C + c] = total;
+  }
 }
 
 bool vec_ok(const IndexedArgs &a) {
@@ -715,19 +731,17 @@ int launch_sum_middle(const float *in, float *out, int64_t outer, int S, int64_t
 
 int launch_sum_rows(const float *in, float *out, int64_t R, int64_t C, float *tmp, cudaStream_t s) {
   if (!C) return P3D_OK;
-  const int rows_per_group = 256;
-  const int64_t groups = (R + rows_per_group - 1) / rows_per_group;
-  const dim3 block(128);
+  const int64_t groups = (R + kSumRowsPerGroup - 1) / kSumRowsPerGroup;
+  const unsigned col_blocks = (unsigned)((C + kSumCols - 1) / kSumCols);
   if (groups <= 1) {
-    sum_rows_kernel<<<dim3((unsigned)((C + 127) / 128), 1), block, 0, s>>>(in, out, R, C, rows_per_group);
+    sum_rows_kernel<<<dim3(col_blocks, 1), kSumThreads, 0, s>>>(in, out, R, C, kSumRowsPerGroup);
     P3D_LAUNCH_CHECK();
     return P3D_OK;
   }
   if (groups > 65535) return fail(P3D_ERR_UNSUPPORTED, "sum_rows: too many rows (%lld)", (long long)R);
-  sum_rows_kernel<<<dim3((unsigned)((C + 127) / 128), (unsigned)groups), block, 0, s>>>(in, tmp, R, C,
-                                                                                       rows_per_group);
+  sum_rows_kernel<<<dim3(col_blocks, (unsigned)groups), kSumThreads, 0, s>>>(in, tmp, R, C, kSumRowsPerGroup);
   P3D_LAUNCH_CHECK();
-  sum_rows_kernel<<<dim3((unsigned)((C + 127) / 128), 1), block, 0, s>>>(tmp, out, groups, C, (int)groups);
+  sum_rows_kernel<<<dim3(col_blocks, 1), kSumThreads, 0, s>>>(tmp, out, groups, C, (int)groups);
   P3D_LAUNCH_CHECK();
   return P3D_OK;
 }

@@ -105,7 +105,8 @@ inline int global_dkv_splits(int tokens) {
 int launch_sum_middle(const float *in, float *out, int64_t outer, int S, int64_t C, cudaStream_t s);
 // out[c] = sum_{r < R} in[r * C + c]; tmp needs ceil(R / 256) * C floats.
 int launch_sum_rows(const float *in, float *out, int64_t R, int64_t C, float *tmp, cudaStream_t s);
-inline int64_t sum_rows_tmp(int64_t R, int64_t C) { return ((R + 255) / 256) * C; }
+constexpr int kSumRowsPerGroup = 128;  // rows per first-pass group of launch_sum_rows
+inline int64_t sum_rows_tmp(int64_t R, int64_t C) { return ((R + kSumRowsPerGroup - 1) / kSumRowsPerGroup) * C; }
 
 // ---- tensor-core (tcgen05) fused forward on complete voxel stencils --------------------
 struct StencilFwdArgs {
