@@ -88,8 +88,10 @@ class PACK3DAttention(nn.Module):
                                                                 self.kv_heads, self.head_dim):
                 q, kl, vl, kg, vg = glue.qkv_project(x, self.to_q.weight, self.to_kv.weight, coords, phases, pairs,
                                                      layout.grid_shape, self.heads, self.kv_heads, self.head_dim)
+                gate_logits = self.gate(x)
             else:
-                q, kl, vl, kg, vg = glue.qkv_split(self.to_q(x), self.to_kv(x), coords, phases, pairs,
+                qp, kvp, gate_logits = glue.projections(x, self.to_q, self.to_kv, self.gate)
+                q, kl, vl, kg, vg = glue.qkv_split(qp, kvp, coords, phases, pairs,
                                                    layout.grid_shape, self.heads, self.kv_heads, self.head_dim)
         else:
             x = self.norm(x)
@@ -98,7 +100,9 @@ class PACK3DAttention(nn.Module):
                               for t in self.to_kv(x).chunk(4, -1))
             check_cuda(q)
             q, kl, kg = rotate_projections(q, kl, kg, layout.coords, pairs, layout.grid_shape, packed=packed)
-        gates = self.gate(x).reshape(b, n, self.heads, 2).softmax(-1)
+        if phases is None:
+            gate_logits = self.gate(x)
+        gates = gate_logits.reshape(b, n, self.heads, 2).softmax(-1)
         gate = gates[..., 1].transpose(1, 2)
         if phases is not None:
             # token-major core output: to_out reads it, and takes the residual, in one GEMM

@@ -193,3 +193,44 @@ def qkv_project(x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, hea
     q / kl / kg rotated, through ``p3d_qkv_project`` (check ``project_supported`` first)."""
     return _QKVProject.apply(x, wq, wkv, coords, phases, tuple(int(p) for p in pairs),
                              tuple(int(e) for e in extents), int(heads), int(kv_heads), int(head_dim))
+
+
+class _Projections(torch.autograd.Function):
+    """``x Wq^T``, ``x Wkv^T`` and ``x Wg^T + bg`` (to_q, to_kv, gate) on one input, whose
+    gradient is accumulated by the GEMMs themselves (dx = dqp Wq, then += dkvp Wkv and
+    += dgl Wg in place) instead of by two elementwise adds of three separate gradients."""
+
+    @staticmethod
+    def forward(ctx, x, wq, wkv, wg, bg):
+        b, n, dim = x.shape
+        x2 = x.reshape(b * n, dim)
+        qp = torch.mm(x2, wq.t()).view(b, n, -1)
+        kvp = torch.mm(x2, wkv.t()).view(b, n, -1)
+        gl = torch.addmm(bg, x2, wg.t()).view(b, n, -1)
+        ctx.save_for_backward(x, wq, wkv, wg)
+        return qp, kvp, gl
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, dqp, dkvp, dgl):
+        x, wq, wkv, wg = ctx.saved_tensors
+        b, n, dim = x.shape
+        x2 = x.reshape(b * n, dim)
+        grads = [(t.reshape(b * n, -1) if t is not None else None, w) for t, w in ((dqp, wq), (dkvp, wkv), (dgl, wg))]
+        dx = None
+        for g, w in grads:
+            if g is None:
+                continue
+            dx = torch.mm(g, w) if dx is None else dx.addmm_(g, w)
+        if dx is None:
+            dx = torch.zeros_like(x2)
+        dw = [torch.mm(g.t(), x2) if g is not None and ctx.needs_input_grad[i + 1] else None
+              for i, (g, _) in enumerate(grads)]
+        dbg = grads[2][0].sum(0) if grads[2][0] is not None and ctx.needs_input_grad[4] else None
+        return dx.view(b, n, dim), dw[0], dw[1], dw[2], dbg
+
+
+def projections(x, to_q, to_kv, gate):
+    """``(to_q(x), to_kv(x), gate(x))`` for bias-free to_q / to_kv and a biased gate, with the
+    input gradient accumulated inside the GEMMs."""
+    return _Projections.apply(x, to_q.weight, to_kv.weight, gate.weight, gate.bias)
