@@ -3,7 +3,7 @@
 Mirrors the reference's ``src/pack3d/_validation.py:4-39`` (same messages, so
 callers catching them keep working) with three deliberate differences:
 
-* head dimension 48 is admitted -- the BASELINE shape (three axes x eight
+* head dimension 48 is admitted -- the benchmark shape (three axes x eight
   rotary pairs); every head dimension the kernels support is listed in
   ``HEAD_DIMS``;
 * the Triton register-tile budget (``_validation.py:22-24``) does not apply:

@@ -200,7 +200,7 @@ int gather_rows(const void *src, void *dst, const int32_t *map, int64_t slabs, i
 // The tensor-core backward needs what the tensor-core forward needs, and at least two
 // summaries (with one the global softmax is constant: no score gradient, reference
 // kernels.py:198-199).
-// The z-slab (multi-GPU) backward is built and tested for radius 2, the BASELINE radius;
+// The z-slab (multi-GPU) backward is built and tested for radius 2, the benchmark configurations' radius;
 // the single-GPU tensor-core kernels take radius 1 or 2.
 bool radius_two(const p3d_operator *op) { return op->radius[0] == 2 && op->radius[1] == 2 && op->radius[2] == 2; }
 

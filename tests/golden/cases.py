@@ -42,7 +42,7 @@ def graph_case(n, d, b, h, g, volume, pool, dtype, seed, empty_block=False):
 def grid_inputs(n, b, h, g, d, dtype, seed, weighted, volume=64):
     """Pre-RoPE projections and operator parameters for a grid case.
 
-    Unweighted cases use the BASELINE settings: mean pooling (weight 0, slot
+    Unweighted cases use the benchmark settings: mean pooling (weight 0, slot
     bias 0), gate 0.5 and the layer's initial branch scales (1 and 0.25).
     """
     gen = torch.Generator().manual_seed(seed)

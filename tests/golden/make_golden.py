@@ -9,7 +9,7 @@ Everything is computed by the reference's own public functions on the CPU:
 ``build_layout`` / ``TokenLayout.repack`` / ``prepare_geometry`` tables,
 ``axial_rope``, ``compress_summaries``, ``pack3d_reference`` (outputs and
 every gradient through autograd) and ``PACK3DAttention`` (backend
-"reference").  Head dimension 48 -- the BASELINE shape -- is refused by the
+"reference").  Head dimension 48 -- the benchmark shape -- is refused by the
 reference's validation (``src/pack3d/_validation.py:17-18``); for those cases
 this script wraps that validation so that only its head-dimension refusal is
 skipped, and the reference arithmetic runs unchanged.
@@ -167,7 +167,7 @@ def main(src):
     for case in cases.CORE_CASES:
         core_case(pack3d, *case)
 
-    # --- BASELINE-shaped grid pipeline (RoPE + pooling + core + every gradient) ------------
+    # --- benchmark-shaped grid pipeline (RoPE + pooling + core + every gradient) ------------
     for case in cases.GRID_CASES:
         grid_case(pack3d, *case)
 
@@ -189,4 +189,6 @@ def main(src):
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src"))
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <reference source tree>/src")
+    main(Path(sys.argv[1]))

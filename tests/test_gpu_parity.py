@@ -1,6 +1,6 @@
 """GPU parity: the CUDA path against the oracle and the reference's golden vectors.
 
-Tolerances are the BASELINE contract: max-abs 1e-5 for fp32, 2e-2 for bf16
+Tolerances: max-abs 1e-5 for fp32, 2e-2 for bf16
 (outputs and gradients), and exact equality for RoPE with a phase table and
 for repeated backward calls (determinism).
 """
@@ -90,7 +90,7 @@ def test_core_graph_cases_match_reference(cuda_device, golden, case):
     assert max_abs(inference, y) <= tol
 
 
-# ---------------------------------------------------------- BASELINE-shaped grid pipeline
+# ---------------------------------------------------------- benchmark-shaped grid pipeline
 
 def _grid_layout(grid):
     layout = build_layout(grid, (4, 4, 4), radius=2, pool_size=1)
