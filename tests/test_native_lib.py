@@ -98,3 +98,37 @@ def test_layer_rejects_unsupported():
 def test_import_does_not_pull_the_oracle():
     code = "import sys, pack3d_b200; assert 'oracle' not in sys.modules; assert 'triton' not in sys.modules"
     subprocess.run([sys.executable, "-c", code], check=True, cwd=str(ROOT))
+
+
+def test_argument_checks_run_before_any_device_call():
+    """Malformed calls of the glue and projection entry points are refused on the host, with
+    a message, before anything touches a device (so they behave the same without a GPU)."""
+    from pack3d_b200 import _native
+    lib = _native.lib()
+    dummy = 16  # a non-null, 16-byte aligned stand-in: never dereferenced on these paths
+    # p3d_qkv_project: null pointer, bad rotation pairs
+    st = lib.p3d_qkv_project(None, dummy, dummy, dummy, dummy, dummy, dummy, dummy, _native.BF16, 1, 4, 4, 64, 192,
+                             48, dummy, 8, 8, 8, dummy, 4, 4, 4, None)
+    assert st == 1 and b"null pointer" in lib.p3d_last_error()
+    st = lib.p3d_qkv_project(dummy, dummy, dummy, dummy, dummy, dummy, dummy, dummy, _native.BF16, 1, 4, 4, 64, 192,
+                             48, dummy, 8, 8, 7, dummy, 4, 4, 4, None)
+    assert st == 1 and b"pairs" in lib.p3d_last_error()
+    # shapes the fused kernel does not run are reported as unsupported, not computed
+    assert lib.p3d_qkv_project_supported(_native.F32, 192, 4, 4, 48) == 0
+    assert lib.p3d_qkv_project_supported(_native.BF16, 96, 4, 4, 48) == 0
+    assert lib.p3d_qkv_project_supported(_native.BF16, 192, 4, 4, 40) == 0
+    # p3d_qkv_split: heads not a multiple of kv_heads
+    st = lib.p3d_qkv_split(dummy, dummy, dummy, dummy, dummy, dummy, dummy, _native.BF16, 1, 5, 3, 64, 48, dummy,
+                           8, 8, 8, dummy, 4, 4, 4, None)
+    assert st == 1 and b"head" in lib.p3d_last_error()
+    # p3d_pool_fwd: more than 64 slots per fine block
+    st = lib.p3d_pool_fwd(dummy, dummy, dummy, dummy, dummy, 4, 65, 1, dummy, dummy, None, None, _native.BF16, 1, 1,
+                          256, 48, 1.0, None)
+    assert st == 1 and b"block table" in lib.p3d_last_error()
+
+
+def test_fused_projection_is_not_offered_for_cpu_tensors():
+    from pack3d_b200 import glue
+    x = torch.zeros(1, 64, 192, dtype=torch.bfloat16)
+    w = torch.zeros(192, 192, dtype=torch.bfloat16)
+    assert not glue.project_supported(x, w, torch.zeros(768, 192, dtype=torch.bfloat16), 4, 4, 48)
