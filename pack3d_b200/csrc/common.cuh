@@ -101,6 +101,23 @@ struct DeviceInfo {
 };
 int device_info(DeviceInfo *info);
 
+// Dynamic shared memory above the 48 KB default needs a per-kernel opt-in, and that setting
+// belongs to the current device's context: a process that launches on several GPUs must set
+// it on each.  `seen` (one per kernel) records the size opted in per device ordinal; the
+// attribute is set again only when a launch needs more than before on that device.
+constexpr int kMaxDevices = 64;
+template <typename K>
+inline int smem_optin(K kernel, size_t bytes, size_t (&seen)[kMaxDevices]) {
+  int dev = 0;
+  P3D_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(P3D_ERR_DEVICE, "device ordinal %d out of range", dev);
+  if (bytes > seen[dev]) {
+    P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    seen[dev] = bytes;
+  }
+  return P3D_OK;
+}
+
 }  // namespace p3d
 
 namespace p3d {

@@ -609,22 +609,12 @@ __global__ void __launch_bounds__(kStageWarps * 32, 7) pool_bwd_staged_kernel(Po
 
 static bool aligned(const void *p, uintptr_t a) { return ((uintptr_t)p & (a - 1)) == 0; }
 
-// Opt a staged kernel in to its dynamic shared memory (the setting only grows).
-template <typename K>
-static int staged_smem(K kernel, size_t bytes, size_t *configured) {
-  if (bytes > *configured) {
-    P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
-    *configured = bytes;
-  }
-  return P3D_OK;
-}
-
 template <typename T, int D>
 static int pool_fwd_staged(const PoolArgs &p, cudaStream_t stream) {
   const unsigned blocks = (unsigned)(((int64_t)p.summaries * p.bg + kStageWarps - 1) / kStageWarps);
-  static size_t configured = 48 * 1024;
+  static size_t seen[kMaxDevices] = {};
   const size_t bytes = Staging<D>::kHead + kStageWarps * Staging<D>::per_warp(p.slots, false);
-  if (int st = staged_smem(pool_fwd_staged_kernel<T, D>, bytes, &configured)) return st;
+  if (int st = smem_optin(pool_fwd_staged_kernel<T, D>, bytes, seen)) return st;
   pool_fwd_staged_kernel<T, D><<<blocks, kStageWarps * 32, bytes, stream>>>(p);
   P3D_LAUNCH_CHECK();
   return P3D_OK;
@@ -633,9 +623,9 @@ static int pool_fwd_staged(const PoolArgs &p, cudaStream_t stream) {
 template <typename T, int D>
 static int pool_bwd_staged(const PoolBwdArgs &p, cudaStream_t stream) {
   const unsigned blocks = (unsigned)(((int64_t)p.summaries * p.bg + kStageWarps - 1) / kStageWarps);
-  static size_t configured = 48 * 1024;
+  static size_t seen[kMaxDevices] = {};
   const size_t bytes = Staging<D>::kHead + kStageWarps * Staging<D>::per_warp(p.slots, true);
-  if (int st = staged_smem(pool_bwd_staged_kernel<T, D>, bytes, &configured)) return st;
+  if (int st = smem_optin(pool_bwd_staged_kernel<T, D>, bytes, seen)) return st;
   pool_bwd_staged_kernel<T, D><<<blocks, kStageWarps * 32, bytes, stream>>>(p);
   P3D_LAUNCH_CHECK();
   return P3D_OK;

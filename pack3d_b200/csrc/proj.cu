@@ -330,11 +330,8 @@ int launch_proj(const ProjArgs &a, cudaStream_t stream) {
   p.table_floats = a.table_floats;
   const size_t smem = proj_smem_bytes(a.dim, gh * D);
   auto kernel = proj_split_kernel<BF16, D>;
-  static size_t configured = 0;
-  if (smem > configured) {
-    P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    configured = smem;
-  }
+  static size_t seen[kMaxDevices] = {};
+  if (int st = smem_optin(kernel, smem, seen)) return st;
   kernel<<<p.groups * p.ctas_per_group, kThreads, smem, stream>>>(tx, twq, twkv, p);
   P3D_LAUNCH_CHECK();
   return P3D_OK;

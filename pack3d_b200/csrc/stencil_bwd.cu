@@ -542,11 +542,8 @@ int launch_dq_t(const StencilBwdArgs &a, cudaStream_t stream) {
   if (units <= 0) return P3D_OK;
   if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");
   auto kernel = stencil_bwd_dq_kernel<D, BF16, R>;
-  static bool configured = false;
-  if (!configured) {
-    P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
-    configured = true;
-  }
+  static size_t seen[kMaxDevices] = {};
+  if (int st = smem_optin(kernel, C::kSmemBytes, seen)) return st;
   kernel<<<(unsigned)units, kDqThreads, C::kSmemBytes, stream>>>(tq, tdol, tdog, tkl, tvl, tsk, tsv, p);
   P3D_LAUNCH_CHECK();
   return P3D_OK;
@@ -944,11 +941,8 @@ int launch_gkv_t(const GlobalDkvArgs &a, cudaStream_t stream) {
   if (units <= 0) return P3D_OK;
   if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");
   auto kernel = global_dkv_tc_kernel<D, BF16>;
-  static bool configured = false;
-  if (!configured) {
-    P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
-    configured = true;
-  }
+  static size_t seen[kMaxDevices] = {};
+  if (int st = smem_optin(kernel, C::kSmemBytes, seen)) return st;
   kernel<<<(unsigned)units, kThreads, C::kSmemBytes, stream>>>(tq, tdo, tsk, tsv, p);
   P3D_LAUNCH_CHECK();
   return P3D_OK;
@@ -1353,11 +1347,8 @@ int launch_lkv_t(const StencilBwdArgs &a, cudaStream_t stream) {
   if (units <= 0) return P3D_OK;
   if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");
   auto kernel = stencil_bwd_dkv_kernel<D, BF16, R>;
-  static bool configured = false;
-  if (!configured) {
-    P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
-    configured = true;
-  }
+  static size_t seen[kMaxDevices] = {};
+  if (int st = smem_optin(kernel, C::kSmemBytes, seen)) return st;
   kernel<<<(unsigned)units, kThreads, C::kSmemBytes, stream>>>(tkl, tvl, tq, tdo, p);
   P3D_LAUNCH_CHECK();
   return P3D_OK;

@@ -651,11 +651,8 @@ int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
   if (units <= 0) return P3D_OK;
   if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");
   auto kernel = stencil_fwd_kernel<D, BF16, R>;
-  static bool configured = false;
-  if (!configured) {
-    P3D_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
-    configured = true;
-  }
+  static size_t seen[kMaxDevices] = {};
+  if (int st = smem_optin(kernel, C::kSmemBytes, seen)) return st;
   kernel<<<(unsigned)units, kThreads, C::kSmemBytes, stream>>>(tq, tkl, tvl, tsk, tsv, p);
   P3D_LAUNCH_CHECK();
   return P3D_OK;
