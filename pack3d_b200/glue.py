@@ -83,22 +83,8 @@ class _QKVSplit(torch.autograd.Function):
     def backward(ctx, dq, dkl, dvl, dkg, dvg):
         coords, phases = ctx.saved_tensors
         pairs, extents, heads, kv_heads, head_dim, b, n, dt = ctx.meta
-        dev = coords.device
-
-        def grad(t, h):
-            if t is None:
-                return torch.zeros((b, h, n, head_dim), dtype=dt, device=dev)
-            return t.to(dt).contiguous()
-
-        dq = grad(dq, heads)
-        dkl, dvl, dkg, dvg = (grad(t, kv_heads) for t in (dkl, dvl, dkg, dvg))
-        dqp = torch.empty((b, n, heads * head_dim), dtype=dt, device=dev)
-        dkvp = torch.empty((b, n, 4 * kv_heads * head_dim), dtype=dt, device=dev)
-        with torch.cuda.device(dev):
-            _native.check(_native.lib().p3d_qkv_merge(
-                _native.ptr(dq), _native.ptr(dkl), _native.ptr(dvl), _native.ptr(dkg), _native.ptr(dvg),
-                _native.ptr(dqp), _native.ptr(dkvp), _native.DTYPE_CODE[dt], b, heads, kv_heads, n, head_dim,
-                _native.ptr(coords), *pairs, _native.ptr(phases), *extents, _native.stream_of(dev)), "p3d_qkv_merge")
+        dqp, dkvp = _merge(dq, dkl, dvl, dkg, dvg, coords, phases, pairs, extents, heads, kv_heads, head_dim, b, n,
+                           dt)
         return dqp, dkvp, None, None, None, None, None, None, None
 
 
