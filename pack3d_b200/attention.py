@@ -25,6 +25,17 @@ class PACK3DAttention(nn.Module):
     Input / output ``[batch, packed_tokens, dim]``; the layout travels with the
     tokens.  Separate local / global K/V projections, one learned fine atom,
     two-stage compression.
+
+    Two attributes choose between equivalent implementations; both paths compute the same
+    layer within the bf16 tolerance:
+
+    * ``fused_glue`` (default True): 16-bit CUDA calls run LayerNorm, the projection split
+      with its RoPE, and their backward halves in the library's kernels, and feed the core's
+      token-major output to ``to_out`` together with the residual in one GEMM.  False keeps
+      the per-op PyTorch path.
+    * ``fused_projection`` (default False): with ``fused_glue``, run the two projections and
+      the split in one tensor-core kernel (``p3d_qkv_project``).  It moves about half the
+      bytes, but it is not faster than cuBLAS plus the split kernel at present.
     """
 
     def __init__(self, dim, *, heads=4, kv_heads=2, head_dim=32, block_volume=8, backend="b200",
