@@ -20,7 +20,6 @@ import argparse
 import json
 import math
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -58,6 +57,9 @@ def parse_args():
                          "8 q-heads / 2 kv-heads x 64, radius 1, (1,4,4) raster blocks, pool 16), layer inference "
                          "and forward + backward, K timed steps each; one JSON line")
     ap.add_argument("--no-allen15", action="store_true", help="skip the allen15 preset in the N = 1 line")
+    ap.add_argument("--no-config2", action="store_true", help="skip the Morton-storage (config 2) sub-object")
+    ap.add_argument("--config4-steps", type=int, default=3,
+                    help="timed steps of the config-4 sub-object (128^3 fwd + bwd at this N; 0 skips it)")
     ap.add_argument("--infer-only", type=int, default=0, metavar="N",
                     help="profiling mode: run the config-1 layer inference forward N times (eager) and exit")
     ap.add_argument("--train-only", type=int, default=0, metavar="N",
@@ -207,13 +209,11 @@ def pipelined_e2e(call, x_host, out_shape, device, stream, steps, warmup):
     return run(steps)
 
 
-def ncu_traffic_per_launch():
-    """DRAM bytes (read + write) per launch of the stencil kernel from the committed ncu summary."""
-    path = ROOT / "profiles" / "stencil_fwd_config1.md"
-    if not path.exists():
-        return None
-    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", path.read_text())
-    return float(m.group(1)) if m else None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one stencil_fwd_kernel launch at
+# config 1, from the ncu capture summarised in profiles/stencil_fwd_config1.md (the command is
+# there); refreshed together with that summary whenever the kernel changes.
+STENCIL_FWD_DRAM_BYTES = 393.5e6
+STENCIL_FWD_DRAM_SOURCE = "ncu capture of stencil_fwd_kernel at config 1 (profiles/stencil_fwd_config1.md)"
 
 
 def measured_peaks():
@@ -226,47 +226,59 @@ def measured_peaks():
 
 # ------------------------------------------------------------------------- CPU baseline
 
-def cpu_layer_seconds(sample_rows=65536, seed=0):
-    """Seconds for one config-1 layer forward with the CPU restatement of the reference, all host cores.
+def cpu_model():
+    """The host CPU's model name (from /proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
-    Projections, RoPE and pooling run for every token; the attention core and the
-    output projection run for `sample_rows` evenly spaced query rows (rows are
-    independent given the summaries) and are scaled to all rows.
+
+def cpu_reference_step(seed=1000):
+    """One config-1 layer forward on the host cores with the CPU restatement of the reference
+    (``oracle``: the reference's layer, RoPE, pooling and core arithmetic in fp32, its grid
+    tables and its seeded layer initialisation), over all 262,144 tokens.
+
+    Returns ``(step, threads)``; ``step()`` runs the whole forward once.  Nothing here loads
+    the B200 library: the tables, the weights and the arithmetic all come from the oracle.
     """
-    import torch.nn.functional as F
     import oracle
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    layout = make_layout(CONFIG["grid"])
-    geom = layout.geometry
-    n = geom.num_tokens
-    h, g, d, dim = CONFIG["heads"], CONFIG["kv_heads"], CONFIG["head_dim"], CONFIG["dim"]
-    layer = make_layer(torch.float32, "cpu")
-    params = {k: v.detach() for k, v in layer.state_dict().items()}
-    x = torch.randn(CONFIG["batch"], n, dim, generator=torch.Generator().manual_seed(seed))
-    b = x.shape[0]
-    rows = torch.arange(0, n, max(1, n // sample_rows))
-    with torch.no_grad():
-        t0 = time.perf_counter()
-        xn = F.layer_norm(x, (dim,), params["norm.weight"], params["norm.bias"])
-        q = F.linear(xn, params["to_q.weight"]).reshape(b, n, h, d).transpose(1, 2)
-        kl, vl, kg, vg = (t.reshape(b, n, g, d).transpose(1, 2) for t in F.linear(xn, params["to_kv.weight"]).chunk(4, -1))
-        gate = F.linear(xn, params["gate.weight"], params["gate.bias"]).reshape(b, n, h, 2).softmax(-1)[..., 1]
-        gate = gate.transpose(1, 2)
-        q, kl, kg = (oracle.axial_rope(t, layout.coords) for t in (q, kl, kg))
-        t1 = time.perf_counter()
-        oracle.compress_summaries(kg, vg, params["pool_weight"], params["slot_bias"], geom.blocks, 1)
-        t2 = time.perf_counter()
-        state = oracle.core_forward(q, kl, vl, kg, vg, params["pool_weight"], params["slot_bias"], gate,
-                                    params["local_scale"], params["global_scale"], geom.neighbors, geom.blocks, 1,
-                                    rows=rows, chunk=1024)
-        out = state["y"].transpose(1, 2).reshape(b, len(rows), -1)
-        _ = x[:, rows] + F.linear(out, params["to_out.weight"])
-        t3 = time.perf_counter()
-    full = (t1 - t0) + (t2 - t1) + ((t3 - t2) - (t2 - t1)) * n / len(rows)
-    sample = (f"LayerNorm, projections, RoPE and pooling for all {n} tokens; attention core and output "
-              f"projection for {len(rows)} evenly spaced query rows, scaled to {n} rows")
-    return full, t3 - t0, threads, sample
+    tables = oracle.grid_layout(CONFIG["grid"], CONFIG["block"], CONFIG["radius"], "raster")
+    torch.manual_seed(0)
+    params = oracle.init_layer(CONFIG["dim"], heads=CONFIG["heads"], kv_heads=CONFIG["kv_heads"],
+                               head_dim=CONFIG["head_dim"], block_volume=math.prod(CONFIG["block"]))
+    n = math.prod(CONFIG["grid"])
+    x = torch.randn(CONFIG["batch"], n, CONFIG["dim"], generator=torch.Generator().manual_seed(seed))
+    rows = torch.arange(n)
+
+    def step():
+        with torch.no_grad():
+            return oracle.layer_forward(x, params, tables["coords"], tables["neighbors"], tables["blocks"],
+                                        CONFIG["pool_size"], heads=CONFIG["heads"], kv_heads=CONFIG["kv_heads"],
+                                        head_dim=CONFIG["head_dim"], rows=rows, chunk=4096)
+    return step, threads
+
+
+CPU_SAMPLE = ("the whole config-1 layer forward (LayerNorm, projections, RoPE, pooling, local + global "
+              "attention over all 262,144 query rows, output projection, residual), fp32, no extrapolation")
+
+
+def config1_desc(parallelism):
+    """The workload description both arms print as ``config``."""
+    return {"workload": "BASELINE config 1: 64^3 raster field, batch 1, dim 192 = 4 heads x 48, radius-2 "
+                        "5x5x5 neighbourhood, 4x4x4 mean-pool summaries (4096), layer forward",
+            "grid": list(CONFIG["grid"]), "batch": CONFIG["batch"], "heads": CONFIG["heads"],
+            "kv_heads": CONFIG["kv_heads"], "head_dim": CONFIG["head_dim"], "dim": CONFIG["dim"],
+            "summaries": math.prod(CONFIG["grid"]) // math.prod(CONFIG["block"]), "radius": CONFIG["radius"],
+            "parallelism": parallelism,
+            "l2": "GPU arm: a 256 MiB write flushes L2 between timed steps (outside the timed events); "
+                  "CPU arm: the per-step working set (several GB) exceeds every cache"}
 
 
 # ------------------------------------------------------------------------------- GPU arm
@@ -395,7 +407,7 @@ def train_only(args, device):
 CONFIG4 = dict(grid=(128, 128, 128), batch=1, heads=8, kv_heads=8, head_dim=48, dim=384, block=(4, 4, 4), radius=2)
 
 
-def config4_fwd_bwd(args, rank, world, device):
+def config4_fwd_bwd(steps, rank, world, device):
     """the layer forward + backward on a 128^3 field (2,097,152 tokens),
     dim 384 = 8 heads x 48, bf16.  N = 1: the whole field on one GPU; N > 1: z-slabs, the
     sharded core (halo exchange, summary all-gather, summary-gradient reduce-scatter) and an
@@ -435,7 +447,7 @@ def config4_fwd_bwd(args, rank, world, device):
     torch.cuda.synchronize(device)
     if world > 1:
         torch.distributed.barrier()
-    times = timed_steps(step, args.config4, torch.cuda.current_stream(device))
+    times = timed_steps(step, steps, torch.cuda.current_stream(device))
     ms = sum(times) / len(times)
     if world > 1:
         t = torch.tensor([ms], device=device)
@@ -446,7 +458,7 @@ def config4_fwd_bwd(args, rank, world, device):
         raise RuntimeError(f"device error flags set: {errors}")
     total = math.prod(grid) * CONFIG4["batch"]
     return {"mode": "config4", "metric": "PACK3D layer bf16 fwd+bwd tokens/s, BASELINE config 4", "n_gpus": world,
-            "steps": args.config4, "ms_per_step": round(ms, 3), "tokens_per_s": round(total / (ms * 1e-3), 1),
+            "steps": steps, "ms_per_step": round(ms, 3), "tokens_per_s": round(total / (ms * 1e-3), 1),
             "scaling": "strong",
             "config": {"workload": "BASELINE config 4: 128^3 field (2,097,152 tokens, raster storage), batch 1, "
                                    "dim 384 = 8 heads x 48, radius 2, 32,768 summaries; layer forward + backward "
@@ -454,6 +466,48 @@ def config4_fwd_bwd(args, rank, world, device):
                                                                              "gradients all-reduced"),
                        "grid": list(grid), "dim": CONFIG4["dim"], "heads": CONFIG4["heads"],
                        "head_dim": CONFIG4["head_dim"]}}
+
+
+def config2_measure(steps, device):
+    """the config-1 field stored in Morton (Z-order) storage -- the
+    reference's native block-Morton layout, tokens, coordinates and tables permuted together
+    -- layer inference in bf16 and f16 (CUDA graph, L2 flushed between steps), next to the
+    same call on raster storage.  Its outputs equal the permuted raster outputs bit for bit
+    (tests/test_gpu_baseline_parity.py)."""
+    from pack3d_b200 import build_layout
+    layout = build_layout(CONFIG["grid"], CONFIG["block"], radius=CONFIG["radius"],
+                          pool_size=CONFIG["pool_size"]).to(device)
+    raster = make_layout(CONFIG["grid"]).to(device)
+    stream = torch.cuda.current_stream(device)
+    flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    out = {"workload": "BASELINE config 2: the 64^3 config-1 field in Morton storage (native block-Morton "
+                       "layout), layer forward, batch 1", "steps": steps}
+    for dtype, tag in ((torch.bfloat16, "bf16"), (torch.float16, "f16")):
+        layer = make_layer(dtype, device)
+        gen = torch.Generator(device=device).manual_seed(1000)
+        x = torch.randn(CONFIG["batch"], layout.geometry.num_tokens, CONFIG["dim"], device=device,
+                        generator=gen).to(dtype)
+        for name, lay in (("morton", layout), ("raster", raster)):
+            with torch.inference_mode():
+                for _ in range(3):
+                    layer(x, lay)
+                side = torch.cuda.Stream(device)
+                side.wait_stream(stream)
+                with torch.cuda.stream(side):
+                    layer(x, lay)
+                stream.wait_stream(side)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    layer(x, lay)
+            for _ in range(3):
+                graph.replay()
+            times = timed_steps(graph.replay, steps, stream, flush_buf.zero_)
+            ms = sum(times) / len(times)
+            out[f"{tag}_{name}_ms"] = round(ms, 4)
+            if name == "morton":
+                out[f"{tag}_tokens_per_s"] = round(layout.geometry.num_tokens / (ms * 1e-3), 1)
+            del graph
+    return out
 
 
 def run_sharded(args, rank, world, device):
@@ -726,7 +780,7 @@ def run_b200(args, rank, world, device):
     if errors:
         raise RuntimeError(f"device error flags set: {errors}")
     tokens = world * b * n
-    launches_per_step = 3 + 1 + 1      # RoPE q/kl/kg, pooling, fused stencil attention
+    launches_per_step = 4      # library kernels per layer forward: LayerNorm, qkv split + RoPE, pooling, stencil
     line = {
         "metric": METRIC,
         "value": round(tokens / (ms * 1e-3), 1),
@@ -740,15 +794,12 @@ def run_b200(args, rank, world, device):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: x ~ N(0,1) (seeded), random-init PACK3DAttention weights (seed 0)",
-        "config": {"workload": "BASELINE config 1: 64^3 raster field, batch 1, dim 192 = 4 heads x 48, radius-2 "
-                               "5x5x5 neighbourhood, 4x4x4 mean-pool summaries (4096), layer forward",
-                   "grid": list(CONFIG["grid"]), "batch": b, "heads": hq, "kv_heads": g, "head_dim": hd,
-                   "dim": CONFIG["dim"], "summaries": m, "radius": CONFIG["radius"],
-                   "parallelism": "single GPU" if world == 1 else f"{world} independent replicas (one field per GPU)",
-                   "cuda_graph": use_graph,
-                   "l2": "flushed between timed steps (256 MiB write outside the timed events)"},
+        "config": config1_desc("none (one device)" if world == 1 else
+                               f"{world} independent replicas (one field per GPU)"),
+        "cuda_graph": use_graph,
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(achieved / peak, 4), "traffic": ncu_traffic_per_launch(),
+                     "frac": round(achieved / peak, 4), "traffic": STENCIL_FWD_DRAM_BYTES,
+                     "traffic_source": STENCIL_FWD_DRAM_SOURCE,
                      "kernel": "stencil_fwd_kernel (stage c: fused local + global attention)",
                      "kernel_ms": round(kernel_ms, 4), "flop_per_launch": flops, "mean_valid_neighbors": w_bar,
                      "peak_kind": peak_kind, "peak_sustained": peak_sustained},
@@ -773,28 +824,31 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
+        # The reference's CPU path (its CPU restatement in oracle/) on the host cores; rank 0
+        # alone under torchrun.  No B200 code is imported on this arm.
         if rank != 0:
             return
-        cpu_s, wall, threads, sample = None, None, None, None
-        for _ in range(max(0, min(args.warmup, 1))):
-            cpu_layer_seconds(sample_rows=2048)
-        samples = []
-        for _ in range(max(1, min(args.steps, 3))):
-            cpu_s, wall, threads, sample = cpu_layer_seconds()
-            samples.append(cpu_s)
-        s = statistics.median(samples)
+        step, threads = cpu_reference_step()
+        for _ in range(args.warmup):
+            step()
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            step()
+            times.append(time.perf_counter() - t0)
+        s = sum(times) / len(times)
         n = math.prod(CONFIG["grid"]) * CONFIG["batch"]
         value = round(n / s, 1)
         print(json.dumps({
             "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": len(samples), "warmup": min(args.warmup, 1), "ms_per_step": round(s * 1e3, 2),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(s * 1e3, 2),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic: x ~ N(0,1) (seeded), random-init PACK3DAttention weights (seed 0)",
-            "config": {"workload": "BASELINE config 1 (64^3, batch 1, 4 heads x 48, radius 2, 4096 summaries), "
-                                   "layer forward"},
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                             "sample": sample + "; CPU restatement of the reference (it refuses head_dim 48)"},
+            "data": "synthetic: x ~ N(0,1) (seeded), the reference layer's seeded initialisation (seed 0)",
+            "config": config1_desc("none (one device)"),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "cpu": cpu_model(),
+                             "kind": "port", "sample": CPU_SAMPLE + "; every step is the whole workload"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "step_s": [round(t, 3) for t in times],
         }), flush=True)
         return
     if not torch.cuda.is_available():
@@ -806,7 +860,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)
     if args.config4:
-        line = config4_fwd_bwd(args, rank, world, device)
+        line = config4_fwd_bwd(args.config4, rank, world, device)
         if rank == 0:
             print(json.dumps(line), flush=True)
         if world > 1:
@@ -817,11 +871,21 @@ def main():
         return
     if world == 1 and not args.no_allen15 and not args.kernel_only:
         line["allen15"] = allen15_measure(5, 2, device)
+    if world == 1 and not args.kernel_only and not args.no_config2:
+        line["config2"] = config2_measure(10, device)
+    if not args.kernel_only and args.config4_steps > 0:
+        # the multi-GPU target (128^3, 8 heads, fwd + bwd) at this N: whole field at N = 1,
+        # z-slabs for N > 1 -- the driver's 1..8 GPU runs give its scaling curve
+        line["config4"] = config4_fwd_bwd(args.config4_steps, rank, world, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu_s, wall, threads, sample = cpu_layer_seconds()
+        step, threads = cpu_reference_step()
+        t0 = time.perf_counter()
+        step()
+        cpu_s = time.perf_counter() - t0
         n = math.prod(CONFIG["grid"]) * CONFIG["batch"]
-        line["cpu_baseline"] = {"value": round(n / cpu_s, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
-                                "sample": sample, "measured_wall_s": round(wall, 2)}
+        line["cpu_baseline"] = {"value": round(n / cpu_s, 1), "unit": "tokens/s", "cores": threads,
+                                "cpu": cpu_model(), "kind": "port", "sample": CPU_SAMPLE + ", timed once",
+                                "measured_wall_s": round(cpu_s, 2)}
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

@@ -6,7 +6,8 @@ reference's readable implementation of the hot path (``pack3d`` 0.1.0):
 * axial RoPE .............. ``src/pack3d/rope.py:7-48``
 * summary pooling ......... ``src/pack3d/compression.py:7-44``
 * local + global core ..... ``src/pack3d/reference.py:8-31``
-* layer glue .............. ``src/pack3d/attention.py:53-89``
+* layer glue .............. ``src/pack3d/attention.py:24-89``
+* grid tables ............. ``src/pack3d/geometry.py:118-126,190-266``
 
 It is pinned against golden vectors produced by the reference itself
 (``tests/golden/make_golden.py``).  Only ``tests/``, ``__graft_entry__.smoke``
@@ -19,7 +20,11 @@ from .pack3d_oracle import (  # noqa: F401
     balanced_pairs,
     compress_summaries,
     core_backward,
+    core_backward_rows,
     core_forward,
+    grid_layout,
+    init_layer,
     layer_forward,
+    morton_codes,
     pack3d_core,
 )

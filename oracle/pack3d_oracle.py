@@ -27,6 +27,72 @@ def _work_dtype(dtype):
     return torch.float64 if dtype == torch.float64 else torch.float32
 
 
+# --------------------------------------------------------------------- geometry
+
+def morton_codes(coords):
+    """Morton code of int64 ``[N, 3]`` coordinates -- ``src/pack3d/geometry.py:118-126``.
+
+    Bit ``b`` of axis ``a`` lands at bit ``3 b + a``: axis 0 (z) takes the lowest bit of
+    every triple.  The number of bit planes is that of the largest coordinate.
+    """
+    bits = int(coords.max()).bit_length()
+    code = torch.zeros(len(coords), dtype=torch.int64)
+    for bit in range(bits):
+        for axis in range(3):
+            code |= ((coords[:, axis] >> bit) & 1) << (3 * bit + axis)
+    return code
+
+
+def grid_layout(grid, block=(4, 4, 4), radius=2, storage="raster"):
+    """Tables of a complete grid with cubic fine blocks, as the reference builds them.
+
+    Restates ``build_layout(grid, block, radius=radius, layout="native_block_morton")``
+    (``src/pack3d/geometry.py:224-266``): tokens sorted by the Morton code of their block
+    and then of their slot inside the block; one neighbour column per offset of the
+    ``(2r+1)^3`` cube in ``itertools.product`` order (z offset slowest), -1 where the
+    neighbour leaves the grid; fine block ``f`` = packed rows ``[f V, (f+1) V)``.
+    ``storage="raster"`` applies ``TokenLayout.repack(order.argsort())``
+    (``geometry.py:190-220``): rows in raster order, block rows and slot columns kept,
+    every index mapped to its raster row.  ``storage="morton"`` keeps the native order.
+
+    Returns ``{"order", "coords", "neighbors", "blocks"}`` (int64, int64, int32, int32).
+    """
+    shape = tuple(int(v) for v in grid)
+    block = tuple(int(v) for v in block)
+    rad = (radius,) * 3 if isinstance(radius, int) else tuple(radius)
+    if any(g % b for g, b in zip(shape, block)):
+        raise ValueError("grid must be divisible by block")
+    n = shape[0] * shape[1] * shape[2]
+    raster = torch.stack(torch.meshgrid(*(torch.arange(s) for s in shape), indexing="ij"), -1).reshape(-1, 3)
+    bt = torch.tensor(block)
+    slot_code = morton_codes(raster % bt)
+    order = (morton_codes(raster // bt) * (int(slot_code.max()) + 1) + slot_code).argsort()
+    if storage == "raster":
+        row_of = torch.arange(n)                       # raster index -> stored row
+        coords = raster
+        blocks = order.reshape(-1, block[0] * block[1] * block[2])
+        stored_order = torch.arange(n)
+    elif storage == "morton":
+        row_of = order.argsort()
+        coords = raster[order]
+        blocks = torch.arange(n).reshape(-1, block[0] * block[1] * block[2])
+        stored_order = order
+    else:
+        raise ValueError("storage must be raster or morton")
+    extent = torch.tensor(shape)
+    strides = torch.tensor([shape[1] * shape[2], shape[2], 1])
+    columns = []
+    for dz in range(-rad[0], rad[0] + 1):
+        for dy in range(-rad[1], rad[1] + 1):
+            for dx in range(-rad[2], rad[2] + 1):
+                target = coords + torch.tensor((dz, dy, dx))
+                valid = ((target >= 0) & (target < extent)).all(-1)
+                index = (target * strides).sum(-1).clamp(0, n - 1)
+                columns.append(torch.where(valid, row_of[index], -1))
+    return {"order": stored_order, "coords": coords, "neighbors": torch.stack(columns, 1).to(torch.int32),
+            "blocks": blocks.to(torch.int32)}
+
+
 # --------------------------------------------------------------------------- RoPE
 
 def balanced_pairs(head_dim):
@@ -171,23 +237,24 @@ def core_forward(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, neighbors, block
     rows = torch.arange(n) if rows is None else rows.long()
     ys, ols, ogs, lls, lgs = [], [], [], [], []
     head_of = torch.arange(h) // rep
+    klw, vlw = kl[:, head_of].to(work), vl[:, head_of].to(work)   # GQA: KV head of every query head
     for start, stop in _chunk_rows(len(rows), chunk):
         r = rows[start:stop]
         qc = q[:, :, r].to(work)
-        logits = (qc @ skr.transpose(-1, -2)) / root
+        logits = (qc @ skr.transpose(-1, -2)).div_(root)
         lg = torch.logsumexp(logits, -1)
-        og = (logits - lg[..., None]).exp() @ svr
+        og = logits.sub_(lg[..., None]).exp_() @ svr
         ni = neighbors[r].long()
         ok = ni >= 0
         idx = ni.clamp_min(0)
-        lk = kl[:, head_of][:, :, idx].to(work)
-        lv = vl[:, head_of][:, :, idx].to(work)
-        scores = (qc[..., None, :] * lk).sum(-1) / root
+        lk = klw[:, :, idx]                                          # [B, H, rows, W, D]
+        lv = vlw[:, :, idx]
+        scores = (lk @ qc[..., None]).squeeze(-1) / root
         scores = scores.masked_fill(~ok, -torch.inf)
         any_ok = ok.any(-1)[None, None, :]
         ll = torch.where(any_ok, torch.logsumexp(scores, -1), torch.full_like(scores[..., 0], -torch.inf))
         p = torch.where(any_ok[..., None], (scores - ll[..., None]).exp(), torch.zeros_like(scores))
-        ol = (p[..., None] * lv).sum(-2)
+        ol = (p[..., None, :] @ lv).squeeze(-2)
         ys.append(slw * ol + gate[:, :, r].to(work)[..., None] * sgw * og)
         ols.append(ol)
         ogs.append(og)
@@ -287,6 +354,53 @@ def core_backward(dy, q, kl, vl, kg, vg, weight, bias, gate, sl, sg, neighbors, 
             dsl.to(sl.dtype), dsg.to(sg.dtype))
 
 
+@torch.no_grad()
+def core_backward_rows(dy, q, kl, vl, kg, vg, weight, bias, gate, sl, sg, neighbors, blocks, pool_size, rows,
+                       temperature=1.0, chunk=2048):
+    """``dq`` and ``dgate`` of :func:`core_backward` for the query rows ``rows`` only.
+
+    A query row's ``dq`` and ``dgate`` depend only on that row's scores, its upstream
+    gradient and the (fixed) summaries, so the sampled rows are exact.  Same arithmetic as
+    :func:`core_backward` (``reference.py:17-31`` under autograd).  Returns
+    ``(dq [B, H, R, D], dgate [B, H, R])`` in the working precision.
+    """
+    b, h, n, d = q.shape
+    g = kl.shape[1]
+    rep = h // g
+    work = _work_dtype(q.dtype)
+    root = math.sqrt(d)
+    sk, sv = compress_summaries(kg.to(work), vg.to(work), weight, bias, blocks, pool_size, temperature)
+    skr, svr = sk.repeat_interleave(rep, 1), sv.repeat_interleave(rep, 1)
+    klr = kl.to(work).repeat_interleave(rep, 1)
+    vlr = vl.to(work).repeat_interleave(rep, 1)
+    slw, sgw = sl.to(work), sg.to(work)
+    rows = rows.long()
+    dqs, dgates = [], []
+    for start, stop in _chunk_rows(len(rows), chunk):
+        r = rows[start:stop]
+        qc, dyc = q[:, :, r].to(work), dy[:, :, r].to(work)
+        gc = gate[:, :, r].to(work)[..., None]
+        pg = ((qc @ skr.transpose(-1, -2)) / root).softmax(-1)
+        og = pg @ svr
+        idx_raw = neighbors[r].long()
+        ok = idx_raw >= 0
+        idx = idx_raw.clamp_min(0)
+        lk, lv = klr[:, :, idx], vlr[:, :, idx]
+        scores = (lk @ qc[..., None]).squeeze(-1) / root
+        scores = scores.masked_fill(~ok, -torch.inf)
+        scores = torch.where(ok.any(-1)[None, None, :, None], scores, torch.zeros_like(scores))
+        pl = scores.softmax(-1)
+        dol, dog = dyc * slw, dyc * gc * sgw
+        dpg = dog @ svr.transpose(-1, -2)
+        dq = (pg * (dpg - (pg * dpg).sum(-1, keepdim=True)) / root) @ skr
+        dpl = (lv @ dol[..., None]).squeeze(-1) * ok
+        dsl_scores = pl * (dpl - (pl * dpl).sum(-1, keepdim=True)) / root
+        dq += (dsl_scores[..., None, :] @ lk).squeeze(-2)
+        dqs.append(dq)
+        dgates.append((dyc * sgw * og).sum(-1))
+    return torch.cat(dqs, 2), torch.cat(dgates, 2)
+
+
 # ------------------------------------------------------------------------- layer
 
 LAYER_PARAMETERS = ("norm.weight", "norm.bias", "to_q.weight", "to_kv.weight", "pool_weight",
@@ -294,17 +408,64 @@ LAYER_PARAMETERS = ("norm.weight", "norm.bias", "to_q.weight", "to_kv.weight", "
                     "to_out.weight")
 
 
+def init_layer(dim, *, heads=4, kv_heads=2, head_dim=32, block_volume=8):
+    """Freshly initialised parameters of the reference layer, by state-dict name.
+
+    Restates the constructor ``src/pack3d/attention.py:24-51``: the same modules and
+    initialisers created in the same order, so that after the same ``torch.manual_seed``
+    the tensors are identical to the reference layer's (``LayerNorm``; ``to_q`` and
+    ``to_kv`` without bias; ``pool_weight`` uniform in +-1/sqrt(head_dim); ``slot_bias``
+    N(0, 0.02^2); the gate ``Linear`` with its bias zeroed; branch scales 1 and 0.25;
+    ``to_out`` without bias).  Consumes the global RNG exactly as the constructor does.
+    """
+    norm = torch.nn.LayerNorm(dim)
+    to_q = torch.nn.Linear(dim, heads * head_dim, bias=False)
+    to_kv = torch.nn.Linear(dim, 4 * kv_heads * head_dim, bias=False)
+    pool_weight = torch.empty(head_dim)
+    torch.nn.init.uniform_(pool_weight, -1 / math.sqrt(head_dim), 1 / math.sqrt(head_dim))
+    slot_bias = torch.empty(block_volume)
+    torch.nn.init.normal_(slot_bias, std=0.02)
+    gate = torch.nn.Linear(dim, heads * 2)
+    torch.nn.init.zeros_(gate.bias)
+    to_out = torch.nn.Linear(heads * head_dim, dim, bias=False)
+    return {"norm.weight": norm.weight.detach(), "norm.bias": norm.bias.detach(),
+            "to_q.weight": to_q.weight.detach(), "to_kv.weight": to_kv.weight.detach(),
+            "pool_weight": pool_weight, "slot_bias": slot_bias, "gate.weight": gate.weight.detach(),
+            "gate.bias": gate.bias.detach(), "local_scale": torch.ones(head_dim),
+            "global_scale": torch.full((head_dim,), 0.25), "to_out.weight": to_out.weight.detach()}
+
+
 def layer_forward(x, params, coords, neighbors, blocks, pool_size, *, heads, kv_heads, head_dim,
-                  temperature=1.0, position_encoding="axial", chunk=None):
+                  temperature=1.0, position_encoding="axial", chunk=None, rows=None, exact_output=False):
     """Whole PACK3D attention layer -- ``src/pack3d/attention.py:53-89``.
 
     LayerNorm, Q and 4-way KV projections, axial (or packed-sequence) RoPE of
     q / local k / global k, the 2-way gate softmax, the core, the output
     projection and the outer residual.  ``params`` maps the reference layer's
     state-dict names (``LAYER_PARAMETERS``) to tensors.
+
+    ``rows`` (1-D token indices) evaluates the core and the output only for those query
+    rows: the projections, RoPE and pooling still cover every token, and each output row
+    depends only on them, so the sampled rows are exact.  That form runs without autograd.
+    ``exact_output`` forms the output projection and the residual in the working precision
+    and returns it unrounded (a checker for a fused GEMM that rounds once).
     """
+    if rows is not None or exact_output:
+        return _layer_rows(x, params, coords, neighbors, blocks, pool_size, heads=heads, kv_heads=kv_heads,
+                           head_dim=head_dim, temperature=temperature, position_encoding=position_encoding,
+                           chunk=chunk, rows=rows, exact_output=exact_output)
     b, n, dim = x.shape
-    residual = x
+    q, kl, vl, kg, vg, gate = _layer_projections(x, params, coords, heads=heads, kv_heads=kv_heads,
+                                                 head_dim=head_dim, position_encoding=position_encoding)
+    out = pack3d_core(q, kl, vl, kg, vg, params["pool_weight"], params["slot_bias"], gate,
+                      params["local_scale"], params["global_scale"], neighbors, blocks, pool_size,
+                      temperature, chunk=chunk)
+    return x + F.linear(out.transpose(1, 2).reshape(b, n, -1), params["to_out.weight"])
+
+
+def _layer_projections(x, params, coords, *, heads, kv_heads, head_dim, position_encoding):
+    """LayerNorm, projections, RoPE and gate of ``attention.py:56-72`` for every token."""
+    b, n, dim = x.shape
     xn = F.layer_norm(x, (dim,), params["norm.weight"], params["norm.bias"])
     q = F.linear(xn, params["to_q.weight"]).reshape(b, n, heads, head_dim).transpose(1, 2)
     kl, vl, kg, vg = (t.reshape(b, n, kv_heads, head_dim).transpose(1, 2)
@@ -319,8 +480,21 @@ def layer_forward(x, params, coords, neighbors, blocks, pool_size, *, heads, kv_
         raise ValueError("position_encoding must be axial or packed")
     q, kl, kg = (axial_rope(t, coords, pairs) for t in (q, kl, kg))
     gates = F.linear(xn, params["gate.weight"], params["gate.bias"]).reshape(b, n, heads, 2).softmax(-1)
-    gate = gates[..., 1].transpose(1, 2)
-    out = pack3d_core(q, kl, vl, kg, vg, params["pool_weight"], params["slot_bias"], gate,
-                      params["local_scale"], params["global_scale"], neighbors, blocks, pool_size,
-                      temperature, chunk=chunk)
-    return residual + F.linear(out.transpose(1, 2).reshape(b, n, -1), params["to_out.weight"])
+    return q, kl, vl, kg, vg, gates[..., 1].transpose(1, 2)
+
+
+@torch.no_grad()
+def _layer_rows(x, params, coords, neighbors, blocks, pool_size, *, heads, kv_heads, head_dim, temperature,
+                position_encoding, chunk, rows, exact_output):
+    b, n, dim = x.shape
+    q, kl, vl, kg, vg, gate = _layer_projections(x, params, coords, heads=heads, kv_heads=kv_heads,
+                                                 head_dim=head_dim, position_encoding=position_encoding)
+    rows = torch.arange(n) if rows is None else rows.long()
+    state = core_forward(q, kl, vl, kg, vg, params["pool_weight"], params["slot_bias"], gate,
+                         params["local_scale"], params["global_scale"], neighbors, blocks, pool_size, temperature,
+                         chunk=chunk or 2048, rows=rows)
+    out = state["y"].transpose(1, 2).reshape(b, len(rows), -1)
+    if exact_output:
+        work = _work_dtype(x.dtype)
+        return x[:, rows].to(work) + F.linear(out.to(work), params["to_out.weight"].to(work))
+    return x[:, rows] + F.linear(out, params["to_out.weight"])

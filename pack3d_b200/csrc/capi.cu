@@ -48,23 +48,6 @@ int device_info(DeviceInfo *info) {
   return P3D_OK;
 }
 
-namespace {
-
-// Bump allocator over a caller-provided workspace (256-byte aligned slices).
-struct Carver {
-  char *base;
-  size_t used = 0, cap;
-  Carver(void *b, size_t c) : base(static_cast<char *>(b)), cap(c) {}
-  template <typename T>
-  T *take(size_t count) {
-    used = (used + 255) & ~size_t(255);
-    T *p = base ? reinterpret_cast<T *>(base + used) : nullptr;
-    used += count * sizeof(T);
-    return p;
-  }
-  bool ok() const { return base != nullptr && used <= cap; }
-};
-
 int summaries_of(const p3d_operator *op) { return (op->fine_blocks + op->pool_size - 1) / op->pool_size; }
 
 int validate(const p3d_operator *op) {
@@ -145,6 +128,23 @@ PoolArgs pool_args(const p3d_operator *op, void *sk, void *sv) {
   return p;
 }
 
+namespace {
+
+// Bump allocator over a caller-provided workspace (256-byte aligned slices).
+struct Carver {
+  char *base;
+  size_t used = 0, cap;
+  Carver(void *b, size_t c) : base(static_cast<char *>(b)), cap(c) {}
+  template <typename T>
+  T *take(size_t count) {
+    used = (used + 255) & ~size_t(255);
+    T *p = base ? reinterpret_cast<T *>(base + used) : nullptr;
+    used += count * sizeof(T);
+    return p;
+  }
+  bool ok() const { return base != nullptr && used <= cap; }
+};
+
 bool use_stencil_path(const p3d_operator *op, unsigned flags) {
   if (flags & P3D_FWD_FORCE_INDEXED) return false;
   if (!op->stencil || (op->options & P3D_OPT_INDEXED_ONLY)) return false;
@@ -184,6 +184,23 @@ __global__ void gather_rows_kernel(const uint4 *src, uint4 *dst, const int32_t *
   dst[(slab * tokens + r) * row_vecs + v] = src[(slab * tokens + map[r]) * row_vecs + v];
 }
 
+// dst[slab, r] = src[slab, map[r]]: per-row fp32 values (logsumexp, Delta) into raster order.
+__global__ void gather_vals_kernel(const float *src, float *dst, const int32_t *map, int64_t slabs, int tokens) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= slabs * tokens) return;
+  const int r = (int)(t % tokens);
+  const int64_t slab = t / tokens;
+  dst[t] = src[slab * tokens + map[r]];
+}
+
+int gather_vals(const float *src, float *dst, const int32_t *map, int64_t slabs, int tokens, cudaStream_t s) {
+  const int64_t total = slabs * tokens;
+  if (!total) return P3D_OK;
+  gather_vals_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(src, dst, map, slabs, tokens);
+  P3D_LAUNCH_CHECK();
+  return P3D_OK;
+}
+
 int gather_rows(const void *src, void *dst, const int32_t *map, int64_t slabs, int tokens, size_t row_bytes,
                 cudaStream_t s) {
   if (row_bytes % 16 || ((uintptr_t)src & 15) || ((uintptr_t)dst & 15))
@@ -217,6 +234,7 @@ bool use_tc_global_dkv(const p3d_operator *op) {
 struct BwdBuffers {
   void *dol, *dog;
   void *q_r, *kl_r, *vl_r, *dol_r, *dog_r;  // raster-order copies (tensor-core path, permuted storage)
+  float *lse_g_r, *delta_g_r;               // raster-order copies for the tensor-core global dSK / dSV
   float *delta_l, *delta_g, *dsl_part, *dsg_part, *dk_part, *dv_part, *dsk, *dsv, *dw_part, *db_part, *tmp;
   int64_t mix_rows, pool_rows;
   int splits, per_split;  // global dSK / dSV partials (per_split: tensor-core kernel only)
@@ -245,6 +263,7 @@ size_t bwd_layout(const p3d_operator *op, void *base, size_t cap, BwdBuffers *b)
   b->dol = c.take<char>(rows * d * es);
   b->dog = c.take<char>(rows * d * es);
   b->q_r = b->kl_r = b->vl_r = b->dol_r = b->dog_r = nullptr;
+  b->lse_g_r = b->delta_g_r = nullptr;
   if (use_stencil_bwd(op) && op->raster_to_packed) {
     const int64_t kv_rows = bg * op->tokens;
     b->q_r = c.take<char>(rows * d * es);
@@ -252,6 +271,10 @@ size_t bwd_layout(const p3d_operator *op, void *base, size_t cap, BwdBuffers *b)
     b->dog_r = c.take<char>(rows * d * es);
     b->kl_r = c.take<char>(kv_rows * d * es);
     b->vl_r = c.take<char>(kv_rows * d * es);
+    if (use_tc_global_dkv(op)) {
+      b->lse_g_r = c.take<float>(rows);
+      b->delta_g_r = c.take<float>(rows);
+    }
   }
   b->delta_l = c.take<float>(rows);
   b->delta_g = c.take<float>(rows);
@@ -588,6 +611,16 @@ int p3d_attn_bwd(const p3d_operator *op, const void *dy, const void *sk, const v
     g.sv = sv;
     g.lse_g = lse_g;
     g.delta_g = b.delta_g;
+    if (b.lse_g_r) {
+      // Permuted storage: visit the queries in raster order, as raster storage does, so that
+      // the fixed-order query sums (and with them dK_g, dV_g) do not depend on the storage.
+      if (int st = gather_vals(lse_g, b.lse_g_r, op->raster_to_packed, bh, op->tokens, s)) return st;
+      if (int st = gather_vals(b.delta_g, b.delta_g_r, op->raster_to_packed, bh, op->tokens, s)) return st;
+      g.q = b.q_r;
+      g.dog = b.dog_r;
+      g.lse_g = b.lse_g_r;
+      g.delta_g = b.delta_g_r;
+    }
     g.dk_part = b.dk_part;
     g.dv_part = b.dv_part;
     if (int st = launch_global_dkv_tc(g, s)) return st;

@@ -5,6 +5,11 @@
 
 namespace p3d {
 
+// Shared by every entry point that takes a p3d_operator (capi.cu): the argument checks of
+// p3d_attn_fwd / p3d_attn_bwd and the descriptor -> launch-argument conversions.
+int summaries_of(const p3d_operator *op);
+int validate(const p3d_operator *op);
+
 struct PoolArgs {
   const void *k, *v;  // [BG, N, D]
   const float *weight, *bias;
@@ -48,6 +53,8 @@ struct IndexedArgs {
 };
 
 // Local branch forward: ol [B,H,N,D] dtype, lse_l [B,H,N] fp32 (nullable; +inf for all-masked rows).
+IndexedArgs indexed_args(const p3d_operator *op, const void *sk, const void *sv);
+PoolArgs pool_args(const p3d_operator *op, void *sk, void *sv);
 int launch_local_fwd_indexed(const IndexedArgs &a, void *ol, float *lse_l, cudaStream_t s);
 // Global branch forward + mix: y, og (nullable), lse_g (nullable).
 int launch_global_fwd_mix(const IndexedArgs &a, const void *ol, void *y, void *og, float *lse_g,

@@ -57,21 +57,10 @@ int scratch_address(void **out) {
 using namespace p3d;
 
 extern "C" int p3d_attn_fwd_noalloc(const p3d_operator *op, void *y, void *sk, void *sv, void *stream) {
-  P3D_CHECK_ARG(op != nullptr && y && sk && sv, "p3d_attn_fwd_noalloc: null argument");
-  P3D_CHECK_ARG(dtype_ok(op->dtype) && dtype_ok(op->gate_dtype), "p3d_attn_fwd_noalloc: unknown dtype");
-  P3D_CHECK_ARG(op->batch >= 1 && op->heads >= 1 && op->kv_heads >= 1 && op->tokens >= 1 &&
-                    op->heads % op->kv_heads == 0,
-                "p3d_attn_fwd_noalloc: bad batch / head / token counts");
-  P3D_CHECK_ARG(op->head_dim >= 2 && op->head_dim <= 128 && op->head_dim % 2 == 0,
-                "p3d_attn_fwd_noalloc: head_dim %d unsupported", op->head_dim);
-  P3D_CHECK_ARG(op->temperature > 0.f && op->temperature < __builtin_huge_valf(),
-                "p3d_attn_fwd_noalloc: temperature must be finite and positive");
-  P3D_CHECK_ARG(op->width >= 1 && op->width <= 128 && op->slots >= 1 && op->slots <= 64 && op->pool_size >= 1 &&
-                    op->pool_size <= 32 && op->fine_blocks >= 1,
-                "p3d_attn_fwd_noalloc: bad geometry description");
-  P3D_CHECK_ARG(op->q && op->kl && op->vl && op->kg && op->vg && op->gate && op->pool_weight && op->slot_bias &&
-                    op->local_scale && op->global_scale && op->neighbors && op->blocks,
-                "p3d_attn_fwd_noalloc: null input");
+  // The same argument checks as p3d_attn_fwd (the shared validate(); the forward reads no
+  // reverse adjacency); only the scratch size is checked here.
+  if (int st = validate(op)) return st;
+  P3D_CHECK_ARG(y && sk && sv, "p3d_attn_fwd_noalloc: y, sk and sv are required");
   const size_t need = (size_t)op->batch * op->heads * op->tokens * op->head_dim * dtype_size(op->dtype);
   if (need > kScratchBytes)
     return fail(P3D_ERR_UNSUPPORTED,
@@ -81,49 +70,8 @@ extern "C" int p3d_attn_fwd_noalloc(const p3d_operator *op, void *y, void *sk, v
   void *scratch = nullptr;
   if (int st = scratch_address(&scratch)) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-
-  PoolArgs pa{};
-  pa.k = op->kg;
-  pa.v = op->vg;
-  pa.weight = op->pool_weight;
-  pa.bias = op->slot_bias;
-  pa.blocks = op->blocks;
-  pa.fine_blocks = op->fine_blocks;
-  pa.slots = op->slots;
-  pa.pool_size = op->pool_size;
-  pa.summaries = (op->fine_blocks + op->pool_size - 1) / op->pool_size;
-  pa.sk = sk;
-  pa.sv = sv;
-  pa.dtype = op->dtype;
-  pa.bg = op->batch * op->kv_heads;
-  pa.tokens = op->tokens;
-  pa.head_dim = op->head_dim;
-  pa.temperature = op->temperature;
-  pa.vec = dtype_size(op->dtype) == 2 && op->head_dim % 8 == 0 && ((uintptr_t)op->kg & 15) == 0 &&
-           ((uintptr_t)op->vg & 15) == 0;
-  if (int st = launch_pool_fwd(pa, s)) return st;
-
-  IndexedArgs a{};
-  a.dtype = op->dtype;
-  a.gate_dtype = op->gate_dtype;
-  a.batch = op->batch;
-  a.heads = op->heads;
-  a.kv_heads = op->kv_heads;
-  a.tokens = op->tokens;
-  a.head_dim = op->head_dim;
-  a.summaries = pa.summaries;
-  a.q = op->q;
-  a.kl = op->kl;
-  a.vl = op->vl;
-  a.sk = sk;
-  a.sv = sv;
-  a.neighbors = op->neighbors;
-  a.width = op->width;
-  a.reverse = op->reverse_neighbors;
-  a.reverse_width = op->reverse_width;
-  a.gate = op->gate;
-  a.sl = op->local_scale;
-  a.sg = op->global_scale;
+  if (int st = launch_pool_fwd(pool_args(op, sk, sv), s)) return st;
+  const IndexedArgs a = indexed_args(op, sk, sv);
   if (int st = launch_local_fwd_indexed(a, scratch, nullptr, s)) return st;
   return launch_global_fwd_mix(a, scratch, y, nullptr, nullptr, s);
 }

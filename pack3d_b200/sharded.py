@@ -116,9 +116,17 @@ class SlabLayout:
 
 
 def slab_layout(grid, block_shape=(4, 4, 4), *, radius=2, pool_size=1, slabs: ZSlabs):
-    """Raster-stored layout of this rank's planes of ``grid``."""
+    """Raster-stored layout of this rank's planes of ``grid``.
+
+    Only ``pool_size=1`` is accepted: each summary is then one fine block, a cube that lies
+    inside one rank, so the ranks' summaries are exactly the whole volume's.  With coarser
+    pooling a rank would group consecutive fine blocks of its own Morton block order, which
+    differs from the whole volume's, and summaries would pool the wrong blocks.
+    """
     if tuple(grid) != tuple(slabs.grid) or block_shape[0] != slabs.block_depth or radius != slabs.radius:
         raise ValueError("the slab partition must match the grid, block depth and radius")
+    if pool_size != 1:
+        raise ValueError("z-slab sharding supports pool_size=1 only (each summary one fine block)")
     local = build_layout((slabs.planes, grid[1], grid[2]), block_shape, radius=radius, pool_size=pool_size)
     local = local.repack(local.order.argsort())
     coords = local.coords.clone()

@@ -83,7 +83,12 @@ def test_core_graph_cases_match_reference(cuda_device, golden, case):
     grads = torch.autograd.grad(y, leaves, dy)
     for nm, got, want in zip(NAMES, grads, ref["grads"]):
         assert got.dtype == want.dtype, nm
-        scale = max(1.0, want.float().abs().max().item()) if dtype != torch.float32 else 1.0
+        # The reference's bf16 gradients are themselves rounded to bf16.  Where they exceed 2 in
+        # magnitude one bf16 step is more than 2e-2, so those are held to 2e-2 relative to their
+        # largest value: in the d48 bf16 case dvl (up to 4.5), dvg (2.0), dweight (2.3),
+        # dlocal_scale (11.1) and dglobal_scale (2.8).  Every other gradient: plain 2e-2.
+        big = dtype != torch.float32 and want.float().abs().max().item() > 2.0
+        scale = want.float().abs().max().item() if big else 1.0
         assert max_abs(got, want) <= tol * scale, (nm, max_abs(got, want))
     with torch.inference_mode():
         inference = pack3d_streamed(*[t.detach() for t in leaves], geom, temperature=temperature)
@@ -151,8 +156,13 @@ def test_grid_bf16_forward_backward_matches_oracle(cuda_device, dtype):
                for i in range(5)]
     ref_y = oracle.pack3d_core(*ref_rot, *ref_leaves[5:], geom.neighbors, geom.blocks, 1, chunk=512)
     ref_grads = torch.autograd.grad(ref_y, ref_leaves, dy.float())
+    # Tensor gradients (largest about 2.8) at plain 2e-2.  The parameter gradients that sum over
+    # all 2 x 4 x 1024 query rows -- dweight (about 18), dlocal_scale (about 39) and
+    # dglobal_scale (about 19) -- at 2e-2 relative to their largest magnitude.
+    summed = {"pool_weight", "local_scale", "global_scale"}
     for nm, a, b in zip(NAMES, grads, ref_grads):
-        assert max_abs(a, b) <= 2e-2 * max(1.0, b.abs().max().item()), (nm, max_abs(a, b))
+        scale = max(1.0, b.abs().max().item()) if nm in summed else 1.0
+        assert max_abs(a, b) <= 2e-2 * scale, (nm, max_abs(a, b))
 
 
 # ------------------------------------------------------------------ contract properties
@@ -167,7 +177,8 @@ def test_repack_equivariance(cuda_device):
         y_r = _pipeline(to_dev(inputs, cuda_device), dev_r)
         permuted = [t[:, :, p] if i in (0, 1, 2, 3, 4, 7) else t for i, t in enumerate(inputs)]
         y_m = _pipeline(to_dev(permuted, cuda_device), dev_m)
-    assert max_abs(y_m, y_r[:, :, p.to(cuda_device)]) <= 2e-2
+    # Morton storage gathers its rows into raster order and runs the same arithmetic: exact.
+    assert torch.equal(y_m, y_r[:, :, p.to(cuda_device)])
 
 
 def test_backward_is_deterministic_and_saves_19(cuda_device):

@@ -3,10 +3,20 @@
 The indexed kernels are pinned to the reference (test_gpu_parity); the tensor-core
 kernels must agree with them on every shape class of the tile decomposition: partial
 tiles on each axis, summary counts that are not a multiple of the 96-row chunk, GQA,
-bf16 and f16, every supported head dimension and permuted (Morton) storage.  Gradient
-tolerance: max-abs 2e-2 times max(1, the gradient's largest magnitude) -- bf16 spacing
-is already 1.6e-2 at magnitude 2.
+bf16 and f16, every supported head dimension and permuted (Morton) storage.
+
+Gradient tolerances (``_bound``):
+* against the oracle (unrounded fp32): max-abs 2e-2 for every per-token gradient;
+* against the indexed CUDA backward, whose result is rounded to the same 16-bit dtype on
+  its own: 2e-2 plus one storage step at the gradient's largest magnitude, since two
+  roundings of nearly equal values can land one step apart (0.0156 per bf16 step for
+  magnitudes in [2, 4));
+* the parameter gradients that sum over every query row (dweight, dlocal_scale,
+  dglobal_scale; magnitudes 10-40 in these cases): 2e-2 relative to their largest value.
+Permuted storage runs the raster arithmetic in the raster order: exact equality.
 """
+import math
+
 import pytest
 import torch
 
@@ -43,8 +53,18 @@ def _err(a, b):
     return (a.detach().float().cpu() - b.detach().float().cpu()).abs().max().item()
 
 
-def _scale(t):
-    return max(1.0, t.detach().float().abs().max().item())
+SUMMED = {"dweight", "dsl", "dsg"}
+
+
+def _bound(name, want, against_16bit):
+    """Largest admissible max-abs difference for gradient ``name`` (see the module docstring)."""
+    top = want.detach().float().abs().max().item()
+    if name in SUMMED:
+        return 2e-2 * max(1.0, top)
+    if not against_16bit or want.dtype == torch.float32 or top == 0.0:
+        return 2e-2
+    mantissa = 7 if want.dtype == torch.bfloat16 else 10
+    return 2e-2 + 2.0 ** (math.floor(math.log2(top)) - mantissa)
 
 
 @pytest.mark.parametrize("grid,b,h,g,d,dtype", [
@@ -66,7 +86,7 @@ def test_stencil_backward_matches_indexed(cuda_device, grid, b, h, g, d, dtype):
     torch.cuda.synchronize()
     assert _native.device_errors() == 0
     for name, got, want in zip(NAMES, tc, ix):
-        assert _err(got, want) <= 2e-2 * _scale(want), (name, _err(got, want))
+        assert _err(got, want) <= _bound(name, want, True), (name, _err(got, want))
 
 
 def test_stencil_backward_matches_oracle(cuda_device):
@@ -79,7 +99,7 @@ def test_stencil_backward_matches_oracle(cuda_device):
                                 geom.blocks, 1, 1.0, chunk=2048)
     assert _native.device_errors() == 0
     for name, got, ref in zip(NAMES, tc, want):
-        assert _err(got, ref) <= 2e-2 * _scale(ref), (name, _err(got, ref))
+        assert _err(got, ref) <= _bound(name, ref, False), (name, _err(got, ref))
 
 
 def test_stencil_backward_on_morton_storage(cuda_device):
@@ -93,7 +113,7 @@ def test_stencil_backward_on_morton_storage(cuda_device):
     g_m = _grads(permuted, dy[:, :, p], morton.geometry, cuda_device, force_indexed=False)
     pd = p.to(cuda_device)
     for i, name in enumerate(NAMES[:5]):
-        assert _err(g_m[i], g_r[i][:, :, pd]) <= 2e-2 * _scale(g_r[i]), name
+        assert torch.equal(g_m[i], g_r[i][:, :, pd]), name
     assert _native.device_errors() == 0
 
 
@@ -130,4 +150,4 @@ def test_radius_one_stencil_backward_matches_indexed(cuda_device, grid, block, p
     torch.cuda.synchronize()
     assert _native.device_errors() == 0
     for name, got, want in zip(NAMES, tc, ix):
-        assert _err(got, want) <= 2e-2 * _scale(want), (name, _err(got, want))
+        assert _err(got, want) <= _bound(name, want, True), (name, _err(got, want))

@@ -45,6 +45,31 @@ def test_slab_layout_has_global_coordinates():
     assert layout.geometry.stencil == ((8, 8, 8), (2, 2, 2))
 
 
+@pytest.mark.parametrize("grid,world", [((16, 16, 16), 4), ((16, 8, 24), 2), ((32, 8, 8), 8)])
+def test_slab_summaries_are_the_whole_volume_summaries(grid, world):
+    """Every rank's summaries (rank-major after the gather) are the whole volume's 4x4x4 cubes,
+    each exactly once, with the same members (global raster indices)."""
+    from pack3d_b200 import build_layout
+    whole = build_layout(grid, (4, 4, 4), radius=2, pool_size=1)
+    whole = whole.repack(whole.order.argsort())
+    want = {frozenset(row.tolist()) for row in whole.geometry.blocks}
+    got = []
+    for rank in range(world):
+        s = ZSlabs(grid, world, rank)
+        layout = slab_layout(grid, slabs=s)
+        lo, _ = s.token_range()
+        got += [frozenset((row + lo).tolist()) for row in layout.geometry.blocks]
+    assert len(got) == len(want) and set(got) == want
+
+
+def test_slab_layout_refuses_coarse_pooling():
+    """A rank's coarse groups follow its own block order, not the whole volume's: refused."""
+    slabs = ZSlabs((16, 16, 16), 4, 1)
+    for pool in (2, 8):
+        with pytest.raises(ValueError, match="pool_size=1"):
+            slab_layout((16, 16, 16), pool_size=pool, slabs=slabs)
+
+
 def _exchange_worker(rank, world, port, grid, out):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
