@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define P3D_ABI_VERSION 1
+#define P3D_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define P3D_API __attribute__((visibility("default")))
@@ -209,6 +209,16 @@ P3D_API int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, vo
 P3D_API size_t p3d_attn_fwd_workspace(const p3d_operator *op, unsigned flags);
 
 /*
+ * bound[b*G + g] = max over the summaries j of |sk[b, g, j, :]| (fp32 Euclidean norm, rounded
+ * up by 2^-10), sk [B,G,M,D] bf16 / f16.  By Cauchy-Schwarz |q| * bound bounds every global
+ * score of query row q (before the 1/sqrt(D) scale).  p3d_attn_fwd computes it itself; the
+ * z-slab forward takes it through p3d_slab.summary_bound.  No reference counterpart (the
+ * Triton kernels track a running maximum).
+ */
+P3D_API int p3d_summary_bound(const void *sk, int dtype, int batch, int kv_heads, int summaries, int head_dim,
+                      float *bound, void *stream);
+
+/*
  * z-slab extents of one rank when a volume is sharded across GPUs along z.  No counterpart
  * in the reference, which runs on one GPU.  op->q, op->gate, y, ol, og, lse_* describe this
  * rank's planes [center_z0, center_z0 + op->grid[0]); op->kl / op->vl hold the planes
@@ -221,6 +231,10 @@ typedef struct {
   int32_t halo_z0;       /* global z of the first plane of op->kl / op->vl */
   int32_t halo_planes;   /* planes in op->kl / op->vl */
   int32_t summaries;     /* rows of the gathered sk / sv: the summaries of all ranks */
+  /* Optional [B*G] fp32 bound of p3d_summary_bound() on the gathered sk, or NULL.  With it
+   * the global softmax takes its exponentials against the per-row score bound instead of a
+   * running maximum (the faster form); p3d_attn_fwd_slab reads it, the backward does not. */
+  const float *summary_bound;
 } p3d_slab;
 
 /*

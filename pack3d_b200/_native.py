@@ -48,7 +48,7 @@ class Slab(ctypes.Structure):
     """Mirror of ``p3d_slab`` in ``include/pack3d_b200.h``."""
 
     _fields_ = [("global_planes", ctypes.c_int32), ("center_z0", ctypes.c_int32), ("halo_z0", ctypes.c_int32),
-                ("halo_planes", ctypes.c_int32), ("summaries", ctypes.c_int32)]
+                ("halo_planes", ctypes.c_int32), ("summaries", ctypes.c_int32), ("summary_bound", _vp)]
 
 
 _SIGNATURES = {
@@ -78,6 +78,7 @@ _SIGNATURES = {
     "p3d_attn_fwd": (_c_int, [ctypes.POINTER(Operator), _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_uint,
                               _vp, ctypes.c_size_t, _vp]),
     "p3d_attn_fwd_workspace": (ctypes.c_size_t, [ctypes.POINTER(Operator), ctypes.c_uint]),
+    "p3d_summary_bound": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp]),
     "p3d_attn_fwd_noalloc": (_c_int, [ctypes.POINTER(Operator), _vp, _vp, _vp, _vp]),
     "p3d_attn_fwd_slab": (_c_int, [ctypes.POINTER(Operator), ctypes.POINTER(Slab), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                    ctypes.c_uint, _vp]),

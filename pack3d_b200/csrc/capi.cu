@@ -152,14 +152,16 @@ bool use_stencil_path(const p3d_operator *op, unsigned flags) {
 }
 
 // Forward workspace: indexed path needs an ol buffer when the caller saves no state;
-// the stencil path needs raster-ordered copies of q, kl, vl when storage is permuted.
+// the stencil path needs the per-(batch, kv-head) summary-norm bound and, when storage is
+// permuted, raster-ordered copies of q, kl, vl.
 size_t fwd_layout(const p3d_operator *op, unsigned flags, void *base, size_t cap, void **ol_ws,
-                  void **q_r, void **kl_r, void **vl_r) {
+                  void **q_r, void **kl_r, void **vl_r, float **kbound) {
   Carver c(base, cap);
   const size_t es = dtype_size(op->dtype);
   const size_t q_elems = (size_t)op->batch * op->heads * op->tokens * op->head_dim;
   const size_t kv_elems = (size_t)op->batch * op->kv_heads * op->tokens * op->head_dim;
   if (use_stencil_path(op, flags)) {
+    *kbound = c.take<float>((size_t)op->batch * op->kv_heads);
     if (op->raster_to_packed) {
       *q_r = c.take<char>(q_elems * es);
       *kl_r = c.take<char>(kv_elems * es);
@@ -361,7 +363,16 @@ int p3d_pool_fwd(const void *k, const void *v, const float *weight, const float 
 size_t p3d_attn_fwd_workspace(const p3d_operator *op, unsigned flags) {
   if (validate(op) != P3D_OK) return 0;
   void *a = nullptr, *b = nullptr, *c = nullptr, *d = nullptr;
-  return fwd_layout(op, flags, nullptr, 0, &a, &b, &c, &d);
+  float *e = nullptr;
+  return fwd_layout(op, flags, nullptr, 0, &a, &b, &c, &d, &e);
+}
+
+int p3d_summary_bound(const void *sk, int dtype, int batch, int kv_heads, int summaries, int head_dim,
+                      float *bound, void *stream) {
+  P3D_CHECK_ARG(sk && bound, "p3d_summary_bound: null pointer");
+  P3D_CHECK_ARG(batch >= 1 && kv_heads >= 1 && summaries >= 1, "p3d_summary_bound: bad shape");
+  return launch_summary_bound(sk, dtype, batch * kv_heads, summaries, head_dim, bound,
+                              static_cast<cudaStream_t>(stream));
 }
 
 int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, void *og, float *lse_l,
@@ -375,11 +386,12 @@ int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, 
   P3D_CHECK_ARG(!save || (ol && og && lse_l && lse_g), "p3d_attn_fwd: saving state needs ol, og, lse_l, lse_g");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   void *ol_ws = nullptr, *q_r = nullptr, *kl_r = nullptr, *vl_r = nullptr;
-  const size_t need = fwd_layout(op, flags, nullptr, 0, &ol_ws, &q_r, &kl_r, &vl_r);
+  float *kbound = nullptr;
+  const size_t need = fwd_layout(op, flags, nullptr, 0, &ol_ws, &q_r, &kl_r, &vl_r, &kbound);
   if (need > 0) {
     if (!workspace || workspace_bytes < need)
       return fail(P3D_ERR_WORKSPACE, "p3d_attn_fwd: workspace of %zu bytes required", need);
-    fwd_layout(op, flags, workspace, workspace_bytes, &ol_ws, &q_r, &kl_r, &vl_r);
+    fwd_layout(op, flags, workspace, workspace_bytes, &ol_ws, &q_r, &kl_r, &vl_r, &kbound);
   }
   if (!(flags & P3D_FWD_SUMMARIES_GIVEN))
     if (int st = launch_pool_fwd(pool_args(op, sk, sv), s)) return st;
@@ -426,6 +438,9 @@ int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, 
     a.lse_l = save ? lse_l : nullptr;
     a.lse_g = save ? lse_g : nullptr;
     a.y_rows = (flags & P3D_FWD_Y_ROWS) != 0;
+    if (int st = launch_summary_bound(sk, op->dtype, op->batch * op->kv_heads, a.summaries, op->head_dim, kbound, s))
+      return st;
+    a.summary_bound = kbound;
     return launch_stencil_fwd(a, s);
   }
   IndexedArgs a = indexed_args(op, sk, sv);
@@ -488,6 +503,7 @@ int p3d_attn_fwd_slab(const p3d_operator *op, const p3d_slab *slab, void *y, con
   a.lse_l = save ? lse_l : nullptr;
   a.lse_g = save ? lse_g : nullptr;
   a.y_rows = (flags & P3D_FWD_Y_ROWS) != 0;
+  a.summary_bound = slab->summary_bound;
   return launch_stencil_fwd(a, static_cast<cudaStream_t>(stream));
 }
 

@@ -132,7 +132,13 @@ struct StencilFwdArgs {
   float *lse_l, *lse_g;               // nullable
   int y_rows;                         // y token-major [B,N,H,D]
   int radius;                         // stencil radius (1 or 2, all axes)
+  const float *summary_bound;         // [B*G] max_j |sk_j| (launch_summary_bound), or NULL
 };
+// bound[bg] = max over the summaries j of |sk[bg, j, :]| (fp32 Euclidean norm, rounded up by
+// 2^-10), sk [BG, M, D] in a 16-bit dtype: the stencil forward's per-row bound on the global
+// scores.
+int launch_summary_bound(const void *sk, int dtype, int bg, int summaries, int head_dim, float *bound,
+                         cudaStream_t stream);
 // Read-and-clear the device failure bits of the tensor-core kernel files (OR-ed into *flags).
 int take_fwd_errors(unsigned *flags);
 

@@ -209,6 +209,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t *r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t *r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -319,6 +325,20 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   const float2 jj = add2(x, make_float2(kMagic, kMagic));          // rint(x) in the low bits
   const float2 r = add2(jj, make_float2(-kMagic, -kMagic));        // rint(x)
   const float2 f = fma2(r, make_float2(-1.f, -1.f), x);            // x - rint(x)
+  float2 p = fma2(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.24261114f, 0.24261114f));
+  p = fma2(p, f, make_float2(0.69326097f, 0.69326097f));
+  p = fma2(p, f, make_float2(0.99992806f, 0.99992806f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(jj.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(jj.y) << 23)));
+}
+
+// exp2_poly2 without the lower clamp, for arguments known to lie in [-125, 127] (the
+// fixed-reference softmax of the stencil forward keeps them in [-64, 0]).
+__device__ __forceinline__ float2 exp2_poly2_inrange(float2 x) {
+  constexpr float kMagic = 12582912.f;  // 1.5 * 2^23
+  const float2 jj = add2(x, make_float2(kMagic, kMagic));
+  const float2 r = add2(jj, make_float2(-kMagic, -kMagic));
+  const float2 f = fma2(r, make_float2(-1.f, -1.f), x);
   float2 p = fma2(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.24261114f, 0.24261114f));
   p = fma2(p, f, make_float2(0.69326097f, 0.69326097f));
   p = fma2(p, f, make_float2(0.99992806f, 0.99992806f));

@@ -16,20 +16,23 @@
 //                 (coordinate test, no neighbour table).  A warp whose query plane is
 //                 more than 2 planes away writes a zero P block.
 //   chunks 8..    global: 96 summaries per chunk.
-// TMEM (256 columns): two 96-column S buffers and one accumulator O.  The QK^T MMA of
-// chunk c+2 and the PV MMA of chunk c run while the softmax warps work on chunk c+1.  O
-// holds the local accumulator during chunks 0..7; when they are done the normalised
-// local output is parked in shared memory, rounded to the storage dtype as the
-// reference rounds it before the mix, and O then accumulates the global branch.
-// Two independent online softmaxes (max / sum per row in registers, conditional
-// rescale of O only when the running max grows by > 2^8).  The epilogue normalises the
+// TMEM (256 columns): one 96-column S buffer, a 48-column P buffer (16-bit pairs) and the
+// accumulator O.  The softmax warps release S as soon as it is in their registers, so the
+// QK^T MMA of chunk c+1 runs while they exponentiate chunk c, and the PV MMA of chunk c
+// runs while they work on chunk c+1.  O holds the local accumulator during chunks 0..7;
+// when they are done the normalised local output is parked in shared memory, rounded to
+// the storage dtype as the reference rounds it before the mix, and O then accumulates the
+// global branch.  Two independent online softmaxes: the local one tracks its maximum (in
+// registers; O is rescaled only when it grows by > 2^8); the global one takes its
+// exponentials against a per-row upper bound of its scores when the summaries' norms give
+// one that is tight enough, so it needs no maximum at all.  The epilogue normalises the
 // global branch, mixes and writes y (and optionally ol, og, lse_l, lse_g) through the
 // raster->packed row map.
 //
 // Roles: warps 0-3 softmax, warp 4 TMA producer, warp 5 MMA issuer (one thread).
 // Operands live in shared memory in the SWIZZLE_32B layout: Q / K are K-major boxes of
-// 16 channels, V is the same bytes read MN-major; P goes back into its S buffer in TMEM
-// as bf16/f16 pairs and feeds the PV MMA as the TMEM A operand.  Every mbarrier wait is
+// 16 channels, V is the same bytes read MN-major; P is written to its TMEM buffer as
+// bf16/f16 pairs and feeds the PV MMA as the TMEM A operand.  Every mbarrier wait is
 // bounded.
 #include <algorithm>
 
@@ -46,8 +49,9 @@ __device__ unsigned g_fwd_errors = 0;  // failure bits of the kernels in this fi
 
 constexpr int kTZ = 4, kTY = 4, kTX = 8;            // one 128-row query tile
 constexpr int kRows = 128;                          // queries per tile
-constexpr int kThreads = 192;
-constexpr int kProducerWarp = 4, kMmaWarp = 5;
+constexpr int kSoftmaxWarps = 4;                    // one per 32-row quarter of the tile
+constexpr int kThreads = 32 * (kSoftmaxWarps + 2);
+constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1;
 constexpr uint32_t kTmemCols = 256;                 // two CTAs per SM
 constexpr float kNegInf = -__builtin_huge_valf();
 constexpr uint64_t kWaitNs = 2000000000ull;        // every mbarrier wait gives up after 2 s
@@ -55,7 +59,8 @@ constexpr uint64_t kWaitNs = 2000000000ull;        // every mbarrier wait gives 
 // Chunk geometry of a radius-R stencil (R = 1 or 2): a local chunk is one halo plane of the
 // tile, a kHY x kHX (y, x) window; chunks are kKeys wide (the window rounded up to 32 keys;
 // the padding rows of every ring stage are zero and masked) and global chunks take kKeys
-// summaries.  TMEM: S buffers [0, kKeys) and [kKeys, 2 kKeys), O [2 kKeys, 2 kKeys + D).
+// summaries.  TMEM: the S buffer [0, kKeys), the P buffer (16-bit pairs) [kKeys, 3 kKeys / 2),
+// O [3 kKeys / 2, 3 kKeys / 2 + D).
 template <int R>
 struct Geo {
   static constexpr int kR = R;
@@ -64,7 +69,7 @@ struct Geo {
   static constexpr int kKeys = (kWin + 31) / 32 * 32;   // 96, 64
   static constexpr int kLocalChunks = kHZ;              // 8, 6 halo planes per tile
   static constexpr int kSumRows = kKeys;                // summaries per global chunk
-  static constexpr uint32_t kSBuf = kKeys, kColO = 2 * kKeys;
+  static constexpr uint32_t kColS = 0, kColP = kKeys, kColO = kKeys + kKeys / 2;
   static_assert(kKeys % 32 == 0 && kKeys <= 96, "chunk size must suit the MMA, TMEM and register budgets");
 };
 
@@ -91,18 +96,23 @@ struct Cfg {
   static_assert(kSmemBytes <= kMaxSmem, "shared memory budget");
 };
 
-// S(c) is complete when its commit arrives: S(0), S(1) commit to kSReady[c], and S(c),
-// c >= 2, to kEmpty[(c-2) % kStages]: S(c) is issued after PV(c-2) has completed (and every
-// MMA before it), so its completion is also the moment chunk c-2's ring stage is free.
-// One release barrier per stage keeps every parity wait unambiguous (see the producer).
+// Barrier map (one 128-row tile; the executable model is tests/stencil_protocol.py):
+//   S(c) commits to kSFull.  The four softmax warps arrive on kSFree once they have loaded
+//   S(c) into registers, and S(c + 1) may then overwrite it -- so the next S is computed
+//   while the softmax warps still work on this one.  They arrive on kPFull once P(c) is in
+//   the P buffer; PV(c) commits to kPFree (P buffer reusable, O quiet: it may be read or
+//   rescaled until PV(c + 1) is issued) and to kEmpty[c % kStages] (both MMAs that read the
+//   ring stage of chunk c have completed: the producer may refill it).  Every parity wait
+//   has the completions before and after the awaited one ruled out.
 enum Bar {
   kQFull = 0,
   kFull = 1,                  // [stage]
-  kSReady = kFull + 4,        // [buf] (chunks 0 and 1)
-  kEmpty = kSReady + 2,       // [stage]: released by S(c + 2), c the chunk it held
-  kPReady = kEmpty + 4,       // [buf] (count 4: the softmax warps stored P)
-  kPvDone = kPReady + 2,      // [buf]: PV of the chunk that last used the buffer is done
-  kOReady = kPvDone + 2,
+  kEmpty = kFull + 4,         // [stage]: released by PV(c), c the chunk it held
+  kSFull = kEmpty + 4,        // S(c) complete
+  kSFree = kSFull + 1,        // count 4: the softmax warps loaded S(c)
+  kPFull = kSFree + 1,        // count 4: the softmax warps stored P(c)
+  kPFree = kPFull + 1,        // PV(c) complete
+  kOReady = kPFree + 1,
   kDrain = kOReady + 1,       // MMA thread: every MMA it issued has completed
   kNumBars = kDrain + 1
 };
@@ -121,7 +131,13 @@ struct FwdParams {
   void *y, *ol, *og;
   float *lse_l, *lse_g;
   int y_rows;  // y is [B, N, H, D] (token-major) instead of [B, H, N, D]
+  const float *kbound;  // [B*G] max_j |sk_j|, or nullptr: the global branch tracks its maximum
 };
+
+// Fixed-reference global softmax (see the softmax warps): used when every p of a row stays
+// within [2^-kFixedRange, 1]; kPolyEighths of every 8 exponential pairs go to the FMA pipe.
+constexpr float kFixedRange = 64.f;
+constexpr int kPolyEighths = 2;
 
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
@@ -160,50 +176,126 @@ __device__ __forceinline__ MaxUpdate begin_max(float m, float mx, float sc) {
   return u;
 }
 
-template <int D>
-__device__ __forceinline__ void rescale_rows(float factor, uint32_t t_o) {
-  uint32_t o[16];
-#pragma unroll
-  for (int c = 0; c < D / 16; ++c) {
-    tmem_ld16(t_o + 16 * c, o);
-    tmem_wait_ld();
-#pragma unroll
-    for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-    tmem_st16(t_o + 16 * c, o);
-  }
-}
-
-// Exponentiate N scores (in registers) against max m, pack to 16-bit pairs and store
-// them as P into TMEM columns [t_p, t_p + N/2).  Returns the row sum of p.
+// Exponentiate N scores (in registers) against max m and pack them to 16-bit pairs in
+// pk[N/2] (P for the TMEM store).  A quarter of the pairs use the polynomial on the FMA pipe.
+// Returns the row sum of p.
 template <int N, bool BF16>
-__device__ __forceinline__ float exp_store(const float *s, float m, float sc, uint32_t t_p) {
-  static_assert(N % 32 == 0, "N must be a multiple of 32");
+__device__ __forceinline__ float exp_pack(const float *s, float m, float sc, uint32_t *pk) {
+  static_assert(N % 16 == 0, "N must be a multiple of 16");
   const float msc = (m == kNegInf) ? 0.f : m * sc;
   const float2 sc2 = make_float2(sc, sc), nmsc2 = make_float2(-msc, -msc);
   float2 sum[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // independent partial sums
 #pragma unroll
-  for (int g = 0; g < N / 32; ++g) {
-    uint32_t pk[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      // fmaf(s, sc, -msc) on each lane of the pair
-      const float2 x = fma2(make_float2(s[32 * g + 2 * i], s[32 * g + 2 * i + 1]), sc2, nmsc2);
-      float p0, p1;
-      if ((i & 3) == 3) {  // a quarter of the exponentials on the FMA pipe: the MUFU is the bound
-        const float2 e = exp2_poly2(x);
-        p0 = e.x;
-        p1 = e.y;
-      } else {
-        p0 = ex2_approx(x.x);
-        p1 = ex2_approx(x.y);
-      }
-      sum[i & 1] = add2(sum[i & 1], make_float2(p0, p1));
-      pk[i] = pack2<BF16>(p0, p1);
+  for (int i = 0; i < N / 2; ++i) {
+    // fmaf(s, sc, -msc) on each lane of the pair
+    const float2 x = fma2(make_float2(s[2 * i], s[2 * i + 1]), sc2, nmsc2);
+    float2 e;
+    if ((i & 3) == 3) {  // a quarter of the exponentials on the FMA pipe: the MUFU is the bound
+      e = exp2_poly2(x);
+    } else {
+      e.x = ex2_approx(x.x);
+      e.y = ex2_approx(x.y);
     }
-    tmem_st16(t_p + 16 * g, pk);
+    sum[i & 1] = add2(sum[i & 1], e);
+    pk[i] = pack2<BF16>(e.x, e.y);
   }
   const float2 t = add2(sum[0], sum[1]);
   return t.x + t.y;
+}
+
+// exp_pack for the fixed-reference global branch: every x = s sc - msc lies in
+// [-kFixedRange, 0] (up to rounding), so no maximum, no rescale and no clamp are needed; a
+// share kPoly of every 8 pairs is evaluated by the polynomial on the FMA pipe, the rest on
+// the MUFU, interleaved.  Returns the row sum of p.
+template <int N, bool BF16, int kPoly>
+__device__ __forceinline__ float exp_pack_fixed(const float *s, float msc, float sc, uint32_t *pk) {
+  static_assert(N % 16 == 0, "N must be a multiple of 16");
+  const float2 sc2 = make_float2(sc, sc), nmsc2 = make_float2(-msc, -msc);
+  float2 sum[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) {
+    const float2 x = fma2(make_float2(s[2 * i], s[2 * i + 1]), sc2, nmsc2);
+    float2 e;
+    if (((i * kPoly) & 7) < kPoly) {
+      e = exp2_poly2_inrange(x);
+    } else {
+      e.x = ex2_approx(x.x);
+      e.y = ex2_approx(x.y);
+    }
+    sum[i & 1] = add2(sum[i & 1], e);
+    pk[i] = pack2<BF16>(e.x, e.y);
+  }
+  const float2 t = add2(sum[0], sum[1]);
+  return t.x + t.y;
+}
+
+// TMEM columns [OFF, OFF + W) of this warp's 32 lanes (t: the warp's lane base, column 0 of
+// the allocation, which is 32-column aligned), loaded (ld_span, then tmem_wait_ld) or stored
+// (st_span, then tmem_wait_st) as .x32 / .x16 / .x8 pieces that each start at a multiple of
+// their own width.
+template <int OFF, int W>
+__device__ __forceinline__ void ld_span(uint32_t t, uint32_t *r) {
+  static_assert(OFF % 8 == 0 && W % 8 == 0, "TMEM spans are whole 8-column groups");
+  if constexpr (W == 0) {
+    return;
+  } else if constexpr (OFF % 32 == 0 && W >= 32) {
+    tmem_ld32(t + OFF, r);
+    ld_span<OFF + 32, W - 32>(t, r + 32);
+  } else if constexpr (OFF % 16 == 0 && W >= 16) {
+    tmem_ld16(t + OFF, *reinterpret_cast<uint32_t(*)[16]>(r));
+    ld_span<OFF + 16, W - 16>(t, r + 16);
+  } else {
+    tmem_ld8(t + OFF, r);
+    ld_span<OFF + 8, W - 8>(t, r + 8);
+  }
+}
+template <int OFF, int W>
+__device__ __forceinline__ void st_span(uint32_t t, const uint32_t *r) {
+  static_assert(OFF % 8 == 0 && W % 8 == 0, "TMEM spans are whole 8-column groups");
+  if constexpr (W == 0) {
+    return;
+  } else if constexpr (OFF % 16 == 0 && W >= 16) {
+    tmem_st16(t + OFF, r);
+    st_span<OFF + 16, W - 16>(t, r + 16);
+  } else {
+    tmem_st8(t + OFF, r);
+    st_span<OFF + 8, W - 8>(t, r + 8);
+  }
+}
+
+// O *= factor on TMEM columns [OFF, OFF + W) (this warp's channels; per-row factor).
+template <int OFF, int W>
+__device__ __forceinline__ void rescale_span(float factor, uint32_t t) {
+  uint32_t o[W];
+  ld_span<OFF, W>(t, o);
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < W; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+  st_span<OFF, W>(t, o);
+}
+
+// Squared Euclidean norm of query row `row` of the Q tile in shared memory: D/16 boxes of
+// 128 rows x 32 bytes (16 channels).  The 32-byte swizzle only permutes the two 16-byte halves
+// of a row, which the sum does not see.
+template <int D, bool BF16>
+__device__ __forceinline__ float q_row_sq(const uint8_t *q_tile, int row) {
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < D / 16; ++c) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(q_tile + c * kRows * 32 + row * 32);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 v = src[h];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = unpack2<BF16>(w[k]);
+        acc = fmaf(f.x, f.x, acc);
+        acc = fmaf(f.y, f.y, acc);
+      }
+    }
+  }
+  return acc;
 }
 
 // Row maximum of N registers as a tree (8 independent chains, then pairwise).
@@ -229,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   using G = Geo<R>;
   constexpr int kR = G::kR, kHY = G::kHY, kHX = G::kHX, kWin = G::kWin, kKeys = G::kKeys;
   constexpr int kLocalChunks = G::kLocalChunks, kSumRows = G::kSumRows;
-  constexpr uint32_t kSBuf = G::kSBuf, kColO = G::kColO;
+  constexpr uint32_t kColO = G::kColO;
   using C = Cfg<D, kKeys>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[kNumBars];
@@ -256,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t q_smem = base;
   const uint32_t ring = base + C::kQBytes;
   uint8_t *ol_park = smem_raw + (base - raw) + C::kQBytes + C::kStages * C::kStageBytes;  // [row][D]
+  const uint8_t *q_tile = smem_raw + (base - raw);                                       // generic view of Q
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
 
   if (tid == 0) {
@@ -264,11 +357,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(bar(kFull + s), 1);
       mbar_init(bar(kEmpty + s), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(kSReady + i), 1);
-      mbar_init(bar(kPReady + i), 4);
-      mbar_init(bar(kPvDone + i), 1);
-    }
+    mbar_init(bar(kSFull), 1);
+    mbar_init(bar(kSFree), kSoftmaxWarps);
+    mbar_init(bar(kPFull), kSoftmaxWarps);
+    mbar_init(bar(kPFree), 1);
     mbar_init(bar(kOReady), 1);
     mbar_init(bar(kDrain), 1);
     fence_mbar_init();
@@ -363,55 +455,45 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint64_t desc_q = desc_sw32(q_smem, 16, 256);          // the Q tile, K-major
       const uint64_t desc_k = desc_sw32(ring, 16, 256);            // K chunks in the ring, K-major
       const uint64_t desc_v = desc_sw32(ring, C::kBoxK, 256);      // V chunks in the ring, MN-major
-      // S(ch) = Q K(ch)^T into S buffer ch%2, then signal the softmax warps.
+      // S(ch) = Q K(ch)^T into the S buffer, then signal the softmax warps.
       auto issue_s = [&](int ch) {
         const uint64_t bk = desc_k + ((uint32_t)((ch % C::kStages) * C::kStageBytes) >> 4);
-        const uint32_t t_s = tmem + (ch & 1) * kSBuf;
+        const uint32_t t_s = tmem + G::kColS;
 #pragma unroll
         for (int c = 0; c < C::kK; ++c)
           mma_ss(t_s, desc_q + c * (C::kBoxQ >> 4), bk + c * (C::kBoxK >> 4), idesc_s, c > 0 ? 1u : 0u);
-        commit(ch >= 2 ? kEmpty + (ch - 2) % C::kStages : kSReady + ch);
+        commit(kSFull);
       };
-      // O += P(c) V(c) once the softmax warps have written P(c).
-      auto issue_pv = [&](int c) -> bool {
-        if (!mbar_wait(bar(kPReady + (c & 1)), (c >> 1) & 1, &g_fwd_errors, kWaitNs, kErrMma)) return false;
-        tc_fence_after();
+      // O += P(c) V(c); its completion frees the P buffer and O, and releases the ring stage.
+      auto issue_pv = [&](int c) {
         const uint64_t bv = desc_v + ((uint32_t)((c % C::kStages) * C::kStageBytes + C::kKeyBytes) >> 4);
-        const uint32_t t_p = tmem + (c & 1) * kSBuf, t_o = tmem + kColO;
+        const uint32_t t_p = tmem + G::kColP, t_o = tmem + kColO;
         const bool first = (c == 0) || (c == kLocalChunks);  // O restarts for the global branch
 #pragma unroll
         for (int j = 0; j < kKeys / 16; ++j)
           mma_ts(t_o, t_p + 8 * j, bv + j * (512 >> 4), idesc_pv, (first && j == 0) ? 0u : 1u);
-        commit(kPvDone + (c & 1));
-        return true;
+        commit(kPFree);
+        commit(kEmpty + c % C::kStages);
       };
-      auto wait_full = [&](int ch) -> bool {
-        if (!mbar_wait(bar(kFull + ch % C::kStages), (ch / C::kStages) & 1, &g_fwd_errors, kWaitNs, kErrMma))
-          return false;
+      auto wait_bar = [&](int b_idx, uint32_t parity) -> bool {
+        if (!mbar_wait(bar(b_idx), parity, &g_fwd_errors, kWaitNs, kErrMma)) return false;
         tc_fence_after();
         return true;
       };
-      // S(c+2) writes the TMEM columns that PV(c) reads as its A operand (P(c)).
-      // tcgen05.mma ops are only ordered among themselves when they share an accumulator,
-      // so PV(c) must have completed before S(c+2) is issued.
-      auto wait_pv = [&](int c) -> bool {
-        if (!mbar_wait(bar(kPvDone + (c & 1)), (c >> 1) & 1, &g_fwd_errors, kWaitNs, kErrMma)) return false;
-        tc_fence_after();
-        return true;
-      };
-      // Prologue: both S buffers.  Steady state per chunk c: PV(c), [PV(c) done] S(c+2).
-      bool ok = mbar_wait(bar(kQFull), 0, &g_fwd_errors, kWaitNs, kErrMma);
-      for (int ch = 0; ok && ch < 2; ++ch) {
-        ok = wait_full(ch);
-        if (!ok) break;
-        issue_s(ch);
-      }
+      auto wait_full = [&](int ch) -> bool { return wait_bar(kFull + ch % C::kStages, (ch / C::kStages) & 1); };
+      // Per chunk c: S(c + 1) as soon as the softmax warps have loaded S(c) (and chunk c + 1
+      // has landed), then PV(c) once they have stored P(c).
+      bool ok = mbar_wait(bar(kQFull), 0, &g_fwd_errors, kWaitNs, kErrMma) && n_chunks > 0 && wait_full(0);
+      if (ok) issue_s(0);
       for (int c = 0; ok && c < n_chunks; ++c) {
-        ok = issue_pv(c);
-        if (!ok || c + 2 >= n_chunks) continue;
-        ok = wait_full(c + 2) && wait_pv(c);
+        if (c + 1 < n_chunks) {
+          ok = wait_full(c + 1) && wait_bar(kSFree, c & 1);
+          if (!ok) break;
+          issue_s(c + 1);
+        }
+        ok = wait_bar(kPFull, c & 1);
         if (!ok) break;
-        issue_s(c + 2);  // its commit also releases chunk c's stage to the producer
+        issue_pv(c);
       }
       if (ok) commit(kOReady);
       // TMEM is freed after the final __syncthreads: make sure every MMA issued above has
@@ -423,17 +505,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
+    // Warp w owns TMEM lanes 32w .. 32w + 31: the 32 queries of plane z = w.
     const int w = warp;
-    const uint32_t lanes = (uint32_t)(w * 32) << 16;
-    const uint32_t t_tile = tmem + lanes;
-    const uint32_t t_o = t_tile + kColO;
+    const uint32_t t_tile = tmem + ((uint32_t)(w * 32) << 16);
     const int row = w * 32 + lane;
     const int qz = w, qy = lane >> 3, qx = lane & 7;
     const int zq = z0 + qz, yq = y0 + qy, xq = x0 + qx;
     const bool row_ok = zq < p.Z && yq < p.Y && xq < p.X;
     uint32_t *park = reinterpret_cast<uint32_t *>(ol_park + (size_t)row * D * 2);
-    // keys of the 8x12 halo window inside this query's cube and inside the volume
-    uint32_t mask[3] = {0u, 0u, 0u};
+    // keys of the halo window inside this query's cube and inside the volume
+    uint32_t mask[kKeys / 32] = {};
 #pragma unroll
     for (int hy = 0; hy < kHY; ++hy) {
 #pragma unroll
@@ -455,91 +536,113 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (all) tc_fence_after();
       return all;
     };
-    // Completion of PV(c), needed before O is read or rescaled.  Testing the phase only
-    // when needed is sound: the next completion of that buffer's barrier is PV(c+2), which
-    // needs this warp's P of chunk c+2.
-    auto wait_pv_done = [&](int c) -> bool { return wait_warp(bar(kPvDone + (c & 1)), (c >> 1) & 1); };
-    for (int ch = 0; ch < n_chunks; ++ch) {
-      const int buf = ch & 1;
-      const uint32_t t_s = t_tile + buf * kSBuf;
+    // Completion c of kPFree: PV(c) has completed, so the P buffer may be rewritten and O
+    // read or rescaled (until this warp's next kPFull arrival lets PV(c + 1) be issued).
+    // Completion c + 1 needs this warp's P of chunk c + 1, so the parity wait is exact.
+    auto wait_pfree = [&](int c) -> bool { return wait_warp(bar(kPFree), c & 1); };
+    // This warp's rows of S are in registers: S(c + 1) may overwrite the S buffer.
+    auto release_s = [&]() {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kSFree));
+    };
+    // Global-branch reference value.  By Cauchy-Schwarz every global score of this row (raw
+    // q.sk) is at most u = |q| max_j |sk_j|.  Taking the exponentials against u itself puts
+    // every p = 2^((s - u) sc) in [2^(-2 u sc), 1]: with 2 u sc <= kFixedRange for every row of
+    // the warp there is no running maximum to track, no rescale of O and no clamp in the
+    // polynomial exp2.  The softmax is the same function of the scores (only its reference
+    // point moves); otherwise, or without a bound, the warp tracks the maximum.
+    bool fixed_g = false;
+    if (p.kbound != nullptr) {
+      ok = wait_warp(bar(kQFull), 0);
+      if (ok) {
+        const float u = sqrtf(q_row_sq<D, BF16>(q_tile, row)) * __ldg(p.kbound + bg);
+        fixed_g = __all_sync(0xffffffffu, 2.f * u * sc <= kFixedRange);
+        if (fixed_g) m_g = u;
+      }
+    }
+    for (int ch = 0; ok && ch < n_chunks; ++ch) {
       if (ch == kLocalChunks) {
         // Local branch done: park its normalised output (storage dtype) and free O.
-        ok = wait_pv_done(kLocalChunks - 1);
+        ok = wait_pfree(kLocalChunks - 1);
         if (!ok) break;
         const float inv_l = l_l > 0.f ? 1.f / l_l : 0.f;
+        uint32_t o[D];
+        ld_span<kColO, D>(t_tile, o);
+        tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < D / 16; ++c) {
-          uint32_t o[16];
-          tmem_ld16(t_o + 16 * c, o);
-          tmem_wait_ld();
-          uint4 v[2];
-          uint32_t *pv = reinterpret_cast<uint32_t *>(v);
+        for (int v = 0; v < D / 8; ++v) {
+          uint4 pw;
+          uint32_t *pv = reinterpret_cast<uint32_t *>(&pw);
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            pv[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
-          reinterpret_cast<uint4 *>(park)[2 * c] = v[0];
-          reinterpret_cast<uint4 *>(park)[2 * c + 1] = v[1];
+          for (int i = 0; i < 4; ++i)
+            pv[i] = pack2<BF16>(__uint_as_float(o[8 * v + 2 * i]) * inv_l, __uint_as_float(o[8 * v + 2 * i + 1]) * inv_l);
+          reinterpret_cast<uint4 *>(park)[v] = pw;
         }
         tc_fence_before();
       }
-      // S(ch) complete (the barrier map is described at enum Bar).  Each is completion
-      // number k of its barrier with k - 1 awaited by this warp before (or k = 0), and
-      // completion k + 1 needs this warp's P of a later chunk.
-      if (ch >= 2)
-        ok = wait_warp(bar(kEmpty + (ch - 2) % C::kStages), ((ch - 2) / C::kStages) & 1);
-      else
-        ok = wait_warp(bar(kSReady + ch), 0);
+      // S(ch) complete: completion ch of kSFull (completion ch + 1 needs this warp's kSFree
+      // arrival for chunk ch).
+      ok = wait_warp(bar(kSFull), ch & 1);
       if (!ok) break;
       const bool local = ch < kLocalChunks;
       const int zp = p.qz0 + z0 - kR + ch;  // global plane of this local chunk
       const bool active = !local || ((unsigned)(ch - qz) <= 2u * kR && zp >= 0 && zp < p.Zg);  // warp-uniform
+      uint32_t pk[kKeys / 2];
+      bool rescale = false;
+      float factor = 1.f;
       if (active) {
         float s[kKeys];
-#pragma unroll
-        for (int g = 0; g < kKeys / 32; ++g) tmem_ld32(t_s + 32 * g, reinterpret_cast<uint32_t *>(s + 32 * g));
+        ld_span<G::kColS, kKeys>(t_tile, reinterpret_cast<uint32_t *>(s));
         tmem_wait_ld();
+        release_s();
+        const int valid = local ? kKeys : p.summaries - (ch - kLocalChunks) * kSumRows;
         if (local) {
 #pragma unroll
           for (int i = 0; i < kKeys; ++i) s[i] = (mask[i >> 5] >> (i & 31)) & 1u ? s[i] : kNegInf;
-        } else {
-          const int valid = p.summaries - (ch - kLocalChunks) * kSumRows;
-          if (valid < kSumRows) {
+        } else if (valid < kSumRows) {
 #pragma unroll
-            for (int i = 0; i < kSumRows; ++i) s[i] = i < valid ? s[i] : kNegInf;
+          for (int i = 0; i < kSumRows; ++i) s[i] = i < valid ? s[i] : kNegInf;
+        }
+        if (!local && fixed_g) {
+          // the last, partial chunk has masked (-inf) scores: the clamped form maps them to 0
+          l_g += valid < kSumRows ? exp_pack<kKeys, BF16>(s, m_g, sc, pk)
+                                  : exp_pack_fixed<kKeys, BF16, kPolyEighths>(s, m_g * sc, sc, pk);
+        } else {
+          const MaxUpdate u = begin_max(local ? m_l : m_g, row_max<kKeys>(s), sc);
+          const float sum = exp_pack<kKeys, BF16>(s, u.m_use, sc, pk);
+          rescale = __any_sync(0xffffffffu, u.rescale);
+          factor = u.factor;
+          if (local) {
+            l_l = l_l * u.factor + sum;
+            m_l = u.m_use;
+          } else {
+            l_g = l_g * u.factor + sum;
+            m_g = u.m_use;
           }
         }
-        const MaxUpdate u = begin_max(local ? m_l : m_g, row_max<kKeys>(s), sc);
-        const float sum = exp_store<kKeys, BF16>(s, u.m_use, sc, t_s);
-        if (__any_sync(0xffffffffu, u.rescale)) {
-          ok = wait_pv_done(ch - 1);
-          if (!ok) break;
-          rescale_rows<D>(u.factor, t_o);
-        }
-        if (local) {
-          l_l = l_l * u.factor + sum;
-          m_l = u.m_use;
-        } else {
-          l_g = l_g * u.factor + sum;
-          m_g = u.m_use;
-        }
       } else {
-        uint32_t zero[16];
+        release_s();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) zero[i] = 0u;
-#pragma unroll
-        for (int g = 0; g < kKeys / 32; ++g) tmem_st16(t_s + 16 * g, zero);
+        for (int i = 0; i < kKeys / 2; ++i) pk[i] = 0u;   // a zero P block: no key of this plane is in range
       }
+      // The P buffer is free, and O may be rescaled, once PV(ch - 1) has completed.
+      if (ch >= 1) {
+        ok = wait_pfree(ch - 1);
+        if (!ok) break;
+      }
+      if (rescale) rescale_span<kColO, D>(factor, t_tile);
+      st_span<G::kColP, kKeys / 2>(t_tile, pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kPReady + buf));
+      if (lane == 0) mbar_arrive(bar(kPFull));
     }
     // ---- epilogue: normalise the global branch, mix, store through the row map
     if (ok) ok = wait_warp(bar(kOReady), 0);
     if (ok) {
       uint32_t og[D];
-#pragma unroll
-      for (int c = 0; c < D / 16; ++c) tmem_ld16(t_o + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(og + 16 * c));
+      ld_span<kColO, D>(t_tile, og);
       tmem_wait_ld();
       if (row_ok) {
         int64_t rr = ((int64_t)zq * p.Y + yq) * p.X + xq;
@@ -647,6 +750,7 @@ int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
   p.lse_l = a.lse_l;
   p.lse_g = a.lse_g;
   p.y_rows = a.y_rows;
+  p.kbound = a.summary_bound;
   const int64_t units = (int64_t)bh * p.tiles_z * p.tiles_y * p.tiles_x;
   if (units <= 0) return P3D_OK;
   if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");
@@ -658,7 +762,51 @@ int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
   return P3D_OK;
 }
 
+// bound[bg] = max_j |sk[bg, j, :]| for the fixed-reference global softmax: one block per
+// (batch, kv-head), a thread per summary row, squared norms in fp32 and a block maximum.  The
+// norm is rounded up by 2^-10 so that rounding in the norm cannot put it below a score.
+template <bool BF16>
+__global__ void __launch_bounds__(1024) summary_bound_kernel(const uint32_t *sk, int M, int D, float *bound) {
+  __shared__ float part[32];
+  const uint32_t *base = sk + (int64_t)blockIdx.x * M * (D / 2);
+  float best = 0.f;
+  for (int j = threadIdx.x; j < M; j += blockDim.x) {
+    const uint32_t *row = base + (int64_t)j * (D / 2);
+    float acc = 0.f;
+    for (int d = 0; d < D / 2; ++d) {
+      const float2 f = unpack2<BF16>(row[d]);
+      acc = fmaf(f.x, f.x, acc);
+      acc = fmaf(f.y, f.y, acc);
+    }
+    best = fmaxf(best, acc);
+  }
+  for (int o = 16; o; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    best = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
+    for (int o = 16; o; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if (threadIdx.x == 0) bound[blockIdx.x] = sqrtf(best) * (1.f + 1.f / 1024.f);
+  }
+}
+
 }  // namespace
+
+int launch_summary_bound(const void *sk, int dtype, int bg, int summaries, int head_dim, float *bound,
+                         cudaStream_t stream) {
+  if (dtype != P3D_BF16 && dtype != P3D_F16) return fail(P3D_ERR_UNSUPPORTED, "summary bound: 16-bit summaries only");
+  if (head_dim < 2 || head_dim % 2 || summaries < 1 || bg < 1)
+    return fail(P3D_ERR_INVALID_ARGUMENT, "summary bound: bad shape");
+  if (((uintptr_t)sk & 3) != 0) return fail(P3D_ERR_INVALID_ARGUMENT, "summary bound: misaligned summaries");
+  const int threads = summaries >= 1024 ? 1024 : (summaries + 31) / 32 * 32;
+  const uint32_t *src = static_cast<const uint32_t *>(sk);
+  if (dtype == P3D_BF16)
+    summary_bound_kernel<true><<<bg, threads, 0, stream>>>(src, summaries, head_dim, bound);
+  else
+    summary_bound_kernel<false><<<bg, threads, 0, stream>>>(src, summaries, head_dim, bound);
+  P3D_LAUNCH_CHECK();
+  return P3D_OK;
+}
 
 bool stencil_fwd_supported(int dtype, int head_dim, const int radius[3], int summaries) {
   if (dtype != P3D_BF16 && dtype != P3D_F16) return false;

@@ -254,7 +254,16 @@ def slab_forward(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, geometry
     op, keep = _operator(q, kl_ext, vl_ext, kl_ext, vl_ext, w32, b32, gate, sl32, sg32, geometry, temperature)
     if geometry.stencil is None or op.raster_to_packed:
         raise ValueError("slab forward needs the complete stencil of a raster-stored slab")
-    slab = _native.Slab(slabs.grid[0], slabs.z0, slabs.halo_z0, slabs.halo_planes, sk.shape[2])
+    # per-(batch, kv-head) bound of the gathered summaries' norms: the forward's fixed-reference
+    # global softmax (a score bound per query row, no running maximum)
+    g = sk.shape[1]
+    bound = torch.empty(b * g, dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):
+        _native.check(_native.lib().p3d_summary_bound(_native.ptr(sk), _native.DTYPE_CODE[sk.dtype], b, g, sk.shape[2],
+                                                      d, _native.ptr(bound), _native.stream_of(q.device)),
+                      "p3d_summary_bound")
+    slab = _native.Slab(slabs.grid[0], slabs.z0, slabs.halo_z0, slabs.halo_planes, sk.shape[2],
+                        ctypes.c_void_p(bound.data_ptr()))
     if y_rows:
         y = torch.empty((b, n, h, d), dtype=q.dtype, device=q.device).transpose(1, 2)
     else:

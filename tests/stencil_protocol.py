@@ -78,6 +78,7 @@ class State:
     stage_landed: dict = field(default_factory=dict)  # stage -> chunk whose copy landed
     p_stored: dict = field(default_factory=dict)     # (tile, chunk) -> warps that stored P
     pv_issued: set = field(default_factory=set)
+    s_loaded: dict = field(default_factory=dict)     # chunk -> softmax warps that loaded S
 
     def bar(self, name):
         return self.bars[name]
@@ -521,9 +522,12 @@ def run_gkv(n_chunks=10, stages=4, seed=0, max_steps=400000):
 
 
 # --------------------------------------------------------------- forward, one tile per CTA
-# Model of the shipped stencil_fwd_kernel: one 128-row tile, two S buffers; S(0), S(1)
-# commit to sready[c], S(c >= 2) to empty[(c-2) % stages], which the producer (stage
-# release) and the softmax warps (S ready) both wait on.
+# Model of the shipped stencil_fwd_kernel: one 128-row tile per CTA with a single S buffer
+# and a separate P buffer in TMEM, four softmax warps (one per 32-row quarter).  S(c)
+# commits to sfull; the softmax warps arrive on sfree once they have loaded S(c) into
+# registers, and S(c + 1) may then overwrite it; they arrive on pfull once P(c) is stored;
+# PV(c) commits to pfree (P buffer reusable, O quiet) and to empty[c % stages] (the ring
+# stage of chunk c released to the producer).
 
 def fwd1_producer(state):
     k = state.stages
@@ -543,7 +547,7 @@ def fwd1_producer(state):
         yield ("step", None)
 
 
-def fwd1_mma(state):
+def fwd1_mma(state, skip_sfree=False):
     k, n = state.stages, state.n_chunks
 
     def commit(name):
@@ -556,84 +560,90 @@ def fwd1_mma(state):
     def issue_s(ch):
         if state.stage_landed.get(ch % k) != ch:
             raise ProtocolError(f"S({ch}) reads stage {ch % k} before chunk {ch} landed")
-        if ch >= 2 and ("PV", 0, ch - 2) not in state.mma_done:
-            raise ProtocolError(f"S({ch}) overwrites P of chunk {ch - 2} before PV({ch - 2}) completed")
+        if ch >= 1 and len(state.s_loaded.get(ch - 1, ())) != WARPS:
+            raise ProtocolError(f"S({ch}) overwrites S({ch - 1}) before the softmax warps loaded it")
         state.mma_queue.append(("S", 0, ch))
-        commit(f"empty{(ch - 2) % k}" if ch >= 2 else f"sready{ch}")
+        commit("sfull")
 
     yield from waits("qfull", 0)
-    for ch in range(min(2, n)):
-        yield from waits(f"full{ch % k}", ch // k)
-        issue_s(ch)
+    if n:
+        yield from waits("full0", 0)
+        issue_s(0)
         yield ("step", None)
     for c in range(n):
-        yield from waits(f"pready{c & 1}", c >> 1)
-        if len(state.p_stored.get((0, c), ())) != 4:
-            raise ProtocolError(f"PV({c}) issued before all four warps stored P")
+        if c + 1 < n:
+            yield from waits(f"full{(c + 1) % k}", (c + 1) // k)
+            if not skip_sfree:
+                yield from waits("sfree", c)
+            issue_s(c + 1)
+            yield ("step", None)
+        yield from waits("pfull", c)
+        if len(state.p_stored.get((0, c), ())) != WARPS:
+            raise ProtocolError(f"PV({c}) issued before all softmax warps stored P")
         state.mma_queue.append(("PV", 0, c))
         state.pv_issued.add((0, c))
-        commit(f"pvdone{c & 1}")
-        yield ("step", None)
-        if c + 2 >= n:
-            continue
-        yield from waits(f"full{(c + 2) % k}", (c + 2) // k)
-        yield from waits(f"pvdone{c & 1}", c >> 1)
-        issue_s(c + 2)
+        commit("pfree")
+        commit(f"empty{c % k}")
         yield ("step", None)
     commit("oready")
     commit("drain")
     yield from waits("drain", 0)
 
 
+WARPS = 4
+
+
 def fwd1_softmax(state, w, rng):
-    k, n = state.stages, state.n_chunks
+    n = state.n_chunks
 
     def waits(name, completion):
         while not _wait(state, name, completion & 1, completion):
             yield ("wait", name)
 
     def pv_done(c):
-        yield from waits(f"pvdone{c & 1}", c >> 1)
+        yield from waits("pfree", c)
         if ("PV", 0, c) not in state.mma_done:
-            raise ProtocolError(f"O touched before PV({c}) completed")
+            raise ProtocolError(f"P buffer or O touched before PV({c}) completed")
         if (0, c + 1) in state.pv_issued:
             raise ProtocolError(f"O touched after PV({c + 1}) was issued")
 
     for ch in range(n):
         if ch == LOCAL_CHUNKS:
-            yield from pv_done(LOCAL_CHUNKS - 1)
-        if ch >= 2:
-            yield from waits(f"empty{(ch - 2) % k}", (ch - 2) // k)
-        else:
-            yield from waits(f"sready{ch}", 0)
+            yield from pv_done(LOCAL_CHUNKS - 1)       # park the local output, free O
+        yield from waits("sfull", ch)
         if ("S", 0, ch) not in state.mma_done:
             raise ProtocolError(f"S({ch}) read before it completed")
+        if ("S", 0, ch + 1) in state.mma_done:
+            raise ProtocolError(f"S({ch}) overwritten before this warp loaded it")
+        state.s_loaded.setdefault(ch, set()).add(w)
+        state.bar("sfree").arrive()
         yield ("step", None)
+        if ch >= 1:
+            yield from pv_done(ch - 1)                 # P buffer free; O may be rescaled now
+            if rng.random() < 0.3:
+                yield ("step", None)                   # a data-dependent rescale of O
         state.p_stored.setdefault((0, ch), set()).add(w)
-        if ch not in (0, LOCAL_CHUNKS) and rng.random() < 0.3:  # data-dependent rescale of O
-            yield from pv_done(ch - 1)
-        state.bar(f"pready{ch & 1}").arrive()
+        state.bar("pfull").arrive()
         yield ("step", None)
     yield from waits("oready", 0)
     if ("PV", 0, n - 1) not in state.mma_done:
         raise ProtocolError("O read before the last PV completed")
 
 
-def run_fwd(n_chunks=14, stages=4, seed=0, max_steps=400000):
-    """Replay one random interleaving of the (one-tile) forward kernel's protocol."""
+def run_fwd(n_chunks=14, stages=4, seed=0, max_steps=400000, skip_sfree=False):
+    """Replay one random interleaving of the (one-tile) forward kernel's protocol.
+
+    ``skip_sfree`` replays a broken variant whose MMA thread overwrites S without waiting
+    for the softmax warps to load it."""
     rng = random.Random(seed)
     state = State(n_chunks=n_chunks, stages=stages)
-    bars = {"qfull": 1, "drain": 1, "oready": 1}
+    bars = {"qfull": 1, "drain": 1, "oready": 1, "sfull": 1, "sfree": WARPS, "pfull": WARPS, "pfree": 1}
     for s in range(4):
         bars[f"full{s}"] = 1
         bars[f"empty{s}"] = 1
-    for b in range(2):
-        bars[f"sready{b}"] = 1
-        bars[f"pready{b}"] = 4
-        bars[f"pvdone{b}"] = 1
     state.bars = {name: Barrier(name, cnt) for name, cnt in bars.items()}
     state.bar("qfull").arrive(tx=0)
-    roles = {"producer": fwd1_producer(state), "mma": fwd1_mma(state)}
-    for w in range(4):
+    roles = {"producer": fwd1_producer(state), "mma": fwd1_mma(state, skip_sfree)}
+    for w in range(WARPS):
         roles[f"softmax{w}"] = fwd1_softmax(state, w, random.Random(rng.random()))
     return _schedule(state, roles, rng, max_steps)

@@ -17,6 +17,17 @@ def test_forward_protocol_holds_under_random_interleavings(stages, n_chunks):
         sp.run_fwd(n_chunks=n_chunks, stages=stages, seed=seed)
 
 
+def test_model_rejects_overwriting_s_before_the_warps_load_it():
+    failures = 0
+    for seed in range(100):
+        try:
+            sp.run_fwd(n_chunks=12, stages=4, seed=seed, skip_sfree=True)
+        except sp.ProtocolError as err:
+            assert "before the softmax warps loaded it" in str(err) or "overwritten before" in str(err)
+            failures += 1
+    assert failures > 0
+
+
 def test_two_tile_protocol_with_release_barriers_holds():
     """The earlier two-tile forward, repaired with per-stage release barriers."""
     for seed in range(100):
