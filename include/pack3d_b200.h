@@ -51,6 +51,15 @@ typedef enum { P3D_F32 = 0, P3D_F16 = 1, P3D_BF16 = 2 } p3d_dtype;
 #define P3D_FWD_FORCE_INDEXED 2u /* use the indexed (neighbour-table) kernels even on a stencil */
 #define P3D_FWD_SUMMARIES_GIVEN 4u /* sk, sv already hold the pooled summaries: skip stage (b) */
 #define P3D_FWD_Y_ROWS 8u /* write y token-major, [B,N,H,D] (the layout to_out reads), not [B,H,N,D] */
+/* q, kl, vl are stored in raster order (rows at each token's raster index; p3d_qkv_split with
+ * P3D_SPLIT_RASTER_QKV) although the layout is permuted: the tensor-core forward reads them as
+ * they are instead of gathering raster copies.  Needs the tensor-core path
+ * (p3d_stencil_fwd_supported); y, gate and the saved state keep the layout's row order. */
+#define P3D_FWD_RASTER_QKV 16u
+
+/* p3d_qkv_split flags: write q, kl, vl at each token's raster index (z * ey + y) * ex + x of its
+ * coordinates (the extents must then be the token grid); kg, vg keep the token rows. */
+#define P3D_SPLIT_RASTER_QKV 1u
 
 /* Static description string of a status code. */
 P3D_API const char *p3d_strerror(int status);
@@ -111,7 +120,8 @@ P3D_API int p3d_layer_norm(const void *x, const void *weight, const void *bias, 
                    int dim, float eps, void *stream);
 P3D_API int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl, void *vl, void *kg, void *vg,
                   int dtype, int batch, int heads, int kv_heads, int tokens, int head_dim, const int64_t *coords,
-                  int pz, int py, int px, const float *phases, int ez, int ey, int ex, void *stream);
+                  int pz, int py, int px, const float *phases, int ez, int ey, int ex, unsigned flags,
+                  void *stream);
 
 /*
  * p3d_qkv_project: the projections and the split in one kernel -- the two nn.Linear calls of
@@ -207,6 +217,11 @@ typedef struct {
 P3D_API int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, void *og, float *lse_l,
                  float *lse_g, unsigned flags, void *workspace, size_t workspace_bytes, void *stream);
 P3D_API size_t p3d_attn_fwd_workspace(const p3d_operator *op, unsigned flags);
+
+/* 1 when p3d_attn_fwd runs the tensor-core stencil kernel for these properties of a complete
+ * stencil (16-bit dtype, head_dim 16/32/48/64, radius 1 or 2 on all axes, at least one
+ * summary, an sm_100 device current), else 0.  No reference counterpart. */
+P3D_API int p3d_stencil_fwd_supported(int dtype, int head_dim, int rz, int ry, int rx, int summaries);
 
 /*
  * bound[b*G + g] = max over the summaries j of |sk[b, g, j, :]| (fp32 Euclidean norm, rounded

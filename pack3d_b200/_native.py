@@ -19,6 +19,8 @@ FWD_SAVE_STATE = 1
 FWD_FORCE_INDEXED = 2
 FWD_SUMMARIES_GIVEN = 4
 FWD_Y_ROWS = 8
+FWD_RASTER_QKV = 16
+SPLIT_RASTER_QKV = 1
 OPT_INDEXED_ONLY = 1
 OPT_DY_ROWS = 2
 
@@ -62,7 +64,7 @@ _SIGNATURES = {
                           _c_int, _c_int, _vp]),
     "p3d_layer_norm": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_i64, _c_int, _c_f32, _vp]),
     "p3d_qkv_split": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
-                               _vp, _c_int, _c_int, _c_int, _vp, _c_int, _c_int, _c_int, _vp]),
+                               _vp, _c_int, _c_int, _c_int, _vp, _c_int, _c_int, _c_int, ctypes.c_uint, _vp]),
     "p3d_qkv_project_supported": (_c_int, [_c_int] * 5),
     "p3d_qkv_project": (_c_int, [_vp] * 8 + [_c_int] * 7 + [_vp] + [_c_int] * 3 + [_vp] + [_c_int] * 3 + [_vp]),
     "p3d_qkv_merge": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
@@ -79,6 +81,7 @@ _SIGNATURES = {
                               _vp, ctypes.c_size_t, _vp]),
     "p3d_attn_fwd_workspace": (ctypes.c_size_t, [ctypes.POINTER(Operator), ctypes.c_uint]),
     "p3d_summary_bound": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp]),
+    "p3d_stencil_fwd_supported": (_c_int, [_c_int] * 6),
     "p3d_attn_fwd_noalloc": (_c_int, [ctypes.POINTER(Operator), _vp, _vp, _vp, _vp]),
     "p3d_attn_fwd_slab": (_c_int, [ctypes.POINTER(Operator), ctypes.POINTER(Slab), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                    ctypes.c_uint, _vp]),

@@ -148,11 +148,16 @@ class PACK3DAttention(nn.Module):
         projection outputs into rotated q / kl / kg and head-major vl / vg; the core writes
         its output token-major so the output projection reads it without a transpose copy.
         """
-        from .ops import forward as core_forward
-        b, n = x.shape[0], x.shape[1]
-        x, q, kl, vl, kg, vg, gate = self._inference_glue(x, layout.coords, layout.grid_shape)
+        from .ops import forward as core_forward, raster_qkv_applies
+        # permuted storage (Morton blocks): the split writes q, kl, vl at raster rows, so the
+        # tensor-core stencil kernel reads them without a gather pass
+        extents = tuple(int(e) for e in layout.grid_shape)
+        raster = (not self.fused_projection and phase_tables(x.device, balanced_pairs(self.head_dim), extents)[1]
+                  is not None and raster_qkv_applies(layout.geometry, x.dtype, self.head_dim, x.device))
+        x, q, kl, vl, kg, vg, gate = self._inference_glue(x, layout.coords, layout.grid_shape, raster_qkv=raster)
         y, _ = core_forward(q, kl, vl, kg, vg, self.pool_weight, self.slot_bias, gate, self.local_scale,
-                            self.global_scale, layout.geometry, self.temperature, save_state=False, y_rows=True)
+                            self.global_scale, layout.geometry, self.temperature, save_state=False, y_rows=True,
+                            raster_qkv=raster)
         return self._out_residual(x, y)
 
     def _out_residual(self, x, y_rows):
@@ -161,9 +166,11 @@ class PACK3DAttention(nn.Module):
         out = torch.addmm(x.reshape(b * n, self.dim), y_rows.transpose(1, 2).reshape(b * n, -1), self.to_out.weight.t())
         return out.view(b, n, self.dim)
 
-    def _inference_glue(self, x, coords, grid_shape):
+    def _inference_glue(self, x, coords, grid_shape, raster_qkv=False):
         """LayerNorm, projections, RoPE at ``coords`` (extents ``grid_shape``) and the gate of
-        the fused inference path: ``(x, q, kl, vl, kg, vg, gate)``, head-major."""
+        the fused inference path: ``(x, q, kl, vl, kg, vg, gate)``, head-major.  ``raster_qkv``
+        stores the rows of q, kl, vl at each token's raster index (the extents must be the
+        token grid)."""
         from . import _native
         from .rope import phase_tables
         b, n = x.shape[0], x.shape[1]
@@ -181,6 +188,8 @@ class PACK3DAttention(nn.Module):
         pairs = balanced_pairs(d)
         extents = tuple(int(e) for e in grid_shape)
         _, phases = phase_tables(dev, pairs, extents)
+        if raster_qkv and (phases is None or self.fused_projection):
+            raise ValueError("raster-ordered q, kl, vl come from p3d_qkv_split with a phase table")
         if phases is not None and self.fused_projection and glue.project_supported(xn, self.to_q.weight,
                                                                                   self.to_kv.weight, h, g, d):
             # projections, split and RoPE in one kernel: the projections never reach HBM
@@ -202,7 +211,8 @@ class PACK3DAttention(nn.Module):
             with torch.cuda.device(dev):
                 _native.check(lib.p3d_qkv_split(_native.ptr(qp), _native.ptr(kvp), _native.ptr(q), _native.ptr(kl),
                                                 _native.ptr(vl), _native.ptr(kg), _native.ptr(vg), code, b, h, g, n, d,
-                                                _native.ptr(coords), *pairs, _native.ptr(phases), *extents, stream),
+                                                _native.ptr(coords), *pairs, _native.ptr(phases), *extents,
+                                                _native.SPLIT_RASTER_QKV if raster_qkv else 0, stream),
                               "p3d_qkv_split")
         gate = self.gate(xn).reshape(b, n, h, 2).softmax(-1)[..., 1].transpose(1, 2).contiguous()
         return x, q, kl, vl, kg, vg, gate

@@ -162,7 +162,7 @@ size_t fwd_layout(const p3d_operator *op, unsigned flags, void *base, size_t cap
   const size_t kv_elems = (size_t)op->batch * op->kv_heads * op->tokens * op->head_dim;
   if (use_stencil_path(op, flags)) {
     *kbound = c.take<float>((size_t)op->batch * op->kv_heads);
-    if (op->raster_to_packed) {
+    if (op->raster_to_packed && !(flags & P3D_FWD_RASTER_QKV)) {
       *q_r = c.take<char>(q_elems * es);
       *kl_r = c.take<char>(kv_elems * es);
       *vl_r = c.take<char>(kv_elems * es);
@@ -367,6 +367,11 @@ size_t p3d_attn_fwd_workspace(const p3d_operator *op, unsigned flags) {
   return fwd_layout(op, flags, nullptr, 0, &a, &b, &c, &d, &e);
 }
 
+int p3d_stencil_fwd_supported(int dtype, int head_dim, int rz, int ry, int rx, int summaries) {
+  const int radius[3] = {rz, ry, rx};
+  return stencil_fwd_supported(dtype, head_dim, radius, summaries) ? 1 : 0;
+}
+
 int p3d_summary_bound(const void *sk, int dtype, int batch, int kv_heads, int summaries, int head_dim,
                       float *bound, void *stream) {
   P3D_CHECK_ARG(sk && bound, "p3d_summary_bound: null pointer");
@@ -380,8 +385,10 @@ int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, 
   if (int st = validate(op)) return st;
   P3D_CHECK_ARG(y && sk && sv, "p3d_attn_fwd: y, sk and sv are required");
   P3D_CHECK_ARG((flags & ~(unsigned)(P3D_FWD_SAVE_STATE | P3D_FWD_FORCE_INDEXED | P3D_FWD_SUMMARIES_GIVEN |
-                                     P3D_FWD_Y_ROWS)) == 0u,
+                                     P3D_FWD_Y_ROWS | P3D_FWD_RASTER_QKV)) == 0u,
                 "p3d_attn_fwd: unknown flags 0x%x", flags);
+  if ((flags & P3D_FWD_RASTER_QKV) && !use_stencil_path(op, flags))
+    return fail(P3D_ERR_UNSUPPORTED, "p3d_attn_fwd: raster-ordered q, kl, vl need the tensor-core stencil path");
   const bool save = flags & P3D_FWD_SAVE_STATE;
   P3D_CHECK_ARG(!save || (ol && og && lse_l && lse_g), "p3d_attn_fwd: saving state needs ol, og, lse_l, lse_g");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -411,7 +418,7 @@ int p3d_attn_fwd(const p3d_operator *op, void *y, void *sk, void *sv, void *ol, 
     a.q = op->q;
     a.kl = op->kl;
     a.vl = op->vl;
-    if (op->raster_to_packed) {
+    if (op->raster_to_packed && !(flags & P3D_FWD_RASTER_QKV)) {
       const size_t row_bytes = (size_t)op->head_dim * dtype_size(op->dtype);
       if (int st = gather_rows(op->q, q_r, op->raster_to_packed, (int64_t)op->batch * op->heads, op->tokens,
                                row_bytes, s))

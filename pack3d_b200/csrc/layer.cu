@@ -360,6 +360,8 @@ struct SplitParams {
   int pairs[3];
   int start[3];           // first phase-table entry of each axis
   const float *phases;    // (cos, sin) per (axis, coordinate, pair)
+  int raster_qkv;         // split: q, kl, vl rows at the token's raster index (ey x ex planes)
+  int ey, ex;
 };
 
 constexpr int kTokensPerWarp = 4;
@@ -422,7 +424,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) qkv_pass_kernel(SplitParams p)
     // offset in the projection rows, whether it rotates
     T *head[kBatch];
     int off[kBatch];
-    bool isq[kBatch], rot[kBatch], act[kBatch];
+    bool isq[kBatch], rot[kBatch], act[kBatch], to_raster[kBatch];
 #pragma unroll
     for (int i = 0; i < kBatch; ++i) {
       const int hr = base + i * kRows + sub;
@@ -433,11 +435,13 @@ __global__ void __launch_bounds__(kWarps * 32, 4) qkv_pass_kernel(SplitParams p)
         head[i] = static_cast<T *>(p.out[0]) + ((int64_t)b * p.heads + r) * p.tokens * D + 8 * grp;
         off[i] = r * D + 8 * grp;
         rot[i] = true;
+        to_raster[i] = true;
       } else {
         const int x = r - p.heads, part = x / p.kv_heads, g = x - part * p.kv_heads;  // 0 kl, 1 vl, 2 kg, 3 vg
         head[i] = pick<T>(p, part) + ((int64_t)b * p.kv_heads + g) * p.tokens * D + 8 * grp;
         off[i] = x * D + 8 * grp;
         rot[i] = (part & 1) == 0;
+        to_raster[i] = part <= 1;  // kl, vl (kg, vg stay in token order for the pooling)
       }
     }
     for (int t = 0; t < kTokensPerWarp; ++t) {
@@ -453,6 +457,8 @@ __global__ void __launch_bounds__(kWarps * 32, 4) qkv_pass_kernel(SplitParams p)
           raw[i] = *reinterpret_cast<const uint4 *>(MERGE ? head[i] + (int64_t)n * D : (isq[i] ? qrow : kvrow) + off[i]);
       }
       const int64_t c[3] = {p.coords[3 * (int64_t)n], p.coords[3 * (int64_t)n + 1], p.coords[3 * (int64_t)n + 2]};
+      // destination row of q, kl, vl: the token's row, or its raster index for the raster form
+      const int64_t nr = (!MERGE && p.raster_qkv) ? (c[0] * p.ey + c[1]) * p.ex + c[2] : n;
       float2 cs[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -472,7 +478,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) qkv_pass_kernel(SplitParams p)
             v[2 * j + 1] = __fadd_rn(__fmul_rn(even, cs[j].y), __fmul_rn(odd, cs[j].x));
           }
         }
-        store8<T>(MERGE ? (isq[i] ? qrow : kvrow) + off[i] : head[i] + (int64_t)n * D, v);
+        store8<T>(MERGE ? (isq[i] ? qrow : kvrow) + off[i] : head[i] + (to_raster[i] ? nr : (int64_t)n) * D, v);
       }
     }
   }
@@ -672,11 +678,15 @@ extern "C" int p3d_layer_norm_bwd(const void *x, const void *weight, const void 
 extern "C" int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl, void *vl, void *kg, void *vg,
                              int dtype, int batch, int heads, int kv_heads, int tokens, int head_dim,
                              const int64_t *coords, int pz, int py, int px, const float *phases, int ez, int ey,
-                             int ex, void *stream) {
+                             int ex, unsigned flags, void *stream) {
   const void *const ptrs[7] = {qp, kvp, q, kl, vl, kg, vg};
   if (int st = check_split("p3d_qkv_split", ptrs, dtype, batch, heads, kv_heads, tokens, head_dim, coords, pz, py,
                            px, phases, ez, ey, ex))
     return st;
+  P3D_CHECK_ARG((flags & ~P3D_SPLIT_RASTER_QKV) == 0u, "p3d_qkv_split: unknown flags 0x%x", flags);
+  P3D_CHECK_ARG(!(flags & P3D_SPLIT_RASTER_QKV) || (int64_t)ez * ey * ex == tokens,
+                "p3d_qkv_split: raster rows need the coordinate extents to be the token grid (%d x %d x %d != %d)",
+                ez, ey, ex, tokens);
   if ((int64_t)batch * tokens == 0) return P3D_OK;
   SplitParams p{};
   p.qp = qp;
@@ -698,6 +708,9 @@ extern "C" int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl,
   p.start[1] = ez * pz;
   p.start[2] = ez * pz + ey * py;
   p.phases = phases;
+  p.raster_qkv = (flags & P3D_SPLIT_RASTER_QKV) ? 1 : 0;
+  p.ey = ey;
+  p.ex = ex;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return dtype == P3D_BF16 ? launch_split<__nv_bfloat16>(p, head_dim, s) : launch_split<__half>(p, head_dim, s);
 }

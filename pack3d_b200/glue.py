@@ -73,7 +73,7 @@ class _QKVSplit(torch.autograd.Function):
             _native.check(_native.lib().p3d_qkv_split(
                 _native.ptr(qp), _native.ptr(kvp), _native.ptr(q), _native.ptr(kl), _native.ptr(vl), _native.ptr(kg),
                 _native.ptr(vg), _native.DTYPE_CODE[dt], b, heads, kv_heads, n, head_dim, _native.ptr(coords), *pairs,
-                _native.ptr(phases), *extents, _native.stream_of(dev)), "p3d_qkv_split")
+                _native.ptr(phases), *extents, 0, _native.stream_of(dev)), "p3d_qkv_split")
         ctx.save_for_backward(coords, phases)
         ctx.meta = (pairs, extents, heads, kv_heads, head_dim, b, n, dt)
         return q, kl, vl, kg, vg

@@ -70,13 +70,27 @@ def _as_gate(gate, q):
     return gate if gate.dtype in _GATE_DTYPES else gate.to(torch.float32)
 
 
+def raster_qkv_applies(geometry, dtype, head_dim, device):
+    """True when the layout stores tokens out of raster order and the tensor-core stencil
+    forward runs for it: q, kl, vl may then be produced at raster rows (``p3d_qkv_split``
+    with ``SPLIT_RASTER_QKV``) and handed to :func:`forward` with ``raster_qkv=True``."""
+    if geometry.stencil is None or geometry._stencil_map is None or dtype not in (torch.bfloat16, torch.float16):
+        return False
+    _, radius = geometry.stencil
+    with torch.cuda.device(device):
+        return bool(_native.lib().p3d_stencil_fwd_supported(_native.DTYPE_CODE[dtype], int(head_dim), *radius,
+                                                            geometry.num_summaries))
+
+
 def forward(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature, *, save_state=True,
-            force_indexed=False, summaries=None, y_rows=False):
+            force_indexed=False, summaries=None, y_rows=False, raster_qkv=False):
     """Launch the forward; returns ``(y, (sk, sv, ol, og, lse_l, lse_g))`` (empty state when not saving).
 
     ``summaries=(sk, sv)`` supplies already pooled summaries and runs stage (c) alone.
     ``y_rows`` writes y token-major: the result is a [B, H, N, D] view of a [B, N, H, D]
     tensor, so ``y.transpose(1, 2).reshape(B, N, H * D)`` needs no copy.
+    ``raster_qkv``: q, kl, vl hold their rows at raster positions (see :func:`raster_qkv_applies`);
+    kg, vg, gate and y keep the layout's row order.
     """
     b, h, n, d = q.shape
     g = kl.shape[1]
@@ -88,6 +102,7 @@ def forward(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, temperature
     y = empty(b, n, h, d).permute(0, 2, 1, 3) if y_rows else empty(b, h, n, d)
     flags = (_native.FWD_SAVE_STATE if save_state else 0) | (_native.FWD_FORCE_INDEXED if force_indexed else 0)
     flags |= _native.FWD_Y_ROWS if y_rows else 0
+    flags |= _native.FWD_RASTER_QKV if raster_qkv else 0
     if summaries is None:
         sk, sv = empty(b, g, m, d), empty(b, g, m, d)
     else:

@@ -160,3 +160,28 @@ def test_config2_morton_storage_is_the_permuted_raster_result(cuda_device, dtype
         assert torch.equal(g_m[i], g_r[i]), name
     for i, name in ((8, "dlocal_scale"), (9, "dglobal_scale")):
         torch.testing.assert_close(g_m[i], g_r[i], atol=1e-3, rtol=1e-4, msg=name)
+
+
+def test_config2_morton_layer_inference_is_the_permuted_raster_layer(cuda_device):
+    """BASELINE config 2 through the layer call the benchmark times: the 64^3 field in Morton
+    storage, where the projection split writes q, kl, vl at raster rows and the tensor-core
+    kernel reads them without a gather pass, gives the raster layer's output permuted, bit for
+    bit (LayerNorm, the projections and the output GEMM are per-row; the pooled summaries visit
+    each block's slots in the same order in both layouts)."""
+    from pack3d_b200 import ops as p3d_ops
+    grid = (64, 64, 64)
+    raster, morton = _layout(grid), _layout(grid, raster=False)
+    assert p3d_ops.raster_qkv_applies(morton.geometry, torch.bfloat16, 48, cuda_device)
+    assert not p3d_ops.raster_qkv_applies(raster.geometry, torch.bfloat16, 48, cuda_device)
+    torch.manual_seed(0)
+    layer = PACK3DAttention(192, heads=4, kv_heads=4, head_dim=48, block_volume=64).to(torch.bfloat16)
+    layer = layer.to(cuda_device)
+    x = torch.randn(1, 64 ** 3, 192, generator=torch.Generator().manual_seed(201)).to(torch.bfloat16)
+    p = morton.order.to(cuda_device)       # Morton row i holds raster token p[i]
+    x = x.to(cuda_device)
+    with torch.inference_mode():
+        y_r = layer(x, raster.to(cuda_device))
+        y_m = layer(x[:, p].contiguous(), morton.to(cuda_device))
+    torch.cuda.synchronize()
+    assert _native.device_errors() == 0
+    assert torch.equal(y_m, y_r[:, p])

@@ -31,7 +31,7 @@ def test_qkv_split_matches_rotation_and_copies(cuda_device, dtype, h, g, d):
     with torch.cuda.device(cuda_device):
         _native.check(_native.lib().p3d_qkv_split(
             _native.ptr(qp), _native.ptr(kvp), *[_native.ptr(t) for t in outs], _native.DTYPE_CODE[dtype], b, h, g, n,
-            d, _native.ptr(coords), *pairs, _native.ptr(phases), *extents, _native.stream_of(cuda_device)),
+            d, _native.ptr(coords), *pairs, _native.ptr(phases), *extents, 0, _native.stream_of(cuda_device)),
             "p3d_qkv_split")
     q, kl, vl, kg, vg = outs
     chunks = [t.reshape(b, n, g, d).transpose(1, 2) for t in kvp.chunk(4, -1)]
@@ -39,6 +39,45 @@ def test_qkv_split_matches_rotation_and_copies(cuda_device, dtype, h, g, d):
                                       pairs, extents, packed=False)
     assert torch.equal(q, wq) and torch.equal(kl, wkl) and torch.equal(kg, wkg)
     assert torch.equal(vl, chunks[1].contiguous()) and torch.equal(vg, chunks[3].contiguous())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("h,g,d", [(4, 4, 48), (2, 1, 32)])
+def test_qkv_split_raster_rows_are_the_token_rows_permuted(cuda_device, dtype, h, g, d):
+    """SPLIT_RASTER_QKV puts each token's q, kl, vl at its raster index and leaves kg, vg in
+    token order: the same values as the plain split, with q, kl, vl rows permuted."""
+    layout = _layout((8, 12, 16), raster=False).to(cuda_device)
+    b, n = 2, layout.geometry.num_tokens
+    gen = torch.Generator(device=cuda_device).manual_seed(7 * h + d)
+    qp = torch.randn(b, n, h * d, device=cuda_device, generator=gen).to(dtype)
+    kvp = torch.randn(b, n, 4 * g * d, device=cuda_device, generator=gen).to(dtype)
+    pairs = balanced_pairs(d)
+    extents = layout.grid_shape
+    _, phases = phase_tables(cuda_device, pairs, extents)
+    coords = layout.coords.contiguous()
+    results = []
+    for flags in (0, _native.SPLIT_RASTER_QKV):
+        outs = [torch.empty((b, h, n, d), dtype=dtype, device=cuda_device)]
+        outs += [torch.empty((b, g, n, d), dtype=dtype, device=cuda_device) for _ in range(4)]
+        with torch.cuda.device(cuda_device):
+            _native.check(_native.lib().p3d_qkv_split(
+                _native.ptr(qp), _native.ptr(kvp), *[_native.ptr(t) for t in outs], _native.DTYPE_CODE[dtype], b, h,
+                g, n, d, _native.ptr(coords), *pairs, _native.ptr(phases), *extents, flags,
+                _native.stream_of(cuda_device)), "p3d_qkv_split")
+        results.append(outs)
+    plain, raster = results
+    c = coords
+    row = (c[:, 0] * extents[1] + c[:, 1]) * extents[2] + c[:, 2]      # raster index of token row i
+    for i, name in enumerate(("q", "kl", "vl")):
+        assert torch.equal(raster[i][:, :, row], plain[i]), name
+    for i, name in ((3, "kg"), (4, "vg")):
+        assert torch.equal(raster[i], plain[i]), name
+    # the raster form needs the extents to be the token grid
+    with pytest.raises(ValueError, match="token grid"):
+        _native.check(_native.lib().p3d_qkv_split(
+            _native.ptr(qp), _native.ptr(kvp), *[_native.ptr(t) for t in plain], _native.DTYPE_CODE[dtype], b, h, g,
+            n, d, _native.ptr(coords), *pairs, _native.ptr(phases), extents[0] + 1, extents[1], extents[2],
+            _native.SPLIT_RASTER_QKV, _native.stream_of(cuda_device)), "p3d_qkv_split")
 
 
 @pytest.mark.parametrize("dim", [192, 384, 64, 128, 256, 40])

@@ -29,7 +29,8 @@ def _unfused(x, wq, wkv, coords, pairs, phases, extents, b, n, h, g, d):
     outs += [torch.empty((b, g, n, d), dtype=x.dtype, device=x.device) for _ in range(4)]
     _native.check(_native.lib().p3d_qkv_split(
         _native.ptr(qp), _native.ptr(kvp), *[_native.ptr(t) for t in outs], _native.DTYPE_CODE[x.dtype], b, h, g, n,
-        d, _native.ptr(coords), *pairs, _native.ptr(phases), *extents, _native.stream_of(x.device)), "p3d_qkv_split")
+        d, _native.ptr(coords), *pairs, _native.ptr(phases), *extents, 0, _native.stream_of(x.device)),
+        "p3d_qkv_split")
     return outs
 
 

@@ -119,7 +119,7 @@ def test_argument_checks_run_before_any_device_call():
     assert lib.p3d_qkv_project_supported(_native.BF16, 192, 4, 4, 40) == 0
     # p3d_qkv_split: heads not a multiple of kv_heads
     st = lib.p3d_qkv_split(dummy, dummy, dummy, dummy, dummy, dummy, dummy, _native.BF16, 1, 5, 3, 64, 48, dummy,
-                           8, 8, 8, dummy, 4, 4, 4, None)
+                           8, 8, 8, dummy, 4, 4, 4, 0, None)
     assert st == 1 and b"head" in lib.p3d_last_error()
     # p3d_pool_fwd: more than 64 slots per fine block
     st = lib.p3d_pool_fwd(dummy, dummy, dummy, dummy, dummy, 4, 65, 1, dummy, dummy, None, None, _native.BF16, 1, 1,
