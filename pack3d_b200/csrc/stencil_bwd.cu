@@ -56,12 +56,8 @@ struct BGeo {
   static constexpr int kKeys = (kWin + 31) / 32 * 32;   // 96, 64
   static constexpr int kLocalChunks = kHZ;              // 8, 6
   static constexpr int kSumRows = kKeys;
-  static constexpr int kHalf = kKeys / 2;               // query columns per softmax warp (dK / dV)
-  static_assert(kKeys % 32 == 0 && kHalf % 16 == 0, "chunk width must suit the MMA and TMEM shapes");
+  static_assert(kKeys % 32 == 0, "chunk width must suit the MMA and TMEM shapes");
 };
-constexpr int kThreads = 320;
-constexpr int kProducerWarp = 8, kMmaWarp = 9;
-constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -254,15 +250,12 @@ __global__ void __launch_bounds__(kDqThreads, 2)
     }
   } else if (warp == kDqMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
+    // Lane 0 issues (measured 0.15 ms faster here than the warp-wide elected form the dK / dV
+    // kernels use).
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(128, kKeys, BF16, false);  // S and dP: N = kKeys, K-major B
       constexpr uint32_t idesc_dq = idesc_f16(128, D, BF16, true);     // dQ: N = D, B = K read MN-major
-      uint32_t commits[kNumBars];
-      for (int i = 0; i < kNumBars; ++i) commits[i] = 0u;
-      auto commit = [&](int bidx) {
-        mma_commit(bar(bidx));
-        ++commits[bidx];
-      };
+      int n_s = 0, n_dp = 0, n_dq = 0;  // commits to kSReady, kDPReady, kDQDone (for the teardown)
       const uint64_t desc_q = desc_sw32(q_smem, 16, 256);
       const uint64_t desc_dol = desc_sw32(dol_smem, 16, 256), desc_dog = desc_sw32(dog_smem, 16, 256);
       const uint64_t desc_k = desc_sw32(ring, 16, 256);          // K / V chunks, K-major
@@ -272,24 +265,30 @@ __global__ void __launch_bounds__(kDqThreads, 2)
         const uint64_t bk = desc_k + stage_off(c);
 #pragma unroll
         for (int kk = 0; kk < C::kK; ++kk)
-          mma_ss(tmem + kColS, desc_q + kk * (C::kBoxQ >> 4), bk + kk * (C::kBoxK >> 4), idesc_s, kk > 0 ? 1u : 0u);
-        commit(kSReady);
+          mma_ss(tmem + kColS, desc_q + kk * (C::kBoxQ >> 4), bk + kk * (C::kBoxK >> 4), idesc_s,
+                      kk > 0 ? 1u : 0u);
+        mma_commit(bar(kSReady));
+        ++n_s;
       };
       auto issue_dp = [&](int c) {
         const uint64_t ad = c < kLocalChunks ? desc_dol : desc_dog;
         const uint64_t bv = desc_k + stage_off(c) + (C::kKeyBytes >> 4);
 #pragma unroll
         for (int kk = 0; kk < C::kK; ++kk)
-          mma_ss(tmem + kColDP, ad + kk * (C::kBoxQ >> 4), bv + kk * (C::kBoxK >> 4), idesc_s, kk > 0 ? 1u : 0u);
-        commit(kDPReady);
+          mma_ss(tmem + kColDP, ad + kk * (C::kBoxQ >> 4), bv + kk * (C::kBoxK >> 4), idesc_s,
+                      kk > 0 ? 1u : 0u);
+        mma_commit(bar(kDPReady));
+        ++n_dp;
       };
       auto issue_dq = [&](int c) {
         const uint64_t bk = desc_kmn + stage_off(c);
         const bool first = (c == 0) || (c == kLocalChunks);  // dQ restarts for the global branch
 #pragma unroll
         for (int j = 0; j < kKeys / 16; ++j)
-          mma_ts(tmem + kColDQ, tmem + kColDP + 8 * j, bk + j * (512 >> 4), idesc_dq, (first && j == 0) ? 0u : 1u);
-        commit(kDQDone);
+          mma_ts(tmem + kColDQ, tmem + kColDP + 8 * j, bk + j * (512 >> 4), idesc_dq,
+                      (first && j == 0) ? 0u : 1u);
+        mma_commit(bar(kDQDone));
+        ++n_dq;
       };
       auto wait_bar = [&](int bidx, int completion) -> bool {
         if (!mbar_wait(bar(bidx), completion & 1, &g_bwd_errors, kWaitNs, kErrMma)) return false;
@@ -325,9 +324,13 @@ __global__ void __launch_bounds__(kDqThreads, 2)
         mbar_arrive(bar(kEmpty + c % C::kStages));
         issue_dp(c + 1);
       }
-      commit(kDrain);
-      for (int i = 0; i < kNumBars; ++i)
-        if (commits[i]) mbar_wait(bar(i), (commits[i] - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+      // the drain commit's arrival means every operation completed; then each barrier's last
+      // commit has arrived or is about to
+      mma_commit(bar(kDrain));
+      mbar_wait(bar(kDrain), 0, &g_bwd_errors, kWaitNs, kErrTeardown);
+      if (n_s) mbar_wait(bar(kSReady), (n_s - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+      if (n_dp) mbar_wait(bar(kDPReady), (n_dp - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+      if (n_dq) mbar_wait(bar(kDQDone), (n_dq - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
@@ -550,55 +553,322 @@ int launch_dq_t(const StencilBwdArgs &a, cudaStream_t stream) {
 }
 
 
-// ============================================================================ global dSK / dSV
+// ============================================================================ dK / dV side
 //
-// Restates the summary-gradient half of the global branch (kernels.py:210-239): for a
-// tile of 128 summaries (TMEM lanes) and a stream of 128-query chunks (columns),
-//   S^T = SK Q^T, dP^T = SV dO_g^T, P^T = exp(S^T / sqrt(D) - lse), dS^T = P^T (dP^T - Delta) / sqrt(D)
-//   dSV += P^T dO_g,  dSK += dS^T Q          (P^T and dS^T rounded to the storage dtype)
-// over the query chunks of one split (the rounded dS^T operand is P^T (dP^T - Delta); the
-// 1/sqrt(D) multiplies the fp32 dSK accumulator once, when it is written); splits write fp32 partials [B*G, splits, M, D] that a
-// fixed-order reduction sums.  The global branch ignores the geometry, so this kernel serves
-// any token order.  Summary rows past M read zeros and are not written; query columns past
-// N get lse = +inf (P = 0).
+// Two kernels give the key-side gradients: global_dkv_tc_kernel (summaries, any token order)
+// and stencil_bwd_dkv_kernel (the local keys of a complete stencil).  Both put 128 keys (or
+// summaries) on the TMEM lanes and stream chunks of 32 queries as columns:
+//   S^T = K Q^T, dP^T = V dO^T, P^T = exp(S^T / sqrt(D) - lse), dS^T = P^T (dP^T - Delta),
+//   dV += P^T dO,  dK += dS^T Q        (the 1/sqrt(D) of dS multiplies dK once, at the end)
+// with P^T and dS^T rounded to the storage dtype for the products (the rounded dS^T operand
+// is P^T (dP^T - Delta); the rounding is relative, so it agrees within the dtype's rounding).
 //
-// TMEM: S^T [0, 128), dP^T [128, 256), P^T [256, 320), dS^T [320, 384) (16-bit pairs),
-// dSK [384, 384 + D), dSV [384 + D, 384 + 2D).  Eight softmax warps: warp w serves TMEM
-// lanes 32(w%4).. and query columns 64(w/4)..+64.  Per chunk the MMA thread issues S^T and
-// dP^T; the softmax warps pull them into registers and release the buffers (the next
-// chunk's S^T / dP^T start at once), then store P^T / dS^T once the previous chunk's dSV /
-// dSK products are done with them, and the MMA thread accumulates dSV and dSK.
-constexpr int kGRows = 128;   // summaries per tile
-constexpr int kGCols = 128;   // queries per chunk
-constexpr uint32_t kGColS = 0, kGColDP = 128, kGColP = 256, kGColDS = 320, kGColAcc = 384;
+// They run two CTAs per SM: the tensor cores are fed by one issuing warp per CTA, and
+// while one CTA's softmax warps work the other CTA's products run.  Each CTA holds 256 TMEM
+// columns: kKvBuf (S^T, dP^T) buffer pairs of kKvCols columns each, then the accumulators
+// dK [A, A + D), dV [A + D, A + 2D) (A = 2 kKvCols kKvBuf).  The softmax warps write P^T and
+// dS^T back over the S^T and dP^T buffer they read, as 16-bit pairs.  Chunk c uses buffer
+// c % kKvBuf.  Per chunk the MMA warp waits for P^T / dS^T of chunk c, issues its dV / dK
+// products, releases the chunk's ring stage, waits for those products to complete
+// (tcgen05.mma operations are ordered only when they share an accumulator, and S^T(c +
+// kKvBuf) overwrites P^T(c)), then issues S^T / dP^T of chunk c + kKvBuf.
+// tests/stencil_protocol.py (run_ip) replays this barrier protocol with the hardware's
+// parity semantics, tensor-core operations completing in order only per accumulator, and
+// the TMEM contents of every softmax warp.
+//
+// Roles: eight softmax warps (warp w serves TMEM lanes 32(w % 4).. and query columns
+// [W(w / 4), W(w / 4) + W) of a chunk, W = kKvCols / 2, its pairs written at the start of its
+// own column range, so it never overwrites scores another warp has still to load), the TMA
+// producer warp (query chunks by TMA, lse / Delta beside them), the MMA warp.  Every wait
+// is bounded.
+constexpr uint32_t kKvTmemCols = 256;
+constexpr int kKvCols = 64;          // queries per chunk
+constexpr int kKvBuf = 1;            // S^T / dP^T buffers
+constexpr int kKvSoft = 8;           // softmax warps
+constexpr int kKvW = 4 * kKvCols / kKvSoft;  // columns per softmax warp
+constexpr int kKvProducer = kKvSoft, kKvMma = kKvSoft + 1, kKvThreads = 32 * (kKvSoft + 2);
+constexpr int kKvMaxStages = 8;
+// Of every 8 exp2 pairs of a softmax warp, this many run as the degree-3 polynomial on the
+// FMA pipe (exp2_poly2, relative error < 1e-4, far below the 16-bit rounding of P) instead of
+// the MUFU: 0 / 2 / 3 / 4 measured 11.06 / 10.96 / 11.14 / 11.23 ms for the config-3 backward.
+constexpr int kKvPolyPairs = 2;
+static_assert(kKvW % 16 == 0, "a warp's columns must be whole groups of 16");
+static_assert(kKvCols <= 64, "the column masks are 64-bit");
+
+enum KvBar {
+  kVKvFull = 0,                            // the K and V (or SK and SV) tiles landed
+  kVFull = 1,                              // [stage]: query chunk copies (tx) + the producer's lse / Delta stores
+  kVEmpty = kVFull + kKvMaxStages,         // [stage]: committed after the dV / dK products of the chunk it held
+  kVSReady = kVEmpty + kKvMaxStages,       // [buffer]: S^T, dP^T of a chunk complete
+  kVPdsReady = kVSReady + kKvBuf,          // [buffer]: every softmax warp stored its P^T, dS^T of a chunk
+  kVAccDone = kVPdsReady + kKvBuf,         // [buffer]: the dV / dK products of a chunk complete
+  kVAccReady = kVAccDone + kKvBuf,         // every product complete: the accumulators are final
+  kVNumBars = kVAccReady + 1
+};
 
 template <int D>
-struct GkvCfg {
+struct KvCfg {
+  static constexpr uint32_t kColAcc = 2 * kKvCols * kKvBuf;
+  static constexpr uint32_t col_s(int b) { return (uint32_t)(2 * kKvCols * b); }
+  static constexpr uint32_t col_dp(int b) { return (uint32_t)(2 * kKvCols * b + kKvCols); }
   static constexpr int kK = D / 16;
-  static constexpr int kBox = 128 * 32;                 // 128 rows x 16 channels
-  static constexpr int kTileBytes = kK * kBox;          // one 128-row operand tile
-  static constexpr int kRowVals = kGCols * 4;           // one chunk of lse (or Delta), fp32
-  static constexpr int kStageBytes = (2 * kTileBytes + 2 * kRowVals + 1023) / 1024 * 1024;
+  static constexpr int kBoxT = kRows * 32;       // key / summary tile: 128 rows x 16 channels
+  static constexpr int kBoxC = kKvCols * 32;     // query chunk: kKvCols rows x 16 channels
+  static constexpr int kTileBytes = kK * kBoxT;
+  static constexpr int kChunkBytes = kK * kBoxC;
+  static constexpr int kVals = kKvCols * 4;      // lse (or Delta) of one chunk, fp32
+  static constexpr int kStageBytes = (2 * kChunkBytes + 2 * kVals + 1023) / 1024 * 1024;
   static constexpr int kFixed = 2 * kTileBytes + 1024;
-  static constexpr int kRoom = (227 * 1024 - 2048 - kFixed) / kStageBytes;
-  static constexpr int kStages = kRoom > 4 ? 4 : kRoom;
+  // two CTAs per SM (<= 113 KB each), never three (> 76 KB: a third CTA's TMEM allocation
+  // would have to wait)
+  static constexpr int kMaxSmem = 113 * 1024, kMinSmem = 78 * 1024;
+  static constexpr int kRoom = (kMaxSmem - kFixed) / kStageBytes;
+  static constexpr int kStages = kRoom > kKvMaxStages ? kKvMaxStages : kRoom;
   static constexpr int kSmemNeed = kFixed + kStages * kStageBytes;
-  static constexpr int kSmemBytes = kSmemNeed > 116 * 1024 ? kSmemNeed : 116 * 1024;
-  static_assert(kStages >= 2, "the ring must hold two chunks");
-  static_assert(kGColAcc + 2 * D <= 512, "TMEM budget");
+  static constexpr int kSmemBytes = kSmemNeed > kMinSmem ? kSmemNeed : kMinSmem;
+  static_assert(kStages >= kKvBuf + 1, "the ring must hold the chunks in flight and the next");
+  static_assert(kSmemBytes <= kMaxSmem, "shared memory budget");
+  static_assert(kColAcc + 2 * D <= kKvTmemCols, "TMEM budget");
 };
 
-enum GkvBar {
-  kGKvFull = 0,
-  kGFull = 1,                  // [stage]: Q, dO_g copies (tx) + lse / Delta stores (one arrive)
-  kGEmpty = kGFull + 4,        // [stage]: released by the commit after dSV / dSK of its chunk
-  kGSReady = kGEmpty + 4,      // S^T(c) and dP^T(c) complete
-  kGSFree = kGSReady + 1,      // the 8 softmax warps have read S^T(c), dP^T(c) (count 8)
-  kGPdsReady = kGSFree + 1,    // the 8 softmax warps stored P^T(c), dS^T(c) (count 8)
-  kGPdsFree = kGPdsReady + 1,  // dSV(c), dSK(c) complete
-  kGDrain = kGPdsFree + 1,
-  kGNumBars = kGDrain + 1
-};
+__device__ __forceinline__ void kv_init(uint64_t *bars, int stages) {
+  mbar_init(smem_u32(&bars[kVKvFull]), 1);
+  for (int s = 0; s < stages; ++s) {
+    mbar_init(smem_u32(&bars[kVFull + s]), 2);
+    mbar_init(smem_u32(&bars[kVEmpty + s]), 1);
+  }
+  for (int b = 0; b < kKvBuf; ++b) {
+    mbar_init(smem_u32(&bars[kVSReady + b]), 1);
+    mbar_init(smem_u32(&bars[kVPdsReady + b]), kKvSoft);
+    mbar_init(smem_u32(&bars[kVAccDone + b]), 1);
+  }
+  mbar_init(smem_u32(&bars[kVAccReady]), 1);
+  fence_mbar_init();
+}
+
+// The producer warp: `tiles()` (lane 0) starts the K / V tile copies on kVKvFull;
+// `chunk(c, s, wait_stage)` (whole warp) may issue its lse / Delta loads, then calls
+// wait_stage() (false: give up), then fills ring stage s with chunk c -- lane 0 issues the
+// copies with their expect_tx, every lane may store lse / Delta -- and returns whether it
+// got the stage.
+template <int kStages, class Tiles, class Chunk>
+__device__ __forceinline__ void kv_producer_role(uint64_t *bars, int n_chunks, int lane, Tiles tiles, Chunk chunk) {
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  if (lane == 0) tiles();
+  int issued = 0;
+  for (int ch = 0; ch < n_chunks; ++ch) {
+    const int s = ch % kStages;
+    // kVEmpty[s]: completion ch / kStages - 1, committed after the products of chunk
+    // ch - kStages; its next completion needs this stage refilled first
+    auto wait_stage = [&]() -> bool {
+      bool ok = true;
+      if (lane == 0 && ch >= kStages)
+        ok = mbar_wait(bar(kVEmpty + s), (ch / kStages - 1) & 1, &g_bwd_errors, kWaitNs, kErrProducer);
+      return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    };
+    if (!chunk(ch, s, wait_stage)) break;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar(kVFull + s));
+    issued = ch + 1;
+  }
+  if (lane == 0) {  // no copy may still be in flight when the CTA exits
+    mbar_wait(bar(kVKvFull), 0, &g_bwd_errors, kWaitNs, kErrTeardown);
+    for (int ch = issued > kStages ? issued - kStages : 0; ch < issued; ++ch)
+      mbar_wait(bar(kVFull + ch % kStages), (ch / kStages) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+  }
+}
+
+// The whole MMA warp: sdp(c, b) issues S^T, dP^T of chunk c into buffer b, acc(c, b) its
+// dV / dK products from buffer b, with the warp-wide (elected-lane) MMA forms; every lane
+// waits on the barriers.
+template <int kStages, class Sdp, class Acc>
+__device__ __forceinline__ void kv_mma_role(uint64_t *bars, int n_chunks, Sdp sdp, Acc acc) {
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  int n_sdp = 0, n_acc = 0;  // chunks whose S^T / dP^T, whose products were issued
+  auto wait_bar = [&](int b, int completion) -> bool {
+    const bool r = mbar_wait(bar(b), completion & 1, &g_bwd_errors, kWaitNs, kErrMma);
+    if (!__all_sync(0xffffffffu, r)) return false;
+    tc_fence_after();
+    return true;
+  };
+  auto issue_sdp = [&](int c) -> bool {
+    if (!wait_bar(kVFull + c % kStages, c / kStages)) return false;
+    sdp(c, c % kKvBuf);
+    mma_commit_warp(bar(kVSReady + c % kKvBuf));
+    n_sdp = c + 1;
+    return true;
+  };
+  bool ok = wait_bar(kVKvFull, 0);
+  for (int c = 0; ok && c < kKvBuf && c < n_chunks; ++c) ok = issue_sdp(c);
+  for (int c = 0; ok && c < n_chunks; ++c) {
+    const int b = c % kKvBuf, round = c / kKvBuf;
+    // pdsready[b]: completion c / kKvBuf; the warps' next arrivals on it need S^T(c + kKvBuf)
+    ok = wait_bar(kVPdsReady + b, round);
+    if (!ok) break;
+    acc(c, b);
+    mma_commit_warp(bar(kVEmpty + c % kStages));
+    mma_commit_warp(bar(kVAccDone + b));
+    n_acc = c + 1;
+    if (c + kKvBuf < n_chunks) {
+      // S^T(c + kKvBuf) overwrites P^T(c): the products of chunk c must have read it
+      ok = wait_bar(kVAccDone + b, round) && issue_sdp(c + kKvBuf);
+    }
+  }
+  mma_commit_warp(bar(kVAccReady));
+  // drain: the last commit first (every operation then complete), then each barrier's last
+  // completion, so that no arrival is in flight when the CTA exits.  A barrier indexed by
+  // buffer was committed once per chunk c < n with c % kKvBuf == b, one indexed by stage
+  // once per chunk c < n_acc with c % kStages == s.
+  mbar_wait(bar(kVAccReady), 0, &g_bwd_errors, kWaitNs, kErrTeardown);
+  for (int b = 0; b < kKvBuf; ++b) {
+    const int ns = n_sdp / kKvBuf + (b < n_sdp % kKvBuf ? 1 : 0), na = n_acc / kKvBuf + (b < n_acc % kKvBuf ? 1 : 0);
+    if (ns) mbar_wait(bar(kVSReady + b), (ns - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+    if (na) mbar_wait(bar(kVAccDone + b), (na - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+  }
+  for (int s = 0; s < kStages; ++s) {
+    const int times = n_acc / kStages + (s < n_acc % kStages ? 1 : 0);
+    if (times > 0) mbar_wait(bar(kVEmpty + s), (times - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+  }
+}
+
+// Softmax-warp wait: every lane polls; the warp proceeds only if all lanes saw the phase.
+__device__ __forceinline__ bool kv_wait_warp(uint64_t *bars, int b, int completion) {
+  const bool r = mbar_wait(smem_u32(&bars[b]), completion & 1, &g_bwd_errors, kWaitNs, kErrSoftmax);
+  const bool all = __all_sync(0xffffffffu, r);
+  if (all) tc_fence_after();
+  return all;
+}
+
+// 16 columns of one lane's row: P^T / dS^T pairs from S^T, dP^T (fp32 bits).  l, d: per
+// column (shared memory) -lse log2(e) and -Delta, or with RAW lse and Delta as saved; bits:
+// bit i for column i valid, unused unless MASKED (a masked column gives exact zeros
+// whatever its inputs).
+template <bool BF16, bool MASKED, bool RAW>
+__device__ __forceinline__ void kv_scores16(const uint32_t (&sv)[16], const uint32_t (&dv)[16], const float *l,
+                                            const float *d, float sc, uint32_t bits, uint32_t (&pw)[8],
+                                            uint32_t (&dw)[8]) {
+  const float2 sc2 = make_float2(sc, sc);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float2 l2 = *reinterpret_cast<const float2 *>(l + 2 * i);
+    float2 d2 = *reinterpret_cast<const float2 *>(d + 2 * i);
+    if (RAW) {
+      l2 = mul2(l2, make_float2(-kLog2e, -kLog2e));
+      d2 = make_float2(-d2.x, -d2.y);
+    }
+    const float2 x = fma2(make_float2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), sc2, l2);
+    // kKvPolyPairs of every 8 pairs take the FMA-pipe polynomial, the rest the MUFU
+    float2 pp = (i % 8) < 8 - kKvPolyPairs ? make_float2(ex2_approx(x.x), ex2_approx(x.y)) : exp2_poly2(x);
+    float2 dd = mul2(pp, add2(make_float2(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])), d2));
+    if (MASKED) {
+      const bool b0 = (bits >> (2 * i)) & 1u, b1 = (bits >> (2 * i + 1)) & 1u;
+      pp = make_float2(b0 ? pp.x : 0.f, b1 ? pp.y : 0.f);
+      dd = make_float2(b0 ? dd.x : 0.f, b1 ? dd.y : 0.f);
+    }
+    pw[i] = pack2<BF16>(pp.x, pp.y);
+    dw[i] = pack2<BF16>(dd.x, dd.y);
+  }
+}
+
+// One chunk of a softmax warp: its kKvW columns of S^T / dP^T (TMEM addresses t_s, t_dp of
+// the first) to P^T / dS^T pairs at the start of the same range.  Groups of 16 columns, the
+// loads of group g + 1 in flight while group g is computed; group g's pairs go to columns
+// [8g, 8g + 8) of the range, which hold scores the warp has already loaded.  mask: bit i
+// for column i of the range.
+template <bool BF16, bool MASKED, bool RAW>
+__device__ __forceinline__ void kv_chunk(uint32_t t_s, uint32_t t_dp, const float *l, const float *d, float sc,
+                                         uint64_t mask) {
+  constexpr int kG = kKvW / 16;
+  uint32_t sv[2][16], dv[2][16];
+  tmem_ld16(t_s, sv[0]);
+  tmem_ld16(t_dp, dv[0]);
+  tmem_wait_ld();
+#pragma unroll
+  for (int g = 0; g < kG; ++g) {
+    if (g + 1 < kG) {
+      tmem_ld16(t_s + 16 * (g + 1), sv[(g + 1) & 1]);
+      tmem_ld16(t_dp + 16 * (g + 1), dv[(g + 1) & 1]);
+    }
+    uint32_t pw[8], dw[8];
+    kv_scores16<BF16, MASKED, RAW>(sv[g & 1], dv[g & 1], l + 16 * g, d + 16 * g, sc,
+                                   (uint32_t)(mask >> (16 * g)) & 0xffffu, pw, dw);
+    tmem_st8(t_s + 8 * g, pw);
+    tmem_st8(t_dp + 8 * g, dw);
+    if (g + 1 < kG) tmem_wait_ld();
+  }
+}
+
+__device__ __forceinline__ void kv_zero_chunk(uint32_t t_s, uint32_t t_dp) {
+  uint32_t z[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) z[i] = 0u;
+#pragma unroll
+  for (int g = 0; g < kKvW / 16; ++g) {
+    tmem_st8(t_s + 8 * g, z);
+    tmem_st8(t_dp + 8 * g, z);
+  }
+}
+
+// TMEM column (within an S^T / dP^T buffer) of the pairs of query group j (queries 16j ..
+// 16j + 15): group g of the softmax warps serving columns [kKvW h, kKvW (h + 1)) sits at
+// kKvW h + 8g.
+__host__ __device__ constexpr uint32_t kv_pair_col(int j) {
+  return (uint32_t)((16 * j / kKvW) * kKvW + 8 * ((16 * j % kKvW) / 16));
+}
+
+// The MMAs of one chunk, shared by both kernels: k_smem / v_smem the 128-row K and V tiles,
+// q / dov the chunk's Q and dO boxes, b the TMEM buffer.
+template <int D, bool BF16>
+__device__ __forceinline__ void kv_issue_sdp(uint32_t tmem, uint32_t k_smem, uint32_t v_smem, uint32_t q,
+                                             uint32_t dov, int b) {
+  using C = KvCfg<D>;
+  constexpr uint32_t idesc_s = idesc_f16(128, kKvCols, BF16, false);
+#pragma unroll
+  for (int kk = 0; kk < C::kK; ++kk)
+    mma_ss_warp(tmem + C::col_s(b), desc_sw32(k_smem + kk * C::kBoxT, 16, 256), desc_sw32(q + kk * C::kBoxC, 16, 256),
+                idesc_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+  for (int kk = 0; kk < C::kK; ++kk)
+    mma_ss_warp(tmem + C::col_dp(b), desc_sw32(v_smem + kk * C::kBoxT, 16, 256),
+                desc_sw32(dov + kk * C::kBoxC, 16, 256), idesc_s, kk > 0 ? 1u : 0u);
+}
+
+template <int D, bool BF16>
+__device__ __forceinline__ void kv_issue_acc(uint32_t tmem, uint32_t q, uint32_t dov, int b, bool first) {
+  using C = KvCfg<D>;
+  constexpr uint32_t idesc_acc = idesc_f16(128, D, BF16, true);
+  // dV += P^T dO and dK += dS^T Q: A from TMEM (query group j: 16 queries as 8 columns of
+  // pairs, kv_pair_col), B the chunk's dO / Q read MN-major (16 query rows of 32 bytes per
+  // step)
+#pragma unroll
+  for (int j = 0; j < kKvCols / 16; ++j)
+    mma_ts_warp(tmem + C::kColAcc + D, tmem + C::col_s(b) + kv_pair_col(j), desc_sw32(dov + j * 512, C::kBoxC, 256),
+                idesc_acc, (first && j == 0) ? 0u : 1u);
+#pragma unroll
+  for (int j = 0; j < kKvCols / 16; ++j)
+    mma_ts_warp(tmem + C::kColAcc, tmem + C::col_dp(b) + kv_pair_col(j), desc_sw32(q + j * 512, C::kBoxC, 256),
+                idesc_acc, (first && j == 0) ? 0u : 1u);
+}
+
+// The epilogue's accumulator rows: warps 0-3 take dK (scaled by 1/sqrt(D)), warps 4-7 dV.
+template <int D>
+__device__ __forceinline__ void kv_load_acc(uint32_t t_lanes, int half, uint32_t (&acc)[D]) {
+#pragma unroll
+  for (int c = 0; c < D / 16; ++c)
+    tmem_ld16(t_lanes + KvCfg<D>::kColAcc + (half ? D : 0) + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(acc + 16 * c));
+  tmem_wait_ld();
+}
+
+// ------------------------------------------------------------------ global dSK / dSV
+//
+// Restates the summary-gradient half of the global branch (kernels.py:210-239): a CTA owns
+// one (batch, kv-head), a tile of 128 summaries and one split of the query chunks (every
+// query head of the group); splits write fp32 partials [B*G, splits, M, D] that a
+// fixed-order reduction sums.  The global branch ignores the geometry, so this kernel serves
+// any token order.  Summary rows past M read zeros and are not written; query columns past
+// N are masked (P = 0).
+constexpr int kGRows = 128;      // summaries per tile
+constexpr int kGCols = kKvCols;  // queries per chunk
 
 struct GkvParams {
   int heads, kv_heads, rep, tokens, summaries, m_tiles, splits, q_chunks, per_split;
@@ -609,13 +879,14 @@ struct GkvParams {
 };
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kKvThreads, 2)
     global_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
                          const __grid_constant__ CUtensorMap tsk, const __grid_constant__ CUtensorMap tsv,
                          const GkvParams p) {
-  using C = GkvCfg<D>;
+  using C = KvCfg<D>;
+  constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[kGNumBars];
+  __shared__ __align__(8) uint64_t bars[kVNumBars];
   __shared__ uint32_t tmem_holder;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -633,26 +904,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sk_smem = base, sv_smem = base + C::kTileBytes;
   const uint32_t ring = base + 2 * C::kTileBytes;
   uint8_t *ring_ptr = smem_raw + (base - raw) + 2 * C::kTileBytes;
-  auto bar = [&](int i) { return smem_u32(&bars[i]); };
 
-  if (tid == 0) {
-    mbar_init(bar(kGKvFull), 1);
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(bar(kGFull + s), 2);
-      mbar_init(bar(kGEmpty + s), 1);
-    }
-    mbar_init(bar(kGSReady), 1);
-    mbar_init(bar(kGSFree), 8);
-    mbar_init(bar(kGPdsReady), 8);
-    mbar_init(bar(kGPdsFree), 1);
-    mbar_init(bar(kGDrain), 1);
-    fence_mbar_init();
-  }
-  if (warp == kMmaWarp) {
-    tmem_alloc(smem_u32(&tmem_holder), kTmemCols);
+  if (tid == 0) kv_init(bars, kStages);
+  if (warp == kKvMma) {
+    tmem_alloc(smem_u32(&tmem_holder), kKvTmemCols);
     tmem_relinquish();
   }
-  if (warp == kProducerWarp && lane == 0) {
+  if (warp == kKvProducer && lane == 0) {
     prefetch_tmap(&tq);
     prefetch_tmap(&tdo);
     prefetch_tmap(&tsk);
@@ -664,224 +922,96 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = tmem_holder;
   auto chunk_head = [&](int c) { return b * p.heads + g * p.rep + (c_begin + c) / p.q_chunks; };
   auto chunk_row0 = [&](int c) { return ((c_begin + c) % p.q_chunks) * kGCols; };
+  auto stage_of = [&](int c) { return ring + (uint32_t)((c % kStages) * C::kStageBytes); };
 
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------------ producer (whole warp)
-    if (lane == 0) {
-      mbar_expect_tx(bar(kGKvFull), 2 * C::kTileBytes);
+  if (warp == kKvProducer) {
+    auto tiles = [&]() {
+      const uint32_t full = smem_u32(&bars[kVKvFull]);
+      mbar_expect_tx(full, 2 * C::kTileBytes);
       for (int c = 0; c < C::kK; ++c) {
-        tma_load_3d(sk_smem + c * C::kBox, &tsk, bar(kGKvFull), 16 * c, m0, bg);
-        tma_load_3d(sv_smem + c * C::kBox, &tsv, bar(kGKvFull), 16 * c, m0, bg);
+        tma_load_3d(sk_smem + c * C::kBoxT, &tsk, full, 16 * c, m0, bg);
+        tma_load_3d(sv_smem + c * C::kBoxT, &tsv, full, 16 * c, m0, bg);
       }
-    }
-    int issued = 0;
-    for (int ch = 0; ch < n_chunks; ++ch) {
-      const int s = ch % C::kStages;
-      // kGEmpty[s]: completion ch/kStages - 1 (the same unambiguity argument as the dQ kernel)
-      bool ok = true;
-      if (lane == 0 && ch >= C::kStages)
-        ok = mbar_wait(bar(kGEmpty + s), (ch / C::kStages - 1) & 1, &g_bwd_errors, kWaitNs, kErrProducer);
-      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
-      const uint32_t stage = ring + s * C::kStageBytes;
-      const uint32_t full = bar(kGFull + s);
+    };
+    auto chunk = [&](int ch, int s, auto wait_stage) -> bool {
+      const uint32_t stage = ring + s * C::kStageBytes, full = smem_u32(&bars[kVFull + s]);
       const int bh = chunk_head(ch), n0 = chunk_row0(ch);
       const int64_t r0 = (int64_t)bh * p.tokens + n0;
       const uint32_t rows = (uint32_t)min(kGCols, p.tokens - n0);
-      // lse and Delta of the chunk's queries (columns past the last row are masked by the
-      // softmax warps): bulk copies beside the tensor tiles, or plain loads in registers
-      // first, then stores (so the loads are not serialised behind the stores).
-      const uint32_t vals_smem = stage + 2 * C::kTileBytes;
-      if (lane == 0) {
-        mbar_expect_tx(full, 2 * C::kTileBytes + (p.bulk_vals ? 2 * rows * 4 : 0));
-        for (int c = 0; c < C::kK; ++c) {
-          tma_load_3d(stage + c * C::kBox, &tq, full, 16 * c, n0, bh);
-          tma_load_3d(stage + C::kTileBytes + c * C::kBox, &tdo, full, 16 * c, n0, bh);
-        }
-        if (p.bulk_vals) {
-          bulk_load(vals_smem, p.lse_g + r0, rows * 4, full);
-          bulk_load(vals_smem + C::kRowVals, p.delta_g + r0, rows * 4, full);
-        }
-      }
-      if (!p.bulk_vals) {
-        float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kTileBytes);
-        float l[kGCols / 32], dl[kGCols / 32];
+      const uint32_t vals_smem = stage + 2 * C::kChunkBytes;
+      float l[kGCols / 32], dl[kGCols / 32];
+      if (!p.bulk_vals) {  // the loads go out before the stage wait
 #pragma unroll
         for (int k = 0; k < kGCols / 32; ++k) {
           const int j = lane + 32 * k;
           l[k] = j < (int)rows ? __ldg(p.lse_g + r0 + j) : 0.f;
           dl[k] = j < (int)rows ? __ldg(p.delta_g + r0 + j) : 0.f;
         }
+      }
+      if (!wait_stage()) return false;
+      if (lane == 0) {
+        mbar_expect_tx(full, 2 * C::kChunkBytes + (p.bulk_vals ? 2 * rows * 4 : 0));
+        for (int c = 0; c < C::kK; ++c) {
+          tma_load_3d(stage + c * C::kBoxC, &tq, full, 16 * c, n0, bh);
+          tma_load_3d(stage + C::kChunkBytes + c * C::kBoxC, &tdo, full, 16 * c, n0, bh);
+        }
+        if (p.bulk_vals) {
+          bulk_load(vals_smem, p.lse_g + r0, rows * 4, full);
+          bulk_load(vals_smem + C::kVals, p.delta_g + r0, rows * 4, full);
+        }
+      }
+      if (!p.bulk_vals) {
+        float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kChunkBytes);
 #pragma unroll
         for (int k = 0; k < kGCols / 32; ++k) {
           vals[lane + 32 * k] = l[k];
           vals[kGCols + lane + 32 * k] = dl[k];
         }
-        __syncwarp();
       }
-      if (lane == 0) mbar_arrive(full);
-      issued = ch + 1;
-    }
-    if (lane == 0) {
-      mbar_wait(bar(kGKvFull), 0, &g_bwd_errors, kWaitNs, kErrTeardown);
-      for (int ch = issued > C::kStages ? issued - C::kStages : 0; ch < issued; ++ch)
-        mbar_wait(bar(kGFull + ch % C::kStages), (ch / C::kStages) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
-    }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_f16(128, kGCols, BF16, false);
-      constexpr uint32_t idesc_acc = idesc_f16(128, D, BF16, true);
-      uint32_t commits[kGNumBars];
-      for (int i = 0; i < kGNumBars; ++i) commits[i] = 0u;
-      auto commit = [&](int bidx) {
-        mma_commit(bar(bidx));
-        ++commits[bidx];
-      };
-      auto stage_of = [&](int c) { return ring + (c % C::kStages) * C::kStageBytes; };
-      auto issue_s_dp = [&](int c) {
-        const uint32_t q = stage_of(c), dov = stage_of(c) + C::kTileBytes;
-        for (int kk = 0; kk < C::kK; ++kk)
-          mma_ss(tmem + kGColS, desc_sw32(sk_smem + kk * C::kBox, 16, 256), desc_sw32(q + kk * C::kBox, 16, 256),
-                 idesc_s, kk > 0 ? 1u : 0u);
-        for (int kk = 0; kk < C::kK; ++kk)
-          mma_ss(tmem + kGColDP, desc_sw32(sv_smem + kk * C::kBox, 16, 256), desc_sw32(dov + kk * C::kBox, 16, 256),
-                 idesc_s, kk > 0 ? 1u : 0u);
-        commit(kGSReady);
-      };
-      auto issue_acc = [&](int c) {
-        const uint32_t q = stage_of(c), dov = stage_of(c) + C::kTileBytes;
-        for (int j = 0; j < kGCols / 16; ++j)
-          mma_ts(tmem + kGColAcc + D, tmem + kGColP + 8 * j, desc_sw32(dov + j * 512, C::kBox, 256), idesc_acc,
-                 (c == 0 && j == 0) ? 0u : 1u);
-        for (int j = 0; j < kGCols / 16; ++j)
-          mma_ts(tmem + kGColAcc, tmem + kGColDS + 8 * j, desc_sw32(q + j * 512, C::kBox, 256), idesc_acc,
-                 (c == 0 && j == 0) ? 0u : 1u);
-        commit(kGPdsFree);
-        commit(kGEmpty + c % C::kStages);  // every reader of chunk c's stage is issued
-      };
-      auto wait_bar = [&](int bidx, int completion) -> bool {
-        if (!mbar_wait(bar(bidx), completion & 1, &g_bwd_errors, kWaitNs, kErrMma)) return false;
-        tc_fence_after();
-        return true;
-      };
-      auto wait_full = [&](int c) { return wait_bar(kGFull + c % C::kStages, c / C::kStages); };
-      bool ok = wait_bar(kGKvFull, 0) && wait_full(0);
-      if (ok) issue_s_dp(0);
-      for (int c = 0; ok && c < n_chunks; ++c) {
-        ok = wait_bar(kGSFree, c);
-        if (!ok) break;
-        if (c + 1 < n_chunks) {
-          ok = wait_full(c + 1);
-          if (!ok) break;
-          issue_s_dp(c + 1);
-        }
-        ok = wait_bar(kGPdsReady, c);
-        if (!ok) break;
-        issue_acc(c);
-      }
-      commit(kGDrain);
-      for (int i = 0; i < kGNumBars; ++i)
-        if (commits[i]) mbar_wait(bar(i), (commits[i] - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
-    }
-  } else {
-    // ------------------------------------------------------------------ softmax (8 warps) + epilogue
-    const int quarter = warp & 3, half = warp >> 2;
-    const uint32_t t_lanes = tmem + ((uint32_t)(quarter * 32) << 16);
-    const int row = quarter * 32 + lane;  // summary m0 + row
-    const float sc = p.sc, inv_sqrt_d = p.inv_sqrt_d;
-    auto wait_warp = [&](int bidx, int completion) -> bool {
-      const bool r = mbar_wait(bar(bidx), completion & 1, &g_bwd_errors, kWaitNs, kErrSoftmax);
-      const bool all = __all_sync(0xffffffffu, r);
-      if (all) tc_fence_after();
-      return all;
+      return true;
     };
+    kv_producer_role<kStages>(bars, n_chunks, lane, tiles, chunk);
+  } else if (warp == kKvMma) {
+    kv_mma_role<kStages>(
+        bars, n_chunks,
+        [&](int c, int bf) {
+          kv_issue_sdp<D, BF16>(tmem, sk_smem, sv_smem, stage_of(c), stage_of(c) + C::kChunkBytes, bf);
+        },
+        [&](int c, int bf) { kv_issue_acc<D, BF16>(tmem, stage_of(c), stage_of(c) + C::kChunkBytes, bf, c == 0); });
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int quarter = warp & 3, half = warp >> 2, col0 = half * kKvW;
+    const uint32_t t_lanes = tmem + ((uint32_t)(quarter * 32) << 16);
+    const float sc = p.sc;
     bool ok = true;
     for (int ch = 0; ch < n_chunks; ++ch) {
-      ok = wait_warp(kGSReady, ch);
+      const int bf = ch % kKvBuf;
+      ok = kv_wait_warp(bars, kVSReady + bf, ch / kKvBuf);
       if (!ok) break;
-      const float4 *vals = reinterpret_cast<const float4 *>(ring_ptr + (size_t)(ch % C::kStages) * C::kStageBytes +
-                                                            2 * C::kTileBytes);
-      const int valid = min(kGCols, p.tokens - chunk_row0(ch));  // query columns inside the volume
-      uint32_t pw[2][16], dw[2][16];
-#pragma unroll
-      for (int gi = 0; gi < 2; ++gi) {
-        const int col0 = 64 * half + 32 * gi;
-        uint32_t sv[32], dv[32];
-        tmem_ld32(t_lanes + kGColS + col0, sv);
-        tmem_ld32(t_lanes + kGColDP + col0, dv);
-        tmem_wait_ld();
-        // P^T = exp2(S^T sc - lse log2e); dS^T = P^T (dP^T - Delta) (its 1/sqrt(D) is applied
-        // to the dSK accumulator at the end)
-        if (col0 + 32 <= valid) {  // every column inside the volume: paired, no masks
-          const float2 sc2 = make_float2(sc, sc), nl2e = make_float2(-kLog2e, -kLog2e);
-#pragma unroll
-          for (int i4 = 0; i4 < 8; ++i4) {
-            const int j = col0 + 4 * i4;
-            const float4 l4 = vals[j / 4], d4 = vals[(kGCols + j) / 4];
-#pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-              const int i = 4 * i4 + 2 * h2;
-              const float2 l2 = h2 ? make_float2(l4.z, l4.w) : make_float2(l4.x, l4.y);
-              const float2 nd2 = h2 ? make_float2(-d4.z, -d4.w) : make_float2(-d4.x, -d4.y);
-              const float2 x =
-                  fma2(make_float2(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), sc2, mul2(l2, nl2e));
-              const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-              const float2 dd = mul2(pp, add2(make_float2(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])), nd2));
-              pw[gi][2 * i4 + h2] = pack2<BF16>(pp.x, pp.y);
-              dw[gi][2 * i4 + h2] = pack2<BF16>(dd.x, dd.y);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int i4 = 0; i4 < 8; ++i4) {
-            const int j = col0 + 4 * i4;
-            const float4 l4 = vals[j / 4], d4 = vals[(kGCols + j) / 4];
-            const float ls[4] = {l4.x, l4.y, l4.z, l4.w}, ds[4] = {d4.x, d4.y, d4.z, d4.w};
-            float pp[4], dd[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i = 4 * i4 + e;
-              // columns past the volume may hold stale values: they give exact zeros
-              const bool in = j + e < valid;
-              pp[e] = in ? ex2_approx(fmaf(__uint_as_float(sv[i]), sc, -ls[e] * kLog2e)) : 0.f;
-              dd[e] = in ? pp[e] * (__uint_as_float(dv[i]) - ds[e]) : 0.f;
-            }
-            pw[gi][2 * i4] = pack2<BF16>(pp[0], pp[1]);
-            pw[gi][2 * i4 + 1] = pack2<BF16>(pp[2], pp[3]);
-            dw[gi][2 * i4] = pack2<BF16>(dd[0], dd[1]);
-            dw[gi][2 * i4 + 1] = pack2<BF16>(dd[2], dd[3]);
-          }
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kGSFree));
-      if (ch > 0) {
-        ok = wait_warp(kGPdsFree, ch - 1);  // dSV / dSK of the previous chunk no longer read P^T / dS^T
-        if (!ok) break;
-      }
-#pragma unroll
-      for (int gi = 0; gi < 2; ++gi) {
-        tmem_st16(t_lanes + kGColP + 32 * half + 16 * gi, pw[gi]);
-        tmem_st16(t_lanes + kGColDS + 32 * half + 16 * gi, dw[gi]);
+      const float *vals =
+          reinterpret_cast<const float *>(ring_ptr + (size_t)(ch % kStages) * C::kStageBytes + 2 * C::kChunkBytes);
+      const int valid = min(kGCols, p.tokens - chunk_row0(ch)) - col0;  // this warp's columns inside the volume
+      const uint32_t ts = t_lanes + C::col_s(bf) + col0, tdp = t_lanes + C::col_dp(bf) + col0;
+      if (valid >= kKvW) {
+        kv_chunk<BF16, false, true>(ts, tdp, vals + col0, vals + kGCols + col0, sc, ~0ull);
+      } else if (valid > 0) {  // columns past the volume may hold stale lse / Delta: masked to exact zeros
+        kv_chunk<BF16, true, true>(ts, tdp, vals + col0, vals + kGCols + col0, sc, ~0ull >> (64 - valid));
+      } else {
+        kv_zero_chunk(ts, tdp);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kGPdsReady));
+      if (lane == 0) mbar_arrive(smem_u32(&bars[kVPdsReady + bf]));
     }
-    if (ok) ok = wait_warp(kGPdsFree, n_chunks - 1);
+    if (ok) ok = kv_wait_warp(bars, kVAccReady, 0);
     if (ok) {
-      // warps 0-3 write dSK rows, warps 4-7 dSV rows
+      const int m = m0 + quarter * 32 + lane;
       uint32_t acc[D];
-      const uint32_t col = kGColAcc + (half ? D : 0);
-#pragma unroll
-      for (int c = 0; c < D / 16; ++c) tmem_ld16(t_lanes + col + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(acc + 16 * c));
-      tmem_wait_ld();
-      const int m = m0 + row;
+      kv_load_acc<D>(t_lanes, half, acc);
       if (m < p.summaries) {
         float *dst = (half ? p.dv_part : p.dk_part) + (((int64_t)bg * p.splits + split) * p.summaries + m) * D;
-        const float scale = half ? 1.f : inv_sqrt_d;  // dSK: the 1/sqrt(D) of dS
+        const float scale = half ? 1.f : p.inv_sqrt_d;
 #pragma unroll
         for (int v = 0; v < D / 4; ++v)
           reinterpret_cast<float4 *>(dst)[v] =
@@ -889,20 +1019,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                           __uint_as_float(acc[4 * v + 2]) * scale, __uint_as_float(acc[4 * v + 3]) * scale);
       }
     }
-    tmem_wait_st();
   }
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kKvMma) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, kKvTmemCols);
   }
 }
 
 template <int D, bool BF16>
 int launch_gkv_t(const GlobalDkvArgs &a, cudaStream_t stream) {
-  using C = GkvCfg<D>;
+  using C = KvCfg<D>;
   const uint64_t es = 2;
   const uint64_t bh = (uint64_t)a.batch * a.heads, bgs = (uint64_t)a.batch * a.kv_heads;
   CUtensorMap tq, tdo, tsk, tsv;
@@ -940,52 +1069,40 @@ int launch_gkv_t(const GlobalDkvArgs &a, cudaStream_t stream) {
   const int64_t units = (int64_t)bgs * p.m_tiles * p.splits;
   if (units <= 0) return P3D_OK;
   if (units > 0x7fffffff) return fail(P3D_ERR_UNSUPPORTED, "too many tiles");
+  const int64_t total = (int64_t)p.rep * p.q_chunks;
+  if (p.per_split < 1 || (int64_t)p.splits * p.per_split < total || (int64_t)(p.splits - 1) * p.per_split >= total)
+    return fail(P3D_ERR_INVALID_ARGUMENT, "global dSK/dSV: splits do not cover the query chunks");
   auto kernel = global_dkv_tc_kernel<D, BF16>;
   static size_t seen[kMaxDevices] = {};
   if (int st = smem_optin(kernel, C::kSmemBytes, seen)) return st;
-  kernel<<<(unsigned)units, kThreads, C::kSmemBytes, stream>>>(tq, tdo, tsk, tsv, p);
+  kernel<<<(unsigned)units, kKvThreads, C::kSmemBytes, stream>>>(tq, tdo, tsk, tsv, p);
   P3D_LAUNCH_CHECK();
   return P3D_OK;
 }
 
 
-// ============================================================================ local dK / dV
+// ------------------------------------------------------------------ local dK / dV
 //
 // Restates the key-gradient half of the local branch (kernels.py:154-176; stencil.py:91-147
-// with QUERY false) on tensor cores.  A CTA owns one (batch, kv-head) and a 4x4x8 (z, y, x)
-// box of 128 keys (TMEM lanes, row order (z, y, x) as for the forward's query tiles) and
-// streams, for every query head of its group, the 8 query halo planes z0-2 .. z0+5 (8x12
-// windows, 96 queries each):
-//   S^T = K Q^T, dP^T = V dO_l^T, P^T = exp(S^T / sqrt(D) - lse_l) on the key's 5x5x5 cube,
-//   dS^T = P^T (dP^T - Delta_l) / sqrt(D),   dV += P^T dO_l,  dK += dS^T Q.
-// The neighbourhood is symmetric (key j is in query i's clipped cube iff i is in j's), so
-// the mask is the forward's with the roles swapped.  P^T and dS^T are rounded to the
-// storage dtype for the products (the reference keeps them in fp32; the difference is far
-// inside the bf16 tolerance).  Each CTA writes its own keys' dK / dV: no atomics, no
-// partials.
-//
-// TMEM (W = kKeys, 96 at radius 2): S^T [0, W), dP^T [W, 2W), P^T [2W, 2.5W), dS^T
-// [2.5W, 3W), dK [3W, 3W + D), dV [3W + D, 3W + 2D).  Eight softmax warps (warp w: TMEM
-// lanes 32(w%4).., query columns (W/2)(w/4)..+W/2); the protocol is the global dSK / dSV
-// kernel's.
-template <int D, int KEYS>
-struct LkvCfg {
-  static constexpr uint32_t kLColS = 0, kLColDP = KEYS, kLColP = 2 * KEYS, kLColDS = 2 * KEYS + KEYS / 2,
-                            kLColAcc = 3 * KEYS;
-  static constexpr int kK = D / 16;
-  static constexpr int kBoxT = kRows * 32;           // key tile: 128 rows x 16 channels
-  static constexpr int kBoxP = KEYS * 32;            // query plane: KEYS rows x 16 channels
-  static constexpr int kTileBytes = kK * kBoxT;
-  static constexpr int kPlaneBytes = kK * kBoxP;
-  static constexpr int kVals = KEYS * 4;              // lse (or Delta) of one plane, fp32
-  static constexpr int kStageBytes = (2 * kPlaneBytes + 2 * kVals + 1023) / 1024 * 1024;
-  static constexpr int kFixed = 2 * kTileBytes + 1024;
-  static constexpr int kRoom = (227 * 1024 - 2048 - kFixed) / kStageBytes;
-  static constexpr int kStages = kRoom > 4 ? 4 : kRoom;
-  static constexpr int kSmemNeed = kFixed + kStages * kStageBytes;
-  static constexpr int kSmemBytes = kSmemNeed > 116 * 1024 ? kSmemNeed : 116 * 1024;
-  static_assert(kStages >= 2, "the ring must hold two chunks");
-  static_assert(kLColAcc + 2 * D <= 512, "TMEM budget");
+// with QUERY false) on tensor cores.  A CTA owns one (batch, kv-head) and an 8 x 4 x 4 (z, y,
+// x) box of 128 keys (TMEM lanes in (z, y, x) order, so softmax warp w holds key planes
+// 2(w % 4) and 2(w % 4) + 1 of the box) and streams, for every query head of the group, the
+// 8 + 2R query planes z0 - R .. z0 + 7 + R of its neighbourhood.  A plane is the (4 + 2R) x
+// (4 + 2R) window of queries around the box, taken as one chunk (64 queries at radius 2; 36,
+// padded, at radius 1) or, with 32-query chunks, as two of (2 + R) rows each.  The
+// neighbourhood is symmetric (key j is
+// in query i's clipped cube iff i is in j's), so a key takes a query iff both lie in the
+// volume and |dz|, |dy|, |dx| <= R.  Each CTA writes its own keys' dK / dV in the storage
+// dtype: no atomics, no partials.
+template <int R>
+struct KGeo {
+  static constexpr int kBZ = 8, kBY = 4, kBX = 4;
+  static constexpr int kHY = kBY + 2 * R, kHX = kBX + 2 * R;
+  static constexpr int kParts = kHY * kHX <= kKvCols ? 1 : 2;  // chunks per plane
+  static constexpr int kRowsH = kHY / kParts;           // window rows per chunk
+  static constexpr int kWin = kRowsH * kHX;             // queries per chunk
+  static constexpr int kPlanes = kBZ + 2 * R;           // 12, 10
+  static_assert(kWin <= kKvCols, "a chunk's window rows must fit its columns");
 };
 
 struct LkvParams {
@@ -1002,18 +1119,16 @@ struct LkvParams {
 };
 
 template <int D, bool BF16, int R>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kKvThreads, 2)
     stencil_bwd_dkv_kernel(const __grid_constant__ CUtensorMap tkl, const __grid_constant__ CUtensorMap tvl,
                            const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
                            const LkvParams p) {
-  using G = BGeo<R>;
-  constexpr int kR = G::kR, kHX = G::kHX, kWin = G::kWin, kKeys = G::kKeys, kHalf = G::kHalf;
-  constexpr int kLocalChunks = G::kLocalChunks;
-  using C = LkvCfg<D, kKeys>;
-  constexpr uint32_t kLColS = C::kLColS, kLColDP = C::kLColDP, kLColP = C::kLColP, kLColDS = C::kLColDS,
-                     kLColAcc = C::kLColAcc;
+  using G = KGeo<R>;
+  constexpr int kHX = G::kHX, kRowsH = G::kRowsH, kWin = G::kWin, kPlanes = G::kPlanes;
+  using C = KvCfg<D>;
+  constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[kGNumBars];
+  __shared__ __align__(8) uint64_t bars[kVNumBars];
   __shared__ uint32_t tmem_holder;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1025,40 +1140,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tz = unit % p.tiles_z;
   const int bg = unit / p.tiles_z;
   const int b = bg / p.kv_heads, g = bg % p.kv_heads;
-  const int x0 = tx * kTX, y0 = ty * kTY, z0 = tz * kTZ;
-  const int n_chunks = p.rep * kLocalChunks;
+  const int x0 = tx * G::kBX, y0 = ty * G::kBY, z0 = tz * G::kBZ;
+  constexpr int kParts = G::kParts;
+  const int n_chunks = p.rep * kPlanes * kParts;
 
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t k_smem = base, v_smem = base + C::kTileBytes;
   const uint32_t ring = base + 2 * C::kTileBytes;
   uint8_t *ring_ptr = smem_raw + (base - raw) + 2 * C::kTileBytes;
-  auto bar = [&](int i) { return smem_u32(&bars[i]); };
 
-  if (tid == 0) {
-    mbar_init(bar(kGKvFull), 1);
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(bar(kGFull + s), 2);
-      mbar_init(bar(kGEmpty + s), 1);
-    }
-    mbar_init(bar(kGSReady), 1);
-    mbar_init(bar(kGSFree), 8);
-    mbar_init(bar(kGPdsReady), 8);
-    mbar_init(bar(kGPdsFree), 1);
-    mbar_init(bar(kGDrain), 1);
-    fence_mbar_init();
-  }
-  if constexpr (kWin < kKeys) {
-    // the query planes fill kWin of the kKeys rows of each box: the rest reads as zeros
+  if (tid == 0) kv_init(bars, kStages);
+  if constexpr (kWin < kKvCols) {
+    // the query windows fill kWin of the kKvCols rows of each box: the rest reads as zeros
     uint4 *ring_v = reinterpret_cast<uint4 *>(ring_ptr);
-    for (int i = tid; i < C::kStages * C::kStageBytes / 16; i += kThreads) ring_v[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = tid; i < kStages * C::kStageBytes / 16; i += kKvThreads) ring_v[i] = make_uint4(0u, 0u, 0u, 0u);
     fence_proxy_async_smem();
   }
-  if (warp == kMmaWarp) {
-    tmem_alloc(smem_u32(&tmem_holder), kTmemCols);
+  if (warp == kKvMma) {
+    tmem_alloc(smem_u32(&tmem_holder), kKvTmemCols);
     tmem_relinquish();
   }
-  if (warp == kProducerWarp && lane == 0) {
+  if (warp == kKvProducer && lane == 0) {
     prefetch_tmap(&tkl);
     prefetch_tmap(&tvl);
     prefetch_tmap(&tq);
@@ -1068,238 +1171,140 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_holder;
-  // chunk c: query head b*H + g*rep + c/8, query plane z0 - 2 + c%8
-  auto chunk_head = [&](int c) { return b * p.heads + g * p.rep + c / kLocalChunks; };
-  auto chunk_plane = [&](int c) { return p.cz0 + z0 - kR + c % kLocalChunks; };  // global z
+  // chunk c: query head b*H + g*rep + c / (kParts kPlanes), query plane z0 - R + (c /
+  // kParts) % kPlanes, window rows kRowsH (c % kParts) ..
+  auto chunk_head = [&](int c) { return b * p.heads + g * p.rep + c / (kParts * kPlanes); };
+  auto chunk_plane = [&](int c) { return (c / kParts) % kPlanes; };  // relative to z0 - R
+  auto stage_of = [&](int c) { return ring + (uint32_t)((c % kStages) * C::kStageBytes); };
 
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------------ producer (whole warp)
-    if (lane == 0) {
-      mbar_expect_tx(bar(kGKvFull), 2 * C::kTileBytes);
+  if (warp == kKvProducer) {
+    auto tiles = [&]() {
+      const uint32_t full = smem_u32(&bars[kVKvFull]);
+      mbar_expect_tx(full, 2 * C::kTileBytes);
       for (int c = 0; c < C::kK; ++c) {
-        tma_load_5d(k_smem + c * C::kBoxT, &tkl, bar(kGKvFull), 16 * c, x0, y0, p.cz0 + z0 - p.kz0, bg);
-        tma_load_5d(v_smem + c * C::kBoxT, &tvl, bar(kGKvFull), 16 * c, x0, y0, p.cz0 + z0 - p.kz0, bg);
+        tma_load_5d(k_smem + c * C::kBoxT, &tkl, full, 16 * c, x0, y0, p.cz0 + z0 - p.kz0, bg);
+        tma_load_5d(v_smem + c * C::kBoxT, &tvl, full, 16 * c, x0, y0, p.cz0 + z0 - p.kz0, bg);
       }
-    }
-    int issued = 0;
-    for (int ch = 0; ch < n_chunks; ++ch) {
-      const int s = ch % C::kStages;
-      bool ok = true;
-      if (lane == 0 && ch >= C::kStages)
-        ok = mbar_wait(bar(kGEmpty + s), (ch / C::kStages - 1) & 1, &g_bwd_errors, kWaitNs, kErrProducer);
-      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
-      const uint32_t stage = ring + s * C::kStageBytes;
-      const uint32_t full = bar(kGFull + s);
-      const int bh = chunk_head(ch), zp = chunk_plane(ch);
-      if (lane == 0) {
-        mbar_expect_tx(full, 2 * C::kK * kWin * 32);
-        for (int c = 0; c < C::kK; ++c) {
-          tma_load_5d(stage + c * C::kBoxP, &tq, full, 16 * c, x0 - kR, y0 - kR, zp - p.xz0, bh);
-          tma_load_5d(stage + C::kPlaneBytes + c * C::kBoxP, &tdo, full, 16 * c, x0 - kR, y0 - kR, zp - p.xz0,
-                      bh);
-        }
-      }
-      // lse (as log2) and Delta of the plane's kWin queries; +inf outside the volume and on
-      // the padding columns (P = 0).
-      // All loads are issued before any store, so they overlap.
-      float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kPlaneBytes);
-      float l[kKeys / 32], dl[kKeys / 32];
+    };
+    auto chunk = [&](int ch, int s, auto wait_stage) -> bool {
+      const uint32_t stage = ring + s * C::kStageBytes, full = smem_u32(&bars[kVFull + s]);
+      const int bh = chunk_head(ch), zp = p.cz0 + z0 - R + chunk_plane(ch), hy0 = kRowsH * (ch % kParts);
+      // -lse log2(e) and -Delta of the chunk's queries (column j: window row hy0 + j / kHX,
+      // column j % kHX); -inf and 0 outside the volume and on the padding columns (P = 0).
+      // The loads go out before the stage wait.
+      constexpr int kPer = kKvCols / 32;
+      float l[kPer], dl[kPer];
 #pragma unroll
-      for (int k = 0; k < kKeys / 32; ++k) {
+      for (int k = 0; k < kPer; ++k) {
         const int j = lane + 32 * k;
-        const int qy = y0 - kR + j / kHX, qx = x0 - kR + j % kHX;
+        const int qy = y0 - R + hy0 + j / kHX, qx = x0 - R + j % kHX;
         const bool in = j < kWin && zp >= 0 && zp < p.Zg && qy >= 0 && qy < p.Y && qx >= 0 && qx < p.X;
-        l[k] = __builtin_huge_valf();
+        l[k] = -__builtin_huge_valf();
         dl[k] = 0.f;
         if (in) {
           int64_t r = ((int64_t)(zp - p.xz0) * p.Y + qy) * p.X + qx;
           if (p.map) r = __ldg(p.map + r);
           const int64_t row = (int64_t)bh * p.xtokens + r;
-          l[k] = __ldg(p.lse_l + row) * kLog2e;
-          dl[k] = __ldg(p.delta_l + row);
+          l[k] = -__ldg(p.lse_l + row) * kLog2e;
+          dl[k] = -__ldg(p.delta_l + row);
         }
       }
+      if (!wait_stage()) return false;
+      if (lane == 0) {
+        mbar_expect_tx(full, 2 * C::kK * kWin * 32);
+        for (int c = 0; c < C::kK; ++c) {
+          tma_load_5d(stage + c * C::kBoxC, &tq, full, 16 * c, x0 - R, y0 - R + hy0, zp - p.xz0, bh);
+          tma_load_5d(stage + C::kChunkBytes + c * C::kBoxC, &tdo, full, 16 * c, x0 - R, y0 - R + hy0, zp - p.xz0,
+                      bh);
+        }
+      }
+      float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kChunkBytes);
 #pragma unroll
-      for (int k = 0; k < kKeys / 32; ++k) {
+      for (int k = 0; k < kPer; ++k) {
         vals[lane + 32 * k] = l[k];
-        vals[kKeys + lane + 32 * k] = dl[k];
+        vals[kKvCols + lane + 32 * k] = dl[k];
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(full);
-      issued = ch + 1;
-    }
-    if (lane == 0) {
-      mbar_wait(bar(kGKvFull), 0, &g_bwd_errors, kWaitNs, kErrTeardown);
-      for (int ch = issued > C::kStages ? issued - C::kStages : 0; ch < issued; ++ch)
-        mbar_wait(bar(kGFull + ch % C::kStages), (ch / C::kStages) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
-    }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_f16(128, kKeys, BF16, false);
-      constexpr uint32_t idesc_acc = idesc_f16(128, D, BF16, true);
-      uint32_t commits[kGNumBars];
-      for (int i = 0; i < kGNumBars; ++i) commits[i] = 0u;
-      auto commit = [&](int bidx) {
-        mma_commit(bar(bidx));
-        ++commits[bidx];
-      };
-      auto stage_of = [&](int c) { return ring + (c % C::kStages) * C::kStageBytes; };
-      auto issue_s_dp = [&](int c) {
-        const uint32_t q = stage_of(c), dov = stage_of(c) + C::kPlaneBytes;
-        for (int kk = 0; kk < C::kK; ++kk)
-          mma_ss(tmem + kLColS, desc_sw32(k_smem + kk * C::kBoxT, 16, 256), desc_sw32(q + kk * C::kBoxP, 16, 256),
-                 idesc_s, kk > 0 ? 1u : 0u);
-        for (int kk = 0; kk < C::kK; ++kk)
-          mma_ss(tmem + kLColDP, desc_sw32(v_smem + kk * C::kBoxT, 16, 256), desc_sw32(dov + kk * C::kBoxP, 16, 256),
-                 idesc_s, kk > 0 ? 1u : 0u);
-        commit(kGSReady);
-      };
-      auto issue_acc = [&](int c) {
-        const uint32_t q = stage_of(c), dov = stage_of(c) + C::kPlaneBytes;
-        for (int j = 0; j < kKeys / 16; ++j)
-          mma_ts(tmem + kLColAcc + D, tmem + kLColP + 8 * j, desc_sw32(dov + j * 512, C::kBoxP, 256), idesc_acc,
-                 (c == 0 && j == 0) ? 0u : 1u);
-        for (int j = 0; j < kKeys / 16; ++j)
-          mma_ts(tmem + kLColAcc, tmem + kLColDS + 8 * j, desc_sw32(q + j * 512, C::kBoxP, 256), idesc_acc,
-                 (c == 0 && j == 0) ? 0u : 1u);
-        commit(kGPdsFree);
-        commit(kGEmpty + c % C::kStages);
-      };
-      auto wait_bar = [&](int bidx, int completion) -> bool {
-        if (!mbar_wait(bar(bidx), completion & 1, &g_bwd_errors, kWaitNs, kErrMma)) return false;
-        tc_fence_after();
-        return true;
-      };
-      auto wait_full = [&](int c) { return wait_bar(kGFull + c % C::kStages, c / C::kStages); };
-      bool ok = wait_bar(kGKvFull, 0) && wait_full(0);
-      if (ok) issue_s_dp(0);
-      for (int c = 0; ok && c < n_chunks; ++c) {
-        ok = wait_bar(kGSFree, c);
-        if (!ok) break;
-        if (c + 1 < n_chunks) {
-          ok = wait_full(c + 1);
-          if (!ok) break;
-          issue_s_dp(c + 1);
-        }
-        ok = wait_bar(kGPdsReady, c);
-        if (!ok) break;
-        issue_acc(c);
-      }
-      commit(kGDrain);
-      for (int i = 0; i < kGNumBars; ++i)
-        if (commits[i]) mbar_wait(bar(i), (commits[i] - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
-    }
-  } else {
-    // ------------------------------------------------------------------ softmax (8 warps) + epilogue
-    const int quarter = warp & 3, half = warp >> 2;
-    const uint32_t t_lanes = tmem + ((uint32_t)(quarter * 32) << 16);
-    const int kz = z0 + quarter, kyl = lane >> 3, kxl = lane & 7;
-    const int ky = y0 + kyl, kx = x0 + kxl;
-    const bool row_ok = kz < p.Z && ky < p.Y && kx < p.X;
-    // this warp's kHalf query columns of the halo window that lie in the key's cube
-    uint64_t mask = 0ull;
-#pragma unroll
-    for (int i = 0; i < kHalf; ++i) {
-      const int j = kHalf * half + i, hy = j / kHX, hx = j % kHX;
-      if (j < kWin && (unsigned)(hy - kyl) <= 2u * kR && (unsigned)(hx - kxl) <= 2u * kR) mask |= 1ull << i;
-    }
-    if (!row_ok) mask = 0ull;
-    const float sc = p.sc, inv_sqrt_d = p.inv_sqrt_d;
-    auto wait_warp = [&](int bidx, int completion) -> bool {
-      const bool r = mbar_wait(bar(bidx), completion & 1, &g_bwd_errors, kWaitNs, kErrSoftmax);
-      const bool all = __all_sync(0xffffffffu, r);
-      if (all) tc_fence_after();
-      return all;
+      return true;
     };
+    kv_producer_role<kStages>(bars, n_chunks, lane, tiles, chunk);
+  } else if (warp == kKvMma) {
+    kv_mma_role<kStages>(
+        bars, n_chunks,
+        [&](int c, int bf) {
+          kv_issue_sdp<D, BF16>(tmem, k_smem, v_smem, stage_of(c), stage_of(c) + C::kChunkBytes, bf);
+        },
+        [&](int c, int bf) { kv_issue_acc<D, BF16>(tmem, stage_of(c), stage_of(c) + C::kChunkBytes, bf, c == 0); });
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int quarter = warp & 3, half = warp >> 2, col0 = half * kKvW;
+    const uint32_t t_lanes = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int zl = 2 * quarter + (lane >> 4), kyl = (lane >> 2) & 3, kxl = lane & 3;  // key within the box
+    const int kz = z0 + zl, ky = y0 + kyl, kx = x0 + kxl;
+    const bool row_ok = kz < p.Z && ky < p.Y && kx < p.X;
+    // this warp's chunk columns inside the key's (y, x) square, per chunk of a plane (bit
+    // i: column col0 + i)
+    uint64_t mask0 = 0ull, mask1 = 0ull;
+#pragma unroll
+    for (int hh = 0; hh < kParts; ++hh)
+#pragma unroll
+      for (int i = 0; i < kKvW; ++i) {
+        const int j = col0 + i, hy = kRowsH * hh + j / kHX, hx = j % kHX;
+        if (row_ok && j < kWin && (unsigned)(hy - kyl) <= 2u * R && (unsigned)(hx - kxl) <= 2u * R)
+          (hh ? mask1 : mask0) |= 1ull << i;
+      }
+    const float sc = p.sc;
     bool ok = true;
     for (int ch = 0; ch < n_chunks; ++ch) {
-      ok = wait_warp(kGSReady, ch);
+      const int bf = ch % kKvBuf;
+      ok = kv_wait_warp(bars, kVSReady + bf, ch / kKvBuf);
       if (!ok) break;
-      const int zp = chunk_plane(ch);
-      const bool active = (unsigned)(zp - (p.cz0 + kz) + kR) <= 2u * kR;  // warp-uniform
-      const float *vals = reinterpret_cast<const float *>(ring_ptr + (size_t)(ch % C::kStages) * C::kStageBytes +
-                                                          2 * C::kPlaneBytes);
-      uint32_t pw[kHalf / 16][8], dw[kHalf / 16][8];
-      if (active) {
-#pragma unroll
-        for (int gi = 0; gi < kHalf / 16; ++gi) {
-          const int col0 = kHalf * half + 16 * gi;
-          uint32_t sv[16], dv[16];
-          tmem_ld16(t_lanes + kLColS + col0, sv);
-          tmem_ld16(t_lanes + kLColDP + col0, dv);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int j = col0 + 2 * i, bit = 16 * gi + 2 * i;
-            const float p0 = (mask >> bit) & 1ull ? ex2_approx(fmaf(__uint_as_float(sv[2 * i]), sc, -vals[j])) : 0.f;
-            const float p1 =
-                (mask >> (bit + 1)) & 1ull ? ex2_approx(fmaf(__uint_as_float(sv[2 * i + 1]), sc, -vals[j + 1])) : 0.f;
-            const float d0 = p0 * (__uint_as_float(dv[2 * i]) - vals[kKeys + j]) * inv_sqrt_d;
-            const float d1 = p1 * (__uint_as_float(dv[2 * i + 1]) - vals[kKeys + j + 1]) * inv_sqrt_d;
-            pw[gi][i] = pack2<BF16>(p0, p1);
-            dw[gi][i] = pack2<BF16>(d0, d1);
-          }
-        }
+      const int pl = chunk_plane(ch);  // query plane z0 - R + pl
+      const float *vals =
+          reinterpret_cast<const float *>(ring_ptr + (size_t)(ch % kStages) * C::kStageBytes + 2 * C::kChunkBytes);
+      const uint32_t ts = t_lanes + C::col_s(bf) + col0, tdp = t_lanes + C::col_dp(bf) + col0;
+      if ((unsigned)(pl - 2 * quarter) <= 2u * R + 1u) {  // the plane reaches one of the warp's key planes
+        const uint64_t m = (unsigned)(pl - zl) <= 2u * R ? ((ch % kParts) ? mask1 : mask0) : 0ull;
+        kv_chunk<BF16, true, false>(ts, tdp, vals + col0, vals + kKvCols + col0, sc, m);
       } else {
-#pragma unroll
-        for (int gi = 0; gi < kHalf / 16; ++gi)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) pw[gi][i] = dw[gi][i] = 0u;
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kGSFree));
-      if (ch > 0) {
-        ok = wait_warp(kGPdsFree, ch - 1);
-        if (!ok) break;
-      }
-#pragma unroll
-      for (int gi = 0; gi < kHalf / 16; ++gi) {
-        tmem_st8(t_lanes + kLColP + (kHalf / 2) * half + 8 * gi, pw[gi]);
-        tmem_st8(t_lanes + kLColDS + (kHalf / 2) * half + 8 * gi, dw[gi]);
+        kv_zero_chunk(ts, tdp);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kGPdsReady));
+      if (lane == 0) mbar_arrive(smem_u32(&bars[kVPdsReady + bf]));
     }
-    if (ok) ok = wait_warp(kGPdsFree, n_chunks - 1);
+    if (ok) ok = kv_wait_warp(bars, kVAccReady, 0);
     if (ok) {
-      // warps 0-3 write dK rows, warps 4-7 dV rows (storage dtype)
+      int64_t r = ((int64_t)kz * p.Y + ky) * p.X + kx;
+      if (row_ok && p.map) r = p.map[r];
       uint32_t acc[D];
-      const uint32_t col = kLColAcc + (half ? D : 0);
-#pragma unroll
-      for (int c = 0; c < D / 16; ++c) tmem_ld16(t_lanes + col + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(acc + 16 * c));
-      tmem_wait_ld();
-      if (row_ok) {
-        int64_t r = ((int64_t)kz * p.Y + ky) * p.X + kx;
-        if (p.map) r = p.map[r];
+      kv_load_acc<D>(t_lanes, half, acc);
+      if (row_ok) {  // storage dtype; warps 0-3 write dK (scaled by 1/sqrt(D)), 4-7 dV
+        const float scale = half ? 1.f : p.inv_sqrt_d;
         uint16_t *dst = static_cast<uint16_t *>(half ? p.dvl : p.dkl) + ((int64_t)bg * p.tokens + r) * D;
         uint32_t out[D / 2];
 #pragma unroll
-        for (int i = 0; i < D / 2; ++i) out[i] = pack2<BF16>(__uint_as_float(acc[2 * i]), __uint_as_float(acc[2 * i + 1]));
+        for (int i = 0; i < D / 2; ++i)
+          out[i] = pack2<BF16>(__uint_as_float(acc[2 * i]) * scale, __uint_as_float(acc[2 * i + 1]) * scale);
 #pragma unroll
         for (int v = 0; v < D / 8; ++v)
           reinterpret_cast<uint4 *>(dst)[v] = make_uint4(out[4 * v], out[4 * v + 1], out[4 * v + 2], out[4 * v + 3]);
       }
     }
-    tmem_wait_st();
   }
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kKvMma) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, kKvTmemCols);
   }
 }
 
 template <int D, bool BF16, int R>
 int launch_lkv_t(const StencilBwdArgs &a, cudaStream_t stream) {
-  using G = BGeo<R>;
-  constexpr int kHY = G::kHY, kHX = G::kHX;
-  using C = LkvCfg<D, G::kKeys>;
+  using G = KGeo<R>;
+  using C = KvCfg<D>;
   const int Z = a.grid[0], Y = a.grid[1], X = a.grid[2];
   const uint64_t es = 2;
   const uint64_t bh = (uint64_t)a.batch * a.heads, bgs = (uint64_t)a.batch * a.kv_heads;
@@ -1308,7 +1313,7 @@ int launch_lkv_t(const StencilBwdArgs &a, cudaStream_t stream) {
     const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)a.k_planes, bgs};
     const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es,
                                  (uint64_t)a.k_planes * Y * X * D * es};
-    const uint32_t box[5] = {16, kTX, kTY, kTZ, 1};
+    const uint32_t box[5] = {16, G::kBX, G::kBY, G::kBZ, 1};
     if (int st = encode_operand(&tkl, a.dtype, a.kl, 5, dims, strides, box)) return st;
     if (int st = encode_operand(&tvl, a.dtype, a.vl, 5, dims, strides, box)) return st;
   }
@@ -1316,7 +1321,7 @@ int launch_lkv_t(const StencilBwdArgs &a, cudaStream_t stream) {
     const uint64_t dims[5] = {(uint64_t)D, (uint64_t)X, (uint64_t)Y, (uint64_t)a.x_planes, bh};
     const uint64_t strides[4] = {D * es, X * D * es, (uint64_t)Y * X * D * es,
                                  (uint64_t)a.x_planes * Y * X * D * es};
-    const uint32_t box[5] = {16, kHX, kHY, 1, 1};
+    const uint32_t box[5] = {16, G::kHX, G::kRowsH, 1, 1};  // one chunk's window rows
     if (int st = encode_operand(&tq, a.dtype, a.q_halo, 5, dims, strides, box)) return st;
     if (int st = encode_operand(&tdo, a.dtype, a.dol_halo, 5, dims, strides, box)) return st;
   }
@@ -1324,9 +1329,9 @@ int launch_lkv_t(const StencilBwdArgs &a, cudaStream_t stream) {
   p.Z = Z;
   p.Y = Y;
   p.X = X;
-  p.tiles_z = (Z + kTZ - 1) / kTZ;
-  p.tiles_y = (Y + kTY - 1) / kTY;
-  p.tiles_x = (X + kTX - 1) / kTX;
+  p.tiles_z = (Z + G::kBZ - 1) / G::kBZ;
+  p.tiles_y = (Y + G::kBY - 1) / G::kBY;
+  p.tiles_x = (X + G::kBX - 1) / G::kBX;
   p.heads = a.heads;
   p.kv_heads = a.kv_heads;
   p.rep = a.heads / a.kv_heads;
@@ -1349,7 +1354,7 @@ int launch_lkv_t(const StencilBwdArgs &a, cudaStream_t stream) {
   auto kernel = stencil_bwd_dkv_kernel<D, BF16, R>;
   static size_t seen[kMaxDevices] = {};
   if (int st = smem_optin(kernel, C::kSmemBytes, seen)) return st;
-  kernel<<<(unsigned)units, kThreads, C::kSmemBytes, stream>>>(tkl, tvl, tq, tdo, p);
+  kernel<<<(unsigned)units, kKvThreads, C::kSmemBytes, stream>>>(tkl, tvl, tq, tdo, p);
   P3D_LAUNCH_CHECK();
   return P3D_OK;
 }
@@ -1382,7 +1387,7 @@ void global_dkv_tc_splits(int batch, int heads, int kv_heads, int tokens, int su
                           int *per_split) {
   const int64_t base = (int64_t)batch * kv_heads * ((summaries + kGRows - 1) / kGRows);
   const int64_t total = (int64_t)(heads / kv_heads) * ((tokens + kGCols - 1) / kGCols);
-  const int sms = sm_count > 0 ? sm_count : 148;
+  const int sms = 2 * (sm_count > 0 ? sm_count : 148);  // two CTAs per SM
   int best_s = 1;
   double best_eff = -1.0;
   for (int s = 1; s <= 64 && s <= total; ++s) {

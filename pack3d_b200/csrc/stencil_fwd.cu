@@ -442,14 +442,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(128, kKeys, BF16, false);
       constexpr uint32_t idesc_pv = idesc_f16(128, D, BF16, true);
-      // Commits issued per barrier: teardown waits for the last phase of each, so that no
-      // arrive from a commit can land after the CTA has exited.
-      uint32_t commits[kNumBars];
-      for (int i = 0; i < kNumBars; ++i) commits[i] = 0u;
-      auto commit = [&](int b_idx) {
-        mma_commit(bar(b_idx));
-        ++commits[b_idx];
-      };
+      // Operations issued, for the teardown: it waits for the last phase of every barrier
+      // committed to, so that no arrive from a commit can land after the CTA has exited.
+      int n_s = 0, n_pv = 0;
+      bool o_ready = false;
       // Shared-memory descriptors are built once; an operand's descriptor is its base plus
       // (byte offset >> 4), one add per MMA (addresses stay inside the 14-bit field).
       const uint64_t desc_q = desc_sw32(q_smem, 16, 256);          // the Q tile, K-major
@@ -462,7 +458,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int c = 0; c < C::kK; ++c)
           mma_ss(t_s, desc_q + c * (C::kBoxQ >> 4), bk + c * (C::kBoxK >> 4), idesc_s, c > 0 ? 1u : 0u);
-        commit(kSFull);
+        mma_commit(bar(kSFull));
+        ++n_s;
       };
       // O += P(c) V(c); its completion frees the P buffer and O, and releases the ring stage.
       auto issue_pv = [&](int c) {
@@ -472,8 +469,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int j = 0; j < kKeys / 16; ++j)
           mma_ts(t_o, t_p + 8 * j, bv + j * (512 >> 4), idesc_pv, (first && j == 0) ? 0u : 1u);
-        commit(kPFree);
-        commit(kEmpty + c % C::kStages);
+        mma_commit(bar(kPFree));
+        mma_commit(bar(kEmpty + c % C::kStages));
+        ++n_pv;
       };
       auto wait_bar = [&](int b_idx, uint32_t parity) -> bool {
         if (!mbar_wait(bar(b_idx), parity, &g_fwd_errors, kWaitNs, kErrMma)) return false;
@@ -483,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       auto wait_full = [&](int ch) -> bool { return wait_bar(kFull + ch % C::kStages, (ch / C::kStages) & 1); };
       // Per chunk c: S(c + 1) as soon as the softmax warps have loaded S(c) (and chunk c + 1
       // has landed), then PV(c) once they have stored P(c).
-      bool ok = mbar_wait(bar(kQFull), 0, &g_fwd_errors, kWaitNs, kErrMma) && n_chunks > 0 && wait_full(0);
+      bool ok = wait_bar(kQFull, 0) && n_chunks > 0 && wait_full(0);
       if (ok) issue_s(0);
       for (int c = 0; ok && c < n_chunks; ++c) {
         if (c + 1 < n_chunks) {
@@ -495,13 +493,23 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!ok) break;
         issue_pv(c);
       }
-      if (ok) commit(kOReady);
+      if (ok) {
+        mma_commit(bar(kOReady));
+        o_ready = true;
+      }
       // TMEM is freed after the final __syncthreads: make sure every MMA issued above has
       // completed, and every commit has arrived, first -- on the normal path and after a
-      // timed-out wait alike.
-      commit(kDrain);
-      for (int i = 0; i < kNumBars; ++i)
-        if (commits[i]) mbar_wait(bar(i), (commits[i] - 1) & 1, &g_fwd_errors, kWaitNs, kErrTeardown);
+      // timed-out wait alike.  The drain commit's arrival means every operation completed;
+      // then each barrier's last commit has arrived or is about to.
+      mma_commit(bar(kDrain));
+      mbar_wait(bar(kDrain), 0, &g_fwd_errors, kWaitNs, kErrTeardown);
+      if (n_s) mbar_wait(bar(kSFull), (n_s - 1) & 1, &g_fwd_errors, kWaitNs, kErrTeardown);
+      if (n_pv) mbar_wait(bar(kPFree), (n_pv - 1) & 1, &g_fwd_errors, kWaitNs, kErrTeardown);
+      if (o_ready) mbar_wait(bar(kOReady), 0, &g_fwd_errors, kWaitNs, kErrTeardown);
+      for (int st = 0; st < C::kStages; ++st) {  // kEmpty[st]: once per PV of a chunk c with c % kStages == st
+        const int times = n_pv / C::kStages + (st < n_pv % C::kStages ? 1 : 0);
+        if (times) mbar_wait(bar(kEmpty + st), (times - 1) & 1, &g_fwd_errors, kWaitNs, kErrTeardown);
+      }
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue

@@ -226,6 +226,29 @@ def run(n_chunks=14, stages=4, seed=0, release="empty", max_steps=400000):
     return _schedule(state, roles, rng, max_steps)
 
 
+def _next_completion(state, rng):
+    """Index in the issue queue of the tensor-core operation that completes next.
+
+    By default operations complete in issue order.  With ``state.ordered_by_acc`` (a map
+    from operation kind to the accumulator it writes) only operations on the same
+    accumulator keep their order, and a commit arrives once every operation issued before
+    it has completed."""
+    order = getattr(state, "ordered_by_acc", None)
+    if order is None:
+        return 0
+    q, seen, ready = state.mma_queue, set(), []
+    for i, op in enumerate(q):
+        if op[0] == "commit":
+            if all(o[0] == "commit" for o in q[:i]):
+                ready.append(i)
+            continue
+        acc = order[op[0]](op)
+        if acc not in seen:
+            ready.append(i)
+            seen.add(acc)
+    return rng.choice(ready)
+
+
 def _schedule(state, roles, rng, max_steps):
     """Run the role programs and asynchronous completions in a random order until all finish."""
     epoch = 0            # bumped whenever an asynchronous event changes some barrier
@@ -245,10 +268,13 @@ def _schedule(state, roles, rng, max_steps):
             state.bar(f"full{s}").complete_tx(1)
             epoch += 1
         elif choice == "<tensor op completes>":
-            op = state.mma_queue.pop(0)  # tensor-core operations complete in issue order
+            op = state.mma_queue.pop(_next_completion(state, rng))
             if op[0] == "commit":
                 state.bar(op[1]).arrive()
             else:
+                hook = getattr(state, "on_complete", None)
+                if hook is not None:
+                    hook(op)
                 state.mma_done.add(op)
             epoch += 1
         else:
@@ -387,6 +413,8 @@ def run_dq(n_chunks=12, stages=3, seed=0, max_steps=400000):
     rng = random.Random(seed)
     state = State(n_chunks=n_chunks, stages=stages)
     state.ds_stored, state.dq_issued, state.s_read = {}, set(), {}
+    # S, dP and dQ are three accumulators: only operations on the same one keep their order
+    state.ordered_by_acc = {"S": lambda op: "s", "DP": lambda op: "dp", "DQ": lambda op: "dq"}
     bars = {"qfull": 1, "drain": 1, "sready": 1, "sfree": 4, "dpready": 1, "dsready": 4, "dqdone": 1}
     for s in range(4):
         bars[f"full{s}"] = 1
@@ -396,128 +424,6 @@ def run_dq(n_chunks=12, stages=3, seed=0, max_steps=400000):
     roles = {"producer": dq_producer(state), "mma": dq_mma(state)}
     for w in range(4):
         roles[f"softmax{w}"] = dq_softmax(state, w)
-    return _schedule(state, roles, rng, max_steps)
-
-
-# ------------------------------------------------------------------ global dSK / dSV kernel
-# Model of global_dkv_tc_kernel -- and of stencil_bwd_dkv_kernel (local dK / dV), which runs
-# the same barrier protocol on other data: one S^T / dP^T buffer pair (released by the eight softmax
-# warps once they have read it), one P^T / dS^T buffer (rewritten once the previous
-# chunk's dSV / dSK products completed), a ring of query chunks filled by TMA copies plus
-# the producer warp's own lse / Delta stores.
-
-def gkv_producer(state):
-    k = state.stages
-    for ch in range(state.n_chunks):
-        s = ch % k
-        if ch >= k:
-            while not _wait(state, f"empty{s}", (ch // k - 1) & 1, ch // k - 1):
-                yield ("wait", f"empty{s}")
-        old = state.stage_chunk.get(s)
-        if old is not None:
-            for op in (("SDP", 0, old), ("ACC", 0, old)):
-                if op not in state.mma_done:
-                    raise ProtocolError(f"stage {s} overwritten with chunk {ch} while {op} is outstanding")
-            if len(state.read_vals.get(old, ())) != 8:
-                raise ProtocolError(f"stage {s} overwritten while softmax warps may read chunk {old}'s lse")
-        state.bar(f"full{s}").arrive(tx=1)  # expect_tx + copies
-        state.stage_chunk[s] = ch
-        state.tma_inflight.append((s, ch))
-        yield ("step", None)
-        state.bar(f"full{s}").arrive()      # lse / Delta stores of the warp
-        yield ("step", None)
-
-
-def gkv_mma(state):
-    k, n = state.stages, state.n_chunks
-
-    def commit(name):
-        state.mma_queue.append(("commit", name))
-
-    def landed(c):
-        if state.stage_landed.get(c % k) != c:
-            raise ProtocolError(f"chunk {c} read before its copy landed")
-
-    def issue_sdp(c):
-        landed(c)
-        if c >= 1 and len(state.sdp_read.get(c - 1, ())) != 8:
-            raise ProtocolError(f"S/dP({c}) overwrite buffers still being read")
-        state.mma_queue.append(("SDP", 0, c))
-        commit("sready")
-
-    def issue_acc(c):
-        landed(c)
-        if len(state.pds_stored.get(c, ())) != 8:
-            raise ProtocolError(f"dSV/dSK({c}) issued before all warps stored P/dS")
-        state.mma_queue.append(("ACC", 0, c))
-        commit("pdsfree")
-        commit(f"empty{c % k}")
-
-    def waits(name, completion):
-        while not _wait(state, name, completion & 1, completion):
-            yield ("wait", name)
-
-    yield from waits("kvfull", 0)
-    yield from waits("full0", 0)
-    issue_sdp(0)
-    yield ("step", None)
-    for c in range(n):
-        yield from waits("sfree", c)
-        if c + 1 < n:
-            yield from waits(f"full{(c + 1) % k}", (c + 1) // k)
-            issue_sdp(c + 1)
-            yield ("step", None)
-        yield from waits("pdsready", c)
-        issue_acc(c)
-        yield ("step", None)
-    commit("drain")
-    yield from waits("drain", 0)
-
-
-def gkv_softmax(state, w):
-    n = state.n_chunks
-
-    def waits(name, completion):
-        while not _wait(state, name, completion & 1, completion):
-            yield ("wait", name)
-
-    for ch in range(n):
-        yield from waits("sready", ch)
-        if ("SDP", 0, ch) not in state.mma_done:
-            raise ProtocolError(f"S/dP({ch}) read before it completed")
-        if state.stage_chunk.get(ch % state.stages) != ch:
-            raise ProtocolError(f"lse of chunk {ch} read from a stage holding another chunk")
-        yield ("step", None)
-        state.read_vals.setdefault(ch, set()).add(w)
-        state.sdp_read.setdefault(ch, set()).add(w)
-        state.bar("sfree").arrive()
-        yield ("step", None)
-        if ch > 0:
-            yield from waits("pdsfree", ch - 1)
-            if ("ACC", 0, ch - 1) not in state.mma_done:
-                raise ProtocolError(f"P/dS({ch}) stored while dSV/dSK({ch - 1}) may read them")
-        state.pds_stored.setdefault(ch, set()).add(w)
-        state.bar("pdsready").arrive()
-        yield ("step", None)
-    yield from waits("pdsfree", n - 1)
-    if ("ACC", 0, n - 1) not in state.mma_done:
-        raise ProtocolError("accumulators read before the last products completed")
-
-
-def run_gkv(n_chunks=10, stages=4, seed=0, max_steps=400000):
-    """Replay one random interleaving of the global dSK / dSV kernel's protocol."""
-    rng = random.Random(seed)
-    state = State(n_chunks=n_chunks, stages=stages)
-    state.sdp_read, state.pds_stored, state.read_vals = {}, {}, {}
-    bars = {"kvfull": 1, "drain": 1, "sready": 1, "sfree": 8, "pdsready": 8, "pdsfree": 1}
-    for s in range(4):
-        bars[f"full{s}"] = 2
-        bars[f"empty{s}"] = 1
-    state.bars = {name: Barrier(name, cnt) for name, cnt in bars.items()}
-    state.bar("kvfull").arrive(tx=0)
-    roles = {"producer": gkv_producer(state), "mma": gkv_mma(state)}
-    for w in range(8):
-        roles[f"softmax{w}"] = gkv_softmax(state, w)
     return _schedule(state, roles, rng, max_steps)
 
 
@@ -637,6 +543,7 @@ def run_fwd(n_chunks=14, stages=4, seed=0, max_steps=400000, skip_sfree=False):
     for the softmax warps to load it."""
     rng = random.Random(seed)
     state = State(n_chunks=n_chunks, stages=stages)
+    state.ordered_by_acc = {"S": lambda op: "s", "PV": lambda op: "o"}  # S and O: separate accumulators
     bars = {"qfull": 1, "drain": 1, "oready": 1, "sfull": 1, "sfree": WARPS, "pfull": WARPS, "pfree": 1}
     for s in range(4):
         bars[f"full{s}"] = 1
@@ -646,4 +553,150 @@ def run_fwd(n_chunks=14, stages=4, seed=0, max_steps=400000, skip_sfree=False):
     roles = {"producer": fwd1_producer(state), "mma": fwd1_mma(state, skip_sfree)}
     for w in range(WARPS):
         roles[f"softmax{w}"] = fwd1_softmax(state, w, random.Random(rng.random()))
+    return _schedule(state, roles, rng, max_steps)
+
+
+# ---------------------------------------------------- dK / dV kernels, two CTAs per SM
+# Model of stencil_bwd_dkv_kernel and global_dkv_tc_kernel (pack3d_b200/csrc/stencil_bwd.cu):
+# TMEM holds ``buffers`` S^T / dP^T buffer pairs, chunk c using buffer c % buffers, and the
+# softmax warps write P^T and dS^T back over the buffer they read, as 16-bit pairs.  The MMA
+# warp issues S^T / dP^T of the first ``buffers`` chunks, then per chunk c waits for
+# pdsready[b](c), issues the dV / dK products, commits empty[c % stages] and accdone[b],
+# waits for accdone[b](c) and issues S^T / dP^T of chunk c + buffers into the same buffer
+# (sready[b]).  Tensor-core operations complete in issue order only when they write the
+# same accumulator (``ordered_by_acc``): S^T(c + buffers) and the products of chunk c write
+# different ones, so only the accdone wait keeps S^T from landing on P^T(c) before the
+# products read it.
+
+def ip_producer(state):
+    k = state.stages
+    for ch in range(state.n_chunks):
+        s = ch % k
+        if ch >= k:
+            while not _wait(state, f"empty{s}", (ch // k - 1) & 1, ch // k - 1):
+                yield ("wait", f"empty{s}")
+        old = state.stage_chunk.get(s)
+        if old is not None:
+            for op in (("SDP", 0, old), ("ACC", 0, old)):
+                if op not in state.mma_done:
+                    raise ProtocolError(f"stage {s} overwritten with chunk {ch} while {op} is outstanding")
+            if len(state.read_vals.get(old, ())) != state.warps:
+                raise ProtocolError(f"stage {s} overwritten while softmax warps may read chunk {old}'s lse")
+        state.bar(f"full{s}").arrive(tx=1)  # expect_tx + copies
+        state.stage_chunk[s] = ch
+        state.tma_inflight.append((s, ch))
+        yield ("step", None)
+        state.bar(f"full{s}").arrive()      # lse / Delta stores of the warp
+        yield ("step", None)
+
+
+def ip_mma(state, skip_accdone=False):
+    k, n, nb = state.stages, state.n_chunks, state.buffers
+
+    def commit(name):
+        state.mma_queue.append(("commit", name))
+
+    def landed(c):
+        if state.stage_landed.get(c % k) != c:
+            raise ProtocolError(f"chunk {c} read before its copy landed")
+
+    def waits(name, completion):
+        while not _wait(state, name, completion & 1, completion):
+            yield ("wait", name)
+
+    def issue_sdp(c):
+        yield from waits(f"full{c % k}", c // k)
+        landed(c)
+        state.mma_queue.append(("SDP", 0, c))
+        commit(f"sready{c % nb}")
+        yield ("step", None)
+
+    yield from waits("kvfull", 0)
+    for c in range(min(nb, n)):
+        yield from issue_sdp(c)
+    for c in range(n):
+        b = c % nb
+        yield from waits(f"pdsready{b}", c // nb)
+        landed(c)
+        if len(state.pds_stored.get(c, ())) != state.warps:
+            raise ProtocolError(f"dV/dK({c}) issued before all warps stored P/dS")
+        state.mma_queue.append(("ACC", 0, c))
+        commit(f"empty{c % k}")
+        commit(f"accdone{b}")
+        yield ("step", None)
+        if c + nb < n:
+            if not skip_accdone:
+                yield from waits(f"accdone{b}", c // nb)
+            yield from issue_sdp(c + nb)
+    commit("accready")
+    yield ("step", None)
+    yield from waits("accready", 0)
+
+
+def ip_softmax(state, w):
+    n, nb = state.n_chunks, state.buffers
+
+    def waits(name, completion):
+        while not _wait(state, name, completion & 1, completion):
+            yield ("wait", name)
+
+    for ch in range(n):
+        b = ch % nb
+        yield from waits(f"sready{b}", ch // nb)
+        if state.tmem.get((w, b)) != ("S", ch):
+            raise ProtocolError(f"warp {w} loaded S/dP({ch}) but its TMEM lanes hold {state.tmem.get((w, b))}")
+        if state.stage_chunk.get(ch % state.stages) != ch:
+            raise ProtocolError(f"lse of chunk {ch} read from a stage holding another chunk")
+        state.read_vals.setdefault(ch, set()).add(w)
+        yield ("step", None)
+        state.tmem[(w, b)] = ("P", ch)     # P^T / dS^T written over S^T / dP^T of buffer b
+        state.pds_stored.setdefault(ch, set()).add(w)
+        state.bar(f"pdsready{b}").arrive()
+        yield ("step", None)
+    yield from waits("accready", 0)
+    if ("ACC", 0, n - 1) not in state.mma_done:
+        raise ProtocolError("accumulators read before the last products completed")
+
+
+def run_ip(n_chunks=10, stages=4, seed=0, warps=8, buffers=1, skip_accdone=False, max_steps=400000):
+    """Replay one random interleaving of the dK / dV kernels' protocol.
+
+    TMEM contents are tracked per (softmax warp, buffer): S^T(c) lands when its MMA
+    completes, P^T(c) when the warp stores it, and the dV / dK products of chunk c must find
+    P^T(c) there when they run."""
+    rng = random.Random(seed)
+    state = State(n_chunks=n_chunks, stages=stages)
+    state.pds_stored, state.read_vals, state.tmem, state.warps = {}, {}, {}, warps
+    state.buffers = buffers
+    state.ordered_by_acc = {"SDP": lambda op: f"sdp{op[2] % buffers}", "ACC": lambda op: "acc"}
+    bars = {"kvfull": 1, "accready": 1}
+    for b in range(buffers):
+        bars[f"sready{b}"] = 1
+        bars[f"pdsready{b}"] = warps
+        bars[f"accdone{b}"] = 1
+    for s in range(stages):
+        bars[f"full{s}"] = 2
+        bars[f"empty{s}"] = 1
+    state.bars = {name: Barrier(name, cnt) for name, cnt in bars.items()}
+    state.bar("kvfull").arrive(tx=0)
+    roles = {"producer": ip_producer(state), "mma": ip_mma(state, skip_accdone)}
+    for w in range(warps):
+        roles[f"softmax{w}"] = ip_softmax(state, w)
+
+    def on_complete(op):
+        kind, _, c = op
+        b = c % buffers
+        if kind == "SDP":
+            for v in range(warps):
+                held = state.tmem.get((v, b))
+                if held == ("P", c - buffers) and ("ACC", 0, c - buffers) not in state.mma_done:
+                    raise ProtocolError(f"S/dP({c}) overwrote P/dS({c - buffers}) before dV/dK({c - buffers}) "
+                                        "read them")
+                state.tmem[(v, b)] = ("S", c)
+        elif kind == "ACC":
+            for v in range(warps):
+                if state.tmem.get((v, b)) != ("P", c):
+                    raise ProtocolError(f"dV/dK({c}) read lanes of warp {v} holding {state.tmem.get((v, b))}")
+
+    state.on_complete = on_complete
     return _schedule(state, roles, rng, max_steps)
