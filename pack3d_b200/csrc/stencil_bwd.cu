@@ -565,52 +565,60 @@ int launch_dq_t(const StencilBwdArgs &a, cudaStream_t stream) {
 //
 // They run two CTAs per SM: the tensor cores are fed by one issuing warp per CTA, and
 // while one CTA's softmax warps work the other CTA's products run.  Each CTA holds 256 TMEM
-// columns: kKvBuf (S^T, dP^T) buffer pairs of kKvCols columns each, then the accumulators
-// dK [A, A + D), dV [A + D, A + 2D) (A = 2 kKvCols kKvBuf).  The softmax warps write P^T and
-// dS^T back over the S^T and dP^T buffer they read, as 16-bit pairs.  Chunk c uses buffer
-// c % kKvBuf.  Per chunk the MMA warp waits for P^T / dS^T of chunk c, issues its dV / dK
-// products, releases the chunk's ring stage, waits for those products to complete
-// (tcgen05.mma operations are ordered only when they share an accumulator, and S^T(c +
-// kKvBuf) overwrites P^T(c)), then issues S^T / dP^T of chunk c + kKvBuf.
-// tests/stencil_protocol.py (run_ip) replays this barrier protocol with the hardware's
-// parity semantics, tensor-core operations completing in order only per accumulator, and
-// the TMEM contents of every softmax warp.
+// columns: an S^T buffer [0, 64), a dP^T buffer [64, 128), then -- for head_dim <= 48 -- a
+// 32-column P^T buffer, then the accumulators dK, dV (D columns each).  The softmax warps
+// write dS^T back over the dP^T columns they read, as 16-bit pairs, and P^T into its own
+// buffer (or, for head_dim 64, where no room is left, over S^T).  S^T(c) and dP^T(c) commit
+// to separate barriers: the warps load S^T, release it (so that, with a separate P^T buffer,
+// S^T(c + 1) is issued at once and runs while they exponentiate), then wait for dP^T.  Per
+// chunk the MMA warp waits for P^T / dS^T of chunk c, issues its dV / dK products, releases
+// the chunk's ring stage, waits for those products to complete (tcgen05.mma operations are
+// ordered only when they share an accumulator, and dP^T(c + 1) overwrites dS^T(c)), then
+// issues dP^T(c + 1) (and S^T(c + 1) when P^T lives over S^T).  tests/stencil_protocol.py
+// (run_ip) replays this barrier protocol with the hardware's parity semantics, tensor-core
+// operations completing in order only per accumulator, and each warp's TMEM contents.
 //
 // Roles: eight softmax warps (warp w serves TMEM lanes 32(w % 4).. and query columns
-// [W(w / 4), W(w / 4) + W) of a chunk, W = kKvCols / 2, its pairs written at the start of its
-// own column range, so it never overwrites scores another warp has still to load), the TMA
-// producer warp (query chunks by TMA, lse / Delta beside them), the MMA warp.  Every wait
-// is bounded.
+// [32(w / 4), 32(w / 4) + 32) of a chunk), the TMA producer warp (query chunks by TMA, lse /
+// Delta beside them), the MMA warp, which issues warp-wide (every lane runs the loop with the
+// same operands and elect.sync picks the issuing lane).  Every wait is bounded.
 constexpr uint32_t kKvTmemCols = 256;
 constexpr int kKvCols = 64;          // queries per chunk
-constexpr int kKvBuf = 1;            // S^T / dP^T buffers
 constexpr int kKvSoft = 8;           // softmax warps
-constexpr int kKvW = 4 * kKvCols / kKvSoft;  // columns per softmax warp
+constexpr int kKvW = 4 * kKvCols / kKvSoft;  // columns per softmax warp (32)
 constexpr int kKvProducer = kKvSoft, kKvMma = kKvSoft + 1, kKvThreads = 32 * (kKvSoft + 2);
 constexpr int kKvMaxStages = 8;
 // Of every 8 exp2 pairs of a softmax warp, this many run as the degree-3 polynomial on the
 // FMA pipe (exp2_poly2, relative error < 1e-4, far below the 16-bit rounding of P) instead of
 // the MUFU: 0 / 2 / 3 / 4 measured 11.06 / 10.96 / 11.14 / 11.23 ms for the config-3 backward.
 constexpr int kKvPolyPairs = 2;
-static_assert(kKvW % 16 == 0, "a warp's columns must be whole groups of 16");
-static_assert(kKvCols <= 64, "the column masks are 64-bit");
+static_assert(kKvW == 32, "a softmax warp serves 32 columns (two groups of 16)");
 
 enum KvBar {
   kVKvFull = 0,                            // the K and V (or SK and SV) tiles landed
   kVFull = 1,                              // [stage]: query chunk copies (tx) + the producer's lse / Delta stores
   kVEmpty = kVFull + kKvMaxStages,         // [stage]: committed after the dV / dK products of the chunk it held
-  kVSReady = kVEmpty + kKvMaxStages,       // [buffer]: S^T, dP^T of a chunk complete
-  kVPdsReady = kVSReady + kKvBuf,          // [buffer]: every softmax warp stored its P^T, dS^T of a chunk
-  kVAccDone = kVPdsReady + kKvBuf,         // [buffer]: the dV / dK products of a chunk complete
-  kVAccReady = kVAccDone + kKvBuf,         // every product complete: the accumulators are final
+  kVSReady = kVEmpty + kKvMaxStages,       // S^T of a chunk complete
+  kVSFree = kVSReady + 1,                  // every softmax warp loaded its S^T columns
+  kVDPReady = kVSFree + 1,                 // dP^T of a chunk complete
+  kVPdsReady = kVDPReady + 1,              // every softmax warp stored its P^T, dS^T of a chunk
+  kVAccDone = kVPdsReady + 1,              // the dV / dK products of a chunk complete
+  kVAccReady = kVAccDone + 1,              // every product complete: the accumulators are final
   kVNumBars = kVAccReady + 1
 };
 
 template <int D>
 struct KvCfg {
-  static constexpr uint32_t kColAcc = 2 * kKvCols * kKvBuf;
-  static constexpr uint32_t col_s(int b) { return (uint32_t)(2 * kKvCols * b); }
-  static constexpr uint32_t col_dp(int b) { return (uint32_t)(2 * kKvCols * b + kKvCols); }
+  // a P^T buffer of its own when it fits beside S^T, dP^T and the accumulators
+  static constexpr bool kSepP = 2 * kKvCols + kKvCols / 2 + 2 * D <= (int)kKvTmemCols;
+  static constexpr uint32_t kColS = 0, kColDP = kKvCols;
+  static constexpr uint32_t kColP = kSepP ? 2 * kKvCols : 0;
+  static constexpr uint32_t kColAcc = kSepP ? 2 * kKvCols + kKvCols / 2 : 2 * kKvCols;
+  // TMEM column of the P^T pairs of query group j (queries 16j .. 16j + 15), and of the
+  // dS^T pairs: softmax warps of column half h store their group g at the start of their
+  // own range (dS^T, in-place P^T: 32h + 8g) or packed (separate P^T: 16h + 8g = 8j)
+  static constexpr uint32_t p_col(int j) { return kColP + (kSepP ? 8 * j : 32 * (j / 2) + 8 * (j % 2)); }
+  static constexpr uint32_t ds_col(int j) { return kColDP + 32 * (j / 2) + 8 * (j % 2); }
   static constexpr int kK = D / 16;
   static constexpr int kBoxT = kRows * 32;       // key / summary tile: 128 rows x 16 channels
   static constexpr int kBoxC = kKvCols * 32;     // query chunk: kKvCols rows x 16 channels
@@ -626,7 +634,7 @@ struct KvCfg {
   static constexpr int kStages = kRoom > kKvMaxStages ? kKvMaxStages : kRoom;
   static constexpr int kSmemNeed = kFixed + kStages * kStageBytes;
   static constexpr int kSmemBytes = kSmemNeed > kMinSmem ? kSmemNeed : kMinSmem;
-  static_assert(kStages >= kKvBuf + 1, "the ring must hold the chunks in flight and the next");
+  static_assert(kStages >= 2, "the ring must hold the chunk in flight and the next");
   static_assert(kSmemBytes <= kMaxSmem, "shared memory budget");
   static_assert(kColAcc + 2 * D <= kKvTmemCols, "TMEM budget");
 };
@@ -637,11 +645,11 @@ __device__ __forceinline__ void kv_init(uint64_t *bars, int stages) {
     mbar_init(smem_u32(&bars[kVFull + s]), 2);
     mbar_init(smem_u32(&bars[kVEmpty + s]), 1);
   }
-  for (int b = 0; b < kKvBuf; ++b) {
-    mbar_init(smem_u32(&bars[kVSReady + b]), 1);
-    mbar_init(smem_u32(&bars[kVPdsReady + b]), kKvSoft);
-    mbar_init(smem_u32(&bars[kVAccDone + b]), 1);
-  }
+  mbar_init(smem_u32(&bars[kVSReady]), 1);
+  mbar_init(smem_u32(&bars[kVSFree]), kKvSoft);
+  mbar_init(smem_u32(&bars[kVDPReady]), 1);
+  mbar_init(smem_u32(&bars[kVPdsReady]), kKvSoft);
+  mbar_init(smem_u32(&bars[kVAccDone]), 1);
   mbar_init(smem_u32(&bars[kVAccReady]), 1);
   fence_mbar_init();
 }
@@ -678,53 +686,66 @@ __device__ __forceinline__ void kv_producer_role(uint64_t *bars, int n_chunks, i
   }
 }
 
-// The whole MMA warp: sdp(c, b) issues S^T, dP^T of chunk c into buffer b, acc(c, b) its
-// dV / dK products from buffer b, with the warp-wide (elected-lane) MMA forms; every lane
-// waits on the barriers.
-template <int kStages, class Sdp, class Acc>
-__device__ __forceinline__ void kv_mma_role(uint64_t *bars, int n_chunks, Sdp sdp, Acc acc) {
+// The whole MMA warp: s(c) issues S^T of chunk c, dp(c) its dP^T, acc(c) its dV / dK
+// products, with the warp-wide (elected-lane) MMA forms; every lane waits on the barriers.
+template <int kStages, bool kSepP, class IssueS, class IssueDP, class Acc>
+__device__ __forceinline__ void kv_mma_role(uint64_t *bars, int n_chunks, IssueS s_mma, IssueDP dp_mma, Acc acc) {
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  int n_sdp = 0, n_acc = 0;  // chunks whose S^T / dP^T, whose products were issued
+  int n_s = 0, n_dp = 0, n_acc = 0;  // chunks whose S^T, dP^T, products were issued
   auto wait_bar = [&](int b, int completion) -> bool {
     const bool r = mbar_wait(bar(b), completion & 1, &g_bwd_errors, kWaitNs, kErrMma);
     if (!__all_sync(0xffffffffu, r)) return false;
     tc_fence_after();
     return true;
   };
-  auto issue_sdp = [&](int c) -> bool {
-    if (!wait_bar(kVFull + c % kStages, c / kStages)) return false;
-    sdp(c, c % kKvBuf);
-    mma_commit_warp(bar(kVSReady + c % kKvBuf));
-    n_sdp = c + 1;
-    return true;
+  auto issue_s = [&](int c) {
+    s_mma(c);
+    mma_commit_warp(bar(kVSReady));
+    n_s = c + 1;
   };
-  bool ok = wait_bar(kVKvFull, 0);
-  for (int c = 0; ok && c < kKvBuf && c < n_chunks; ++c) ok = issue_sdp(c);
+  auto issue_dp = [&](int c) {
+    dp_mma(c);
+    mma_commit_warp(bar(kVDPReady));
+    n_dp = c + 1;
+  };
+  bool ok = wait_bar(kVKvFull, 0) && wait_bar(kVFull, 0);
+  if (ok) {
+    issue_s(0);
+    issue_dp(0);
+  }
   for (int c = 0; ok && c < n_chunks; ++c) {
-    const int b = c % kKvBuf, round = c / kKvBuf;
-    // pdsready[b]: completion c / kKvBuf; the warps' next arrivals on it need S^T(c + kKvBuf)
-    ok = wait_bar(kVPdsReady + b, round);
+    const bool more = c + 1 < n_chunks;
+    if (kSepP && more) {
+      // S^T(c + 1) overwrites S^T(c) once every warp holds its columns (sfree: completion c;
+      // the warps' next arrivals need S^T(c + 1))
+      ok = wait_bar(kVSFree, c) && wait_bar(kVFull + (c + 1) % kStages, (c + 1) / kStages);
+      if (!ok) break;
+      issue_s(c + 1);
+    }
+    ok = wait_bar(kVPdsReady, c);  // completion c; the next arrivals need dP^T(c + 1)
     if (!ok) break;
-    acc(c, b);
+    acc(c);
     mma_commit_warp(bar(kVEmpty + c % kStages));
-    mma_commit_warp(bar(kVAccDone + b));
+    mma_commit_warp(bar(kVAccDone));
     n_acc = c + 1;
-    if (c + kKvBuf < n_chunks) {
-      // S^T(c + kKvBuf) overwrites P^T(c): the products of chunk c must have read it
-      ok = wait_bar(kVAccDone + b, round) && issue_sdp(c + kKvBuf);
+    if (more) {
+      // dP^T(c + 1) (and, with P^T over S^T, S^T(c + 1)) overwrite what the products of
+      // chunk c read: they must have completed
+      ok = wait_bar(kVAccDone, c);
+      if (!kSepP) ok = ok && wait_bar(kVFull + (c + 1) % kStages, (c + 1) / kStages);
+      if (!ok) break;
+      if (!kSepP) issue_s(c + 1);
+      issue_dp(c + 1);
     }
   }
   mma_commit_warp(bar(kVAccReady));
   // drain: the last commit first (every operation then complete), then each barrier's last
-  // completion, so that no arrival is in flight when the CTA exits.  A barrier indexed by
-  // buffer was committed once per chunk c < n with c % kKvBuf == b, one indexed by stage
+  // completion, so that no arrival is in flight when the CTA exits.  kVEmpty[s] was committed
   // once per chunk c < n_acc with c % kStages == s.
   mbar_wait(bar(kVAccReady), 0, &g_bwd_errors, kWaitNs, kErrTeardown);
-  for (int b = 0; b < kKvBuf; ++b) {
-    const int ns = n_sdp / kKvBuf + (b < n_sdp % kKvBuf ? 1 : 0), na = n_acc / kKvBuf + (b < n_acc % kKvBuf ? 1 : 0);
-    if (ns) mbar_wait(bar(kVSReady + b), (ns - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
-    if (na) mbar_wait(bar(kVAccDone + b), (na - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
-  }
+  if (n_s) mbar_wait(bar(kVSReady), (n_s - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+  if (n_dp) mbar_wait(bar(kVDPReady), (n_dp - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
+  if (n_acc) mbar_wait(bar(kVAccDone), (n_acc - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
   for (int s = 0; s < kStages; ++s) {
     const int times = n_acc / kStages + (s < n_acc % kStages ? 1 : 0);
     if (times > 0) mbar_wait(bar(kVEmpty + s), (times - 1) & 1, &g_bwd_errors, kWaitNs, kErrTeardown);
@@ -733,121 +754,120 @@ __device__ __forceinline__ void kv_mma_role(uint64_t *bars, int n_chunks, Sdp sd
 
 // Softmax-warp wait: every lane polls; the warp proceeds only if all lanes saw the phase.
 __device__ __forceinline__ bool kv_wait_warp(uint64_t *bars, int b, int completion) {
+  // (suspending try_wait, as mbar_wait does: spinning on try_wait or test_wait instead
+  // measured 0.3 ms slower over the config-3 backward -- the spinning warps take issue slots)
   const bool r = mbar_wait(smem_u32(&bars[b]), completion & 1, &g_bwd_errors, kWaitNs, kErrSoftmax);
   const bool all = __all_sync(0xffffffffu, r);
   if (all) tc_fence_after();
   return all;
 }
 
-// 16 columns of one lane's row: P^T / dS^T pairs from S^T, dP^T (fp32 bits).  l, d: per
-// column (shared memory) -lse log2(e) and -Delta, or with RAW lse and Delta as saved; bits:
-// bit i for column i valid, unused unless MASKED (a masked column gives exact zeros
-// whatever its inputs).
-template <bool BF16, bool MASKED, bool RAW>
-__device__ __forceinline__ void kv_scores16(const uint32_t (&sv)[16], const uint32_t (&dv)[16], const float *l,
-                                            const float *d, float sc, uint32_t bits, uint32_t (&pw)[8],
-                                            uint32_t (&dw)[8]) {
-  const float2 sc2 = make_float2(sc, sc);
+// One chunk of a softmax warp, columns [col0, col0 + 32) of its 32 TMEM lanes: wait for S^T,
+// load it, release it (sfree), exponentiate, wait for dP^T, load it, form dS^T = P^T (dP^T -
+// Delta) and store both as 16-bit pairs (P^T at C::p_col, dS^T at C::ds_col of the warp's
+// two query groups).  l, d: the chunk's per-column -lse log2(e) and -Delta in shared memory
+// (with RAW: lse and Delta as saved); mask: bit i for column col0 + i, a masked column gives
+// exact zeros whatever its inputs; active false: the warp's rows take no query of this
+// chunk and store zeros.  Returns false if a wait timed out.
+template <class C, bool BF16, bool MASKED, bool RAW>
+__device__ __forceinline__ bool kv_chunk(uint64_t *bars, int ch, uint32_t t_lanes, int col0, const float *l,
+                                         const float *d, float sc, uint32_t mask, bool active) {
+  float pf[kKvW];
+  if (!kv_wait_warp(bars, kVSReady, ch)) return false;
+  if (active) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float2 l2 = *reinterpret_cast<const float2 *>(l + 2 * i);
-    float2 d2 = *reinterpret_cast<const float2 *>(d + 2 * i);
-    if (RAW) {
-      l2 = mul2(l2, make_float2(-kLog2e, -kLog2e));
-      d2 = make_float2(-d2.x, -d2.y);
+    for (int g = 0; g < kKvW / 16; ++g) {  // S^T in groups of 16 columns, exponentiated as loaded
+      uint32_t sv[16];
+      tmem_ld16(t_lanes + C::kColS + col0 + 16 * g, sv);
+      tmem_wait_ld();
+      if (g + 1 == kKvW / 16) {  // every column loaded: S^T may be overwritten
+        tc_fence_before();
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(smem_u32(&bars[kVSFree]));
+      }
+      const float2 sc2 = make_float2(sc, sc);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int k = 16 * g + 2 * i;
+        float2 l2 = *reinterpret_cast<const float2 *>(l + col0 + k);
+        if (RAW) l2 = mul2(l2, make_float2(-kLog2e, -kLog2e));
+        const float2 x = fma2(make_float2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), sc2, l2);
+        // kKvPolyPairs of every 8 pairs take the FMA-pipe polynomial, the rest the MUFU
+        const float2 e = i < 8 - kKvPolyPairs ? make_float2(ex2_approx(x.x), ex2_approx(x.y)) : exp2_poly2(x);
+        pf[k] = e.x;
+        pf[k + 1] = e.y;
+      }
     }
-    const float2 x = fma2(make_float2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), sc2, l2);
-    // kKvPolyPairs of every 8 pairs take the FMA-pipe polynomial, the rest the MUFU
-    float2 pp = (i % 8) < 8 - kKvPolyPairs ? make_float2(ex2_approx(x.x), ex2_approx(x.y)) : exp2_poly2(x);
-    float2 dd = mul2(pp, add2(make_float2(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])), d2));
-    if (MASKED) {
-      const bool b0 = (bits >> (2 * i)) & 1u, b1 = (bits >> (2 * i + 1)) & 1u;
-      pp = make_float2(b0 ? pp.x : 0.f, b1 ? pp.y : 0.f);
-      dd = make_float2(b0 ? dd.x : 0.f, b1 ? dd.y : 0.f);
-    }
-    pw[i] = pack2<BF16>(pp.x, pp.y);
-    dw[i] = pack2<BF16>(dd.x, dd.y);
+  } else {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(smem_u32(&bars[kVSFree]));
   }
-}
-
-// One chunk of a softmax warp: its kKvW columns of S^T / dP^T (TMEM addresses t_s, t_dp of
-// the first) to P^T / dS^T pairs at the start of the same range.  Groups of 16 columns, the
-// loads of group g + 1 in flight while group g is computed; group g's pairs go to columns
-// [8g, 8g + 8) of the range, which hold scores the warp has already loaded.  mask: bit i
-// for column i of the range.
-template <bool BF16, bool MASKED, bool RAW>
-__device__ __forceinline__ void kv_chunk(uint32_t t_s, uint32_t t_dp, const float *l, const float *d, float sc,
-                                         uint64_t mask) {
-  constexpr int kG = kKvW / 16;
-  uint32_t sv[2][16], dv[2][16];
-  tmem_ld16(t_s, sv[0]);
-  tmem_ld16(t_dp, dv[0]);
-  tmem_wait_ld();
-#pragma unroll
-  for (int g = 0; g < kG; ++g) {
-    if (g + 1 < kG) {
-      tmem_ld16(t_s + 16 * (g + 1), sv[(g + 1) & 1]);
-      tmem_ld16(t_dp + 16 * (g + 1), dv[(g + 1) & 1]);
-    }
-    uint32_t pw[8], dw[8];
-    kv_scores16<BF16, MASKED, RAW>(sv[g & 1], dv[g & 1], l + 16 * g, d + 16 * g, sc,
-                                   (uint32_t)(mask >> (16 * g)) & 0xffffu, pw, dw);
-    tmem_st8(t_s + 8 * g, pw);
-    tmem_st8(t_dp + 8 * g, dw);
-    if (g + 1 < kG) tmem_wait_ld();
-  }
-}
-
-__device__ __forceinline__ void kv_zero_chunk(uint32_t t_s, uint32_t t_dp) {
-  uint32_t z[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) z[i] = 0u;
+  // dpready(c) also means the products of chunk c - 1 completed: the P^T buffer is free
+  if (!kv_wait_warp(bars, kVDPReady, ch)) return false;
+  const int j0 = col0 / 16;  // the warp's first query group
 #pragma unroll
   for (int g = 0; g < kKvW / 16; ++g) {
-    tmem_st8(t_s + 8 * g, z);
-    tmem_st8(t_dp + 8 * g, z);
+    uint32_t pw[8], dw[8];
+    if (active) {
+      uint32_t dv[16];
+      tmem_ld16(t_lanes + C::kColDP + col0 + 16 * g, dv);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int k = 16 * g + 2 * i;
+        float2 d2 = *reinterpret_cast<const float2 *>(d + col0 + k);
+        if (RAW) d2 = make_float2(-d2.x, -d2.y);
+        float2 pp = make_float2(pf[k], pf[k + 1]);
+        float2 dd = mul2(pp, add2(make_float2(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])), d2));
+        if (MASKED) {  // selects, not products
+          const bool b0 = (mask >> k) & 1u, b1 = (mask >> (k + 1)) & 1u;
+          pp = make_float2(b0 ? pp.x : 0.f, b1 ? pp.y : 0.f);
+          dd = make_float2(b0 ? dd.x : 0.f, b1 ? dd.y : 0.f);
+        }
+        pw[i] = pack2<BF16>(pp.x, pp.y);
+        dw[i] = pack2<BF16>(dd.x, dd.y);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pw[i] = dw[i] = 0u;
+    }
+    // dS^T group g lands on dP^T columns this warp has already loaded (its own first 16)
+    tmem_st8(t_lanes + C::p_col(j0 + g), pw);
+    tmem_st8(t_lanes + C::ds_col(j0 + g), dw);
   }
+  tmem_wait_st();
+  tc_fence_before();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(smem_u32(&bars[kVPdsReady]));
+  return true;
 }
 
-// TMEM column (within an S^T / dP^T buffer) of the pairs of query group j (queries 16j ..
-// 16j + 15): group g of the softmax warps serving columns [kKvW h, kKvW (h + 1)) sits at
-// kKvW h + 8g.
-__host__ __device__ constexpr uint32_t kv_pair_col(int j) {
-  return (uint32_t)((16 * j / kKvW) * kKvW + 8 * ((16 * j % kKvW) / 16));
-}
-
-// The MMAs of one chunk, shared by both kernels: k_smem / v_smem the 128-row K and V tiles,
-// q / dov the chunk's Q and dO boxes, b the TMEM buffer.
+// The MMAs of one chunk, shared by both kernels: kt the 128-row K (or V) tile, qc the
+// chunk's Q (or dO) box, col the TMEM buffer (S^T or dP^T).
 template <int D, bool BF16>
-__device__ __forceinline__ void kv_issue_sdp(uint32_t tmem, uint32_t k_smem, uint32_t v_smem, uint32_t q,
-                                             uint32_t dov, int b) {
+__device__ __forceinline__ void kv_issue_scores(uint32_t tmem, uint32_t col, uint32_t kt, uint32_t qc) {
   using C = KvCfg<D>;
   constexpr uint32_t idesc_s = idesc_f16(128, kKvCols, BF16, false);
 #pragma unroll
   for (int kk = 0; kk < C::kK; ++kk)
-    mma_ss_warp(tmem + C::col_s(b), desc_sw32(k_smem + kk * C::kBoxT, 16, 256), desc_sw32(q + kk * C::kBoxC, 16, 256),
-                idesc_s, kk > 0 ? 1u : 0u);
-#pragma unroll
-  for (int kk = 0; kk < C::kK; ++kk)
-    mma_ss_warp(tmem + C::col_dp(b), desc_sw32(v_smem + kk * C::kBoxT, 16, 256),
-                desc_sw32(dov + kk * C::kBoxC, 16, 256), idesc_s, kk > 0 ? 1u : 0u);
+    mma_ss_warp(tmem + col, desc_sw32(kt + kk * C::kBoxT, 16, 256), desc_sw32(qc + kk * C::kBoxC, 16, 256), idesc_s,
+                kk > 0 ? 1u : 0u);
 }
 
 template <int D, bool BF16>
-__device__ __forceinline__ void kv_issue_acc(uint32_t tmem, uint32_t q, uint32_t dov, int b, bool first) {
+__device__ __forceinline__ void kv_issue_acc(uint32_t tmem, uint32_t q, uint32_t dov, bool first) {
   using C = KvCfg<D>;
   constexpr uint32_t idesc_acc = idesc_f16(128, D, BF16, true);
   // dV += P^T dO and dK += dS^T Q: A from TMEM (query group j: 16 queries as 8 columns of
-  // pairs, kv_pair_col), B the chunk's dO / Q read MN-major (16 query rows of 32 bytes per
-  // step)
+  // pairs), B the chunk's dO / Q read MN-major (16 query rows of 32 bytes per step)
 #pragma unroll
   for (int j = 0; j < kKvCols / 16; ++j)
-    mma_ts_warp(tmem + C::kColAcc + D, tmem + C::col_s(b) + kv_pair_col(j), desc_sw32(dov + j * 512, C::kBoxC, 256),
-                idesc_acc, (first && j == 0) ? 0u : 1u);
+    mma_ts_warp(tmem + C::kColAcc + D, tmem + C::p_col(j), desc_sw32(dov + j * 512, C::kBoxC, 256), idesc_acc,
+                (first && j == 0) ? 0u : 1u);
 #pragma unroll
   for (int j = 0; j < kKvCols / 16; ++j)
-    mma_ts_warp(tmem + C::kColAcc, tmem + C::col_dp(b) + kv_pair_col(j), desc_sw32(q + j * 512, C::kBoxC, 256),
-                idesc_acc, (first && j == 0) ? 0u : 1u);
+    mma_ts_warp(tmem + C::kColAcc, tmem + C::ds_col(j), desc_sw32(q + j * 512, C::kBoxC, 256), idesc_acc,
+                (first && j == 0) ? 0u : 1u);
 }
 
 // The epilogue's accumulator rows: warps 0-3 take dK (scaled by 1/sqrt(D)), warps 4-7 dV.
@@ -972,37 +992,26 @@ __global__ void __launch_bounds__(kKvThreads, 2)
     };
     kv_producer_role<kStages>(bars, n_chunks, lane, tiles, chunk);
   } else if (warp == kKvMma) {
-    kv_mma_role<kStages>(
-        bars, n_chunks,
-        [&](int c, int bf) {
-          kv_issue_sdp<D, BF16>(tmem, sk_smem, sv_smem, stage_of(c), stage_of(c) + C::kChunkBytes, bf);
-        },
-        [&](int c, int bf) { kv_issue_acc<D, BF16>(tmem, stage_of(c), stage_of(c) + C::kChunkBytes, bf, c == 0); });
+    kv_mma_role<kStages, C::kSepP>(
+        bars, n_chunks, [&](int c) { kv_issue_scores<D, BF16>(tmem, C::kColS, sk_smem, stage_of(c)); },
+        [&](int c) { kv_issue_scores<D, BF16>(tmem, C::kColDP, sv_smem, stage_of(c) + C::kChunkBytes); },
+        [&](int c) { kv_issue_acc<D, BF16>(tmem, stage_of(c), stage_of(c) + C::kChunkBytes, c == 0); });
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
     const int quarter = warp & 3, half = warp >> 2, col0 = half * kKvW;
     const uint32_t t_lanes = tmem + ((uint32_t)(quarter * 32) << 16);
     const float sc = p.sc;
     bool ok = true;
-    for (int ch = 0; ch < n_chunks; ++ch) {
-      const int bf = ch % kKvBuf;
-      ok = kv_wait_warp(bars, kVSReady + bf, ch / kKvBuf);
-      if (!ok) break;
+    for (int ch = 0; ch < n_chunks && ok; ++ch) {
       const float *vals =
           reinterpret_cast<const float *>(ring_ptr + (size_t)(ch % kStages) * C::kStageBytes + 2 * C::kChunkBytes);
       const int valid = min(kGCols, p.tokens - chunk_row0(ch)) - col0;  // this warp's columns inside the volume
-      const uint32_t ts = t_lanes + C::col_s(bf) + col0, tdp = t_lanes + C::col_dp(bf) + col0;
       if (valid >= kKvW) {
-        kv_chunk<BF16, false, true>(ts, tdp, vals + col0, vals + kGCols + col0, sc, ~0ull);
-      } else if (valid > 0) {  // columns past the volume may hold stale lse / Delta: masked to exact zeros
-        kv_chunk<BF16, true, true>(ts, tdp, vals + col0, vals + kGCols + col0, sc, ~0ull >> (64 - valid));
-      } else {
-        kv_zero_chunk(ts, tdp);
+        ok = kv_chunk<C, BF16, false, true>(bars, ch, t_lanes, col0, vals, vals + kGCols, sc, ~0u, true);
+      } else {  // columns past the volume may hold stale lse / Delta: masked to exact zeros
+        const uint32_t mask = valid > 0 ? ~0u >> (32 - valid) : 0u;
+        ok = kv_chunk<C, BF16, true, true>(bars, ch, t_lanes, col0, vals, vals + kGCols, sc, mask, valid > 0);
       }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars[kVPdsReady + bf]));
     }
     if (ok) ok = kv_wait_warp(bars, kVAccReady, 0);
     if (ok) {
@@ -1228,12 +1237,10 @@ __global__ void __launch_bounds__(kKvThreads, 2)
     };
     kv_producer_role<kStages>(bars, n_chunks, lane, tiles, chunk);
   } else if (warp == kKvMma) {
-    kv_mma_role<kStages>(
-        bars, n_chunks,
-        [&](int c, int bf) {
-          kv_issue_sdp<D, BF16>(tmem, k_smem, v_smem, stage_of(c), stage_of(c) + C::kChunkBytes, bf);
-        },
-        [&](int c, int bf) { kv_issue_acc<D, BF16>(tmem, stage_of(c), stage_of(c) + C::kChunkBytes, bf, c == 0); });
+    kv_mma_role<kStages, C::kSepP>(
+        bars, n_chunks, [&](int c) { kv_issue_scores<D, BF16>(tmem, C::kColS, k_smem, stage_of(c)); },
+        [&](int c) { kv_issue_scores<D, BF16>(tmem, C::kColDP, v_smem, stage_of(c) + C::kChunkBytes); },
+        [&](int c) { kv_issue_acc<D, BF16>(tmem, stage_of(c), stage_of(c) + C::kChunkBytes, c == 0); });
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
     const int quarter = warp & 3, half = warp >> 2, col0 = half * kKvW;
@@ -1243,35 +1250,26 @@ __global__ void __launch_bounds__(kKvThreads, 2)
     const bool row_ok = kz < p.Z && ky < p.Y && kx < p.X;
     // this warp's chunk columns inside the key's (y, x) square, per chunk of a plane (bit
     // i: column col0 + i)
-    uint64_t mask0 = 0ull, mask1 = 0ull;
+    uint32_t mask0 = 0u, mask1 = 0u;
 #pragma unroll
     for (int hh = 0; hh < kParts; ++hh)
 #pragma unroll
       for (int i = 0; i < kKvW; ++i) {
         const int j = col0 + i, hy = kRowsH * hh + j / kHX, hx = j % kHX;
         if (row_ok && j < kWin && (unsigned)(hy - kyl) <= 2u * R && (unsigned)(hx - kxl) <= 2u * R)
-          (hh ? mask1 : mask0) |= 1ull << i;
+          (hh ? mask1 : mask0) |= 1u << i;
       }
     const float sc = p.sc;
     bool ok = true;
-    for (int ch = 0; ch < n_chunks; ++ch) {
-      const int bf = ch % kKvBuf;
-      ok = kv_wait_warp(bars, kVSReady + bf, ch / kKvBuf);
-      if (!ok) break;
+    for (int ch = 0; ch < n_chunks && ok; ++ch) {
       const int pl = chunk_plane(ch);  // query plane z0 - R + pl
       const float *vals =
           reinterpret_cast<const float *>(ring_ptr + (size_t)(ch % kStages) * C::kStageBytes + 2 * C::kChunkBytes);
-      const uint32_t ts = t_lanes + C::col_s(bf) + col0, tdp = t_lanes + C::col_dp(bf) + col0;
-      if ((unsigned)(pl - 2 * quarter) <= 2u * R + 1u) {  // the plane reaches one of the warp's key planes
-        const uint64_t m = (unsigned)(pl - zl) <= 2u * R ? ((ch % kParts) ? mask1 : mask0) : 0ull;
-        kv_chunk<BF16, true, false>(ts, tdp, vals + col0, vals + kKvCols + col0, sc, m);
-      } else {
-        kv_zero_chunk(ts, tdp);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars[kVPdsReady + bf]));
+      // the plane reaches one of the warp's key planes (warp-uniform); lanes of the other plane
+      // take the chunk through a zero mask
+      const bool active = (unsigned)(pl - 2 * quarter) <= 2u * R + 1u;
+      const uint32_t m = (unsigned)(pl - zl) <= 2u * R ? ((ch % kParts) ? mask1 : mask0) : 0u;
+      ok = kv_chunk<C, BF16, true, false>(bars, ch, t_lanes, col0, vals, vals + kKvCols, sc, m, active);
     }
     if (ok) ok = kv_wait_warp(bars, kVAccReady, 0);
     if (ok) {

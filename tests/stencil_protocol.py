@@ -558,15 +558,16 @@ def run_fwd(n_chunks=14, stages=4, seed=0, max_steps=400000, skip_sfree=False):
 
 # ---------------------------------------------------- dK / dV kernels, two CTAs per SM
 # Model of stencil_bwd_dkv_kernel and global_dkv_tc_kernel (pack3d_b200/csrc/stencil_bwd.cu):
-# TMEM holds ``buffers`` S^T / dP^T buffer pairs, chunk c using buffer c % buffers, and the
-# softmax warps write P^T and dS^T back over the buffer they read, as 16-bit pairs.  The MMA
-# warp issues S^T / dP^T of the first ``buffers`` chunks, then per chunk c waits for
-# pdsready[b](c), issues the dV / dK products, commits empty[c % stages] and accdone[b],
-# waits for accdone[b](c) and issues S^T / dP^T of chunk c + buffers into the same buffer
-# (sready[b]).  Tensor-core operations complete in issue order only when they write the
-# same accumulator (``ordered_by_acc``): S^T(c + buffers) and the products of chunk c write
-# different ones, so only the accdone wait keeps S^T from landing on P^T(c) before the
-# products read it.
+# TMEM holds one S^T and one dP^T buffer; the softmax warps write dS^T back over dP^T as
+# 16-bit pairs, and P^T either over S^T (``sep_p=False``) or into a buffer of its own
+# (``sep_p=True``, head_dim <= 48).  S^T(c) commits sready, dP^T(c) dpready.  The warps load
+# S^T(c) and arrive on sfree, exponentiate, wait for dpready(c), load dP^T(c), store P^T and
+# dS^T and arrive on pdsready.  The MMA warp issues the products of chunk c after
+# pdsready(c) (committing empty[c % stages] and accdone), waits for accdone(c) and issues
+# dP^T(c + 1).  S^T(c + 1) is issued after sfree(c) with a separate P^T buffer, after
+# accdone(c) otherwise.  Tensor-core operations complete in issue order only when they
+# write the same accumulator (``ordered_by_acc``).  The model tracks each warp's TMEM
+# regions (S, DP, P) and checks every read and overwrite against them.
 
 def ip_producer(state):
     k = state.stages
@@ -577,7 +578,7 @@ def ip_producer(state):
                 yield ("wait", f"empty{s}")
         old = state.stage_chunk.get(s)
         if old is not None:
-            for op in (("SDP", 0, old), ("ACC", 0, old)):
+            for op in (("S", 0, old), ("DP", 0, old), ("ACC", 0, old)):
                 if op not in state.mma_done:
                     raise ProtocolError(f"stage {s} overwritten with chunk {ch} while {op} is outstanding")
             if len(state.read_vals.get(old, ())) != state.warps:
@@ -591,7 +592,7 @@ def ip_producer(state):
 
 
 def ip_mma(state, skip_accdone=False):
-    k, n, nb = state.stages, state.n_chunks, state.buffers
+    k, n, sep = state.stages, state.n_chunks, state.sep_p
 
     def commit(name):
         state.mma_queue.append(("commit", name))
@@ -604,76 +605,89 @@ def ip_mma(state, skip_accdone=False):
         while not _wait(state, name, completion & 1, completion):
             yield ("wait", name)
 
-    def issue_sdp(c):
-        yield from waits(f"full{c % k}", c // k)
+    def issue(kind, c):
         landed(c)
-        state.mma_queue.append(("SDP", 0, c))
-        commit(f"sready{c % nb}")
-        yield ("step", None)
+        state.mma_queue.append((kind, 0, c))
+        commit("sready" if kind == "S" else "dpready")
 
     yield from waits("kvfull", 0)
-    for c in range(min(nb, n)):
-        yield from issue_sdp(c)
+    yield from waits("full0", 0)
+    issue("S", 0)
+    issue("DP", 0)
+    yield ("step", None)
     for c in range(n):
-        b = c % nb
-        yield from waits(f"pdsready{b}", c // nb)
+        if sep and c + 1 < n:
+            yield from waits("sfree", c)
+            yield from waits(f"full{(c + 1) % k}", (c + 1) // k)
+            issue("S", c + 1)
+            yield ("step", None)
+        yield from waits("pdsready", c)
         landed(c)
         if len(state.pds_stored.get(c, ())) != state.warps:
             raise ProtocolError(f"dV/dK({c}) issued before all warps stored P/dS")
         state.mma_queue.append(("ACC", 0, c))
         commit(f"empty{c % k}")
-        commit(f"accdone{b}")
+        commit("accdone")
         yield ("step", None)
-        if c + nb < n:
+        if c + 1 < n:
             if not skip_accdone:
-                yield from waits(f"accdone{b}", c // nb)
-            yield from issue_sdp(c + nb)
+                yield from waits("accdone", c)
+            if not sep:
+                yield from waits(f"full{(c + 1) % k}", (c + 1) // k)
+                issue("S", c + 1)
+            issue("DP", c + 1)
+            yield ("step", None)
     commit("accready")
     yield ("step", None)
     yield from waits("accready", 0)
 
 
 def ip_softmax(state, w):
-    n, nb = state.n_chunks, state.buffers
+    n, sep = state.n_chunks, state.sep_p
+    p_region = "P" if sep else "S"
 
     def waits(name, completion):
         while not _wait(state, name, completion & 1, completion):
             yield ("wait", name)
 
+    def holds(region, want, what):
+        got = state.tmem.get((w, region))
+        if got != want:
+            raise ProtocolError(f"warp {w} {what} but its TMEM lanes hold {got}")
+
     for ch in range(n):
-        b = ch % nb
-        yield from waits(f"sready{b}", ch // nb)
-        if state.tmem.get((w, b)) != ("S", ch):
-            raise ProtocolError(f"warp {w} loaded S/dP({ch}) but its TMEM lanes hold {state.tmem.get((w, b))}")
+        yield from waits("sready", ch)
+        holds("S", ("S", ch), f"loaded S({ch})")
         if state.stage_chunk.get(ch % state.stages) != ch:
             raise ProtocolError(f"lse of chunk {ch} read from a stage holding another chunk")
         state.read_vals.setdefault(ch, set()).add(w)
+        state.s_loaded.setdefault(ch, set()).add(w)
+        state.bar("sfree").arrive()
         yield ("step", None)
-        state.tmem[(w, b)] = ("P", ch)     # P^T / dS^T written over S^T / dP^T of buffer b
+        yield from waits("dpready", ch)
+        holds("DP", ("DP", ch), f"loaded dP({ch})")
+        yield ("step", None)
+        old = state.tmem.get((w, p_region))
+        if old is not None and old[0] == "P" and ("ACC", 0, old[1]) not in state.mma_done:
+            raise ProtocolError(f"P({ch}) stored over P({old[1]}) before dV/dK({old[1]}) read it")
+        state.tmem[(w, p_region)] = ("P", ch)
+        state.tmem[(w, "DP")] = ("dS", ch)
         state.pds_stored.setdefault(ch, set()).add(w)
-        state.bar(f"pdsready{b}").arrive()
+        state.bar("pdsready").arrive()
         yield ("step", None)
     yield from waits("accready", 0)
     if ("ACC", 0, n - 1) not in state.mma_done:
         raise ProtocolError("accumulators read before the last products completed")
 
 
-def run_ip(n_chunks=10, stages=4, seed=0, warps=8, buffers=1, skip_accdone=False, max_steps=400000):
-    """Replay one random interleaving of the dK / dV kernels' protocol.
-
-    TMEM contents are tracked per (softmax warp, buffer): S^T(c) lands when its MMA
-    completes, P^T(c) when the warp stores it, and the dV / dK products of chunk c must find
-    P^T(c) there when they run."""
+def run_ip(n_chunks=10, stages=4, seed=0, warps=8, sep_p=True, skip_accdone=False, max_steps=400000):
+    """Replay one random interleaving of the dK / dV kernels' protocol."""
     rng = random.Random(seed)
     state = State(n_chunks=n_chunks, stages=stages)
-    state.pds_stored, state.read_vals, state.tmem, state.warps = {}, {}, {}, warps
-    state.buffers = buffers
-    state.ordered_by_acc = {"SDP": lambda op: f"sdp{op[2] % buffers}", "ACC": lambda op: "acc"}
-    bars = {"kvfull": 1, "accready": 1}
-    for b in range(buffers):
-        bars[f"sready{b}"] = 1
-        bars[f"pdsready{b}"] = warps
-        bars[f"accdone{b}"] = 1
+    state.pds_stored, state.read_vals, state.tmem, state.warps, state.sep_p = {}, {}, {}, warps, sep_p
+    state.ordered_by_acc = {"S": lambda op: "s", "DP": lambda op: "dp", "ACC": lambda op: "acc"}
+    bars = {"kvfull": 1, "accready": 1, "sready": 1, "sfree": warps, "dpready": 1, "pdsready": warps,
+            "accdone": 1}
     for s in range(stages):
         bars[f"full{s}"] = 2
         bars[f"empty{s}"] = 1
@@ -685,18 +699,24 @@ def run_ip(n_chunks=10, stages=4, seed=0, warps=8, buffers=1, skip_accdone=False
 
     def on_complete(op):
         kind, _, c = op
-        b = c % buffers
-        if kind == "SDP":
-            for v in range(warps):
-                held = state.tmem.get((v, b))
-                if held == ("P", c - buffers) and ("ACC", 0, c - buffers) not in state.mma_done:
-                    raise ProtocolError(f"S/dP({c}) overwrote P/dS({c - buffers}) before dV/dK({c - buffers}) "
-                                        "read them")
-                state.tmem[(v, b)] = ("S", c)
-        elif kind == "ACC":
-            for v in range(warps):
-                if state.tmem.get((v, b)) != ("P", c):
-                    raise ProtocolError(f"dV/dK({c}) read lanes of warp {v} holding {state.tmem.get((v, b))}")
+        for v in range(warps):
+            if kind == "S":
+                held = state.tmem.get((v, "S"))
+                if held is not None and held[0] == "S" and v not in state.s_loaded.get(held[1], ()):
+                    raise ProtocolError(f"S({c}) overwrote S({held[1]}) before warp {v} loaded it")
+                if held is not None and held[0] == "P" and ("ACC", 0, held[1]) not in state.mma_done:
+                    raise ProtocolError(f"S({c}) overwrote P({held[1]}) before dV/dK({held[1]}) read it")
+                state.tmem[(v, "S")] = ("S", c)
+            elif kind == "DP":
+                held = state.tmem.get((v, "DP"))
+                if held is not None and held[0] == "dS" and ("ACC", 0, held[1]) not in state.mma_done:
+                    raise ProtocolError(f"dP({c}) overwrote dS({held[1]}) before dV/dK({held[1]}) read it")
+                state.tmem[(v, "DP")] = ("DP", c)
+            elif kind == "ACC":
+                p_held = state.tmem.get((v, "P" if state.sep_p else "S"))
+                if p_held != ("P", c) or state.tmem.get((v, "DP")) != ("dS", c):
+                    raise ProtocolError(f"dV/dK({c}) read lanes of warp {v} holding {p_held}, "
+                                        f"{state.tmem.get((v, 'DP'))}")
 
     state.on_complete = on_complete
     return _schedule(state, roles, rng, max_steps)

@@ -51,22 +51,22 @@ def test_dq_protocol_holds_under_random_interleavings(stages):
         sp.run_dq(n_chunks=12, stages=stages, seed=seed)
 
 
-@pytest.mark.parametrize("buffers", [1, 2])
-@pytest.mark.parametrize("stages", [3, 4, 8])
+@pytest.mark.parametrize("sep_p", [True, False])
+@pytest.mark.parametrize("stages", [2, 4, 8])
 @pytest.mark.parametrize("n_chunks", [1, 2, 3, 14])
-def test_dkv_protocol_holds(buffers, stages, n_chunks):
-    """dK / dV kernels at two CTAs per SM: S^T / dP^T buffers with P^T / dS^T written over them,
-    tensor-core operations ordered only per accumulator (the kernels use one buffer)."""
+def test_dkv_protocol_holds(sep_p, stages, n_chunks):
+    """dK / dV kernels at two CTAs per SM: dS^T over dP^T, P^T over S^T or in a buffer of its
+    own, tensor-core operations ordered only per accumulator."""
     for seed in range(80):
-        sp.run_ip(n_chunks=n_chunks, stages=stages, seed=seed, buffers=buffers)
+        sp.run_ip(n_chunks=n_chunks, stages=stages, seed=seed, sep_p=sep_p)
 
 
 def test_model_rejects_issuing_the_next_scores_before_the_products_complete():
     failures = 0
     for seed in range(150):
         try:
-            sp.run_ip(n_chunks=10, stages=4, seed=seed, buffers=1 + seed % 2, skip_accdone=True)
+            sp.run_ip(n_chunks=10, stages=4, seed=seed, sep_p=seed % 2 == 0, skip_accdone=True)
         except sp.ProtocolError as err:
-            assert "overwrote P/dS" in str(err) or "read lanes" in str(err) or "lanes hold" in str(err)
+            assert "before dV/dK" in str(err) or "read lanes" in str(err) or "lanes hold" in str(err)
             failures += 1
     assert failures > 0
