@@ -765,11 +765,11 @@ __device__ __forceinline__ bool kv_wait_warp(uint64_t *bars, int b, int completi
 // One chunk of a softmax warp, columns [col0, col0 + 32) of its 32 TMEM lanes: wait for S^T,
 // load it, release it (sfree), exponentiate, wait for dP^T, load it, form dS^T = P^T (dP^T -
 // Delta) and store both as 16-bit pairs (P^T at C::p_col, dS^T at C::ds_col of the warp's
-// two query groups).  l, d: the chunk's per-column -lse log2(e) and -Delta in shared memory
-// (with RAW: lse and Delta as saved); mask: bit i for column col0 + i, a masked column gives
+// two query groups).  l, d: the chunk's per-column -lse log2(e) and -Delta in shared memory;
+// mask: bit i for column col0 + i, a masked column gives
 // exact zeros whatever its inputs; active false: the warp's rows take no query of this
 // chunk and store zeros.  Returns false if a wait timed out.
-template <class C, bool BF16, bool MASKED, bool RAW>
+template <class C, bool BF16, bool MASKED>
 __device__ __forceinline__ bool kv_chunk(uint64_t *bars, int ch, uint32_t t_lanes, int col0, const float *l,
                                          const float *d, float sc, uint32_t mask, bool active) {
   float pf[kKvW];
@@ -789,8 +789,7 @@ __device__ __forceinline__ bool kv_chunk(uint64_t *bars, int ch, uint32_t t_lane
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int k = 16 * g + 2 * i;
-        float2 l2 = *reinterpret_cast<const float2 *>(l + col0 + k);
-        if (RAW) l2 = mul2(l2, make_float2(-kLog2e, -kLog2e));
+        const float2 l2 = *reinterpret_cast<const float2 *>(l + col0 + k);
         const float2 x = fma2(make_float2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), sc2, l2);
         // kKvPolyPairs of every 8 pairs take the FMA-pipe polynomial, the rest the MUFU
         const float2 e = i < 8 - kKvPolyPairs ? make_float2(ex2_approx(x.x), ex2_approx(x.y)) : exp2_poly2(x);
@@ -815,8 +814,7 @@ __device__ __forceinline__ bool kv_chunk(uint64_t *bars, int ch, uint32_t t_lane
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int k = 16 * g + 2 * i;
-        float2 d2 = *reinterpret_cast<const float2 *>(d + col0 + k);
-        if (RAW) d2 = make_float2(-d2.x, -d2.y);
+        const float2 d2 = *reinterpret_cast<const float2 *>(d + col0 + k);
         float2 pp = make_float2(pf[k], pf[k + 1]);
         float2 dd = mul2(pp, add2(make_float2(__uint_as_float(dv[2 * i]), __uint_as_float(dv[2 * i + 1])), d2));
         if (MASKED) {  // selects, not products
@@ -892,7 +890,6 @@ constexpr int kGCols = kKvCols;  // queries per chunk
 
 struct GkvParams {
   int heads, kv_heads, rep, tokens, summaries, m_tiles, splits, q_chunks, per_split;
-  int bulk_vals;  // lse / Delta rows are 16-byte aligned (N % 4 == 0): bulk-copy them
   float sc, inv_sqrt_d;
   const float *lse_g, *delta_g;  // [B*H, N]
   float *dk_part, *dv_part;      // [B*G, splits, M, D]
@@ -958,35 +955,29 @@ __global__ void __launch_bounds__(kKvThreads, 2)
       const int bh = chunk_head(ch), n0 = chunk_row0(ch);
       const int64_t r0 = (int64_t)bh * p.tokens + n0;
       const uint32_t rows = (uint32_t)min(kGCols, p.tokens - n0);
-      const uint32_t vals_smem = stage + 2 * C::kChunkBytes;
+      // -lse log2(e) and -Delta of the chunk's queries, formed once here rather than by every
+      // softmax lane (columns past N: zeros, masked there).  The loads go out before the
+      // stage wait.
       float l[kGCols / 32], dl[kGCols / 32];
-      if (!p.bulk_vals) {  // the loads go out before the stage wait
 #pragma unroll
-        for (int k = 0; k < kGCols / 32; ++k) {
-          const int j = lane + 32 * k;
-          l[k] = j < (int)rows ? __ldg(p.lse_g + r0 + j) : 0.f;
-          dl[k] = j < (int)rows ? __ldg(p.delta_g + r0 + j) : 0.f;
-        }
+      for (int k = 0; k < kGCols / 32; ++k) {
+        const int j = lane + 32 * k;
+        l[k] = j < (int)rows ? -__ldg(p.lse_g + r0 + j) * kLog2e : 0.f;
+        dl[k] = j < (int)rows ? -__ldg(p.delta_g + r0 + j) : 0.f;
       }
       if (!wait_stage()) return false;
       if (lane == 0) {
-        mbar_expect_tx(full, 2 * C::kChunkBytes + (p.bulk_vals ? 2 * rows * 4 : 0));
+        mbar_expect_tx(full, 2 * C::kChunkBytes);
         for (int c = 0; c < C::kK; ++c) {
           tma_load_3d(stage + c * C::kBoxC, &tq, full, 16 * c, n0, bh);
           tma_load_3d(stage + C::kChunkBytes + c * C::kBoxC, &tdo, full, 16 * c, n0, bh);
         }
-        if (p.bulk_vals) {
-          bulk_load(vals_smem, p.lse_g + r0, rows * 4, full);
-          bulk_load(vals_smem + C::kVals, p.delta_g + r0, rows * 4, full);
-        }
       }
-      if (!p.bulk_vals) {
-        float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kChunkBytes);
+      float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kChunkBytes);
 #pragma unroll
-        for (int k = 0; k < kGCols / 32; ++k) {
-          vals[lane + 32 * k] = l[k];
-          vals[kGCols + lane + 32 * k] = dl[k];
-        }
+      for (int k = 0; k < kGCols / 32; ++k) {
+        vals[lane + 32 * k] = l[k];
+        vals[kGCols + lane + 32 * k] = dl[k];
       }
       return true;
     };
@@ -1007,10 +998,10 @@ __global__ void __launch_bounds__(kKvThreads, 2)
           reinterpret_cast<const float *>(ring_ptr + (size_t)(ch % kStages) * C::kStageBytes + 2 * C::kChunkBytes);
       const int valid = min(kGCols, p.tokens - chunk_row0(ch)) - col0;  // this warp's columns inside the volume
       if (valid >= kKvW) {
-        ok = kv_chunk<C, BF16, false, true>(bars, ch, t_lanes, col0, vals, vals + kGCols, sc, ~0u, true);
+        ok = kv_chunk<C, BF16, false>(bars, ch, t_lanes, col0, vals, vals + kGCols, sc, ~0u, true);
       } else {  // columns past the volume may hold stale lse / Delta: masked to exact zeros
         const uint32_t mask = valid > 0 ? ~0u >> (32 - valid) : 0u;
-        ok = kv_chunk<C, BF16, true, true>(bars, ch, t_lanes, col0, vals, vals + kGCols, sc, mask, valid > 0);
+        ok = kv_chunk<C, BF16, true>(bars, ch, t_lanes, col0, vals, vals + kGCols, sc, mask, valid > 0);
       }
     }
     if (ok) ok = kv_wait_warp(bars, kVAccReady, 0);
@@ -1068,7 +1059,6 @@ int launch_gkv_t(const GlobalDkvArgs &a, cudaStream_t stream) {
   p.q_chunks = (a.tokens + kGCols - 1) / kGCols;
   p.splits = a.splits;
   p.per_split = a.per_split;
-  p.bulk_vals = a.tokens % 4 == 0 && ((uintptr_t)a.lse_g & 15) == 0 && ((uintptr_t)a.delta_g & 15) == 0;
   p.sc = kLog2e / sqrtf((float)D);
   p.inv_sqrt_d = 1.f / sqrtf((float)D);
   p.lse_g = a.lse_g;
@@ -1269,7 +1259,7 @@ __global__ void __launch_bounds__(kKvThreads, 2)
       // take the chunk through a zero mask
       const bool active = (unsigned)(pl - 2 * quarter) <= 2u * R + 1u;
       const uint32_t m = (unsigned)(pl - zl) <= 2u * R ? ((ch % kParts) ? mask1 : mask0) : 0u;
-      ok = kv_chunk<C, BF16, true, false>(bars, ch, t_lanes, col0, vals, vals + kKvCols, sc, m, active);
+      ok = kv_chunk<C, BF16, true>(bars, ch, t_lanes, col0, vals, vals + kKvCols, sc, m, active);
     }
     if (ok) ok = kv_wait_warp(bars, kVAccReady, 0);
     if (ok) {
