@@ -123,6 +123,19 @@ P3D_API int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl, vo
                   int pz, int py, int px, const float *phases, int ez, int ey, int ex, unsigned flags,
                   void *stream);
 
+/* p3d_qkv_gate_split: p3d_qkv_split plus the layer's gate, from one GEMM output.  proj is
+ *   [B*N, proj_cols] (row stride proj_cols elements, a multiple of 8): columns [0, H*D) the to_q
+ *   projection, the next 4*G*D the to_kv projection, the next 2*H the gate logits (head-major
+ *   pairs, as nn.Linear(dim, 2H) of attention.py:64 lays them out); further columns are
+ *   ignored.  q .. vg as p3d_qkv_split; gate [B, H, N] = softmax over each logit pair, second
+ *   entry (attention.py:84-86), computed in fp32 and rounded once.  Replaces the to_q / to_kv
+ *   / gate Linear outputs' reshapes, the rotations and the gate softmax of attention.py:70-86
+ *   in one pass; the caller runs one GEMM with the three weights stacked. */
+P3D_API int p3d_qkv_gate_split(const void *proj, int proj_cols, void *q, void *kl, void *vl, void *kg, void *vg,
+                       void *gate, int dtype, int batch, int heads, int kv_heads, int tokens, int head_dim,
+                       const int64_t *coords, int pz, int py, int px, const float *phases, int ez, int ey, int ex,
+                       unsigned flags, void *stream);
+
 /*
  * p3d_qkv_project: the projections and the split in one kernel -- the two nn.Linear calls of
  *   attention.py:70-72 (to_q, to_kv; weights wq [H*D, dim], wkv [4*G*D, dim], no bias) on x

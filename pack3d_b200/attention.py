@@ -155,9 +155,9 @@ class PACK3DAttention(nn.Module):
         raster = (not self.fused_projection and phase_tables(x.device, balanced_pairs(self.head_dim), extents)[1]
                   is not None and raster_qkv_applies(layout.geometry, x.dtype, self.head_dim, x.device))
         x, q, kl, vl, kg, vg, gate = self._inference_glue(x, layout.coords, layout.grid_shape, raster_qkv=raster)
-        y, _ = core_forward(q, kl, vl, kg, vg, self.pool_weight, self.slot_bias, gate, self.local_scale,
-                            self.global_scale, layout.geometry, self.temperature, save_state=False, y_rows=True,
-                            raster_qkv=raster)
+        w32, b32, sl32, sg32 = self._core_params_f32()
+        y, _ = core_forward(q, kl, vl, kg, vg, w32, b32, gate, sl32, sg32, layout.geometry, self.temperature,
+                            save_state=False, y_rows=True, raster_qkv=raster)
         return self._out_residual(x, y)
 
     def _out_residual(self, x, y_rows):
@@ -198,12 +198,32 @@ class PACK3DAttention(nn.Module):
                                                        extents, h, g, d)
             gate = self.gate(xn).reshape(b, n, h, 2).softmax(-1)[..., 1].transpose(1, 2).contiguous()
             return x, q, kl, vl, kg, vg, gate
-        qp, kvp = self.to_q(xn), self.to_kv(xn)
+        if phases is not None and h <= 16:
+            # one GEMM for to_q, to_kv and gate (weights stacked, gate bias in the epilogue); one
+            # pass splits, rotates and forms the gate (p3d_qkv_gate_split, up to 16 heads)
+            w, bias = self._stacked_projection(x.dtype, dev)
+            proj = torch.addmm(bias, xn.view(b * n, self.dim), w.t())
+            qp = kvp = None
+        else:
+            qp, kvp = self.to_q(xn), self.to_kv(xn)
         if phases is None:   # coordinate extents too large for a table: the general RoPE path
             q, kl, kg = rotate_projections(qp.reshape(b, n, h, d).transpose(1, 2),
                                            *(t.reshape(b, n, g, d).transpose(1, 2) for t in kvp.chunk(4, -1)[0::2]),
                                            coords, pairs, extents, packed=False)
             vl, vg = (t.reshape(b, n, g, d).transpose(1, 2).contiguous() for t in kvp.chunk(4, -1)[1::2])
+        elif qp is None:
+            coords = coords.to(device=dev, dtype=torch.int64).contiguous()
+            q = torch.empty((b, h, n, d), dtype=x.dtype, device=dev)
+            kl, vl, kg, vg = (torch.empty((b, g, n, d), dtype=x.dtype, device=dev) for _ in range(4))
+            gate = torch.empty((b, h, n), dtype=x.dtype, device=dev)
+            with torch.cuda.device(dev):
+                _native.check(lib.p3d_qkv_gate_split(_native.ptr(proj), proj.shape[1], _native.ptr(q), _native.ptr(kl),
+                                                     _native.ptr(vl), _native.ptr(kg), _native.ptr(vg),
+                                                     _native.ptr(gate), code, b, h, g, n, d, _native.ptr(coords),
+                                                     *pairs, _native.ptr(phases), *extents,
+                                                     _native.SPLIT_RASTER_QKV if raster_qkv else 0, stream),
+                              "p3d_qkv_gate_split")
+            return x, q, kl, vl, kg, vg, gate
         else:
             coords = coords.to(device=dev, dtype=torch.int64).contiguous()
             q = torch.empty((b, h, n, d), dtype=x.dtype, device=dev)
@@ -216,3 +236,35 @@ class PACK3DAttention(nn.Module):
                               "p3d_qkv_split")
         gate = self.gate(xn).reshape(b, n, h, 2).softmax(-1)[..., 1].transpose(1, 2).contiguous()
         return x, q, kl, vl, kg, vg, gate
+
+    def _core_params_f32(self):
+        """``(pool_weight, slot_bias, local_scale, global_scale)`` in fp32, as the core's kernels
+        take them, cached until any of them changes (inference calls would otherwise convert
+        them on every call)."""
+        params = (self.pool_weight, self.slot_bias, self.local_scale, self.global_scale)
+        key = tuple((t.data_ptr(), t._version, t.device) for t in params)
+        hit = getattr(self, "_params_f32", None)
+        if hit is None or hit[0] != key:
+            with torch.inference_mode(False), torch.no_grad():
+                hit = (key, tuple(t.detach().to(torch.float32).contiguous() for t in params))
+            self._params_f32 = hit
+        return hit[1]
+
+    def _stacked_projection(self, dtype, device):
+        """``(W, bias)``: the to_q, to_kv and gate weights stacked row-wise (zero rows pad the
+        count to a multiple of 8) and the matching bias (zero, zero, gate bias), cached until
+        any of those parameters changes."""
+        params = (self.to_q.weight, self.to_kv.weight, self.gate.weight, self.gate.bias)
+        key = (dtype, device) + tuple((t.data_ptr(), t._version) for t in params)
+        hit = getattr(self, "_stacked", None)
+        if hit is not None and hit[0] == key:
+            return hit[1], hit[2]
+        with torch.inference_mode(False), torch.no_grad():
+            rows = self.to_q.weight.shape[0] + self.to_kv.weight.shape[0] + self.gate.weight.shape[0]
+            pad = -rows % 8
+            w = torch.cat([self.to_q.weight, self.to_kv.weight, self.gate.weight,
+                           self.gate.weight.new_zeros(pad, self.dim)]).to(device=device, dtype=dtype).contiguous()
+            bias = torch.cat([self.gate.bias.new_zeros(self.to_q.weight.shape[0] + self.to_kv.weight.shape[0]),
+                              self.gate.bias, self.gate.bias.new_zeros(pad)]).to(device=device, dtype=dtype)
+        self._stacked = (key, w, bias)
+        return w, bias

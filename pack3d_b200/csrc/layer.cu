@@ -362,9 +362,14 @@ struct SplitParams {
   const float *phases;    // (cos, sin) per (axis, coordinate, pair)
   int raster_qkv;         // split: q, kl, vl rows at the token's raster index (ey x ex planes)
   int ey, ex;
+  int q_stride, kv_stride;  // elements between consecutive tokens' rows of qp / kvp
+  const void *gate_logits;  // split only, or null: [token][head][2] logits at gate_stride per token
+  int gate_stride;
+  void *gate;               // [B, H, N]: softmax over each logit pair, second entry
 };
 
 constexpr int kTokensPerWarp = 4;
+constexpr int kGateRounds = 2;  // lanes x rounds cover the (token, head) gates of a warp: heads <= 16
 
 template <typename T>
 __device__ __forceinline__ T *pick(const SplitParams &p, int part) {  // out[1 + part] without a local array
@@ -417,8 +422,20 @@ __global__ void __launch_bounds__(kWarps * 32, 4) qkv_pass_kernel(SplitParams p)
   const int b = blockIdx.y;
   const int n_begin = (blockIdx.x * kWarps + (threadIdx.x >> 5)) * kTokensPerWarp;
   const int rows = p.heads + 4 * p.kv_heads;  // head rows per token
-  const int qw = p.heads * D, kvw = 4 * p.kv_heads * D;  // elements per projection row
+  const int qw = p.q_stride, kvw = p.kv_stride;  // elements between projection rows
   T *qrow_w = static_cast<T *>(const_cast<void *>(p.qp)), *kvrow_w = static_cast<T *>(const_cast<void *>(p.kvp));
+  // the gate logit pairs of this warp's tokens (split with a gate only), loaded first so that
+  // their latency overlaps the head rows
+  uint32_t gate_pair[kGateRounds] = {};
+  if (!MERGE && p.gate_logits != nullptr) {
+#pragma unroll
+    for (int r = 0; r < kGateRounds; ++r) {
+      const int k = lane + 32 * r, t = k / p.heads, h = k - t * p.heads, n = n_begin + t;
+      if (k < kTokensPerWarp * p.heads && n < p.tokens)
+        gate_pair[r] = __ldg(reinterpret_cast<const uint32_t *>(static_cast<const T *>(p.gate_logits) +
+                                                                ((int64_t)b * p.tokens + n) * p.gate_stride + 2 * h));
+    }
+  }
   for (int base = 0; base < rows; base += kRows * kBatch) {
     // token-independent: each pass's head row, its head-major tensor row of token 0, its
     // offset in the projection rows, whether it rotates
@@ -480,6 +497,21 @@ __global__ void __launch_bounds__(kWarps * 32, 4) qkv_pass_kernel(SplitParams p)
         }
         store8<T>(MERGE ? (isq[i] ? qrow : kvrow) + off[i] : head[i] + (to_raster[i] ? nr : (int64_t)n) * D, v);
       }
+    }
+  }
+  if (!MERGE && p.gate_logits != nullptr) {
+    // the gate of the reference layer (attention.py:84-86): softmax over each head's logit pair,
+    // second entry, in fp32 (expf, then a division) and rounded to the storage type once; a
+    // lane per (token, head), its pair loaded before the head rows (gate_pair)
+    T *gate = static_cast<T *>(p.gate);
+#pragma unroll
+    for (int r = 0; r < kGateRounds; ++r) {
+      const int k = lane + 32 * r, t = k / p.heads, h = k - t * p.heads, n = n_begin + t;
+      if (k >= kTokensPerWarp * p.heads || n >= p.tokens) continue;
+      const float2 l = unpack2<T>(gate_pair[r]);
+      const float m = fmaxf(l.x, l.y);
+      const float e0 = expf(l.x - m), e1 = expf(l.y - m);
+      gate[((int64_t)b * p.heads + h) * p.tokens + n] = from_f32<T>(e1 / (e0 + e1));
     }
   }
 }
@@ -711,6 +743,58 @@ extern "C" int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl,
   p.raster_qkv = (flags & P3D_SPLIT_RASTER_QKV) ? 1 : 0;
   p.ey = ey;
   p.ex = ex;
+  p.q_stride = heads * head_dim;
+  p.kv_stride = 4 * kv_heads * head_dim;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return dtype == P3D_BF16 ? launch_split<__nv_bfloat16>(p, head_dim, s) : launch_split<__half>(p, head_dim, s);
+}
+
+extern "C" int p3d_qkv_gate_split(const void *proj, int proj_cols, void *q, void *kl, void *vl, void *kg, void *vg,
+                                  void *gate, int dtype, int batch, int heads, int kv_heads, int tokens, int head_dim,
+                                  const int64_t *coords, int pz, int py, int px, const float *phases, int ez, int ey,
+                                  int ex, unsigned flags, void *stream) {
+  const void *const ptrs[7] = {proj, gate, q, kl, vl, kg, vg};
+  if (int st = check_split("p3d_qkv_gate_split", ptrs, dtype, batch, heads, kv_heads, tokens, head_dim, coords, pz,
+                           py, px, phases, ez, ey, ex))
+    return st;
+  P3D_CHECK_ARG((flags & ~P3D_SPLIT_RASTER_QKV) == 0u, "p3d_qkv_gate_split: unknown flags 0x%x", flags);
+  P3D_CHECK_ARG(!(flags & P3D_SPLIT_RASTER_QKV) || (int64_t)ez * ey * ex == tokens,
+                "p3d_qkv_gate_split: raster rows need the coordinate extents to be the token grid (%d x %d x %d != %d)",
+                ez, ey, ex, tokens);
+  P3D_CHECK_ARG(heads <= 32 * kGateRounds / kTokensPerWarp, "p3d_qkv_gate_split: at most %d heads",
+                32 * kGateRounds / kTokensPerWarp);
+  const int used = (heads + 4 * kv_heads) * head_dim + 2 * heads;
+  P3D_CHECK_ARG(proj_cols >= used && proj_cols % 8 == 0,
+                "p3d_qkv_gate_split: proj_cols %d must cover the %d projection columns and be a multiple of 8",
+                proj_cols, used);
+  if ((int64_t)batch * tokens == 0) return P3D_OK;
+  const size_t es = 2;
+  SplitParams p{};
+  p.qp = proj;
+  p.kvp = static_cast<const char *>(proj) + es * heads * head_dim;
+  p.out[0] = q;
+  p.out[1] = kl;
+  p.out[2] = vl;
+  p.out[3] = kg;
+  p.out[4] = vg;
+  p.batch = batch;
+  p.heads = heads;
+  p.kv_heads = kv_heads;
+  p.tokens = tokens;
+  p.coords = coords;
+  p.pairs[0] = pz;
+  p.pairs[1] = py;
+  p.pairs[2] = px;
+  p.start[0] = 0;
+  p.start[1] = ez * pz;
+  p.start[2] = ez * pz + ey * py;
+  p.phases = phases;
+  p.raster_qkv = (flags & P3D_SPLIT_RASTER_QKV) ? 1 : 0;
+  p.ey = ey;
+  p.ex = ex;
+  p.q_stride = p.kv_stride = p.gate_stride = proj_cols;
+  p.gate_logits = static_cast<const char *>(proj) + es * (heads + 4 * kv_heads) * head_dim;
+  p.gate = gate;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return dtype == P3D_BF16 ? launch_split<__nv_bfloat16>(p, head_dim, s) : launch_split<__half>(p, head_dim, s);
 }
@@ -744,6 +828,8 @@ extern "C" int p3d_qkv_merge(const void *dq, const void *dkl, const void *dvl, c
   p.start[1] = ez * pz;
   p.start[2] = ez * pz + ey * py;
   p.phases = phases;
+  p.q_stride = heads * head_dim;
+  p.kv_stride = 4 * kv_heads * head_dim;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return dtype == P3D_BF16 ? launch_merge<__nv_bfloat16>(p, head_dim, s) : launch_merge<__half>(p, head_dim, s);
 }

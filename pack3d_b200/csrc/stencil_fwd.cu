@@ -770,19 +770,21 @@ int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
   return P3D_OK;
 }
 
-// bound[bg] = max_j |sk[bg, j, :]| for the fixed-reference global softmax: one block per
-// (batch, kv-head), a thread per summary row, squared norms in fp32 and a block maximum.  The
-// norm is rounded up by 2^-10 so that rounding in the norm cannot put it below a score.
+// bound[bg] = max_j |sk[bg, j, :]| for the fixed-reference global softmax: blockIdx.y is the
+// (batch, kv-head), blockIdx.x a slice of its summary rows, a thread per row; squared norms in
+// fp32, a block maximum, then an atomic maximum on the float's bits (non-negative floats order
+// as unsigned integers; bound[] starts at zero).  The norm is rounded up by 2^-10 so that
+// rounding in the norm cannot put it below a score.
 template <bool BF16>
-__global__ void __launch_bounds__(1024) summary_bound_kernel(const uint32_t *sk, int M, int D, float *bound) {
-  __shared__ float part[32];
-  const uint32_t *base = sk + (int64_t)blockIdx.x * M * (D / 2);
+__global__ void __launch_bounds__(128) summary_bound_kernel(const uint32_t *sk, int M, int D, float *bound) {
+  __shared__ float part[4];
+  const uint32_t *base = sk + (int64_t)blockIdx.y * M * (D / 2);
   float best = 0.f;
-  for (int j = threadIdx.x; j < M; j += blockDim.x) {
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < M; j += gridDim.x * blockDim.x) {
     const uint32_t *row = base + (int64_t)j * (D / 2);
     float acc = 0.f;
     for (int d = 0; d < D / 2; ++d) {
-      const float2 f = unpack2<BF16>(row[d]);
+      const float2 f = unpack2<BF16>(__ldg(row + d));
       acc = fmaf(f.x, f.x, acc);
       acc = fmaf(f.y, f.y, acc);
     }
@@ -791,10 +793,10 @@ __global__ void __launch_bounds__(1024) summary_bound_kernel(const uint32_t *sk,
   for (int o = 16; o; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
   if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = best;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    best = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
-    for (int o = 16; o; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
-    if (threadIdx.x == 0) bound[blockIdx.x] = sqrtf(best) * (1.f + 1.f / 1024.f);
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = fmaxf(best, part[w]);
+    const float b = sqrtf(best) * (1.f + 1.f / 1024.f);
+    atomicMax(reinterpret_cast<unsigned *>(bound) + blockIdx.y, __float_as_uint(b));
   }
 }
 
@@ -806,12 +808,14 @@ int launch_summary_bound(const void *sk, int dtype, int bg, int summaries, int h
   if (head_dim < 2 || head_dim % 2 || summaries < 1 || bg < 1)
     return fail(P3D_ERR_INVALID_ARGUMENT, "summary bound: bad shape");
   if (((uintptr_t)sk & 3) != 0) return fail(P3D_ERR_INVALID_ARGUMENT, "summary bound: misaligned summaries");
-  const int threads = summaries >= 1024 ? 1024 : (summaries + 31) / 32 * 32;
+  if (bg > 65535) return fail(P3D_ERR_UNSUPPORTED, "summary bound: too many (batch, kv-head) pairs");
+  P3D_CUDA_TRY(cudaMemsetAsync(bound, 0, sizeof(float) * (size_t)bg, stream));
+  const dim3 grid((unsigned)std::min((summaries + 127) / 128, 64), (unsigned)bg);
   const uint32_t *src = static_cast<const uint32_t *>(sk);
   if (dtype == P3D_BF16)
-    summary_bound_kernel<true><<<bg, threads, 0, stream>>>(src, summaries, head_dim, bound);
+    summary_bound_kernel<true><<<grid, 128, 0, stream>>>(src, summaries, head_dim, bound);
   else
-    summary_bound_kernel<false><<<bg, threads, 0, stream>>>(src, summaries, head_dim, bound);
+    summary_bound_kernel<false><<<grid, 128, 0, stream>>>(src, summaries, head_dim, bound);
   P3D_LAUNCH_CHECK();
   return P3D_OK;
 }

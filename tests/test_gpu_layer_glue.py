@@ -80,6 +80,50 @@ def test_qkv_split_raster_rows_are_the_token_rows_permuted(cuda_device, dtype, h
             _native.SPLIT_RASTER_QKV, _native.stream_of(cuda_device)), "p3d_qkv_split")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("h,g,d", [(4, 4, 48), (3, 1, 32), (2, 2, 64)])
+def test_qkv_gate_split_matches_the_split_and_the_torch_gate(cuda_device, dtype, h, g, d):
+    """p3d_qkv_gate_split on one stacked projection buffer (q, kv, gate logits, padding columns)
+    gives the split's q .. vg bit for bit and the layer's gate (softmax over each logit pair,
+    second entry) as torch computes it."""
+    layout = _layout((8, 12, 16), raster=False).to(cuda_device)
+    b, n = 2, layout.geometry.num_tokens
+    gen = torch.Generator(device=cuda_device).manual_seed(31 * h + d)
+    used = (h + 4 * g) * d + 2 * h
+    cols = used + (-used % 8) + 8  # padding columns beyond the ones the kernel reads
+    proj = (torch.randn(b, n, cols, device=cuda_device, generator=gen) * 2).to(dtype)
+    qp, kvp = proj[..., :h * d].contiguous(), proj[..., h * d:(h + 4 * g) * d].contiguous()
+    logits = proj[..., (h + 4 * g) * d:used]
+    pairs = balanced_pairs(d)
+    extents = layout.grid_shape
+    _, phases = phase_tables(cuda_device, pairs, extents)
+    coords = layout.coords.contiguous()
+    lib = _native.lib()
+    want = [torch.empty((b, h, n, d), dtype=dtype, device=cuda_device)]
+    want += [torch.empty((b, g, n, d), dtype=dtype, device=cuda_device) for _ in range(4)]
+    got = [torch.empty_like(t) for t in want]
+    gate = torch.empty((b, h, n), dtype=dtype, device=cuda_device)
+    code, stream = _native.DTYPE_CODE[dtype], _native.stream_of(cuda_device)
+    with torch.cuda.device(cuda_device):
+        _native.check(lib.p3d_qkv_split(_native.ptr(qp), _native.ptr(kvp), *[_native.ptr(t) for t in want], code, b,
+                                        h, g, n, d, _native.ptr(coords), *pairs, _native.ptr(phases), *extents, 0,
+                                        stream), "p3d_qkv_split")
+        _native.check(lib.p3d_qkv_gate_split(_native.ptr(proj), cols, *[_native.ptr(t) for t in got],
+                                             _native.ptr(gate), code, b, h, g, n, d, _native.ptr(coords), *pairs,
+                                             _native.ptr(phases), *extents, 0, stream), "p3d_qkv_gate_split")
+    for name, w, o in zip(("q", "kl", "vl", "kg", "vg"), want, got):
+        assert torch.equal(w, o), name
+    want_gate = logits.reshape(b, n, h, 2).softmax(-1)[..., 1].transpose(1, 2)
+    step = 2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11
+    assert (gate.float() - want_gate.float()).abs().max().item() <= step, "gate"
+    assert torch.equal(gate, want_gate) or (gate != want_gate).float().mean().item() < 1e-3
+    # the column count must cover the projections and keep rows 16-byte aligned
+    with pytest.raises(ValueError, match="proj_cols"):
+        _native.check(lib.p3d_qkv_gate_split(_native.ptr(proj), used - 2, *[_native.ptr(t) for t in got],
+                                             _native.ptr(gate), code, b, h, g, n, d, _native.ptr(coords), *pairs,
+                                             _native.ptr(phases), *extents, 0, stream), "p3d_qkv_gate_split")
+
+
 @pytest.mark.parametrize("dim", [192, 384, 64, 128, 256, 40])
 def test_layer_norm_matches_torch(cuda_device, dim):
     # 64 k <= 256: segment layout (4 rows per warp pass; 2999 rows leave a ragged last group)

@@ -120,3 +120,23 @@ def test_radius_one_stencil_forward_matches_indexed_and_oracle(cuda_device, grid
     want = oracle.core_forward(*[t.float() if t.dtype != torch.float32 else t for t in inputs[:5]], *inputs[5:],
                                geom.neighbors, geom.blocks, pool, chunk=2048)
     assert (y_tc.float().cpu() - want["y"].float()).abs().max().item() <= tol
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("bg,m,d", [(4, 4096, 48), (3, 300, 64), (1, 1, 16), (2, 8191, 32)])
+def test_summary_bound_is_the_largest_summary_norm(cuda_device, dtype, bg, m, d):
+    """p3d_summary_bound: per (batch, kv-head) the largest summary-row norm, rounded up by 2^-10
+    (never below a norm the kernel's own arithmetic could see)."""
+    from pack3d_b200 import _native
+    gen = torch.Generator(device=cuda_device).manual_seed(bg * 1000 + m)
+    sk = (torch.randn(bg, m, d, device=cuda_device, generator=gen) * 3).to(dtype)
+    sk[0, m // 2] *= 4  # one row clearly the largest
+    bound = torch.full((bg,), -1.0, device=cuda_device)
+    with torch.cuda.device(cuda_device):
+        _native.check(_native.lib().p3d_summary_bound(_native.ptr(sk), _native.DTYPE_CODE[dtype], 1, bg, m, d,
+                                                      _native.ptr(bound), _native.stream_of(cuda_device)),
+                      "p3d_summary_bound")
+    want = sk.double().norm(dim=-1).amax(dim=-1)
+    got = bound.double()
+    assert torch.all(got >= want * (1 + 2.0 ** -12)), (got, want)
+    assert torch.all(got <= want * (1 + 2.0 ** -9)), (got, want)
