@@ -46,7 +46,7 @@ enum : int {
   kXFull = 1,       // [2]
   kXEmpty = 3,      // [2]
   kAccFull = 5,     // [2]
-  kAccEmpty = 7,    // [2], 128 arrivals (the epilogue threads)
+  kAccEmpty = 7,    // [2], one arrival per epilogue warp
   kDrain = 9,
   kNumBars = 10
 };
@@ -94,7 +94,18 @@ __device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
   return BF16 ? pack_bf16(lo, hi) : pack_f16(lo, hi);
 }
 
-template <bool BF16, int D>
+// Pairs per axis of balanced_pairs(D) (rope.py: D / 2 pairs dealt evenly over z, y, x, the
+// remainder first): when the call uses them, the epilogue knows every pair's axis at compile
+// time and reads its (cos, sin) at a constant offset from the token's per-axis table row.
+template <int D>
+struct Balanced {
+  static constexpr int kShare = D / 2 / 3, kExtra = D / 2 % 3;
+  static constexpr int count(int axis) { return kShare + (axis < kExtra ? 1 : 0); }
+  static constexpr int axis_of(int pair) { return pair < count(0) ? 0 : pair < count(0) + count(1) ? 1 : 2; }
+  static constexpr int first(int axis) { return axis == 0 ? 0 : axis == 1 ? count(0) : count(0) + count(1); }
+};
+
+template <bool BF16, int D, bool kBalanced>
 __global__ void __launch_bounds__(kThreads, 1)
     proj_split_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap twq,
                       const __grid_constant__ CUtensorMap twkv, const ProjParams p) {
@@ -125,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kXFull + s), 1);
       mbar_init(bar(kXEmpty + s), 1);
       mbar_init(bar(kAccFull + s), 1);
-      mbar_init(bar(kAccEmpty + s), kEpilogueThreads);
+      mbar_init(bar(kAccEmpty + s), kEpilogueThreads / 32);
     }
     mbar_init(bar(kDrain), 1);
     fence_mbar_init();
@@ -173,12 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(kTile, G, BF16, false);
-      uint32_t commits[kNumBars];
-      for (int i = 0; i < kNumBars; ++i) commits[i] = 0u;
-      auto commit = [&](int b_idx) {
-        mma_commit(bar(b_idx));
-        ++commits[b_idx];
-      };
+      int n_mma = 0;  // tiles whose MMAs were issued (each commits kXEmpty and kAccFull of its stage)
       const uint64_t desc_w = desc_sw128(w_smem, 1024);  // K-major, 8-row groups of 128-byte rows
       const uint64_t desc_x = desc_sw128(x_smem, 1024);
       bool ok = mbar_wait(bar(kWFull), 0, &g_proj_errors, kWaitNs, kErrMma);
@@ -195,12 +201,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 4; ++k)  // K = 16 slices: 32 bytes along the 128-byte rows
             mma_ss(tmem + a * G, dx + ((c * x_atom + 32 * k) >> 4), desc_w + ((c * w_atom + 32 * k) >> 4), idesc,
                    (c | k) ? 1u : 0u);
-        commit(kXEmpty + s);
-        commit(kAccFull + a);
+        mma_commit(bar(kXEmpty + s));
+        mma_commit(bar(kAccFull + a));
+        n_mma = i + 1;
       }
-      commit(kDrain);
-      for (int i = 0; i < kNumBars; ++i)
-        if (commits[i]) mbar_wait(bar(i), (commits[i] - 1) & 1, &g_proj_errors, kWaitNs, kErrTeardown);
+      // drain: the last commit first, then each barrier's last phase (stage / accumulator s was
+      // committed once per tile i < n_mma with i % 2 == s)
+      mma_commit(bar(kDrain));
+      mbar_wait(bar(kDrain), 0, &g_proj_errors, kWaitNs, kErrTeardown);
+      for (int st = 0; st < 2; ++st) {
+        const int times = n_mma / 2 + (st < n_mma % 2 ? 1 : 0);
+        if (times) {
+          mbar_wait(bar(kXEmpty + st), (times - 1) & 1, &g_proj_errors, kWaitNs, kErrTeardown);
+          mbar_wait(bar(kAccFull + st), (times - 1) & 1, &g_proj_errors, kWaitNs, kErrTeardown);
+        }
+      }
     }
   } else {
     // ------------------------------------------------------------------ epilogue
@@ -256,23 +271,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           packed[q2] = pack_pair<BF16>(__uint_as_float(acc[2 * q2]), __uint_as_float(acc[2 * q2 + 1]));
         }
         if (rot) {
+          // the token's table row of each axis (balanced pairs: pair q2 sits at a constant
+          // offset from the row of its axis)
+          const float *row_axis[3];
+#pragma unroll
+          for (int ax = 0; ax < 3; ++ax) row_axis[ax] = tab + 2 * (p.start[ax] + c3[ax] * p.pairs[ax]);
 #pragma unroll
           for (int q2 = 0; q2 < D / 2; ++q2) {
             const float2 e_o = unpack_pair<BF16>(packed[q2]);
-            const float2 c = pair_cs(p, tab, c3, q2);
+            float2 c;
+            if constexpr (kBalanced) {  // q2 is a constant in each unrolled step: the axis folds
+              const int ax = Balanced<D>::axis_of(q2);
+              c = *reinterpret_cast<const float2 *>(row_axis[ax] + 2 * (q2 - Balanced<D>::first(ax)));
+            } else {
+              c = pair_cs(p, tab, c3, q2);
+            }
             const float even = __fsub_rn(__fmul_rn(e_o.x, c.x), __fmul_rn(e_o.y, c.y));
             const float odd = __fadd_rn(__fmul_rn(e_o.x, c.y), __fmul_rn(e_o.y, c.x));
             packed[q2] = pack_pair<BF16>(even, odd);
           }
         }
-        void *o = is_q ? p.out[0] : p.out[1 + part];
+        // a select chain, not p.out[1 + part]: a runtime index would move the parameters to local memory
+        void *o = is_q ? p.out[0] : part == 0 ? p.out[1] : part == 1 ? p.out[2] : part == 2 ? p.out[3] : p.out[4];
         uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(o) + (((int64_t)b * ht + hh) * p.tokens + n) * D);
 #pragma unroll
         for (int v = 0; v < D / 8; ++v)
           dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
       }
       tc_fence_before();
-      mbar_arrive(bar(kAccEmpty + a));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kAccEmpty + a));
     }
   }
   __syncwarp();
@@ -329,9 +357,11 @@ int launch_proj(const ProjArgs &a, cudaStream_t stream) {
   p.phases = a.phases;
   p.table_floats = a.table_floats;
   const size_t smem = proj_smem_bytes(a.dim, gh * D);
-  auto kernel = proj_split_kernel<BF16, D>;
-  static size_t seen[kMaxDevices] = {};
-  if (int st = smem_optin(kernel, smem, seen)) return st;
+  const bool balanced = p.pairs[0] == Balanced<D>::count(0) && p.pairs[1] == Balanced<D>::count(1) &&
+                        p.pairs[2] == Balanced<D>::count(2);
+  auto kernel = balanced ? proj_split_kernel<BF16, D, true> : proj_split_kernel<BF16, D, false>;
+  static size_t seen[2][kMaxDevices] = {};
+  if (int st = smem_optin(kernel, smem, seen[balanced ? 1 : 0])) return st;
   kernel<<<p.groups * p.ctas_per_group, kThreads, smem, stream>>>(tx, twq, twkv, p);
   P3D_LAUNCH_CHECK();
   return P3D_OK;
