@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define P3D_ABI_VERSION 2
+#define P3D_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define P3D_API __attribute__((visibility("default")))
@@ -131,6 +131,12 @@ P3D_API int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl, vo
  *   entry (attention.py:84-86), computed in fp32 and rounded once.  Replaces the to_q / to_kv
  *   / gate Linear outputs' reshapes, the rotations and the gate softmax of attention.py:70-86
  *   in one pass; the caller runs one GEMM with the three weights stacked. */
+/* p3d_gate_pairs: the layer's gate from its Linear's output: logits [B*N, stride] (row stride in
+ *   elements; columns 2h, 2h + 1 are head h's pair), gate [B, H, N] = softmax over each pair,
+ *   second entry (attention.py:84-86), in fp32, rounded once.  Used beside p3d_qkv_project. */
+P3D_API int p3d_gate_pairs(const void *logits, int stride, void *gate, int dtype, int batch, int heads, int tokens,
+                   void *stream);
+
 P3D_API int p3d_qkv_gate_split(const void *proj, int proj_cols, void *q, void *kl, void *vl, void *kg, void *vg,
                        void *gate, int dtype, int batch, int heads, int kv_heads, int tokens, int head_dim,
                        const int64_t *coords, int pz, int py, int px, const float *phases, int ez, int ey, int ex,
@@ -141,14 +147,15 @@ P3D_API int p3d_qkv_gate_split(const void *proj, int proj_cols, void *q, void *k
  *   attention.py:70-72 (to_q, to_kv; weights wq [H*D, dim], wkv [4*G*D, dim], no bias) on x
  *   [B*N, dim], followed by p3d_qkv_split: each projection is rounded to dtype, as the GEMM's
  *   output would be, then rotated and stored head-major as p3d_qkv_split stores it.  The
- *   projections never reach HBM.  Shapes p3d_qkv_project_supported() rejects return
- *   P3D_ERR_UNSUPPORTED (callers then run the GEMMs and p3d_qkv_split).
+ *   projections never reach HBM.  flags: P3D_SPLIT_RASTER_QKV as for p3d_qkv_split.  Shapes
+ *   p3d_qkv_project_supported() rejects return P3D_ERR_UNSUPPORTED (callers then run the
+ *   GEMMs and p3d_qkv_split).
  */
 P3D_API int p3d_qkv_project_supported(int dtype, int dim, int heads, int kv_heads, int head_dim);
 P3D_API int p3d_qkv_project(const void *x, const void *wq, const void *wkv, void *q, void *kl, void *vl, void *kg,
                     void *vg, int dtype, int batch, int heads, int kv_heads, int tokens, int dim, int head_dim,
                     const int64_t *coords, int pz, int py, int px, const float *phases, int ez, int ey, int ex,
-                    void *stream);
+                    unsigned flags, void *stream);
 
 /*
  * Layer glue of the training path (their backward halves):

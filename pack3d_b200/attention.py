@@ -33,9 +33,10 @@ class PACK3DAttention(nn.Module):
       with its RoPE, and their backward halves in the library's kernels, and feed the core's
       token-major output to ``to_out`` together with the residual in one GEMM.  False keeps
       the per-op PyTorch path.
-    * ``fused_projection`` (default False): with ``fused_glue``, run the two projections and
-      the split in one tensor-core kernel (``p3d_qkv_project``).  It moves about half the
-      bytes, but it is not faster than cuBLAS plus the split kernel at present.
+    * ``fused_projection`` (default True): with ``fused_glue``, run the two projections and
+      the split with its RoPE in one tensor-core kernel (``p3d_qkv_project``) where it
+      supports the shape (16-bit, dim a multiple of 64); the projections never reach HBM.
+      False runs cuBLAS GEMMs and the split kernel instead.
     """
 
     def __init__(self, dim, *, heads=4, kv_heads=2, head_dim=32, block_volume=8, backend="b200",
@@ -69,10 +70,10 @@ class PACK3DAttention(nn.Module):
         # 16-bit CUDA training calls run LayerNorm and the projection split (with RoPE) in the
         # fused library kernels of pack3d_b200.glue; False keeps the per-op PyTorch path.
         self.fused_glue = True
-        # p3d_qkv_project (projections + split in one tensor-core kernel) instead of the two
-        # cuBLAS projections and p3d_qkv_split: less HBM traffic, but not faster at present
-        # (0.355 vs 0.324 ms at config 1), so off by default
-        self.fused_projection = False
+        # p3d_qkv_project (projections + split + RoPE in one tensor-core kernel, the projections
+        # never written to HBM) where it supports the shape: 0.22 ms at config 1 against 0.36 ms
+        # for the stacked cuBLAS GEMM and p3d_qkv_gate_split; False keeps the latter
+        self.fused_projection = True
 
     def forward(self, x, layout: TokenLayout):
         layout.check_unmodified()
@@ -152,8 +153,8 @@ class PACK3DAttention(nn.Module):
         # permuted storage (Morton blocks): the split writes q, kl, vl at raster rows, so the
         # tensor-core stencil kernel reads them without a gather pass
         extents = tuple(int(e) for e in layout.grid_shape)
-        raster = (not self.fused_projection and phase_tables(x.device, balanced_pairs(self.head_dim), extents)[1]
-                  is not None and raster_qkv_applies(layout.geometry, x.dtype, self.head_dim, x.device))
+        raster = (phase_tables(x.device, balanced_pairs(self.head_dim), extents)[1] is not None
+                  and raster_qkv_applies(layout.geometry, x.dtype, self.head_dim, x.device))
         x, q, kl, vl, kg, vg, gate = self._inference_glue(x, layout.coords, layout.grid_shape, raster_qkv=raster)
         w32, b32, sl32, sg32 = self._core_params_f32()
         y, _ = core_forward(q, kl, vl, kg, vg, w32, b32, gate, sl32, sg32, layout.geometry, self.temperature,
@@ -188,15 +189,20 @@ class PACK3DAttention(nn.Module):
         pairs = balanced_pairs(d)
         extents = tuple(int(e) for e in grid_shape)
         _, phases = phase_tables(dev, pairs, extents)
-        if raster_qkv and (phases is None or self.fused_projection):
-            raise ValueError("raster-ordered q, kl, vl come from p3d_qkv_split with a phase table")
+        if raster_qkv and phases is None:
+            raise ValueError("raster-ordered q, kl, vl need a phase table")
         if phases is not None and self.fused_projection and glue.project_supported(xn, self.to_q.weight,
                                                                                   self.to_kv.weight, h, g, d):
-            # projections, split and RoPE in one kernel: the projections never reach HBM
+            # projections, split and RoPE in one kernel: the projections never reach HBM; the
+            # gate from its own GEMM and p3d_gate_pairs
             coords = coords.to(device=dev, dtype=torch.int64).contiguous()
             q, kl, vl, kg, vg = glue.project_split_raw(xn, self.to_q.weight, self.to_kv.weight, coords, phases, pairs,
-                                                       extents, h, g, d)
-            gate = self.gate(xn).reshape(b, n, h, 2).softmax(-1)[..., 1].transpose(1, 2).contiguous()
+                                                       extents, h, g, d, raster_qkv=raster_qkv)
+            logits = torch.addmm(self.gate.bias, xn.view(b * n, self.dim), self.gate.weight.t())
+            gate = torch.empty((b, h, n), dtype=x.dtype, device=dev)
+            with torch.cuda.device(dev):
+                _native.check(lib.p3d_gate_pairs(_native.ptr(logits), logits.shape[1], _native.ptr(gate), code, b, h,
+                                                 n, stream), "p3d_gate_pairs")
             return x, q, kl, vl, kg, vg, gate
         if phases is not None and h <= 16:
             # one GEMM for to_q, to_kv and gate (weights stacked, gate bias in the epilogue); one

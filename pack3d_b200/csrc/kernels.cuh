@@ -73,6 +73,7 @@ struct ProjArgs {
   int pairs[3], start[3];
   const float *phases;
   int table_floats;             // floats in the phase table
+  int raster_qkv, ey, ex;       // q, kl, vl rows at each token's raster index (ey x ex planes)
 };
 int proj_group_heads(int head_dim, int heads, int kv_heads, int dim, size_t smem_limit);
 size_t proj_smem_bytes(int dim, int group_cols);

@@ -749,6 +749,46 @@ extern "C" int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl,
   return dtype == P3D_BF16 ? launch_split<__nv_bfloat16>(p, head_dim, s) : launch_split<__half>(p, head_dim, s);
 }
 
+// gate[b, h, n] = softmax(logits[b, n, 2h .. 2h + 1])[1] (attention.py:84-86), in fp32 with expf and
+// a division, rounded once; a thread per (head, token) in gate order (coalesced stores), logits
+// read as one 4-byte pair.
+template <typename T>
+__global__ void __launch_bounds__(256) gate_pairs_kernel(const T *logits, int stride, T *gate, int heads,
+                                                         int tokens, int64_t total) {
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < total; k += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t bh = k / tokens, n = k - bh * tokens, b = bh / heads;
+    const int h = (int)(bh - b * heads);
+    const float2 l = unpack2<T>(__ldg(reinterpret_cast<const uint32_t *>(logits + (b * tokens + n) * stride + 2 * h)));
+    const float m = fmaxf(l.x, l.y);
+    const float e0 = expf(l.x - m), e1 = expf(l.y - m);
+    gate[k] = from_f32<T>(e1 / (e0 + e1));
+  }
+}
+
+extern "C" int p3d_gate_pairs(const void *logits, int stride, void *gate, int dtype, int batch, int heads,
+                              int tokens, void *stream) {
+  P3D_CHECK_ARG(dtype == P3D_BF16 || dtype == P3D_F16, "p3d_gate_pairs: bf16 or f16 only");
+  P3D_CHECK_ARG(logits && gate, "p3d_gate_pairs: null pointer");
+  P3D_CHECK_ARG(batch >= 0 && heads >= 1 && tokens >= 0 && stride >= 2 * heads && stride % 2 == 0,
+                "p3d_gate_pairs: bad shape (stride %d for %d heads)", stride, heads);
+  P3D_CHECK_ARG(((uintptr_t)logits & 3) == 0, "p3d_gate_pairs: logits must be 4-byte aligned");
+  const int64_t total = (int64_t)batch * tokens * heads;
+  if (total == 0) return P3D_OK;
+  DeviceInfo info{};
+  if (int st = device_info(&info)) return st;
+  const int64_t want = (total + 255) / 256, cap = (int64_t)info.sm_count * 8;
+  const unsigned blocks = (unsigned)(want < cap ? want : cap);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == P3D_BF16)
+    gate_pairs_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(logits), stride,
+                                                             static_cast<__nv_bfloat16 *>(gate), heads, tokens, total);
+  else
+    gate_pairs_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half *>(logits), stride,
+                                                     static_cast<__half *>(gate), heads, tokens, total);
+  P3D_LAUNCH_CHECK();
+  return P3D_OK;
+}
+
 extern "C" int p3d_qkv_gate_split(const void *proj, int proj_cols, void *q, void *kl, void *vl, void *kg, void *vg,
                                   void *gate, int dtype, int batch, int heads, int kv_heads, int tokens, int head_dim,
                                   const int64_t *coords, int pz, int py, int px, const float *phases, int ez, int ey,

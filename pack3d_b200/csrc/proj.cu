@@ -65,6 +65,7 @@ struct ProjParams {
   int pairs[3], start[3];
   const float *phases;
   int table_floats;    // 2 * (ez pz + ey py + ex px); staged in shared memory when <= kMaxTableFloats
+  int raster_qkv, ey, ex;  // q, kl, vl rows at each token's raster index (c0 ey + c1) ex + c2
 };
 
 // (cos, sin) of rotation pair `pair` of a token at coordinates c, from the table `tab`.
@@ -293,7 +294,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // a select chain, not p.out[1 + part]: a runtime index would move the parameters to local memory
         void *o = is_q ? p.out[0] : part == 0 ? p.out[1] : part == 1 ? p.out[2] : part == 2 ? p.out[3] : p.out[4];
-        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(o) + (((int64_t)b * ht + hh) * p.tokens + n) * D);
+        // q, kl, vl go to the token's raster row in the raster form (kg, vg stay in token order)
+        const int64_t nd = (p.raster_qkv && (is_q || part <= 1)) ? ((int64_t)c3[0] * p.ey + c3[1]) * p.ex + c3[2] : n;
+        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(o) + (((int64_t)b * ht + hh) * p.tokens + nd) * D);
 #pragma unroll
         for (int v = 0; v < D / 8; ++v)
           dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
@@ -356,6 +359,9 @@ int launch_proj(const ProjArgs &a, cudaStream_t stream) {
   }
   p.phases = a.phases;
   p.table_floats = a.table_floats;
+  p.raster_qkv = a.raster_qkv;
+  p.ey = a.ey;
+  p.ex = a.ex;
   const size_t smem = proj_smem_bytes(a.dim, gh * D);
   const bool balanced = p.pairs[0] == Balanced<D>::count(0) && p.pairs[1] == Balanced<D>::count(1) &&
                         p.pairs[2] == Balanced<D>::count(2);
@@ -423,8 +429,12 @@ extern "C" int p3d_qkv_project_supported(int dtype, int dim, int heads, int kv_h
 extern "C" int p3d_qkv_project(const void *x, const void *wq, const void *wkv, void *q, void *kl, void *vl, void *kg,
                                void *vg, int dtype, int batch, int heads, int kv_heads, int tokens, int dim,
                                int head_dim, const int64_t *coords, int pz, int py, int px, const float *phases,
-                               int ez, int ey, int ex, void *stream) {
+                               int ez, int ey, int ex, unsigned flags, void *stream) {
   P3D_CHECK_ARG(x && wq && wkv && q && kl && vl && kg && vg && coords && phases, "p3d_qkv_project: null pointer");
+  P3D_CHECK_ARG((flags & ~P3D_SPLIT_RASTER_QKV) == 0u, "p3d_qkv_project: unknown flags 0x%x", flags);
+  P3D_CHECK_ARG(!(flags & P3D_SPLIT_RASTER_QKV) || (int64_t)ez * ey * ex == tokens,
+                "p3d_qkv_project: raster rows need the coordinate extents to be the token grid (%d x %d x %d != %d)",
+                ez, ey, ex, tokens);
   P3D_CHECK_ARG(batch >= 0 && tokens >= 0 && (int64_t)batch * tokens < (int64_t(1) << 31),
                 "p3d_qkv_project: bad batch / token counts");
   P3D_CHECK_ARG(pz >= 0 && py >= 0 && px >= 0 && 2 * (pz + py + px) == head_dim && ez >= 1 && ey >= 1 && ex >= 1,
@@ -454,6 +464,9 @@ extern "C" int p3d_qkv_project(const void *x, const void *wq, const void *wkv, v
   a.out[2] = vl;
   a.out[3] = kg;
   a.out[4] = vg;
+  a.raster_qkv = (flags & P3D_SPLIT_RASTER_QKV) ? 1 : 0;
+  a.ey = ey;
+  a.ex = ex;
   a.coords = coords;
   a.pairs[0] = pz;
   a.pairs[1] = py;

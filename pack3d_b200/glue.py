@@ -131,8 +131,9 @@ def project_supported(x, wq, wkv, heads, kv_heads, head_dim):
                                                             kv_heads, head_dim))
 
 
-def project_split_raw(x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, head_dim):
-    """``p3d_qkv_project`` on x [B, N, dim] (no autograd): ``(q, kl, vl, kg, vg)``."""
+def project_split_raw(x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, head_dim, raster_qkv=False):
+    """``p3d_qkv_project`` on x [B, N, dim] (no autograd): ``(q, kl, vl, kg, vg)``; ``raster_qkv``
+    stores q, kl, vl at each token's raster row."""
     b, n, dim = x.shape
     x = x.contiguous()
     dev, dt = x.device, x.dtype
@@ -142,7 +143,8 @@ def project_split_raw(x, wq, wkv, coords, phases, pairs, extents, heads, kv_head
         _native.check(_native.lib().p3d_qkv_project(
             _native.ptr(x), _native.ptr(wq), _native.ptr(wkv), _native.ptr(q), _native.ptr(kl), _native.ptr(vl),
             _native.ptr(kg), _native.ptr(vg), _native.DTYPE_CODE[dt], b, heads, kv_heads, n, dim, head_dim,
-            _native.ptr(coords), *pairs, _native.ptr(phases), *extents, _native.stream_of(dev)), "p3d_qkv_project")
+            _native.ptr(coords), *pairs, _native.ptr(phases), *extents,
+            _native.SPLIT_RASTER_QKV if raster_qkv else 0, _native.stream_of(dev)), "p3d_qkv_project")
     return q, kl, vl, kg, vg
 
 

@@ -254,3 +254,21 @@ def test_fused_training_glue_matches_the_per_op_path(cuda_device):
     for k in g1:
         assert (g0[k].float() - g1[k].float()).abs().max().item() <= tol(g1[k]), k
     assert _native.device_errors() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gate_pairs_is_the_torch_gate(cuda_device, dtype):
+    """p3d_gate_pairs: softmax over each head's logit pair, second entry, [B, H, N], from logits
+    with a row stride wider than the pairs."""
+    b, n, h, stride = 2, 777, 5, 16
+    gen = torch.Generator(device=cuda_device).manual_seed(5)
+    logits = (torch.randn(b * n, stride, device=cuda_device, generator=gen) * 3).to(dtype)
+    gate = torch.empty((b, h, n), dtype=dtype, device=cuda_device)
+    with torch.cuda.device(cuda_device):
+        _native.check(_native.lib().p3d_gate_pairs(_native.ptr(logits), stride, _native.ptr(gate),
+                                                   _native.DTYPE_CODE[dtype], b, h, n, _native.stream_of(cuda_device)),
+                      "p3d_gate_pairs")
+    want = logits[:, :2 * h].reshape(b, n, h, 2).softmax(-1)[..., 1].transpose(1, 2)
+    step = 2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11
+    assert (gate.float() - want.float()).abs().max().item() <= step
+    assert (gate != want).float().mean().item() < 1e-3

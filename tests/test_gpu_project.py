@@ -55,7 +55,7 @@ def test_project_matches_gemm_then_split(cuda_device, case):
     with torch.cuda.device(cuda_device):
         _native.check(lib.p3d_qkv_project(
             _native.ptr(x), _native.ptr(wq), _native.ptr(wkv), *[_native.ptr(t) for t in got], code, b, h, g, n, dim,
-            d, _native.ptr(coords), *pairs, _native.ptr(phases), *extents, _native.stream_of(cuda_device)),
+            d, _native.ptr(coords), *pairs, _native.ptr(phases), *extents, 0, _native.stream_of(cuda_device)),
             "p3d_qkv_project")
     torch.cuda.synchronize()
     assert _native.device_errors() == 0

@@ -40,7 +40,7 @@ def test_library_exports_every_declared_symbol():
 def test_library_metadata_calls():
     from pack3d_b200 import _native
     handle = _native.lib()
-    assert handle.p3d_abi_version() == 2
+    assert handle.p3d_abi_version() == 3
     assert handle.p3d_strerror(0) == b"success"
     assert handle.p3d_strerror(4).startswith(b"workspace")
     assert handle.p3d_device_count() >= 0
@@ -108,10 +108,10 @@ def test_argument_checks_run_before_any_device_call():
     dummy = 16  # a non-null, 16-byte aligned stand-in: never dereferenced on these paths
     # p3d_qkv_project: null pointer, bad rotation pairs
     st = lib.p3d_qkv_project(None, dummy, dummy, dummy, dummy, dummy, dummy, dummy, _native.BF16, 1, 4, 4, 64, 192,
-                             48, dummy, 8, 8, 8, dummy, 4, 4, 4, None)
+                             48, dummy, 8, 8, 8, dummy, 4, 4, 4, 0, None)
     assert st == 1 and b"null pointer" in lib.p3d_last_error()
     st = lib.p3d_qkv_project(dummy, dummy, dummy, dummy, dummy, dummy, dummy, dummy, _native.BF16, 1, 4, 4, 64, 192,
-                             48, dummy, 8, 8, 7, dummy, 4, 4, 4, None)
+                             48, dummy, 8, 8, 7, dummy, 4, 4, 4, 0, None)
     assert st == 1 and b"pairs" in lib.p3d_last_error()
     # shapes the fused kernel does not run are reported as unsupported, not computed
     assert lib.p3d_qkv_project_supported(_native.F32, 192, 4, 4, 48) == 0
