@@ -49,6 +49,9 @@ def parse_args():
     ap.add_argument("--fwd-bwd-steps", type=int, default=3, help="timed fwd+bwd steps (0 disables)")
     ap.add_argument("--backward-only", type=int, default=0, metavar="N",
                     help="profiling mode: run the operator backward N times on config-3 inputs and exit")
+    ap.add_argument("--rope-only", type=int, default=0, metavar="N",
+                    help="profiling mode: time N iterations of the standalone rotation (p3d_rope) of q, kl, kg "
+                         "views at config-1 shapes and exit")
     ap.add_argument("--config4", type=int, default=0, metavar="K",
                     help="separate mode: BASELINE config 4 (128^3 field, dim 384 = 8 heads x 48) layer forward + "
                          "backward, K timed steps, on the launch's N GPUs (z-slabs for N > 1); one JSON line")
@@ -362,6 +365,28 @@ def allen15_measure(steps, warmup, device):
             "tokens": n, "summaries": layout.geometry.num_summaries, "eager": True, "steps": steps}
 
 
+def rope_only(args, device):
+    """Profiling mode: ``rotate_projections`` (three ``p3d_rope`` calls) on strided views of the
+    config-1 projection rows, as the per-op layer path calls it."""
+    from pack3d_b200.rope import balanced_pairs, rotate_projections
+    layout = make_layout(CONFIG["grid"]).to(device)
+    n, h, d = layout.geometry.num_tokens, CONFIG["heads"], CONFIG["head_dim"]
+    gen = torch.Generator(device=device).manual_seed(4)
+    qp = torch.randn(1, n, h * d, device=device, generator=gen).to(torch.bfloat16)
+    kvp = torch.randn(1, n, 4 * h * d, device=device, generator=gen).to(torch.bfloat16)
+    q = qp.reshape(1, n, h, d).transpose(1, 2)
+    kl, _, kg, _ = (t.reshape(1, n, h, d).transpose(1, 2) for t in kvp.chunk(4, -1))
+    pairs = balanced_pairs(d)
+
+    def step():
+        with torch.no_grad():
+            rotate_projections(q, kl, kg, layout.coords, pairs, layout.grid_shape, packed=False)
+    for _ in range(max(args.warmup, 1)):
+        step()
+    times = timed_steps(step, args.rope_only, torch.cuda.current_stream(device))
+    print(json.dumps({"rope_three_calls_ms": [round(t, 4) for t in times]}), flush=True)
+
+
 def infer_only(args, device):
     """Profiling mode: the config-1 layer inference forward alone (eager calls)."""
     from pack3d_b200 import _native
@@ -654,6 +679,8 @@ def run_b200(args, rank, world, device):
         return backward_only(args, device)
     if args.train_only:
         return train_only(args, device)
+    if args.rope_only:
+        return rope_only(args, device)
     if args.infer_only:
         return infer_only(args, device)
     if args.allen15:

@@ -31,47 +31,34 @@ struct RopeParams {
   int packed, inverse;
 };
 
-template <typename T, bool kVector>
+template <typename T, bool kVector, typename Index>
 __global__ void __launch_bounds__(256) rope_kernel(RopeParams p) {
   const int half = p.head_dim / 2;
   const int groups = (half + kPairsPerThread - 1) / kPairsPerThread;
-  const int64_t total = (int64_t)p.batch * p.tokens * p.heads * groups;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
-    // Thread order (group, head, token, batch): consecutive threads walk one token's
-    // projection row (all heads), which is contiguous in the [B, N, H*D] projection.
-    const int grp = (int)(t % groups);
-    int64_t rest = t / groups;
-    const int h = (int)(rest % p.heads);
-    rest /= p.heads;
-    const int n = (int)(rest % p.tokens);
-    const int b = (int)(rest / p.tokens);
-    const T *src = static_cast<const T *>(p.x) + b * p.sb + h * p.sh + n * p.sn;
-    T *dst = static_cast<T *>(p.out) + (((int64_t)b * p.heads + h) * p.tokens + n) * p.head_dim;
-    float vals[2 * kPairsPerThread];
+  const Index total = (Index)p.batch * p.tokens * groups;
+  const Index stride = (Index)gridDim.x * blockDim.x;
+  for (Index t = (Index)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
+    // A thread owns one group of kPairsPerThread pairs of one token and walks all its heads:
+    // the token's coordinates and the group's (cos, sin) are fetched once and reused for
+    // every head row.  Consecutive threads take consecutive groups of one token, so each
+    // head row's channels are read and written as contiguous runs.  Index is 32-bit whenever
+    // the thread count allows: the divisions are the costliest arithmetic here.
+    const Index bn = t / groups;
+    const int grp = (int)(t - bn * groups);
+    const int b = (int)(bn / p.tokens), n = (int)(bn - (Index)b * p.tokens);
     const int pair0 = grp * kPairsPerThread;
     const int npairs = min(kPairsPerThread, half - pair0);
-    if (kVector && npairs == kPairsPerThread) {
-      // 8 contiguous, 8-element-aligned channels (checked on the host).
-      if constexpr (sizeof(T) == 2) {
-        const uint4 raw = *reinterpret_cast<const uint4 *>(src + 2 * pair0);
-        const T *e = reinterpret_cast<const T *>(&raw);
+    // the token's coordinates (the packed encoding uses the row index on axis 0)
+    int64_t coord3[3] = {n, 0, 0};
+    if (!p.packed)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) vals[i] = to_f32<T>(e[i]);
-      } else {
-        const float4 a = *reinterpret_cast<const float4 *>(src + 2 * pair0);
-        const float4 c = *reinterpret_cast<const float4 *>(src + 2 * pair0 + 4);
-        vals[0] = a.x; vals[1] = a.y; vals[2] = a.z; vals[3] = a.w;
-        vals[4] = c.x; vals[5] = c.y; vals[6] = c.z; vals[7] = c.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 2 * kPairsPerThread; ++i)
-        vals[i] = (i < 2 * npairs) ? to_f32<T>(src[(int64_t)(2 * pair0 + i) * p.sd]) : 0.f;
-    }
+      for (int a = 0; a < 3; ++a) coord3[a] = p.coords[n * p.csn + a * p.csa];
+    float cs[kPairsPerThread], sn[kPairsPerThread];
 #pragma unroll
     for (int j = 0; j < kPairsPerThread; ++j) {
-      if (j >= npairs) break;
+      cs[j] = 1.f;
+      sn[j] = 0.f;
+      if (j >= npairs) continue;
       const int pair = pair0 + j;
       int axis, local, start;
       if (pair < p.pairs[0]) {
@@ -82,33 +69,56 @@ __global__ void __launch_bounds__(256) rope_kernel(RopeParams p) {
         axis = 2; local = pair - p.pairs[0] - p.pairs[1];
         start = p.extent[0] * p.pairs[0] + p.extent[1] * p.pairs[1];
       }
-      const int64_t coord = p.packed ? (int64_t)n : p.coords[n * p.csn + axis * p.csa];
-      float c, s;
+      const int64_t coord = axis == 0 ? coord3[0] : axis == 1 ? coord3[1] : coord3[2];
       if (p.phases != nullptr) {
-        const int64_t entry = start + coord * p.pairs[axis] + local;
-        c = p.phases[2 * entry];
-        s = p.phases[2 * entry + 1];
+        const float2 e = *reinterpret_cast<const float2 *>(p.phases + 2 * (start + coord * p.pairs[axis] + local));
+        cs[j] = e.x;
+        sn[j] = e.y;
       } else {
         const float angle = __fmul_rn((float)coord, p.freqs[pair]);
-        sincosf(angle, &s, &c);
+        sincosf(angle, &sn[j], &cs[j]);
       }
-      if (p.inverse) s = -s;
-      const float even = vals[2 * j], odd = vals[2 * j + 1];
-      // (even*c - odd*s, even*s + odd*c) with each product rounded: no FMA contraction.
-      vals[2 * j] = __fsub_rn(__fmul_rn(even, c), __fmul_rn(odd, s));
-      vals[2 * j + 1] = __fadd_rn(__fmul_rn(even, s), __fmul_rn(odd, c));
+      if (p.inverse) sn[j] = -sn[j];
     }
-    if (npairs == kPairsPerThread && sizeof(T) == 2) {
-      uint4 raw;
-      T *e = reinterpret_cast<T *>(&raw);
+    for (int h = 0; h < p.heads; ++h) {
+      const T *src = static_cast<const T *>(p.x) + b * p.sb + h * p.sh + n * p.sn;
+      T *dst = static_cast<T *>(p.out) + (((int64_t)b * p.heads + h) * p.tokens + n) * p.head_dim;
+      float vals[2 * kPairsPerThread];
+      if (kVector && npairs == kPairsPerThread) {
+        // 8 contiguous, 8-element-aligned channels (checked on the host).
+        if constexpr (sizeof(T) == 2) {
+          const uint4 raw = *reinterpret_cast<const uint4 *>(src + 2 * pair0);
+          const T *e = reinterpret_cast<const T *>(&raw);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) e[i] = from_f32<T>(vals[i]);
-      if (((uintptr_t)(dst + 2 * pair0) & 15) == 0) {
+          for (int i = 0; i < 8; ++i) vals[i] = to_f32<T>(e[i]);
+        } else {
+          const float4 a = *reinterpret_cast<const float4 *>(src + 2 * pair0);
+          const float4 c = *reinterpret_cast<const float4 *>(src + 2 * pair0 + 4);
+          vals[0] = a.x; vals[1] = a.y; vals[2] = a.z; vals[3] = a.w;
+          vals[4] = c.x; vals[5] = c.y; vals[6] = c.z; vals[7] = c.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 2 * kPairsPerThread; ++i)
+          vals[i] = (i < 2 * npairs) ? to_f32<T>(src[(int64_t)(2 * pair0 + i) * p.sd]) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < kPairsPerThread; ++j) {
+        const float even = vals[2 * j], odd = vals[2 * j + 1];
+        // (even*c - odd*s, even*s + odd*c) with each product rounded: no FMA contraction.
+        vals[2 * j] = __fsub_rn(__fmul_rn(even, cs[j]), __fmul_rn(odd, sn[j]));
+        vals[2 * j + 1] = __fadd_rn(__fmul_rn(even, sn[j]), __fmul_rn(odd, cs[j]));
+      }
+      if (npairs == kPairsPerThread && sizeof(T) == 2 && ((uintptr_t)(dst + 2 * pair0) & 15) == 0) {
+        uint4 raw;
+        T *e = reinterpret_cast<T *>(&raw);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) e[i] = from_f32<T>(vals[i]);
         *reinterpret_cast<uint4 *>(dst + 2 * pair0) = raw;
-        continue;
+      } else {
+        for (int i = 0; i < 2 * npairs; ++i) dst[2 * pair0 + i] = from_f32<T>(vals[i]);
       }
     }
-    for (int i = 0; i < 2 * npairs; ++i) dst[2 * pair0 + i] = from_f32<T>(vals[i]);
   }
 }
 
@@ -116,16 +126,20 @@ template <typename T>
 int launch_rope(const RopeParams &p, bool vector, cudaStream_t stream) {
   const int half = p.head_dim / 2;
   const int groups = (half + kPairsPerThread - 1) / kPairsPerThread;
-  const int64_t total = (int64_t)p.batch * p.tokens * p.heads * groups;
+  const int64_t total = (int64_t)p.batch * p.tokens * groups;
   DeviceInfo info;
   if (int st = device_info(&info)) return st;
   const int64_t want = (total + 255) / 256;
   const int blocks = (int)std::min<int64_t>(want, (int64_t)info.sm_count * 16);
   if (blocks == 0) return P3D_OK;
+  // 32-bit index arithmetic while the last thread index (plus one grid stride) fits
+  const bool narrow = total + (int64_t)blocks * 256 < (int64_t(1) << 31);
   if (vector)
-    rope_kernel<T, true><<<blocks, 256, 0, stream>>>(p);
+    narrow ? rope_kernel<T, true, uint32_t><<<blocks, 256, 0, stream>>>(p)
+           : rope_kernel<T, true, uint64_t><<<blocks, 256, 0, stream>>>(p);
   else
-    rope_kernel<T, false><<<blocks, 256, 0, stream>>>(p);
+    narrow ? rope_kernel<T, false, uint32_t><<<blocks, 256, 0, stream>>>(p)
+           : rope_kernel<T, false, uint64_t><<<blocks, 256, 0, stream>>>(p);
   P3D_LAUNCH_CHECK();
   return P3D_OK;
 }
