@@ -573,7 +573,7 @@ def run_sharded(args, rank, world, device):
     torch.cuda.synchronize(device)
     run, graph = step, None
     if not args.no_graph:
-        # the whole rank step (its NCCL point-to-point batch included) as one CUDA graph
+        # the whole rank step (its peer exchange included) as one CUDA graph
         side = torch.cuda.Stream(device)
         side.wait_stream(stream)
         with torch.cuda.stream(side):
@@ -651,9 +651,9 @@ def run_sharded(args, rank, world, device):
                                "summaries) split into z-slabs, one per GPU; layer forward",
                    "grid": list(grid), "batch": b, "heads": hq, "kv_heads": g, "head_dim": hd, "dim": dim,
                    "summaries": m, "radius": CONFIG["radius"],
-                   "parallelism": f"{world} z-slabs of {slabs.planes} planes; one batch of NCCL point-to-point "
-                                  "operations per layer: halo exchange (2 planes of kl, vl each way) + summary "
-                                  "all-gather",
+                   "parallelism": f"{world} z-slabs of {slabs.planes} planes; peer-memory exchange per layer "
+                                  "(p3d_peer_push over NVLink: 2 halo planes of kl, vl to each neighbour, the "
+                                  "rank's summaries to every rank; bounded counter waits), no NCCL in the step",
                    "cuda_graph": used_graph,
                    "l2": "flushed between timed steps (256 MiB write outside the timed events)"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
@@ -666,7 +666,9 @@ def run_sharded(args, rank, world, device):
                 "d2h_bytes_per_step": x_host.numel() * x_host.element_size() * world,   # y: x's shape and dtype
                 "pipelined": "copy-in, compute and copy-out on three streams per rank; double-buffered, every "
                              "step copies its own input in and result out inside the timed region"},
-        "gpu_launches": 5 * args.steps,
+        # per step: layer norm, fused projection, gate pairs, pooling, credit wait, push,
+        # arrival wait, summary bound, slab forward, credit signal
+        "gpu_launches": 10 * args.steps,
         "clocks": clock_summary,
     }
 
@@ -914,6 +916,8 @@ def main():
                                 "cpu": cpu_model(), "kind": "port", "sample": CPU_SAMPLE + ", timed once",
                                 "measured_wall_s": round(cpu_s, 2)}
     if world > 1:
+        from pack3d_b200.sharded import release_peers
+        release_peers()   # the peer-exchange regions go before the process group
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     if rank == 0:

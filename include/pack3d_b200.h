@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define P3D_ABI_VERSION 3
+#define P3D_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define P3D_API __attribute__((visibility("default")))
@@ -71,7 +71,8 @@ P3D_API int p3d_device_count(void);
 /* Read and clear the device-side failure flags of the current device.  Bit 0: a
  * bounded wait inside a tensor-core kernel timed out and the kernel unwound; bits
  * 1-4 name the waiting role (2 TMA producer, 4 MMA issuer, 8 softmax / epilogue,
- * 16 a drain before tensor memory is freed).  Synchronises with the device.  No
+ * 16 a drain before tensor memory is freed); bit 5 (32): a peer-exchange wait
+ * (p3d_peer_wait) ran out.  Synchronises with the device.  No
  * reference counterpart (the Triton kernels have no device-side waits). */
 P3D_API int p3d_device_errors(unsigned *flags);
 
@@ -270,6 +271,11 @@ typedef struct {
    * the global softmax takes its exponentials against the per-row score bound instead of a
    * running maximum (the faster form); p3d_attn_fwd_slab reads it, the backward does not. */
   const float *summary_bound;
+  /* p3d_attn_fwd_slab only: run the 4-plane query tiles [tile_z_begin, tile_z_end) of this
+   * rank's planes (tile_z_end 0: up to the last tile; 0, 0: all of them).  A caller overlapping the halo exchange runs the tiles
+   * whose neighbourhood lies in its own planes first and the others once the halo planes of
+   * op->kl / op->vl have arrived; op->kl / op->vl must hold every plane the tiles run read. */
+  int32_t tile_z_begin, tile_z_end;
 } p3d_slab;
 
 /*
@@ -316,6 +322,47 @@ P3D_API int p3d_pool_bwd(const void *k, const void *v, const float *weight, cons
                  float temperature, void *workspace, size_t workspace_bytes, void *stream);
 P3D_API size_t p3d_pool_bwd_workspace(int fine_blocks, int slots, int pool_size, int batch, int kv_heads,
                               int head_dim);
+
+/*
+ * Peer-memory exchange of the z-slab sharding (one process per GPU on one node).  No
+ * counterpart in the reference, which runs on one GPU.  Each rank allocates one region
+ * (p3d_peer_alloc: device memory, zeroed, with its 64-byte CUDA IPC handle) and maps the
+ * other ranks' regions from their handles (p3d_peer_open: NVLink peer memory, valid on the
+ * calling process's device).  Per layer call a rank waits for its peers' credits
+ * (p3d_peer_wait), pushes its rows into the peers' regions (p3d_peer_push), waits for the
+ * peers' pushes (p3d_peer_wait), runs its kernels on its own region and then raises every
+ * peer's credit (p3d_peer_signal).  Counters are 64-bit, only grow, and live in the regions;
+ * the expected values live in device memory and advance on the device, so a CUDA graph
+ * captured over a call replays correctly.
+ */
+#define P3D_PEER_HANDLE_BYTES 64
+#define P3D_PEER_MAX_COPIES 32
+#define P3D_PEER_MAX_TARGETS 16
+typedef struct {
+  const void *src;   /* this process's memory */
+  void *dst;         /* a peer's mapped region, or this process's memory */
+  int64_t rows;      /* rows of row_bytes bytes (a multiple of 16) */
+  int64_t row_bytes;
+  int64_t src_stride, dst_stride;  /* bytes between rows (multiples of 16; 16-byte aligned pointers) */
+} p3d_peer_copy;
+P3D_API int p3d_peer_alloc(size_t bytes, void **ptr, void *handle);
+P3D_API int p3d_peer_free(void *ptr);
+P3D_API int p3d_peer_open(const void *handle, void **ptr);
+P3D_API int p3d_peer_close(void *ptr);
+/* copies[0, n_remote) are written first; then each of the ctas CTAs adds one to every
+ * arrive[i] (release, system scope) after its part of them; then copies[n_remote,
+ * n_copies) (rows that no peer waits for).  A consumer of the remote rows waits for
+ * ctas arrivals per pusher. */
+P3D_API int p3d_peer_push(const p3d_peer_copy *copies, int n_copies, int n_remote, uint64_t *const *arrive,
+                  int n_arrive, int ctas, void *stream);
+/* One device thread: wait until *counter >= *expected (acquire, system scope), for at most
+ * timeout_s seconds, then *expected += step.  A wait that runs out sets bits 1 | 32 of
+ * p3d_device_errors and returns. */
+P3D_API int p3d_peer_wait(const uint64_t *counter, uint64_t *expected, uint64_t step, double timeout_s,
+                  void *stream);
+/* One device thread, after the stream's earlier work: add one to each counter (release,
+ * system scope). */
+P3D_API int p3d_peer_signal(uint64_t *const *counters, int n, void *stream);
 
 /*
  * Forward (inference, no saved state) that allocates nothing and needs no workspace.

@@ -50,8 +50,20 @@ class Slab(ctypes.Structure):
     """Mirror of ``p3d_slab`` in ``include/pack3d_b200.h``."""
 
     _fields_ = [("global_planes", ctypes.c_int32), ("center_z0", ctypes.c_int32), ("halo_z0", ctypes.c_int32),
-                ("halo_planes", ctypes.c_int32), ("summaries", ctypes.c_int32), ("summary_bound", _vp)]
+                ("halo_planes", ctypes.c_int32), ("summaries", ctypes.c_int32), ("summary_bound", _vp),
+                ("tile_z_begin", ctypes.c_int32), ("tile_z_end", ctypes.c_int32)]
 
+
+class PeerCopy(ctypes.Structure):
+    """Mirror of ``p3d_peer_copy`` in ``include/pack3d_b200.h``."""
+
+    _fields_ = [("src", _vp), ("dst", _vp), ("rows", ctypes.c_int64), ("row_bytes", ctypes.c_int64),
+                ("src_stride", ctypes.c_int64), ("dst_stride", ctypes.c_int64)]
+
+
+PEER_HANDLE_BYTES = 64
+PEER_MAX_COPIES = 32
+PEER_MAX_TARGETS = 16
 
 _SIGNATURES = {
     "p3d_strerror": (ctypes.c_char_p, [_c_int]),
@@ -93,6 +105,13 @@ _SIGNATURES = {
     "p3d_attn_bwd": (_c_int, [ctypes.POINTER(Operator), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                               _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "p3d_attn_bwd_workspace": (ctypes.c_size_t, [ctypes.POINTER(Operator)]),
+    "p3d_peer_alloc": (_c_int, [ctypes.c_size_t, ctypes.POINTER(_vp), _vp]),
+    "p3d_peer_free": (_c_int, [_vp]),
+    "p3d_peer_open": (_c_int, [_vp, ctypes.POINTER(_vp)]),
+    "p3d_peer_close": (_c_int, [_vp]),
+    "p3d_peer_push": (_c_int, [ctypes.POINTER(PeerCopy), _c_int, _c_int, ctypes.POINTER(_vp), _c_int, _c_int, _vp]),
+    "p3d_peer_wait": (_c_int, [_vp, _vp, ctypes.c_uint64, ctypes.c_double, _vp]),
+    "p3d_peer_signal": (_c_int, [ctypes.POINTER(_vp), _c_int, _vp]),
     "p3d_bwd_mix": (_c_int, [ctypes.POINTER(Operator)] + [_vp] * 10 + [_vp, ctypes.c_size_t, _vp]),
     "p3d_bwd_mix_workspace": (ctypes.c_size_t, [ctypes.POINTER(Operator)]),
     "p3d_bwd_attn_slab": (_c_int, [ctypes.POINTER(Operator), ctypes.POINTER(Slab)] + [_vp] * 17 +

@@ -336,6 +336,7 @@ int p3d_device_errors(unsigned *flags) {
   *flags = 0;
   if (int st = take_fwd_errors(flags)) return st;
   if (int st = take_proj_errors(flags)) return st;
+  if (int st = take_peer_errors(flags)) return st;
   return take_bwd_errors(flags);
 }
 
@@ -511,6 +512,11 @@ int p3d_attn_fwd_slab(const p3d_operator *op, const p3d_slab *slab, void *y, con
   a.lse_g = save ? lse_g : nullptr;
   a.y_rows = (flags & P3D_FWD_Y_ROWS) != 0;
   a.summary_bound = slab->summary_bound;
+  P3D_CHECK_ARG(slab->tile_z_begin >= 0 && slab->tile_z_end >= 0 &&
+                    (slab->tile_z_end == 0 || slab->tile_z_begin < slab->tile_z_end),
+                "p3d_attn_fwd_slab: bad tile range [%d, %d)", slab->tile_z_begin, slab->tile_z_end);
+  a.tile_z_begin = slab->tile_z_begin;
+  a.tile_z_end = slab->tile_z_end;
   return launch_stencil_fwd(a, static_cast<cudaStream_t>(stream));
 }
 

@@ -79,6 +79,7 @@ int proj_group_heads(int head_dim, int heads, int kv_heads, int dim, size_t smem
 size_t proj_smem_bytes(int dim, int group_cols);
 int launch_proj_split(const ProjArgs &a, cudaStream_t stream);
 int take_proj_errors(unsigned *flags);
+int take_peer_errors(unsigned *flags);  // peer.cu
 
 struct MixBwdArgs {
   int dtype, gate_dtype, bh, tokens, head_dim, chunk_rows;
@@ -134,6 +135,7 @@ struct StencilFwdArgs {
   int y_rows;                         // y token-major [B,N,H,D]
   int radius;                         // stencil radius (1 or 2, all axes)
   const float *summary_bound;         // [B*G] max_j |sk_j| (launch_summary_bound), or NULL
+  int tile_z_begin, tile_z_end;       // 4-plane query tiles [begin, end) of the buffer; 0, 0: all
 };
 // bound[bg] = max over the summaries j of |sk[bg, j, :]| (fp32 Euclidean norm, rounded up by
 // 2^-10), sk [BG, M, D] in a 16-bit dtype: the stencil forward's per-row bound on the global

@@ -118,7 +118,8 @@ enum Bar {
 };
 
 struct FwdParams {
-  int Z, Y, X, tiles_z, tiles_y, tiles_x;  // Z: planes of the query (centre) buffer
+  int Z, Y, X, tiles_z, tiles_y, tiles_x;  // Z: planes of the query (centre) buffer; tiles_z: of the range run
+  int tz0;                                 // first 4-plane query tile of the range
   int Zg, qz0, kz0;  // global planes; global z of query-buffer plane 0 and of K/V-buffer plane 0
   int heads, kv_heads, summaries, global_chunks;
   int64_t tokens;
@@ -335,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   unit /= p.tiles_x;
   const int ty = unit % p.tiles_y;
   unit /= p.tiles_y;
-  const int tz = unit % p.tiles_z;
+  const int tz = p.tz0 + unit % p.tiles_z;
   const int bh = unit / p.tiles_z;
   const int x0 = tx * kTX, y0 = ty * kTY, z0 = tz * kTZ;
   const int b = bh / p.heads, h = bh % p.heads;
@@ -737,7 +738,11 @@ int launch_t(const StencilFwdArgs &a, cudaStream_t stream) {
   p.kz0 = a.k_z0;
   p.Y = Y;
   p.X = X;
-  p.tiles_z = (Z + kTZ - 1) / kTZ;
+  const int all_z = (Z + kTZ - 1) / kTZ;
+  const int tz_end = a.tile_z_end > 0 ? std::min(a.tile_z_end, all_z) : all_z;
+  p.tz0 = std::max(0, a.tile_z_begin);
+  p.tiles_z = tz_end - p.tz0;
+  if (p.tiles_z <= 0) return P3D_OK;  // an empty tile range
   p.tiles_y = (Y + kTY - 1) / kTY;
   p.tiles_x = (X + kTX - 1) / kTX;
   p.heads = a.heads;

@@ -238,6 +238,81 @@ def pool_summaries(kg, vg, weight, bias, geometry, temperature=1.0):
     return sk, sv
 
 
+def _summary_bound(sk, device):
+    """Per-(batch, kv-head) bound of the gathered summaries' norms (``p3d_summary_bound``): the
+    forward's fixed-reference global softmax takes its exponentials against a score bound per
+    query row instead of a running maximum."""
+    b, g, m, d = sk.shape
+    bound = torch.empty(b * g, dtype=torch.float32, device=device)
+    with torch.cuda.device(device):
+        _native.check(_native.lib().p3d_summary_bound(_native.ptr(sk), _native.DTYPE_CODE[sk.dtype], b, g, m, d,
+                                                      _native.ptr(bound), _native.stream_of(device)),
+                      "p3d_summary_bound")
+    return bound
+
+
+TILE_PLANES = 4   # planes of one query tile of p3d_attn_fwd_slab (4 x 4 x 8 = 128 rows)
+
+
+def interior_tiles(slabs: ZSlabs):
+    """The query tiles of this rank whose keys and values lie in its own planes or outside
+    the volume -- none in a halo plane: ``(begin, end)``, empty when ``begin >= end``.  Tile t
+    covers planes ``[4t, 4t + 4)`` of the rank and reads ``radius`` planes more on each side."""
+    tiles = -(-slabs.planes // TILE_PLANES)
+    reach = -(-slabs.radius // TILE_PLANES)
+    return (reach if slabs.halo_lo else 0), tiles - (reach if slabs.halo_hi else 0)
+
+
+class _SlabCall:
+    """One rank's ``p3d_attn_fwd_slab`` set up once and launched over ranges of its 4-plane
+    query tiles (the pointers of ``kl_ext`` / ``vl_ext`` are fixed here; a range may run only
+    once every plane its tiles read has been written)."""
+
+    def __init__(self, q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, geometry, slabs, temperature,
+                 save_state, y_rows):
+        b, h, n, d = q.shape
+        if n != slabs.tokens or kl_ext.shape[2] != slabs.halo_planes * slabs.plane_tokens:
+            raise ValueError("q / kl rows do not match the slab")
+        self.device = q.device
+        self.gate = _as_gate(gate, q).contiguous()
+        self.f32 = tuple(_f32(t) for t in (weight, bias, sl, sg))
+        self.op, self.keep = _operator(q, kl_ext, vl_ext, kl_ext, vl_ext, *self.f32[:2], self.gate, *self.f32[2:],
+                                       geometry, temperature)
+        if geometry.stencil is None or self.op.raster_to_packed:
+            raise ValueError("slab forward needs the complete stencil of a raster-stored slab")
+        self.sk, self.sv = sk, sv
+        self.bound = _summary_bound(sk, q.device)
+        self.slabs = slabs
+        self.tiles_z = -(-slabs.planes // TILE_PLANES)
+        if y_rows:
+            self.y = torch.empty((b, n, h, d), dtype=q.dtype, device=q.device).transpose(1, 2)
+        else:
+            self.y = torch.empty_like(q)
+        self.state = (None,) * 4
+        self.flags = _native.FWD_Y_ROWS if y_rows else 0
+        if save_state:
+            ol, og = torch.empty_like(q), torch.empty_like(q)
+            lse_l = torch.empty((b, h, n), dtype=torch.float32, device=q.device)
+            self.state = (ol, og, lse_l, torch.empty_like(lse_l))
+            self.flags |= _native.FWD_SAVE_STATE
+
+    def run(self, tile_z_begin=0, tile_z_end=0):
+        """Launch the query tiles ``[tile_z_begin, tile_z_end)`` (0, 0: all of them)."""
+        slabs = self.slabs
+        slab = _native.Slab(slabs.grid[0], slabs.z0, slabs.halo_z0, slabs.halo_planes, self.sk.shape[2],
+                            ctypes.c_void_p(self.bound.data_ptr()), tile_z_begin, tile_z_end)
+        with torch.cuda.device(self.device):
+            status = _native.lib().p3d_attn_fwd_slab(self.op, ctypes.byref(slab), _native.ptr(self.y),
+                                                     _native.ptr(self.sk), _native.ptr(self.sv),
+                                                     *[_native.ptr(t) for t in self.state], self.flags,
+                                                     _native.stream_of(self.device))
+        _native.check(status, "p3d_attn_fwd_slab")
+
+    def result(self):
+        ol, og, lse_l, lse_g = self.state
+        return self.y, ((self.sk, self.sv, ol, og, lse_l, lse_g) if self.flags & _native.FWD_SAVE_STATE else ())
+
+
 def slab_forward(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, geometry, slabs: ZSlabs, temperature=1.0,
                  save_state=False, y_rows=False):
     """``p3d_attn_fwd_slab`` on one rank: returns ``(y, state)``.
@@ -246,52 +321,220 @@ def slab_forward(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, geometry
     gathered summaries of all ranks.  With ``y_rows`` y is stored token-major ([B, N, H, D];
     the returned [B, H, N, D] tensor is a view of it).
     """
-    b, h, n, d = q.shape
-    if n != slabs.tokens or kl_ext.shape[2] != slabs.halo_planes * slabs.plane_tokens:
-        raise ValueError("q / kl rows do not match the slab")
-    gate = _as_gate(gate, q).contiguous()
-    w32, b32, sl32, sg32 = (_f32(t) for t in (weight, bias, sl, sg))
-    op, keep = _operator(q, kl_ext, vl_ext, kl_ext, vl_ext, w32, b32, gate, sl32, sg32, geometry, temperature)
-    if geometry.stencil is None or op.raster_to_packed:
-        raise ValueError("slab forward needs the complete stencil of a raster-stored slab")
-    # per-(batch, kv-head) bound of the gathered summaries' norms: the forward's fixed-reference
-    # global softmax (a score bound per query row, no running maximum)
-    g = sk.shape[1]
-    bound = torch.empty(b * g, dtype=torch.float32, device=q.device)
-    with torch.cuda.device(q.device):
-        _native.check(_native.lib().p3d_summary_bound(_native.ptr(sk), _native.DTYPE_CODE[sk.dtype], b, g, sk.shape[2],
-                                                      d, _native.ptr(bound), _native.stream_of(q.device)),
-                      "p3d_summary_bound")
-    slab = _native.Slab(slabs.grid[0], slabs.z0, slabs.halo_z0, slabs.halo_planes, sk.shape[2],
-                        ctypes.c_void_p(bound.data_ptr()))
-    if y_rows:
-        y = torch.empty((b, n, h, d), dtype=q.dtype, device=q.device).transpose(1, 2)
-    else:
-        y = torch.empty_like(q)
-    ol = og = lse_l = lse_g = None
-    flags = _native.FWD_Y_ROWS if y_rows else 0
-    if save_state:
-        ol, og = torch.empty_like(q), torch.empty_like(q)
-        lse_l = torch.empty((b, h, n), dtype=torch.float32, device=q.device)
-        lse_g = torch.empty_like(lse_l)
-        flags |= _native.FWD_SAVE_STATE
-    with torch.cuda.device(q.device):
-        status = _native.lib().p3d_attn_fwd_slab(op, ctypes.byref(slab), _native.ptr(y), _native.ptr(sk),
-                                                 _native.ptr(sv), _native.ptr(ol), _native.ptr(og),
-                                                 _native.ptr(lse_l), _native.ptr(lse_g), flags,
-                                                 _native.stream_of(q.device))
-    _native.check(status, "p3d_attn_fwd_slab")
-    del keep
-    return y, ((sk, sv, ol, og, lse_l, lse_g) if save_state else ())
+    call = _SlabCall(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, geometry, slabs, temperature,
+                     save_state, y_rows)
+    call.run()
+    return call.result()
+
+
+class _DeviceBytes:
+    """A raw device allocation seen by ``torch.as_tensor`` (CUDA array interface)."""
+
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 2,
+                                         "strides": None}
+
+
+class SlabPeers:
+    """The peer-memory exchange of one z-slab partition (``p3d_peer_*``): every rank's region
+    of device memory, mapped into every other rank's process over NVLink.
+
+    A rank's region holds what its slab kernel reads -- its keys / values with the halo
+    planes around them ([B, G, halo_planes * Y * X, D] each) and the summaries of every rank
+    ([B, G, world * M, D] each, rank-major) -- and two counters.  :meth:`exchange` waits for
+    the peers' credits, pushes this rank's summaries to every peer and its boundary planes
+    to its neighbours (one kernel, 16-byte stores over NVLink), copies its own rows into its
+    region and waits for the peers' pushes; :meth:`release` raises every peer's credit once
+    this rank's kernels have read the region.  Building one is collective (the ranks trade
+    IPC handles through the process group) and must happen outside stream capture; the calls
+    after it capture into CUDA graphs.  :meth:`close` (collective) unmaps and frees.
+    """
+
+    ARRIVALS, CREDITS, HEADER = 0, 128, 4096
+
+    def __init__(self, slabs: ZSlabs, batch, kv_heads, head_dim, summaries, dtype, device, group=None, ctas=None,
+                 timeout_s=10.0):
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("SlabPeers is set up outside stream capture (its first call runs eagerly)")
+        self.world = dist.get_world_size(group)
+        if dist.get_rank(group) != slabs.rank:
+            raise ValueError("the slab partition's rank is not this process's rank in the group")
+        if slabs.planes < slabs.radius:
+            raise ValueError("a rank's planes must cover the halo depth")
+        self.slabs, self.group, self.device, self.dtype = slabs, group, torch.device(device), dtype
+        self.shape = (batch, kv_heads, head_dim, summaries)
+        self.timeout_s = float(timeout_s)
+        props = torch.cuda.get_device_properties(self.device)
+        self.ctas = int(ctas or 2 * props.multi_processor_count)
+        es = torch.empty((), dtype=dtype).element_size()
+        pt = slabs.plane_tokens
+        self.row_bytes = head_dim * es
+        rows_max = (slabs.planes + 2 * slabs.radius) * pt
+        align = lambda v: -(-v // 4096) * 4096  # noqa: E731
+        self.ext_bytes = align(batch * kv_heads * rows_max * self.row_bytes)
+        self.summ_bytes = align(batch * kv_heads * self.world * summaries * self.row_bytes)
+        self.offsets = {"k": self.HEADER, "v": self.HEADER + self.ext_bytes,
+                        "sk": self.HEADER + 2 * self.ext_bytes, "sv": self.HEADER + 2 * self.ext_bytes + self.summ_bytes}
+        self.nbytes = self.HEADER + 2 * self.ext_bytes + 2 * self.summ_bytes
+        lib = _native.lib()
+        handle = ctypes.create_string_buffer(_native.PEER_HANDLE_BYTES)
+        own = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _native.check(lib.p3d_peer_alloc(self.nbytes, ctypes.byref(own), handle), "p3d_peer_alloc")
+        self.own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.bases = [None] * self.world
+        self.opened = []
+        for r in range(self.world):
+            if r == slabs.rank:
+                self.bases[r] = self.own
+                continue
+            ptr = ctypes.c_void_p()
+            with torch.cuda.device(self.device):
+                _native.check(lib.p3d_peer_open(ctypes.create_string_buffer(handles[r], len(handles[r])),
+                                                ctypes.byref(ptr)), "p3d_peer_open")
+            self.bases[r] = ptr.value
+            self.opened.append(ptr.value)
+        region = torch.as_tensor(_DeviceBytes(self.own, self.nbytes), device=self.device)
+        self.region = region
+        b, g, d, m = self.shape
+        rows = slabs.halo_planes * pt
+        view = lambda key, n_rows: region[self.offsets[key]:self.offsets[key] + b * g * n_rows * self.row_bytes].view(  # noqa: E731
+            dtype).view(b, g, n_rows, d)
+        self.kl_ext, self.vl_ext = view("k", rows), view("v", rows)
+        self.sk, self.sv = view("sk", self.world * m), view("sv", self.world * m)
+        # expected arrivals (every peer pushes with `ctas` CTAs) and credits (one per peer)
+        self.expected = torch.tensor([(self.world - 1) * self.ctas, 0], dtype=torch.int64, device=self.device)
+        peers = [r for r in range(self.world) if r != slabs.rank]
+        self._arrive = (ctypes.c_void_p * max(1, len(peers)))(*[self.bases[r] + self.ARRIVALS for r in peers])
+        self._credit = (ctypes.c_void_p * max(1, len(peers)))(*[self.bases[r] + self.CREDITS for r in peers])
+        self.peers = peers
+
+    def _ext_rows(self, rank):
+        s = ZSlabs(self.slabs.grid, self.world, rank, self.slabs.radius, self.slabs.block_depth)
+        return s, s.halo_planes * s.plane_tokens
+
+    def _copies(self, kl, vl, sk_rank, sv_rank):
+        """(remote copies, local copies) of one call, as ``p3d_peer_copy`` records."""
+        s, rb = self.slabs, self.row_bytes
+        b, g, d, m = self.shape
+        pt, n = s.plane_tokens, s.tokens
+        remote, local = [], []
+
+        def rec(src, src_off, dst, rows_each, src_rows, dst_rows):
+            return (src.data_ptr() + src_off * rb, dst, b * g, rows_each * rb, src_rows * rb, dst_rows * rb)
+
+        for key, t in (("sk", sk_rank), ("sv", sv_rank)):
+            for r in range(self.world):
+                dst = self.bases[r] + self.offsets[key] + s.rank * m * rb
+                (local if r == s.rank else remote).append(rec(t, 0, dst, m, m, self.world * m))
+        for key, t in (("k", kl), ("v", vl)):
+            if s.halo_lo:   # my first planes are the lower neighbour's upper halo
+                nb, rows = self._ext_rows(s.rank - 1)
+                dst = self.bases[s.rank - 1] + self.offsets[key] + (nb.halo_lo + nb.planes) * pt * rb
+                remote.append(rec(t, 0, dst, nb.halo_hi * pt, n, rows))
+            if s.halo_hi:   # my last planes are the upper neighbour's lower halo
+                nb, rows = self._ext_rows(s.rank + 1)
+                dst = self.bases[s.rank + 1] + self.offsets[key]
+                remote.append(rec(t, n - nb.halo_lo * pt, dst, nb.halo_lo * pt, n, rows))
+            own_rows = s.halo_planes * pt
+            local.append(rec(t, 0, self.own + self.offsets[key] + s.halo_lo * pt * rb, n, n, own_rows))
+        return remote, local
+
+    def exchange(self, kl, vl, sk_rank, sv_rank):
+        """``(kl_ext, vl_ext, sk, sv)`` as :func:`exchange_slab` returns them, as views of this
+        rank's region (valid until :meth:`release`)."""
+        b, g, d, m = self.shape
+        want = (b, g, self.slabs.tokens, d)
+        if tuple(kl.shape) != want or tuple(vl.shape) != want or tuple(sk_rank.shape) != (b, g, m, d) or \
+                tuple(sv_rank.shape) != (b, g, m, d) or any(t.dtype != self.dtype for t in (kl, vl, sk_rank, sv_rank)):
+            raise ValueError("exchange inputs do not match the peer regions")
+        kl, vl, sk_rank, sv_rank = (t.contiguous() for t in (kl, vl, sk_rank, sv_rank))
+        remote, local = self._copies(kl, vl, sk_rank, sv_rank)
+        copies = (_native.PeerCopy * len(remote + local))(*[_native.PeerCopy(*c) for c in remote + local])
+        lib, stream = _native.lib(), _native.stream_of(self.device)
+        exp = self.expected.data_ptr()
+        with torch.cuda.device(self.device):
+            if self.peers:
+                _native.check(lib.p3d_peer_wait(self.own + self.CREDITS, exp + 8, len(self.peers), self.timeout_s,
+                                                stream), "p3d_peer_wait")
+            _native.check(lib.p3d_peer_push(copies, len(copies), len(remote), self._arrive, len(self.peers),
+                                            self.ctas, stream), "p3d_peer_push")
+            if self.peers:
+                _native.check(lib.p3d_peer_wait(self.own + self.ARRIVALS, exp, len(self.peers) * self.ctas,
+                                                self.timeout_s, stream), "p3d_peer_wait")
+        return self.kl_ext, self.vl_ext, self.sk, self.sv
+
+    def release(self):
+        """Raise every peer's credit: this rank's kernels that read its region are enqueued."""
+        if self.peers:
+            with torch.cuda.device(self.device):
+                _native.check(_native.lib().p3d_peer_signal(self._credit, len(self.peers),
+                                                            _native.stream_of(self.device)), "p3d_peer_signal")
+
+    def close(self):
+        """Collective: wait for every rank's work, then unmap the peers' regions and free this one."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        lib = _native.lib()
+        with torch.cuda.device(self.device):
+            for ptr in self.opened:
+                _native.check(lib.p3d_peer_close(ptr), "p3d_peer_close")
+            self.opened = []
+            self.region = self.kl_ext = self.vl_ext = self.sk = self.sv = None
+            if self.own:
+                _native.check(lib.p3d_peer_free(self.own), "p3d_peer_free")
+                self.own = None
+        dist.barrier(group=self.group)
+
+
+_PEERS = {}
+
+
+def slab_peers(slabs: ZSlabs, kl, sk_rank, group=None):
+    """The cached :class:`SlabPeers` for this partition, shapes and group (built on first use)."""
+    b, g, _, d = kl.shape
+    key = (slabs, b, g, d, sk_rank.shape[2], kl.dtype, kl.device, id(group))
+    if key not in _PEERS:
+        _PEERS[key] = SlabPeers(slabs, b, g, d, sk_rank.shape[2], kl.dtype, kl.device, group)
+    return _PEERS[key]
+
+
+def release_peers():
+    """Collective: close every cached :class:`SlabPeers` (before the process group is destroyed)."""
+    for key in list(_PEERS):
+        _PEERS.pop(key).close()
+
+
+def peer_exchange_supported(kl, sk_rank):
+    """The peer exchange moves 16-byte words: every row it copies must be a multiple of 16 bytes."""
+    return kl.is_cuda and (kl.shape[3] * kl.element_size()) % 16 == 0
 
 
 def sharded_core_forward(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, slabs: ZSlabs, group=None,
                          temperature=1.0):
-    """The attention core of one rank's planes (inference): pool, gather, exchange, attend."""
+    """The attention core of one rank's planes (inference): pool, exchange (:func:`peer_forward`)
+    and attend."""
     sk_rank, sv_rank = pool_summaries(kg, vg, weight, bias, geometry, temperature)
-    sk, sv = gather_summaries(sk_rank, group), gather_summaries(sv_rank, group)
-    kl_ext, vl_ext = exchange_halos(kl, slabs, group), exchange_halos(vl, slabs, group)
-    y, _ = slab_forward(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, geometry, slabs, temperature)
+    return peer_forward(q, kl, vl, sk_rank, sv_rank, weight, bias, gate, sl, sg, geometry, slabs, group, temperature)
+
+
+def peer_forward(q, kl, vl, sk_rank, sv_rank, weight, bias, gate, sl, sg, geometry, slabs: ZSlabs, group=None,
+                 temperature=1.0, y_rows=False):
+    """Exchange and attend on one rank: the halo planes and summaries through the peer
+    regions (:class:`SlabPeers`) when the rows allow it and more than one rank runs, else one
+    NCCL point-to-point batch (:func:`exchange_slab`); then ``p3d_attn_fwd_slab``.  Returns y."""
+    if dist.get_world_size(group) > 1 and peer_exchange_supported(kl, sk_rank):
+        peers = slab_peers(slabs, kl, sk_rank, group)
+        kl_ext, vl_ext, sk, sv = peers.exchange(kl, vl, sk_rank, sv_rank)
+        y, _ = slab_forward(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, geometry, slabs, temperature,
+                            y_rows=y_rows)
+        peers.release()
+        return y
+    kl_ext, vl_ext, sk, sv = exchange_slab(kl, vl, sk_rank, sv_rank, slabs, group)
+    y, _ = slab_forward(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, geometry, slabs, temperature,
+                        y_rows=y_rows)
     return y
 
 
@@ -313,13 +556,12 @@ def sharded_layer_forward(layer, x, layout: SlabLayout, group=None):
         raise ValueError("x must be [batch, rank tokens, dim]")
     h, g, d = layer.heads, layer.kv_heads, layer.head_dim
     if layer._fast_inference(x):
-        # the fused glue of the single-GPU inference path, one exchange batch, token-major y
+        # the fused glue of the single-GPU inference path, the peer exchange, token-major y
         x, q, kl, vl, kg, vg, gate = layer._inference_glue(x, layout.coords, layout.grid_shape)
         sk_rank, sv_rank = pool_summaries(kg, vg, layer.pool_weight, layer.slot_bias, layout.geometry,
                                           layer.temperature)
-        kl_ext, vl_ext, sk, sv = exchange_slab(kl, vl, sk_rank, sv_rank, layout.slabs, group)
-        y, _ = slab_forward(q, kl_ext, vl_ext, sk, sv, layer.pool_weight, layer.slot_bias, gate, layer.local_scale,
-                            layer.global_scale, layout.geometry, layout.slabs, layer.temperature, y_rows=True)
+        y = peer_forward(q, kl, vl, sk_rank, sv_rank, layer.pool_weight, layer.slot_bias, gate, layer.local_scale,
+                         layer.global_scale, layout.geometry, layout.slabs, group, layer.temperature, y_rows=True)
         return layer._out_residual(x, y)
     xn = layer.norm(x)
     q = layer.to_q(xn).reshape(b, n, h, d).transpose(1, 2)

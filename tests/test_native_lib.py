@@ -40,7 +40,7 @@ def test_library_exports_every_declared_symbol():
 def test_library_metadata_calls():
     from pack3d_b200 import _native
     handle = _native.lib()
-    assert handle.p3d_abi_version() == 3
+    assert handle.p3d_abi_version() == 4
     assert handle.p3d_strerror(0) == b"success"
     assert handle.p3d_strerror(4).startswith(b"workspace")
     assert handle.p3d_device_count() >= 0

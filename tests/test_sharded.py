@@ -10,7 +10,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from pack3d_b200.sharded import ZSlabs, exchange_halos, exchange_slab, gather_summaries, slab_layout
+from pack3d_b200.sharded import (SlabPeers, ZSlabs, exchange_halos, exchange_slab, gather_summaries, interior_tiles,
+                                 release_peers, slab_layout)
 
 
 def _free_port():
@@ -35,6 +36,22 @@ def test_partition_covers_the_volume_with_clipped_halos():
         ZSlabs((30, 8, 8), 2, 0)    # 15 planes: not whole 4-plane blocks
     with pytest.raises(ValueError):
         ZSlabs((32, 8, 8), 2, 2)
+
+
+@pytest.mark.parametrize("radius", [1, 2])
+def test_interior_tiles_read_no_halo_plane(radius):
+    """A tile in the interior range reads keys / values of the rank's own planes only (planes
+    outside the volume are masked, not read); every tile outside it reads a halo plane."""
+    grid = (64, 8, 8)
+    for world in (1, 2, 4, 8):
+        for rank in range(world):
+            s = ZSlabs(grid, world, rank, radius=radius)
+            begin, end = interior_tiles(s)
+            for t in range(s.planes // 4):
+                lo = max(0, s.z0 + 4 * t - radius)
+                hi = min(grid[0], s.z0 + 4 * t + 4 + radius)
+                own = s.z0 <= lo and hi <= s.z0 + s.planes
+                assert own == (begin <= t < end), (world, rank, t)
 
 
 def test_slab_layout_has_global_coordinates():
@@ -153,9 +170,169 @@ def test_slab_forward_matches_the_whole_volume(cuda_device, world):
     assert _native.device_errors() == 0
 
 
+@pytest.mark.gpu
+def test_slab_forward_tile_ranges_compose(cuda_device):
+    """The slab forward run over ranges of its query tiles (the overlapped exchange's interior
+    first, the tiles at the ends after) writes the same y as one launch over all of them."""
+    from pack3d_b200 import _native
+    from pack3d_b200.sharded import _SlabCall, pool_summaries, slab_forward
+    grid, world = (48, 16, 24), 4   # 12 planes a rank: an interior tile in the middle ranks
+    layout, inputs = _case(grid, torch.bfloat16, 12)
+    dev = [t.to(cuda_device) for t in inputs]
+    slabs = [ZSlabs(grid, world, r) for r in range(world)]
+    layouts = [slab_layout(grid, slabs=s).to(cuda_device) for s in slabs]
+    parts = [_slab_inputs(dev, s) for s in slabs]
+    pooled = [pool_summaries(p[3], p[4], p[5], p[6], lay.geometry) for p, lay in zip(parts, layouts)]
+    sk = torch.cat([p[0] for p in pooled], dim=2)
+    sv = torch.cat([p[1] for p in pooled], dim=2)
+    for s, lay, p in zip(slabs, layouts, parts):
+        q, kl_ext, vl_ext, _, _, weight, bias, gate, sl, sg = p
+        want, _ = slab_forward(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, lay.geometry, s, y_rows=True)
+        begin, end = interior_tiles(s)
+        call = _SlabCall(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, lay.geometry, s, 1.0, False, True)
+        call.y.zero_()
+        if begin < end:
+            call.run(begin, end)
+        begin, end = min(begin, end), max(begin, end)   # an empty interior: all tiles after
+        lo_rows, hi_rows = begin * 4 * s.plane_tokens, end * 4 * s.plane_tokens
+        assert torch.equal(call.y[:, :, lo_rows:hi_rows], want[:, :, lo_rows:hi_rows]), s.rank
+        assert not call.y[:, :, :lo_rows].any() and not call.y[:, :, hi_rows:].any(), s.rank
+        for t0, t1 in ((0, begin), (end, call.tiles_z)):
+            if t0 < t1:
+                call.run(t0, t1)
+        assert torch.equal(call.y, want), s.rank
+    assert _native.device_errors() == 0
+
+
+def _emulated_exchange(grid, world, radius, b, g, d, m, dtype=torch.bfloat16):
+    """Every rank's peer-exchange copy records applied to emulated regions (host byte arrays
+    at made-up base addresses): the regions' views against what the NCCL batch gives."""
+    import numpy as np
+    es = torch.empty((), dtype=dtype).element_size()
+    gen = torch.Generator().manual_seed(3)
+    full_k = torch.randn(b, g, grid[0] * grid[1] * grid[2], d, generator=gen).to(dtype)
+    full_v = torch.randn(full_k.shape, generator=gen).to(dtype)
+    summ = [(torch.randn(b, g, m, d, generator=gen).to(dtype), torch.randn(b, g, m, d, generator=gen).to(dtype))
+            for _ in range(world)]
+    peers, inputs, regions = [], [], []
+    for r in range(world):
+        s = ZSlabs(grid, world, r, radius=radius)
+        p = SlabPeers.__new__(SlabPeers)
+        p.slabs, p.world, p.shape, p.row_bytes = s, world, (b, g, d, m), d * es
+        rows_max = (s.planes + 2 * radius) * s.plane_tokens
+        align = lambda v: -(-v // 4096) * 4096  # noqa: E731
+        p.ext_bytes = align(b * g * rows_max * p.row_bytes)
+        p.summ_bytes = align(b * g * world * m * p.row_bytes)
+        p.offsets = {"k": p.HEADER, "v": p.HEADER + p.ext_bytes, "sk": p.HEADER + 2 * p.ext_bytes,
+                     "sv": p.HEADER + 2 * p.ext_bytes + p.summ_bytes}
+        p.nbytes = p.HEADER + 2 * p.ext_bytes + 2 * p.summ_bytes
+        p.bases = [(q + 1) << 40 for q in range(world)]
+        p.own = p.bases[r]
+        lo, hi = s.token_range()
+        peers.append(p)
+        inputs.append((full_k[:, :, lo:hi].contiguous(), full_v[:, :, lo:hi].contiguous()) + summ[r])
+        regions.append(np.zeros(p.nbytes, dtype=np.uint8))
+    sources = [t for inp in inputs for t in inp]
+
+    def src_bytes(addr, nbytes):
+        for t in sources:
+            base = t.data_ptr()
+            if base <= addr and addr + nbytes <= base + t.numel() * es:
+                flat = t.view(torch.uint8).flatten().numpy() if dtype != torch.bfloat16 else \
+                    t.view(torch.int16).flatten().numpy().view(np.uint8)
+                return flat[addr - base:addr - base + nbytes]
+        raise AssertionError("copy source outside every input")
+
+    for r in range(world):
+        remote, local = peers[r]._copies(*inputs[r])
+        for src, dst, rows, row_bytes, src_stride, dst_stride in remote + local:
+            dst_rank = (dst >> 40) - 1
+            assert (dst_rank != r) == ((src, dst, rows, row_bytes, src_stride, dst_stride) in remote)
+            off = dst - peers[0].bases[dst_rank]
+            for i in range(rows):
+                chunk = src_bytes(src + i * src_stride, row_bytes)
+                o = off + i * dst_stride
+                assert 0 <= o and o + row_bytes <= peers[dst_rank].nbytes
+                regions[dst_rank][o:o + row_bytes] = chunk
+    for r in range(world):
+        p, s = peers[r], peers[r].slabs
+        region = torch.from_numpy(regions[r].view(np.int16)).view(dtype) if es == 2 else None
+        rows = s.halo_planes * s.plane_tokens
+        view = lambda key, n: region[p.offsets[key] // es:p.offsets[key] // es + b * g * n * d].view(b, g, n, d)  # noqa: E731
+        pt = s.plane_tokens
+        want = full_k[:, :, s.halo_z0 * pt:(s.halo_z0 + s.halo_planes) * pt]
+        assert torch.equal(view("k", rows), want), r
+        assert torch.equal(view("v", rows), full_v[:, :, s.halo_z0 * pt:(s.halo_z0 + s.halo_planes) * pt]), r
+        assert torch.equal(view("sk", world * m), torch.cat([x[0] for x in summ], dim=2)), r
+        assert torch.equal(view("sv", world * m), torch.cat([x[1] for x in summ], dim=2)), r
+
+
+@pytest.mark.parametrize("world,radius", [(2, 2), (4, 2), (4, 1), (8, 2)])
+def test_peer_exchange_copies_build_the_slab_buffers(world, radius):
+    """The peer exchange's copy records (every rank's, applied to emulated regions) leave in
+    each rank's region exactly its planes with the halo planes around them and every rank's
+    summaries in rank order -- what the NCCL exchange hands the slab kernel."""
+    _emulated_exchange((8 * world, 4, 6), world, radius, 2, 3, 8, 5)
+
+
+@pytest.mark.gpu
+def test_peer_wait_times_out_and_reports(cuda_device):
+    """A peer wait on a counter that nothing raises gives up after its limit, sets the peer
+    bits of the device error flags and leaves the context usable."""
+    import ctypes
+    from pack3d_b200 import _native
+    lib = _native.lib()
+    counter = torch.zeros(2, dtype=torch.int64, device=cuda_device)
+    expected = torch.tensor([1, 0], dtype=torch.int64, device=cuda_device)
+    _native.device_errors()
+    with torch.cuda.device(cuda_device):
+        _native.check(lib.p3d_peer_wait(counter.data_ptr(), expected.data_ptr(), 5, 0.05,
+                                        _native.stream_of(cuda_device)), "p3d_peer_wait")
+    torch.cuda.synchronize(cuda_device)
+    assert _native.device_errors() == 33
+    assert expected.tolist() == [6, 0]
+    # a counter that is high enough passes at once; a signal raises the counters
+    counter.fill_(6)
+    targets = (ctypes.c_void_p * 2)(counter.data_ptr(), counter.data_ptr() + 8)
+    with torch.cuda.device(cuda_device):
+        stream = _native.stream_of(cuda_device)
+        _native.check(lib.p3d_peer_wait(counter.data_ptr(), expected.data_ptr(), 1, 1.0, stream), "p3d_peer_wait")
+        _native.check(lib.p3d_peer_signal(targets, 2, stream), "p3d_peer_signal")
+    torch.cuda.synchronize(cuda_device)
+    assert _native.device_errors() == 0
+    assert counter.tolist() == [7, 7] and expected.tolist() == [7, 0]
+
+
+@pytest.mark.gpu
+def test_peer_push_copies_strided_rows_and_arrives(cuda_device):
+    """p3d_peer_push on one device: strided rows land where the records say, untouched bytes
+    stay, and every CTA adds one arrival to each target."""
+    import ctypes
+    from pack3d_b200 import _native
+    lib = _native.lib()
+    gen = torch.Generator(device=cuda_device).manual_seed(4)
+    src = torch.randint(-2**15, 2**15, (6, 40), dtype=torch.int16, device=cuda_device, generator=gen)
+    dst = torch.zeros(6, 64, dtype=torch.int16, device=cuda_device)
+    small = torch.zeros(3, 16, dtype=torch.int16, device=cuda_device)
+    counters = torch.zeros(2, dtype=torch.int64, device=cuda_device)
+    copies = (_native.PeerCopy * 2)(
+        _native.PeerCopy(src.data_ptr() + 16, dst.data_ptr() + 32, 6, 48, 80, 128),     # words 1-3 of each row
+        _native.PeerCopy(src.data_ptr(), small.data_ptr(), 3, 32, 160, 32))              # rows 0, 2, 4: words 0-1
+    targets = (ctypes.c_void_p * 2)(counters.data_ptr(), counters.data_ptr() + 8)
+    with torch.cuda.device(cuda_device):
+        _native.check(lib.p3d_peer_push(copies, 2, 1, targets, 2, 7, _native.stream_of(cuda_device)), "p3d_peer_push")
+    torch.cuda.synchronize(cuda_device)
+    want = torch.zeros_like(dst)
+    want[:, 16:40] = src[:, 8:32]
+    assert torch.equal(dst, want)
+    assert torch.equal(small, src[0::2, :16])
+    assert counters.tolist() == [7, 7]
+    assert _native.device_errors() == 0
+
+
 def _nccl_worker(rank, world, port, grid, out):
     from pack3d_b200 import _native
-    from pack3d_b200.sharded import sharded_core_forward
+    from pack3d_b200.sharded import pool_summaries, sharded_core_forward, slab_forward, slab_peers
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
@@ -169,8 +346,19 @@ def _nccl_worker(rank, world, port, grid, out):
         cut = lambda t: t[:, :, lo:hi].contiguous()  # noqa: E731
         y = sharded_core_forward(cut(q), cut(kl), cut(vl), cut(kg), cut(vg), weight, bias, cut(gate), sl, sg,
                                  lay.geometry, s)
+        # the overlapped exchange (interior tiles while the halo planes are in flight) gives
+        # bit for bit what the one-batch exchange followed by one launch gives
+        skr, svr = pool_summaries(cut(kg), cut(vg), weight, bias, lay.geometry)
+        kx, vx, skx, svx = exchange_slab(cut(kl), cut(vl), skr, svr, s)
+        y_one, _ = slab_forward(cut(q), kx, vx, skx, svx, weight, bias, cut(gate), sl, sg, lay.geometry, s)
+        # the peer exchange's buffers equal the NCCL batch's
+        peers = slab_peers(s, cut(kl), skr)
+        got = [t.clone() for t in peers.exchange(cut(kl), cut(vl), skr, svr)]
+        peers.release()
+        same = torch.equal(y, y_one) and all(torch.equal(a, b) for a, b in zip(got, (kx, vx, skx, svx)))
         torch.cuda.synchronize(dev)
-        out[rank] = (y.cpu(), _native.device_errors())
+        out[rank] = (y.cpu(), _native.device_errors(), same)
+        release_peers()
     finally:
         dist.destroy_process_group()
 
@@ -190,10 +378,10 @@ def test_sharded_forward_over_nccl():
     dev = torch.device("cuda", 0)
     y_full, _ = p3d_ops.forward(*[t.to(dev) for t in inputs], layout.geometry.to(dev), 1.0, save_state=False)
     for rank in range(world):
-        y, errors = results[rank]
+        y, errors, same = results[rank]
         s = ZSlabs(grid, world, rank)
         lo, hi = s.token_range()
-        assert errors == 0
+        assert errors == 0 and same, rank
         assert (y.float() - y_full[:, :, lo:hi].float().cpu()).abs().max().item() <= 2e-2, rank
 
 
@@ -296,6 +484,7 @@ def _train_worker(rank, world, port, grid, out):
         torch.cuda.synchronize(dev)
         out[rank] = (y.detach().cpu(), x.grad.cpu(), {k: p.grad.cpu() for k, p in layer.named_parameters()},
                      _native.device_errors(), y_inf)
+        release_peers()
     finally:
         dist.destroy_process_group()
 
@@ -370,6 +559,9 @@ def _graph_worker(rank, world, port, grid, out):
                 torch.cuda.synchronize(dev)
                 got.append(y.clone())
         out[rank] = ([torch.equal(g, want) for g in got], _native.device_errors())
+        del graph   # a graph holding the exchange is released before its peer regions
+        graph = None
+        release_peers()
     finally:
         del graph   # a graph holding NCCL calls is released before the process group
         dist.destroy_process_group()
