@@ -150,13 +150,15 @@ P3D_API int p3d_qkv_gate_split(const void *proj, int proj_cols, void *q, void *k
  *   output would be, then rotated and stored head-major as p3d_qkv_split stores it.  The
  *   projections never reach HBM.  flags: P3D_SPLIT_RASTER_QKV as for p3d_qkv_split.  Shapes
  *   p3d_qkv_project_supported() rejects return P3D_ERR_UNSUPPORTED (callers then run the
- *   GEMMs and p3d_qkv_split).
+ *   GEMMs and p3d_qkv_split).  kl and vl are stored [B, G, kv_rows, D] with token row n at
+ *   row kv_row0 + n (kv_rows 0: tokens, the dense layout): a z-slab rank writes its keys and
+ *   values straight between the halo rows of its extended buffers.
  */
 P3D_API int p3d_qkv_project_supported(int dtype, int dim, int heads, int kv_heads, int head_dim);
 P3D_API int p3d_qkv_project(const void *x, const void *wq, const void *wkv, void *q, void *kl, void *vl, void *kg,
                     void *vg, int dtype, int batch, int heads, int kv_heads, int tokens, int dim, int head_dim,
                     const int64_t *coords, int pz, int py, int px, const float *phases, int ez, int ey, int ex,
-                    unsigned flags, void *stream);
+                    int64_t kv_rows, int64_t kv_row0, unsigned flags, void *stream);
 
 /*
  * Layer glue of the training path (their backward halves):

@@ -167,11 +167,24 @@ class PACK3DAttention(nn.Module):
         out = torch.addmm(x.reshape(b * n, self.dim), y_rows.transpose(1, 2).reshape(b * n, -1), self.to_out.weight.t())
         return out.view(b, n, self.dim)
 
-    def _inference_glue(self, x, coords, grid_shape, raster_qkv=False):
+    def _inference_glue(self, x, coords, grid_shape, raster_qkv=False, kv_out=None):
         """LayerNorm, projections, RoPE at ``coords`` (extents ``grid_shape``) and the gate of
         the fused inference path: ``(x, q, kl, vl, kg, vg, gate)``, head-major.  ``raster_qkv``
         stores the rows of q, kl, vl at each token's raster index (the extents must be the
-        token grid)."""
+        token grid).  ``kv_out = (kl_ext, vl_ext, row0)``: kl and vl are rows
+        ``[row0, row0 + N)`` of those [B, G, rows, D] buffers (a z-slab rank's extended
+        buffers); the fused projection writes them there, the other forms copy them in."""
+        glue_out = self._inference_glue_rows(x, coords, grid_shape, raster_qkv, kv_out)
+        if kv_out is None or glue_out[2].data_ptr() == kv_out[0][:, :, kv_out[2]:].data_ptr():
+            return glue_out
+        x, q, kl, vl, kg, vg, gate = glue_out
+        n = kl.shape[2]
+        kl_ext, vl_ext, row0 = kv_out
+        kl_ext[:, :, row0:row0 + n].copy_(kl)
+        vl_ext[:, :, row0:row0 + n].copy_(vl)
+        return x, q, kl_ext[:, :, row0:row0 + n], vl_ext[:, :, row0:row0 + n], kg, vg, gate
+
+    def _inference_glue_rows(self, x, coords, grid_shape, raster_qkv, kv_out):
         from . import _native
         from .rope import phase_tables
         b, n = x.shape[0], x.shape[1]
@@ -197,7 +210,7 @@ class PACK3DAttention(nn.Module):
             # gate from its own GEMM and p3d_gate_pairs
             coords = coords.to(device=dev, dtype=torch.int64).contiguous()
             q, kl, vl, kg, vg = glue.project_split_raw(xn, self.to_q.weight, self.to_kv.weight, coords, phases, pairs,
-                                                       extents, h, g, d, raster_qkv=raster_qkv)
+                                                       extents, h, g, d, raster_qkv=raster_qkv, kv_out=kv_out)
             logits = torch.addmm(self.gate.bias, xn.view(b * n, self.dim), self.gate.weight.t())
             gate = torch.empty((b, h, n), dtype=x.dtype, device=dev)
             with torch.cuda.device(dev):

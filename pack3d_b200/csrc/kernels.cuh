@@ -74,6 +74,7 @@ struct ProjArgs {
   const float *phases;
   int table_floats;             // floats in the phase table
   int raster_qkv, ey, ex;       // q, kl, vl rows at each token's raster index (ey x ex planes)
+  int64_t kv_rows, kv_row0;     // kl, vl: [B, G, kv_rows, D], token row n at kv_row0 + n
 };
 int proj_group_heads(int head_dim, int heads, int kv_heads, int dim, size_t smem_limit);
 size_t proj_smem_bytes(int dim, int group_cols);

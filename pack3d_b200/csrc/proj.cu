@@ -66,6 +66,7 @@ struct ProjParams {
   const float *phases;
   int table_floats;    // 2 * (ez pz + ey py + ex px); staged in shared memory when <= kMaxTableFloats
   int raster_qkv, ey, ex;  // q, kl, vl rows at each token's raster index (c0 ey + c1) ex + c2
+  int64_t kv_rows, kv_row0;  // kl, vl: [B, G, kv_rows, D], token row n at kv_row0 + n
 };
 
 // (cos, sin) of rotation pair `pair` of a token at coordinates c, from the table `tab`.
@@ -296,7 +297,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         void *o = is_q ? p.out[0] : part == 0 ? p.out[1] : part == 1 ? p.out[2] : part == 2 ? p.out[3] : p.out[4];
         // q, kl, vl go to the token's raster row in the raster form (kg, vg stay in token order)
         const int64_t nd = (p.raster_qkv && (is_q || part <= 1)) ? ((int64_t)c3[0] * p.ey + c3[1]) * p.ex + c3[2] : n;
-        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(o) + (((int64_t)b * ht + hh) * p.tokens + nd) * D);
+        const bool kv_local = !is_q && part <= 1;
+        const int64_t head_rows = kv_local ? p.kv_rows : (int64_t)p.tokens;
+        const int64_t row = kv_local ? p.kv_row0 + nd : nd;
+        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(o) + (((int64_t)b * ht + hh) * head_rows + row) * D);
 #pragma unroll
         for (int v = 0; v < D / 8; ++v)
           dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
@@ -352,6 +356,8 @@ int launch_proj(const ProjArgs &a, cudaStream_t stream) {
   if (int st = device_info(&info)) return st;
   p.ctas_per_group = info.sm_count / p.groups > 0 ? info.sm_count / p.groups : 1;
   for (int i = 0; i < 5; ++i) p.out[i] = a.out[i];
+  p.kv_rows = a.kv_rows;
+  p.kv_row0 = a.kv_row0;
   p.coords = a.coords;
   for (int i = 0; i < 3; ++i) {
     p.pairs[i] = a.pairs[i];
@@ -429,8 +435,12 @@ extern "C" int p3d_qkv_project_supported(int dtype, int dim, int heads, int kv_h
 extern "C" int p3d_qkv_project(const void *x, const void *wq, const void *wkv, void *q, void *kl, void *vl, void *kg,
                                void *vg, int dtype, int batch, int heads, int kv_heads, int tokens, int dim,
                                int head_dim, const int64_t *coords, int pz, int py, int px, const float *phases,
-                               int ez, int ey, int ex, unsigned flags, void *stream) {
+                               int ez, int ey, int ex, int64_t kv_rows, int64_t kv_row0, unsigned flags,
+                               void *stream) {
   P3D_CHECK_ARG(x && wq && wkv && q && kl && vl && kg && vg && coords && phases, "p3d_qkv_project: null pointer");
+  if (kv_rows == 0) kv_rows = tokens;
+  P3D_CHECK_ARG(kv_row0 >= 0 && kv_row0 + tokens <= kv_rows, "p3d_qkv_project: kl / vl rows [%lld, %lld) outside "
+                "%lld rows", (long long)kv_row0, (long long)(kv_row0 + tokens), (long long)kv_rows);
   P3D_CHECK_ARG((flags & ~P3D_SPLIT_RASTER_QKV) == 0u, "p3d_qkv_project: unknown flags 0x%x", flags);
   P3D_CHECK_ARG(!(flags & P3D_SPLIT_RASTER_QKV) || (int64_t)ez * ey * ex == tokens,
                 "p3d_qkv_project: raster rows need the coordinate extents to be the token grid (%d x %d x %d != %d)",
@@ -459,6 +469,8 @@ extern "C" int p3d_qkv_project(const void *x, const void *wq, const void *wkv, v
   a.x = x;
   a.wq = wq;
   a.wkv = wkv;
+  a.kv_rows = kv_rows;
+  a.kv_row0 = kv_row0;
   a.out[0] = q;
   a.out[1] = kl;
   a.out[2] = vl;

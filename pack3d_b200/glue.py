@@ -131,19 +131,34 @@ def project_supported(x, wq, wkv, heads, kv_heads, head_dim):
                                                             kv_heads, head_dim))
 
 
-def project_split_raw(x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, head_dim, raster_qkv=False):
+def project_split_raw(x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, head_dim, raster_qkv=False,
+                      kv_out=None):
     """``p3d_qkv_project`` on x [B, N, dim] (no autograd): ``(q, kl, vl, kg, vg)``; ``raster_qkv``
-    stores q, kl, vl at each token's raster row."""
+    stores q, kl, vl at each token's raster row.  ``kv_out = (kl_ext, vl_ext, row0)`` writes kl
+    and vl into rows ``[row0, row0 + N)`` of the given [B, G, rows, D] buffers (a z-slab rank's
+    extended buffers) and returns those row ranges as kl, vl."""
     b, n, dim = x.shape
     x = x.contiguous()
     dev, dt = x.device, x.dtype
     q = torch.empty((b, heads, n, head_dim), dtype=dt, device=dev)
-    kl, vl, kg, vg = (torch.empty((b, kv_heads, n, head_dim), dtype=dt, device=dev) for _ in range(4))
+    kg, vg = (torch.empty((b, kv_heads, n, head_dim), dtype=dt, device=dev) for _ in range(2))
+    kv_rows = row0 = 0
+    if kv_out is None:
+        kl, vl = (torch.empty((b, kv_heads, n, head_dim), dtype=dt, device=dev) for _ in range(2))
+        dst_k, dst_v = kl, vl
+    else:
+        dst_k, dst_v, row0 = kv_out
+        want = (b, kv_heads, dst_k.shape[2], head_dim)
+        if tuple(dst_k.shape) != want or tuple(dst_v.shape) != want or not (dst_k.is_contiguous() and
+                                                                           dst_v.is_contiguous()):
+            raise ValueError("kv_out buffers must be contiguous [B, G, rows, D]")
+        kv_rows = dst_k.shape[2]
+        kl, vl = dst_k[:, :, row0:row0 + n], dst_v[:, :, row0:row0 + n]
     with torch.cuda.device(dev):
         _native.check(_native.lib().p3d_qkv_project(
-            _native.ptr(x), _native.ptr(wq), _native.ptr(wkv), _native.ptr(q), _native.ptr(kl), _native.ptr(vl),
+            _native.ptr(x), _native.ptr(wq), _native.ptr(wkv), _native.ptr(q), _native.ptr(dst_k), _native.ptr(dst_v),
             _native.ptr(kg), _native.ptr(vg), _native.DTYPE_CODE[dt], b, heads, kv_heads, n, dim, head_dim,
-            _native.ptr(coords), *pairs, _native.ptr(phases), *extents,
+            _native.ptr(coords), *pairs, _native.ptr(phases), *extents, kv_rows, row0,
             _native.SPLIT_RASTER_QKV if raster_qkv else 0, _native.stream_of(dev)), "p3d_qkv_project")
     return q, kl, vl, kg, vg
 

@@ -416,31 +416,41 @@ class SlabPeers:
         return s, s.halo_planes * s.plane_tokens
 
     def _copies(self, kl, vl, sk_rank, sv_rank):
-        """(remote copies, local copies) of one call, as ``p3d_peer_copy`` records."""
+        """(remote copies, local copies) of one call, as ``p3d_peer_copy`` records.  Every input
+        is [B, G, rows, D] with contiguous rows per head (:func:`_head_stride`); kl / vl already
+        in place between this rank's halo rows (``p3d_qkv_project`` with ``kv_out``) are not
+        copied again."""
         s, rb = self.slabs, self.row_bytes
         b, g, d, m = self.shape
         pt, n = s.plane_tokens, s.tokens
         remote, local = [], []
 
-        def rec(src, src_off, dst, rows_each, src_rows, dst_rows):
-            return (src.data_ptr() + src_off * rb, dst, b * g, rows_each * rb, src_rows * rb, dst_rows * rb)
+        def rec(src, src_off, dst, rows_each, dst_rows):
+            return (src.data_ptr() + src_off * rb, dst, b * g, rows_each * rb, _head_stride(src), dst_rows * rb)
 
         for key, t in (("sk", sk_rank), ("sv", sv_rank)):
             for r in range(self.world):
                 dst = self.bases[r] + self.offsets[key] + s.rank * m * rb
-                (local if r == s.rank else remote).append(rec(t, 0, dst, m, m, self.world * m))
+                (local if r == s.rank else remote).append(rec(t, 0, dst, m, self.world * m))
+        own_rows = s.halo_planes * pt
         for key, t in (("k", kl), ("v", vl)):
             if s.halo_lo:   # my first planes are the lower neighbour's upper halo
                 nb, rows = self._ext_rows(s.rank - 1)
                 dst = self.bases[s.rank - 1] + self.offsets[key] + (nb.halo_lo + nb.planes) * pt * rb
-                remote.append(rec(t, 0, dst, nb.halo_hi * pt, n, rows))
+                remote.append(rec(t, 0, dst, nb.halo_hi * pt, rows))
             if s.halo_hi:   # my last planes are the upper neighbour's lower halo
                 nb, rows = self._ext_rows(s.rank + 1)
                 dst = self.bases[s.rank + 1] + self.offsets[key]
-                remote.append(rec(t, n - nb.halo_lo * pt, dst, nb.halo_lo * pt, n, rows))
-            own_rows = s.halo_planes * pt
-            local.append(rec(t, 0, self.own + self.offsets[key] + s.halo_lo * pt * rb, n, n, own_rows))
+                remote.append(rec(t, n - nb.halo_lo * pt, dst, nb.halo_lo * pt, rows))
+            dst = self.own + self.offsets[key] + s.halo_lo * pt * rb
+            if t.data_ptr() != dst or _head_stride(t) != own_rows * rb:
+                local.append(rec(t, 0, dst, n, own_rows))
         return remote, local
+
+    def kv_out(self):
+        """``(kl_ext, vl_ext, row0)``: where ``p3d_qkv_project`` writes this rank's kl / vl so
+        that :meth:`exchange` copies nothing locally."""
+        return self.kl_ext, self.vl_ext, self.slabs.halo_lo * self.slabs.plane_tokens
 
     def exchange(self, kl, vl, sk_rank, sv_rank):
         """``(kl_ext, vl_ext, sk, sv)`` as :func:`exchange_slab` returns them, as views of this
@@ -450,7 +460,7 @@ class SlabPeers:
         if tuple(kl.shape) != want or tuple(vl.shape) != want or tuple(sk_rank.shape) != (b, g, m, d) or \
                 tuple(sv_rank.shape) != (b, g, m, d) or any(t.dtype != self.dtype for t in (kl, vl, sk_rank, sv_rank)):
             raise ValueError("exchange inputs do not match the peer regions")
-        kl, vl, sk_rank, sv_rank = (t.contiguous() for t in (kl, vl, sk_rank, sv_rank))
+        kl, vl, sk_rank, sv_rank = (t if _head_stride(t) else t.contiguous() for t in (kl, vl, sk_rank, sv_rank))
         remote, local = self._copies(kl, vl, sk_rank, sv_rank)
         copies = (_native.PeerCopy * len(remote + local))(*[_native.PeerCopy(*c) for c in remote + local])
         lib, stream = _native.lib(), _native.stream_of(self.device)
@@ -489,15 +499,23 @@ class SlabPeers:
         dist.barrier(group=self.group)
 
 
+def _head_stride(t):
+    """Bytes between the heads of a [B, G, rows, D] tensor whose rows are contiguous within a
+    head and whose heads are evenly spaced across the batch; None for other layouts."""
+    b, g, n, d = t.shape
+    if t.stride(3) != 1 or (n > 1 and t.stride(2) != d) or (b > 1 and t.stride(0) != g * t.stride(1)):
+        return None
+    return t.stride(1) * t.element_size()
+
+
 _PEERS = {}
 
 
-def slab_peers(slabs: ZSlabs, kl, sk_rank, group=None):
+def slab_peers(slabs: ZSlabs, batch, kv_heads, head_dim, summaries, dtype, device, group=None):
     """The cached :class:`SlabPeers` for this partition, shapes and group (built on first use)."""
-    b, g, _, d = kl.shape
-    key = (slabs, b, g, d, sk_rank.shape[2], kl.dtype, kl.device, id(group))
+    key = (slabs, batch, kv_heads, head_dim, summaries, dtype, torch.device(device), id(group))
     if key not in _PEERS:
-        _PEERS[key] = SlabPeers(slabs, b, g, d, sk_rank.shape[2], kl.dtype, kl.device, group)
+        _PEERS[key] = SlabPeers(slabs, batch, kv_heads, head_dim, summaries, dtype, device, group)
     return _PEERS[key]
 
 
@@ -507,9 +525,11 @@ def release_peers():
         _PEERS.pop(key).close()
 
 
-def peer_exchange_supported(kl, sk_rank):
-    """The peer exchange moves 16-byte words: every row it copies must be a multiple of 16 bytes."""
-    return kl.is_cuda and (kl.shape[3] * kl.element_size()) % 16 == 0
+def peer_exchange_supported(head_dim, dtype, device, group=None):
+    """More than one rank, and rows the peer exchange can move (16-byte words: a row of
+    head_dim elements must be a multiple of 16 bytes)."""
+    es = torch.empty((), dtype=dtype).element_size()
+    return torch.device(device).type == "cuda" and dist.get_world_size(group) > 1 and (head_dim * es) % 16 == 0
 
 
 def sharded_core_forward(q, kl, vl, kg, vg, weight, bias, gate, sl, sg, geometry, slabs: ZSlabs, group=None,
@@ -525,8 +545,9 @@ def peer_forward(q, kl, vl, sk_rank, sv_rank, weight, bias, gate, sl, sg, geomet
     """Exchange and attend on one rank: the halo planes and summaries through the peer
     regions (:class:`SlabPeers`) when the rows allow it and more than one rank runs, else one
     NCCL point-to-point batch (:func:`exchange_slab`); then ``p3d_attn_fwd_slab``.  Returns y."""
-    if dist.get_world_size(group) > 1 and peer_exchange_supported(kl, sk_rank):
-        peers = slab_peers(slabs, kl, sk_rank, group)
+    if peer_exchange_supported(kl.shape[3], kl.dtype, kl.device, group):
+        b, g, _, d = kl.shape
+        peers = slab_peers(slabs, b, g, d, sk_rank.shape[2], kl.dtype, kl.device, group)
         kl_ext, vl_ext, sk, sv = peers.exchange(kl, vl, sk_rank, sv_rank)
         y, _ = slab_forward(q, kl_ext, vl_ext, sk, sv, weight, bias, gate, sl, sg, geometry, slabs, temperature,
                             y_rows=y_rows)
@@ -556,8 +577,13 @@ def sharded_layer_forward(layer, x, layout: SlabLayout, group=None):
         raise ValueError("x must be [batch, rank tokens, dim]")
     h, g, d = layer.heads, layer.kv_heads, layer.head_dim
     if layer._fast_inference(x):
-        # the fused glue of the single-GPU inference path, the peer exchange, token-major y
-        x, q, kl, vl, kg, vg, gate = layer._inference_glue(x, layout.coords, layout.grid_shape)
+        # the fused glue of the single-GPU inference path writing kl, vl into this rank's peer
+        # region, the peer exchange, token-major y
+        kv_out = None
+        if peer_exchange_supported(d, x.dtype, x.device, group):
+            kv_out = slab_peers(layout.slabs, b, g, d, layout.geometry.num_summaries, x.dtype, x.device,
+                                group).kv_out()
+        x, q, kl, vl, kg, vg, gate = layer._inference_glue(x, layout.coords, layout.grid_shape, kv_out=kv_out)
         sk_rank, sv_rank = pool_summaries(kg, vg, layer.pool_weight, layer.slot_bias, layout.geometry,
                                           layer.temperature)
         y = peer_forward(q, kl, vl, sk_rank, sv_rank, layer.pool_weight, layer.slot_bias, gate, layer.local_scale,

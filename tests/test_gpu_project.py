@@ -55,10 +55,26 @@ def test_project_matches_gemm_then_split(cuda_device, case):
     with torch.cuda.device(cuda_device):
         _native.check(lib.p3d_qkv_project(
             _native.ptr(x), _native.ptr(wq), _native.ptr(wkv), *[_native.ptr(t) for t in got], code, b, h, g, n, dim,
-            d, _native.ptr(coords), *pairs, _native.ptr(phases), *extents, 0, _native.stream_of(cuda_device)),
+            d, _native.ptr(coords), *pairs, _native.ptr(phases), *extents, 0, 0, 0, _native.stream_of(cuda_device)),
             "p3d_qkv_project")
+    # kl, vl between halo rows of an extended buffer (a z-slab rank's layout): the same rows,
+    # nothing written outside them
+    lo, extra = 3, 7
+    ext = [torch.full((b, g, n + extra, d), float("nan"), dtype=dtype, device=cuda_device) for _ in range(2)]
+    other = [torch.empty_like(t) for t in got]
+    with torch.cuda.device(cuda_device):
+        _native.check(lib.p3d_qkv_project(
+            _native.ptr(x), _native.ptr(wq), _native.ptr(wkv), _native.ptr(other[0]), _native.ptr(ext[0]),
+            _native.ptr(ext[1]), _native.ptr(other[3]), _native.ptr(other[4]), code, b, h, g, n, dim, d,
+            _native.ptr(coords), *pairs, _native.ptr(phases), *extents, n + extra, lo, 0,
+            _native.stream_of(cuda_device)), "p3d_qkv_project")
     torch.cuda.synchronize()
     assert _native.device_errors() == 0
+    for e, dense in zip(ext, got[1:3]):
+        assert torch.equal(e[:, :, lo:lo + n], dense)
+        assert torch.isnan(e[:, :, :lo]).all() and torch.isnan(e[:, :, lo + n:]).all()
+    for i in (0, 3, 4):
+        assert torch.equal(other[i], got[i])
     step = 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10
     for nm, a, w in zip(("q", "kl", "vl", "kg", "vg"), got, want):
         assert not torch.isnan(a).any(), nm

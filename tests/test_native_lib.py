@@ -3,6 +3,7 @@
 No compute entry point is called here (there may be no device); the product's
 CUDA requirement is checked to fail loudly instead of falling back.
 """
+import ctypes
 import re
 import subprocess
 import sys
@@ -108,11 +109,23 @@ def test_argument_checks_run_before_any_device_call():
     dummy = 16  # a non-null, 16-byte aligned stand-in: never dereferenced on these paths
     # p3d_qkv_project: null pointer, bad rotation pairs
     st = lib.p3d_qkv_project(None, dummy, dummy, dummy, dummy, dummy, dummy, dummy, _native.BF16, 1, 4, 4, 64, 192,
-                             48, dummy, 8, 8, 8, dummy, 4, 4, 4, 0, None)
+                             48, dummy, 8, 8, 8, dummy, 4, 4, 4, 0, 0, 0, None)
     assert st == 1 and b"null pointer" in lib.p3d_last_error()
     st = lib.p3d_qkv_project(dummy, dummy, dummy, dummy, dummy, dummy, dummy, dummy, _native.BF16, 1, 4, 4, 64, 192,
-                             48, dummy, 8, 8, 7, dummy, 4, 4, 4, 0, None)
+                             48, dummy, 8, 8, 7, dummy, 4, 4, 4, 0, 0, 0, None)
     assert st == 1 and b"pairs" in lib.p3d_last_error()
+    # kl / vl rows past the end of their buffers
+    st = lib.p3d_qkv_project(dummy, dummy, dummy, dummy, dummy, dummy, dummy, dummy, _native.BF16, 1, 4, 4, 64, 192,
+                             48, dummy, 8, 8, 8, dummy, 4, 4, 4, 70, 8, 0, None)
+    assert st == 1 and b"outside" in lib.p3d_last_error()
+    # the peer exchange: a row that is not whole 16-byte words, too many copies
+    copy = _native.PeerCopy(dummy, dummy, 2, 24, 32, 32)
+    st = lib.p3d_peer_push(ctypes.byref(copy), 1, 1, None, 0, 4, None)
+    assert st == 1 and b"multiple of 16" in lib.p3d_last_error()
+    st = lib.p3d_peer_push(ctypes.byref(copy), 33, 0, None, 0, 4, None)
+    assert st == 1 and b"at most" in lib.p3d_last_error()
+    st = lib.p3d_peer_wait(dummy, dummy, 1, 0.0, None)
+    assert st == 1 and b"timeout" in lib.p3d_last_error()
     # shapes the fused kernel does not run are reported as unsupported, not computed
     assert lib.p3d_qkv_project_supported(_native.F32, 192, 4, 4, 48) == 0
     assert lib.p3d_qkv_project_supported(_native.BF16, 96, 4, 4, 48) == 0

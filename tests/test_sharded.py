@@ -352,7 +352,8 @@ def _nccl_worker(rank, world, port, grid, out):
         kx, vx, skx, svx = exchange_slab(cut(kl), cut(vl), skr, svr, s)
         y_one, _ = slab_forward(cut(q), kx, vx, skx, svx, weight, bias, cut(gate), sl, sg, lay.geometry, s)
         # the peer exchange's buffers equal the NCCL batch's
-        peers = slab_peers(s, cut(kl), skr)
+        kb, kg_, _, kd = kl.shape
+        peers = slab_peers(s, kb, kg_, kd, skr.shape[2], kl.dtype, dev)
         got = [t.clone() for t in peers.exchange(cut(kl), cut(vl), skr, svr)]
         peers.release()
         same = torch.equal(y, y_one) and all(torch.equal(a, b) for a, b in zip(got, (kx, vx, skx, svx)))
