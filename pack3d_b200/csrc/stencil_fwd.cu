@@ -135,9 +135,14 @@ struct FwdParams {
   const float *kbound;  // [B*G] max_j |sk_j|, or nullptr: the global branch tracks its maximum
 };
 
-// Fixed-reference global softmax (see the softmax warps): used when every p of a row stays
-// within [2^-kFixedRange, 1]; kPolyEighths of every 8 exponential pairs go to the FMA pipe.
-constexpr float kFixedRange = 64.f;
+// Fixed-reference global softmax (see the softmax warps): used when the largest p of every row
+// is at least 2^-fixed_range, so that it is a normal number of the 16-bit type P is stored in
+// (bf16 keeps fp32's exponent range; f16's smallest normal is 2^-14, and below 2^-24 a p would
+// be stored as zero).  kPolyEighths of every 8 exponential pairs go to the FMA pipe.
+template <bool BF16>
+__device__ __forceinline__ constexpr float fixed_range() {
+  return BF16 ? 64.f : 14.f;
+}
 constexpr int kPolyEighths = 2;
 
 template <bool BF16>
@@ -205,7 +210,7 @@ __device__ __forceinline__ float exp_pack(const float *s, float m, float sc, uin
 }
 
 // exp_pack for the fixed-reference global branch: every x = s sc - msc lies in
-// [-kFixedRange, 0] (up to rounding), so no maximum, no rescale and no clamp are needed; a
+// [-fixed_range(), 0] (up to rounding), so no maximum, no rescale and no clamp are needed; a
 // share kPoly of every 8 pairs is evaluated by the polynomial on the FMA pipe, the rest on
 // the MUFU, interleaved.  Returns the row sum of p.
 template <int N, bool BF16, int kPoly>
@@ -557,16 +562,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     };
     // Global-branch reference value.  By Cauchy-Schwarz every global score of this row (raw
     // q.sk) is at most u = |q| max_j |sk_j|.  Taking the exponentials against u itself puts
-    // every p = 2^((s - u) sc) in [2^(-2 u sc), 1]: with 2 u sc <= kFixedRange for every row of
-    // the warp there is no running maximum to track, no rescale of O and no clamp in the
-    // polynomial exp2.  The softmax is the same function of the scores (only its reference
-    // point moves); otherwise, or without a bound, the warp tracks the maximum.
+    // every p = 2^((s - u) sc) in [2^(-2 u sc), 1]: with 2 u sc <= fixed_range() for every row
+    // of the warp there is no running maximum to track, no rescale of O and no clamp in the
+    // polynomial exp2, and the row's largest p is a normal number of P's storage type.  The
+    // softmax is the same function of the scores (only its reference point moves); otherwise,
+    // or without a bound, the warp tracks the maximum.
     bool fixed_g = false;
     if (p.kbound != nullptr) {
       ok = wait_warp(bar(kQFull), 0);
       if (ok) {
         const float u = sqrtf(q_row_sq<D, BF16>(q_tile, row)) * __ldg(p.kbound + bg);
-        fixed_g = __all_sync(0xffffffffu, 2.f * u * sc <= kFixedRange);
+        fixed_g = __all_sync(0xffffffffu, 2.f * u * sc <= fixed_range<BF16>());
         if (fixed_g) m_g = u;
       }
     }

@@ -140,3 +140,35 @@ def test_summary_bound_is_the_largest_summary_norm(cuda_device, dtype, bg, m, d)
     got = bound.double()
     assert torch.all(got >= want * (1 + 2.0 ** -12)), (got, want)
     assert torch.all(got <= want * (1 + 2.0 ** -9)), (got, want)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_global_branch_with_a_loose_score_bound(cuda_device, dtype):
+    """Queries orthogonal to every summary, both of norm 12: every global score is 0 while the
+    Cauchy-Schwarz bound u = |q| max|sk| is 144, so p = 2^((0 - u) log2(e) / sqrt(D)) = 2^-30
+    against the bound.  That is a normal bf16 number but below f16's range, so for f16 the
+    kernel must track the row maximum instead (the global softmax is then uniform and og the
+    summaries' mean, here 1)."""
+    layout = _layout((8, 8, 16))
+    geom = layout.geometry
+    b, h, d = 1, 2, 48
+    n = geom.num_tokens
+    inputs = grid_inputs(n, b, h, h, d, torch.float32, 11, False)
+    q = torch.zeros(b, h, n, d)
+    q[..., : d // 2] = 12.0 / (d // 2) ** 0.5       # |q| = 12 in the first half of the channels
+    kg = torch.zeros(b, h, n, d)
+    kg[..., d // 2:] = 12.0 / (d // 2) ** 0.5      # |sk| = 12 in the second half: q . sk = 0
+    vg = torch.ones(b, h, n, d)
+    inputs[0], inputs[3], inputs[4] = q, kg, vg
+    inputs = [t.to(dtype) if i < 5 else t for i, t in enumerate(inputs)]
+    y_tc, (_, _, _, og, _, lse_g) = _run(inputs, geom, cuda_device)
+    y_ix, (_, _, _, og_i, _, lg_i) = _run(inputs, geom, cuda_device, force_indexed=True)
+    torch.cuda.synchronize()
+    assert _native.device_errors() == 0
+    assert (og.float() - 1).abs().max().item() <= 2e-2
+    assert (og.float() - og_i.float()).abs().max().item() <= 2e-2
+    assert (lse_g - lg_i).abs().max().item() <= 1e-2
+    assert (y_tc.float() - y_ix.float()).abs().max().item() <= 2e-2
+    want = oracle.core_forward(*[t.float() for t in inputs[:5]], *inputs[5:], geom.neighbors, geom.blocks, 1,
+                               chunk=2048)
+    assert (y_tc.float().cpu() - want["y"].float()).abs().max().item() <= 2e-2
