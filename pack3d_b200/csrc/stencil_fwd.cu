@@ -16,10 +16,10 @@
 //                 (coordinate test, no neighbour table).  A warp whose query plane is
 //                 more than 2 planes away writes a zero P block.
 //   chunks 8..    global: 96 summaries per chunk.
-// TMEM (256 columns): one 96-column S buffer, a 48-column P buffer (16-bit pairs) and the
-// accumulator O.  The softmax warps release S as soon as it is in their registers, so the
-// QK^T MMA of chunk c+1 runs while they exponentiate chunk c, and the PV MMA of chunk c
-// runs while they work on chunk c+1.  O holds the local accumulator during chunks 0..7;
+// TMEM (256 columns): one 96-column S buffer, two 48-column P buffers (16-bit pairs; chunk c
+// uses buffer c % 2) and the accumulator O.  The softmax warps release S as soon as it is in
+// their registers, so the QK^T MMA of chunk c+1 runs while they exponentiate chunk c, and the
+// PV MMA of chunk c runs while they work on chunk c+1.  O holds the local accumulator during chunks 0..7;
 // when they are done the normalised local output is parked in shared memory, rounded to
 // the storage dtype as the reference rounds it before the mix, and O then accumulates the
 // global branch.  Two independent online softmaxes: the local one tracks its maximum (in
@@ -59,8 +59,8 @@ constexpr uint64_t kWaitNs = 2000000000ull;        // every mbarrier wait gives 
 // Chunk geometry of a radius-R stencil (R = 1 or 2): a local chunk is one halo plane of the
 // tile, a kHY x kHX (y, x) window; chunks are kKeys wide (the window rounded up to 32 keys;
 // the padding rows of every ring stage are zero and masked) and global chunks take kKeys
-// summaries.  TMEM: the S buffer [0, kKeys), the P buffer (16-bit pairs) [kKeys, 3 kKeys / 2),
-// O [3 kKeys / 2, 3 kKeys / 2 + D).
+// summaries.  TMEM: the S buffer [0, kKeys), P buffers 0 and 1 (16-bit pairs, kKeys / 2
+// columns each) [kKeys, 2 kKeys), O [2 kKeys, 2 kKeys + D).
 template <int R>
 struct Geo {
   static constexpr int kR = R;
@@ -69,8 +69,9 @@ struct Geo {
   static constexpr int kKeys = (kWin + 31) / 32 * 32;   // 96, 64
   static constexpr int kLocalChunks = kHZ;              // 8, 6 halo planes per tile
   static constexpr int kSumRows = kKeys;                // summaries per global chunk
-  static constexpr uint32_t kColS = 0, kColP = kKeys, kColO = kKeys + kKeys / 2;
+  static constexpr uint32_t kColS = 0, kColP = kKeys, kPStride = kKeys / 2, kColO = 2 * kKeys;
   static_assert(kKeys % 32 == 0 && kKeys <= 96, "chunk size must suit the MMA, TMEM and register budgets");
+  static_assert(kPStride % 16 == 0, "P buffers start on 16-column boundaries (tcgen05.st pieces)");
 };
 
 template <int D, int KEYS>
@@ -99,19 +100,23 @@ struct Cfg {
 // Barrier map (one 128-row tile; the executable model is tests/stencil_protocol.py):
 //   S(c) commits to kSFull.  The four softmax warps arrive on kSFree once they have loaded
 //   S(c) into registers, and S(c + 1) may then overwrite it -- so the next S is computed
-//   while the softmax warps still work on this one.  They arrive on kPFull once P(c) is in
-//   the P buffer; PV(c) commits to kPFree (P buffer reusable, O quiet: it may be read or
-//   rescaled until PV(c + 1) is issued) and to kEmpty[c % kStages] (both MMAs that read the
-//   ring stage of chunk c have completed: the producer may refill it).  Every parity wait
-//   has the completions before and after the awaited one ruled out.
+//   while the softmax warps still work on this one.  They arrive on kPFull[c % 2] once P(c)
+//   is in P buffer c % 2 (one barrier per buffer: the warps may finish chunk c + 1 before
+//   the MMA thread has seen chunk c's arrivals, but not chunk c + 2, whose S is issued only
+//   after PV(c)); PV(c) commits to kPFree (O quiet: it may be read or rescaled until
+//   PV(c + 1) is issued) and to kEmpty[c % kStages] (both MMAs that read the ring stage of
+//   chunk c have completed: the producer may refill it).  P buffer c % 2 needs no wait of its
+//   own: PV(c - 2), its last reader, was issued before S(c), and the kSFull commit of S(c),
+//   which the warps wait for first, arrives only once every MMA issued before it completed.
+//   Every parity wait has the completions before and after the awaited one ruled out.
 enum Bar {
   kQFull = 0,
   kFull = 1,                  // [stage]
   kEmpty = kFull + 4,         // [stage]: released by PV(c), c the chunk it held
   kSFull = kEmpty + 4,        // S(c) complete
   kSFree = kSFull + 1,        // count 4: the softmax warps loaded S(c)
-  kPFull = kSFree + 1,        // count 4: the softmax warps stored P(c)
-  kPFree = kPFull + 1,        // PV(c) complete
+  kPFull = kSFree + 1,        // [c % 2], count 4: the softmax warps stored P(c)
+  kPFree = kPFull + 2,        // PV(c) complete
   kOReady = kPFree + 1,
   kDrain = kOReady + 1,       // MMA thread: every MMA it issued has completed
   kNumBars = kDrain + 1
@@ -329,6 +334,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   constexpr int kLocalChunks = G::kLocalChunks, kSumRows = G::kSumRows;
   constexpr uint32_t kColO = G::kColO;
   using C = Cfg<D, kKeys>;
+  static_assert(kColO + D <= kTmemCols, "S, both P buffers and O must fit the CTA's TMEM columns");
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[kNumBars];
   __shared__ uint32_t tmem_holder;
@@ -366,6 +372,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(bar(kSFull), 1);
     mbar_init(bar(kSFree), kSoftmaxWarps);
     mbar_init(bar(kPFull), kSoftmaxWarps);
+    mbar_init(bar(kPFull + 1), kSoftmaxWarps);
     mbar_init(bar(kPFree), 1);
     mbar_init(bar(kOReady), 1);
     mbar_init(bar(kDrain), 1);
@@ -470,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // O += P(c) V(c); its completion frees the P buffer and O, and releases the ring stage.
       auto issue_pv = [&](int c) {
         const uint64_t bv = desc_v + ((uint32_t)((c % C::kStages) * C::kStageBytes + C::kKeyBytes) >> 4);
-        const uint32_t t_p = tmem + G::kColP, t_o = tmem + kColO;
+        const uint32_t t_p = tmem + G::kColP + (uint32_t)(c & 1) * G::kPStride, t_o = tmem + kColO;
         const bool first = (c == 0) || (c == kLocalChunks);  // O restarts for the global branch
 #pragma unroll
         for (int j = 0; j < kKeys / 16; ++j)
@@ -495,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (!ok) break;
           issue_s(c + 1);
         }
-        ok = wait_bar(kPFull, c & 1);
+        ok = wait_bar(kPFull + (c & 1), (c >> 1) & 1);
         if (!ok) break;
         issue_pv(c);
       }
@@ -550,9 +557,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (all) tc_fence_after();
       return all;
     };
-    // Completion c of kPFree: PV(c) has completed, so the P buffer may be rewritten and O
-    // read or rescaled (until this warp's next kPFull arrival lets PV(c + 1) be issued).
-    // Completion c + 1 needs this warp's P of chunk c + 1, so the parity wait is exact.
+    // Completion c of kPFree: PV(c) has completed, so O may be read or rescaled (until this
+    // warp's next kPFull arrival lets PV(c + 1) be issued).  A warp that waits for it has
+    // waited for completion c - 1 at its previous chunk (it skips these waits only from its
+    // first fixed-reference global chunk on), and completion c + 1 needs this warp's P of
+    // chunk c + 1, so the parity wait is exact.
     auto wait_pfree = [&](int c) -> bool { return wait_warp(bar(kPFree), c & 1); };
     // This warp's rows of S are in registers: S(c + 1) may overwrite the S buffer.
     auto release_s = [&]() {
@@ -641,17 +650,20 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int i = 0; i < kKeys / 2; ++i) pk[i] = 0u;   // a zero P block: no key of this plane is in range
       }
-      // The P buffer is free, and O may be rescaled, once PV(ch - 1) has completed.
-      if (ch >= 1) {
+      // P buffer ch % 2 is free: its last reader PV(ch - 2) completed before S(ch) did (see
+      // the barrier map).  O may be rescaled only once PV(ch - 1) has completed: the warp
+      // waits for that on every chunk except the global chunks of the fixed-reference path,
+      // which never rescale (and, so that every kPFree parity wait stays exact, never wait).
+      if (ch >= 1 && !(fixed_g && !local)) {
         ok = wait_pfree(ch - 1);
         if (!ok) break;
       }
       if (rescale) rescale_span<kColO, D>(factor, t_tile);
-      st_span<G::kColP, kKeys / 2>(t_tile, pk);
+      st_span<G::kColP, kKeys / 2>(t_tile + (uint32_t)(ch & 1) * G::kPStride, pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kPFull));
+      if (lane == 0) mbar_arrive(bar(kPFull + (ch & 1)));
     }
     // ---- epilogue: normalise the global branch, mix, store through the row map
     if (ok) ok = wait_warp(bar(kOReady), 0);

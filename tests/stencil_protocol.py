@@ -483,7 +483,7 @@ def fwd1_mma(state, skip_sfree=False):
                 yield from waits("sfree", c)
             issue_s(c + 1)
             yield ("step", None)
-        yield from waits("pfull", c)
+        yield from waits(f"pfull{c % 2}", c // 2)     # one barrier per P buffer
         if len(state.p_stored.get((0, c), ())) != WARPS:
             raise ProtocolError(f"PV({c}) issued before all softmax warps stored P")
         state.mma_queue.append(("PV", 0, c))
@@ -499,8 +499,15 @@ def fwd1_mma(state, skip_sfree=False):
 WARPS = 4
 
 
-def fwd1_softmax(state, w, rng):
+def fwd1_softmax(state, w, rng, p_buffers=2, wait_on_rescale_only=False):
+    """A softmax warp of the forward kernel.  P(c) goes to P buffer c % p_buffers; its last
+    reader, PV(c - p_buffers), must have completed (with two buffers the kernel relies on the
+    kSFull commit of S(c), issued after PV(c - 2)).  The warp waits for PV(c - 1) on every
+    chunk (its O may be rescaled after that) except the global chunks of a warp on the
+    fixed-reference path, which never rescale; the warp's path is drawn at random.
+    ``wait_on_rescale_only`` is the broken variant that skips the wait unless it rescales."""
     n = state.n_chunks
+    fixed = rng.random() < 0.5
 
     def waits(name, completion):
         while not _wait(state, name, completion & 1, completion):
@@ -509,7 +516,7 @@ def fwd1_softmax(state, w, rng):
     def pv_done(c):
         yield from waits("pfree", c)
         if ("PV", 0, c) not in state.mma_done:
-            raise ProtocolError(f"P buffer or O touched before PV({c}) completed")
+            raise ProtocolError(f"O touched before PV({c}) completed")
         if (0, c + 1) in state.pv_issued:
             raise ProtocolError(f"O touched after PV({c + 1}) was issued")
 
@@ -524,27 +531,37 @@ def fwd1_softmax(state, w, rng):
         state.s_loaded.setdefault(ch, set()).add(w)
         state.bar("sfree").arrive()
         yield ("step", None)
-        if ch >= 1:
-            yield from pv_done(ch - 1)                 # P buffer free; O may be rescaled now
-            if rng.random() < 0.3:
-                yield ("step", None)                   # a data-dependent rescale of O
+        local = ch < LOCAL_CHUNKS
+        rescale = ch >= 1 and not (fixed and not local) and rng.random() < 0.3
+        if ch >= 1 and (rescale if wait_on_rescale_only else not (fixed and not local)):
+            yield from pv_done(ch - 1)
+        if rescale:
+            yield ("step", None)                       # a data-dependent rescale of O
+        last_reader = ch - p_buffers
+        if last_reader >= 0 and ("PV", 0, last_reader) not in state.mma_done:
+            raise ProtocolError(f"P buffer {ch % p_buffers} overwritten while PV({last_reader}) may read it")
         state.p_stored.setdefault((0, ch), set()).add(w)
-        state.bar("pfull").arrive()
+        state.bar(f"pfull{ch % 2}").arrive()
         yield ("step", None)
     yield from waits("oready", 0)
     if ("PV", 0, n - 1) not in state.mma_done:
         raise ProtocolError("O read before the last PV completed")
 
 
-def run_fwd(n_chunks=14, stages=4, seed=0, max_steps=400000, skip_sfree=False):
+def run_fwd(n_chunks=14, stages=4, seed=0, max_steps=400000, skip_sfree=False, p_buffers=2,
+            wait_on_rescale_only=False):
     """Replay one random interleaving of the (one-tile) forward kernel's protocol.
 
-    ``skip_sfree`` replays a broken variant whose MMA thread overwrites S without waiting
-    for the softmax warps to load it."""
+    Broken variants: ``skip_sfree`` (the MMA thread overwrites S without waiting for the
+    softmax warps to load it), ``p_buffers=1`` (one P buffer, written without waiting for the
+    PV that reads it on the fixed-reference global chunks) and ``wait_on_rescale_only`` (the
+    kPFree waits skipped on every chunk without a rescale, which makes the parity waits that
+    remain ambiguous)."""
     rng = random.Random(seed)
     state = State(n_chunks=n_chunks, stages=stages)
     state.ordered_by_acc = {"S": lambda op: "s", "PV": lambda op: "o"}  # S and O: separate accumulators
-    bars = {"qfull": 1, "drain": 1, "oready": 1, "sfull": 1, "sfree": WARPS, "pfull": WARPS, "pfree": 1}
+    bars = {"qfull": 1, "drain": 1, "oready": 1, "sfull": 1, "sfree": WARPS, "pfull0": WARPS, "pfull1": WARPS,
+            "pfree": 1}
     for s in range(4):
         bars[f"full{s}"] = 1
         bars[f"empty{s}"] = 1
@@ -552,7 +569,8 @@ def run_fwd(n_chunks=14, stages=4, seed=0, max_steps=400000, skip_sfree=False):
     state.bar("qfull").arrive(tx=0)
     roles = {"producer": fwd1_producer(state), "mma": fwd1_mma(state, skip_sfree)}
     for w in range(WARPS):
-        roles[f"softmax{w}"] = fwd1_softmax(state, w, random.Random(rng.random()))
+        roles[f"softmax{w}"] = fwd1_softmax(state, w, random.Random(rng.random()), p_buffers,
+                                                wait_on_rescale_only)
     return _schedule(state, roles, rng, max_steps)
 
 

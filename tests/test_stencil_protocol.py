@@ -3,7 +3,8 @@
 The kernel's producer / MMA / softmax roles are replayed under many random
 interleavings with the hardware's parity-wait semantics.  The shipped barrier map must
 survive all of them; the earlier stage-release scheme, which let the producer pass its
-first release waits before the MMAs had finished with the stage, must be caught.
+first release waits before the MMAs had finished with the stage, and the broken variants
+of the two-P-buffer scheme must be caught.
 """
 import pytest
 
@@ -24,6 +25,32 @@ def test_model_rejects_overwriting_s_before_the_warps_load_it():
             sp.run_fwd(n_chunks=12, stages=4, seed=seed, skip_sfree=True)
         except sp.ProtocolError as err:
             assert "before the softmax warps loaded it" in str(err) or "overwritten before" in str(err)
+            failures += 1
+    assert failures > 0
+
+
+def test_model_rejects_one_p_buffer_without_a_wait():
+    """With a single P buffer, storing P(c) needs PV(c - 1) to have completed; the kSFull
+    commit that covers the two-buffer scheme does not cover that."""
+    failures = 0
+    for seed in range(100):
+        try:
+            sp.run_fwd(n_chunks=12, stages=4, seed=seed, p_buffers=1)
+        except sp.ProtocolError as err:
+            assert "may read it" in str(err)
+            failures += 1
+    assert failures > 0
+
+
+def test_model_rejects_kpfree_waits_on_rescale_only():
+    """Skipping the wait for PV(c - 1) on every chunk without a rescale lets kPFree run more
+    than one completion ahead of a later parity wait."""
+    failures = 0
+    for seed in range(300):
+        try:
+            sp.run_fwd(n_chunks=12, stages=4, seed=seed, wait_on_rescale_only=True)
+        except sp.ProtocolError as err:
+            assert "passed at" in str(err) or "before PV" in str(err)
             failures += 1
     assert failures > 0
 
