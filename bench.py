@@ -535,6 +535,42 @@ def config2_measure(steps, device):
     return out
 
 
+def sharded_phases(layer, x, layout, steps, stream, flush, max_over_ranks):
+    """Per-phase CUDA-event times (ms, median over ``steps`` eager steps, then max over ranks)
+    of one rank's sharded inference step, the same calls ``sharded_layer_forward`` makes:
+    glue (LayerNorm, fused projection writing kl / vl into the peer region, gate), pooling,
+    the peer exchange (credit wait, push, arrival wait: includes waiting for the slowest
+    peer), the slab kernel (summary bound + attention), and release + output projection."""
+    from pack3d_b200.sharded import pool_summaries, slab_forward, slab_peers
+    b, g, d = x.shape[0], layer.kv_heads, layer.head_dim
+    names = ("glue", "pooling", "exchange", "slab_attention", "output")
+    samples = {k: [] for k in names}
+    with torch.inference_mode():
+        peers = slab_peers(layout.slabs, b, g, d, layout.geometry.num_summaries, x.dtype, x.device)
+        for _ in range(steps):
+            flush()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+            ev[0].record(stream)
+            xr, q, kl, vl, kg, vg, gate = layer._inference_glue(x, layout.coords, layout.grid_shape,
+                                                                kv_out=peers.kv_out())
+            ev[1].record(stream)
+            skr, svr = pool_summaries(kg, vg, layer.pool_weight, layer.slot_bias, layout.geometry, layer.temperature)
+            ev[2].record(stream)
+            kl_ext, vl_ext, sk, sv = peers.exchange(kl, vl, skr, svr)
+            ev[3].record(stream)
+            y, _ = slab_forward(q, kl_ext, vl_ext, sk, sv, layer.pool_weight, layer.slot_bias, gate,
+                                layer.local_scale, layer.global_scale, layout.geometry, layout.slabs,
+                                layer.temperature, y_rows=True)
+            ev[4].record(stream)
+            peers.release()
+            layer._out_residual(xr, y)
+            ev[5].record(stream)
+            ev[5].synchronize()
+            for i, k in enumerate(names):
+                samples[k].append(ev[i].elapsed_time(ev[i + 1]))
+    return {k: round(max_over_ranks(statistics.median(v)), 4) for k, v in samples.items()}
+
+
 def run_sharded(args, rank, world, device):
     """N > 1: the config-1 field split into z-slabs, one per rank (the same 64^3 field at
     every N: strong scaling).  Each rank runs the layer on its planes with the halo
@@ -617,6 +653,10 @@ def run_sharded(args, rank, world, device):
         torch.distributed.barrier()
         kernel_ms = max_over_ranks(statistics.median(timed_steps(kernel, max(args.steps, 10), stream)))
 
+    torch.cuda.synchronize(device)
+    torch.distributed.barrier()
+    phases = sharded_phases(layer, x, layout, max(args.steps, 10), stream, flush, max_over_ranks)
+
     x_host = x.detach().cpu().pin_memory()
     torch.cuda.synchronize(device)
     torch.distributed.barrier()
@@ -666,6 +706,8 @@ def run_sharded(args, rank, world, device):
                 "d2h_bytes_per_step": x_host.numel() * x_host.element_size() * world,   # y: x's shape and dtype
                 "pipelined": "copy-in, compute and copy-out on three streams per rank; double-buffered, every "
                              "step copies its own input in and result out inside the timed region"},
+        "phases_ms": dict(phases, note="eager step (no CUDA graph), each phase's median over ranks' "
+                                        "steps, max over ranks; the graphed step above is the headline"),
         # per step: layer norm, fused projection, gate pairs, pooling, credit wait, push,
         # arrival wait, summary bound, slab forward, credit signal
         "gpu_launches": 10 * args.steps,
