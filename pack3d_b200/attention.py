@@ -98,9 +98,10 @@ class PACK3DAttention(nn.Module):
             coords = layout.coords.to(device=x.device, dtype=torch.int64).contiguous()
             if self.fused_projection and glue.project_supported(x, self.to_q.weight, self.to_kv.weight, self.heads,
                                                                 self.kv_heads, self.head_dim):
-                q, kl, vl, kg, vg = glue.qkv_project(x, self.to_q.weight, self.to_kv.weight, coords, phases, pairs,
-                                                     layout.grid_shape, self.heads, self.kv_heads, self.head_dim)
-                gate_logits = self.gate(x)
+                q, kl, vl, kg, vg, gate_logits = glue.qkv_project(x, self.to_q.weight, self.to_kv.weight,
+                                                                  self.gate.weight, self.gate.bias, coords, phases,
+                                                                  pairs, layout.grid_shape, self.heads,
+                                                                  self.kv_heads, self.head_dim)
             else:
                 qp, kvp, gate_logits = glue.projections(x, self.to_q, self.to_kv, self.gate)
                 q, kl, vl, kg, vg = glue.qkv_split(qp, kvp, coords, phases, pairs,

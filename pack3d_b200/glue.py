@@ -164,37 +164,47 @@ def project_split_raw(x, wq, wkv, coords, phases, pairs, extents, heads, kv_head
 
 
 class _QKVProject(torch.autograd.Function):
-    """The projections (to_q, to_kv: no bias) and the split in one kernel; backward: the merge,
-    then dx = dqp Wq + dkvp Wkv (the second GEMM accumulating into the first) and the weight
-    gradients."""
+    """The projections (to_q, to_kv: no bias) and the split in one kernel, and the gate logits
+    (``x Wg^T + bg``) on the same input; backward: the merge, then dx = dqp Wq + dkvp Wkv +
+    dgl Wg with each GEMM accumulating into the first one's output (no elementwise add of
+    separate input gradients), and the weight gradients."""
 
     @staticmethod
-    def forward(ctx, x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, head_dim):
+    def forward(ctx, x, wq, wkv, wg, bg, coords, phases, pairs, extents, heads, kv_heads, head_dim):
         x = x.contiguous()
         outs = project_split_raw(x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, head_dim)
-        ctx.save_for_backward(x, wq, wkv, coords, phases)
+        b, n, dim = x.shape
+        gl = torch.addmm(bg, x.view(b * n, dim), wg.t()).view(b, n, -1)
+        ctx.save_for_backward(x, wq, wkv, wg, coords, phases)
         ctx.meta = (pairs, extents, heads, kv_heads, head_dim)
-        return outs
+        return (*outs, gl)
 
     @staticmethod
     @once_differentiable
-    def backward(ctx, dq, dkl, dvl, dkg, dvg):
-        x, wq, wkv, coords, phases = ctx.saved_tensors
+    def backward(ctx, dq, dkl, dvl, dkg, dvg, dgl):
+        x, wq, wkv, wg, coords, phases = ctx.saved_tensors
         pairs, extents, heads, kv_heads, head_dim = ctx.meta
         b, n, dim = x.shape
         dqp, dkvp = _merge(dq, dkl, dvl, dkg, dvg, coords, phases, pairs, extents, heads, kv_heads, head_dim, b, n,
                            x.dtype)
         dqp2, dkvp2, x2 = dqp.view(b * n, -1), dkvp.view(b * n, -1), x.view(b * n, dim)
         dx = torch.mm(dqp2, wq).addmm_(dkvp2, wkv)
-        dwq = torch.mm(dqp2.t(), x2) if ctx.needs_input_grad[1] else None
-        dwkv = torch.mm(dkvp2.t(), x2) if ctx.needs_input_grad[2] else None
-        return dx.view(b, n, dim), dwq, dwkv, None, None, None, None, None, None, None
+        dgl2 = dgl.reshape(b * n, -1) if dgl is not None else None
+        if dgl2 is not None:
+            dx.addmm_(dgl2, wg)
+        need = ctx.needs_input_grad
+        dwq = torch.mm(dqp2.t(), x2) if need[1] else None
+        dwkv = torch.mm(dkvp2.t(), x2) if need[2] else None
+        dwg = torch.mm(dgl2.t(), x2) if dgl2 is not None and need[3] else None
+        dbg = dgl2.sum(0) if dgl2 is not None and need[4] else None
+        return dx.view(b, n, dim), dwq, dwkv, dwg, dbg, None, None, None, None, None, None, None
 
 
-def qkv_project(x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, head_dim):
-    """Differentiable ``x -> (x Wq^T, x Wkv^T) -> split``: ``(q, kl, vl, kg, vg)`` head-major,
-    q / kl / kg rotated, through ``p3d_qkv_project`` (check ``project_supported`` first)."""
-    return _QKVProject.apply(x, wq, wkv, coords, phases, tuple(int(p) for p in pairs),
+def qkv_project(x, wq, wkv, wg, bg, coords, phases, pairs, extents, heads, kv_heads, head_dim):
+    """Differentiable ``x -> (x Wq^T, x Wkv^T) -> split`` and the gate logits ``x Wg^T + bg``:
+    ``(q, kl, vl, kg, vg, gate_logits)``, the split head-major with q / kl / kg rotated,
+    through ``p3d_qkv_project`` (check ``project_supported`` first)."""
+    return _QKVProject.apply(x, wq, wkv, wg, bg, coords, phases, tuple(int(p) for p in pairs),
                              tuple(int(e) for e in extents), int(heads), int(kv_heads), int(head_dim))
 
 
