@@ -71,6 +71,7 @@ struct ProjArgs {
   void *out[5];                 // q [B,H,N,D], kl, vl, kg, vg [B,G,N,D]
   const int64_t *coords;        // [N, 3]
   int pairs[3], start[3];
+  int ext[3];                   // coordinate extents (rows of the phase table per axis)
   const float *phases;
   int table_floats;             // floats in the phase table
   int raster_qkv, ey, ex;       // q, kl, vl rows at each token's raster index (ey x ex planes)

@@ -17,7 +17,8 @@
 // Roles (576 threads): warp 0 TMA producer (W slice once, X tiles through a 2-stage ring),
 // warp 1 MMA issuer (Z tile into one of two TMEM accumulators), warps 2-17 epilogue: a token
 // row (TMEM lane) per thread, four warps per lane quarter splitting the group's heads.  The
-// RoPE phase table is staged in shared memory once per CTA; a token's coordinates are fetched
+// RoPE phase table is staged in shared memory once per CTA (rows at an odd pitch, so that a
+// warp's tokens read it without bank conflicts); a token's coordinates are fetched
 // a tile ahead, so the epilogue does not wait on global loads.  Every wait is bounded (2 s): on a timeout the kernel records an
 // error bit (p3d_device_errors), drains its copies and MMAs and frees TMEM.
 #include "common.cuh"
@@ -64,20 +65,27 @@ struct ProjParams {
   const int64_t *coords;
   int pairs[3], start[3];
   const float *phases;
-  int table_floats;    // 2 * (ez pz + ey py + ex px); staged in shared memory when <= kMaxTableFloats
+  int table_floats;    // 2 * (ez pz + ey py + ex px)
+  // The shared-memory copy of the table: the rows of axis a start at entry tstart[a] and are
+  // tpitch[a] = pairs[a] | 1 entries apart (an odd pitch: the 32 tokens of a warp, consecutive
+  // along x, then read their (cos, sin) from distinct banks instead of 16 lanes per bank);
+  // staged when its smem_floats <= kMaxTableFloats.
+  int tstart[3], tpitch[3], smem_floats;
   int raster_qkv, ey, ex;  // q, kl, vl rows at each token's raster index (c0 ey + c1) ex + c2
   int64_t kv_rows, kv_row0;  // kl, vl: [B, G, kv_rows, D], token row n at kv_row0 + n
 };
 
-// (cos, sin) of rotation pair `pair` of a token at coordinates c, from the table `tab`.
-__device__ __forceinline__ float2 pair_cs(const ProjParams &p, const float *tab, const int (&c)[3], int pair) {
+// (cos, sin) of rotation pair `pair` of a token at coordinates c, from the table `tab` whose
+// axis-a rows start at entry st[a] and are pitch[a] entries apart.
+__device__ __forceinline__ float2 pair_cs(const ProjParams &p, const float *tab, const int *st, const int *pitch,
+                                          const int (&c)[3], int pair) {
   int entry;
   if (pair < p.pairs[0]) {
-    entry = p.start[0] + c[0] * p.pairs[0] + pair;
+    entry = st[0] + c[0] * pitch[0] + pair;
   } else if (pair < p.pairs[0] + p.pairs[1]) {
-    entry = p.start[1] + c[1] * p.pairs[1] + (pair - p.pairs[0]);
+    entry = st[1] + c[1] * pitch[1] + (pair - p.pairs[0]);
   } else {
-    entry = p.start[2] + c[2] * p.pairs[2] + (pair - p.pairs[0] - p.pairs[1]);
+    entry = st[2] + c[2] * pitch[2] + (pair - p.pairs[0] - p.pairs[1]);
   }
   return *reinterpret_cast<const float2 *>(tab + 2 * entry);
 }
@@ -151,9 +159,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tx);
     prefetch_tmap(is_q ? &twq : &twkv);
   }
-  const bool table_in_smem = p.table_floats <= kMaxTableFloats;
-  if (table_in_smem)
-    for (int i = threadIdx.x; i < p.table_floats; i += kThreads) table[i] = p.phases[i];
+  const bool table_in_smem = p.smem_floats <= kMaxTableFloats;
+  if (table_in_smem) {
+    // entry e of the table (axis a, coordinate c, pair k: e = start[a] + c pairs[a] + k) goes
+    // to tstart[a] + c tpitch[a] + k
+    for (int e = threadIdx.x; 2 * e < p.table_floats; e += kThreads) {
+      const int a = e < p.start[1] ? 0 : e < p.start[2] ? 1 : 2;
+      const int local = e - p.start[a], c = local / p.pairs[a], k = local - c * p.pairs[a];
+      reinterpret_cast<float2 *>(table)[p.tstart[a] + c * p.tpitch[a] + k] =
+          reinterpret_cast<const float2 *>(p.phases)[e];
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -226,6 +242,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quarter * 32 + lane;              // token row within the tile = TMEM lane
     const uint32_t t_lanes = tmem + ((uint32_t)(quarter * 32) << 16);
     const float *tab = table_in_smem ? table : p.phases;
+    int tst[3], tpitch[3];  // row start and pitch (entries) of each axis in `tab`
+#pragma unroll
+    for (int ax = 0; ax < 3; ++ax) {
+      tst[ax] = table_in_smem ? p.tstart[ax] : p.start[ax];
+      tpitch[ax] = table_in_smem ? p.tpitch[ax] : p.pairs[ax];
+    }
     const int head_rows = is_q ? p.heads : 4 * p.kv_heads;
     // coordinates of this thread's token in tile i (fetched one tile ahead)
     auto fetch = [&](int i, int (&c)[3]) {
@@ -277,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // offset from the row of its axis)
           const float *row_axis[3];
 #pragma unroll
-          for (int ax = 0; ax < 3; ++ax) row_axis[ax] = tab + 2 * (p.start[ax] + c3[ax] * p.pairs[ax]);
+          for (int ax = 0; ax < 3; ++ax) row_axis[ax] = tab + 2 * (tst[ax] + c3[ax] * tpitch[ax]);
 #pragma unroll
           for (int q2 = 0; q2 < D / 2; ++q2) {
             const float2 e_o = unpack_pair<BF16>(packed[q2]);
@@ -286,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int ax = Balanced<D>::axis_of(q2);
               c = *reinterpret_cast<const float2 *>(row_axis[ax] + 2 * (q2 - Balanced<D>::first(ax)));
             } else {
-              c = pair_cs(p, tab, c3, q2);
+              c = pair_cs(p, tab, tst, tpitch, c3, q2);
             }
             const float even = __fsub_rn(__fmul_rn(e_o.x, c.x), __fmul_rn(e_o.y, c.y));
             const float odd = __fadd_rn(__fmul_rn(e_o.x, c.y), __fmul_rn(e_o.y, c.x));
@@ -359,10 +381,15 @@ int launch_proj(const ProjArgs &a, cudaStream_t stream) {
   p.kv_rows = a.kv_rows;
   p.kv_row0 = a.kv_row0;
   p.coords = a.coords;
+  int tstart = 0;
   for (int i = 0; i < 3; ++i) {
     p.pairs[i] = a.pairs[i];
     p.start[i] = a.start[i];
+    p.tpitch[i] = a.pairs[i] | 1;
+    p.tstart[i] = tstart;
+    tstart += a.ext[i] * p.tpitch[i];
   }
+  p.smem_floats = 2 * tstart;
   p.phases = a.phases;
   p.table_floats = a.table_floats;
   p.raster_qkv = a.raster_qkv;
@@ -486,6 +513,9 @@ extern "C" int p3d_qkv_project(const void *x, const void *wq, const void *wkv, v
   a.start[0] = 0;
   a.start[1] = ez * pz;
   a.start[2] = ez * pz + ey * py;
+  a.ext[0] = ez;
+  a.ext[1] = ey;
+  a.ext[2] = ex;
   a.phases = phases;
   a.table_floats = 2 * (ez * pz + ey * py + ex * px);
   return launch_proj_split(a, static_cast<cudaStream_t>(stream));
