@@ -533,6 +533,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int qz = w, qy = lane >> 3, qx = lane & 7;
     const int zq = z0 + qz, yq = y0 + qy, xq = x0 + qx;
     const bool row_ok = zq < p.Z && yq < p.Y && xq < p.X;
+    // The row's storage index and gate, loaded now so that the epilogue does not wait on them.
+    int64_t rr = 0, grow = 0;
+    float gate = 0.f;
+    if (row_ok) {
+      rr = ((int64_t)zq * p.Y + yq) * p.X + xq;
+      if (p.map) rr = p.map[rr];
+      grow = (int64_t)bh * p.tokens + rr;
+      gate = load_any(p.gate, p.gate_dtype, grow);
+    }
     uint32_t *park = reinterpret_cast<uint32_t *>(ol_park + (size_t)row * D * 2);
     // keys of the halo window inside this query's cube and inside the volume
     uint32_t mask[kKeys / 32] = {};
@@ -672,10 +681,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       ld_span<kColO, D>(t_tile, og);
       tmem_wait_ld();
       if (row_ok) {
-        int64_t rr = ((int64_t)zq * p.Y + yq) * p.X + xq;
-        if (p.map) rr = p.map[rr];
-        const int64_t grow = (int64_t)bh * p.tokens + rr;
-        const float gate = load_any(p.gate, p.gate_dtype, grow);
         const float inv_g = 1.f / l_g;
         uint32_t packed_y[D / 2], packed_g[D / 2];
 #pragma unroll
