@@ -957,13 +957,17 @@ __global__ void __launch_bounds__(kKvThreads, 2)
       const uint32_t rows = (uint32_t)min(kGCols, p.tokens - n0);
       // -lse log2(e) and -Delta of the chunk's queries, formed once here rather than by every
       // softmax lane (columns past N: zeros, masked there).  The loads go out before the
-      // stage wait.
+      // stage wait and are first used after the chunk's copies are issued.
       float l[kGCols / 32], dl[kGCols / 32];
 #pragma unroll
       for (int k = 0; k < kGCols / 32; ++k) {
         const int j = lane + 32 * k;
-        l[k] = j < (int)rows ? -__ldg(p.lse_g + r0 + j) * kLog2e : 0.f;
-        dl[k] = j < (int)rows ? -__ldg(p.delta_g + r0 + j) : 0.f;
+        l[k] = -0.f;
+        dl[k] = -0.f;
+        if (j < (int)rows) {
+          l[k] = __ldg(p.lse_g + r0 + j);
+          dl[k] = __ldg(p.delta_g + r0 + j);
+        }
       }
       if (!wait_stage()) return false;
       if (lane == 0) {
@@ -976,8 +980,8 @@ __global__ void __launch_bounds__(kKvThreads, 2)
       float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kChunkBytes);
 #pragma unroll
       for (int k = 0; k < kGCols / 32; ++k) {
-        vals[lane + 32 * k] = l[k];
-        vals[kGCols + lane + 32 * k] = dl[k];
+        vals[lane + 32 * k] = -l[k] * kLog2e;
+        vals[kGCols + lane + 32 * k] = -dl[k];
       }
       return true;
     };
@@ -1188,9 +1192,10 @@ __global__ void __launch_bounds__(kKvThreads, 2)
     auto chunk = [&](int ch, int s, auto wait_stage) -> bool {
       const uint32_t stage = ring + s * C::kStageBytes, full = smem_u32(&bars[kVFull + s]);
       const int bh = chunk_head(ch), zp = p.cz0 + z0 - R + chunk_plane(ch), hy0 = kRowsH * (ch % kParts);
-      // -lse log2(e) and -Delta of the chunk's queries (column j: window row hy0 + j / kHX,
-      // column j % kHX); -inf and 0 outside the volume and on the padding columns (P = 0).
-      // The loads go out before the stage wait.
+      // lse and Delta of the chunk's queries (column j: window row hy0 + j / kHX, column
+      // j % kHX); +inf and -0 outside the volume and on the padding columns (P = 0).  The loads
+      // go out before the stage wait and are first used after the chunk's copies are issued,
+      // so the copies do not wait for them.
       constexpr int kPer = kKvCols / 32;
       float l[kPer], dl[kPer];
 #pragma unroll
@@ -1198,14 +1203,14 @@ __global__ void __launch_bounds__(kKvThreads, 2)
         const int j = lane + 32 * k;
         const int qy = y0 - R + hy0 + j / kHX, qx = x0 - R + j % kHX;
         const bool in = j < kWin && zp >= 0 && zp < p.Zg && qy >= 0 && qy < p.Y && qx >= 0 && qx < p.X;
-        l[k] = -__builtin_huge_valf();
-        dl[k] = 0.f;
+        l[k] = __builtin_huge_valf();
+        dl[k] = -0.f;
         if (in) {
           int64_t r = ((int64_t)(zp - p.xz0) * p.Y + qy) * p.X + qx;
           if (p.map) r = __ldg(p.map + r);
           const int64_t row = (int64_t)bh * p.xtokens + r;
-          l[k] = -__ldg(p.lse_l + row) * kLog2e;
-          dl[k] = -__ldg(p.delta_l + row);
+          l[k] = __ldg(p.lse_l + row);
+          dl[k] = __ldg(p.delta_l + row);
         }
       }
       if (!wait_stage()) return false;
@@ -1219,9 +1224,9 @@ __global__ void __launch_bounds__(kKvThreads, 2)
       }
       float *vals = reinterpret_cast<float *>(ring_ptr + (size_t)s * C::kStageBytes + 2 * C::kChunkBytes);
 #pragma unroll
-      for (int k = 0; k < kPer; ++k) {
-        vals[lane + 32 * k] = l[k];
-        vals[kKvCols + lane + 32 * k] = dl[k];
+      for (int k = 0; k < kPer; ++k) {  // -lse log2(e) (-inf where masked) and -Delta
+        vals[lane + 32 * k] = -l[k] * kLog2e;
+        vals[kKvCols + lane + 32 * k] = -dl[k];
       }
       return true;
     };
