@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define P3D_ABI_VERSION 4
+#define P3D_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define P3D_API __attribute__((visibility("default")))
@@ -170,6 +170,11 @@ P3D_API int p3d_qkv_project(const void *x, const void *wq, const void *wkv, void
  * p3d_layer_norm_bwd: the backward of p3d_layer_norm (nn.LayerNorm, attention.py:64): dx
  *   [rows, dim] in dtype, dweight and dbias [dim] fp32 (sums over rows in fixed order,
  *   bitwise repeatable); workspace of p3d_layer_norm_bwd_workspace(rows, dim) bytes.
+ * p3d_layer_norm_bwd_residual: p3d_layer_norm_bwd with dres [rows, dim] (dtype), the gradient
+ *   that reaches the LayerNorm's input through the layer's outer residual (attention.py:64 and
+ *   :89, `residual + to_out(...)` with `x = norm(residual)`): dx = round(LayerNorm dx) + dres,
+ *   rounded to dtype -- the same bits as autograd's sum of the two gradients, in one pass.
+ *   Same workspace.
  */
 P3D_API int p3d_qkv_merge(const void *dq, const void *dkl, const void *dvl, const void *dkg, const void *dvg,
                   void *dqp, void *dkvp, int dtype, int batch, int heads, int kv_heads, int tokens, int head_dim,
@@ -179,6 +184,9 @@ P3D_API size_t p3d_layer_norm_bwd_workspace(int64_t rows, int dim);
 P3D_API int p3d_layer_norm_bwd(const void *x, const void *weight, const void *dy, void *dx, float *dweight,
                        float *dbias, int dtype, int64_t rows, int dim, float eps, void *workspace,
                        size_t workspace_bytes, void *stream);
+P3D_API int p3d_layer_norm_bwd_residual(const void *x, const void *weight, const void *dy, const void *dres,
+                                void *dx, float *dweight, float *dbias, int dtype, int64_t rows, int dim,
+                                float eps, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * Geometry tables (host code, no GPU): the native builders behind pack3d_b200.geometry for

@@ -92,6 +92,8 @@ _SIGNATURES = {
     "p3d_layer_norm_bwd_workspace": (ctypes.c_size_t, [_c_i64, _c_int]),
     "p3d_layer_norm_bwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_i64, _c_int, _c_f32, _vp,
                                     ctypes.c_size_t, _vp]),
+    "p3d_layer_norm_bwd_residual": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_i64, _c_int, _c_f32,
+                                             _vp, ctypes.c_size_t, _vp]),
     "p3d_pool_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _c_int,
                               _c_int, _c_int, _c_int, _c_int, _c_f32, _vp]),
     "p3d_attn_fwd": (_c_int, [ctypes.POINTER(Operator), _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_uint,

@@ -94,7 +94,9 @@ class PACK3DAttention(nn.Module):
         if phases is not None:
             # the fused training glue: LayerNorm and the projection split (with RoPE) and their
             # backward halves in the library kernels (pack3d_b200.glue)
-            x = glue.layer_norm(x, self.norm)
+            # the residual operand is the LayerNorm's second output: both gradients of x meet in
+            # one backward kernel (p3d_layer_norm_bwd_residual) instead of an extra add
+            x, residual = glue.layer_norm_residual(x, self.norm)
             coords = layout.coords.to(device=x.device, dtype=torch.int64).contiguous()
             if self.fused_projection and glue.project_supported(x, self.to_q.weight, self.to_kv.weight, self.heads,
                                                                 self.kv_heads, self.head_dim):

@@ -41,6 +41,15 @@ __device__ __forceinline__ void store8(T *dst, const float (&v)[8]) {
   *reinterpret_cast<uint4 *>(dst) = raw;
 }
 
+// o = round(o) + r in fp32: the LayerNorm input gradient rounded to the storage type, then the
+// residual branch's gradient added as a separate elementwise add of two T tensors would (the
+// caller's store rounds the sum), so the fused form is bit-identical to the two-step one.
+template <typename T>
+__device__ __forceinline__ void add_rounded8(float (&o)[8], const float (&r)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = to_f32<T>(from_f32<T>(o[i])) + r[i];
+}
+
 // ---------------------------------------------------------------------------- LayerNorm
 template <typename T, int kChunks>
 __global__ void __launch_bounds__(kWarps * 32)
@@ -95,10 +104,10 @@ __global__ void __launch_bounds__(kWarps * 32)
 // (reduced afterwards in fixed order: bitwise-repeatable).
 constexpr int kLnBwdBlocks = 1024;  // at most 8192 warps: the partials' row count
 
-template <typename T, int kChunks>
+template <typename T, int kChunks, bool kRes>
 __global__ void __launch_bounds__(kWarps * 32)
-    layer_norm_bwd_kernel(const T *x, const T *weight, const T *dy, T *dx, float *dw_part, float *db_part,
-                          int64_t rows, int dim, float eps) {
+    layer_norm_bwd_kernel(const T *x, const T *weight, const T *dy, const T *dres, T *dx, float *dw_part,
+                          float *db_part, int64_t rows, int dim, float eps) {
   const int lane = threadIdx.x & 31;
   const int64_t warp_id = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
   const int64_t n_warps = (int64_t)gridDim.x * kWarps;
@@ -164,6 +173,11 @@ __global__ void __launch_bounds__(kWarps * 32)
         float o[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[i] = rstd * (g[k][i] - m1 - v[k][i] * m2);
+        if constexpr (kRes) {
+          float r[8];
+          load8<T>(dres + row * dim + c, r);
+          add_rounded8<T>(o, r);
+        }
         store8<T>(dx + row * dim + c, o);
       }
     }
@@ -256,10 +270,10 @@ __global__ void __launch_bounds__(kWarps * 32, 3)
   }
 }
 
-template <typename T, int K>
+template <typename T, int K, bool kRes>
 __global__ void __launch_bounds__(kWarps * 32, 2)
-    layer_norm_bwd_seg_kernel(const T *x, const T *weight, const T *dy, T *dx, float *dw_part, float *db_part,
-                              int64_t rows, float eps) {
+    layer_norm_bwd_seg_kernel(const T *x, const T *weight, const T *dy, const T *dres, T *dx, float *dw_part,
+                              float *db_part, int64_t rows, float eps) {
   constexpr int D = 64 * K;
   const int lane = threadIdx.x & 31, seg = lane >> 3, l = lane & 7;
   const int64_t warp_id = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
@@ -273,13 +287,14 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
   for (int64_t g = warp_id; 4 * g < rows; g += n_warps) {
     const int64_t row = 4 * g + seg;
     const bool on = row < rows;
-    uint4 rx[K], rg[K];
+    uint4 rx[K], rg[K], rr[kRes ? K : 1];
 #pragma unroll
     for (int j = 0; j < K; ++j) {
       rx[j] = rg[j] = make_uint4(0u, 0u, 0u, 0u);
       if (on) {
         rx[j] = *reinterpret_cast<const uint4 *>(x + row * D + 8 * (l + 8 * j));
         rg[j] = *reinterpret_cast<const uint4 *>(dy + row * D + 8 * (l + 8 * j));
+        if constexpr (kRes) rr[j] = *reinterpret_cast<const uint4 *>(dres + row * D + 8 * (l + 8 * j));
       }
     }
     float v[K][8], gr[K][8];
@@ -325,6 +340,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
         float o[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[i] = rstd * (gr[j][i] - m1 - v[j][i] * m2);
+        if constexpr (kRes) {
+          float r[8];
+          unpack8x<T>(rr[j], r);
+          add_rounded8<T>(o, r);
+        }
         store8<T>(dx + row * D + 8 * (l + 8 * j), o);
       }
     }
@@ -586,19 +606,19 @@ int launch_ln(const void *x, const void *w, const void *b, void *y, int64_t rows
   return P3D_OK;
 }
 
-template <typename T>
-int launch_ln_bwd(const void *x, const void *w, const void *dy, void *dx, float *dw_part, float *db_part,
-                  int64_t rows, int dim, float eps, unsigned blocks, cudaStream_t s) {
+template <typename T, bool kRes>
+int launch_ln_bwd(const void *x, const void *w, const void *dy, const void *dres, void *dx, float *dw_part,
+                  float *db_part, int64_t rows, int dim, float eps, unsigned blocks, cudaStream_t s) {
   if (dim % 64 == 0 && dim <= 192) {  // segment layout (same grid: one partials row per warp)
     auto seg = [&](auto kernel) {
       kernel<<<blocks, kWarps * 32, 0, s>>>(static_cast<const T *>(x), static_cast<const T *>(w),
-                                            static_cast<const T *>(dy), static_cast<T *>(dx), dw_part, db_part, rows,
-                                            eps);
+                                            static_cast<const T *>(dy), static_cast<const T *>(dres),
+                                            static_cast<T *>(dx), dw_part, db_part, rows, eps);
     };
     switch (dim / 64) {
-      case 1: seg(layer_norm_bwd_seg_kernel<T, 1>); break;
-      case 2: seg(layer_norm_bwd_seg_kernel<T, 2>); break;
-      default: seg(layer_norm_bwd_seg_kernel<T, 3>); break;
+      case 1: seg(layer_norm_bwd_seg_kernel<T, 1, kRes>); break;
+      case 2: seg(layer_norm_bwd_seg_kernel<T, 2, kRes>); break;
+      default: seg(layer_norm_bwd_seg_kernel<T, 3, kRes>); break;
     }
     P3D_LAUNCH_CHECK();
     return P3D_OK;
@@ -606,18 +626,25 @@ int launch_ln_bwd(const void *x, const void *w, const void *dy, void *dx, float 
   const int chunks = (dim / 8 + 31) / 32;
   auto args = [&](auto kernel) {
     kernel<<<blocks, kWarps * 32, 0, s>>>(static_cast<const T *>(x), static_cast<const T *>(w),
-                                          static_cast<const T *>(dy), static_cast<T *>(dx), dw_part, db_part, rows,
-                                          dim, eps);
+                                          static_cast<const T *>(dy), static_cast<const T *>(dres),
+                                          static_cast<T *>(dx), dw_part, db_part, rows, dim, eps);
   };
   switch (chunks) {
-    case 1: args(layer_norm_bwd_kernel<T, 1>); break;
-    case 2: args(layer_norm_bwd_kernel<T, 2>); break;
-    case 3: args(layer_norm_bwd_kernel<T, 3>); break;
-    case 4: args(layer_norm_bwd_kernel<T, 4>); break;
+    case 1: args(layer_norm_bwd_kernel<T, 1, kRes>); break;
+    case 2: args(layer_norm_bwd_kernel<T, 2, kRes>); break;
+    case 3: args(layer_norm_bwd_kernel<T, 3, kRes>); break;
+    case 4: args(layer_norm_bwd_kernel<T, 4, kRes>); break;
     default: return fail(P3D_ERR_UNSUPPORTED, "p3d_layer_norm_bwd: dim %d above 1024", dim);
   }
   P3D_LAUNCH_CHECK();
   return P3D_OK;
+}
+
+template <typename T>
+int launch_ln_bwd_any(const void *x, const void *w, const void *dy, const void *dres, void *dx, float *dw_part,
+                      float *db_part, int64_t rows, int dim, float eps, unsigned blocks, cudaStream_t s) {
+  return dres ? launch_ln_bwd<T, true>(x, w, dy, dres, dx, dw_part, db_part, rows, dim, eps, blocks, s)
+              : launch_ln_bwd<T, false>(x, w, dy, dres, dx, dw_part, db_part, rows, dim, eps, blocks, s);
 }
 
 unsigned ln_bwd_blocks(int64_t rows) {
@@ -682,29 +709,47 @@ extern "C" size_t p3d_layer_norm_bwd_workspace(int64_t rows, int dim) {
   return ln_bwd_layout(rows, dim, nullptr, &a, &b, &t);
 }
 
-extern "C" int p3d_layer_norm_bwd(const void *x, const void *weight, const void *dy, void *dx, float *dweight,
-                                  float *dbias, int dtype, int64_t rows, int dim, float eps, void *workspace,
-                                  size_t workspace_bytes, void *stream) {
-  P3D_CHECK_ARG(dtype == P3D_BF16 || dtype == P3D_F16, "p3d_layer_norm_bwd: bf16 or f16 only");
-  P3D_CHECK_ARG(x && weight && dy && dx && dweight && dbias, "p3d_layer_norm_bwd: null pointer");
-  P3D_CHECK_ARG(rows >= 1 && dim >= 8 && dim % 8 == 0, "p3d_layer_norm_bwd: rows >= 1, dim a positive multiple of 8");
-  P3D_CHECK_ARG(aligned16(x) && aligned16(weight) && aligned16(dy) && aligned16(dx),
-                "p3d_layer_norm_bwd: 16-byte aligned tensors required");
-  P3D_CHECK_ARG(eps >= 0.f, "p3d_layer_norm_bwd: negative eps");
+namespace {
+int layer_norm_bwd(const char *name, const void *x, const void *weight, const void *dy, const void *dres, void *dx,
+                   float *dweight, float *dbias, int dtype, int64_t rows, int dim, float eps, void *workspace,
+                   size_t workspace_bytes, void *stream) {
+  P3D_CHECK_ARG(dtype == P3D_BF16 || dtype == P3D_F16, "%s: bf16 or f16 only", name);
+  P3D_CHECK_ARG(x && weight && dy && dx && dweight && dbias, "%s: null pointer", name);
+  P3D_CHECK_ARG(rows >= 1 && dim >= 8 && dim % 8 == 0, "%s: rows >= 1, dim a positive multiple of 8", name);
+  P3D_CHECK_ARG(aligned16(x) && aligned16(weight) && aligned16(dy) && aligned16(dx) && aligned16(dres),
+                "%s: 16-byte aligned tensors required", name);
+  P3D_CHECK_ARG(eps >= 0.f, "%s: negative eps", name);
   float *dw_part, *db_part, *tmp;
   const size_t need = ln_bwd_layout(rows, dim, workspace, &dw_part, &db_part, &tmp);
   if (!workspace || workspace_bytes < need)
-    return fail(P3D_ERR_WORKSPACE, "p3d_layer_norm_bwd: workspace of %zu bytes required", need);
-  P3D_CHECK_ARG(((uintptr_t)workspace & 15) == 0, "p3d_layer_norm_bwd: 16-byte aligned workspace required");
+    return fail(P3D_ERR_WORKSPACE, "%s: workspace of %zu bytes required", name, need);
+  P3D_CHECK_ARG(((uintptr_t)workspace & 15) == 0, "%s: 16-byte aligned workspace required", name);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const unsigned blocks = ln_bwd_blocks(rows);
-  const int st = dtype == P3D_BF16
-                     ? launch_ln_bwd<__nv_bfloat16>(x, weight, dy, dx, dw_part, db_part, rows, dim, eps, blocks, s)
-                     : launch_ln_bwd<__half>(x, weight, dy, dx, dw_part, db_part, rows, dim, eps, blocks, s);
+  const int st =
+      dtype == P3D_BF16
+          ? launch_ln_bwd_any<__nv_bfloat16>(x, weight, dy, dres, dx, dw_part, db_part, rows, dim, eps, blocks, s)
+          : launch_ln_bwd_any<__half>(x, weight, dy, dres, dx, dw_part, db_part, rows, dim, eps, blocks, s);
   if (st) return st;
   const int64_t warps = (int64_t)blocks * kWarps;
   if (int e = launch_sum_rows(dw_part, dweight, warps, dim, tmp, s)) return e;
   return launch_sum_rows(db_part, dbias, warps, dim, tmp, s);
+}
+}  // namespace
+
+extern "C" int p3d_layer_norm_bwd(const void *x, const void *weight, const void *dy, void *dx, float *dweight,
+                                  float *dbias, int dtype, int64_t rows, int dim, float eps, void *workspace,
+                                  size_t workspace_bytes, void *stream) {
+  return layer_norm_bwd("p3d_layer_norm_bwd", x, weight, dy, nullptr, dx, dweight, dbias, dtype, rows, dim, eps,
+                        workspace, workspace_bytes, stream);
+}
+
+extern "C" int p3d_layer_norm_bwd_residual(const void *x, const void *weight, const void *dy, const void *dres,
+                                           void *dx, float *dweight, float *dbias, int dtype, int64_t rows, int dim,
+                                           float eps, void *workspace, size_t workspace_bytes, void *stream) {
+  P3D_CHECK_ARG(dres, "p3d_layer_norm_bwd_residual: null pointer");
+  return layer_norm_bwd("p3d_layer_norm_bwd_residual", x, weight, dy, dres, dx, dweight, dbias, dtype, rows, dim,
+                        eps, workspace, workspace_bytes, stream);
 }
 
 extern "C" int p3d_qkv_split(const void *qp, const void *kvp, void *q, void *kl, void *vl, void *kg, void *vg,

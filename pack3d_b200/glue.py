@@ -2,7 +2,9 @@
 ``attention.py:53-89``): autograd functions over the library's glue kernels.
 
 * :func:`layer_norm` -- ``nn.LayerNorm`` (``attention.py:64``) as ``p3d_layer_norm`` with
-  ``p3d_layer_norm_bwd`` as its backward (dweight / dbias summed in fixed order).
+  ``p3d_layer_norm_bwd`` as its backward (dweight / dbias summed in fixed order);
+  :func:`layer_norm_residual` also hands x on to the outer residual (``attention.py:89``) and
+  adds that branch's gradient inside the same backward kernel.
 * :func:`qkv_split` -- the projection split of ``attention.py:70-81``: the row-major
   ``to_q`` / ``to_kv`` outputs become rotated head-major q, kl, kg and head-major vl, vg in
   one ``p3d_qkv_split`` pass; its backward, ``p3d_qkv_merge``, rotates dq, dkl, dkg back and
@@ -23,42 +25,84 @@ def _empty_ws(nbytes, device):
     return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
 
 
+def _ln_forward(ctx, x, weight, bias, eps):
+    x = x.contiguous()
+    y = torch.empty_like(x)
+    rows, dim = x.numel() // x.shape[-1], x.shape[-1]
+    with torch.cuda.device(x.device):
+        _native.check(_native.lib().p3d_layer_norm(_native.ptr(x), _native.ptr(weight), _native.ptr(bias),
+                                                   _native.ptr(y), _native.DTYPE_CODE[x.dtype], rows, dim,
+                                                   float(eps), _native.stream_of(x.device)), "p3d_layer_norm")
+    ctx.save_for_backward(x, weight)
+    ctx.eps = float(eps)
+    return x, y
+
+
+def _ln_backward(ctx, dy, dres=None):
+    """``(dx, dweight, dbias, None)``; with ``dres`` (the residual branch's gradient of x) the
+    kernel adds it into dx (``p3d_layer_norm_bwd_residual``)."""
+    x, weight = ctx.saved_tensors
+    dy = dy.contiguous()
+    rows, dim = x.numel() // x.shape[-1], x.shape[-1]
+    dx = torch.empty_like(x)
+    f32 = dict(dtype=torch.float32, device=x.device)
+    dw, db = torch.empty(dim, **f32), torch.empty(dim, **f32)
+    lib = _native.lib()
+    ws = _empty_ws(lib.p3d_layer_norm_bwd_workspace(rows, dim), x.device)
+    tail = (_native.ptr(dx), _native.ptr(dw), _native.ptr(db), _native.DTYPE_CODE[x.dtype], rows, dim, ctx.eps,
+            _native.ptr(ws), ws.numel(), _native.stream_of(x.device))
+    with torch.cuda.device(x.device):
+        if dres is None:
+            _native.check(lib.p3d_layer_norm_bwd(_native.ptr(x), _native.ptr(weight), _native.ptr(dy), *tail),
+                          "p3d_layer_norm_bwd")
+        else:
+            # bound to a name: a temporary whose pointer alone is passed could be freed before the launch
+            dres = dres.to(x.dtype).contiguous()
+            _native.check(lib.p3d_layer_norm_bwd_residual(_native.ptr(x), _native.ptr(weight), _native.ptr(dy),
+                                                          _native.ptr(dres), *tail), "p3d_layer_norm_bwd_residual")
+    return dx, dw.to(weight.dtype), db.to(weight.dtype), None
+
+
 class _LayerNorm(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, bias, eps):
-        x = x.contiguous()
-        y = torch.empty_like(x)
-        rows, dim = x.numel() // x.shape[-1], x.shape[-1]
-        with torch.cuda.device(x.device):
-            _native.check(_native.lib().p3d_layer_norm(_native.ptr(x), _native.ptr(weight), _native.ptr(bias),
-                                                       _native.ptr(y), _native.DTYPE_CODE[x.dtype], rows, dim,
-                                                       float(eps), _native.stream_of(x.device)), "p3d_layer_norm")
-        ctx.save_for_backward(x, weight)
-        ctx.eps = float(eps)
-        return y
+        return _ln_forward(ctx, x, weight, bias, eps)[1]
 
     @staticmethod
     @once_differentiable
     def backward(ctx, dy):
-        x, weight = ctx.saved_tensors
-        dy = dy.contiguous()
-        rows, dim = x.numel() // x.shape[-1], x.shape[-1]
-        dx = torch.empty_like(x)
-        f32 = dict(dtype=torch.float32, device=x.device)
-        dw, db = torch.empty(dim, **f32), torch.empty(dim, **f32)
-        lib = _native.lib()
-        ws = _empty_ws(lib.p3d_layer_norm_bwd_workspace(rows, dim), x.device)
-        with torch.cuda.device(x.device):
-            _native.check(lib.p3d_layer_norm_bwd(_native.ptr(x), _native.ptr(weight), _native.ptr(dy), _native.ptr(dx),
-                                                 _native.ptr(dw), _native.ptr(db), _native.DTYPE_CODE[x.dtype], rows,
-                                                 dim, ctx.eps, _native.ptr(ws), ws.numel(),
-                                                 _native.stream_of(x.device)), "p3d_layer_norm_bwd")
-        return dx, dw.to(weight.dtype), db.to(weight.dtype), None
+        return _ln_backward(ctx, dy)
 
 
 def layer_norm(x, norm):
     """``norm(x)`` for an ``nn.LayerNorm`` over the last dimension, in the library kernels."""
     return _LayerNorm.apply(x, norm.weight, norm.bias, norm.eps)
+
+
+class _LayerNormResidual(torch.autograd.Function):
+    """``(norm(x), x)``: the second output is x itself, which the layer's outer residual
+    (``attention.py:89``) reads, so both gradients of x arrive in one backward call and
+    ``p3d_layer_norm_bwd_residual`` adds the residual's into the LayerNorm's dx in the same pass
+    -- the bits autograd's separate add of the two would give, one elementwise pass fewer."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):
+        ctx.set_materialize_grads(False)
+        xc, y = _ln_forward(ctx, x, weight, bias, eps)
+        return y, xc
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, dy, dres):
+        if dy is None:
+            return (None if dres is None else dres), None, None, None
+        return _ln_backward(ctx, dy, dres)
+
+
+def layer_norm_residual(x, norm):
+    """``(norm(x), x)`` with the two gradients of x summed inside the LayerNorm backward kernel;
+    the second output is the residual operand of the layer's output GEMM."""
+    return _LayerNormResidual.apply(x, norm.weight, norm.bias, norm.eps)
 
 
 class _QKVSplit(torch.autograd.Function):

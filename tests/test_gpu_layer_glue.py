@@ -232,6 +232,42 @@ def test_layer_norm_backward_matches_torch(cuda_device, dim):
     assert torch.equal(xa2.grad, got[0]) and torch.equal(norm.weight.grad, got[1])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("dim", [192, 384, 40])
+def test_layer_norm_residual_backward_is_the_two_step_sum(cuda_device, dtype, dim):
+    """p3d_layer_norm_bwd_residual (through glue.layer_norm_residual feeding an addmm residual,
+    as the layer does) gives the same bits as glue.layer_norm plus autograd's separate add."""
+    from pack3d_b200 import glue
+    gen = torch.Generator(device=cuda_device).manual_seed(dim + 7)
+    x = (torch.randn(2, 1537, dim, device=cuda_device, generator=gen) * 2 + 0.5).to(dtype)
+    m = torch.randn(2 * 1537, dim, device=cuda_device, generator=gen).to(dtype)
+    w_out = (torch.randn(dim, dim, device=cuda_device, generator=gen) / dim ** 0.5).to(dtype)
+    dy = torch.randn(2, 1537, dim, device=cuda_device, generator=gen).to(dtype)
+    norm = torch.nn.LayerNorm(dim).to(cuda_device, dtype)
+    with torch.no_grad():
+        norm.weight.normal_()
+        norm.bias.normal_()
+    results = []
+    for fused in (True, False):
+        norm.zero_grad(set_to_none=True)
+        xa = x.clone().requires_grad_()
+        if fused:
+            xn, res = glue.layer_norm_residual(xa, norm)
+        else:
+            xn, res = glue.layer_norm(xa, norm), xa
+        y = torch.addmm(res.reshape(-1, dim), xn.reshape(-1, dim) * m, w_out.t()).view_as(x)
+        y.backward(dy)
+        results.append((y.detach(), xa.grad, norm.weight.grad.clone(), norm.bias.grad.clone()))
+    for a, b in zip(*results):
+        assert torch.equal(a, b)
+    # the residual output alone (LayerNorm output unused): its gradient passes straight through
+    xa = x.clone().requires_grad_()
+    _, res = glue.layer_norm_residual(xa, norm)
+    res.backward(dy)
+    assert torch.equal(xa.grad, dy)
+    assert _native.device_errors() == 0
+
+
 def test_fused_training_glue_matches_the_per_op_path(cuda_device):
     layout = _layout((16, 16, 16)).to(cuda_device)
     torch.manual_seed(0)

@@ -41,7 +41,7 @@ def test_library_exports_every_declared_symbol():
 def test_library_metadata_calls():
     from pack3d_b200 import _native
     handle = _native.lib()
-    assert handle.p3d_abi_version() == 4
+    assert handle.p3d_abi_version() == 5
     assert handle.p3d_strerror(0) == b"success"
     assert handle.p3d_strerror(4).startswith(b"workspace")
     assert handle.p3d_device_count() >= 0
@@ -138,6 +138,16 @@ def test_argument_checks_run_before_any_device_call():
     st = lib.p3d_pool_fwd(dummy, dummy, dummy, dummy, dummy, 4, 65, 1, dummy, dummy, None, None, _native.BF16, 1, 1,
                           256, 48, 1.0, None)
     assert st == 1 and b"block table" in lib.p3d_last_error()
+    # p3d_layer_norm_bwd_residual: the residual gradient is required; misaligned, or no workspace
+    st = lib.p3d_layer_norm_bwd_residual(dummy, dummy, dummy, None, dummy, dummy, dummy, _native.BF16, 8, 192, 1e-5,
+                                         dummy, 1 << 20, None)
+    assert st == 1 and b"null pointer" in lib.p3d_last_error()
+    st = lib.p3d_layer_norm_bwd_residual(dummy, dummy, dummy, dummy + 2, dummy, dummy, dummy, _native.BF16, 8, 192,
+                                         1e-5, dummy, 1 << 20, None)
+    assert st == 1 and b"aligned" in lib.p3d_last_error()
+    st = lib.p3d_layer_norm_bwd_residual(dummy, dummy, dummy, dummy, dummy, dummy, dummy, _native.BF16, 8, 192, 1e-5,
+                                         None, 0, None)
+    assert st == 4 and b"p3d_layer_norm_bwd_residual: workspace" in lib.p3d_last_error()
 
 
 def test_fused_projection_is_not_offered_for_cpu_tensors():
