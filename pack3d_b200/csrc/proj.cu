@@ -38,6 +38,8 @@ constexpr int kEpilogueThreads = 128 * kSplit;
 constexpr int kThreads = 64 + kEpilogueThreads;
 constexpr int kProducerWarp = 0, kMmaWarp = 1;  // warps 2..: epilogue
 constexpr int kMaxTableFloats = 8192;           // phase tables up to 32 KB live in shared memory
+constexpr int kEpilogueWarps = kEpilogueThreads / 32;
+constexpr int kStageRows = 16;                  // rows of a warp's head staged per pass (half its 32)
 constexpr int kTile = 128;                      // tokens per tile (MMA M)
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr int kTmemCols = 512;
@@ -71,6 +73,8 @@ struct ProjParams {
   // along x, then read their (cos, sin) from distinct banks instead of 16 lanes per bank);
   // staged when its smem_floats <= kMaxTableFloats.
   int tstart[3], tpitch[3], smem_floats;
+  int table_in_smem;   // the table is staged (it fits beside the W slice and X ring)
+  int stage_out;       // per-warp output staging in shared memory (kStageRows rows of D values)
   int raster_qkv, ey, ex;  // q, kl, vl rows at each token's raster index (c0 ey + c1) ex + c2
   int64_t kv_rows, kv_row0;  // kl, vl: [B, G, kv_rows, D], token row n at kv_row0 + n
 };
@@ -130,7 +134,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t x_smem = w_smem + p.kc * w_atom;  // 2 stages of kc * x_atom
   const uint32_t x_stage = p.kc * x_atom;
   const uint32_t bars = x_smem + 2 * x_stage;
-  float *table = reinterpret_cast<float *>(smem_raw + (bars + 8u * kNumBars + 15u - raw) / 16u * 16u);
+  // after the barriers: the epilogue warps' output staging (if any), then the phase table
+  const uint32_t stage_off = (bars + 8u * kNumBars + 15u - raw) / 16u * 16u;
+  const uint32_t stage_bytes = p.stage_out ? (uint32_t)kEpilogueWarps * kStageRows * D * 2u : 0u;
+  float *table = reinterpret_cast<float *>(smem_raw + stage_off + stage_bytes);
   __shared__ uint32_t tmem_holder;
   auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
 
@@ -159,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tx);
     prefetch_tmap(is_q ? &twq : &twkv);
   }
-  const bool table_in_smem = p.smem_floats <= kMaxTableFloats;
+  const bool table_in_smem = p.table_in_smem != 0;
   if (table_in_smem) {
     // entry e of the table (axis a, coordinate c, pair k: e = start[a] + c pairs[a] + k) goes
     // to tstart[a] + c tpitch[a] + k
@@ -280,7 +287,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int q16 = 0; q16 < D / 16; ++q16)
           tmem_ld16(t_lanes + a * G + j * D + 16 * q16, *reinterpret_cast<uint32_t(*)[16]>(acc + 16 * q16));
         tmem_wait_ld();
-        if (!valid) continue;
         int part = 0, hh = hr;
         if (!is_q) {
           part = hr / p.kv_heads;
@@ -294,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // the projection pair rounded to the storage type (as the GEMM output would be)
           packed[q2] = pack_pair<BF16>(__uint_as_float(acc[2 * q2]), __uint_as_float(acc[2 * q2 + 1]));
         }
-        if (rot) {
+        if (rot && valid) {
           // the token's table row of each axis (balanced pairs: pair q2 sits at a constant
           // offset from the row of its axis)
           const float *row_axis[3];
@@ -323,9 +329,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t head_rows = kv_local ? p.kv_rows : (int64_t)p.tokens;
         const int64_t row = kv_local ? p.kv_row0 + nd : nd;
         uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(o) + (((int64_t)b * ht + hh) * head_rows + row) * D);
+        // When the warp's 32 rows are one contiguous run of the output (every row valid, one
+        // batch, token order), each thread's D values go through shared memory, kStageRows rows
+        // at a time, and the warp writes the run as whole 512-byte spans; a thread's own row
+        // would otherwise be D / 8 stores at a D-element stride, each touching as many lines
+        // as there are threads.
+        uint4 *const dst0 = reinterpret_cast<uint4 *>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(dst), 0));
+        const bool run = p.stage_out && __all_sync(0xffffffffu, valid && dst == dst0 + lane * (D / 8));
+        if (run) {
+          uint4 *stg = reinterpret_cast<uint4 *>(smem_raw + stage_off) + (warp - 2) * (kStageRows * D / 8);
+          constexpr int kChunks = kStageRows * D / 8;  // 16-byte pieces per pass
 #pragma unroll
-        for (int v = 0; v < D / 8; ++v)
-          dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          for (int h2 = 0; h2 < 32 / kStageRows; ++h2) {
+            if (lane / kStageRows == h2) {
+#pragma unroll
+              for (int v = 0; v < D / 8; ++v)
+                stg[(lane % kStageRows) * (D / 8) + v] =
+                    make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+            }
+            __syncwarp();
+            uint4 *out = dst0 + h2 * kChunks;
+#pragma unroll
+            for (int k = lane; k < kChunks; k += 32) out[k] = stg[k];
+            __syncwarp();
+          }
+        } else if (valid) {
+#pragma unroll
+          for (int v = 0; v < D / 8; ++v)
+            dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -395,7 +427,16 @@ int launch_proj(const ProjArgs &a, cudaStream_t stream) {
   p.raster_qkv = a.raster_qkv;
   p.ey = a.ey;
   p.ex = a.ex;
-  const size_t smem = proj_smem_bytes(a.dim, gh * D);
+  // shared memory: the W slice and the X ring (always), the phase table when it has at most
+  // kMaxTableFloats entries (the budget proj_group_heads reserves for it), then the output
+  // staging of the epilogue warps if it still fits
+  const size_t table_bytes = 4 * (size_t)p.smem_floats;
+  const size_t stage_bytes = (size_t)kEpilogueWarps * kStageRows * D * 2;
+  size_t smem = proj_smem_bytes(a.dim, gh * D) - 4 * (size_t)kMaxTableFloats;
+  p.table_in_smem = p.smem_floats <= kMaxTableFloats ? 1 : 0;
+  p.stage_out = smem + stage_bytes + (p.table_in_smem ? table_bytes : 0) + 1024 <= info.smem_optin ? 1 : 0;
+  if (p.stage_out) smem += stage_bytes;
+  if (p.table_in_smem) smem += table_bytes;
   const bool balanced = p.pairs[0] == Balanced<D>::count(0) && p.pairs[1] == Balanced<D>::count(1) &&
                         p.pairs[2] == Balanced<D>::count(2);
   auto kernel = balanced ? proj_split_kernel<BF16, D, true> : proj_split_kernel<BF16, D, false>;
