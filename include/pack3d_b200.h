@@ -159,6 +159,21 @@ P3D_API int p3d_qkv_project(const void *x, const void *wq, const void *wkv, void
                     void *vg, int dtype, int batch, int heads, int kv_heads, int tokens, int dim, int head_dim,
                     const int64_t *coords, int pz, int py, int px, const float *phases, int ez, int ey, int ex,
                     int64_t kv_rows, int64_t kv_row0, unsigned flags, void *stream);
+/*
+ * p3d_qkv_gate_project: p3d_qkv_project with the gate Linear folded in -- attention.py:84-86
+ *   (`self.gate(x)`, its pair softmax and the transpose), the job of a third GEMM and
+ *   p3d_gate_pairs: wg [2*heads, dim] and bg [2*heads] (nn.Linear weight and bias, dtype),
+ *   gate [B, H, N] = softmax(logits[b, n, 2h .. 2h + 1])[1], each logit rounded to dtype with
+ *   its bias added, as the Linear's output would be.  q, kl, vl, kg, vg are the bits
+ *   p3d_qkv_project writes.  p3d_qkv_gate_project_supported() (heads <= 8 and room for the
+ *   logit rows beside the last column group's) rejects: P3D_ERR_UNSUPPORTED.
+ */
+P3D_API int p3d_qkv_gate_project_supported(int dtype, int dim, int heads, int kv_heads, int head_dim);
+P3D_API int p3d_qkv_gate_project(const void *x, const void *wq, const void *wkv, const void *wg, const void *bg,
+                         void *q, void *kl, void *vl, void *kg, void *vg, void *gate, int dtype, int batch,
+                         int heads, int kv_heads, int tokens, int dim, int head_dim, const int64_t *coords,
+                         int pz, int py, int px, const float *phases, int ez, int ey, int ex, int64_t kv_rows,
+                         int64_t kv_row0, unsigned flags, void *stream);
 
 /*
  * Layer glue of the training path (their backward halves):

@@ -82,6 +82,9 @@ _SIGNATURES = {
                                     ctypes.c_uint, _vp]),
     "p3d_gate_pairs": (_c_int, [_vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int, _vp]),
     "p3d_qkv_project_supported": (_c_int, [_c_int] * 5),
+    "p3d_qkv_gate_project_supported": (_c_int, [_c_int] * 5),
+    "p3d_qkv_gate_project": (_c_int, [_vp] * 11 + [_c_int] * 7 + [_vp] + [_c_int] * 3 + [_vp] + [_c_int] * 3 +
+                             [_c_i64] * 2 + [ctypes.c_uint, _vp]),
     "p3d_qkv_project": (_c_int, [_vp] * 8 + [_c_int] * 7 + [_vp] + [_c_int] * 3 + [_vp] + [_c_int] * 3 + [_c_i64] * 2 +
                         [ctypes.c_uint, _vp]),
     "p3d_qkv_merge": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,

@@ -210,8 +210,13 @@ class PACK3DAttention(nn.Module):
         if phases is not None and self.fused_projection and glue.project_supported(xn, self.to_q.weight,
                                                                                   self.to_kv.weight, h, g, d):
             # projections, split and RoPE in one kernel: the projections never reach HBM; the
-            # gate from its own GEMM and p3d_gate_pairs
+            # gate folded in (its logit rows beside the first q group's), or else from its own
+            # GEMM and p3d_gate_pairs
             coords = coords.to(device=dev, dtype=torch.int64).contiguous()
+            if glue.gate_project_supported(xn, self.gate.weight, self.gate.bias, h, g, d):
+                return (x, *glue.project_split_raw(xn, self.to_q.weight, self.to_kv.weight, coords, phases, pairs,
+                                                   extents, h, g, d, raster_qkv=raster_qkv, kv_out=kv_out,
+                                                   gate=(self.gate.weight, self.gate.bias)))
             q, kl, vl, kg, vg = glue.project_split_raw(xn, self.to_q.weight, self.to_kv.weight, coords, phases, pairs,
                                                        extents, h, g, d, raster_qkv=raster_qkv, kv_out=kv_out)
             logits = torch.addmm(self.gate.bias, xn.view(b * n, self.dim), self.gate.weight.t())

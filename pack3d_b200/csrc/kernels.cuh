@@ -76,6 +76,9 @@ struct ProjArgs {
   int table_floats;             // floats in the phase table
   int raster_qkv, ey, ex;       // q, kl, vl rows at each token's raster index (ey x ex planes)
   int64_t kv_rows, kv_row0;     // kl, vl: [B, G, kv_rows, D], token row n at kv_row0 + n
+  int gate_cols;                // 2 * heads with the gate folded in (wg [2H, dim], bg [2H], gate [B,H,N]), else 0
+  const void *wg, *bg;
+  void *gate;
 };
 int proj_group_heads(int head_dim, int heads, int kv_heads, int dim, size_t smem_limit);
 size_t proj_smem_bytes(int dim, int group_cols);

@@ -21,6 +21,8 @@
 // warp's tokens read it without bank conflicts); a token's coordinates are fetched
 // a tile ahead, so the epilogue does not wait on global loads.  Every wait is bounded (2 s): on a timeout the kernel records an
 // error bit (p3d_device_errors), drains its copies and MMAs and frees TMEM.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "sm100.cuh"
@@ -40,6 +42,7 @@ constexpr int kProducerWarp = 0, kMmaWarp = 1;  // warps 2..: epilogue
 constexpr int kMaxTableFloats = 8192;           // phase tables up to 32 KB live in shared memory
 constexpr int kEpilogueWarps = kEpilogueThreads / 32;
 constexpr int kStageRows = 16;                  // rows of a warp's head staged per pass (half its 32)
+constexpr int kGateRows = 16;                   // gate logit rows (2 H <= 16, zero-padded) beside the last group's W
 constexpr int kTile = 128;                      // tokens per tile (MMA M)
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr int kTmemCols = 512;
@@ -77,6 +80,13 @@ struct ProjParams {
   int stage_out;       // per-warp output staging in shared memory (kStageRows rows of D values)
   int raster_qkv, ey, ex;  // q, kl, vl rows at each token's raster index (c0 ey + c1) ex + c2
   int64_t kv_rows, kv_row0;  // kl, vl: [B, G, kv_rows, D], token row n at kv_row0 + n
+  // The gate (attention.py:84-86) in the CTAs of the last group (vg head rows: no rotation, the
+  // lightest epilogue): gate_cols = 2 H logit rows of wg
+  // [2H, dim] (nn.Linear weight, bias bg [2H]) beside the group's W slice, zero-padded to
+  // kGateRows; gate [B, H, N] = softmax(logit pair of head h)[1].  0: no gate.
+  int gate_cols;
+  const void *wg, *bg;
+  void *gate;
 };
 
 // (cos, sin) of rotation pair `pair` of a token at coordinates c, from the table `tab` whose
@@ -125,9 +135,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap twkv, const ProjParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = p.group_heads * D;                 // accumulator columns (MMA N)
+  const int G = p.group_heads * D;                 // projection columns of the group
+  const int group0 = blockIdx.x % p.groups;
+  const bool has_gate = p.gate_cols > 0 && group0 == p.groups - 1;
+  const int Gp = G + (has_gate ? kGateRows : 0);   // accumulator columns (MMA N): + the gate logits
   const uint32_t x_atom = kTile * 128;             // bytes of one 64-channel box of an X tile
-  const uint32_t w_atom = (uint32_t)G * 128;       // of the W slice (G multiple of 16: 1024-aligned)
+  const uint32_t w_atom = (uint32_t)Gp * 128;      // of the W slice (Gp multiple of 16: 1024-aligned)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t w_smem = base;
@@ -141,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint32_t tmem_holder;
   auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
 
-  const int group = blockIdx.x % p.groups, slot = blockIdx.x / p.groups;
+  const int group = group0, slot = blockIdx.x / p.groups;
   const bool is_q = group < p.groups_q;
   const int head0 = (is_q ? group : group - p.groups_q) * p.group_heads;  // first head row of the group
   const int n_tiles = (p.rows + kTile - 1) / kTile;
@@ -177,6 +190,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           reinterpret_cast<const float2 *>(p.phases)[e];
     }
   }
+  if (has_gate) {
+    // the gate's logit rows after the group's G rows of every 64-channel box, in the layout
+    // the TMA writes there (128-byte rows, 16-byte chunk j of row r at j ^ (r mod 8); G is a
+    // multiple of 8), rows past 2 H zero
+    const uint16_t *wg = static_cast<const uint16_t *>(p.wg);
+    for (int e = threadIdx.x; e < p.kc * kGateRows * 8; e += kThreads) {
+      const int c = e / (kGateRows * 8), r = (e / 8) % kGateRows, j = e % 8;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < p.gate_cols) v = *reinterpret_cast<const uint4 *>(wg + (int64_t)r * (p.kc * 64) + 64 * c + 8 * j);
+      const uint32_t at = w_smem + c * w_atom + (uint32_t)(G + r) * 128u + (uint32_t)((j ^ (r & 7)) * 16);
+      *reinterpret_cast<uint4 *>(smem_raw + (at - raw)) = v;
+    }
+    fence_proxy_async_smem();  // generic-proxy writes, read by the tensor core (async proxy)
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -186,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const CUtensorMap *tw = is_q ? &twq : &twkv;
-      mbar_expect_tx(bar(kWFull), p.kc * w_atom);
+      mbar_expect_tx(bar(kWFull), p.kc * (uint32_t)G * 128u);  // the TMA copies G rows per box
       for (int c = 0; c < p.kc; ++c) tma_load_3d(w_smem + c * w_atom, tw, bar(kWFull), 64 * c, head0 * D, 0);
       int issued = 0;
       for (int i = 0; i < my_tiles; ++i) {
@@ -208,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(kTile, G, BF16, false);
+      const uint32_t idesc = idesc_f16(kTile, Gp, BF16, false);
       int n_mma = 0;  // tiles whose MMAs were issued (each commits kXEmpty and kAccFull of its stage)
       const uint64_t desc_w = desc_sw128(w_smem, 1024);  // K-major, 8-row groups of 128-byte rows
       const uint64_t desc_x = desc_sw128(x_smem, 1024);
@@ -224,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < p.kc; ++c)
 #pragma unroll
           for (int k = 0; k < 4; ++k)  // K = 16 slices: 32 bytes along the 128-byte rows
-            mma_ss(tmem + a * G, dx + ((c * x_atom + 32 * k) >> 4), desc_w + ((c * w_atom + 32 * k) >> 4), idesc,
+            mma_ss(tmem + a * Gp, dx + ((c * x_atom + 32 * k) >> 4), desc_w + ((c * w_atom + 32 * k) >> 4), idesc,
                    (c | k) ? 1u : 0u);
         mma_commit(bar(kXEmpty + s));
         mma_commit(bar(kAccFull + a));
@@ -285,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t acc[D];
 #pragma unroll
         for (int q16 = 0; q16 < D / 16; ++q16)
-          tmem_ld16(t_lanes + a * G + j * D + 16 * q16, *reinterpret_cast<uint32_t(*)[16]>(acc + 16 * q16));
+          tmem_ld16(t_lanes + a * Gp + j * D + 16 * q16, *reinterpret_cast<uint32_t(*)[16]>(acc + 16 * q16));
         tmem_wait_ld();
         int part = 0, hh = hr;
         if (!is_q) {
@@ -359,6 +386,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
         }
       }
+      if (has_gate) {
+        // this thread's token's gate (heads split over the warps of the lane quarter as the
+        // group's heads are): each logit rounded to the storage type with its bias added (as
+        // the gate Linear's output would be), then the pair softmax of p3d_gate_pairs, stored
+        // at gate[b, h, n]
+        using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+        uint32_t gl[kGateRows];
+        tmem_ld16(t_lanes + a * Gp + G, *reinterpret_cast<uint32_t(*)[kGateRows]>(gl));
+        tmem_wait_ld();
+        if (valid) {
+          const T *bg = static_cast<const T *>(p.bg);
+          T *gate = static_cast<T *>(p.gate);
+#pragma unroll
+          for (int hg = 0; hg < kGateRows / 2; ++hg) {
+            if (2 * hg < p.gate_cols && hg % kSplit == split) {
+              const float l0 = to_f32<T>(from_f32<T>(__uint_as_float(gl[2 * hg]) + to_f32<T>(bg[2 * hg])));
+              const float l1 = to_f32<T>(from_f32<T>(__uint_as_float(gl[2 * hg + 1]) + to_f32<T>(bg[2 * hg + 1])));
+              const float m = fmaxf(l0, l1);
+              const float e0 = expf(l0 - m), e1 = expf(l1 - m);
+              gate[((int64_t)b * p.heads + hg) * p.tokens + n] = from_f32<T>(e1 / (e0 + e1));
+            }
+          }
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kAccEmpty + a));
@@ -427,12 +478,16 @@ int launch_proj(const ProjArgs &a, cudaStream_t stream) {
   p.raster_qkv = a.raster_qkv;
   p.ey = a.ey;
   p.ex = a.ex;
+  p.gate_cols = a.gate_cols;
+  p.wg = a.wg;
+  p.bg = a.bg;
+  p.gate = a.gate;
   // shared memory: the W slice and the X ring (always), the phase table when it has at most
   // kMaxTableFloats entries (the budget proj_group_heads reserves for it), then the output
   // staging of the epilogue warps if it still fits
   const size_t table_bytes = 4 * (size_t)p.smem_floats;
   const size_t stage_bytes = (size_t)kEpilogueWarps * kStageRows * D * 2;
-  size_t smem = proj_smem_bytes(a.dim, gh * D) - 4 * (size_t)kMaxTableFloats;
+  size_t smem = proj_smem_bytes(a.dim, gh * D + (a.gate_cols > 0 ? kGateRows : 0)) - 4 * (size_t)kMaxTableFloats;
   p.table_in_smem = p.smem_floats <= kMaxTableFloats ? 1 : 0;
   p.stage_out = smem + stage_bytes + (p.table_in_smem ? table_bytes : 0) + 1024 <= info.smem_optin ? 1 : 0;
   if (p.stage_out) smem += stage_bytes;
@@ -500,29 +555,44 @@ extern "C" int p3d_qkv_project_supported(int dtype, int dim, int heads, int kv_h
   return proj_smem_bytes(dim, gh * head_dim) + 1024 <= info.smem_optin ? 1 : 0;
 }
 
-extern "C" int p3d_qkv_project(const void *x, const void *wq, const void *wkv, void *q, void *kl, void *vl, void *kg,
-                               void *vg, int dtype, int batch, int heads, int kv_heads, int tokens, int dim,
-                               int head_dim, const int64_t *coords, int pz, int py, int px, const float *phases,
-                               int ez, int ey, int ex, int64_t kv_rows, int64_t kv_row0, unsigned flags,
-                               void *stream) {
-  P3D_CHECK_ARG(x && wq && wkv && q && kl && vl && kg && vg && coords && phases, "p3d_qkv_project: null pointer");
+extern "C" int p3d_qkv_gate_project_supported(int dtype, int dim, int heads, int kv_heads, int head_dim) {
+  if (!p3d_qkv_project_supported(dtype, dim, heads, kv_heads, head_dim) || 2 * heads > kGateRows) return 0;
+  DeviceInfo info{};
+  if (device_info(&info) != P3D_OK) return 0;
+  // the last group carries the gate's logit rows: its MMA N and its two TMEM accumulators grow by kGateRows
+  const int cols = proj_group_heads(head_dim, heads, kv_heads, dim, info.smem_optin) * head_dim + kGateRows;
+  return cols <= 256 && proj_smem_bytes(dim, cols) + 1024 <= info.smem_optin ? 1 : 0;
+}
+
+namespace {
+int qkv_project(const char *name, const void *x, const void *wq, const void *wkv, const void *wg, const void *bg,
+                void *q, void *kl, void *vl, void *kg, void *vg, void *gate, int dtype, int batch, int heads,
+                int kv_heads, int tokens, int dim, int head_dim, const int64_t *coords, int pz, int py, int px,
+                const float *phases, int ez, int ey, int ex, int64_t kv_rows, int64_t kv_row0, unsigned flags,
+                void *stream) {
+  P3D_CHECK_ARG(x && wq && wkv && q && kl && vl && kg && vg && coords && phases, "%s: null pointer", name);
   if (kv_rows == 0) kv_rows = tokens;
-  P3D_CHECK_ARG(kv_row0 >= 0 && kv_row0 + tokens <= kv_rows, "p3d_qkv_project: kl / vl rows [%lld, %lld) outside "
-                "%lld rows", (long long)kv_row0, (long long)(kv_row0 + tokens), (long long)kv_rows);
-  P3D_CHECK_ARG((flags & ~P3D_SPLIT_RASTER_QKV) == 0u, "p3d_qkv_project: unknown flags 0x%x", flags);
+  P3D_CHECK_ARG(kv_row0 >= 0 && kv_row0 + tokens <= kv_rows, "%s: kl / vl rows [%lld, %lld) outside "
+                "%lld rows", name, (long long)kv_row0, (long long)(kv_row0 + tokens), (long long)kv_rows);
+  P3D_CHECK_ARG((flags & ~P3D_SPLIT_RASTER_QKV) == 0u, "%s: unknown flags 0x%x", name, flags);
   P3D_CHECK_ARG(!(flags & P3D_SPLIT_RASTER_QKV) || (int64_t)ez * ey * ex == tokens,
-                "p3d_qkv_project: raster rows need the coordinate extents to be the token grid (%d x %d x %d != %d)",
-                ez, ey, ex, tokens);
+                "%s: raster rows need the coordinate extents to be the token grid (%d x %d x %d != %d)",
+                name, ez, ey, ex, tokens);
   P3D_CHECK_ARG(batch >= 0 && tokens >= 0 && (int64_t)batch * tokens < (int64_t(1) << 31),
-                "p3d_qkv_project: bad batch / token counts");
+                "%s: bad batch / token counts", name);
   P3D_CHECK_ARG(pz >= 0 && py >= 0 && px >= 0 && 2 * (pz + py + px) == head_dim && ez >= 1 && ey >= 1 && ex >= 1,
-                "p3d_qkv_project: bad rotation pairs / extents");
+                "%s: bad rotation pairs / extents", name);
   for (const void *t : {x, wq, wkv, (const void *)q, (const void *)kl, (const void *)vl, (const void *)kg,
                         (const void *)vg})
-    P3D_CHECK_ARG(((uintptr_t)t & 15) == 0, "p3d_qkv_project: 16-byte aligned tensors required");
-  if (!p3d_qkv_project_supported(dtype, dim, heads, kv_heads, head_dim))
-    return fail(P3D_ERR_UNSUPPORTED, "p3d_qkv_project: unsupported shape (dtype %d, dim %d, heads %d/%d, D %d)",
-                dtype, dim, heads, kv_heads, head_dim);
+    P3D_CHECK_ARG(((uintptr_t)t & 15) == 0, "%s: 16-byte aligned tensors required", name);
+  if (wg) {
+    P3D_CHECK_ARG(bg && gate, "%s: null pointer", name);
+    P3D_CHECK_ARG(((uintptr_t)wg & 15) == 0 && ((uintptr_t)bg & 1) == 0 && ((uintptr_t)gate & 1) == 0,
+                  "%s: 16-byte aligned gate weight required", name);
+  }
+  if (!(wg ? p3d_qkv_gate_project_supported : p3d_qkv_project_supported)(dtype, dim, heads, kv_heads, head_dim))
+    return fail(P3D_ERR_UNSUPPORTED, "%s: unsupported shape (dtype %d, dim %d, heads %d/%d, D %d)", name, dtype, dim,
+                heads, kv_heads, head_dim);
   ProjArgs a{};
   a.dtype = dtype;
   a.rows = batch * tokens;
@@ -559,5 +629,31 @@ extern "C" int p3d_qkv_project(const void *x, const void *wq, const void *wkv, v
   a.ext[2] = ex;
   a.phases = phases;
   a.table_floats = 2 * (ez * pz + ey * py + ex * px);
+  a.gate_cols = wg ? 2 * heads : 0;
+  a.wg = wg;
+  a.bg = bg;
+  a.gate = gate;
   return launch_proj_split(a, static_cast<cudaStream_t>(stream));
+}
+}  // namespace
+
+extern "C" int p3d_qkv_project(const void *x, const void *wq, const void *wkv, void *q, void *kl, void *vl, void *kg,
+                               void *vg, int dtype, int batch, int heads, int kv_heads, int tokens, int dim,
+                               int head_dim, const int64_t *coords, int pz, int py, int px, const float *phases,
+                               int ez, int ey, int ex, int64_t kv_rows, int64_t kv_row0, unsigned flags,
+                               void *stream) {
+  return qkv_project("p3d_qkv_project", x, wq, wkv, nullptr, nullptr, q, kl, vl, kg, vg, nullptr, dtype, batch, heads,
+                     kv_heads, tokens, dim, head_dim, coords, pz, py, px, phases, ez, ey, ex, kv_rows, kv_row0, flags,
+                     stream);
+}
+
+extern "C" int p3d_qkv_gate_project(const void *x, const void *wq, const void *wkv, const void *wg, const void *bg,
+                                    void *q, void *kl, void *vl, void *kg, void *vg, void *gate, int dtype, int batch,
+                                    int heads, int kv_heads, int tokens, int dim, int head_dim, const int64_t *coords,
+                                    int pz, int py, int px, const float *phases, int ez, int ey, int ex,
+                                    int64_t kv_rows, int64_t kv_row0, unsigned flags, void *stream) {
+  P3D_CHECK_ARG(wg, "p3d_qkv_gate_project: null pointer");
+  return qkv_project("p3d_qkv_gate_project", x, wq, wkv, wg, bg, q, kl, vl, kg, vg, gate, dtype, batch, heads,
+                     kv_heads, tokens, dim, head_dim, coords, pz, py, px, phases, ez, ey, ex, kv_rows, kv_row0, flags,
+                     stream);
 }

@@ -175,12 +175,25 @@ def project_supported(x, wq, wkv, heads, kv_heads, head_dim):
                                                             kv_heads, head_dim))
 
 
+def gate_project_supported(x, wg, bg, heads, kv_heads, head_dim):
+    """Whether ``p3d_qkv_gate_project`` folds this gate Linear (weight ``wg``, bias ``bg``) into
+    the fused projection (project_supported must hold too)."""
+    if not (wg.is_contiguous() and bg.is_contiguous() and wg.dtype == x.dtype and bg.dtype == x.dtype):
+        return False
+    if wg.data_ptr() % 16 or bg.data_ptr() % 2:
+        return False
+    with torch.cuda.device(x.device):
+        return bool(_native.lib().p3d_qkv_gate_project_supported(_native.DTYPE_CODE[x.dtype], x.shape[-1], heads,
+                                                                 kv_heads, head_dim))
+
+
 def project_split_raw(x, wq, wkv, coords, phases, pairs, extents, heads, kv_heads, head_dim, raster_qkv=False,
-                      kv_out=None):
+                      kv_out=None, gate=None):
     """``p3d_qkv_project`` on x [B, N, dim] (no autograd): ``(q, kl, vl, kg, vg)``; ``raster_qkv``
     stores q, kl, vl at each token's raster row.  ``kv_out = (kl_ext, vl_ext, row0)`` writes kl
     and vl into rows ``[row0, row0 + N)`` of the given [B, G, rows, D] buffers (a z-slab rank's
-    extended buffers) and returns those row ranges as kl, vl."""
+    extended buffers) and returns those row ranges as kl, vl.  ``gate = (wg, bg)`` folds the gate
+    Linear and its pair softmax in (``p3d_qkv_gate_project``) and appends the gate [B, H, N]."""
     b, n, dim = x.shape
     x = x.contiguous()
     dev, dt = x.device, x.dtype
@@ -198,13 +211,22 @@ def project_split_raw(x, wq, wkv, coords, phases, pairs, extents, heads, kv_head
             raise ValueError("kv_out buffers must be contiguous [B, G, rows, D]")
         kv_rows = dst_k.shape[2]
         kl, vl = dst_k[:, :, row0:row0 + n], dst_v[:, :, row0:row0 + n]
+    tail = (_native.DTYPE_CODE[dt], b, heads, kv_heads, n, dim, head_dim, _native.ptr(coords), *pairs,
+            _native.ptr(phases), *extents, kv_rows, row0, _native.SPLIT_RASTER_QKV if raster_qkv else 0,
+            _native.stream_of(dev))
     with torch.cuda.device(dev):
-        _native.check(_native.lib().p3d_qkv_project(
-            _native.ptr(x), _native.ptr(wq), _native.ptr(wkv), _native.ptr(q), _native.ptr(dst_k), _native.ptr(dst_v),
-            _native.ptr(kg), _native.ptr(vg), _native.DTYPE_CODE[dt], b, heads, kv_heads, n, dim, head_dim,
-            _native.ptr(coords), *pairs, _native.ptr(phases), *extents, kv_rows, row0,
-            _native.SPLIT_RASTER_QKV if raster_qkv else 0, _native.stream_of(dev)), "p3d_qkv_project")
-    return q, kl, vl, kg, vg
+        if gate is None:
+            _native.check(_native.lib().p3d_qkv_project(
+                _native.ptr(x), _native.ptr(wq), _native.ptr(wkv), _native.ptr(q), _native.ptr(dst_k),
+                _native.ptr(dst_v), _native.ptr(kg), _native.ptr(vg), *tail), "p3d_qkv_project")
+            return q, kl, vl, kg, vg
+        wg, bg = gate
+        g = torch.empty((b, heads, n), dtype=dt, device=dev)
+        _native.check(_native.lib().p3d_qkv_gate_project(
+            _native.ptr(x), _native.ptr(wq), _native.ptr(wkv), _native.ptr(wg), _native.ptr(bg), _native.ptr(q),
+            _native.ptr(dst_k), _native.ptr(dst_v), _native.ptr(kg), _native.ptr(vg), _native.ptr(g), *tail),
+            "p3d_qkv_gate_project")
+    return q, kl, vl, kg, vg, g
 
 
 class _QKVProject(torch.autograd.Function):

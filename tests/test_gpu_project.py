@@ -85,6 +85,60 @@ def test_project_matches_gemm_then_split(cuda_device, case):
         assert (a == w).float().mean().item() > 0.95, nm
 
 
+GATE_CASES = [c for c in CASES if 2 * c[3] <= 16]
+
+
+@pytest.mark.parametrize("case", GATE_CASES, ids=[f"b{c[0]}_dim{c[2]}_h{c[3]}g{c[4]}_d{c[5]}" for c in GATE_CASES])
+def test_gate_project_folds_the_gate_linear(cuda_device, case):
+    """p3d_qkv_gate_project: q, kl, vl, kg, vg are p3d_qkv_project's bits, and the gate is the
+    separate path's (cuBLAS logits with the bias, p3d_gate_pairs) up to the logits' summation
+    order: a logit may sit one storage step away, which moves the gate by at most a quarter of
+    that step (softmax of a pair: dg/dl <= 1/4) plus the gate's own rounding."""
+    b, grid, dim, h, g, d, dtype = case
+    lib = _native.lib()
+    code = _native.DTYPE_CODE[dtype]
+    if not lib.p3d_qkv_gate_project_supported(code, dim, h, g, d):
+        pytest.skip("no room for the gate rows at this shape")
+    layout = build_layout(grid, 1, radius=0, pool_size=1).to(cuda_device)
+    n = layout.geometry.num_tokens
+    gen = torch.Generator(device=cuda_device).manual_seed(dim + h + d + 1)
+    x = torch.randn(b * n, dim, device=cuda_device, generator=gen).to(dtype)
+    wq = (torch.randn(h * d, dim, device=cuda_device, generator=gen) / dim ** 0.5).to(dtype)
+    wkv = (torch.randn(4 * g * d, dim, device=cuda_device, generator=gen) / dim ** 0.5).to(dtype)
+    wg = (torch.randn(2 * h, dim, device=cuda_device, generator=gen) / dim ** 0.5).to(dtype)
+    bg = (torch.randn(2 * h, device=cuda_device, generator=gen) * 0.5).to(dtype)
+    pairs = balanced_pairs(d)
+    extents = tuple(int(e) for e in layout.grid_shape)
+    _, phases = phase_tables(cuda_device, pairs, extents)
+    coords = layout.coords.to(torch.int64).contiguous()
+    args = (code, b, h, g, n, dim, d, _native.ptr(coords), *pairs, _native.ptr(phases), *extents, 0, 0, 0,
+            _native.stream_of(cuda_device))
+    plain = [torch.empty((b, h, n, d), dtype=dtype, device=cuda_device)]
+    plain += [torch.empty((b, g, n, d), dtype=dtype, device=cuda_device) for _ in range(4)]
+    fused = [torch.full_like(t, float("nan")) for t in plain]
+    gate = torch.full((b, h, n), float("nan"), dtype=dtype, device=cuda_device)
+    logits = torch.addmm(bg, x, wg.t())
+    want_gate = torch.empty_like(gate)
+    with torch.cuda.device(cuda_device):
+        _native.check(lib.p3d_qkv_project(_native.ptr(x), _native.ptr(wq), _native.ptr(wkv),
+                                          *[_native.ptr(t) for t in plain], *args), "p3d_qkv_project")
+        _native.check(lib.p3d_qkv_gate_project(_native.ptr(x), _native.ptr(wq), _native.ptr(wkv), _native.ptr(wg),
+                                               _native.ptr(bg), *[_native.ptr(t) for t in fused], _native.ptr(gate),
+                                               *args), "p3d_qkv_gate_project")
+        _native.check(lib.p3d_gate_pairs(_native.ptr(logits), 2 * h, _native.ptr(want_gate), code, b, h, n,
+                                         _native.stream_of(cuda_device)), "p3d_gate_pairs")
+    torch.cuda.synchronize()
+    assert _native.device_errors() == 0
+    for a, w in zip(fused, plain):
+        assert torch.equal(a, w)
+    assert not torch.isnan(gate).any()
+    step = 2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11   # half an ulp at 1, relative
+    logit_ulp = 2 * step * logits.float().abs().max().item()
+    err = (gate.float() - want_gate.float()).abs().max().item()
+    assert err <= 0.25 * logit_ulp + 4 * step, err
+    assert (gate == want_gate).float().mean().item() > 0.9
+
+
 def test_project_rejects_what_it_cannot_run(cuda_device):
     lib = _native.lib()
     assert lib.p3d_qkv_project_supported(_native.F32, 192, 4, 4, 48) == 0
