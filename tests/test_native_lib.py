@@ -138,6 +138,17 @@ def test_argument_checks_run_before_any_device_call():
     st = lib.p3d_pool_fwd(dummy, dummy, dummy, dummy, dummy, 4, 65, 1, dummy, dummy, None, None, _native.BF16, 1, 1,
                           256, 48, 1.0, None)
     assert st == 1 and b"block table" in lib.p3d_last_error()
+    # p3d_qkv_gate_project: the gate weight, bias and output are required; the weight 16-byte aligned
+    proj_tail = (_native.BF16, 1, 4, 4, 64, 192, 48, dummy, 8, 8, 8, dummy, 4, 4, 4, 0, 0, 0, None)
+    st = lib.p3d_qkv_gate_project(dummy, dummy, dummy, None, dummy, dummy, dummy, dummy, dummy, dummy, dummy,
+                                  *proj_tail)
+    assert st == 1 and b"p3d_qkv_gate_project: null pointer" in lib.p3d_last_error()
+    st = lib.p3d_qkv_gate_project(dummy, dummy, dummy, dummy, dummy, dummy, dummy, dummy, dummy, dummy, None,
+                                  *proj_tail)
+    assert st == 1 and b"p3d_qkv_gate_project: null pointer" in lib.p3d_last_error()
+    st = lib.p3d_qkv_gate_project(dummy, dummy, dummy, dummy + 8, dummy, dummy, dummy, dummy, dummy, dummy, dummy,
+                                  *proj_tail)
+    assert st == 1 and b"aligned gate weight" in lib.p3d_last_error()
     # p3d_layer_norm_bwd_residual: the residual gradient is required; misaligned, or no workspace
     st = lib.p3d_layer_norm_bwd_residual(dummy, dummy, dummy, None, dummy, dummy, dummy, _native.BF16, 8, 192, 1e-5,
                                          dummy, 1 << 20, None)
